@@ -1,0 +1,191 @@
+/* smg.h — C ABI of the B200-native scenemap objprob per-frame update.
+ *
+ * One `smg_batch` holds M independent maps on one GPU: each map is one scenemap
+ * (ObjectMap + Mapper2D occupancy grid).  A call to smg_push_frames runs, for every map,
+ * the reference keyframe path for one depth frame:
+ *   Mapper2D::keyframe  (scenemap src/mapper2d.cpp:100-160: makeScan + OccGrid::insert)
+ *   ObjectMap::update   (scenemap src/objmap.cpp:516-1086)
+ *   ObjectMap::addPoints for every emitted observation cloud (scenemap src/capi.cpp:986-992)
+ * entirely on the device, on the caller's stream.  Nothing falls back to the CPU: without a
+ * usable sm_100 device every entry point returns SMG_ERR_DEVICE.
+ *
+ * Conventions (scenemap include/scenemap.h:421 convention): 0 = ok, negative = error.
+ * No exception crosses this ABI.  One host thread per batch; calls on one batch must not
+ * overlap.  All pointers are plain; "device" pointers are CUDA device addresses.
+ */
+#ifndef SMG_H
+#define SMG_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  SMG_OK = 0,
+  SMG_ERR_ARGS = -1,       /* bad arguments / unsupported input form */
+  SMG_ERR_PARAM = -2,      /* unknown parameter key */
+  SMG_ERR_CAPACITY = -3,   /* an object / point / cell capacity would be exceeded */
+  SMG_ERR_DEVICE = -4,     /* CUDA error, or the device error word was set */
+};
+
+enum { SMG_MEM_DEVICE = 0, SMG_MEM_HOST = 1 };
+enum { SMG_EMB_F32 = 0, SMG_EMB_BF16 = 1 };
+
+/* Parameters.  Field names and defaults mirror the reference structs:
+ * ObjParams (scenemap include/scenemap/objmap.hpp:50-129), ApParams (objprob.hpp:56-142),
+ * KappaParams (bestview.hpp:67-69), GridParams (grid.hpp:18-21), ScanParams (scan.hpp:37-48),
+ * MapperParams (mapper2d.hpp:14-26).  Fill with smg_params_default, override with
+ * smg_params_apply ("key=val,..." — the reference's applyParams key names, objmap.cpp:132-205). */
+typedef struct smg_params {
+  /* ObjParams */
+  int32_t min_points;
+  float zmin, zmax, hand_r, hand_frac;
+  double big;
+  int32_t confirm;
+  double prune_s, moved_d;
+  int32_t gone_misses;
+  double gone_min_s, mad_k, mad_floor, grow_max, max_ext, occl;
+  int32_t min_px;
+  double self_pad;
+  int32_t step, max_pts;
+  double voxel;
+  int32_t cloud_cap;
+  double cloud_hand_r, body_r, merge_min_ext, floor_h;
+  int32_t absent_samples;
+  double absent_vis, absent_min_px, absent_det_k;
+  int32_t gone_misses_big;
+  double gone_min_s_big;
+  int32_t spurious_obs;
+  double gone_view_d, gone_step_d, gone_step_deg, gone_eps;
+  double link_v, link_d0, link_max_d;
+  int32_t link_min_obs;
+  double link_wait_s, link_window_s, link_view_gap_s, view_cell;
+  int32_t move_n;
+  double move_v, move_min_d, move_max_cam_w;
+  double ap_q_pos, ap_r0, ap_r1;
+  /* ApParams */
+  double same_p, merge_p, w[8], wm[8], guard_obj, guard_obs, name_veto;
+  int32_t bridge_drop, frame_group;
+  double cos0, gate, contact_cell;
+  int32_t contact_samples, topk;
+  double temper_d, temper_deg, temper, kappa_ref;
+  double plane_thick, ransac_tau0, ransac_tau_k, ransac_tau_max, obj_tau, plane_inl, obj_plane_inl;
+  int32_t ransac_iters;
+  double wall_vert, ceil_z, horiz, floor_z, ceil_band, ceil_frac, ceil_wide;
+  double tall_h, tall_floor, tall_ceil, tall_w, tall_ps, tall_w_any;
+  double obj_wall_span, obj_wall_top, obj_wall_h, obj_thick;
+  double struct_obj_p;
+  int32_t struct_obj_min_views;
+  double link_cos;
+  /* KappaParams */
+  double kap_k0, kap_s0, kap_trunc, kap_d0, kap_occ, kap_blur_w;
+  /* GridParams + ScanParams + MapperParams (insert policy) */
+  float grid_res, l_hit, l_miss, l_min, l_max;
+  float scan_zmin, scan_zmax, band_lo, band_hi;
+  int32_t bins;
+  float self_r, eef_r, arm_r, shoulder[2][3], match_hi, vert_nz, match_cell;
+  int32_t dense, change_bins, change_cells, still_every;
+} smg_params;
+
+/* One frame of one map.  depth/label/emb/dets live in device memory (SMG_MEM_DEVICE) or in
+ * host memory (SMG_MEM_HOST: copied in by the call, on the caller's stream).
+ * The detector mask of detection k is the set of pixels whose label equals det_label[k]
+ * (mask grid = depth image grid); the reference's bit-mask form (scenemap.h:20-34) maps to
+ * it one to one when mask_sx = mask_sy = 1 and mask_ox = mask_oy = 0. */
+typedef struct smg_frame {
+  double stamp;
+  int32_t w, h;
+  const float* depth;          /* w*h optical depth, metres */
+  const uint16_t* label;       /* w*h instance labels */
+  float fx, fy, cx, cy;
+  double T_mc[12];             /* map <- camera optical, row-major 3x4 (ObjFrame::T_mc) */
+  float T_bc[12];              /* base <- camera optical (DepthView::T_bc) */
+  double base[3];              /* base pose in the map (x, y, yaw): the grid insert pose */
+  double eef[2][3];            /* hand points, map frame (ObjFrame::eef) */
+  float eef_base[2][3];        /* hand points, base frame (BodyState::eef) */
+  int32_t n_det;
+  const uint16_t* det_label;   /* n_det */
+  const float* box;            /* n_det x 4: x0 y0 x1 y1 pixels */
+  const int32_t* cls;          /* n_det */
+  const float* score;          /* n_det or NULL */
+  const void* emb;             /* n_det x emb_dim, L2-normalised */
+  int32_t emb_dtype;           /* SMG_EMB_F32 | SMG_EMB_BF16 */
+} smg_frame;
+
+typedef struct smg_batch smg_batch;
+
+/* sizeof(smg_params), for bindings that treat the struct as an opaque buffer. */
+int smg_params_size(void);
+/* scenemap objmap.hpp:50-129 defaults (+ objprob.hpp:56-142, bestview.hpp:67-69, grid.hpp:18-21,
+ * scan.hpp:37-48, mapper2d.hpp:14-26). */
+int smg_params_default(smg_params* p);
+/* ObjectMap::applyParams (scenemap src/objmap.cpp:132-205): "key=val,...".  Returns the number
+ * of unknown keys (0 = all known), or SMG_ERR_ARGS. */
+int smg_params_apply(smg_params* p, const char* kv);
+
+/* Create M maps on device `dev`.  max_objects: object slots per map; emb_dim: embedding width
+ * (<= 2048); max_w/max_h: largest frame; max_det: detections per frame (<= 64);
+ * grid_w/grid_h and grid_x0/grid_y0: the fixed occupancy window in global cell indices.
+ * Replaces `new ObjectMap(p)` + `Mapper2D(p)` (scenemap objmap.hpp:235, mapper2d.hpp:39). */
+int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, int max_w, int max_h, int max_det, int grid_w,
+               int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out);
+int smg_destroy(smg_batch* b);
+
+/* One keyframe for each of the first n maps (frames[i] -> map i).  Replaces, per map,
+ * the keyframe block of sm_push_image_rgb (scenemap src/capi.cpp:811-992):
+ * Mapper2D::keyframe, ObjectMap::update, ObjectMap::addPoints.  `stream` is a cudaStream_t
+ * (NULL = the legacy default stream).  Returns before the device work finishes; results
+ * are read with the getters below (which synchronise the stream). */
+int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, void* stream);
+
+/* ---- results (device -> host on request; each getter synchronises the batch stream) ---- */
+typedef struct smg_object {
+  uint32_t id;
+  int32_t cls;
+  double pos[3], ext[3], first_pos[3], lo[3], hi[3];
+  uint32_t n_obs;
+  double first_seen, last_seen;
+  int32_t state, confirmed, moved, misses;
+  uint32_t n_vis_miss;
+  float score;
+  double max_det_z, last_kf;
+  int32_t appeared;
+  int32_t cloud_n;
+  uint32_t cloud_version;
+  double cloud_org[3];
+  uint32_t ap_ver;
+  double k_frag;
+  int32_t n_views, n_ap_obs, need_whole;
+  double P[3];
+  int32_t n_cams, geo;
+} smg_object;
+
+/* ObjectMap::objects() (scenemap objmap.hpp:242) of map m, in the reference's order. */
+int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap);
+/* r_frag (emb_dim floats) and the top-k views (fp16 bits, emb_dim each) of object i of map m. */
+int smg_get_object_vectors(smg_batch* b, int m, int i, float* r_frag, uint16_t* views, float* vkappa, double* vstamp, int vcap);
+/* Cloud of object i of map m: points relative to cloud_org (float xyz) and seq; returns count. */
+int smg_get_object_cloud(smg_batch* b, int m, int i, float* xyz, uint32_t* seq, int cap);
+/* ObjectMap::lastAssoc() (objmap.hpp:251) of map m: per detection obj_id, n_valid, area_px, depth_med. */
+int smg_get_assoc(smg_batch* b, int m, uint32_t* obj_id, int32_t* n_valid, float* area_px, float* depth_med, int cap);
+/* ApStats (objmap.hpp:132-139) of map m, 16 counters in declaration order. */
+int smg_get_stats(smg_batch* b, int m, int64_t* out16);
+/* Events of the last frame of map m (ObjEvent, objmap.hpp:150-155): t, id, kind. */
+int smg_get_events(smg_batch* b, int m, double* t, uint32_t* id, int32_t* kind, int cap);
+/* Occupancy window of map m: log-odds (1/256 fixed point), seen flag, export8 value
+ * (OccGrid::export8, grid.cpp:209-213), grid_w*grid_h cells, row-major. */
+int smg_get_grid(smg_batch* b, int m, int16_t* L, uint8_t* seen, int8_t* c8);
+/* Keyframe stats of the last frame of map m: inserted, changed_cells, n_hits (KeyframeStats). */
+int smg_get_keyframe(smg_batch* b, int m, int32_t* out3);
+/* Device error word (0 = none) and a static description of the last host-side error. */
+int smg_error_word(smg_batch* b);
+const char* smg_last_error(void);
+/* Number of kernels the library has launched since creation (instrumentation). */
+int64_t smg_kernel_launches(smg_batch* b);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SMG_H */

@@ -1,0 +1,260 @@
+"""ctypes binding of the oracle libraries (TEST INFRASTRUCTURE ONLY).
+
+``_ref/libscenemap_ref.so`` is the reference scenemap code compiled in place by
+``oracle/Makefile`` plus ``ref_driver.cpp``; ``_ref/libport.so`` is the C restatement in
+``port/``.  Only tests, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg use this
+module, as the checker or the timed CPU baseline; the product never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_SO = os.path.join(HERE, "_ref", "libscenemap_ref.so")
+PORT_SO = os.path.join(HERE, "_ref", "libport.so")
+
+
+class RfFrame(C.Structure):
+    _fields_ = [("stamp", C.c_double), ("w", C.c_int), ("h", C.c_int), ("depth", C.POINTER(C.c_float)),
+                ("label", C.POINTER(C.c_uint16)), ("fx", C.c_float), ("fy", C.c_float), ("cx", C.c_float),
+                ("cy", C.c_float), ("T_mc", C.c_double * 12), ("T_bc", C.c_float * 12), ("base", C.c_double * 3),
+                ("eef", C.c_double * 6), ("eef_base", C.c_float * 6), ("n_det", C.c_int),
+                ("det_label", C.POINTER(C.c_uint16)), ("box", C.POINTER(C.c_float)), ("cls", C.POINTER(C.c_int32)),
+                ("score", C.POINTER(C.c_float)), ("emb", C.POINTER(C.c_float)), ("emb_dim", C.c_int),
+                ("grid_only", C.c_int)]
+
+
+class RfObj(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("cls", C.c_int32), ("pos", C.c_double * 3), ("ext", C.c_double * 3),
+                ("first_pos", C.c_double * 3), ("lo", C.c_double * 3), ("hi", C.c_double * 3), ("n_obs", C.c_uint32),
+                ("first_seen", C.c_double), ("last_seen", C.c_double), ("state", C.c_int32), ("confirmed", C.c_int32),
+                ("moved", C.c_int32), ("misses", C.c_int32), ("n_vis_miss", C.c_uint32), ("score", C.c_float),
+                ("max_det_z", C.c_double), ("last_kf", C.c_double), ("gone_t", C.c_double), ("appeared", C.c_int32),
+                ("mv_cnt", C.c_int32), ("trk_pos", C.c_double * 3), ("trk_t", C.c_double), ("trk_step", C.c_double * 2),
+                ("moving_t", C.c_double), ("move_from_t", C.c_double), ("first_miss", C.c_double),
+                ("miss_cam", C.c_double * 3), ("last_miss_cam", C.c_double * 3), ("last_miss_fwd", C.c_double * 3),
+                ("cloud_n", C.c_int32), ("cloud_version", C.c_uint32), ("cloud_org", C.c_double * 3),
+                ("ap_ver", C.c_uint32), ("k_frag", C.c_double), ("k_whole", C.c_double), ("n_views", C.c_int32),
+                ("n_ap_obs", C.c_int32), ("n_wall_obs", C.c_int32), ("n_struct_look", C.c_int32),
+                ("need_whole", C.c_int32), ("n_whole", C.c_int32), ("P", C.c_double * 3), ("n_cams", C.c_int32),
+                ("geo", C.c_int32), ("drop", C.c_int32), ("hide", C.c_int32)]
+
+
+STAT_FIELDS = ["n_through", "n_obs", "n_wall", "n_wall_name", "n_ceil", "n_floor", "n_assoc", "n_new", "n_merge",
+               "n_obj_struct", "n_reenc_req", "n_reenc_done", "n_blocked", "n_wall_tall", "n_so_big", "n_bridge"]
+
+
+class RfStats(C.Structure):
+    _fields_ = [(n, C.c_long) for n in STAT_FIELDS]
+
+
+_ref = None
+
+
+def available() -> bool:
+    return os.path.exists(REF_SO)
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        if not available():
+            raise RuntimeError(f"reference oracle not built: {REF_SO}")
+        L = C.CDLL(REF_SO)
+        P = C.POINTER
+        L.ref_create.restype = C.c_void_p
+        L.ref_create.argtypes = [C.c_char_p, C.c_double, C.c_int, C.c_int, P(C.c_float), C.c_int]
+        L.ref_destroy.argtypes = [C.c_void_p]
+        L.ref_frame.argtypes = [C.c_void_p, P(RfFrame)]
+        L.ref_n_objects.argtypes = [C.c_void_p]
+        L.ref_objects.argtypes = [C.c_void_p, P(RfObj), C.c_int]
+        L.ref_object_vectors.argtypes = [C.c_void_p, C.c_int, P(C.c_float), C.c_int, P(C.c_uint16), P(C.c_float),
+                                         P(C.c_double), C.c_int]
+        L.ref_object_cloud.argtypes = [C.c_void_p, C.c_int, P(C.c_float), P(C.c_uint32), C.c_int]
+        L.ref_assoc.argtypes = [C.c_void_p, P(C.c_uint32), P(C.c_int32), P(C.c_float), P(C.c_float), C.c_int]
+        L.ref_n_points.argtypes = [C.c_void_p]
+        L.ref_points.argtypes = [C.c_void_p, C.c_int, P(C.c_uint32), P(C.c_int32), P(C.c_float), P(C.c_int32), C.c_int]
+        L.ref_stats.argtypes = [C.c_void_p, P(RfStats)]
+        L.ref_n_events.argtypes = [C.c_void_p]
+        L.ref_events.argtypes = [C.c_void_p, P(C.c_double), P(C.c_uint32), P(C.c_int32), C.c_int]
+        L.ref_kf.argtypes = [C.c_void_p, P(C.c_int32)]
+        L.ref_grid_geom.argtypes = [C.c_void_p, P(C.c_int32)]
+        L.ref_grid_cells.argtypes = [C.c_void_p, P(C.c_int16), P(C.c_uint8), P(C.c_int8)]
+        L.ref_occ_create.restype = C.c_void_p
+        L.ref_occ_create.argtypes = [P(C.c_float)]
+        L.ref_occ_destroy.argtypes = [C.c_void_p]
+        L.ref_occ_insert.argtypes = [C.c_void_p, C.c_float, C.c_float, P(C.c_float), P(C.c_float), C.c_int,
+                                     P(C.c_float), P(C.c_float), C.c_int, P(C.c_float), P(C.c_float), P(C.c_float),
+                                     P(C.c_float), C.c_int, P(C.c_double)]
+        L.ref_occ_geom.argtypes = [C.c_void_p, P(C.c_int32)]
+        L.ref_occ_cells.argtypes = [C.c_void_p, P(C.c_int16), P(C.c_uint8), P(C.c_int8), P(C.c_float)]
+        L.ref_make_scan.argtypes = [C.c_int, C.c_int, P(C.c_float), C.c_float, C.c_float, C.c_float, C.c_float,
+                                    P(C.c_float), P(C.c_float)] + [P(C.c_float)] * 8 + [P(C.c_int16), C.c_float,
+                                                                                          P(C.c_int32), P(C.c_float)]
+        L.ref_plane_fit.argtypes = [P(C.c_float), C.c_int, C.c_double, C.c_uint64, C.c_int, P(C.c_double)]
+        L.ref_ap_seed.restype = C.c_uint64
+        L.ref_ap_seed.argtypes = [C.c_uint64, C.c_uint64]
+        L.ref_to_f16.argtypes = [P(C.c_float), P(C.c_uint16), C.c_int]
+        L.ref_voxel_key.restype = C.c_uint64
+        L.ref_voxel_key.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
+        L.ref_contact.restype = C.c_double
+        L.ref_contact.argtypes = [P(C.c_float), C.c_int, P(C.c_float), C.c_int, C.c_double]
+        _ref = L
+    return _ref
+
+
+def _p(a, t):
+    return a.ctypes.data_as(C.POINTER(t))
+
+
+def make_rf_frame(fr: dict, keep: list) -> RfFrame:
+    """Fill an RfFrame from a synth frame dict; `keep` holds the arrays alive."""
+    f = RfFrame()
+    f.stamp = fr["stamp"]
+    f.w, f.h = fr["w"], fr["h"]
+    depth = np.ascontiguousarray(fr["depth"], np.float32)
+    label = np.ascontiguousarray(fr["label"], np.uint16)
+    keep += [depth, label]
+    f.depth = _p(depth, C.c_float)
+    f.label = _p(label, C.c_uint16)
+    f.fx, f.fy, f.cx, f.cy = fr["fx"], fr["fy"], fr["cx"], fr["cy"]
+    for i in range(12):
+        f.T_mc[i] = fr["T_mc"][i]
+        f.T_bc[i] = fr["T_bc"][i]
+    for i in range(3):
+        f.base[i] = fr["base"][i]
+    eef = np.asarray(fr["eef"], np.float64).reshape(-1)
+    eefb = np.asarray(fr["eef_base"], np.float32).reshape(-1)
+    for i in range(6):
+        f.eef[i] = eef[i]
+        f.eef_base[i] = eefb[i]
+    n = int(fr["n_det"])
+    f.n_det = n
+    if n:
+        dl = np.ascontiguousarray(fr["det_label"], np.uint16)
+        bx = np.ascontiguousarray(fr["box"], np.float32)
+        cl = np.ascontiguousarray(fr["cls"], np.int32)
+        sc = np.ascontiguousarray(fr["score"], np.float32)
+        em = np.ascontiguousarray(fr["emb"], np.float32)
+        keep += [dl, bx, cl, sc, em]
+        f.det_label = _p(dl, C.c_uint16)
+        f.box = _p(bx, C.c_float)
+        f.cls = _p(cl, C.c_int32)
+        f.score = _p(sc, C.c_float)
+        f.emb = _p(em, C.c_float)
+        f.emb_dim = int(fr["emb_dim"])
+    f.grid_only = 0
+    return f
+
+
+class RefMap:
+    """One reference scenemap (ObjectMap + Mapper2D) driven frame by frame."""
+
+    def __init__(self, obj_kv: str = "", voxel: float = 0.02, cloud_cap: int = 8000, grid=(0.05, 0.85, -0.4, -4.0, 4.0),
+                 grid_on: bool = True, attach_on: bool = False):
+        L = ref_lib()
+        g = np.asarray(grid, np.float32)
+        self._h = L.ref_create(obj_kv.encode(), voxel, cloud_cap, 1 if grid_on else 0, _p(g, C.c_float),
+                               1 if attach_on else 0)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            ref_lib().ref_destroy(self._h)
+            self._h = None
+
+    def frame(self, fr: dict) -> None:
+        keep = []
+        f = make_rf_frame(fr, keep)
+        rc = ref_lib().ref_frame(self._h, C.byref(f))
+        if rc != 0:
+            raise RuntimeError(f"ref_frame rc={rc}")
+
+    def objects(self) -> list:
+        L = ref_lib()
+        n = L.ref_n_objects(self._h)
+        arr = (RfObj * max(n, 1))()
+        L.ref_objects(self._h, arr, n)
+        out = []
+        for i in range(n):
+            o = arr[i]
+            d = {}
+            for name, _ in RfObj._fields_:
+                v = getattr(o, name)
+                d[name] = list(v) if hasattr(v, "__len__") else v
+            out.append(d)
+        return out
+
+    def object_vectors(self, i: int, D: int):
+        L = ref_lib()
+        r = np.zeros(D, np.float32)
+        views = np.zeros((5, D), np.uint16)
+        vk = np.zeros(5, np.float32)
+        vs = np.zeros(5, np.float64)
+        nv = L.ref_object_vectors(self._h, i, _p(r, C.c_float), D, _p(views, C.c_uint16), _p(vk, C.c_float),
+                                  _p(vs, C.c_double), 5)
+        return r, views[:nv], vk[:nv], vs[:nv]
+
+    def object_cloud(self, i: int):
+        L = ref_lib()
+        n = L.ref_object_cloud(self._h, i, None, None, 0)
+        xyz = np.zeros((max(n, 1), 3), np.float32)
+        seq = np.zeros(max(n, 1), np.uint32)
+        L.ref_object_cloud(self._h, i, _p(xyz, C.c_float), _p(seq, C.c_uint32), n)
+        return xyz[:n], seq[:n]
+
+    def assoc(self):
+        L = ref_lib()
+        cap = 256
+        oid = np.zeros(cap, np.uint32)
+        nv = np.zeros(cap, np.int32)
+        ar = np.zeros(cap, np.float32)
+        dm = np.zeros(cap, np.float32)
+        n = L.ref_assoc(self._h, _p(oid, C.c_uint32), _p(nv, C.c_int32), _p(ar, C.c_float), _p(dm, C.c_float), cap)
+        return dict(obj_id=oid[:n], n_valid=nv[:n], area_px=ar[:n], depth_med=dm[:n])
+
+    def points(self) -> list:
+        L = ref_lib()
+        out = []
+        for j in range(L.ref_n_points(self._h)):
+            n = L.ref_points(self._h, j, None, None, None, None, 0)
+            oid = C.c_uint32()
+            det = C.c_int32()
+            xyz = np.zeros((max(n, 1), 3), np.float32)
+            px = np.zeros((max(n, 1), 2), np.int32)
+            L.ref_points(self._h, j, C.byref(oid), C.byref(det), _p(xyz, C.c_float), _p(px, C.c_int32), n)
+            out.append(dict(obj_id=oid.value, det=det.value, xyz=xyz[:n], px=px[:n]))
+        return out
+
+    def stats(self) -> dict:
+        s = RfStats()
+        ref_lib().ref_stats(self._h, C.byref(s))
+        return {n: getattr(s, n) for n in STAT_FIELDS}
+
+    def events(self):
+        L = ref_lib()
+        n = L.ref_n_events(self._h)
+        t = np.zeros(max(n, 1), np.float64)
+        i = np.zeros(max(n, 1), np.uint32)
+        k = np.zeros(max(n, 1), np.int32)
+        L.ref_events(self._h, _p(t, C.c_double), _p(i, C.c_uint32), _p(k, C.c_int32), n)
+        return list(zip(t[:n].tolist(), i[:n].tolist(), k[:n].tolist()))
+
+    def kf(self):
+        o = np.zeros(3, np.int32)
+        ref_lib().ref_kf(self._h, _p(o, C.c_int32))
+        return dict(inserted=int(o[0]), changed=int(o[1]), n_hits=int(o[2]))
+
+    def grid(self):
+        L = ref_lib()
+        g = np.zeros(4, np.int32)
+        if L.ref_grid_geom(self._h, _p(g, C.c_int32)) != 0:
+            return None
+        x0, y0, w, h = (int(v) for v in g)
+        Lq = np.zeros((h, w), np.int16)
+        seen = np.zeros((h, w), np.uint8)
+        c8 = np.zeros((h, w), np.int8)
+        L.ref_grid_cells(self._h, _p(Lq, C.c_int16), _p(seen, C.c_uint8), _p(c8, C.c_int8))
+        return dict(x0=x0, y0=y0, w=w, h=h, L=Lq, seen=seen, c8=c8)

@@ -1,0 +1,430 @@
+// Oracle driver (TEST INFRASTRUCTURE ONLY — never part of the product path).
+//
+// Drives the reference scenemap C++ code, compiled in place from the reference sources by
+// oracle/Makefile into oracle/_ref/libscenemap_ref.so, through its C++ API:
+//   Mapper2D::keyframe (scenemap src/mapper2d.cpp:100)  -> makeScan + OccGrid::insert
+//   ObjectMap::update   (scenemap src/objmap.cpp:516)    -> the objprob per-frame update
+//   ObjectMap::addPoints(scenemap src/objmap.cpp:508)    -> ObjCloud::add (cloud.cpp:86)
+// in the order the reference's keyframe glue runs them (scenemap src/capi.cpp:811-992),
+// minus robot FK, best-view crops and re-encode requests (outside the hot path).
+// The label image is turned into the sm_detections bit masks the reference consumes
+// (scenemap include/scenemap.h:20-34), with the mask grid equal to the image grid.
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <memory>
+#include <vector>
+
+#include "scenemap/grid.hpp"
+#include "scenemap/mapper2d.hpp"
+#include "scenemap/objmap.hpp"
+#include "scenemap/objprob.hpp"
+#include "scenemap/scan.hpp"
+#include "scenemap/cloud.hpp"
+
+using namespace scenemap;
+
+extern "C" {
+
+typedef struct {
+  double stamp;
+  int w, h;
+  const float* depth;
+  const uint16_t* label;
+  float fx, fy, cx, cy;
+  double T_mc[12];
+  float T_bc[12];
+  double base[3];         // map pose of the base (x, y, th): the grid insert pose
+  double eef[2][3];       // hand points, map frame (objprob hand filters)
+  float eef_base[2][3];   // hand points, base frame (scan body mask)
+  int n_det;
+  const uint16_t* det_label;
+  const float* box;
+  const int32_t* cls;
+  const float* score;
+  const float* emb;
+  int emb_dim;
+  int grid_only;          // 1: keyframe only (no detections)
+} rf_frame;
+
+typedef struct {
+  uint32_t id;
+  int32_t cls;
+  double pos[3], ext[3], first_pos[3], lo[3], hi[3];
+  uint32_t n_obs;
+  double first_seen, last_seen;
+  int32_t state, confirmed, moved, misses;
+  uint32_t n_vis_miss;
+  float score;
+  double max_det_z, last_kf, gone_t;
+  int32_t appeared, mv_cnt;
+  double trk_pos[3], trk_t, trk_step[2], moving_t, move_from_t;
+  double first_miss, miss_cam[3], last_miss_cam[3], last_miss_fwd[3];
+  // cloud
+  int32_t cloud_n;
+  uint32_t cloud_version;
+  double cloud_org[3];
+  // objprob state
+  uint32_t ap_ver;
+  double k_frag, k_whole;
+  int32_t n_views, n_ap_obs, n_wall_obs, n_struct_look, need_whole, n_whole;
+  double P[3];
+  int32_t n_cams, geo;
+  int32_t drop, hide;
+} rf_obj;
+
+typedef struct {
+  long n_through, n_obs, n_wall, n_wall_name, n_ceil, n_floor, n_assoc, n_new, n_merge, n_obj_struct, n_reenc_req, n_reenc_done,
+      n_blocked, n_wall_tall, n_so_big, n_bridge;
+} rf_stats;
+
+struct RefMap {
+  ObjectMap om;
+  std::unique_ptr<Mapper2D> mapper;
+  KeyframeStats kf;
+  std::vector<uint32_t> bits;
+  std::vector<ObsPoints> pts;   // copy of lastPoints() as handed to addPoints
+  explicit RefMap(const ObjParams& p) : om(p) {}
+};
+
+void* ref_create(const char* obj_kv, double voxel, int cloud_cap, int grid_on, const float* grid /* res, l_hit, l_miss, l_min, l_max */,
+                 int attach_on) {
+  ObjParams p;
+  if (obj_kv && *obj_kv) ObjectMap::applyParams(&p, obj_kv, false);
+  if (voxel > 0) p.voxel = voxel;
+  if (cloud_cap > 0) p.cloud_cap = cloud_cap;
+  RefMap* m = new RefMap(p);
+  if (grid_on) {
+    MapperParams mp;
+    if (grid) {
+      mp.grid.res = grid[0];
+      mp.grid.l_hit = grid[1];
+      mp.grid.l_miss = grid[2];
+      mp.grid.l_min = grid[3];
+      mp.grid.l_max = grid[4];
+    }
+    mp.attach.enabled = attach_on != 0;
+    m->mapper.reset(new Mapper2D(mp));
+  }
+  return m;
+}
+
+void ref_destroy(void* h) { delete static_cast<RefMap*>(h); }
+
+int ref_frame(void* h, const rf_frame* f) {
+  RefMap* m = static_cast<RefMap*>(h);
+  if (!m || !f || f->w <= 0 || f->h <= 0 || !f->depth) return -1;
+  if (m->mapper) {   // Mapper2D::keyframe as capi.cpp:809-820 sets it up (no FK capsules)
+    DepthView dv;
+    dv.w = f->w;
+    dv.h = f->h;
+    dv.m = f->depth;
+    dv.step = std::max(1, int(std::lround(f->w / 160.0)));
+    dv.fx = f->fx; dv.fy = f->fy; dv.cx = f->cx; dv.cy = f->cy;
+    memcpy(dv.T_bc, f->T_bc, sizeof(dv.T_bc));
+    BodyState b;
+    for (int s = 0; s < 2; ++s) for (int k = 0; k < 3; ++k) b.eef[s][k] = f->eef_base[s][k];
+    Pose2 known{f->base[0], f->base[1], f->base[2]};
+    m->kf = m->mapper->keyframe(dv, b, known, nullptr);
+  }
+  if (f->grid_only) return 0;
+  // label image -> sm_detections (mask grid = image grid)
+  const int n = f->n_det;
+  const size_t words = (size_t(f->w) * f->h + 31) / 32;
+  m->bits.assign(words * size_t(std::max(0, n)), 0u);
+  std::vector<size_t> slot(65536, SIZE_MAX);
+  for (int k = 0; k < n; ++k) slot[f->det_label[k]] = size_t(k);
+  if (f->label)
+    for (size_t c = 0; c < size_t(f->w) * f->h; ++c) {
+      const size_t k = slot[f->label[c]];
+      if (k != SIZE_MAX) m->bits[k * words + (c >> 5)] |= 1u << (c & 31);
+    }
+  sm_detections d;
+  memset(&d, 0, sizeof(d));
+  d.stamp = f->stamp;
+  d.img_w = f->w;
+  d.img_h = f->h;
+  d.n = n;
+  d.cls = f->cls;
+  d.score = f->score;
+  d.box = f->box;
+  d.mask_w = f->w;
+  d.mask_h = f->h;
+  d.mask_sx = d.mask_sy = 1.f;
+  d.mask_ox = d.mask_oy = 0.f;
+  d.mask_bits = m->bits.data();
+  ObjFrame F;
+  F.stamp = f->stamp;
+  F.w = f->w;
+  F.h = f->h;
+  F.depth_m = f->depth;
+  F.fx = f->fx; F.fy = f->fy; F.cx = f->cx; F.cy = f->cy;
+  memcpy(F.T_mc, f->T_mc, sizeof(F.T_mc));
+  F.dets = n > 0 ? &d : nullptr;
+  for (int s = 0; s < 2; ++s) for (int k = 0; k < 3; ++k) F.eef[s][k] = f->eef[s][k];
+  F.grip[0] = F.grip[1] = 1.f;
+  F.base_yaw = f->base[2];
+  F.base_xy[0] = f->base[0];
+  F.base_xy[1] = f->base[1];
+  F.emb = f->emb;
+  F.emb_dim = f->emb_dim;
+  m->om.update(F);
+  // cloud points, uncoloured (capi.cpp:986-992 with no RGB source)
+  m->pts = m->om.lastPoints();
+  for (const ObsPoints& q : m->pts) m->om.addPoints(q.obj_id, q.xyz.data(), nullptr, int(q.px.size() / 2), f->stamp);
+  return 0;
+}
+
+int ref_n_objects(void* h) { return int(static_cast<RefMap*>(h)->om.objects().size()); }
+
+int ref_objects(void* h, rf_obj* out, int cap) {
+  const auto& objs = static_cast<RefMap*>(h)->om.objects();
+  const int n = std::min<int>(cap, int(objs.size()));
+  for (int i = 0; i < n; ++i) {
+    const MapObject& o = objs[size_t(i)];
+    rf_obj& r = out[i];
+    memset(&r, 0, sizeof(r));
+    r.id = o.id;
+    r.cls = o.cls;
+    for (int k = 0; k < 3; ++k) {
+      r.pos[k] = o.pos[k]; r.ext[k] = o.ext[k]; r.first_pos[k] = o.first_pos[k]; r.lo[k] = o.lo[k]; r.hi[k] = o.hi[k];
+      r.trk_pos[k] = o.trk_pos[k]; r.miss_cam[k] = o.miss_cam[k]; r.last_miss_cam[k] = o.last_miss_cam[k];
+      r.last_miss_fwd[k] = o.last_miss_fwd[k]; r.cloud_org[k] = o.cloud.org[k];
+    }
+    r.n_obs = o.n_obs;
+    r.first_seen = o.first_seen;
+    r.last_seen = o.last_seen;
+    r.state = o.state;
+    r.confirmed = o.confirmed;
+    r.moved = o.moved;
+    r.misses = o.misses;
+    r.n_vis_miss = o.n_vis_miss;
+    r.score = o.score;
+    r.max_det_z = o.max_det_z;
+    r.last_kf = o.last_kf;
+    r.gone_t = o.gone_t;
+    r.appeared = o.appeared;
+    r.mv_cnt = o.mv_cnt;
+    r.trk_t = o.trk_t;
+    r.trk_step[0] = o.trk_step[0];
+    r.trk_step[1] = o.trk_step[1];
+    r.moving_t = o.moving_t;
+    r.move_from_t = o.move_from_t;
+    r.first_miss = o.first_miss;
+    r.cloud_n = int(o.cloud.size());
+    r.cloud_version = o.cloud.version;
+    if (o.ap) {
+      const ApState& s = *o.ap;
+      r.ap_ver = s.ver;
+      r.k_frag = s.k_frag;
+      r.k_whole = s.k_whole;
+      r.n_views = int(s.views.size());
+      r.n_ap_obs = s.n_ap_obs;
+      r.n_wall_obs = s.n_wall_obs;
+      r.n_struct_look = s.n_struct_look;
+      r.need_whole = s.need_whole;
+      r.n_whole = s.n_whole;
+      for (int k = 0; k < 3; ++k) r.P[k] = s.P[k];
+      r.n_cams = int(s.cams.size());
+      r.geo = s.geo;
+      r.drop = s.drop;
+      r.hide = s.hide;
+    }
+  }
+  return n;
+}
+
+// objprob vectors of object i: r_frag (D floats), views (up to 5: D fp16 each, kappa, stamp)
+int ref_object_vectors(void* h, int i, float* r_frag, int D, uint16_t* views, float* vkappa, double* vstamp, int vcap) {
+  const auto& objs = static_cast<RefMap*>(h)->om.objects();
+  if (i < 0 || size_t(i) >= objs.size() || !objs[size_t(i)].ap) return -1;
+  const ApState& s = *objs[size_t(i)].ap;
+  if (r_frag) {
+    for (int k = 0; k < D; ++k) r_frag[k] = size_t(k) < s.r_frag.size() ? s.r_frag[size_t(k)] : 0.f;
+  }
+  const int nv = std::min<int>(vcap, int(s.views.size()));
+  for (int v = 0; v < nv; ++v) {
+    const ApView& w = s.views[size_t(v)];
+    if (views) for (int k = 0; k < D; ++k) views[size_t(v) * D + k] = size_t(k) < w.z.size() ? w.z[size_t(k)] : 0;
+    if (vkappa) vkappa[v] = w.kappa;
+    if (vstamp) vstamp[v] = w.stamp;
+  }
+  return nv;
+}
+
+// cloud of object i in map coordinates (float(org + p), as the reference reads it back) and seq
+int ref_object_cloud(void* h, int i, float* xyz, uint32_t* seq, int cap) {
+  const auto& objs = static_cast<RefMap*>(h)->om.objects();
+  if (i < 0 || size_t(i) >= objs.size()) return -1;
+  const MapObject& o = objs[size_t(i)];
+  if (!o.cloud.data) return 0;
+  const auto& pts = o.cloud.data->pts;
+  const int n = std::min<int>(cap, int(pts.size()));
+  for (int k = 0; k < n; ++k) {
+    if (xyz) {
+      xyz[3 * k] = pts[size_t(k)].x;
+      xyz[3 * k + 1] = pts[size_t(k)].y;
+      xyz[3 * k + 2] = pts[size_t(k)].z;
+    }
+    if (seq) seq[k] = pts[size_t(k)].seq;
+  }
+  return int(pts.size());
+}
+
+// per detection: obj_id, n_valid, area_px, depth_med (ObjectMap::lastAssoc)
+int ref_assoc(void* h, uint32_t* obj_id, int32_t* n_valid, float* area_px, float* depth_med, int cap) {
+  const auto& as = static_cast<RefMap*>(h)->om.lastAssoc();
+  const int n = std::min<int>(cap, int(as.size()));
+  for (int k = 0; k < n; ++k) {
+    obj_id[k] = as[size_t(k)].obj_id;
+    n_valid[k] = as[size_t(k)].n_valid;
+    area_px[k] = as[size_t(k)].area_px;
+    depth_med[k] = as[size_t(k)].depth_med;
+  }
+  return int(as.size());
+}
+
+// observation cloud candidates of the last update, in emission order
+int ref_n_points(void* h) { return int(static_cast<RefMap*>(h)->pts.size()); }
+int ref_points(void* h, int j, uint32_t* obj_id, int32_t* det, float* xyz, int32_t* px, int cap) {
+  const auto& P = static_cast<RefMap*>(h)->pts;
+  if (j < 0 || size_t(j) >= P.size()) return -1;
+  const ObsPoints& q = P[size_t(j)];
+  const int n = int(q.px.size() / 2);
+  if (obj_id) *obj_id = q.obj_id;
+  if (det) *det = q.det;
+  for (int k = 0; k < std::min(n, cap); ++k) {
+    if (xyz) for (int c = 0; c < 3; ++c) xyz[3 * k + c] = q.xyz[size_t(3 * k + c)];
+    if (px) for (int c = 0; c < 2; ++c) px[2 * k + c] = q.px[size_t(2 * k + c)];
+  }
+  return n;
+}
+
+void ref_stats(void* h, rf_stats* s) {
+  const ApStats& a = static_cast<RefMap*>(h)->om.apStats();
+  s->n_through = a.n_through; s->n_obs = a.n_obs; s->n_wall = a.n_wall; s->n_wall_name = a.n_wall_name; s->n_ceil = a.n_ceil;
+  s->n_floor = a.n_floor; s->n_assoc = a.n_assoc; s->n_new = a.n_new; s->n_merge = a.n_merge; s->n_obj_struct = a.n_obj_struct;
+  s->n_reenc_req = a.n_reenc_req; s->n_reenc_done = a.n_reenc_done; s->n_blocked = a.n_blocked; s->n_wall_tall = a.n_wall_tall;
+  s->n_so_big = a.n_so_big; s->n_bridge = a.n_bridge;
+}
+
+int ref_n_events(void* h) { return int(static_cast<RefMap*>(h)->om.events().size()); }
+int ref_events(void* h, double* t, uint32_t* id, int32_t* kind, int cap) {
+  const auto& ev = static_cast<RefMap*>(h)->om.events();
+  const int n = std::min<int>(cap, int(ev.size()));
+  for (int k = 0; k < n; ++k) { t[k] = ev[size_t(k)].t; id[k] = ev[size_t(k)].id; kind[k] = ev[size_t(k)].kind; }
+  return int(ev.size());
+}
+
+// keyframe stats of the last frame: inserted, changed_cells, n_hits
+void ref_kf(void* h, int32_t* out3) {
+  const KeyframeStats& k = static_cast<RefMap*>(h)->kf;
+  out3[0] = k.inserted;
+  out3[1] = k.changed_cells;
+  out3[2] = k.n_hits;
+}
+
+// grid geometry (x0, y0, w, h) and per-cell log-odds (1/256 fixed point), seen flag and export8 value
+int ref_grid_geom(void* h, int32_t* g4) {
+  RefMap* m = static_cast<RefMap*>(h);
+  if (!m->mapper) return -1;
+  const OccGrid& G = m->mapper->grid();
+  g4[0] = G.x0(); g4[1] = G.y0(); g4[2] = G.width(); g4[3] = G.height();
+  return 0;
+}
+int ref_grid_cells(void* h, int16_t* L, uint8_t* seen, int8_t* c8) {
+  RefMap* m = static_cast<RefMap*>(h);
+  if (!m->mapper) return -1;
+  const OccGrid& G = m->mapper->grid();
+  const int w = G.width(), hh = G.height();
+  std::vector<int8_t> e = G.export8();
+  for (int y = 0; y < hh; ++y)
+    for (int x = 0; x < w; ++x) {
+      const size_t i = size_t(y) * w + x;
+      const int ix = G.x0() + x, iy = G.y0() + y;
+      if (L) L[i] = int16_t(std::lround(G.logOdds(ix, iy) * OccGrid::kQ));
+      if (seen) seen[i] = G.seen(ix, iy);
+      if (c8) c8[i] = e[i];
+    }
+  return w * hh;
+}
+
+// ---- standalone occupancy grid (config 3) ----
+void* ref_occ_create(const float* grid5) {
+  GridParams p;
+  p.res = grid5[0]; p.l_hit = grid5[1]; p.l_miss = grid5[2]; p.l_min = grid5[3]; p.l_max = grid5[4];
+  return new OccGrid(p);
+}
+void ref_occ_destroy(void* g) { delete static_cast<OccGrid*>(g); }
+// laser hits (hx, hy), free-ray ends (fx, fy), match points (mx, my, mnx, mny) in the base frame
+int ref_occ_insert(void* g, float ox, float oy, const float* hx, const float* hy, int nh, const float* fx, const float* fy, int nf,
+                   const float* mx, const float* my, const float* mnx, const float* mny, int nm, const double* pose3) {
+  Scan2 s;
+  s.ox = ox; s.oy = oy;
+  s.hx.assign(hx, hx + nh); s.hy.assign(hy, hy + nh);
+  s.fx.assign(fx, fx + nf); s.fy.assign(fy, fy + nf);
+  s.mx.assign(mx, mx + nm); s.my.assign(my, my + nm);
+  if (mnx && mny) { s.mnx.assign(mnx, mnx + nm); s.mny.assign(mny, mny + nm); }
+  return static_cast<OccGrid*>(g)->insert(s, Pose2{pose3[0], pose3[1], pose3[2]});
+}
+void ref_occ_geom(void* g, int32_t* g4) {
+  const OccGrid& G = *static_cast<OccGrid*>(g);
+  g4[0] = G.x0(); g4[1] = G.y0(); g4[2] = G.width(); g4[3] = G.height();
+}
+void ref_occ_cells(void* g, int16_t* L, uint8_t* seen, int8_t* c8, float* prob) {
+  const OccGrid& G = *static_cast<OccGrid*>(g);
+  std::vector<int8_t> e = G.export8();
+  for (int y = 0; y < G.height(); ++y)
+    for (int x = 0; x < G.width(); ++x) {
+      const size_t i = size_t(y) * G.width() + x;
+      const int ix = G.x0() + x, iy = G.y0() + y;
+      if (L) L[i] = int16_t(std::lround(G.logOdds(ix, iy) * OccGrid::kQ));
+      if (seen) seen[i] = G.seen(ix, iy);
+      if (c8) c8[i] = e[i];
+      if (prob) prob[i] = G.prob(ix, iy);
+    }
+}
+
+// ---- makeScan on one depth frame (no body capsules, no attach filter) ----
+// out sizes: returns nh, nf, nm in n3; arrays must hold 720 / 720 / 12288 entries.
+int ref_make_scan(int w, int h, const float* depth, float fx, float fy, float cx, float cy, const float* T_bc, const float* eef_base6,
+                  float* hx, float* hy, float* fxo, float* fyo, float* mx, float* my, float* mnx, float* mny, int16_t* sig, float sig_cell,
+                  int32_t* n3, float* oxy) {
+  DepthView dv;
+  dv.w = w; dv.h = h; dv.m = depth;
+  dv.step = std::max(1, int(std::lround(w / 160.0)));
+  dv.fx = fx; dv.fy = fy; dv.cx = cx; dv.cy = cy;
+  memcpy(dv.T_bc, T_bc, sizeof(dv.T_bc));
+  BodyState b;
+  for (int s = 0; s < 2; ++s) for (int k = 0; k < 3; ++k) b.eef[s][k] = eef_base6[3 * s + k];
+  ScanParams p;
+  Scan2 out;
+  ScanWork W;
+  makeScan(dv, b, p, &out, nullptr, nullptr, &W, sig_cell);
+  n3[0] = int(out.hx.size()); n3[1] = int(out.fx.size()); n3[2] = int(out.mx.size());
+  for (size_t k = 0; k < out.hx.size(); ++k) { hx[k] = out.hx[k]; hy[k] = out.hy[k]; }
+  for (size_t k = 0; k < out.fx.size(); ++k) { fxo[k] = out.fx[k]; fyo[k] = out.fy[k]; }
+  for (size_t k = 0; k < out.mx.size(); ++k) { mx[k] = out.mx[k]; my[k] = out.my[k]; mnx[k] = out.mnx[k]; mny[k] = out.mny[k]; }
+  if (sig) for (size_t k = 0; k < out.sig.size(); ++k) sig[k] = out.sig[k];
+  oxy[0] = out.ox; oxy[1] = out.oy;
+  return 0;
+}
+
+// ---- objprob primitives (known-answer pins for the restatement and the kernels) ----
+int ref_plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_iters, double* out /* ok,n0,n1,n2,thick,inl,zmed,zlo,zhi,hspan */) {
+  const ApPlane p = apPlaneFit(xyz, n, tau, seed, max_iters);
+  out[0] = p.ok; out[1] = p.n[0]; out[2] = p.n[1]; out[3] = p.n[2]; out[4] = p.thick; out[5] = p.inl; out[6] = p.zmed; out[7] = p.zlo;
+  out[8] = p.zhi; out[9] = p.hspan;
+  return p.ok;
+}
+uint64_t ref_ap_seed(uint64_t a, uint64_t b) { return apSeed(a, b); }
+void ref_to_f16(const float* in, uint16_t* out, int n) { apToF16(in, out, n); }
+uint64_t ref_voxel_key(float x, float y, float z, float inv) { return voxelKey(x, y, z, inv); }
+double ref_contact(const float* cloud, int nc, const float* pts, int np, double cell) {
+  ApContactIdx idx;
+  apBuildContact(cloud, nc, cell, &idx);
+  return apContact(pts, np, idx, cell);
+}
+
+}  // extern "C"

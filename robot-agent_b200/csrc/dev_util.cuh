@@ -1,0 +1,400 @@
+// Device helpers: block-wide reductions / scans / exact k-th selection, hashing, and the
+// scalar formulas of the reference's objprob math (scenemap include/scenemap/objprob_math.h)
+// restated for the device.  Compiled with --fmad=false so that every float/double expression
+// rounds exactly like the reference's host build (baseline x86-64, no FMA contraction).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "smg_internal.h"
+
+#define DEV __device__ __forceinline__
+
+// ---------------------------------------------------------------- block primitives
+// All helpers assume blockDim.x is a multiple of 32 and <= 1024, and that every thread of the
+// block calls them (they contain __syncthreads).
+
+struct BlockScratch {
+  double d[32];
+  long long ll[32];
+  int i[33];
+};
+
+DEV double warp_sum_d(double v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+DEV long long warp_sum_ll(long long v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+DEV int warp_sum_i(int v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+DEV double warp_max_d(double v) {
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+DEV double warp_min_d(double v) {
+  for (int o = 16; o > 0; o >>= 1) v = fmin(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// deterministic block sum (fixed tree for a given blockDim)
+DEV double block_sum_d(double v, BlockScratch& s) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) s.d[wid] = v;
+  __syncthreads();
+  double r = 0;
+  if (wid == 0) {
+    r = lane < nw ? s.d[lane] : 0.0;
+    r = warp_sum_d(r);
+    if (lane == 0) s.d[0] = r;
+  }
+  __syncthreads();
+  r = s.d[0];
+  __syncthreads();
+  return r;
+}
+DEV long long block_sum_ll(long long v, BlockScratch& s) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum_ll(v);
+  __syncthreads();
+  if (lane == 0) s.ll[wid] = v;
+  __syncthreads();
+  long long r = 0;
+  if (wid == 0) {
+    r = lane < nw ? s.ll[lane] : 0;
+    r = warp_sum_ll(r);
+    if (lane == 0) s.ll[0] = r;
+  }
+  __syncthreads();
+  r = s.ll[0];
+  __syncthreads();
+  return r;
+}
+DEV int block_sum_i(int v, BlockScratch& s) { return (int)block_sum_ll(v, s); }
+DEV double block_max_d(double v, BlockScratch& s) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max_d(v);
+  __syncthreads();
+  if (lane == 0) s.d[wid] = v;
+  __syncthreads();
+  double r = -1e308;
+  if (wid == 0) {
+    r = lane < nw ? s.d[lane] : -1e308;
+    r = warp_max_d(r);
+    if (lane == 0) s.d[0] = r;
+  }
+  __syncthreads();
+  r = s.d[0];
+  __syncthreads();
+  return r;
+}
+DEV double block_min_d(double v, BlockScratch& s) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_min_d(v);
+  __syncthreads();
+  if (lane == 0) s.d[wid] = v;
+  __syncthreads();
+  double r = 1e308;
+  if (wid == 0) {
+    r = lane < nw ? s.d[lane] : 1e308;
+    r = warp_min_d(r);
+    if (lane == 0) s.d[0] = r;
+  }
+  __syncthreads();
+  r = s.d[0];
+  __syncthreads();
+  return r;
+}
+
+// Exclusive scan of a 0/1 (or small int) flag across the block; returns the prefix for this
+// thread and writes the block total to *total.  Order = thread order (used for ordered
+// stream compaction: chunk c covers elements c*blockDim .. c*blockDim+blockDim-1).
+DEV int block_excl_scan(int flag, int* total, BlockScratch& s) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = flag;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) s.i[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int w = lane < nw ? s.i[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) s.i[lane] = w;   // inclusive per-warp totals
+  }
+  __syncthreads();
+  const int before = wid > 0 ? s.i[wid - 1] : 0;
+  *total = s.i[nw - 1];
+  __syncthreads();
+  return before + x - flag;
+}
+
+// order-preserving double <-> uint64 map (total order, -0.0 < +0.0)
+DEV uint64_t d_ord(double v) {
+  const uint64_t u = (uint64_t)__double_as_longlong(v);
+  return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
+DEV double d_unord(uint64_t k) {
+  const uint64_t u = (k >> 63) ? (k & 0x7fffffffffffffffull) : ~k;
+  return __longlong_as_double((long long)u);
+}
+
+// Exact k-th smallest (0-based) of a[0..n) by MSB-first radix selection on the ordered bit
+// pattern: returns exactly the value std::nth_element leaves at position k.
+// hist: 256 shared ints.  All threads of the block must call it.
+DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& s) {
+  uint64_t prefix = 0, mask = 0;
+  for (int pass = 0; pass < 8; ++pass) {
+    const int shift = 56 - 8 * pass;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint64_t key = d_ord(a[i]);
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      int c[8], tot = 0;
+      for (int j = 0; j < 8; ++j) { c[j] = hist[lane * 8 + j]; tot += c[j]; }
+      int incl = tot;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int excl = incl - tot;
+      if (k >= excl && k < incl) {
+        int kk = k - excl, b = 0;
+        for (int j = 0; j < 8; ++j) {
+          if (kk < c[j]) { b = j; break; }
+          kk -= c[j];
+        }
+        s.i[0] = lane * 8 + b;
+        s.i[1] = kk;
+      }
+    }
+    __syncthreads();
+    const int sel = s.i[0];
+    k = s.i[1];
+    __syncthreads();
+    prefix |= (uint64_t)sel << shift;
+    mask |= 0xffull << shift;
+  }
+  return d_unord(prefix);
+}
+
+// ---------------------------------------------------------------- hashing / keys
+// splitmix64 step and seed mixing (scenemap objprob.cpp:116-128)
+DEV uint64_t splitmix(uint64_t& s) {
+  uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+DEV uint64_t ap_seed(uint64_t a, uint64_t b) {
+  uint64_t s = a * 0x9E3779B97F4A7C15ull ^ (b + 0x632BE59BD9B4E019ull);
+  return splitmix(s);
+}
+// 21-bit packed voxel key of float coordinates (scenemap cloud.cpp:66-69)
+DEV uint64_t voxel_key(float x, float y, float z, float inv) {
+  const uint64_t qx = (uint64_t)((long long)floorf(x * inv) + (1 << 20)) & 0x1FFFFFull;
+  const uint64_t qy = (uint64_t)((long long)floorf(y * inv) + (1 << 20)) & 0x1FFFFFull;
+  const uint64_t qz = (uint64_t)((long long)floorf(z * inv) + (1 << 20)) & 0x1FFFFFull;
+  return qx | qy << 21 | qz << 42;
+}
+// 21-bit packed contact-cell key (scenemap objprob.cpp:92-95)
+DEV uint64_t cell_key3(long long i, long long j, long long k) {
+  return ((uint64_t)(i + (1 << 20)) & 0x1FFFFFull) | ((uint64_t)(j + (1 << 20)) & 0x1FFFFFull) << 21 |
+         ((uint64_t)(k + (1 << 20)) & 0x1FFFFFull) << 42;
+}
+// 64-bit mixer for open addressing (device-side tables only; not a reference structure)
+DEV uint32_t hmix(uint64_t k) {
+  k ^= k >> 33;
+  k *= 0xff51afd7ed558ccdull;
+  k ^= k >> 33;
+  k *= 0xc4ceb9fe1a85ec53ull;
+  k ^= k >> 33;
+  return (uint32_t)k;
+}
+
+// float -> fp16 bits with the reference's own rounding (scenemap objprob.cpp:12-29): round half
+// up on the mantissa, small numbers flushed per its subnormal rule.  Integer-only, bit-exact.
+DEV uint16_t ref_f2h(float f) {
+  const uint32_t x = __float_as_uint(f);
+  const uint32_t sign = (x >> 16) & 0x8000u;
+  int32_t e = (int32_t)((x >> 23) & 0xff) - 127 + 15;
+  uint32_t m = x & 0x7fffffu;
+  if (e <= 0) {
+    if (e < -10) return (uint16_t)sign;
+    m |= 0x800000u;
+    const int sh = 14 - e;
+    return (uint16_t)(sign | ((m + (1u << (sh - 1))) >> sh));
+  }
+  if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+  const uint32_t r = m + 0x1000u;
+  if (r & 0x800000u) {
+    m = 0;
+    ++e;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+  } else {
+    m = r;
+  }
+  return (uint16_t)(sign | ((uint32_t)e << 10) | (m >> 13));
+}
+// fp16 bits -> float (scenemap objprob.cpp:31-47; exact widening)
+DEV float ref_h2f(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ffu, x;
+  if (e == 0) {
+    if (m == 0) {
+      x = sign;
+    } else {
+      e = 127 - 15 + 1;
+      while (!(m & 0x400u)) { m <<= 1; --e; }
+      m &= 0x3ffu;
+      x = sign | (e << 23) | (m << 13);
+    }
+  } else if (e == 31) {
+    x = sign | 0x7f800000u | (m << 13);
+  } else {
+    x = sign | ((e + 127 - 15) << 23) | (m << 13);
+  }
+  return __uint_as_float(x);
+}
+
+DEV float emb_at(const void* emb, int dtype, int D, int k, int i) {
+  if (dtype == SMG_EMB_BF16) {
+    const uint16_t b = ((const uint16_t*)emb)[(size_t)k * D + i];
+    return __uint_as_float((uint32_t)b << 16);
+  }
+  return ((const float*)emb)[(size_t)k * D + i];
+}
+
+// ---------------------------------------------------------------- objprob scalar math
+// (scenemap include/scenemap/objprob_math.h, T = double)
+// opm::max2/min2/max3 (objprob_math.h:16-18)
+DEV double dmax2(double a, double b) { return a > b ? a : b; }
+DEV double dmin2(double a, double b) { return a < b ? a : b; }
+DEV double dmax3(double a, double b, double c) { return dmax2(dmax2(a, b), c); }
+// std::max / std::min (returns the first argument on ties, like <algorithm>)
+DEV double smax(double a, double b) { return (a < b) ? b : a; }
+DEV double smin(double a, double b) { return (b < a) ? b : a; }
+// std::max({0.0, a, b}) (first largest of an initializer list)
+DEV double smax3(double a, double b, double c) { double r = a; if (r < b) r = b; if (r < c) r = c; return r; }
+
+// objprob_math.h:25-30
+DEV double same_logit(const double w[8], const double f[7]) {
+  double v = w[0];
+  for (int k = 0; k < 7; ++k) v += w[k + 1] * f[k];
+  if (f[5] > 0) v = -30.0;
+  return v;
+}
+DEV double sigmoid(double x) { return 1.0 / (1.0 + exp(-x)); }
+
+// objprob_math.h:34-45 (da boxOverlap, da/src/merge.cpp:8-20)
+DEV double box_overlap(const double alo[3], const double ahi[3], const double blo[3], const double bhi[3], double min_ext) {
+  double r = 1.0;
+  for (int k = 0; k < 3; ++k) {
+    const double ca = 0.5 * (alo[k] + ahi[k]), cb = 0.5 * (blo[k] + bhi[k]);
+    const double ha = 0.5 * dmax2(ahi[k] - alo[k], min_ext), hb = 0.5 * dmax2(bhi[k] - blo[k], min_ext);
+    const double ov = dmin2(ca + ha, cb + hb) - dmax2(ca - ha, cb - hb);
+    const double f = ov <= 0 ? 0.0 : dmin2(1.0, ov / (2.0 * dmin2(ha, hb)));
+    r *= f;
+    if (r <= 0) return 0.0;
+  }
+  return r;
+}
+
+// objprob_math.h:49-74
+DEV void pair_geo(const double alo[3], const double ahi[3], const double apos[3], const double blo[3], const double bhi[3],
+                  const double bpos[3], double cs, double cos0, double f[7]) {
+  double g2 = 0;
+  for (int k = 0; k < 3; ++k) {
+    const double g = dmax3(0.0, alo[k] - bhi[k], blo[k] - ahi[k]);
+    g2 += g * g;
+  }
+  f[1] = sqrt(g2);
+  const double ea = dmax3(ahi[0] - alo[0], ahi[1] - alo[1], ahi[2] - alo[2]);
+  const double eb = dmax3(bhi[0] - blo[0], bhi[1] - blo[1], bhi[2] - blo[2]);
+  const double dd = sqrt((apos[0] - bpos[0]) * (apos[0] - bpos[0]) + (apos[1] - bpos[1]) * (apos[1] - bpos[1]) +
+                         (apos[2] - bpos[2]) * (apos[2] - bpos[2]));
+  f[2] = dd / (0.5 * (ea + eb) + 0.05);
+  f[3] = cs > -1.5 ? cs - cos0 : 0.0;
+  f[4] = box_overlap(alo, ahi, blo, bhi, 0.05);
+  const bool a_small = ea < eb;
+  const double *slo = a_small ? alo : blo, *shi = a_small ? ahi : bhi, *llo = a_small ? blo : alo, *lhi = a_small ? bhi : ahi;
+  const double es = dmin2(ea, eb), el = dmax2(ea, eb);
+  f[5] = 0.0;
+  if (es < 0.6 * el) {
+    const double cx = 0.5 * (slo[0] + shi[0]), cy = 0.5 * (slo[1] + shi[1]);
+    const bool inside = cx > llo[0] - 0.05 && cx < lhi[0] + 0.05 && cy > llo[1] - 0.05 && cy < lhi[1] + 0.05;
+    const double dz = slo[2] - lhi[2];
+    if (inside && (dz < 0 ? -dz : dz) < 0.08) f[5] = 1.0;
+  }
+}
+
+// objprob_math.h:78-87 with occ/blur handled by the caller-provided factors
+DEV double view_kappa(double size_px, bool trunc, double depth, double k0, double s0, double trunc_k, double d0, double occ,
+                      double blur_w, double blur_fac) {
+  const double s = dmax2(0.0, size_px), d = dmax2(0.0, depth);
+  double k = k0 * s / (s + s0);
+  if (trunc) k *= trunc_k;
+  k /= 1.0 + (d / d0) * (d / d0);
+  k *= pow(1.0, occ);   // vis = 1 for detection fragments: pow(1, y) == 1 exactly
+  if (blur_w > 0) k *= blur_fac;
+  return dmax2(k, 1e-3);
+}
+
+// objprob_math.h:139-156
+DEV double kalman_gain(double& P, double q, double dt, double R) {
+  P += q * dmax2(0.0, dt);
+  const double K = P / (P + R);
+  P *= 1.0 - K;
+  return K;
+}
+DEV double kalman_R(double r0, double r1, double depth, bool trunc, double ext) {
+  const double sd = r0 + r1 * depth;
+  return sd * sd + (trunc ? 0.25 * ext * ext : 0.0);
+}
+DEV void kalman_big(double& P, double q, double dt, double sd, double ext) {
+  const double R = sd * sd + 0.0625 * ext * ext;
+  P = 1.0 / (1.0 / (P + q * dmax2(0.0, dt)) + 1.0 / R);
+}
+DEV double merge_var(double a, double b) { return 1.0 / (1.0 / dmax2(a, 1e-9) + 1.0 / dmax2(b, 1e-9)); }
+
+// 3-argument hypot by scaling with the largest magnitude
+DEV double hypot3(double x, double y, double z) {
+  x = fabs(x); y = fabs(y); z = fabs(z);
+  const double a = dmax3(x, y, z);
+  if (a == 0.0) return 0.0;
+  x /= a; y /= a; z /= a;
+  return a * sqrt(x * x + y * y + z * z);
+}
+DEV double dist3(const double* a, const double* b) {
+  return sqrt((a[0] - b[0]) * (a[0] - b[0]) + (a[1] - b[1]) * (a[1] - b[1]) + (a[2] - b[2]) * (a[2] - b[2]));
+}
+
+DEV void set_err(MapRec* m, int bit) { atomicOr(&m->err, bit); }
+
+// event in program order: key = phase << 24 | position
+DEV void push_event(const Batch& B, int map, double t, const ObjRec& o, int kind, uint32_t key) {
+  MapRec* M = &B.maps[map];
+  const int e = atomicAdd(&M->n_events, 1);
+  if (e >= SMG_MAX_EVENTS) { set_err(M, SMG_E_CAP_EVENTS); return; }
+  EventRec& r = B.events[(size_t)map * SMG_MAX_EVENTS + e];
+  r.t = t;
+  r.id = o.id;
+  r.kind = kind;
+  r.key = key;
+}

@@ -1,0 +1,177 @@
+// Association of observations with memory objects (scenemap src/objmap.cpp:767-810) and the
+// pair primitives shared with the merge pass: apCosMax (objprob.cpp:266-285), apContact
+// (objprob.cpp:489-504), pairFeatures (objmap.cpp:86-96).
+//
+// One CTA per (observation, map).  Warps take objects in list order; the box-gap gate is
+// evaluated first, and only gate-passing pairs pay for the D-length cosines (double
+// accumulation of the fp32 r-vector and the fp16 views against the fp32 detection embedding)
+// and the 27-neighbour contact probes of <= 2*contact_samples points.  The per-object P values
+// are reduced in list order (first maximum wins, P > same_p), like the reference loop.
+#pragma once
+#include "dev_util.cuh"
+
+#define ASSOC_THREADS 256
+#define SP_MAX 1024
+
+DEV const ObjRec& obj_at(const Batch& B, int m, int pos) { return B.objs[(size_t)m * B.O + B.order[(size_t)m * B.O + pos]]; }
+DEV int slot_at(const Batch& B, int m, int pos) { return B.order[(size_t)m * B.O + pos]; }
+DEV size_t oglob(const Batch& B, int m, int slot) { return (size_t)m * B.O + slot; }
+
+// contact-cell set membership (ApContactIdx keys, generation-tagged open addressing)
+DEV bool contact_has(const Batch& B, size_t cs, uint32_t gen, uint64_t key) {
+  const uint64_t* K = B.ckey + cs * B.HCC;
+  const uint32_t* G = B.cgen + cs * B.HCC;
+  uint32_t h = hmix(key) & (uint32_t)(B.HCC - 1);
+  for (int probe = 0; probe < B.HCC; ++probe) {
+    if (G[h] != gen) return false;
+    if (K[h] == key) return true;
+    h = (h + 1) & (uint32_t)(B.HCC - 1);
+  }
+  return false;
+}
+
+// apContact: number of the n sample points (float xyz) whose 27-neighbourhood of `cell` cells
+// touches the cloud's contact set.  Warp-level; returns the hit count on every lane.
+DEV int contact_hits_warp(const Batch& B, size_t cs, const float* sp, int n, double cell) {
+  const CloudRec& C = B.clouds[cs];
+  if (n <= 0 || C.cn <= 0) return 0;
+  const double inv = 1.0 / cell;
+  const int lane = threadIdx.x & 31;
+  int hit = 0;
+  for (int i = lane; i < n; i += 32) {
+    const long long a = (long long)floor((double)sp[3 * i] * inv), b = (long long)floor((double)sp[3 * i + 1] * inv),
+                    c = (long long)floor((double)sp[3 * i + 2] * inv);
+    if (a < C.clo[0] - 1 || a > C.chi[0] + 1 || b < C.clo[1] - 1 || b > C.chi[1] + 1 || c < C.clo[2] - 1 || c > C.chi[2] + 1) continue;
+    bool h = false;
+    for (int dx = -1; dx <= 1 && !h; ++dx)
+      for (int dy = -1; dy <= 1 && !h; ++dy)
+        for (int dz = -1; dz <= 1 && !h; ++dz) h = contact_has(B, cs, C.cgen, cell_key3(a + dx, b + dy, c + dz));
+    hit += h;
+  }
+  return warp_sum_i(hit);
+}
+
+DEV const float* rfrag_of(const Batch& B, size_t og) { return B.rfrag + og * B.D; }
+DEV const uint16_t* view_of(const Batch& B, size_t og, int phys) { return B.views + (og * (B.topk + 1) + phys) * B.D; }
+
+// apCosMax of object o against the fp32 vector z (shared or global), warp-level: the fragment
+// mean direction r_frag/|r_frag| and each stored fp16 view; returns the max on every lane.
+DEV double cos_max_warp(const Batch& B, size_t og, const ObjRec& o, const float* z) {
+  const int lane = threadIdx.x & 31, D = B.D;
+  double best = -1;
+  if (o.nrm_frag > 0) {
+    const float* r = rfrag_of(B, og);
+    double dot = 0;
+    for (int i = lane; i < D; i += 32) dot += (double)r[i] * (double)z[i];
+    dot = warp_sum_d(dot);
+    best = smax(best, dot / sqrt(o.nrm_frag));
+  }
+  for (int v = 0; v < o.n_views; ++v) {
+    const uint16_t* q = view_of(B, og, o.view_slot[v]);
+    double dot = 0;
+    for (int i = lane; i < D; i += 32) dot += (double)ref_h2f(q[i]) * (double)z[i];
+    dot = warp_sum_d(dot);
+    best = smax(best, dot);
+  }
+  return best;
+}
+
+// pairFeatures -> P (objmap.cpp:86-96): f0 = contact fraction, f1..f5 = pair_geo, logit, sigmoid
+DEV double pair_p(const double alo[3], const double ahi[3], const double apos[3], double contact, const double blo[3],
+                  const double bhi[3], const double bpos[3], double cs, const smg_params& P, bool merge, double* f0_out) {
+  double f[7] = {0, 0, 0, 0, 0, 0, 0};
+  f[0] = contact;
+  pair_geo(alo, ahi, apos, blo, bhi, bpos, cs, P.cos0, f);
+  if (f0_out) *f0_out = f[0];
+  return sigmoid(same_logit(merge ? P.wm : P.w, f));
+}
+
+__global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
+  extern __shared__ unsigned char smem_raw[];
+  float* zs = (float*)smem_raw;                   // D
+  float* sp = zs + B.D;                           // 3 * SP_MAX
+  double* pp = (double*)(smem_raw + (((size_t)B.D * 4 + SP_MAX * 12 + 7) & ~(size_t)7));   // O
+  __shared__ BlockScratch bs;
+  const int a = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+  const FrameDev& F = B.frames[m];
+  const MapRec& R = B.maps[m];
+  if (!F.active || a >= R.n_obs) return;
+  const smg_params& P = B.p;
+  const int det = B.obs_list[(size_t)m * B.max_det + a];
+  ObsRec* O = &B.obs[(size_t)m * B.max_det + det];
+  const bool has_z = F.emb != nullptr;
+  for (int i = tid; i < B.D; i += blockDim.x) zs[i] = has_z ? emb_at(F.emb, F.emb_dtype, B.D, det, i) : 0.f;
+  // contact sample of the observation's cloud candidates (objmap.cpp:776-779)
+  const int nc = O->nc;
+  const int stp = max(1, nc / max(8, P.contact_samples));
+  const int nsp = nc > 0 ? (nc + stp - 1) / stp : 0;
+  if (nsp > SP_MAX) {
+    if (tid == 0) set_err(&B.maps[m], SMG_E_ARGS);
+    return;
+  }
+  const float* CX = B.cxyz + ((size_t)m * B.max_det + det) * 3 * B.pmax;
+  for (int i = tid; i < nsp; i += blockDim.x) {
+    sp[3 * i] = CX[3 * (size_t)i * stp];
+    sp[3 * i + 1] = CX[3 * (size_t)i * stp + 1];
+    sp[3 * i + 2] = CX[3 * (size_t)i * stp + 2];
+  }
+  __syncthreads();
+  const int nobj = R.n_obj;
+  const int lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const double gate2 = P.gate * P.gate;
+  for (int b = wid; b < nobj; b += nw) {
+    const int slot = slot_at(B, m, b);
+    const size_t og = oglob(B, m, slot);
+    const ObjRec& ob = B.objs[og];
+    double g2 = 0;
+    for (int k = 0; k < 3; ++k) {
+      const double g = smax3(0.0, O->lo[k] - ob.hi[k], ob.lo[k] - O->hi[k]);
+      g2 += g * g;
+    }
+    if (g2 > gate2) {
+      if (lane == 0) pp[b] = -1.0;
+      continue;
+    }
+    const double cs = has_z ? cos_max_warp(B, og, ob, zs) : -2.0;
+    const size_t cslot = oglob(B, m, ob.cloud_slot);
+    const int hits = contact_hits_warp(B, cslot, sp, nsp, P.contact_cell);
+    if (lane == 0) {
+      const double contact = (nsp > 0 && B.clouds[cslot].cn > 0) ? (double)hits / (double)nsp : 0.0;
+      double f0;
+      const double p = pair_p(O->lo, O->hi, O->pos, contact, ob.lo, ob.hi, ob.pos, cs, P, false, &f0);
+      if (f0 >= 0.3 || p >= 0.2) B.touched[(size_t)m * B.O + b] = 1;
+      pp[b] = p;
+    }
+  }
+  __syncthreads();
+  // first maximum in list order with P > same_p; count P >= same_p (objmap.cpp:780-806)
+  double bp = -2.0;
+  int bi = -1, ns = 0;
+  for (int b = tid; b < nobj; b += blockDim.x) {
+    const double p = pp[b];
+    ns += p >= P.same_p;
+    if (p > bp) { bp = p; bi = b; }
+  }
+  // combine (max p, then smallest index)
+  for (int o = 16; o > 0; o >>= 1) {
+    const double p2 = __shfl_xor_sync(0xffffffffu, bp, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (p2 > bp || (p2 == bp && i2 >= 0 && (bi < 0 || i2 < bi))) { bp = p2; bi = i2; }
+  }
+  __shared__ double wbp[32];
+  __shared__ int wbi[32];
+  if (lane == 0) { wbp[wid] = bp; wbi[wid] = bi; }
+  const int nsame = block_sum_i(ns, bs);
+  if (tid == 0) {
+    double best = P.same_p;
+    int to = -1;
+    double mp = -2.0;
+    int mi = -1;
+    for (int w = 0; w < nw; ++w)
+      if (wbp[w] > mp || (wbp[w] == mp && wbi[w] >= 0 && (mi < 0 || wbi[w] < mi))) { mp = wbp[w]; mi = wbi[w]; }
+    if (mi >= 0 && mp > best) to = mi;
+    O->obs_to = to;
+    O->n_same = nsame;
+    O->blocked = 0;
+  }
+}

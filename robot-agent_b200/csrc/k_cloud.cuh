@@ -1,0 +1,278 @@
+// Object point clouds: ObjCloud::add (scenemap src/cloud.cpp:86-127) and the contact-cell index
+// (apBuildContact, objprob.cpp:470-487), as block-wide device functions.
+//
+// Cloud slot layout: cpts[2*cap] float4 (x, y, z relative to org, seq as bits), crgb[2*cap]
+// (room for the points of one call before the trim), a persistent voxel-key -> index hash
+// (generation-tagged, HC >= 2 * 2*cap slots) and the contact-cell set (HCC >= 2*cap slots).
+// An add call keeps the reference's sequential semantics: a key new to the cloud is appended at
+// its FIRST occurrence in the call, and every voxel keeps the data of the LAST point that hit it.
+// The call is parallel: a per-call hash of the call's keys records first/last occurrence, first
+// occurrences of new keys are appended by an ordered compaction.
+#pragma once
+#include "k_update.cuh"
+
+struct CloudCall {
+  unsigned long long key;
+  uint32_t first, last;
+};
+
+// per-CTA work area (global): call hash, keys, destinations, trim buffers
+struct Work {
+  CloudCall* tab;   // 4 * WORK_N (a call of n <= WORK_N points uses pow2 >= 2n slots)
+  uint64_t* keys;   // WORK_N
+  int32_t* dst;     // WORK_N
+  double* scr;      // WORK_N
+  float4* t4;       // WORK_N
+  uint32_t* tc;     // WORK_N
+};
+
+DEV Work work_at(const Batch& B, int m, int j) {
+  unsigned char* w = B.work + ((size_t)m * WORK_SLOTS + j) * B.work_stride;
+  Work r;
+  const size_t N = (size_t)B.work_n;
+  r.tab = (CloudCall*)w;
+  r.keys = (uint64_t*)(w + 4 * N * sizeof(CloudCall));
+  r.dst = (int32_t*)(r.keys + N);
+  r.scr = (double*)(r.dst + N + (N & 1));
+  r.t4 = (float4*)(r.scr + N);
+  r.tc = (uint32_t*)(r.t4 + N);
+  return r;
+}
+
+DEV int voxel_lookup(const Batch& B, size_t cs, uint32_t gen, uint64_t key) {
+  const uint64_t* K = B.chkey + cs * B.HC;
+  const uint32_t* G = B.chgen + cs * B.HC;
+  const uint32_t* I = B.chidx + cs * B.HC;
+  uint32_t h = hmix(key) & (uint32_t)(B.HC - 1);
+  for (int probe = 0; probe < B.HC; ++probe) {
+    if (G[h] != gen) return -1;
+    if (K[h] == key) return (int)I[h];
+    h = (h + 1) & (uint32_t)(B.HC - 1);
+  }
+  return -1;
+}
+// insert a key known to be absent (keys inserted concurrently are distinct)
+DEV void voxel_insert(const Batch& B, size_t cs, uint32_t gen, uint64_t key, uint32_t idx) {
+  uint64_t* K = B.chkey + cs * B.HC;
+  uint32_t* G = B.chgen + cs * B.HC;
+  uint32_t* I = B.chidx + cs * B.HC;
+  uint32_t h = hmix(key) & (uint32_t)(B.HC - 1);
+  for (int probe = 0; probe < B.HC; ++probe) {
+    const uint32_t g = G[h];
+    if (g != gen && atomicCAS(&G[h], g, gen) == g) {
+      K[h] = key;
+      I[h] = idx;
+      return;
+    }
+    if (g == gen || G[h] == gen) h = (h + 1) & (uint32_t)(B.HC - 1);
+  }
+}
+
+DEV uint32_t pack_rgb(const uint8_t* rgb, int i) {
+  return rgb ? ((uint32_t)rgb[3 * i] | (uint32_t)rgb[3 * i + 1] << 8 | (uint32_t)rgb[3 * i + 2] << 16) : (128u | 128u << 8 | 128u << 16);
+}
+
+// cap trim (cloud.cpp:114-123): keep the max(1, cap*9/10) newest points by seq in their
+// original order; among points whose seq equals the cut value the highest indices are kept
+// (std::nth_element leaves which of the tied points survive, and their order, unspecified).
+DEV void cloud_trim(const Batch& B, size_t cs, const Work& W, int* hist, BlockScratch& bs) {
+  CloudRec& C = B.clouds[cs];
+  const int cap = B.p.cloud_cap;
+  const int n = C.n;
+  if (cap <= 0 || n <= cap) return;
+  const int keep = max(1, cap * 9 / 10), drop = n - keep;
+  float4* pts = B.cpts + cs * B.cap;
+  uint32_t* col = B.crgb + cs * B.cap;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) W.scr[i] = (double)__float_as_uint(pts[i].w);
+  __syncthreads();
+  const double cut = block_select(W.scr, n, drop, hist, bs);
+  int lt = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) lt += W.scr[i] < cut;
+  const int eq_drop = drop - block_sum_i(lt, bs);
+  int w = 0, eq_seen = 0;
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int i = c0 + threadIdx.x;
+    const int is_eq = i < n && W.scr[i] == cut;
+    int toteq;
+    const int peq = block_excl_scan(is_eq, &toteq, bs);
+    const int k = i < n && (W.scr[i] > cut || (is_eq && eq_seen + peq >= eq_drop));
+    int tot;
+    const int pos = block_excl_scan(k, &tot, bs);
+    if (k) { W.t4[w + pos] = pts[i]; W.tc[w + pos] = col[i]; }
+    w += tot;
+    eq_seen += toteq;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < w; i += blockDim.x) { pts[i] = W.t4[i]; col[i] = W.tc[i]; }
+  __shared__ uint32_t sh_gen;
+  if (threadIdx.x == 0) { C.n = w; sh_gen = ++C.vgen; }
+  __syncthreads();
+  for (int i = threadIdx.x; i < w; i += blockDim.x)
+    voxel_insert(B, cs, sh_gen, voxel_key(pts[i].x, pts[i].y, pts[i].z, B.inv_vox_cloud), (uint32_t)i);
+  __syncthreads();
+}
+
+// ObjCloud::add of n map-frame points (float xyz, optional rgb).  Block-wide.
+DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uint8_t* rgb, int n, double stamp, const Work& W,
+                   int* hist, BlockScratch& bs) {
+  if (n <= 0) return;
+  CloudRec& C = B.clouds[cs];
+  const int tid = threadIdx.x;
+  if (n > B.work_n) {
+    if (tid == 0) set_err(&B.maps[m], SMG_E_CAP_PTS);
+    return;
+  }
+  __shared__ uint32_t sh_seq, sh_vgen;
+  __shared__ double sh_org[3];
+  __shared__ int sh_base;
+  if (tid == 0) {
+    if (!C.has_org) {
+      for (int k = 0; k < 3; ++k) C.org[k] = (double)xyz[k];
+      C.has_org = 1;
+    }
+    sh_seq = ++C.seq;
+    sh_vgen = C.vgen;
+    sh_base = C.n;
+    for (int k = 0; k < 3; ++k) sh_org[k] = C.org[k];
+  }
+  int hs = 1;
+  while (hs < 2 * n) hs <<= 1;
+  for (int i = tid; i < hs; i += blockDim.x) { W.tab[i].key = ~0ull; W.tab[i].first = 0xffffffffu; W.tab[i].last = 0; }
+  __syncthreads();
+  const float inv = B.inv_vox_cloud;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float x = (float)((double)xyz[3 * i] - sh_org[0]), y = (float)((double)xyz[3 * i + 1] - sh_org[1]),
+                z = (float)((double)xyz[3 * i + 2] - sh_org[2]);
+    const uint64_t key = voxel_key(x, y, z, inv);
+    W.keys[i] = key;
+    uint32_t h = hmix(key) & (uint32_t)(hs - 1);
+    for (int probe = 0; probe < hs; ++probe) {
+      const unsigned long long prev = atomicCAS(&W.tab[h].key, ~0ull, (unsigned long long)key);
+      if (prev == ~0ull || prev == key) {
+        atomicMin(&W.tab[h].first, (uint32_t)i);
+        atomicMax(&W.tab[h].last, (uint32_t)i);
+        break;
+      }
+      h = (h + 1) & (uint32_t)(hs - 1);
+    }
+  }
+  __syncthreads();
+  const int base = sh_base;
+  float4* pts = B.cpts + cs * B.cap;
+  uint32_t* col = B.crgb + cs * B.cap;
+  int added = 0;
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    int isnew = 0, last = -1, old = -1;
+    if (i < n) {
+      const uint64_t key = W.keys[i];
+      uint32_t h = hmix(key) & (uint32_t)(hs - 1);
+      for (int probe = 0; probe < hs && W.tab[h].key != key; ++probe) h = (h + 1) & (uint32_t)(hs - 1);
+      if (W.tab[h].first == (uint32_t)i) {
+        last = (int)W.tab[h].last;
+        old = voxel_lookup(B, cs, sh_vgen, key);
+        isnew = old < 0;
+      }
+    }
+    int tot;
+    const int pos = block_excl_scan(isnew, &tot, bs);
+    if (i < n) W.dst[i] = -1;
+    if (last >= 0) {
+      const int d = isnew ? base + added + pos : old;
+      if (d < B.cap) {
+        const float x = (float)((double)xyz[3 * last] - sh_org[0]), y = (float)((double)xyz[3 * last + 1] - sh_org[1]),
+                    z = (float)((double)xyz[3 * last + 2] - sh_org[2]);
+        pts[d] = make_float4(x, y, z, __uint_as_float(sh_seq));
+        col[d] = pack_rgb(rgb, last);
+        if (isnew) W.dst[i] = d;
+      }
+    }
+    added += tot;
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += blockDim.x)
+    if (W.dst[i] >= 0) voxel_insert(B, cs, sh_vgen, W.keys[i], (uint32_t)W.dst[i]);
+  __syncthreads();
+  if (tid == 0) {
+    C.n = base + added;
+    if (C.n > B.cap) { C.n = B.cap; set_err(&B.maps[m], SMG_E_CAP_PTS); }
+  }
+  __syncthreads();
+  cloud_trim(B, cs, W, hist, bs);
+  if (tid == 0) {
+    ++C.version;
+    C.stamp = stamp;
+  }
+  __syncthreads();
+}
+
+// apBuildContact over the cloud's map-frame points float(org + p) (objmap.cpp:1090-1103).
+// Keys are a set: a racing duplicate of one key only costs a slot.
+DEV void contact_rebuild(const Batch& B, size_t cs, BlockScratch& bs) {
+  CloudRec& C = B.clouds[cs];
+  __shared__ uint32_t sh_gen;
+  if (threadIdx.x == 0) sh_gen = ++C.cgen;
+  __syncthreads();
+  const uint32_t gen = sh_gen;
+  const int n = C.n;
+  const double inv = 1.0 / B.p.contact_cell;
+  const float4* pts = B.cpts + cs * B.cap;
+  uint64_t* K = B.ckey + cs * B.HCC;
+  uint32_t* G = B.cgen + cs * B.HCC;
+  double lo[3] = {1e300, 1e300, 1e300}, hi[3] = {-1e300, -1e300, -1e300};
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float4 p = pts[i];
+    const float q[3] = {(float)(C.org[0] + (double)p.x), (float)(C.org[1] + (double)p.y), (float)(C.org[2] + (double)p.z)};
+    long long c[3];
+    for (int k = 0; k < 3; ++k) {
+      c[k] = (long long)floor((double)q[k] * inv);
+      lo[k] = fmin(lo[k], (double)c[k]);
+      hi[k] = fmax(hi[k], (double)c[k]);
+    }
+    const uint64_t key = cell_key3(c[0], c[1], c[2]);
+    uint32_t h = hmix(key) & (uint32_t)(B.HCC - 1);
+    for (int probe = 0; probe < B.HCC; ++probe) {
+      const uint32_t g = G[h];
+      if (g == gen) {
+        if (K[h] == key) break;
+      } else if (atomicCAS(&G[h], g, gen) == g) {
+        K[h] = key;
+        break;
+      } else {
+        continue;   // lost the slot to another writer: look at it again
+      }
+      h = (h + 1) & (uint32_t)(B.HCC - 1);
+    }
+  }
+  for (int k = 0; k < 3; ++k) {
+    const double l = block_min_d(lo[k], bs), u = block_max_d(hi[k], bs);
+    if (threadIdx.x == 0 && n > 0) { C.clo[k] = (long long)l; C.chi[k] = (long long)u; }
+  }
+  if (threadIdx.x == 0) { C.cn = n; C.cver = C.version; }
+  __syncthreads();
+}
+
+// Cloud additions of the frame: CTA j of map m adds, in emission order, every observation
+// cloud of target object j (ObjectMap::addPoints, objmap.cpp:508-514 via capi.cpp:986-992), then
+// rebuilds its contact index.  Targets also include objects whose cloud moved (translate).
+__global__ void __launch_bounds__(512) k_cloud_add(Batch B) {
+  __shared__ BlockScratch bs;
+  __shared__ int hist[256];
+  const int m = blockIdx.y;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  const MapRec& R = B.maps[m];
+  const Work W = work_at(B, m, blockIdx.x);
+  for (int j = blockIdx.x; j < R.n_targets; j += gridDim.x) {
+    const int slot = B.tgt_slot[(size_t)m * B.O + j];
+    const ObjRec& o = B.objs[oglob(B, m, slot)];
+    const size_t cs = (size_t)m * B.O + o.cloud_slot;
+    for (int e = 0; e < R.n_pts; ++e) {
+      const PtsRec& pr = B.ptsl[(size_t)m * B.max_det + e];
+      if (pr.obj_id != o.id) continue;
+      const float* xyz = B.cxyz + ((size_t)m * B.max_det + pr.det) * 3 * B.pmax;
+      cloud_add(B, m, cs, xyz, nullptr, pr.n, F.stamp, W, hist, bs);
+    }
+    if (B.clouds[cs].cver != B.clouds[cs].version) contact_rebuild(B, cs, bs);
+  }
+}

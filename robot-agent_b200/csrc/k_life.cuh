@@ -1,0 +1,414 @@
+// Change detection and clean-up of one keyframe (scenemap src/objmap.cpp:1020-1084):
+// absence evidence and misses (k_absent, one warp per object), relink of gone/appeared pairs
+// (k_relink, per map), geometry of merged clouds (k_struct, apStructObject :1255-1350), drop and
+// prune plus the cloud-addition target list (k_prune, per map), and the seen-cells record
+// (k_markview, markView :219-245).
+#pragma once
+#include "k_cloud.cuh"
+#include "k_obs.cuh"
+
+// toCam of absentEvidence (objmap.cpp:256-261)
+DEV void to_cam(const double* T, const double p[3], double c[3]) {
+  const double d[3] = {p[0] - T[3], p[1] - T[7], p[2] - T[11]};
+  c[0] = T[0] * d[0] + T[4] * d[1] + T[8] * d[2];
+  c[1] = T[1] * d[0] + T[5] * d[1] + T[9] * d[2];
+  c[2] = T[2] * d[0] + T[6] * d[1] + T[10] * d[2];
+}
+
+// absentEvidence (objmap.cpp:254-312), warp-level: 2 = not seen and the space behind is seen,
+// 1 = should be seen but is not, 0 = cannot tell
+DEV int absent_evidence_warp(const Batch& B, int m, const ObjRec& o, const FrameDev& F) {
+  const smg_params& P = B.p;
+  const double* T = F.T_mc;
+  double cc[3];
+  to_cam(T, o.pos, cc);
+  if (cc[2] < 0.3 || cc[2] > (double)P.zmax) return 0;
+  if (o.max_det_z > 0 && cc[2] > P.absent_det_k * o.max_det_z + 0.2) return 0;
+  const size_t cs = (size_t)m * B.O + o.cloud_slot;
+  const CloudRec& C = B.clouds[cs];
+  const int nc = C.n;
+  const int K = max(8, P.absent_samples);
+  int ns;
+  size_t stride = 1;
+  if (nc >= 8) {
+    stride = (size_t)nc / (size_t)K > 1 ? (size_t)nc / (size_t)K : 1;
+    ns = (int)(((size_t)nc + stride - 1) / stride);
+    if (ns > K) ns = K;
+  } else {
+    ns = 27;
+  }
+  const int lane = threadIdx.x & 31;
+  int vis = 0, thru = 0;
+  double u0 = 1e9, v0 = 1e9, u1 = -1e9, v1 = -1e9;
+  const float4* pts = B.cpts + cs * B.cap;
+  for (int s = lane; s < ns; s += 32) {
+    double p[3];
+    if (nc >= 8) {
+      const float4 q = pts[(size_t)s * stride];
+      p[0] = C.org[0] + (double)q.x; p[1] = C.org[1] + (double)q.y; p[2] = C.org[2] + (double)q.z;
+    } else {
+      const int a = s / 9, b = (s / 3) % 3, c = s % 3;
+      p[0] = o.lo[0] + 0.5 * a * (o.hi[0] - o.lo[0]);
+      p[1] = o.lo[1] + 0.5 * b * (o.hi[1] - o.lo[1]);
+      p[2] = o.lo[2] + 0.5 * c * (o.hi[2] - o.lo[2]);
+    }
+    double c[3];
+    to_cam(T, p, c);
+    if (c[2] < 0.2) continue;
+    const double uf = (double)F.fx * c[0] / c[2] + (double)F.cx, vf = (double)F.fy * c[1] / c[2] + (double)F.cy;
+    const int u = (int)uf, v = (int)vf;
+    if (u < 2 || v < 2 || u >= F.w - 2 || v >= F.h - 2) continue;
+    const float d = F.depth[(size_t)v * F.w + u];
+    if (!(d > 0)) continue;
+    if ((double)d < c[2] - P.occl) continue;
+    ++vis;
+    if ((double)d > c[2] + smax(P.occl, 0.1)) ++thru;
+    u0 = smin(u0, uf); u1 = smax(u1, uf); v0 = smin(v0, vf); v1 = smax(v1, vf);
+  }
+  vis = warp_sum_i(vis);
+  thru = warp_sum_i(thru);
+  u0 = warp_min_d(u0); v0 = warp_min_d(v0); u1 = warp_max_d(u1); v1 = warp_max_d(v1);
+  if (vis < max(3, (int)(P.absent_vis * ns + 0.5))) return 0;
+  if (sqrt(smax(0.0, u1 - u0) * smax(0.0, v1 - v0)) < P.absent_min_px) return 0;
+  return thru * 10 >= vis * 3 ? 2 : 1;
+}
+
+DEV bool is_big(const smg_params& P, const ObjRec& o) {
+  return smax(smax(o.hi[0] - o.lo[0], o.hi[1] - o.lo[1]), o.hi[2] - o.lo[2]) > P.big;
+}
+
+// absence and misses (objmap.cpp:1021-1061), one warp per object in list order
+__global__ void __launch_bounds__(256) k_absent(Batch B) {
+  const int m = blockIdx.y;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  MapRec* R = &B.maps[m];
+  const smg_params& P = B.p;
+  const double* T = F.T_mc;
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), nwarps = gridDim.x * (blockDim.x >> 5);
+  for (int b = gw; b < R->n_obj; b += nwarps) {
+    ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
+    if (!o.confirmed || B.obj_hit[(size_t)m * B.O + b] || o.state == 1) continue;
+    if (dist3(o.pos, F.eef[0]) < (double)P.hand_r + 0.1 || dist3(o.pos, F.eef[1]) < (double)P.hand_r + 0.1) continue;
+    const int ev = absent_evidence_warp(B, m, o, F);
+    if (lane != 0 || !ev || B.touched[(size_t)m * B.O + b]) continue;
+    const double cam_now[3] = {T[3], T[7], T[11]}, fwd[3] = {T[2], T[6], T[10]};
+    if (o.misses > 0 && ev != 2) {
+      const double cosang = fwd[0] * o.last_miss_fwd[0] + fwd[1] * o.last_miss_fwd[1] + fwd[2] * o.last_miss_fwd[2];
+      if (dist3(cam_now, o.last_miss_cam) < P.gone_step_d && cosang > B.cos_gone_step) continue;
+    }
+    for (int k = 0; k < 3; ++k) { o.last_miss_cam[k] = cam_now[k]; o.last_miss_fwd[k] = fwd[k]; }
+    const bool big = is_big(P, o);
+    ++o.n_vis_miss;
+    if (o.misses++ == 0) {
+      o.first_miss = F.stamp;
+      for (int k = 0; k < 3; ++k) o.miss_cam[k] = T[4 * k + 3];
+    }
+    const double pr = ((double)o.n_obs + 1.0) / ((double)o.n_obs + (double)o.n_vis_miss + 2.0);
+    const int k_rate = pr >= 1.0 ? 0 : (int)ceil(log(P.gone_eps) / log(1.0 - pr));
+    const int need = min(max(big ? P.gone_misses_big : P.gone_misses, k_rate), 60);
+    const double need_s = big ? P.gone_min_s_big : P.gone_min_s;
+    const bool indep = F.stamp - o.first_miss >= need_s - 1e-9 || dist3(cam_now, o.miss_cam) >= P.gone_view_d;
+    if (o.misses >= need && indep) {
+      o.state = 1;
+      o.gone_t = F.stamp;
+      o.n_vis_miss -= (uint32_t)min(o.misses, (int)o.n_vis_miss);
+      push_event(B, m, F.stamp, o, 3, (3u << 24) | (uint32_t)b);
+    }
+  }
+}
+
+// remove list position `pos` (order kept); the object slot is freed, and the cloud slot too
+// unless keep_cloud
+DEV void erase_pos(const Batch& B, int m, int pos, bool keep_cloud) {
+  MapRec* R = &B.maps[m];
+  int32_t* ord = B.order + (size_t)m * B.O;
+  const int slot = ord[pos];
+  const ObjRec& o = B.objs[oglob(B, m, slot)];
+  if (!keep_cloud) B.cfreel[(size_t)m * B.O + R->n_cfree++] = o.cloud_slot;
+  B.freel[(size_t)m * B.O + R->n_free++] = slot;
+  for (int i = pos + 1; i < R->n_obj; ++i) ord[i - 1] = ord[i];
+  --R->n_obj;
+}
+
+DEV int find_pos(const Batch& B, int m, uint32_t id) {
+  const MapRec& R = B.maps[m];
+  for (int i = 0; i < R.n_obj; ++i)
+    if (obj_at(B, m, i).id == id) return i;
+  return -1;
+}
+
+// remapId (objmap.cpp:314-318) on this frame's association and cloud lists
+DEV void remap_id(const Batch& B, int m, uint32_t from, uint32_t to) {
+  const MapRec& R = B.maps[m];
+  const FrameDev& F = B.frames[m];
+  for (int k = 0; k < F.n_det; ++k)
+    if (B.assoc[(size_t)m * B.max_det + k].obj_id == from) B.assoc[(size_t)m * B.max_det + k].obj_id = to;
+  for (int e = 0; e < R.n_pts; ++e)
+    if (B.ptsl[(size_t)m * B.max_det + e].obj_id == from) B.ptsl[(size_t)m * B.max_det + e].obj_id = to;
+}
+
+#define RELINK_MAXC 256
+// relink (objmap.cpp:321-385), per map: candidate pairs pass the scalar tests, a warp per pair
+// evaluates the embedding cosine of n's mean direction against m, then pairs are applied nearest
+// first.  Also emits the cloud-candidate list of the update (objmap.cpp:1010-1019) beforehand.
+__global__ void __launch_bounds__(256) k_relink(Batch B) {
+  __shared__ int cn_, cm_[RELINK_MAXC], cnn_[RELINK_MAXC];
+  __shared__ double cd_[RELINK_MAXC], ccos_[RELINK_MAXC];
+  __shared__ int np_;
+  __shared__ double pd_[RELINK_MAXC];
+  __shared__ uint32_t pm_[RELINK_MAXC], pn_[RELINK_MAXC];
+  extern __shared__ unsigned char smem_raw[];
+  float* mu = (float*)smem_raw;   // D per warp
+  const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  MapRec* R = &B.maps[m];
+  const smg_params& P = B.p;
+  const double t = F.stamp;
+  if (tid == 0) {
+    // cloud candidates in observation order (objmap.cpp:1010-1019)
+    int e = 0;
+    for (int a = 0; a < R->n_obs; ++a) {
+      const int det = B.obs_list[(size_t)m * B.max_det + a];
+      const uint32_t id = B.assoc[(size_t)m * B.max_det + det].obj_id;
+      const int nc = B.obs[(size_t)m * B.max_det + det].nc;
+      if (!id || nc <= 0) continue;
+      PtsRec& pr = B.ptsl[(size_t)m * B.max_det + e++];
+      pr.obj_id = id;
+      pr.det = det;
+      pr.n = nc;
+    }
+    R->n_pts = e;
+    // scalar tests of the relink candidates
+    cn_ = 0;
+    for (int i = 0; i < R->n_obj; ++i) {
+      const ObjRec& n = obj_at(B, m, i);
+      if (!n.appeared || !n.confirmed || n.state == 1 || (int)n.n_obs < P.link_min_obs) continue;
+      if (t - n.first_seen > P.link_window_s) continue;
+      for (int j = 0; j < R->n_obj; ++j) {
+        const ObjRec& mm = obj_at(B, m, j);
+        if (j == i || mm.state != 1 || !mm.confirmed || (!mm.moved && (int)mm.n_obs < P.spurious_obs)) continue;
+        if (!(n.first_seen > mm.last_seen)) continue;
+        const double d = dist3(n.pos, mm.pos);
+        if (d > smin(P.link_max_d, P.link_d0 + P.link_v * (n.first_seen - mm.last_seen))) continue;
+        bool wait = false;
+        if (t - n.first_seen < P.link_wait_s)
+          for (int q = 0; q < R->n_obj; ++q) {
+            const ObjRec& qq = obj_at(B, m, q);
+            if (q == i || q == j || !qq.confirmed || qq.state == 1 || qq.cls != n.cls) continue;
+            if (qq.last_seen < n.first_seen && dist3(qq.pos, n.pos) < d) { wait = true; break; }
+          }
+        if (wait) continue;
+        if (cn_ < RELINK_MAXC) { cm_[cn_] = j; cnn_[cn_] = i; cd_[cn_] = d; ++cn_; }
+        else set_err(R, SMG_E_ARGS);
+      }
+    }
+  }
+  __syncthreads();
+  // apCosMax(m, mu(n)) >= link_cos (mu = r_frag / |r_frag| as float, objprob.cpp:233-239)
+  float* myu = mu + (size_t)wid * B.D;
+  for (int c = wid; c < cn_; c += nw) {
+    const ObjRec& n = obj_at(B, m, cnn_[c]);
+    const size_t ogn = oglob(B, m, slot_at(B, m, cnn_[c]));
+    double cs = -3.0;
+    if (n.nrm_frag > 0) {
+      const double nn = sqrt(n.nrm_frag);
+      const float* r = B.rfrag + ogn * B.D;
+      for (int i = lane; i < B.D; i += 32) myu[i] = (float)((double)r[i] / nn);
+      __syncwarp();
+      const size_t ogm = oglob(B, m, slot_at(B, m, cm_[c]));
+      cs = cos_max_warp(B, ogm, B.objs[ogm], myu);
+    }
+    if (lane == 0) ccos_[c] = cs;
+    __syncwarp();
+  }
+  __syncthreads();
+  if (tid != 0) return;
+  np_ = 0;
+  for (int c = 0; c < cn_; ++c) {
+    if (ccos_[c] < -2.5 || ccos_[c] < P.link_cos) continue;
+    pd_[np_] = cd_[c];
+    pm_[np_] = obj_at(B, m, cm_[c]).id;
+    pn_[np_] = obj_at(B, m, cnn_[c]).id;
+    ++np_;
+  }
+  // sort (d, mid, nid) ascending
+  for (int i = 1; i < np_; ++i) {
+    const double d = pd_[i];
+    const uint32_t a = pm_[i], b = pn_[i];
+    int j = i;
+    while (j > 0 && (pd_[j - 1] > d || (pd_[j - 1] == d && (pm_[j - 1] > a || (pm_[j - 1] == a && pn_[j - 1] > b))))) {
+      pd_[j] = pd_[j - 1]; pm_[j] = pm_[j - 1]; pn_[j] = pn_[j - 1];
+      --j;
+    }
+    pd_[j] = d; pm_[j] = a; pn_[j] = b;
+  }
+  uint32_t used[2 * RELINK_MAXC];
+  int nused = 0;
+  for (int p = 0; p < np_; ++p) {
+    bool u = false;
+    for (int q = 0; q < nused; ++q) u = u || used[q] == pm_[p] || used[q] == pn_[p];
+    if (u) continue;
+    used[nused++] = pm_[p];
+    used[nused++] = pn_[p];
+    const int mi = find_pos(B, m, pm_[p]), ni = find_pos(B, m, pn_[p]);
+    ObjRec& mo = B.objs[oglob(B, m, slot_at(B, m, mi))];
+    const ObjRec& no = B.objs[oglob(B, m, slot_at(B, m, ni))];
+    for (int k = 0; k < 3; ++k) { mo.pos[k] = no.pos[k]; mo.ext[k] = no.ext[k]; mo.lo[k] = no.lo[k]; mo.hi[k] = no.hi[k]; }
+    // m takes n's cloud (m.cloud = n.cloud; version = n.version + 1); m's old cloud slot is freed
+    B.cfreel[(size_t)m * B.O + R->n_cfree++] = mo.cloud_slot;
+    mo.cloud_slot = no.cloud_slot;
+    ++B.clouds[(size_t)m * B.O + mo.cloud_slot].version;
+    mo.n_obs += no.n_obs;
+    mo.last_seen = no.last_seen;
+    mo.last_kf = no.last_kf;
+    mo.score = (mo.score < no.score) ? no.score : mo.score;
+    mo.max_det_z = smax(mo.max_det_z, no.max_det_z);
+    for (int k = 0; k < 3; ++k) mo.trk_pos[k] = no.trk_pos[k];
+    mo.trk_t = no.trk_t;
+    mo.mv_cnt = 0;
+    mo.appeared = 0;
+    mo.moved = 1;
+    mo.state = 2;
+    mo.misses = 0;
+    remap_id(B, m, pn_[p], pm_[p]);
+    push_event(B, m, t, mo, 2, (4u << 24) | (uint32_t)p);
+    erase_pos(B, m, ni, true);
+  }
+}
+
+// apStructObject geometry (objmap.cpp:1255-1319) for objects whose cloud changed; no wall
+// segments and no text model, so only geo 1 (wall-size vertical plane) / 2 (ceiling) matter.
+__global__ void __launch_bounds__(256) k_struct(Batch B) {
+  __shared__ BlockScratch bs;
+  __shared__ int hist[256];
+  __shared__ PlaneOut pout;
+  const int m = blockIdx.y;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  const MapRec& R = B.maps[m];
+  const smg_params& P = B.p;
+  const Work W = work_at(B, m, blockIdx.x);
+  float* Pt = (float*)W.t4;
+  for (int b = blockIdx.x; b < R.n_obj; b += gridDim.x) {
+    ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
+    const size_t cs = (size_t)m * B.O + o.cloud_slot;
+    const CloudRec& C = B.clouds[cs];
+    if (o.geo_ver == C.version || C.n < 30) continue;
+    // cloudSample(m, 800) (objmap.cpp:1107-1114)
+    const size_t stp = (size_t)C.n / 800 > 1 ? (size_t)C.n / 800 : 1;
+    const int n = (int)(((size_t)C.n + stp - 1) / stp);
+    const float4* pts = B.cpts + cs * B.cap;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float4 q = pts[(size_t)i * stp];
+      Pt[3 * i] = (float)(C.org[0] + (double)q.x);
+      Pt[3 * i + 1] = (float)(C.org[1] + (double)q.y);
+      Pt[3 * i + 2] = (float)(C.org[2] + (double)q.z);
+    }
+    __syncthreads();
+    plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, W.scr, B.work_n / 2, hist, bs,
+              &pout);
+    int up = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) up += (double)Pt[3 * i + 2] > R.ceil_est - P.ceil_band;
+    up = block_sum_i(up, bs);
+    if (threadIdx.x == 0) {
+      o.geo_ver = C.version;
+      int geo = 0;
+      const double nz = fabs(pout.n[2]);
+      const bool plane = pout.ok && pout.inl >= P.obj_plane_inl;
+      if (plane && pout.thick < P.obj_thick) {
+        if (nz < P.wall_vert && (pout.hspan >= P.obj_wall_span || (pout.zhi >= P.obj_wall_top && pout.zhi - pout.zlo >= P.obj_wall_h))) geo = 1;
+        else if (nz > P.horiz && pout.zmed > P.ceil_z) geo = 2;
+      }
+      if (!geo && R.ceil_est > 0 && n > 0)
+        if (up >= P.ceil_frac * n && smax(o.hi[0] - o.lo[0], o.hi[1] - o.lo[1]) >= P.ceil_wide) geo = 2;
+      o.geo = geo;
+    }
+    __syncthreads();
+  }
+}
+
+// drop + prune (objmap.cpp:1064-1073), then the cloud-addition targets (objects named by this
+// frame's cloud lists, first appearance order, plus objects whose cloud moved)
+__global__ void k_prune(Batch B) {
+  const int m = blockIdx.x;
+  const FrameDev& F = B.frames[m];
+  if (!F.active || threadIdx.x != 0) return;
+  MapRec* R = &B.maps[m];
+  const smg_params& P = B.p;
+  for (int b = 0; b < R->n_obj;) {
+    ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
+    o.hide = 0;
+    o.drop = o.geo == 1 || o.geo == 2;
+    bool rm;
+    if (o.drop) { ++R->st.n_obj_struct; rm = true; }
+    else if (!o.confirmed) rm = F.stamp - o.last_seen > P.prune_s;
+    else rm = o.state == 1 && !o.moved && (int)o.n_obs < P.spurious_obs;
+    if (rm) erase_pos(B, m, b, false);
+    else ++b;
+  }
+  int nt = 0;
+  for (int e = 0; e < R->n_pts; ++e) {
+    const int pos = find_pos(B, m, B.ptsl[(size_t)m * B.max_det + e].obj_id);
+    if (pos < 0) continue;
+    const int slot = slot_at(B, m, pos);
+    bool seen = false;
+    for (int q = 0; q < nt; ++q) seen = seen || B.tgt_slot[(size_t)m * B.O + q] == slot;
+    if (!seen) B.tgt_slot[(size_t)m * B.O + nt++] = slot;
+  }
+  for (int b = 0; b < R->n_obj; ++b) {
+    const int slot = slot_at(B, m, b);
+    const ObjRec& o = B.objs[oglob(B, m, slot)];
+    const CloudRec& C = B.clouds[(size_t)m * B.O + o.cloud_slot];
+    if (C.cver == C.version || C.n == 0) continue;
+    bool seen = false;
+    for (int q = 0; q < nt; ++q) seen = seen || B.tgt_slot[(size_t)m * B.O + q] == slot;
+    if (!seen) B.tgt_slot[(size_t)m * B.O + nt++] = slot;
+  }
+  R->n_targets = nt;
+}
+
+// markView (objmap.cpp:219-245): sparse depth samples, horizontal camera->point segments, first
+// time each 2D cell was seen per range band.  Fresh cells are pre-filled with "never".
+__global__ void __launch_bounds__(256) k_markview(Batch B) {
+  const int m = blockIdx.x;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  const smg_params& P = B.p;
+  const double* T = F.T_mc;
+  const double cell = smax(0.05, P.view_cell);
+  const int stp = max(1, F.w / 32);
+  const int nu = (F.w - stp / 2 + stp - 1) / stp, nv = (F.h - stp / 2 + stp - 1) / stp;
+  int64_t* K = B.vkey + (size_t)m * B.view_slots;
+  for (int s = threadIdx.x; s < nu * nv; s += blockDim.x) {
+    const int u = stp / 2 + (s % nu) * stp, v = stp / 2 + (s / nu) * stp;
+    const float z = F.depth[(size_t)v * F.w + u];
+    if (!(z > P.zmin && z < P.zmax)) continue;
+    const double xc = (double)(((float)u - F.cx) / F.fx * z), yc = (double)(((float)v - F.cy) / F.fy * z);
+    const double zd = (double)z;
+    const double px = T[0] * xc + T[1] * yc + T[2] * zd + T[3];
+    const double py = T[4] * xc + T[5] * yc + T[6] * zd + T[7];
+    const double dx = px - T[3], dy = py - T[7];
+    const double L = sqrt(dx * dx + dy * dy), Lm = smin(L, (double)SMG_VIEW_BANDS);
+    if (L < 1e-6) continue;
+    const int ns = (int)ceil(Lm / (0.5 * cell));
+    for (int q = 0; q <= ns; ++q) {
+      const double r = Lm * q / (double)max(1, ns);
+      const int64_t key = view_cell_key(T[3] + r / L * dx, T[7] + r / L * dy, cell);
+      uint32_t h = hmix((uint64_t)key) & (uint32_t)(B.view_slots - 1);
+      int probe = 0;
+      for (; probe < B.view_slots; ++probe) {
+        const unsigned long long prev =
+            atomicCAS((unsigned long long*)&K[h], (unsigned long long)INT64_MIN, (unsigned long long)key);
+        if (prev == (unsigned long long)INT64_MIN || prev == (unsigned long long)key) break;
+        h = (h + 1) & (uint32_t)(B.view_slots - 1);
+      }
+      if (probe == B.view_slots) { set_err(&B.maps[m], SMG_E_CAP_VIEW); continue; }
+      double* e = B.vfirst + ((size_t)m * B.view_slots + h) * SMG_VIEW_BANDS;
+      for (int b = max(0, (int)ceil(r) - 1); b < SMG_VIEW_BANDS; ++b)
+        if (e[b] < -1e299) e[b] = F.stamp;
+    }
+  }
+}

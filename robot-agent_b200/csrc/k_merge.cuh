@@ -1,0 +1,278 @@
+// Object-object merge pass at the start of a keyframe (apMergePass, scenemap src/objmap.cpp:
+// 1154-1225, apPairObj :1118-1135, da::absorbObject da/src/merge.cpp:32-82, apMerge
+// objprob.cpp:358-394).
+//
+// k_merge_pairs: warps take the rows i of the object list and test every j > i: box-gap and
+// size gates, then for surviving pairs the contact fraction of a <= 2*contact_samples sample of
+// the smaller cloud against the larger cloud's contact set, and the symmetric embedding cosine
+// (each object's mean direction against the other's vectors).  Pairs with P >= merge_p go to a
+// per-map candidate list.  (The reference's pair cache only skips recomputing identical inputs,
+// so evaluating every gated pair gives the same P.)
+// k_merge_apply: one CTA per map sorts the candidates by P and merges greedily, each object at
+// most once per pass, as the reference does.
+#pragma once
+#include "k_life.cuh"
+
+#define MP_CTAS 8
+#define MP_SPW 640
+
+__global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
+  extern __shared__ unsigned char smem_raw[];
+  const int m = blockIdx.y, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  const MapRec& R = B.maps[m];
+  const smg_params& P = B.p;
+  float* mu = (float*)smem_raw + (size_t)wid * (B.D + 3 * MP_SPW);
+  float* sp = mu + B.D;
+  const int n = R.n_obj;
+  const double gate2 = P.gate * P.gate;
+  for (int i = blockIdx.x * nw + wid; i < n; i += gridDim.x * nw) {
+    const int si = slot_at(B, m, i);
+    const ObjRec& a = B.objs[oglob(B, m, si)];
+    if (a.state == 1) continue;
+    for (int j = i + 1; j < n; ++j) {
+      const int sj = slot_at(B, m, j);
+      const ObjRec& b = B.objs[oglob(B, m, sj)];
+      if (b.state == 1) continue;
+      double g2 = 0;
+      bool too_big = false;
+      for (int k = 0; k < 3; ++k) {
+        const double g = smax3(0.0, a.lo[k] - b.hi[k], b.lo[k] - a.hi[k]);
+        g2 += g * g;
+        too_big = too_big || smax(a.hi[k], b.hi[k]) - smin(a.lo[k], b.lo[k]) > P.max_ext;
+      }
+      if (g2 > gate2 || too_big) continue;
+      const size_t csa = (size_t)m * B.O + a.cloud_slot, csb = (size_t)m * B.O + b.cloud_slot;
+      const bool a_small = B.clouds[csa].n <= B.clouds[csb].n;
+      const ObjRec& sm = a_small ? a : b;
+      const ObjRec& lg = a_small ? b : a;
+      const size_t css = a_small ? csa : csb, csl = a_small ? csb : csa;
+      // cloudSample(sm, contact_samples) (objmap.cpp:1107-1114)
+      const CloudRec& Cs = B.clouds[css];
+      const int cn = Cs.n;
+      const int stp = max(1, cn / max(1, P.contact_samples));
+      const int nsp = cn > 0 ? (cn + stp - 1) / stp : 0;
+      if (nsp > MP_SPW) { if (lane == 0) set_err(&B.maps[m], SMG_E_ARGS); continue; }
+      const float4* pts = B.cpts + css * B.cap;
+      for (int q = lane; q < nsp; q += 32) {
+        const float4 p = pts[(size_t)q * stp];
+        sp[3 * q] = (float)(Cs.org[0] + (double)p.x);
+        sp[3 * q + 1] = (float)(Cs.org[1] + (double)p.y);
+        sp[3 * q + 2] = (float)(Cs.org[2] + (double)p.z);
+      }
+      __syncwarp();
+      double cs = -2;
+      for (int dir = 0; dir < 2; ++dir) {
+        const ObjRec& x = dir == 0 ? a : b;
+        const size_t ogx = oglob(B, m, dir == 0 ? si : sj), ogy = oglob(B, m, dir == 0 ? sj : si);
+        if (!(x.nrm_frag > 0)) continue;
+        const double nn = sqrt(x.nrm_frag);
+        const float* r = B.rfrag + ogx * B.D;
+        for (int q = lane; q < B.D; q += 32) mu[q] = (float)((double)r[q] / nn);
+        __syncwarp();
+        cs = smax(cs, cos_max_warp(B, ogy, B.objs[ogy], mu));
+        __syncwarp();
+      }
+      const int hits = contact_hits_warp(B, csl, sp, nsp, P.contact_cell);
+      if (lane == 0) {
+        const double contact = (nsp > 0 && B.clouds[csl].cn > 0) ? (double)hits / (double)nsp : 0.0;
+        const double p = pair_p(sm.lo, sm.hi, sm.pos, contact, lg.lo, lg.hi, lg.pos, cs, P, true, nullptr);
+        if (p >= P.merge_p) {
+          const int c = atomicAdd(&B.mcand_n[m], 1);
+          if (c < B.O * 8) {
+            B.mcand_p[(size_t)m * B.O * 8 + c] = p;
+            B.mcand_ab[((size_t)m * B.O * 8 + c) * 2] = a.id;
+            B.mcand_ab[((size_t)m * B.O * 8 + c) * 2 + 1] = b.id;
+          } else {
+            set_err(&B.maps[m], SMG_E_ARGS);
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+__global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
+  __shared__ BlockScratch bs;
+  __shared__ int hist[256];
+  __shared__ int sh_go, sh_ka, sh_kb, nused;
+  __shared__ uint32_t used[2 * 256];
+  const int m = blockIdx.x, tid = threadIdx.x;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  MapRec* R = &B.maps[m];
+  const smg_params& P = B.p;
+  const double t = F.stamp;
+  const int nc = min(B.mcand_n[m], B.O * 8);
+  double* cp = B.mcand_p + (size_t)m * B.O * 8;
+  uint32_t* cab = B.mcand_ab + (size_t)m * B.O * 8 * 2;
+  if (tid == 0) {
+    R->n_evn = 0;
+    nused = 0;
+    for (int i = 1; i < nc; ++i) {   // descending P (stable for equal P)
+      const double p = cp[i];
+      const uint32_t x = cab[2 * i], y = cab[2 * i + 1];
+      int j = i;
+      while (j > 0 && cp[j - 1] < p) { cp[j] = cp[j - 1]; cab[2 * j] = cab[2 * j - 2]; cab[2 * j + 1] = cab[2 * j - 1]; --j; }
+      cp[j] = p; cab[2 * j] = x; cab[2 * j + 1] = y;
+    }
+  }
+  __syncthreads();
+  const Work W = work_at(B, m, 0);
+  float* xyz = B.cxyz + (size_t)m * B.max_det * 3 * B.pmax;
+  uint8_t* rgb = (uint8_t*)(B.cpx + (size_t)m * B.max_det * 2 * B.pmax);
+  for (int c = 0; c < nc; ++c) {
+    if (tid == 0) {
+      sh_go = 0;
+      const uint32_t ia = cab[2 * c], ib = cab[2 * c + 1];
+      bool u = false;
+      for (int q = 0; q < nused; ++q) u = u || used[q] == ia || used[q] == ib;
+      const int pa = find_pos(B, m, ia), pb = find_pos(B, m, ib);
+      if (!u && pa >= 0 && pb >= 0 && nused + 2 <= 2 * 256) {
+        int ka = pa, kb = pb;
+        const ObjRec& A = obj_at(B, m, pa);
+        const ObjRec& Bo = obj_at(B, m, pb);
+        if (Bo.n_obs > A.n_obs || (Bo.n_obs == A.n_obs && ib < ia)) { ka = pb; kb = pa; }
+        used[nused++] = ia;
+        used[nused++] = ib;
+        sh_ka = slot_at(B, m, ka);
+        sh_kb = slot_at(B, m, kb);
+        sh_go = 1;
+        // da::absorb scalar part (merge.cpp:33-62)
+        ObjRec& a = B.objs[oglob(B, m, sh_ka)];
+        const ObjRec& b = B.objs[oglob(B, m, sh_kb)];
+        const bool big = smax(smax(a.hi[0] - a.lo[0], a.hi[1] - a.lo[1]), smax(b.hi[0] - b.lo[0], b.hi[1] - b.lo[1])) > P.big;
+        const double wa = smax((double)a.n_obs, 1.0), wb = smax((double)b.n_obs, 1.0);
+        for (int k = 0; k < 3; ++k) {
+          if (big) {
+            a.lo[k] = smin(a.lo[k], b.lo[k]);
+            a.hi[k] = smax(a.hi[k], b.hi[k]);
+            a.pos[k] = 0.5 * (a.lo[k] + a.hi[k]);
+            a.ext[k] = a.hi[k] - a.lo[k];
+          } else {
+            a.pos[k] = (a.pos[k] * wa + b.pos[k] * wb) / (wa + wb);
+            a.ext[k] = (a.ext[k] * wa + b.ext[k] * wb) / (wa + wb);
+            a.lo[k] = (a.lo[k] * wa + b.lo[k] * wb) / (wa + wb);
+            a.hi[k] = (a.hi[k] * wa + b.hi[k] * wb) / (wa + wb);
+          }
+        }
+        if (b.first_seen < a.first_seen) {
+          a.first_seen = b.first_seen;
+          for (int k = 0; k < 3; ++k) a.first_pos[k] = b.first_pos[k];
+        }
+        a.n_obs += b.n_obs;
+        a.last_seen = smax(a.last_seen, b.last_seen);
+        a.last_kf = smax(a.last_kf, b.last_kf);
+        a.score = (a.score < b.score) ? b.score : a.score;
+        a.max_det_z = smax(a.max_det_z, b.max_det_z);
+        a.moved = a.moved || b.moved;
+        a.misses = min(a.misses, b.misses);
+        a.n_vis_miss += b.n_vis_miss;
+        if (a.state != 0 && b.state == 0) a.state = 0;
+      }
+    }
+    __syncthreads();
+    if (!sh_go) continue;
+    const size_t oga = oglob(B, m, sh_ka), ogb = oglob(B, m, sh_kb);
+    ObjRec& a = B.objs[oga];
+    const ObjRec& b = B.objs[ogb];
+    const size_t csa = (size_t)m * B.O + a.cloud_slot, csb = (size_t)m * B.O + b.cloud_slot;
+    // cloud: b's points (org + p) into a (merge.cpp:64-75)
+    const CloudRec& Cb = B.clouds[csb];
+    const int nb = Cb.n;
+    const float4* pb = B.cpts + csb * B.cap;
+    const uint32_t* colb = B.crgb + csb * B.cap;
+    for (int i = tid; i < nb; i += blockDim.x) {
+      const float4 p = pb[i];
+      xyz[3 * i] = (float)(Cb.org[0] + (double)p.x);
+      xyz[3 * i + 1] = (float)(Cb.org[1] + (double)p.y);
+      xyz[3 * i + 2] = (float)(Cb.org[2] + (double)p.z);
+      rgb[3 * i] = (uint8_t)(colb[i] & 255u);
+      rgb[3 * i + 1] = (uint8_t)((colb[i] >> 8) & 255u);
+      rgb[3 * i + 2] = (uint8_t)((colb[i] >> 16) & 255u);
+    }
+    __syncthreads();
+    if (nb > 0) cloud_add(B, m, csa, xyz, rgb, nb, t, W, hist, bs);
+    // apMerge: vectors (objprob.cpp:359-377)
+    float* ra = B.rfrag + oga * B.D;
+    const float* rb = B.rfrag + ogb * B.D;
+    for (int i = tid; i < B.D; i += blockDim.x) ra[i] += rb[i];
+    __syncthreads();
+    // views: a's and b's in one list, fragments, stable by kappa desc, top-k (objprob.cpp:382-385)
+    __shared__ int vsrc[2 * SMG_TOPK_MAX + 2], vphys[2 * SMG_TOPK_MAX + 2], dstp[2 * SMG_TOPK_MAX + 2], nkeep;
+    __shared__ float vk[2 * SMG_TOPK_MAX + 2];
+    __shared__ double vs[2 * SMG_TOPK_MAX + 2];
+    if (tid == 0) {
+      int nv = 0;
+      for (int v = 0; v < a.n_views; ++v) { vsrc[nv] = 0; vphys[nv] = a.view_slot[v]; vk[nv] = a.vkappa[v]; vs[nv] = a.vstamp[v]; ++nv; }
+      for (int v = 0; v < b.n_views; ++v) { vsrc[nv] = 1; vphys[nv] = b.view_slot[v]; vk[nv] = b.vkappa[v]; vs[nv] = b.vstamp[v]; ++nv; }
+      for (int i = 1; i < nv; ++i) {
+        const int s0 = vsrc[i], p0 = vphys[i];
+        const float k0 = vk[i];
+        const double t0 = vs[i];
+        int j = i;
+        while (j > 0 && vk[j - 1] < k0) { vsrc[j] = vsrc[j - 1]; vphys[j] = vphys[j - 1]; vk[j] = vk[j - 1]; vs[j] = vs[j - 1]; --j; }
+        vsrc[j] = s0; vphys[j] = p0; vk[j] = k0; vs[j] = t0;
+      }
+      nkeep = min(nv, B.topk);
+      int usedm = 0;
+      for (int v = 0; v < nkeep; ++v) if (vsrc[v] == 0) usedm |= 1 << vphys[v];
+      for (int v = 0; v < nkeep; ++v) {
+        if (vsrc[v] == 0) { dstp[v] = vphys[v]; continue; }
+        int f = 0;
+        while (usedm & (1 << f)) ++f;
+        usedm |= 1 << f;
+        dstp[v] = f;
+      }
+    }
+    __syncthreads();
+    for (int v = 0; v < nkeep; ++v) {
+      if (vsrc[v] != 1) continue;
+      const uint16_t* src = B.views + (ogb * (B.topk + 1) + vphys[v]) * B.D;
+      uint16_t* dst = B.views + (oga * (B.topk + 1) + dstp[v]) * B.D;
+      for (int i = tid; i < B.D; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    if (tid == 0) {
+      for (int v = 0; v < nkeep; ++v) { a.view_slot[v] = dstp[v]; a.vkappa[v] = vk[v]; a.vstamp[v] = vs[v]; }
+      a.n_views = nkeep;
+      ++a.ver;
+      a.k_frag += (0.0 + b.k_frag) + 0.0;
+      a.n_whole = 0;
+      a.whole_kappa = 0;
+      a.need_whole = 1;
+      // cams: append b's, keep the newest 32
+      int nc2 = a.n_cams;
+      for (int q = 0; q < b.n_cams; ++q) {
+        if (nc2 == SMG_CAMS) {
+          for (int r = 1; r < SMG_CAMS; ++r)
+            for (int j = 0; j < 7; ++j) a.cams[r - 1][j] = a.cams[r][j];
+          --nc2;
+        }
+        for (int j = 0; j < 7; ++j) a.cams[nc2][j] = b.cams[q][j];
+        ++nc2;
+      }
+      a.n_cams = nc2;
+      for (int k = 0; k < 3; ++k) a.P[k] = merge_var(a.P[k], b.P[k]);
+      a.n_wall_obs += b.n_wall_obs;
+      a.n_ap_obs += b.n_ap_obs;
+      a.n_struct_look += b.n_struct_look;
+      a.wall_like = a.wall_like && b.wall_like;
+      a.confirmed = a.confirmed || b.confirmed;
+      ++R->st.n_merge;
+      erase_pos(B, m, find_pos(B, m, b.id), false);
+      push_event(B, m, t, a, 7, (1u << 24) | (uint32_t)R->n_evn++);
+    }
+    __syncthreads();
+    refresh_nrm(B, oga, bs);
+    if (B.clouds[csa].cver != B.clouds[csa].version) contact_rebuild(B, csa, bs);
+  }
+  // reset the per-frame association flags (list positions)
+  for (int i = tid; i < B.O; i += blockDim.x) {
+    B.touched[(size_t)m * B.O + i] = 0;
+    B.obj_hit[(size_t)m * B.O + i] = 0;
+  }
+  if (tid == 0) B.mcand_n[m] = 0;
+}

@@ -1,0 +1,528 @@
+// Observation build: one CTA per (detection, map).
+//
+// Restates scenemap src/objmap.cpp:645-765 (per-detection back-projection, MAD depth band,
+// per-observation voxel de-duplication, 10/50/90 percentile boxes, view kappa) and the plane
+// fit of apObsStructural (objmap.cpp:565-575 -> apPlaneFit, objprob.cpp:130-209).  The final,
+// order-dependent structural decision (ceiling estimate) is taken by k_obs_finalize in
+// detection order.
+//
+// Device data flow per CTA: the box is scanned at stride sk in raster order; valid pixels are
+// compacted in raster order (block scan) into L2-resident scratch; every order-sensitive rule of
+// the reference (subsample v[(i*n)/2048], first point per voxel, percentiles) is applied to that
+// raster-ordered list, and percentiles are exact k-th order statistics (radix selection).
+#pragma once
+#include "dev_util.cuh"
+
+#define OBS_THREADS 512
+#define OBS_HASH 8192
+
+struct PlaneOut {
+  int ok;
+  double n[3], thick, inl, zmed, zlo, zhi, hspan;
+};
+
+// 3x3 symmetric Jacobi eigen-decomposition (scenemap objprob.cpp:50-84): ascending ev, columns V.
+DEV void eig_sym3(double A[3][3], double ev[3], double V[3][3]) {
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) V[i][j] = i == j;
+  for (int it = 0; it < 32; ++it) {
+    int p = 0, q = 1;
+    double best = fabs(A[0][1]);
+    if (fabs(A[0][2]) > best) { best = fabs(A[0][2]); p = 0; q = 2; }
+    if (fabs(A[1][2]) > best) { best = fabs(A[1][2]); p = 1; q = 2; }
+    if (best < 1e-12) break;
+    const double th = 0.5 * atan2(2 * A[p][q], A[q][q] - A[p][p]);
+    const double c = cos(th), s = sin(th);
+    for (int k = 0; k < 3; ++k) {
+      const double akp = A[k][p], akq = A[k][q];
+      A[k][p] = c * akp - s * akq;
+      A[k][q] = s * akp + c * akq;
+    }
+    for (int k = 0; k < 3; ++k) {
+      const double apk = A[p][k], aqk = A[q][k];
+      A[p][k] = c * apk - s * aqk;
+      A[q][k] = s * apk + c * aqk;
+    }
+    for (int k = 0; k < 3; ++k) {
+      const double vkp = V[k][p], vkq = V[k][q];
+      V[k][p] = c * vkp - s * vkq;
+      V[k][q] = s * vkp + c * vkq;
+    }
+  }
+  // stable ascending order of the diagonal (insertion sort, like std::sort on 3 elements)
+  int o[3] = {0, 1, 2};
+  for (int i = 1; i < 3; ++i) {
+    const int v = o[i];
+    int j = i;
+    while (j > 0 && A[v][v] < A[o[j - 1]][o[j - 1]]) { o[j] = o[j - 1]; --j; }
+    o[j] = v;
+  }
+  double W[3][3];
+  for (int k = 0; k < 3; ++k) {
+    ev[k] = A[o[k]][o[k]];
+    for (int i = 0; i < 3; ++i) W[i][k] = V[i][o[k]];
+  }
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) V[i][j] = W[i][j];
+}
+
+DEV int pct_index(int n, double q) {   // min(n-1, size_t(q*(n-1) + 0.5)) (objmap.cpp:17, objprob.cpp:87)
+  const int k = (int)(q * (double)(n - 1) + 0.5);
+  return k < n - 1 ? k : n - 1;
+}
+
+// apPlaneFit (scenemap objprob.cpp:130-209).  xyz: n float points (global).  scr: 4*cap doubles
+// of scratch.  The RANSAC iterations run on warp 0 in the reference's sequence (same splitmix
+// draws, same adaptive stop; the stop count comes from a host-libm table).  Inlier sums are
+// block reductions (deterministic tree).  span1/span2 are not produced (no caller reads them).
+DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_iters, const int32_t* need_tab, double* scr, int cap,
+                   int* hist, BlockScratch& bs, PlaneOut* out) {
+  __shared__ double sh_best[4];
+  __shared__ int sh_bestc;
+  __shared__ double sh_m[3], sh_V[3][3], sh_ev[3];
+  const int tid = threadIdx.x;
+  if (n < 8 || !(tau > 0)) {
+    if (tid == 0) out->ok = 0;
+    __syncthreads();
+    return;
+  }
+  if (tid < 32) {
+    const int lane = tid;
+    uint64_t rs = seed ^ ((uint64_t)n << 32);
+    const int ns = n < 256 ? n : 256;
+    const int sstep = n / ns > 1 ? n / ns : 1;
+    const int nsamp = (n + sstep - 1) / sstep;
+    double best[4] = {0, 0, 1, 0};
+    int best_c = -1;
+    int need = max_iters > 1 ? max_iters : 1;
+    for (int it = 0; it < need && it < max_iters; ++it) {
+      int id0 = 0, id1 = 0, id2 = 0;
+      if (lane == 0) {
+        id0 = (int)(splitmix(rs) % (uint64_t)n);
+        do id1 = (int)(splitmix(rs) % (uint64_t)n); while (id1 == id0);
+        do id2 = (int)(splitmix(rs) % (uint64_t)n); while (id2 == id0 || id2 == id1);
+      }
+      id0 = __shfl_sync(0xffffffffu, id0, 0);
+      id1 = __shfl_sync(0xffffffffu, id1, 0);
+      id2 = __shfl_sync(0xffffffffu, id2, 0);
+      const float* a = xyz + 3 * id0;
+      const float* b = xyz + 3 * id1;
+      const float* c = xyz + 3 * id2;
+      const double u[3] = {(double)(b[0] - a[0]), (double)(b[1] - a[1]), (double)(b[2] - a[2])};
+      const double v[3] = {(double)(c[0] - a[0]), (double)(c[1] - a[1]), (double)(c[2] - a[2])};
+      double nn[3] = {u[1] * v[2] - u[2] * v[1], u[2] * v[0] - u[0] * v[2], u[0] * v[1] - u[1] * v[0]};
+      const double L = sqrt(nn[0] * nn[0] + nn[1] * nn[1] + nn[2] * nn[2]);
+      if (L < 1e-6) continue;
+      for (int k = 0; k < 3; ++k) nn[k] /= L;
+      const double d0 = -(nn[0] * (double)a[0] + nn[1] * (double)a[1] + nn[2] * (double)a[2]);
+      int cnt = 0;
+      for (int s = lane; s < nsamp; s += 32) {
+        const int i = s * sstep;
+        cnt += fabs(nn[0] * (double)xyz[3 * i] + nn[1] * (double)xyz[3 * i + 1] + nn[2] * (double)xyz[3 * i + 2] + d0) <= tau;
+      }
+      cnt = warp_sum_i(cnt);
+      if (cnt > best_c) {
+        best_c = cnt;
+        best[0] = nn[0]; best[1] = nn[1]; best[2] = nn[2]; best[3] = d0;
+        const double w = (double)cnt / (double)nsamp;
+        const double pw = w * w * w;
+        if (pw > 0.999999) break;
+        if (pw > 1e-9) need = need_tab[nsamp * 257 + cnt];
+      }
+    }
+    if (lane == 0) {
+      sh_bestc = best_c;
+      for (int k = 0; k < 4; ++k) sh_best[k] = best[k];
+    }
+  }
+  __syncthreads();
+  if (sh_bestc < 3) {
+    if (tid == 0) out->ok = 0;
+    __syncthreads();
+    return;
+  }
+  // two PCA refits (objprob.cpp:166-180); mp = plane whose inliers the last pass used
+  double pl[4] = {sh_best[0], sh_best[1], sh_best[2], sh_best[3]};
+  double mp[4];
+  int ni = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int k = 0; k < 4; ++k) mp[k] = pl[k];
+    double s0 = 0, s1 = 0, s2 = 0;
+    int cnt = 0;
+    for (int i = tid; i < n; i += blockDim.x) {
+      const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
+      if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) { s0 += x; s1 += y; s2 += z; ++cnt; }
+    }
+    ni = block_sum_i(cnt, bs);
+    if (ni < 3) {
+      if (tid == 0) out->ok = 0;
+      __syncthreads();
+      return;
+    }
+    const double inv = 1.0 / (double)(ni > 1 ? ni : 1);
+    double m[3] = {block_sum_d(s0, bs), block_sum_d(s1, bs), block_sum_d(s2, bs)};
+    for (int k = 0; k < 3; ++k) m[k] *= inv;
+    double c[6] = {0, 0, 0, 0, 0, 0};
+    for (int i = tid; i < n; i += blockDim.x) {
+      const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
+      if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) {
+        const double d[3] = {x - m[0], y - m[1], z - m[2]};
+        c[0] += d[0] * d[0]; c[1] += d[0] * d[1]; c[2] += d[0] * d[2];
+        c[3] += d[1] * d[1]; c[4] += d[1] * d[2]; c[5] += d[2] * d[2];
+      }
+    }
+    double C[3][3];
+    C[0][0] = block_sum_d(c[0], bs) * inv; C[0][1] = block_sum_d(c[1], bs) * inv; C[0][2] = block_sum_d(c[2], bs) * inv;
+    C[1][1] = block_sum_d(c[3], bs) * inv; C[1][2] = block_sum_d(c[4], bs) * inv; C[2][2] = block_sum_d(c[5], bs) * inv;
+    C[1][0] = C[0][1]; C[2][0] = C[0][2]; C[2][1] = C[1][2];
+    if (tid == 0) {
+      double ev[3], V[3][3];
+      eig_sym3(C, ev, V);
+      for (int i = 0; i < 3; ++i) {
+        sh_ev[i] = ev[i];
+        sh_m[i] = m[i];
+        for (int j = 0; j < 3; ++j) sh_V[i][j] = V[i][j];
+      }
+    }
+    __syncthreads();
+    pl[0] = sh_V[0][0]; pl[1] = sh_V[1][0]; pl[2] = sh_V[2][0];
+    pl[3] = -(pl[0] * sh_m[0] + pl[1] * sh_m[1] + pl[2] * sh_m[2]);
+  }
+  const double m0 = sh_m[0], m1 = sh_m[1];
+  // horizontal principal direction of the inliers (objprob.cpp:187-192)
+  double a0 = 0, a1 = 0, a2 = 0;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
+    if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) {
+      const double dx = x - m0, dy = y - m1;
+      a0 += dx * dx; a1 += dx * dy; a2 += dy * dy;
+    }
+  }
+  const double sxx = block_sum_d(a0, bs), sxy = block_sum_d(a1, bs), syy = block_sum_d(a2, bs);
+  const double th = 0.5 * atan2(2 * sxy, sxx - syy), hc = cos(th), hs = sin(th);
+  // z and horizontal-span projections of the inliers -> exact percentiles (objprob.cpp:193-206)
+  __shared__ int sh_cnt;
+  if (tid == 0) sh_cnt = 0;
+  __syncthreads();
+  double* zs = scr;
+  double* hsp = scr + cap;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
+    if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) {
+      const int q = atomicAdd(&sh_cnt, 1);
+      zs[q] = z;
+      hsp[q] = (x - m0) * hc + (y - m1) * hs;
+    }
+  }
+  __syncthreads();
+  const double h9 = block_select(hsp, ni, pct_index(ni, 0.9), hist, bs);
+  const double h1 = block_select(hsp, ni, pct_index(ni, 0.1), hist, bs);
+  const double zlo = block_select(zs, ni, pct_index(ni, 0.1), hist, bs);
+  const double zhi = block_select(zs, ni, pct_index(ni, 0.9), hist, bs);
+  const double zmd = block_select(zs, ni, pct_index(ni, 0.5), hist, bs);
+  if (tid == 0) {
+    out->ok = 1;
+    for (int k = 0; k < 3; ++k) out->n[k] = sh_V[k][0];
+    out->thick = sqrt(smax(0.0, sh_ev[0]));
+    out->inl = (double)ni / (double)n;
+    out->hspan = h9 - h1;
+    out->zlo = zlo;
+    out->zhi = zhi;
+    out->zmed = zmd;
+  }
+  __syncthreads();
+}
+
+// subsample (objmap.cpp:37-42) of v[0..n) into S (<= SMG_SUB values); returns its size
+DEV int subsample_to(const double* v, int n, double* S) {
+  const int nS = n <= SMG_SUB ? n : SMG_SUB;
+  for (int i = threadIdx.x; i < nS; i += blockDim.x) S[i] = n <= SMG_SUB ? v[i] : v[(size_t)i * (size_t)n / SMG_SUB];
+  __syncthreads();
+  return nS;
+}
+
+DEV bool lab_is(const uint16_t* label, int W, int H, int u, int v, uint16_t L) {
+  return u >= 0 && v >= 0 && u < W && v < H && label[(size_t)v * W + u] == L;
+}
+
+__global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
+  extern __shared__ unsigned char smem_raw[];
+  uint64_t* hkey = (uint64_t*)smem_raw;                         // OBS_HASH keys
+  uint32_t* hidx = (uint32_t*)(smem_raw + OBS_HASH * 8);        // OBS_HASH first index
+  double* S = (double*)smem_raw;                                // SMG_SUB values (aliases the hash)
+  __shared__ int hist[256];
+  __shared__ BlockScratch bs;
+  __shared__ PlaneOut pout;
+  const int m = blockIdx.y, k = blockIdx.x, tid = threadIdx.x;
+  const FrameDev& F = B.frames[m];
+  ObsRec* O = &B.obs[(size_t)m * B.max_det + k];
+  if (!F.active || k >= F.n_det) {
+    if (tid == 0) { O->valid = 0; O->stage = -1; O->floor_drop = 0; }
+    return;
+  }
+  const smg_params& P = B.p;
+  const int W = F.w, H = F.h;
+  const size_t slot = (size_t)m * B.max_det + k;
+  double* X = B.px + slot * 4 * B.pmax;
+  double* Y = X + B.pmax;
+  double* Z = Y + B.pmax;
+  double* ZC = Z + B.pmax;
+  int32_t* PU = B.ppix + slot * 2 * B.pmax;
+  int32_t* PV = PU + B.pmax;
+  double* XK = B.pk + slot * 3 * B.pmax;
+  double* YK = XK + B.pmax;
+  double* ZK = YK + B.pmax;
+  float* CX = B.cxyz + slot * 3 * B.pmax;
+  int32_t* CP = B.cpx + slot * 2 * B.pmax;
+  double* SCR = B.sel + slot * 4 * B.pmax;
+  const uint16_t L = F.det_label[k];
+  const float* b = F.box[k];
+  // box scan (objmap.cpp:648-652); label grid == depth grid, so the detection->depth scale is 1
+  const int st = P.step > 1 ? P.step : 1;
+  const int u0 = max(0, (int)(b[0]) - 1), u1 = min(W - 1, (int)(b[2]) + 1);
+  const int v0 = max(0, (int)(b[1]) - 1), v1 = min(H - 1, (int)(b[3]) + 1);
+  const double box_px = (double)max(0, u1 - u0 + 1) * (double)max(0, v1 - v0 + 1);
+  const int sk = max(st, (int)ceil(sqrt(box_px / (double)max(1, P.max_pts))));
+  const int ncols = u1 >= u0 ? (u1 - u0) / sk + 1 : 0, nrows = v1 >= v0 ? (v1 - v0) / sk + 1 : 0;
+  const int npix = ncols * nrows;
+  if (npix > B.pmax) {
+    if (tid == 0) { O->valid = 0; O->stage = 0; set_err(&B.maps[m], SMG_E_CAP_PTS); }
+    return;
+  }
+  const double* T = F.T_mc;
+  // 1. back-projection in raster order (objmap.cpp:667-688), ordered compaction
+  int n = 0;
+  for (int c0 = 0; c0 < npix; c0 += blockDim.x) {
+    const int idx = c0 + tid;
+    int ok = 0;
+    double px = 0, py = 0, pz = 0, zz = 0;
+    int uu = 0, vv = 0;
+    if (idx < npix) {
+      const int r = idx / ncols, cc = idx - r * ncols;
+      uu = u0 + cc * sk;
+      vv = v0 + r * sk;
+      // mask cell (i, j) = pixel (u, v); 1-cell erosion; rows j < 1 or j >= MH-1 are skipped
+      if (vv >= 1 && vv < H - 1 && lab_is(F.label, W, H, uu, vv, L) && lab_is(F.label, W, H, uu - 1, vv, L) &&
+          lab_is(F.label, W, H, uu + 1, vv, L) && lab_is(F.label, W, H, uu, vv - 1, L) && lab_is(F.label, W, H, uu, vv + 1, L)) {
+        const float z = F.depth[(size_t)vv * W + uu];
+        if (z > P.zmin && z < P.zmax) {
+          const double xc = (double)(((float)uu - F.cx) / F.fx * z), yc = (double)(((float)vv - F.cy) / F.fy * z);
+          const double zd = (double)z;
+          px = T[0] * xc + T[1] * yc + T[2] * zd + T[3];
+          py = T[4] * xc + T[5] * yc + T[6] * zd + T[7];
+          pz = T[8] * xc + T[9] * yc + T[10] * zd + T[11];
+          zz = zd;
+          ok = 1;
+        }
+      }
+    }
+    int tot;
+    const int pos = block_excl_scan(ok, &tot, bs);
+    if (ok) {
+      X[n + pos] = px; Y[n + pos] = py; Z[n + pos] = pz; ZC[n + pos] = zz;
+      PU[n + pos] = uu; PV[n + pos] = vv;
+    }
+    n += tot;
+  }
+  if (n < P.min_points) {
+    if (tid == 0) { O->valid = 0; O->stage = 1; O->floor_drop = 0; }
+    return;
+  }
+  __syncthreads();
+  // 2. MAD depth band (objmap.cpp:692-695)
+  int nS = subsample_to(ZC, n, S);
+  const int kmed = pct_index(nS, 0.5);
+  const double zmed = block_select(S, nS, kmed, hist, bs);
+  for (int i = tid; i < nS; i += blockDim.x) S[i] = fabs(S[i] - zmed);
+  __syncthreads();
+  const double mad = block_select(S, nS, kmed, hist, bs);
+  const double band = smax(P.mad_k * 1.4826 * mad, P.mad_floor);
+  __syncthreads();
+  // 3. band filter, hand count, first point per voxel (objmap.cpp:696-719)
+  for (int i = tid; i < OBS_HASH; i += blockDim.x) { hkey[i] = ~0ull; hidx[i] = 0xffffffffu; }
+  __syncthreads();
+  const double hand2 = (double)(P.hand_r * P.hand_r), chand2 = P.cloud_hand_r * P.cloud_hand_r, body2 = P.body_r * P.body_r;
+  const double* E0 = F.eef[0];
+  const double* E1 = F.eef[1];
+  int near_local = 0, w = 0;
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    int keep = 0;
+    if (i < n) {
+      keep = !(fabs(ZC[i] - zmed) > band);
+      if (keep) {
+        const double x = X[i], y = Y[i], z = Z[i];
+        const double d0 = (x - E0[0]) * (x - E0[0]) + (y - E0[1]) * (y - E0[1]) + (z - E0[2]) * (z - E0[2]);
+        const double d1 = (x - E1[0]) * (x - E1[0]) + (y - E1[1]) * (y - E1[1]) + (z - E1[2]) * (z - E1[2]);
+        const double dh2 = smin(d0, d1);
+        near_local += dh2 < hand2;
+        const double bx = x - F.base[0], by = y - F.base[1];
+        if (dh2 >= chand2 && bx * bx + by * by >= body2) {
+          const uint64_t key = voxel_key((float)x, (float)y, (float)z, B.inv_vox);
+          uint32_t h = hmix(key) & (OBS_HASH - 1);
+          for (int probe = 0; probe < OBS_HASH; ++probe) {
+            const unsigned long long prev = atomicCAS((unsigned long long*)&hkey[h], ~0ull, (unsigned long long)key);
+            if (prev == ~0ull || prev == key) { atomicMin(&hidx[h], (uint32_t)i); break; }
+            h = (h + 1) & (OBS_HASH - 1);
+          }
+        }
+      }
+    }
+    int tot;
+    const int pos = block_excl_scan(keep, &tot, bs);
+    if (keep) { XK[w + pos] = X[i]; YK[w + pos] = Y[i]; ZK[w + pos] = Z[i]; }
+    w += tot;
+  }
+  const int near_hand = block_sum_i(near_local, bs);
+  const int np = w;
+  // emit the first point of each voxel, raster order
+  int nc = 0;
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    int emit = 0;
+    if (i < n && !(fabs(ZC[i] - zmed) > band)) {
+      const double x = X[i], y = Y[i], z = Z[i];
+      const double d0 = (x - E0[0]) * (x - E0[0]) + (y - E0[1]) * (y - E0[1]) + (z - E0[2]) * (z - E0[2]);
+      const double d1 = (x - E1[0]) * (x - E1[0]) + (y - E1[1]) * (y - E1[1]) + (z - E1[2]) * (z - E1[2]);
+      const double dh2 = smin(d0, d1);
+      const double bx = x - F.base[0], by = y - F.base[1];
+      if (dh2 >= chand2 && bx * bx + by * by >= body2) {
+        const uint64_t key = voxel_key((float)x, (float)y, (float)z, B.inv_vox);
+        uint32_t h = hmix(key) & (OBS_HASH - 1);
+        for (int probe = 0; probe < OBS_HASH; ++probe) {
+          if (hkey[h] == key) { emit = hidx[h] == (uint32_t)i; break; }
+          h = (h + 1) & (OBS_HASH - 1);
+        }
+      }
+    }
+    int tot;
+    const int pos = block_excl_scan(emit, &tot, bs);
+    if (emit) {
+      CX[3 * (nc + pos)] = (float)X[i];
+      CX[3 * (nc + pos) + 1] = (float)Y[i];
+      CX[3 * (nc + pos) + 2] = (float)Z[i];
+      CP[2 * (nc + pos)] = PU[i];
+      CP[2 * (nc + pos) + 1] = PV[i];
+    }
+    nc += tot;
+  }
+  if (np < P.min_points || (float)near_hand >= P.hand_frac * (float)np) {
+    if (tid == 0) { O->valid = 0; O->stage = 2; O->floor_drop = 0; }
+    return;
+  }
+  __syncthreads();
+  // 4. 10/50/90 percentiles per axis (objmap.cpp:730-738)
+  double lo[3], md[3], hi[3];
+  const double* AX[3] = {XK, YK, ZK};
+  for (int a = 0; a < 3; ++a) {
+    nS = subsample_to(AX[a], np, S);
+    md[a] = block_select(S, nS, pct_index(nS, 0.5), hist, bs);
+    lo[a] = block_select(S, nS, pct_index(nS, 0.1), hist, bs);
+    hi[a] = block_select(S, nS, pct_index(nS, 0.9), hist, bs);
+    __syncthreads();
+  }
+  const int trunc = (b[0] <= 2 || b[1] <= 2 || b[2] >= W - 3 || b[3] >= H - 3);
+  if (tid == 0) {
+    O->det = k;
+    O->sk = sk;
+    O->cls = F.cls[k];
+    O->score = F.score[k];
+    O->trunc = trunc;
+    O->n = np;
+    O->nc = nc;
+    O->zmed = zmed;
+    for (int a = 0; a < 3; ++a) { O->pos[a] = md[a]; O->lo[a] = lo[a]; O->hi[a] = hi[a]; O->ext[a] = hi[a] - lo[a]; }
+    O->floor_drop = hi[2] < P.floor_h;   // no floor-level class table: floorLevel() is false
+    // viewKappa of a detection fragment (objmap.cpp:757-762, bestview.cpp:77-81)
+    const float size_px = (float)sqrt((double)np * sk * sk / smax(1e-9, 1.0));
+    const float depth_m = (float)zmed;
+    O->kappa = view_kappa((double)fmaxf(0.f, size_px), trunc, (double)fmaxf(0.f, depth_m), P.kap_k0, P.kap_s0, P.kap_trunc,
+                          P.kap_d0, P.kap_occ, P.kap_blur_w, F.blur_fac);
+    O->obs_to = -1;
+    O->n_same = 0;
+    O->blocked = 0;
+    O->sec = 0;
+  }
+  if (hi[2] < P.floor_h) {
+    if (tid == 0) { O->valid = 0; O->stage = 3; }
+    return;
+  }
+  // 5. plane fit of the cloud candidates (apObsStructural, objmap.cpp:565-575)
+  double c0s = 0, c1s = 0, c2s = 0;
+  for (int i = tid; i < nc; i += blockDim.x) { c0s += CX[3 * i]; c1s += CX[3 * i + 1]; c2s += CX[3 * i + 2]; }
+  const double cen0 = block_sum_d(c0s, bs), cen1 = block_sum_d(c1s, bs), cen2 = block_sum_d(c2s, bs);
+  if (nc >= 8) {
+    const double dc = hypot3(cen0 / nc - T[3], cen1 / nc - T[7], cen2 / nc - T[11]);
+    const double tau = smin(P.ransac_tau_max, P.ransac_tau0 + P.ransac_tau_k * dc * dc);
+    const uint64_t sb = (uint64_t)__double_as_longlong(F.stamp);
+    plane_fit(CX, nc, tau, ap_seed(sb, (uint64_t)k), P.ransac_iters, B.need_tab, SCR, B.pmax, hist, bs, &pout);
+  } else if (tid == 0) {
+    pout.ok = 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    O->pl_ok = pout.ok;
+    for (int a = 0; a < 3; ++a) O->pl_n[a] = pout.n[a];
+    O->pl_thick = pout.thick;
+    O->pl_inl = pout.inl;
+    O->pl_zmed = pout.zmed;
+    O->pl_zlo = pout.zlo;
+    O->pl_zhi = pout.zhi;
+    O->pl_hspan = pout.hspan;
+    O->valid = 1;
+    O->stage = 4;
+  }
+}
+
+// Structural decision and observation list, in detection order (objmap.cpp:741-765 and the
+// apObsStructural branches at :576-621 with no wall segments and no text model).
+__global__ void k_obs_finalize(Batch B) {
+  const int m = blockIdx.x;
+  if (threadIdx.x != 0) return;
+  const FrameDev& F = B.frames[m];
+  MapRec* R = &B.maps[m];
+  if (!F.active) return;
+  const smg_params& P = B.p;
+  int n = 0;
+  for (int k = 0; k < F.n_det; ++k) {
+    ObsRec* O = &B.obs[(size_t)m * B.max_det + k];
+    if (!O->valid) {
+      if (O->stage == 3) ++R->st.n_floor;
+      continue;
+    }
+    ++R->st.n_obs;
+    bool drop = false;
+    if (O->nc >= 8 && O->pl_ok && !(O->pl_inl < P.plane_inl) && !(O->pl_thick > P.plane_thick)) {
+      const double nz = fabs(O->pl_n[2]);
+      if (nz > P.horiz) {
+        if (O->pl_zmed > 1.8) {
+          if (R->n_ceil >= SMG_CEIL_OBS) {
+            for (int i = 1; i < R->n_ceil; ++i) R->ceil_obs[i - 1] = R->ceil_obs[i];
+            --R->n_ceil;
+          }
+          R->ceil_obs[R->n_ceil++] = O->pl_zmed;
+          if (R->n_ceil >= 20) {   // nth_element value at size/2
+            const int kk = R->n_ceil / 2;
+            double val = 0;
+            for (int i = 0; i < R->n_ceil; ++i) {
+              int less = 0, eq = 0;
+              for (int j = 0; j < R->n_ceil; ++j) { less += R->ceil_obs[j] < R->ceil_obs[i]; eq += R->ceil_obs[j] == R->ceil_obs[i]; }
+              if (less <= kk && kk < less + eq) { val = R->ceil_obs[i]; break; }
+            }
+            R->ceil_est = val;
+          }
+        }
+        const double cz = R->ceil_est > 0 ? smin(P.ceil_z, R->ceil_est - P.ceil_band) : P.ceil_z;
+        if (O->pl_zmed > cz) { ++R->st.n_ceil; drop = true; }
+        else if (O->pl_zhi < P.floor_z) { ++R->st.n_floor; drop = true; }
+      } else if (!(nz > P.wall_vert)) {
+        const double cz = R->ceil_est > 0 ? R->ceil_est : P.ceil_z + 0.4;
+        const bool tall = O->pl_zhi - O->pl_zlo >= P.tall_h || (O->pl_zlo <= P.tall_floor && O->pl_zhi >= cz - P.tall_ceil);
+        const bool wide = O->pl_hspan >= P.tall_w_any;   // structure probability -1 < tall_ps
+        if (tall && wide) { ++R->st.n_wall_tall; drop = true; }
+      }
+    }
+    if (!drop) B.obs_list[(size_t)m * B.max_det + n++] = k;
+  }
+  R->n_obs = n;
+}

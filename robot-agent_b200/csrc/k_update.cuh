@@ -1,0 +1,393 @@
+// Object update of one keyframe, one CTA per map (scenemap src/objmap.cpp:807-1019).
+//
+// The reference's update is a sequence over observations whose later steps depend on the
+// earlier ones (fragments fuse into the first, largest one; new objects are appended mid-loop
+// and can capture later fragments).  That order is kept: thread 0 walks the observations and
+// takes every scalar decision; the whole block joins for the D-length work (r_frag += k z in
+// fp32, fp16 view encoding, the frame-grouping dot product, |r_frag|^2).  Parallelism comes from
+// the batch of maps (one CTA each).
+#pragma once
+#include "k_assoc.cuh"
+
+#define UPD_THREADS 256
+
+DEV size_t cslot_glob(const Batch& B, int m, const ObjRec& o) { return (size_t)m * B.O + o.cloud_slot; }
+
+// ObjectMap::firstView (objmap.cpp:247-252) over the view-first hash
+DEV int64_t view_cell_key(double x, double y, double cell) {
+  const long long i = (long long)floor(x / cell), j = (long long)floor(y / cell);
+  return (int64_t)(((unsigned long long)i << 32) ^ ((unsigned long long)j & 0xffffffffull));
+}
+DEV double first_view(const Batch& B, int m, double x, double y, double range) {
+  const double cell = smax(0.05, B.p.view_cell);
+  const int64_t key = view_cell_key(x, y, cell);
+  const int64_t* K = B.vkey + (size_t)m * B.view_slots;
+  uint32_t h = hmix((uint64_t)key) & (uint32_t)(B.view_slots - 1);
+  for (int probe = 0; probe < B.view_slots; ++probe) {
+    if (K[h] == INT64_MIN) return 1e300;
+    if (K[h] == key) {
+      int b = (int)ceil(range) - 1;
+      b = b < 0 ? 0 : (b > SMG_VIEW_BANDS - 1 ? SMG_VIEW_BANDS - 1 : b);
+      const double v = B.vfirst[((size_t)m * B.view_slots + h) * SMG_VIEW_BANDS + b];
+      return v < -1e299 ? 1e300 : v;
+    }
+    h = (h + 1) & (uint32_t)(B.view_slots - 1);
+  }
+  return 1e300;
+}
+
+// |r_frag|^2 refresh (ApState mu cache, objprob.cpp:228-240), block-wide
+DEV void refresh_nrm(const Batch& B, size_t og, BlockScratch& bs) {
+  const float* r = B.rfrag + og * B.D;
+  double s = 0;
+  for (int i = threadIdx.x; i < B.D; i += blockDim.x) s += (double)r[i] * (double)r[i];
+  s = block_sum_d(s, bs);
+  if (threadIdx.x == 0) B.objs[og].nrm_frag = s;
+  __syncthreads();
+}
+
+// apAddView (scenemap objprob.cpp:312-356) for a detection fragment (whole = false), no text
+// model.  Block-wide; z is the fp32 embedding (global).  Returns nothing (tempered kappa is only
+// used for the label terms, absent here).
+DEV void ap_add_view(const Batch& B, size_t og, const float* z_sh, double kappa, double stamp, const double cam[6],
+                     BlockScratch& bs) {
+  __shared__ double sh_k;
+  __shared__ int sh_free;
+  ObjRec& o = B.objs[og];
+  const int tid = threadIdx.x, D = B.D;
+  if (tid == 0) {
+    double k = kappa;
+    const double cmin = B.cos_temper;
+    for (int c = 0; c < o.n_cams; ++c) {
+      const double* cc = o.cams[c];
+      if (fabs(cc[6] - stamp) < 1e-6) continue;
+      const double dd = hypot3(cc[0] - cam[0], cc[1] - cam[1], cc[2] - cam[2]);
+      const double ca = cc[3] * cam[3] + cc[4] * cam[4] + cc[5] * cam[5];
+      if (dd < B.p.temper_d && ca > cmin) { k = kappa * B.p.temper; break; }
+    }
+    if (o.n_cams >= SMG_CAMS) {   // keep the newest 32 (push, then erase the front)
+      for (int c = 1; c < SMG_CAMS; ++c)
+        for (int j = 0; j < 7; ++j) o.cams[c - 1][j] = o.cams[c][j];
+      o.n_cams = SMG_CAMS - 1;
+    }
+    for (int j = 0; j < 6; ++j) o.cams[o.n_cams][j] = cam[j];
+    o.cams[o.n_cams][6] = stamp;
+    ++o.n_cams;
+    ++o.ver;
+    o.k_frag += k;
+    sh_k = k;
+    // free physical view slot: the one of 0..topk not referenced by the current views
+    int used = 0;
+    for (int v = 0; v < o.n_views; ++v) used |= 1 << o.view_slot[v];
+    int f = 0;
+    while (used & (1 << f)) ++f;
+    sh_free = f;
+  }
+  __syncthreads();
+  const double k = sh_k;
+  float* r = B.rfrag + og * D;
+  uint16_t* vz = B.views + (og * (B.topk + 1) + sh_free) * D;
+  for (int i = tid; i < D; i += blockDim.x) {
+    const float zi = z_sh[i];
+    r[i] += (float)(k * (double)zi);
+    vz[i] = ref_f2h(zi);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // stable sort by (whole desc, kappa desc): every view is a fragment, so insert after the
+    // views whose kappa is >= the new one, then keep the top-k
+    const float kv = (float)kappa;
+    int pos = o.n_views;
+    while (pos > 0 && o.vkappa[pos - 1] < kv) --pos;
+    for (int v = o.n_views; v > pos; --v) {
+      o.view_slot[v] = o.view_slot[v - 1];
+      o.vkappa[v] = o.vkappa[v - 1];
+      o.vstamp[v] = o.vstamp[v - 1];
+    }
+    o.view_slot[pos] = sh_free;
+    o.vkappa[pos] = kv;
+    o.vstamp[pos] = stamp;
+    ++o.n_views;
+    if (o.n_views > B.topk) o.n_views = B.topk;
+  }
+  __syncthreads();
+  refresh_nrm(B, og, bs);
+}
+
+// allocate an object slot + cloud slot for a new object (appended at list position n_obj)
+DEV int new_object_slot(const Batch& B, int m, int* cslot) {
+  MapRec* R = &B.maps[m];
+  if (R->n_free <= 0 || R->n_cfree <= 0 || R->n_obj >= B.O) { set_err(R, SMG_E_CAP_OBJ); return -1; }
+  const int slot = B.freel[(size_t)m * B.O + --R->n_free];
+  *cslot = B.cfreel[(size_t)m * B.O + --R->n_cfree];
+  B.order[(size_t)m * B.O + R->n_obj++] = slot;
+  return slot;
+}
+
+__global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
+  extern __shared__ unsigned char smem_raw[];
+  float* zs = (float*)smem_raw;   // D
+  __shared__ BlockScratch bs;
+  __shared__ int sh_act, sh_slot, sh_cslot, sh_go;
+  __shared__ int head[SMG_MAX_DET];
+  __shared__ int evn;
+  const int m = blockIdx.x, tid = threadIdx.x;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  MapRec* R = &B.maps[m];
+  const smg_params& P = B.p;
+  const double* T = F.T_mc;
+  const int nobs = R->n_obs;
+  const bool has_z = F.emb != nullptr;
+  ObsRec* OB = B.obs + (size_t)m * B.max_det;
+  const int32_t* OL = B.obs_list + (size_t)m * B.max_det;
+  const double cam6[6] = {T[3], T[7], T[11], T[2], T[6], T[10]};
+  if (tid == 0) {
+    evn = 0;
+    // association bookkeeping (objmap.cpp:807-809)
+    for (int a = 0; a < nobs; ++a) {
+      ObsRec& o = OB[OL[a]];
+      if (P.bridge_drop && o.n_same >= 2 && o.obs_to >= 0) { o.obs_to = -2; ++R->st.n_bridge; continue; }
+      if (o.obs_to >= 0) { B.obj_hit[(size_t)m * B.O + o.obs_to] = 1; ++R->st.n_assoc; }
+      else if (o.blocked) { o.obs_to = -2; ++R->st.n_blocked; }
+    }
+    // fragment fusion (objmap.cpp:812-835): head = first fragment with the most points
+    for (int a = 0; a < nobs; ++a) {
+      head[a] = -1;
+      const int b = OB[OL[a]].obs_to;
+      if (b < 0) continue;
+      int h = -1;
+      for (int a2 = 0; a2 < nobs; ++a2)
+        if (OB[OL[a2]].obs_to == b && (h < 0 || OB[OL[a2]].n > OB[OL[h]].n)) h = a2;
+      head[a] = h;
+    }
+    for (int a = 0; a < nobs; ++a) {
+      ObsRec& o = OB[OL[a]];
+      const int b = o.obs_to;
+      if (b < 0 || head[a] == a) continue;
+      ObsRec& h = OB[OL[head[a]]];
+      const double wh = h.n, wo = o.n;
+      for (int k = 0; k < 3; ++k) {
+        h.lo[k] = smin(h.lo[k], o.lo[k]);
+        h.hi[k] = smax(h.hi[k], o.hi[k]);
+        h.pos[k] = (h.pos[k] * wh + o.pos[k] * wo) / (wh + wo);
+        h.ext[k] = h.hi[k] - h.lo[k];
+      }
+      h.n += o.n;
+      h.trunc = h.trunc || o.trunc;
+      h.zmed = smin(h.zmed, o.zmed);
+      h.score = (h.score < o.score) ? o.score : h.score;
+      o.sec = 1;
+    }
+  }
+  __syncthreads();
+  // update loop (objmap.cpp:837-997)
+  for (int a = 0; a < nobs; ++a) {
+    if (tid == 0) {
+      ObsRec& o = OB[OL[a]];
+      AssocRec& as = B.assoc[(size_t)m * B.max_det + o.det];
+      as.n_valid = o.n;
+      as.area_px = (float)o.n * o.sk * o.sk;
+      as.depth_med = (float)o.zmed;
+      sh_act = 0;
+      if (o.obs_to >= 0) {
+        sh_act = 1;
+        sh_slot = slot_at(B, m, o.obs_to);
+        as.obj_id = B.objs[oglob(B, m, sh_slot)].id;
+      } else if (o.obs_to == -1) {
+        int cs = -1;
+        const int s = new_object_slot(B, m, &cs);
+        if (s >= 0) { sh_act = 2; sh_slot = s; sh_cslot = cs; }
+      }
+    }
+    __syncthreads();
+    const int act = sh_act;
+    ObsRec& o = OB[OL[a]];
+    if (act != 0 && has_z) {
+      for (int i = tid; i < B.D; i += blockDim.x) zs[i] = emb_at(F.emb, F.emb_dtype, B.D, o.det, i);
+    }
+    __syncthreads();
+    const size_t og = oglob(B, m, sh_slot);
+    if (act == 1) {
+      if (has_z) ap_add_view(B, og, zs, o.kappa, F.stamp, cam6, bs);
+      if (tid == 0) {
+        ObjRec& mo = B.objs[og];
+        ++mo.n_ap_obs;
+        mo.wall_like = 2 * mo.n_wall_obs >= mo.n_ap_obs;
+        if (!o.sec) {
+          const double dt_seen = F.stamp - mo.last_seen;
+          if (mo.last_kf != F.stamp) ++mo.n_obs;
+          mo.last_kf = F.stamp;
+          const bool big = smax(smax(mo.hi[0] - mo.lo[0], mo.hi[1] - mo.lo[1]), smax(o.ext[0], o.ext[1])) > P.big;
+          bool snap = false;
+          if (P.move_n > 0 && mo.trk_t > 0 && !o.trunc && F.cam_steady) {
+            const double dt = F.stamp - mo.trk_t;
+            const double sx = o.pos[0] - mo.trk_pos[0], sy = o.pos[1] - mo.trk_pos[1];
+            const double sp = dt > 1e-6 && dt <= 0.6 ? sqrt(sx * sx + sy * sy) / dt : 0.0;
+            const bool same_dir = sx * mo.trk_step[0] + sy * mo.trk_step[1] > 0;
+            mo.mv_cnt = sp > P.move_v && (same_dir || mo.mv_cnt == 0) ? mo.mv_cnt + 1 : 0;
+            mo.trk_step[0] = sx;
+            mo.trk_step[1] = sy;
+            const double rx = o.pos[0] - mo.pos[0], ry = o.pos[1] - mo.pos[1];
+            const double away = sqrt(rx * rx + ry * ry);
+            const bool moving = F.stamp - mo.moving_t < 1.0;
+            const bool left = away > smax(P.move_min_d, 0.5 * smax(o.ext[0], o.ext[1])) &&
+                              box_overlap(o.lo, o.hi, mo.lo, mo.hi, P.merge_min_ext) < 0.1;
+            if (mo.mv_cnt >= P.move_n && (moving || left)) {
+              if (!moving) mo.move_from_t = F.stamp;
+              mo.moving_t = F.stamp;
+              snap = true;
+            } else if (moving && sp > 0.5 * P.move_v) {
+              snap = true;
+              mo.moving_t = F.stamp;
+            }
+          }
+          if (!o.trunc) {
+            for (int k = 0; k < 3; ++k) mo.trk_pos[k] = o.pos[k];
+            mo.trk_t = F.stamp;
+          }
+          if (snap) {
+            double d3[3];
+            for (int k = 0; k < 3; ++k) {
+              d3[k] = o.pos[k] - mo.pos[k];
+              mo.pos[k] = o.pos[k]; mo.ext[k] = o.ext[k]; mo.lo[k] = o.lo[k]; mo.hi[k] = o.hi[k];
+            }
+            CloudRec& C = B.clouds[cslot_glob(B, m, mo)];
+            if (C.n > 0 && !(d3[0] == 0 && d3[1] == 0 && d3[2] == 0)) {   // ObjCloud::translate (cloud.cpp:79-84)
+              for (int k = 0; k < 3; ++k) C.org[k] += d3[k];
+              ++C.version;
+              C.stamp = F.stamp;
+            }
+            if (dist3(mo.pos, mo.first_pos) > P.moved_d) mo.moved = 1;
+            if (mo.moved && mo.state == 0) mo.state = 2;
+          }
+          const bool fresh = mo.first_seen == F.stamp;
+          for (int k = 0; k < 3 && !snap; ++k) {
+            if (fresh) {
+              mo.lo[k] = smin(mo.lo[k], o.lo[k]);
+              mo.hi[k] = smax(mo.hi[k], o.hi[k]);
+              mo.pos[k] = 0.5 * (mo.lo[k] + mo.hi[k]);
+              mo.ext[k] = mo.hi[k] - mo.lo[k];
+              continue;
+            }
+            if (big) {
+              const double lo = smax(smin(mo.lo[k], o.lo[k]), mo.lo[k] - P.grow_max);
+              const double hi = smin(smax(mo.hi[k], o.hi[k]), mo.hi[k] + P.grow_max);
+              if (hi - lo <= P.max_ext) { mo.lo[k] = lo; mo.hi[k] = hi; }
+              mo.pos[k] = 0.5 * (mo.lo[k] + mo.hi[k]);
+              mo.ext[k] = mo.hi[k] - mo.lo[k];
+            } else {
+              const double K = kalman_gain(mo.P[k], P.ap_q_pos, dt_seen, kalman_R(P.ap_r0, P.ap_r1, o.zmed, o.trunc, o.ext[k]));
+              mo.pos[k] += K * (o.pos[k] - mo.pos[k]);
+              mo.lo[k] += K * (o.lo[k] - mo.lo[k]);
+              mo.hi[k] += K * (o.hi[k] - mo.hi[k]);
+              mo.ext[k] = mo.hi[k] - mo.lo[k];
+            }
+            if (big) kalman_big(mo.P[k], P.ap_q_pos, dt_seen, P.ap_r0 + P.ap_r1 * o.zmed, mo.ext[k]);
+          }
+          mo.score = (mo.score < o.score) ? o.score : mo.score;
+          mo.max_det_z = smax(mo.max_det_z, o.zmed);
+          mo.last_seen = F.stamp;
+          mo.misses = 0;
+          if (mo.state == 1) {
+            mo.state = mo.moved ? 2 : 0;
+            push_event(B, m, F.stamp, mo, 6, (2u << 24) | (uint32_t)evn++);
+          }
+          if (!mo.confirmed && (int)mo.n_obs >= P.confirm) {
+            mo.confirmed = 1;
+            push_event(B, m, F.stamp, mo, 1, (2u << 24) | (uint32_t)evn++);
+          }
+        }
+      }
+    } else if (act == 2) {
+      if (tid == 0) {   // new candidate (objmap.cpp:951-978)
+        ObjRec& mo = B.objs[og];
+        const int cs = sh_cslot;
+        memset(&mo, 0, sizeof(ObjRec));
+        mo.id = R->next_id++;
+        mo.cls = o.cls;
+        for (int k = 0; k < 3; ++k) { mo.pos[k] = mo.first_pos[k] = o.pos[k]; mo.ext[k] = o.ext[k]; mo.lo[k] = o.lo[k]; mo.hi[k] = o.hi[k]; }
+        mo.n_obs = 1;
+        mo.first_seen = mo.last_seen = mo.last_kf = F.stamp;
+        for (int k = 0; k < 3; ++k) mo.trk_pos[k] = o.pos[k];
+        mo.trk_t = F.stamp;
+        mo.score = o.score;
+        mo.max_det_z = o.zmed;
+        mo.moving_t = -1e300;
+        {
+          const double hx = o.pos[0] - T[3], hy = o.pos[1] - T[7];
+          mo.appeared = first_view(B, m, o.pos[0], o.pos[1], sqrt(hx * hx + hy * hy) + P.view_cell) < F.stamp - P.link_view_gap_s;
+        }
+        mo.confirmed = P.confirm <= 1;
+        B.assoc[(size_t)m * B.max_det + o.det].obj_id = mo.id;
+        mo.cloud_slot = cs;
+        mo.need_whole = 1;
+        mo.geo_ver = 0xffffffffu;
+        const double sd = P.ap_r0 + P.ap_r1 * o.zmed;
+        for (int k = 0; k < 3; ++k) mo.P[k] = sd * sd + (o.trunc ? 0.25 * o.ext[k] * o.ext[k] : 0.0);
+        CloudRec& C = B.clouds[(size_t)m * B.O + cs];
+        C.has_org = 0;
+        C.n = 0;
+        C.version = 0;
+        C.seq = 0;
+        C.stamp = 0;
+        C.cn = 0;
+        ++C.cgen;
+        ++C.vgen;
+        C.cver = 0xffffffffu;
+        B.touched[(size_t)m * B.O + R->n_obj - 1] = 1;
+        B.obj_hit[(size_t)m * B.O + R->n_obj - 1] = 1;
+      }
+      __syncthreads();
+      {   // a recycled slot starts from an empty r_frag (objprob.cpp:329 assigns zeros)
+        float* r = B.rfrag + og * B.D;
+        for (int i = tid; i < B.D; i += blockDim.x) r[i] = 0.f;
+        __syncthreads();
+      }
+      if (has_z) ap_add_view(B, og, zs, o.kappa, F.stamp, cam6, bs);
+      if (tid == 0) {
+        ObjRec& mo = B.objs[og];
+        mo.n_ap_obs = 1;
+        mo.n_wall_obs = 0;
+        mo.n_struct_look = 0;
+        mo.wall_like = 0;
+        ++R->st.n_new;
+      }
+      // frame grouping (objmap.cpp:980-995): later unmatched fragments touching this one
+      if (P.frame_group) {
+        for (int b2 = a + 1; b2 < nobs; ++b2) {
+          if (tid == 0) {
+            const ObsRec& q = OB[OL[b2]];
+            sh_go = 0;
+            if (q.obs_to == -1 && has_z) {
+              double g2 = 0;
+              for (int k = 0; k < 3; ++k) {
+                const double g = smax3(0.0, q.lo[k] - o.hi[k], o.lo[k] - q.hi[k]);
+                g2 += g * g;
+              }
+              sh_go = !(g2 > 0.02 * 0.02);
+            }
+          }
+          __syncthreads();
+          if (sh_go) {
+            const ObsRec& q = OB[OL[b2]];
+            double dot = 0;
+            for (int i = tid; i < B.D; i += blockDim.x)
+              dot += (double)emb_at(F.emb, F.emb_dtype, B.D, q.det, i) * (double)zs[i];
+            dot = block_sum_d(dot, bs);
+            if (tid == 0) {
+              double f[7] = {0, 0, 0, 0, 0, 0, 0};
+              pair_geo(q.lo, q.hi, q.pos, o.lo, o.hi, o.pos, dot, P.cos0, f);
+              f[0] = 1.0;
+              if (1.0 / (1.0 + exp(-same_logit(P.w, f))) >= P.same_p) OB[OL[b2]].obs_to = R->n_obj - 1;
+            }
+          }
+          __syncthreads();
+        }
+      }
+      if (tid == 0) push_event(B, m, F.stamp, B.objs[og], 0, (2u << 24) | (uint32_t)evn++);
+    }
+    __syncthreads();
+  }
+  if (tid == 0) R->n_evn = evn;
+}

@@ -1,0 +1,727 @@
+// C ABI of the B200 scenemap objprob update (include/smg.h): parameters, batch allocation,
+// the per-keyframe launch chain, and device->host getters.
+//
+// Launch chain of one smg_push_frames call (all maps of the batch in every launch):
+//   k_begin         per-frame resets
+//   k_merge_pairs   apMergePass pair evaluation        (objmap.cpp:1154-1200)
+//   k_merge_apply   greedy merges (absorb + apMerge)   (objmap.cpp:1202-1224)
+//   k_obs           back-projection .. plane fit       (objmap.cpp:645-765)
+//   k_obs_finalize  structural decisions, obs list     (objmap.cpp:576-621)
+//   k_assoc         association                        (objmap.cpp:767-810)
+//   k_update        fusion, update, new objects        (objmap.cpp:811-997)
+//   k_absent        absence / misses                   (objmap.cpp:1020-1061)
+//   k_relink        cloud lists + relink               (objmap.cpp:1010-1019, 1062)
+//   k_struct        merged-cloud geometry              (objmap.cpp:1064, 1255-1319)
+//   k_prune         drop / prune, cloud targets        (objmap.cpp:1066-1073)
+//   k_markview      seen cells                         (objmap.cpp:1084)
+//   k_cloud_add     ObjectMap::addPoints + contact     (capi.cpp:986-992, cloud.cpp:86-127)
+//   k_grid          makeScan + insert policy + insert  (mapper2d.cpp:100-160)
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "k_grid.cuh"
+
+static thread_local std::string g_err;
+static int fail(int code, const char* msg) {
+  g_err = msg;
+  return code;
+}
+#define CK(x)                                                     \
+  do {                                                            \
+    cudaError_t e_ = (x);                                         \
+    if (e_ != cudaSuccess) {                                      \
+      g_err = std::string(#x) + ": " + cudaGetErrorString(e_);    \
+      return SMG_ERR_DEVICE;                                      \
+    }                                                             \
+  } while (0)
+
+struct smg_batch {
+  Batch B;
+  int dev;
+  int max_w, max_h;
+  std::vector<void*> allocs;
+  FrameDev* h_frames = nullptr;   // pinned
+  float* d_depth = nullptr;       // staging for SMG_MEM_HOST
+  uint16_t* d_label = nullptr;
+  unsigned char* d_emb = nullptr;
+  std::vector<double> last_cam_t, last_cam_fwd;
+  long long launches = 0;
+  cudaStream_t last_stream = nullptr;
+};
+
+extern "C" int smg_destroy(smg_batch* b);
+template <class T>
+static int dalloc(smg_batch* b, T** p, size_t n, int fill_byte = 0) {
+  void* q = nullptr;
+  const size_t bytes = std::max<size_t>(n, 1) * sizeof(T);
+  CK(cudaMalloc(&q, bytes));
+  CK(cudaMemset(q, fill_byte, bytes));
+  b->allocs.push_back(q);
+  *p = (T*)q;
+  return SMG_OK;
+}
+#define DA(ptr, n)                                 \
+  do {                                             \
+    int r_ = dalloc(b, &(ptr), (size_t)(n));       \
+    if (r_) { smg_destroy(b); return r_; }         \
+  } while (0)
+
+__global__ void k_fill_d(double* p, size_t n, double v) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
+}
+__global__ void k_fill_i64(int64_t* p, size_t n, int64_t v) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
+}
+__global__ void k_fill_i8(int8_t* p, size_t n, int8_t v) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
+}
+
+
+extern "C" {
+
+const char* smg_last_error(void) { return g_err.c_str(); }
+
+int smg_params_size(void) { return (int)sizeof(smg_params); }
+
+int smg_params_default(smg_params* p) {
+  if (!p) return SMG_ERR_ARGS;
+  memset(p, 0, sizeof(*p));
+  // ObjParams (objmap.hpp:50-129)
+  p->min_points = 20;
+  p->zmin = 0.15f; p->zmax = 3.0f; p->hand_r = 0.10f; p->hand_frac = 0.5f;
+  p->big = 0.5; p->confirm = 2; p->prune_s = 10.0; p->moved_d = 0.15; p->gone_misses = 3; p->gone_min_s = 2.0;
+  p->mad_k = 3.0; p->mad_floor = 0.10; p->grow_max = 0.25; p->max_ext = 4.0; p->occl = 0.10; p->min_px = 6;
+  p->self_pad = 0.01; p->step = 1; p->max_pts = 6000; p->voxel = 0.02; p->cloud_cap = 8000; p->cloud_hand_r = 0.05;
+  p->body_r = 0.22; p->merge_min_ext = 0.05; p->floor_h = 0.05; p->absent_samples = 48; p->absent_vis = 0.5;
+  p->absent_min_px = 12; p->absent_det_k = 1.15; p->gone_misses_big = 6; p->gone_min_s_big = 4.0; p->spurious_obs = 5;
+  p->gone_view_d = 0.5; p->gone_step_d = 0.10; p->gone_step_deg = 5.0; p->gone_eps = 0.02;
+  p->link_v = 1.0; p->link_d0 = 1.0; p->link_max_d = 8.0; p->link_min_obs = 3; p->link_wait_s = 30.0;
+  p->link_window_s = 180.0; p->link_view_gap_s = 5.0; p->view_cell = 0.5;
+  p->move_n = 3; p->move_v = 0.3; p->move_min_d = 0.25; p->move_max_cam_w = 0.6;
+  p->ap_q_pos = 1e-4; p->ap_r0 = 0.02; p->ap_r1 = 0.01;
+  // ApParams (objprob.hpp:56-142)
+  p->same_p = 0.6; p->merge_p = 0.7;
+  const double w[8] = {-5.116, 4.553, -4.976, 0.376, 8.814, 1.824, -0.186, 0.0};
+  const double wm[8] = {-4.265, 1.094, -3.378, 0.627, 8.823, 3.205, -2.500, 1.717};
+  memcpy(p->w, w, sizeof w);
+  memcpy(p->wm, wm, sizeof wm);
+  p->guard_obj = 0.6; p->guard_obs = 0.2; p->name_veto = 0; p->bridge_drop = 0; p->frame_group = 1;
+  p->cos0 = 0.75; p->gate = 0.30; p->contact_cell = 0.04; p->contact_samples = 160; p->topk = 5;
+  p->temper_d = 0.30; p->temper_deg = 15.0; p->temper = 0.3; p->kappa_ref = 3000;
+  p->plane_thick = 0.035; p->ransac_tau0 = 0.01; p->ransac_tau_k = 0.0025; p->ransac_tau_max = 0.05; p->obj_tau = 0.02;
+  p->plane_inl = 0.8; p->obj_plane_inl = 0.92; p->ransac_iters = 64;
+  p->wall_vert = 0.30; p->ceil_z = 2.0; p->horiz = 0.85; p->floor_z = 0.06; p->ceil_band = 0.35; p->ceil_frac = 0.5;
+  p->ceil_wide = 0.6; p->tall_h = 1.7; p->tall_floor = 0.3; p->tall_ceil = 0.4; p->tall_w = 1.5; p->tall_ps = 0.3;
+  p->tall_w_any = 3.0; p->obj_wall_span = 1.5; p->obj_wall_top = 1.9; p->obj_wall_h = 1.0; p->obj_thick = 0.04;
+  p->struct_obj_p = 0.6; p->struct_obj_min_views = 2; p->link_cos = 0.8;
+  // KappaParams (bestview.hpp:67-69)
+  p->kap_k0 = 4369; p->kap_s0 = 40; p->kap_trunc = 1.0; p->kap_d0 = 100.0; p->kap_occ = 1.0; p->kap_blur_w = 0.0;
+  // GridParams (grid.hpp:18-21), ScanParams (scan.hpp:37-48), MapperParams (mapper2d.hpp:14-26)
+  p->grid_res = 0.05f; p->l_hit = 0.85f; p->l_miss = -0.4f; p->l_min = -4.f; p->l_max = 4.f;
+  p->scan_zmin = 0.3f; p->scan_zmax = 3.0f; p->band_lo = 0.05f; p->band_hi = 0.50f; p->bins = 720;
+  p->self_r = 0.22f; p->eef_r = 0.08f; p->arm_r = 0.06f;
+  for (int s = 0; s < 2; ++s) { p->shoulder[s][0] = -0.05f; p->shoulder[s][1] = 0.f; p->shoulder[s][2] = 0.25f; }
+  p->match_hi = 3.0f; p->vert_nz = 0.7f; p->match_cell = 0.025f; p->dense = 1;
+  p->change_bins = 2; p->change_cells = 1; p->still_every = 50;
+  return SMG_OK;
+}
+
+// ObjectMap::applyParams key table (scenemap src/objmap.cpp:135-180).  Keys of features this
+// build does not run (text model, wall segments, re-encode, inspect) are accepted and stored
+// nowhere, like a field the caller never reads.
+int smg_params_apply(smg_params* p, const char* kv) {
+  if (!p) return SMG_ERR_ARGS;
+  if (!kv || !*kv) return 0;
+  struct K { const char* n; double* d; int32_t* i; };
+  static double sink_d;
+  static int32_t sink_i;
+  const K keys[] = {
+      {"floor_h", &p->floor_h, 0}, {"absent_samples", 0, &p->absent_samples}, {"absent_vis", &p->absent_vis, 0},
+      {"absent_min_px", &p->absent_min_px, 0}, {"absent_det_k", &p->absent_det_k, 0}, {"gone_misses", 0, &p->gone_misses},
+      {"gone_min_s", &p->gone_min_s, 0}, {"gone_misses_big", 0, &p->gone_misses_big}, {"gone_min_s_big", &p->gone_min_s_big, 0},
+      {"gone_view_d", &p->gone_view_d, 0}, {"gone_eps", &p->gone_eps, 0}, {"gone_step_d", &p->gone_step_d, 0},
+      {"gone_step_deg", &p->gone_step_deg, 0}, {"spurious_obs", 0, &p->spurious_obs}, {"link_v", &p->link_v, 0},
+      {"link_d0", &p->link_d0, 0}, {"link_max_d", &p->link_max_d, 0}, {"link_min_obs", 0, &p->link_min_obs},
+      {"link_wait_s", &p->link_wait_s, 0}, {"link_window_s", &p->link_window_s, 0}, {"link_view_gap_s", &p->link_view_gap_s, 0},
+      {"view_cell", &p->view_cell, 0}, {"confirm", 0, &p->confirm}, {"move_v", &p->move_v, 0}, {"move_n", 0, &p->move_n},
+      {"move_min_d", &p->move_min_d, 0}, {"move_max_cam_w", &p->move_max_cam_w, 0}, {"self_pad", &p->self_pad, 0},
+      {"inspect", 0, &sink_i},
+      {"ap_same_p", &p->same_p, 0}, {"ap_merge_p", &p->merge_p, 0}, {"ap_gate", &p->gate, 0}, {"ap_name_tau", &sink_d, 0},
+      {"ap_name_wmax", &sink_d, 0}, {"ap_size_w", &sink_d, 0}, {"ap_kappa_ref", &p->kappa_ref, 0}, {"ap_temper", &p->temper, 0},
+      {"ap_wall_big", &sink_d, 0}, {"ap_struct_p", &sink_d, 0}, {"ap_ceil_z", &p->ceil_z, 0}, {"ap_struct_obj_p", &p->struct_obj_p, 0},
+      {"ap_obj_wall_span", &p->obj_wall_span, 0}, {"ap_obj_wall_top", &p->obj_wall_top, 0}, {"ap_reenc_max", 0, &sink_i},
+      {"ap_reenc_gain", &sink_d, 0}, {"ap_link_cos", &p->link_cos, 0}, {"ap_whole_w", &sink_d, 0}, {"ap_export_named", 0, &sink_i},
+      {"ap_guard_obj", &p->guard_obj, 0}, {"ap_guard_obs", &p->guard_obs, 0}, {"ap_geo_w", &sink_d, 0},
+      {"ap_name_veto", &p->name_veto, 0}, {"ap_through_d", &sink_d, 0}, {"ap_bridge_max", &sink_d, 0},
+      {"ap_frame_group", 0, &p->frame_group}, {"ap_struct_obj_min_views", 0, &p->struct_obj_min_views},
+      {"ap_plane_inl", &p->plane_inl, 0}, {"ap_obj_plane_inl", &p->obj_plane_inl, 0}, {"ap_ransac_tau0", &p->ransac_tau0, 0},
+      {"ap_ransac_tau_k", &p->ransac_tau_k, 0}, {"ap_obj_tau", &p->obj_tau, 0}, {"ap_ransac_iters", 0, &p->ransac_iters},
+      {"ap_so_dw_w", &sink_d, 0}, {"ap_so_dw_thick", &sink_d, 0}, {"ap_so_max_h", &sink_d, 0}, {"ap_so_pillar", &sink_d, 0},
+      {"ap_so_stairs", &sink_d, 0}, {"ap_wallhug_frac", &sink_d, 0}, {"ap_wallhug_w", &sink_d, 0},
+      {"ap_struct_look_block", 0, &sink_i}, {"ap_flat_max_w", &sink_d, 0}, {"ap_tall_h", &p->tall_h, 0}, {"ap_tall_w", &p->tall_w, 0},
+      {"ap_tall_ps", &p->tall_ps, 0}, {"ap_tall_w_any", &p->tall_w_any, 0}, {"ap_big_vinl", &sink_d, 0}, {"ap_so_dw_min", &sink_d, 0},
+      {"ap_so_hide_k", &sink_d, 0},
+      {"ap_w0", &p->w[0], 0}, {"ap_w1", &p->w[1], 0}, {"ap_w2", &p->w[2], 0}, {"ap_w3", &p->w[3], 0}, {"ap_w4", &p->w[4], 0},
+      {"ap_w5", &p->w[5], 0}, {"ap_w6", &p->w[6], 0}, {"ap_w7", &p->w[7], 0},
+      {"ap_wm0", &p->wm[0], 0}, {"ap_wm1", &p->wm[1], 0}, {"ap_wm2", &p->wm[2], 0}, {"ap_wm3", &p->wm[3], 0}, {"ap_wm4", &p->wm[4], 0},
+      {"ap_wm5", &p->wm[5], 0}, {"ap_wm6", &p->wm[6], 0}, {"ap_wm7", &p->wm[7], 0},
+      {"ap_cos0", &p->cos0, 0}, {"ap_bridge_drop", 0, &p->bridge_drop},
+      {"kap_k0", &p->kap_k0, 0}, {"kap_s0", &p->kap_s0, 0}, {"kap_trunc", &p->kap_trunc, 0}, {"kap_d0", &p->kap_d0, 0}};
+  int n_bad = 0;
+  std::string s(kv);
+  size_t a = 0;
+  while (a < s.size()) {
+    size_t b = s.find(',', a);
+    if (b == std::string::npos) b = s.size();
+    const std::string item = s.substr(a, b - a);
+    a = b + 1;
+    const size_t q = item.find('=');
+    if (q == std::string::npos) continue;
+    const std::string k = item.substr(0, q);
+    const double v = atof(item.c_str() + q + 1);
+    bool ok = false;
+    for (const K& x : keys)
+      if (k == x.n) {
+        if (x.d) *x.d = v;
+        if (x.i) *x.i = (x.i == &p->bridge_drop || x.i == &p->frame_group) ? (v != 0) : (int32_t)v;
+        ok = true;
+      }
+    if (!ok) ++n_bad;
+  }
+  if (n_bad) g_err = "unknown parameter key";
+  return n_bad;
+}
+
+int smg_destroy(smg_batch* b) {
+  if (!b) return SMG_ERR_ARGS;
+  for (void* p : b->allocs) cudaFree(p);
+  if (b->h_frames) cudaFreeHost(b->h_frames);
+  delete b;
+  return SMG_OK;
+}
+
+static int pow2_at_least(long long n) {
+  int v = 1;
+  while (v < n) v <<= 1;
+  return v;
+}
+
+int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, int max_w, int max_h, int max_det, int grid_w,
+               int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out) {
+  if (!p || !out || n_maps <= 0 || max_objects <= 0 || emb_dim <= 0 || emb_dim > 2048 || max_w <= 0 || max_h <= 0 || max_det <= 0 ||
+      max_det > SMG_MAX_DET || grid_w <= 0 || grid_h <= 0 || p->topk <= 0 || p->topk > SMG_TOPK_MAX || p->bins <= 0 ||
+      p->bins > SMG_BINS_MAX || p->cloud_cap <= 0 || p->voxel <= 0)
+    return fail(SMG_ERR_ARGS, "smg_create: bad arguments");
+  *out = nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || dev < 0 || dev >= ndev) return fail(SMG_ERR_DEVICE, "smg_create: no CUDA device");
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major < 10)
+    return fail(SMG_ERR_DEVICE, "smg_create: needs an sm_100 device");
+  if (cudaSetDevice(dev) != cudaSuccess) return fail(SMG_ERR_DEVICE, "smg_create: cudaSetDevice");
+  smg_batch* b = new smg_batch();
+  b->dev = dev;
+  b->max_w = max_w;
+  b->max_h = max_h;
+  Batch& B = b->B;
+  memset(&B, 0, sizeof(B));
+  const int M = n_maps, O = max_objects, D = emb_dim;
+  B.M = M; B.O = O; B.D = D; B.topk = p->topk; B.max_det = max_det; B.W = max_w; B.H = max_h;
+  B.p = *p;
+  B.cap = 2 * p->cloud_cap;
+  B.HC = pow2_at_least(2LL * B.cap);
+  B.HCC = pow2_at_least(2LL * p->cloud_cap);
+  {   // box scan bound: max_pts + rows + cols + 1 (objmap.cpp:652), at least cloud_cap for merges
+    const long long pm = std::max<long long>((long long)p->max_pts + max_w + max_h + 1, p->cloud_cap);
+    B.pmax = pow2_at_least(pm);
+  }
+  B.work_n = std::max(B.cap, B.pmax);
+  B.work_stride = ((size_t)B.work_n * (4 * 16 + 8 + 4 + 8 + 16 + 4) + 64 + 255) / 256 * 256;
+  B.gw_grid = grid_w; B.gh_grid = grid_h; B.gx0 = grid_x0; B.gy0 = grid_y0;
+  B.view_slots = 8192;
+  {
+    const int step = std::max(1, (int)lround(max_w / 160.0));
+    B.scan_pmax = ((max_w + step - 1) / step) * ((max_h + step - 1) / step);
+  }
+  B.cos_temper = cos(p->temper_deg * M_PI / 180.0);
+  B.cos_gone_step = cos(p->gone_step_deg * M_PI / 180.0);
+  B.inv_vox = (float)(1.0 / std::max(1e-3, p->voxel));
+  B.inv_vox_cloud = (float)(1.0 / p->voxel);
+  B.q_hit = (int16_t)lround(p->l_hit * 256);
+  B.q_miss = (int16_t)lround(p->l_miss * 256);
+  B.q_min = (int16_t)lround(p->l_min * 256);
+  B.q_max = (int16_t)lround(p->l_max * 256);
+  B.lut_off = -B.q_min;
+  const size_t MO = (size_t)M * O;
+  DA(B.maps, M);
+  DA(B.frames, M);
+  DA(B.objs, MO);
+  DA(B.order, MO);
+  DA(B.freel, MO);
+  DA(B.cfreel, MO);
+  DA(B.assoc, (size_t)M * max_det);
+  DA(B.rfrag, MO * D);
+  DA(B.views, MO * (B.topk + 1) * D);
+  DA(B.clouds, MO);
+  DA(B.cpts, MO * B.cap);
+  DA(B.crgb, MO * B.cap);
+  DA(B.chkey, MO * B.HC);
+  DA(B.chidx, MO * B.HC);
+  DA(B.chgen, MO * B.HC);
+  DA(B.ckey, MO * B.HCC);
+  DA(B.cgen, MO * B.HCC);
+  const size_t MD = (size_t)M * max_det;
+  DA(B.px, MD * 4 * B.pmax);
+  DA(B.ppix, MD * 2 * B.pmax);
+  DA(B.pk, MD * 3 * B.pmax);
+  DA(B.cxyz, MD * 3 * B.pmax);
+  DA(B.cpx, MD * 2 * B.pmax);
+  DA(B.sel, MD * 4 * B.pmax);
+  DA(B.obs, MD);
+  DA(B.obs_list, MD);
+  DA(B.touched, MO + max_det);
+  DA(B.obj_hit, MO + max_det);
+  DA(B.ptsl, MD);
+  DA(B.tgt_slot, MO);
+  DA(B.events, (size_t)M * SMG_MAX_EVENTS);
+  DA(B.mcand_p, MO * 8);
+  DA(B.mcand_ab, MO * 8 * 2);
+  DA(B.mcand_n, M);
+  DA(B.vkey, (size_t)M * B.view_slots);
+  DA(B.vfirst, (size_t)M * B.view_slots * SMG_VIEW_BANDS);
+  DA(B.need_tab, 257 * 257);
+  const size_t G = (size_t)M * grid_w * grid_h;
+  DA(B.gL, G);
+  DA(B.gc8, G);
+  DA(B.gflags, G);
+  DA(B.gcold, G);
+  DA(B.gcnt, G);
+  DA(B.gtouch, G);
+  CK(cudaMemset(B.gtouch, 0xff, sizeof(unsigned long long) * G));
+  const int nlut = B.q_max - B.q_min + 1;
+  DA(B.lut8, nlut);
+  DA(B.lutp, nlut);
+  DA(B.sP, (size_t)M * B.scan_pmax);
+  DA(B.bin_cos, p->bins);
+  DA(B.bin_sin, p->bins);
+  DA(B.hit_key, (size_t)M * p->bins);
+  DA(B.floor_r, (size_t)M * p->bins);
+  DA(B.sig, (size_t)M * p->bins);
+  DA(B.ins_sig, (size_t)M * p->bins);
+  DA(B.mkey, (size_t)M * B.scan_pmax);
+  DA(B.mval, (size_t)M * B.scan_pmax);
+  DA(B.mh_key, (size_t)M * MH_SLOTS);
+  DA(B.mh_first, (size_t)M * MH_SLOTS);
+  DA(B.mh_cell, (size_t)M * MH_SLOTS);
+  DA(B.mcell_first, (size_t)M * B.scan_pmax);
+  DA(B.mcell_cnt, (size_t)M * B.scan_pmax);
+  DA(B.mcell_off, (size_t)M * B.scan_pmax);
+  DA(B.mcell_pix, (size_t)M * B.scan_pmax);
+  DA(B.sc_pts, (size_t)M * (2 * SMG_BINS_MAX + SMG_MATCH_CELLS) * 4);
+  DA(B.work, (size_t)M * WORK_SLOTS * B.work_stride);
+  DA(b->d_depth, (size_t)M * max_w * max_h);
+  DA(b->d_label, (size_t)M * max_w * max_h);
+  DA(b->d_emb, (size_t)M * max_det * D * 4);
+  // host-side initial state
+  {
+    std::vector<MapRec> maps((size_t)M);
+    for (auto& r : maps) {
+      memset(&r, 0, sizeof(r));
+      r.next_id = 1;
+      r.n_free = O;
+      r.n_cfree = O;
+      r.kf_first = 1;
+      r.kf_last_changed = 1 << 30;
+    }
+    CK(cudaMemcpy(B.maps, maps.data(), sizeof(MapRec) * M, cudaMemcpyHostToDevice));
+    std::vector<int32_t> fl(MO);
+    for (int m = 0; m < M; ++m)
+      for (int i = 0; i < O; ++i) fl[(size_t)m * O + i] = O - 1 - i;   // pop order 0, 1, 2, ...
+    CK(cudaMemcpy(B.freel, fl.data(), sizeof(int32_t) * MO, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(B.cfreel, fl.data(), sizeof(int32_t) * MO, cudaMemcpyHostToDevice));
+    std::vector<CloudRec> cl(MO);
+    for (auto& c : cl) { memset(&c, 0, sizeof(c)); c.vgen = 1; c.cgen = 1; c.cver = 0xffffffffu; }
+    CK(cudaMemcpy(B.clouds, cl.data(), sizeof(CloudRec) * MO, cudaMemcpyHostToDevice));
+    // RANSAC adaptive-iteration table: need = max(8, ceil(log(0.01)/log(1-w^3))) for w = cnt/nsamp
+    std::vector<int32_t> need(257 * 257, 0);
+    for (int ns = 1; ns <= 256; ++ns)
+      for (int c = 0; c <= ns; ++c) {
+        const double w = double(c) / double(ns), pw = w * w * w;
+        need[ns * 257 + c] = pw > 1e-9 && pw <= 0.999999 ? std::max(8, int(std::ceil(std::log(0.01) / std::log(1.0 - pw)))) : 0;
+      }
+    CK(cudaMemcpy(B.need_tab, need.data(), sizeof(int32_t) * need.size(), cudaMemcpyHostToDevice));
+    // export8 / probability LUTs (grid.cpp:118-123)
+    std::vector<int8_t> l8(nlut);
+    std::vector<float> lp(nlut);
+    for (int k = 0; k < nlut; ++k) {
+      const float L = float(k - B.lut_off) / 256;
+      const float pr = 1.f / (1.f + std::exp(-L));
+      lp[k] = pr;
+      l8[k] = (int8_t)std::lround(100.f * pr);
+    }
+    CK(cudaMemcpy(B.lut8, l8.data(), nlut, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(B.lutp, lp.data(), sizeof(float) * nlut, cudaMemcpyHostToDevice));
+    // free-ray bin directions (scan.cpp:435-437)
+    std::vector<float> bc(p->bins), bsn(p->bins);
+    const float bin_scale = p->bins / (2.f * float(M_PI));
+    for (int k = 0; k < p->bins; ++k) {
+      const float a = (k + 0.5f) / bin_scale - float(M_PI);
+      bc[k] = std::cos(a);
+      bsn[k] = std::sin(a);
+    }
+    CK(cudaMemcpy(B.bin_cos, bc.data(), sizeof(float) * p->bins, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(B.bin_sin, bsn.data(), sizeof(float) * p->bins, cudaMemcpyHostToDevice));
+  }
+  k_fill_d<<<256, 256>>>(B.vfirst, (size_t)M * B.view_slots * SMG_VIEW_BANDS, -1e300);
+  k_fill_i64<<<256, 256>>>(B.vkey, (size_t)M * B.view_slots, INT64_MIN);
+  k_fill_i8<<<256, 256>>>(B.gc8, G, (int8_t)-1);
+  b->launches += 3;
+  CK(cudaGetLastError());
+  CK(cudaMallocHost(&b->h_frames, sizeof(FrameDev) * M));
+  b->last_cam_t.assign(M, -1e300);
+  b->last_cam_fwd.assign(3 * (size_t)M, 0.0);
+  // kernels with large dynamic shared memory
+  CK(cudaFuncSetAttribute(k_obs, cudaFuncAttributeMaxDynamicSharedMemorySize, OBS_HASH * 12));
+  {
+    const int sm_assoc = ((D * 4 + SP_MAX * 12 + 7) & ~7) + O * 8;
+    CK(cudaFuncSetAttribute(k_assoc, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_assoc));
+    CK(cudaFuncSetAttribute(k_merge_pairs, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * (D + 3 * MP_SPW) * 4));
+    CK(cudaFuncSetAttribute(k_relink, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * D * 4));
+  }
+  CK(cudaDeviceSynchronize());
+  *out = b;
+  return SMG_OK;
+}
+
+__global__ void k_begin(Batch B) {
+  const int m = blockIdx.x;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  for (int k = threadIdx.x; k < B.max_det; k += blockDim.x) {
+    AssocRec& a = B.assoc[(size_t)m * B.max_det + k];
+    a.obj_id = 0; a.n_valid = 0; a.area_px = 0; a.depth_med = 0;
+  }
+  if (threadIdx.x == 0) {
+    MapRec* R = &B.maps[m];
+    R->n_events = 0;
+    R->n_evn = 0;
+    R->n_obs = 0;
+    R->n_pts = 0;
+    R->n_targets = 0;
+    R->kf_inserted = 0;
+    R->kf_changed = 0;
+    B.mcand_n[m] = 0;
+  }
+}
+
+int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, void* stream) {
+  if (!b || !frames || n <= 0 || n > b->B.M || (where != SMG_MEM_DEVICE && where != SMG_MEM_HOST))
+    return fail(SMG_ERR_ARGS, "smg_push_frames: bad arguments");
+  Batch& B = b->B;
+  cudaStream_t st = (cudaStream_t)stream;
+  b->last_stream = st;
+  CK(cudaSetDevice(b->dev));
+  const smg_params& P = B.p;
+  for (int i = 0; i < n; ++i) {
+    const smg_frame& f = frames[i];
+    if (f.w <= 0 || f.h <= 0 || f.w > b->max_w || f.h > b->max_h || !f.depth || f.n_det < 0 || f.n_det > B.max_det ||
+        (f.n_det > 0 && (!f.label || !f.det_label || !f.box || !f.cls)) || (f.emb && f.emb_dtype != SMG_EMB_F32 && f.emb_dtype != SMG_EMB_BF16))
+      return fail(SMG_ERR_ARGS, "smg_push_frames: bad frame");
+  }
+  const size_t WH = (size_t)b->max_w * b->max_h;
+  const size_t esz = 4;
+  for (int m = 0; m < B.M; ++m) {
+    FrameDev& d = b->h_frames[m];
+    memset(&d, 0, sizeof(d));
+    if (m >= n) continue;
+    const smg_frame& f = frames[m];
+    d.active = 1;
+    d.stamp = f.stamp;
+    d.w = f.w;
+    d.h = f.h;
+    d.fx = f.fx; d.fy = f.fy; d.cx = f.cx; d.cy = f.cy;
+    memcpy(d.T_mc, f.T_mc, sizeof d.T_mc);
+    memcpy(d.T_bc, f.T_bc, sizeof d.T_bc);
+    memcpy(d.base, f.base, sizeof d.base);
+    memcpy(d.eef, f.eef, sizeof d.eef);
+    memcpy(d.eef_base, f.eef_base, sizeof d.eef_base);
+    d.n_det = f.n_det;
+    for (int k = 0; k < f.n_det; ++k) {
+      d.det_label[k] = f.det_label[k];
+      for (int c = 0; c < 4; ++c) d.box[k][c] = f.box[4 * k + c];
+      d.cls[k] = f.cls[k];
+      d.score[k] = f.score ? f.score[k] : 1.f;
+    }
+    d.emb_dtype = f.emb_dtype;
+    if (where == SMG_MEM_DEVICE) {
+      d.depth = f.depth;
+      d.label = f.label;
+      d.emb = f.emb;
+    } else {
+      d.depth = b->d_depth + (size_t)m * WH;
+      d.label = b->d_label + (size_t)m * WH;
+      d.emb = f.emb ? (const void*)(b->d_emb + (size_t)m * B.max_det * B.D * esz) : nullptr;
+    }
+    // host-libm scalars (objmap.cpp:520-531, bestview.cpp:77-81, grid.cpp:202)
+    const double* T = f.T_mc;
+    const double fwd[3] = {T[2], T[6], T[10]};
+    const double dt = f.stamp - b->last_cam_t[m];
+    double cam_w = 0;
+    if (b->last_cam_t[m] > -1e299 && dt > 1e-6) {
+      const double c = std::clamp(fwd[0] * b->last_cam_fwd[3 * m] + fwd[1] * b->last_cam_fwd[3 * m + 1] + fwd[2] * b->last_cam_fwd[3 * m + 2], -1.0, 1.0);
+      cam_w = std::acos(c) / dt;
+    }
+    for (int k = 0; k < 3; ++k) b->last_cam_fwd[3 * m + k] = fwd[k];
+    b->last_cam_t[m] = f.stamp;
+    d.cam_w = cam_w;
+    d.cam_steady = cam_w <= P.move_max_cam_w;
+    d.blur_fac = P.kap_blur_w > 0 ? std::exp(-std::max(0.0, (double)std::max(0.f, (float)cam_w)) / P.kap_blur_w) : 1.0;
+    d.cos_th = std::cos(f.base[2]);
+    d.sin_th = std::sin(f.base[2]);
+  }
+  if (where == SMG_MEM_HOST) {
+    // contiguous host inputs (map i at base + i*stride) go in one copy each
+    auto contiguous = [&](auto get, size_t stride) {
+      for (int i = 1; i < n; ++i)
+        if ((const char*)get(i) != (const char*)get(0) + i * stride) return false;
+      return true;
+    };
+    const smg_frame& f0 = frames[0];
+    const bool same_size = [&] {
+      for (int i = 1; i < n; ++i) if (frames[i].w != f0.w || frames[i].h != f0.h) return false;
+      return true;
+    }();
+    const size_t px = (size_t)f0.w * f0.h;
+    if (same_size && px == WH && contiguous([&](int i) { return (const void*)frames[i].depth; }, px * 4) &&
+        contiguous([&](int i) { return (const void*)frames[i].label; }, px * 2)) {
+      CK(cudaMemcpyAsync(b->d_depth, f0.depth, px * 4 * n, cudaMemcpyHostToDevice, st));
+      if (f0.label) CK(cudaMemcpyAsync(b->d_label, f0.label, px * 2 * n, cudaMemcpyHostToDevice, st));
+    } else {
+      for (int i = 0; i < n; ++i) {
+        const size_t pi = (size_t)frames[i].w * frames[i].h;
+        CK(cudaMemcpyAsync(b->d_depth + i * WH, frames[i].depth, pi * 4, cudaMemcpyHostToDevice, st));
+        if (frames[i].label) CK(cudaMemcpyAsync(b->d_label + i * WH, frames[i].label, pi * 2, cudaMemcpyHostToDevice, st));
+      }
+    }
+    for (int i = 0; i < n; ++i) {
+      if (!frames[i].emb || frames[i].n_det <= 0) continue;
+      const size_t eb = (size_t)frames[i].n_det * B.D * (frames[i].emb_dtype == SMG_EMB_BF16 ? 2 : 4);
+      CK(cudaMemcpyAsync(b->d_emb + (size_t)i * B.max_det * B.D * esz, frames[i].emb, eb, cudaMemcpyHostToDevice, st));
+    }
+  }
+  CK(cudaMemcpyAsync(B.frames, b->h_frames, sizeof(FrameDev) * B.M, cudaMemcpyHostToDevice, st));
+  const int M = B.M;
+  k_begin<<<M, 128, 0, st>>>(B);
+  k_merge_pairs<<<dim3(MP_CTAS, M), 256, 8 * (B.D + 3 * MP_SPW) * 4, st>>>(B);
+  k_merge_apply<<<M, 512, 0, st>>>(B);
+  k_obs<<<dim3(B.max_det, M), OBS_THREADS, OBS_HASH * 12, st>>>(B);
+  k_obs_finalize<<<M, 32, 0, st>>>(B);
+  k_assoc<<<dim3(B.max_det, M), ASSOC_THREADS, ((B.D * 4 + SP_MAX * 12 + 7) & ~7) + B.O * 8, st>>>(B);
+  k_update<<<M, UPD_THREADS, B.D * 4, st>>>(B);
+  k_absent<<<dim3(4, M), 256, 0, st>>>(B);
+  k_relink<<<M, 256, 8 * B.D * 4, st>>>(B);
+  k_struct<<<dim3(WORK_SLOTS, M), 256, 0, st>>>(B);
+  k_prune<<<M, 32, 0, st>>>(B);
+  k_markview<<<M, 256, 0, st>>>(B);
+  k_cloud_add<<<dim3(WORK_SLOTS, M), 512, 0, st>>>(B);
+  k_grid<<<M, GRID_THREADS, 0, st>>>(B);
+  b->launches += 14;
+  CK(cudaGetLastError());
+  return SMG_OK;
+}
+
+static int sync_b(smg_batch* b) {
+  CK(cudaSetDevice(b->dev));
+  CK(cudaStreamSynchronize(b->last_stream));
+  return SMG_OK;
+}
+
+static int read_map(smg_batch* b, int m, MapRec* R) {
+  CK(cudaMemcpy(R, b->B.maps + m, sizeof(MapRec), cudaMemcpyDeviceToHost));
+  return SMG_OK;
+}
+
+int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap) {
+  if (!b || m < 0 || m >= b->B.M) return fail(SMG_ERR_ARGS, "smg_get_objects: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  std::vector<int32_t> ord(R.n_obj);
+  if (R.n_obj) CK(cudaMemcpy(ord.data(), B.order + (size_t)m * B.O, sizeof(int32_t) * R.n_obj, cudaMemcpyDeviceToHost));
+  for (int i = 0; i < R.n_obj && i < cap && out; ++i) {
+    ObjRec o;
+    CK(cudaMemcpy(&o, B.objs + (size_t)m * B.O + ord[i], sizeof(ObjRec), cudaMemcpyDeviceToHost));
+    CloudRec c;
+    CK(cudaMemcpy(&c, B.clouds + (size_t)m * B.O + o.cloud_slot, sizeof(CloudRec), cudaMemcpyDeviceToHost));
+    smg_object& r = out[i];
+    memset(&r, 0, sizeof(r));
+    r.id = o.id;
+    r.cls = o.cls;
+    for (int k = 0; k < 3; ++k) {
+      r.pos[k] = o.pos[k]; r.ext[k] = o.ext[k]; r.first_pos[k] = o.first_pos[k]; r.lo[k] = o.lo[k]; r.hi[k] = o.hi[k];
+      r.P[k] = o.P[k]; r.cloud_org[k] = c.org[k];
+    }
+    r.n_obs = o.n_obs;
+    r.first_seen = o.first_seen;
+    r.last_seen = o.last_seen;
+    r.state = o.state;
+    r.confirmed = o.confirmed;
+    r.moved = o.moved;
+    r.misses = o.misses;
+    r.n_vis_miss = o.n_vis_miss;
+    r.score = o.score;
+    r.max_det_z = o.max_det_z;
+    r.last_kf = o.last_kf;
+    r.appeared = o.appeared;
+    r.cloud_n = c.n;
+    r.cloud_version = c.version;
+    r.ap_ver = o.ver;
+    r.k_frag = o.k_frag;
+    r.n_views = o.n_views;
+    r.n_ap_obs = o.n_ap_obs;
+    r.need_whole = o.need_whole;
+    r.n_cams = o.n_cams;
+    r.geo = o.geo;
+  }
+  return R.n_obj;
+}
+
+int smg_get_object_vectors(smg_batch* b, int m, int i, float* r_frag, uint16_t* views, float* vkappa, double* vstamp, int vcap) {
+  if (!b || m < 0 || m >= b->B.M) return fail(SMG_ERR_ARGS, "smg_get_object_vectors: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  if (i < 0 || i >= R.n_obj) return fail(SMG_ERR_ARGS, "smg_get_object_vectors: bad index");
+  int32_t slot;
+  CK(cudaMemcpy(&slot, B.order + (size_t)m * B.O + i, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  const size_t og = (size_t)m * B.O + slot;
+  ObjRec o;
+  CK(cudaMemcpy(&o, B.objs + og, sizeof(ObjRec), cudaMemcpyDeviceToHost));
+  if (r_frag) CK(cudaMemcpy(r_frag, B.rfrag + og * B.D, sizeof(float) * B.D, cudaMemcpyDeviceToHost));
+  const int nv = std::min(vcap, o.n_views);
+  for (int v = 0; v < nv; ++v) {
+    if (views) CK(cudaMemcpy(views + (size_t)v * B.D, B.views + (og * (B.topk + 1) + o.view_slot[v]) * B.D, 2 * B.D, cudaMemcpyDeviceToHost));
+    if (vkappa) vkappa[v] = o.vkappa[v];
+    if (vstamp) vstamp[v] = o.vstamp[v];
+  }
+  return nv;
+}
+
+int smg_get_object_cloud(smg_batch* b, int m, int i, float* xyz, uint32_t* seq, int cap) {
+  if (!b || m < 0 || m >= b->B.M) return fail(SMG_ERR_ARGS, "smg_get_object_cloud: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  if (i < 0 || i >= R.n_obj) return fail(SMG_ERR_ARGS, "smg_get_object_cloud: bad index");
+  int32_t slot;
+  CK(cudaMemcpy(&slot, B.order + (size_t)m * B.O + i, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  ObjRec o;
+  CK(cudaMemcpy(&o, B.objs + (size_t)m * B.O + slot, sizeof(ObjRec), cudaMemcpyDeviceToHost));
+  const size_t cs = (size_t)m * B.O + o.cloud_slot;
+  CloudRec c;
+  CK(cudaMemcpy(&c, B.clouds + cs, sizeof(CloudRec), cudaMemcpyDeviceToHost));
+  const int n = std::min(cap, c.n);
+  if (n > 0 && (xyz || seq)) {
+    std::vector<float4> pts(n);
+    CK(cudaMemcpy(pts.data(), B.cpts + cs * B.cap, sizeof(float4) * n, cudaMemcpyDeviceToHost));
+    for (int k = 0; k < n; ++k) {
+      if (xyz) { xyz[3 * k] = pts[k].x; xyz[3 * k + 1] = pts[k].y; xyz[3 * k + 2] = pts[k].z; }
+      if (seq) { uint32_t s; memcpy(&s, &pts[k].w, 4); seq[k] = s; }
+    }
+  }
+  return c.n;
+}
+
+int smg_get_assoc(smg_batch* b, int m, uint32_t* obj_id, int32_t* n_valid, float* area_px, float* depth_med, int cap) {
+  if (!b || m < 0 || m >= b->B.M) return fail(SMG_ERR_ARGS, "smg_get_assoc: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  FrameDev f;
+  CK(cudaMemcpy(&f, B.frames + m, sizeof(FrameDev), cudaMemcpyDeviceToHost));
+  std::vector<AssocRec> a(B.max_det);
+  CK(cudaMemcpy(a.data(), B.assoc + (size_t)m * B.max_det, sizeof(AssocRec) * B.max_det, cudaMemcpyDeviceToHost));
+  for (int k = 0; k < f.n_det && k < cap; ++k) {
+    if (obj_id) obj_id[k] = a[k].obj_id;
+    if (n_valid) n_valid[k] = a[k].n_valid;
+    if (area_px) area_px[k] = a[k].area_px;
+    if (depth_med) depth_med[k] = a[k].depth_med;
+  }
+  return f.n_det;
+}
+
+int smg_get_stats(smg_batch* b, int m, int64_t* out16) {
+  if (!b || m < 0 || m >= b->B.M || !out16) return fail(SMG_ERR_ARGS, "smg_get_stats: bad arguments");
+  if (int r = sync_b(b)) return r;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  const long long* s = &R.st.n_through;
+  for (int k = 0; k < 16; ++k) out16[k] = s[k];
+  return SMG_OK;
+}
+
+int smg_get_events(smg_batch* b, int m, double* t, uint32_t* id, int32_t* kind, int cap) {
+  if (!b || m < 0 || m >= b->B.M) return fail(SMG_ERR_ARGS, "smg_get_events: bad arguments");
+  if (int r = sync_b(b)) return r;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  const int n = std::min(R.n_events, SMG_MAX_EVENTS);
+  std::vector<EventRec> ev(n);
+  if (n) CK(cudaMemcpy(ev.data(), b->B.events + (size_t)m * SMG_MAX_EVENTS, sizeof(EventRec) * n, cudaMemcpyDeviceToHost));
+  std::stable_sort(ev.begin(), ev.end(), [](const EventRec& a, const EventRec& c) { return a.key < c.key; });
+  for (int k = 0; k < n && k < cap; ++k) {
+    if (t) t[k] = ev[k].t;
+    if (id) id[k] = ev[k].id;
+    if (kind) kind[k] = ev[k].kind;
+  }
+  return n;
+}
+
+int smg_get_grid(smg_batch* b, int m, int16_t* L, uint8_t* seen, int8_t* c8) {
+  if (!b || m < 0 || m >= b->B.M) return fail(SMG_ERR_ARGS, "smg_get_grid: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  const size_t G = (size_t)B.gw_grid * B.gh_grid, o = (size_t)m * G;
+  if (L) CK(cudaMemcpy(L, B.gL + o, 2 * G, cudaMemcpyDeviceToHost));
+  if (c8) CK(cudaMemcpy(c8, B.gc8 + o, G, cudaMemcpyDeviceToHost));
+  if (seen) {
+    CK(cudaMemcpy(seen, B.gflags + o, G, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < G; ++i) seen[i] &= 1;
+  }
+  return (int)G;
+}
+
+int smg_get_keyframe(smg_batch* b, int m, int32_t* out3) {
+  if (!b || m < 0 || m >= b->B.M || !out3) return fail(SMG_ERR_ARGS, "smg_get_keyframe: bad arguments");
+  if (int r = sync_b(b)) return r;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  out3[0] = R.kf_inserted;
+  out3[1] = R.kf_changed;
+  out3[2] = R.kf_hits;
+  return SMG_OK;
+}
+
+int smg_error_word(smg_batch* b) {
+  if (!b) return SMG_ERR_ARGS;
+  if (int r = sync_b(b)) return r;
+  int e = 0;
+  for (int m = 0; m < b->B.M; ++m) {
+    MapRec R;
+    if (int r = read_map(b, m, &R)) return r;
+    e |= R.err;
+  }
+  return e;
+}
+
+int64_t smg_kernel_launches(smg_batch* b) { return b ? b->launches : -1; }
+
+}  // extern "C"

@@ -1,0 +1,273 @@
+// Internal device-state layout of an smg_batch (host + device visible PODs).
+//
+// HBM layout (one batch = M maps, O object slots per map, D embedding width):
+//   MapRec[M]                 per-map scalars (ids, camera history, ceiling estimate, ApStats,
+//                             insert-policy state, error word)
+//   ObjRec[M*O]               per-object scalars of MapObject + ApState (scenemap objmap.hpp:157-187,
+//                             objprob.hpp:156-193); objects are kept in the reference's list order
+//                             through order[M*O] (slot indices), slots are recycled through a free list
+//   rfrag[M*O*D]  f32         ApState::r_frag
+//   views[M*O*(topk+1)*D] u16 ApState::views[].z (fp16 bits), one spare slot for insertion
+//   cloud pool, one per object slot (ObjCloud, cloud.hpp:165-189):
+//     cpts[cap] float4 (x,y,z relative to org, seq bits), crgb[cap] u32,
+//     chkey/chidx[HC]   voxel-key -> point index hash (VoxelIndex, cloud.cpp:48-64),
+//     ckey/cgen[HC]     4 cm contact-cell set (ApContactIdx, objprob.cpp:470-487), generation-cleared
+//   per-frame scratch per (map, detection): back-projected points, observation records, cloud candidates
+//   occupancy grid per map: hot (L, c8, flags, stamp) + cold sums, fixed window (OccGrid, grid.hpp:63-98)
+//   view-first hash per map (ObjectMap::view_first_, objmap.hpp:333)
+#pragma once
+#include <stdint.h>
+
+#include "../../include/smg.h"
+
+#define SMG_MAX_DET 64
+#define SMG_TOPK_MAX 8
+#define SMG_CAMS 32
+#define SMG_CEIL_OBS 400
+#define SMG_VIEW_BANDS 5
+#define SMG_SUB 2048          // kPctMax (scenemap objmap.cpp:36)
+#define SMG_MAX_EVENTS 1024   // per map per frame
+#define SMG_BINS_MAX 1440
+#define SMG_MATCH_CELLS 12288 // kH * 3 / 4 (scenemap scan.cpp:319, :399)
+#define WORK_SLOTS 8          // per-map work areas (cloud add / struct CTAs per map)
+
+// error word bits
+#define SMG_E_CAP_OBJ 1
+#define SMG_E_CAP_PTS 2
+#define SMG_E_CAP_GRID 4
+#define SMG_E_CAP_VIEW 8
+#define SMG_E_CAP_EVENTS 16
+#define SMG_E_ARGS 32
+
+// Per (map, frame) input descriptor on the device (smg_frame + host-derived scalars).
+typedef struct {
+  double stamp;
+  int32_t w, h;
+  const float* depth;
+  const uint16_t* label;
+  float fx, fy, cx, cy;
+  double T_mc[12];
+  float T_bc[12];
+  double base[3];
+  double eef[2][3];
+  float eef_base[2][3];
+  int32_t n_det;
+  uint16_t det_label[SMG_MAX_DET];
+  float box[SMG_MAX_DET][4];
+  int32_t cls[SMG_MAX_DET];
+  float score[SMG_MAX_DET];
+  const void* emb;
+  int32_t emb_dtype;
+  // host-derived with the host libm (same values the reference computes)
+  double cam_w;          // camera optical-axis angular speed (objmap.cpp:520-530)
+  int32_t cam_steady;    // cam_w <= move_max_cam_w
+  double blur_fac;       // exp(-cam_w/blur_w) factor of viewKappa (1 when blur_w == 0)
+  double cos_th, sin_th; // cos/sin of base yaw (grid.cpp:202)
+  int32_t active;        // map takes part in this push
+} FrameDev;
+
+// Observation (one detection after back-projection; scenemap objmap.cpp:52-74 `Obs`)
+typedef struct {
+  int32_t valid;         // 1 = survived to the structural test
+  int32_t stage;         // where it stopped (diagnostics)
+  int32_t det, sk, cls, trunc, n, nc, nsp;
+  float score;
+  double zmed, pos[3], ext[3], lo[3], hi[3], kappa;
+  int32_t floor_drop;    // dropped by the 90th-percentile floor test (counts n_floor)
+  // plane fit of the cloud candidates (apObsStructural, objmap.cpp:565-575)
+  int32_t pl_ok;
+  double pl_n[3], pl_thick, pl_inl, pl_zmed, pl_zlo, pl_zhi, pl_hspan;
+  // association results
+  int32_t obs_to, n_same, blocked, sec;
+} ObsRec;
+
+typedef struct {
+  uint32_t id;
+  int32_t cls;
+  double pos[3], ext[3], first_pos[3], lo[3], hi[3];
+  uint32_t n_obs;
+  double first_seen, last_seen;
+  int32_t state, confirmed, moved, misses;
+  double first_miss, miss_cam[3], last_miss_cam[3], last_miss_fwd[3];
+  uint32_t n_vis_miss;
+  double trk_pos[3], trk_t, trk_step[2];
+  int32_t mv_cnt;
+  double moving_t, move_from_t;
+  float score;
+  double last_kf, max_det_z, gone_t;
+  int32_t appeared;
+  int32_t cloud_slot;    // cloud pool slot owned by this object
+  // ApState
+  uint32_t ver;
+  double k_frag;
+  int32_t n_whole, n_views;
+  int32_t view_slot[SMG_TOPK_MAX + 1];
+  float vkappa[SMG_TOPK_MAX + 1];
+  double vstamp[SMG_TOPK_MAX + 1];
+  int32_t n_cams;
+  double cams[SMG_CAMS][7];
+  int32_t n_wall_obs, n_ap_obs, n_struct_look;
+  double whole_kappa;
+  int32_t need_whole;
+  double P[3];
+  int32_t wall_like;
+  uint32_t geo_ver;
+  int32_t geo, drop, hide;
+  double nrm_frag;       // |r_frag|^2 (ApState::nrm_frag, refreshed whenever r_frag changes)
+} ObjRec;
+
+typedef struct {
+  double org[3];
+  int32_t has_org;
+  uint32_t version;
+  int32_t n;
+  uint32_t seq;
+  double stamp;
+  uint32_t vgen;         // generation of the voxel-key hash (clear = ++vgen)
+  uint32_t cver;         // cloud version the contact index was built for
+  // contact index (ApContactIdx): generation, count and cell range
+  uint32_t cgen;
+  int32_t cn;
+  int64_t clo[3], chi[3];
+} CloudRec;
+
+typedef struct {
+  long long n_through, n_obs, n_wall, n_wall_name, n_ceil, n_floor, n_assoc, n_new, n_merge, n_obj_struct, n_reenc_req,
+      n_reenc_done, n_blocked, n_wall_tall, n_so_big, n_bridge;
+} StatsRec;
+
+typedef struct {
+  double t;
+  uint32_t id;
+  int32_t kind;
+  uint32_t key;          // program-order key (phase << 24 | position)
+  int32_t pad;
+} EventRec;
+
+typedef struct {
+  uint32_t next_id;
+  int32_t n_obj;
+  int32_t n_free, n_cfree;
+  int32_t n_evn;         // running event counter of the current phase
+  int32_t err;
+  double ceil_est;
+  int32_t n_ceil;
+  int32_t n_obs;         // observations surviving to association this frame
+  int32_t n_events;
+  int32_t n_pts;         // cloud-candidate lists emitted this frame
+  int32_t n_targets;     // objects receiving cloud points / contact rebuilds this frame
+  StatsRec st;
+  double ceil_obs[SMG_CEIL_OBS];
+  // Mapper2D insert policy (mapper2d.cpp:118-146)
+  int32_t kf_first, kf_since, kf_last_changed, kf_inserted, kf_changed, kf_hits, kf_sig_n;
+  double kf_last_ins[3];
+  uint32_t scan_id;
+  int32_t view_n;
+} MapRec;
+
+// ObjectMap::lastAssoc entry (DetAssoc, objmap.hpp:194-199)
+typedef struct {
+  uint32_t obj_id;
+  int32_t n_valid;
+  float area_px, depth_med;
+} AssocRec;
+
+// Per map per frame: emitted cloud-candidate list (ObsPoints, objmap.hpp:225-230)
+typedef struct {
+  uint32_t obj_id;
+  int32_t det;
+  int32_t n;
+} PtsRec;
+
+typedef struct {
+  // sizes
+  int32_t M, O, D, topk, cap, HC, HCC, pmax, max_det, W, H;
+  int32_t work_n;                       // points per work area
+  size_t work_stride;                   // bytes per work area
+  int32_t gw_grid, gh_grid, gx0, gy0;   // occupancy window
+  int32_t view_slots;                   // view-first hash slots per map
+  int32_t scan_pmax;                    // makeScan grid capacity
+  // parameters
+  smg_params p;
+  double cos_temper;                    // cos(temper_deg * pi / 180)  (objprob.cpp:317)
+  double cos_gone_step;                 // cos(gone_step_deg * pi / 180) (objmap.cpp:1036)
+  float inv_vox;                        // float(1.0 / max(1e-3, voxel)) (objmap.cpp:631)
+  float inv_vox_cloud;                  // float(1.0 / voxel) (cloud.cpp:95)
+  int16_t q_hit, q_miss, q_min, q_max;  // grid.cpp:110-113
+  int32_t lut_off;
+  // device arrays
+  MapRec* maps;
+  FrameDev* frames;
+  ObjRec* objs;
+  int32_t* order;        // [M*O]
+  int32_t* freel;        // [M*O] free object-slot stack
+  int32_t* cfreel;       // [M*O] free cloud-slot stack
+  AssocRec* assoc;       // [M*max_det]
+  float* rfrag;          // [M*O*D]
+  uint16_t* views;       // [M*O*(topk+1)*D]
+  CloudRec* clouds;      // [M*O]
+  float4* cpts;          // [M*O*cap]
+  uint32_t* crgb;        // [M*O*cap]
+  uint64_t* chkey;       // [M*O*HC]
+  uint32_t* chidx;       // [M*O*HC]
+  uint32_t* chgen;       // [M*O*HC]
+  uint64_t* ckey;        // [M*O*HCC]
+  uint32_t* cgen;        // [M*O*HCC]
+  // per-frame scratch
+  double* px;            // [M*max_det*pmax] x4 (X, Y, Z, ZC)
+  int32_t* ppix;         // [M*max_det*pmax] x2 (PU, PV)
+  double* pk;            // [M*max_det*pmax] x3 (kept X, Y, Z)
+  float* cxyz;           // [M*max_det*pmax*3]
+  int32_t* cpx;          // [M*max_det*pmax*2]
+  double* sel;           // [M*max_det*pmax] x4 selection scratch
+  ObsRec* obs;           // [M*max_det] by detection
+  int32_t* obs_list;     // [M*max_det] detection index of observation a
+  uint8_t* touched;      // [M*O]  by list position
+  uint8_t* obj_hit;      // [M*O]
+  double* pairp;         // [M*max_det*O] association P per (obs, object position)
+  PtsRec* ptsl;          // [M*max_det]
+  int32_t* tgt_slot;     // [M*O] cloud-addition targets (object slots)
+  unsigned char* work;   // [M*WORK_SLOTS*work_stride]
+  EventRec* events;      // [M*SMG_MAX_EVENTS]
+  // merge pass scratch
+  double* mcand_p;       // [M*O*8] candidate P
+  uint32_t* mcand_ab;    // [M*O*8*2]
+  int32_t* mcand_n;      // [M]
+  // view-first hash (markView)
+  int64_t* vkey;         // [M*view_slots], INT64_MIN = empty
+  double* vfirst;        // [M*view_slots*5]
+  // RANSAC adaptive iteration table need[nsamp][cnt] (objprob.cpp:161), host libm
+  int32_t* need_tab;     // [257*257]
+  // occupancy grid
+  int16_t* gL;           // [M*gw*gh]
+  int8_t* gc8;
+  uint8_t* gflags;
+  uint32_t* gstamp;
+  float4* gcold;         // sx, sy, nx, ny
+  uint32_t* gcnt;        // cnt | cntn << 16
+  unsigned long long* gtouch;   // per-scan first-touch key
+  int8_t* lut8;          // export8 LUT (grid.cpp:118-123), host libm
+  float* lutp;
+  // makeScan scratch
+  float4* sP;            // [M*scan_pmax] base-frame point + optical z
+  int16_t* pbin;         // [M*scan_pmax]
+  float* phs2;           // [M*scan_pmax]
+  float* bin_cos;        // [bins] cos/sin of bin centres, host libm (scan.cpp:435-437)
+  float* bin_sin;
+  unsigned long long* hit_key;   // [M*bins] (rr2 bits << 32 | pixel)
+  float* floor_r;        // [M*bins]
+  int16_t* sig;          // [M*bins] this scan's signature
+  int16_t* ins_sig;      // [M*bins] signature of the last inserted scan
+  int64_t* mkey;         // [M*scan_pmax] match key per pixel (INT64_MIN = none)
+  float4* mval;          // [M*scan_pmax] px, py, ux, uy
+  int64_t* mh_key;       // [M*16384] match-cell hash
+  int32_t* mh_first;     // [M*16384]
+  int32_t* mh_cell;      // [M*16384] rank of the cell in first-seen order
+  int32_t* mcell_first;  // [M*scan_pmax] first pixel of cell rank r
+  int32_t* mcell_cnt;    // [M*scan_pmax]
+  int32_t* mcell_off;    // [M*scan_pmax]
+  int32_t* mcell_pix;    // [M*scan_pmax]
+  float* sc_pts;         // [M*(2*bins + SMG_MATCH_CELLS)*6] insert point list: x, y, nx, ny (base frame)
+  int32_t* sc_n;         // [M*3] nm, nh, nf
+  int32_t* err_global;
+} Batch;

@@ -1,0 +1,251 @@
+"""Host-side binding of the B200 scenemap objprob update (ctypes over libsmg.so).
+
+Mirrors the reference's C++ surface for one batch of independent maps: create the maps
+(``ObjectMap(p)`` + ``Mapper2D``), push one keyframe per map (``Mapper2D::keyframe`` +
+``ObjectMap::update`` + ``addPoints``), read objects / association / grid back.  The compute
+runs only in the CUDA library; if it is missing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "libsmg.so")
+
+SMG_MEM_DEVICE, SMG_MEM_HOST = 0, 1
+SMG_EMB_F32, SMG_EMB_BF16 = 0, 1
+STAT_FIELDS = ["n_through", "n_obs", "n_wall", "n_wall_name", "n_ceil", "n_floor", "n_assoc", "n_new", "n_merge",
+               "n_obj_struct", "n_reenc_req", "n_reenc_done", "n_blocked", "n_wall_tall", "n_so_big", "n_bridge"]
+
+
+class SmgFrame(C.Structure):
+    _fields_ = [("stamp", C.c_double), ("w", C.c_int32), ("h", C.c_int32), ("depth", C.c_void_p), ("label", C.c_void_p),
+                ("fx", C.c_float), ("fy", C.c_float), ("cx", C.c_float), ("cy", C.c_float), ("T_mc", C.c_double * 12),
+                ("T_bc", C.c_float * 12), ("base", C.c_double * 3), ("eef", C.c_double * 6), ("eef_base", C.c_float * 6),
+                ("n_det", C.c_int32), ("det_label", C.c_void_p), ("box", C.c_void_p), ("cls", C.c_void_p),
+                ("score", C.c_void_p), ("emb", C.c_void_p), ("emb_dtype", C.c_int32)]
+
+
+class SmgObject(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("cls", C.c_int32), ("pos", C.c_double * 3), ("ext", C.c_double * 3),
+                ("first_pos", C.c_double * 3), ("lo", C.c_double * 3), ("hi", C.c_double * 3), ("n_obs", C.c_uint32),
+                ("first_seen", C.c_double), ("last_seen", C.c_double), ("state", C.c_int32), ("confirmed", C.c_int32),
+                ("moved", C.c_int32), ("misses", C.c_int32), ("n_vis_miss", C.c_uint32), ("score", C.c_float),
+                ("max_det_z", C.c_double), ("last_kf", C.c_double), ("appeared", C.c_int32), ("cloud_n", C.c_int32),
+                ("cloud_version", C.c_uint32), ("cloud_org", C.c_double * 3), ("ap_ver", C.c_uint32),
+                ("k_frag", C.c_double), ("n_views", C.c_int32), ("n_ap_obs", C.c_int32), ("need_whole", C.c_int32),
+                ("P", C.c_double * 3), ("n_cams", C.c_int32), ("geo", C.c_int32)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"CUDA library not built: {LIB_PATH} (run __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        P, vp = C.POINTER, C.c_void_p
+        L.smg_params_size.restype = C.c_int
+        L.smg_params_default.argtypes = [vp]
+        L.smg_params_apply.argtypes = [vp, C.c_char_p]
+        L.smg_create.argtypes = [vp] + [C.c_int] * 11 + [P(vp)]
+        L.smg_destroy.argtypes = [vp]
+        L.smg_push_frames.argtypes = [vp, P(SmgFrame), C.c_int, C.c_int, vp]
+        L.smg_get_objects.argtypes = [vp, C.c_int, P(SmgObject), C.c_int]
+        L.smg_get_object_vectors.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int]
+        L.smg_get_object_cloud.argtypes = [vp, C.c_int, C.c_int, vp, vp, C.c_int]
+        L.smg_get_assoc.argtypes = [vp, C.c_int, vp, vp, vp, vp, C.c_int]
+        L.smg_get_stats.argtypes = [vp, C.c_int, vp]
+        L.smg_get_events.argtypes = [vp, C.c_int, vp, vp, vp, C.c_int]
+        L.smg_get_grid.argtypes = [vp, C.c_int, vp, vp, vp]
+        L.smg_get_keyframe.argtypes = [vp, C.c_int, vp]
+        L.smg_error_word.argtypes = [vp]
+        L.smg_last_error.restype = C.c_char_p
+        L.smg_kernel_launches.restype = C.c_int64
+        L.smg_kernel_launches.argtypes = [vp]
+        _lib = L
+    return _lib
+
+
+EXPORTED = ["smg_params_size", "smg_params_default", "smg_params_apply", "smg_create", "smg_destroy", "smg_push_frames",
+            "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
+            "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
+            "smg_kernel_launches"]
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+class SmgError(RuntimeError):
+    pass
+
+
+def _check(rc, what):
+    if rc < 0:
+        raise SmgError(f"{what} rc={rc}: {lib().smg_last_error().decode()}")
+    return rc
+
+
+class Params:
+    """smg_params as an opaque buffer (defaults of the reference structs + applyParams keys)."""
+
+    def __init__(self, kv: str = ""):
+        L = lib()
+        self.buf = C.create_string_buffer(L.smg_params_size())
+        _check(L.smg_params_default(self.buf), "smg_params_default")
+        if kv:
+            n_bad = L.smg_params_apply(self.buf, kv.encode())
+            if n_bad:
+                raise SmgError(f"unknown parameter keys in {kv!r}")
+
+
+class Batch:
+    def __init__(self, n_maps: int, max_objects: int = 256, emb_dim: int = 1152, max_w: int = 640, max_h: int = 480,
+                 max_det: int = 32, grid=(512, 512, -256 + 60, -256 + 50), params: Params | None = None, dev: int = 0):
+        L = lib()
+        self.params = params or Params()
+        self.n_maps, self.max_objects, self.D, self.max_det = n_maps, max_objects, emb_dim, max_det
+        self.grid = grid
+        h = C.c_void_p()
+        _check(L.smg_create(self.params.buf, n_maps, max_objects, emb_dim, max_w, max_h, max_det, grid[0], grid[1],
+                            grid[2], grid[3], dev, C.byref(h)), "smg_create")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None) and self.h.value:
+            lib().smg_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def frame_struct(fr: dict, keep: list, emb_dtype: int = SMG_EMB_F32, ptrs: dict | None = None) -> SmgFrame:
+        """smg_frame from a synth frame dict (host numpy arrays, or device pointers in `ptrs`)."""
+        f = SmgFrame()
+        f.stamp = fr["stamp"]
+        f.w, f.h = fr["w"], fr["h"]
+        f.fx, f.fy, f.cx, f.cy = fr["fx"], fr["fy"], fr["cx"], fr["cy"]
+        for i in range(12):
+            f.T_mc[i] = fr["T_mc"][i]
+            f.T_bc[i] = fr["T_bc"][i]
+        for i in range(3):
+            f.base[i] = fr["base"][i]
+        eef = np.asarray(fr["eef"], np.float64).reshape(-1)
+        eefb = np.asarray(fr["eef_base"], np.float32).reshape(-1)
+        for i in range(6):
+            f.eef[i] = eef[i]
+            f.eef_base[i] = eefb[i]
+        n = int(fr["n_det"])
+        f.n_det = n
+        dl = np.ascontiguousarray(fr["det_label"], np.uint16)
+        bx = np.ascontiguousarray(fr["box"], np.float32)
+        cl = np.ascontiguousarray(fr["cls"], np.int32)
+        sc = np.ascontiguousarray(fr["score"], np.float32)
+        keep += [dl, bx, cl, sc]
+        f.det_label, f.box, f.cls, f.score = _ptr(dl), _ptr(bx), _ptr(cl), _ptr(sc)
+        f.emb_dtype = emb_dtype
+        if ptrs is not None:
+            f.depth, f.label, f.emb = ptrs["depth"], ptrs["label"], ptrs["emb"]
+        else:
+            depth = np.ascontiguousarray(fr["depth"], np.float32)
+            label = np.ascontiguousarray(fr["label"], np.uint16)
+            if emb_dtype == SMG_EMB_BF16:
+                e32 = np.ascontiguousarray(fr["emb"], np.float32)
+                emb = (e32.view(np.uint32) >> 16).astype(np.uint16)
+            else:
+                emb = np.ascontiguousarray(fr["emb"], np.float32)
+            keep += [depth, label, emb]
+            f.depth, f.label, f.emb = _ptr(depth), _ptr(label), (_ptr(emb) if n else None)
+        return f
+
+    def push(self, frames: list, where: int = SMG_MEM_HOST, emb_dtype: int = SMG_EMB_F32, stream: int = 0,
+             structs=None):
+        keep = []
+        if structs is None:
+            arr = (SmgFrame * len(frames))(*[self.frame_struct(fr, keep, emb_dtype) for fr in frames])
+        else:
+            arr = structs
+        _check(lib().smg_push_frames(self.h, arr, len(arr), where, C.c_void_p(stream)), "smg_push_frames")
+        self._keep = keep
+
+    def objects(self, m: int = 0) -> list:
+        L = lib()
+        n = _check(L.smg_get_objects(self.h, m, None, 0), "smg_get_objects")
+        arr = (SmgObject * max(n, 1))()
+        L.smg_get_objects(self.h, m, arr, n)
+        out = []
+        for i in range(n):
+            o = arr[i]
+            d = {}
+            for name, _ in SmgObject._fields_:
+                v = getattr(o, name)
+                d[name] = list(v) if hasattr(v, "__len__") else v
+            out.append(d)
+        return out
+
+    def object_vectors(self, m: int, i: int):
+        r = np.zeros(self.D, np.float32)
+        views = np.zeros((8, self.D), np.uint16)
+        vk = np.zeros(8, np.float32)
+        vs = np.zeros(8, np.float64)
+        nv = _check(lib().smg_get_object_vectors(self.h, m, i, _ptr(r), _ptr(views), _ptr(vk), _ptr(vs), 8),
+                    "smg_get_object_vectors")
+        return r, views[:nv], vk[:nv], vs[:nv]
+
+    def object_cloud(self, m: int, i: int):
+        n = _check(lib().smg_get_object_cloud(self.h, m, i, None, None, 0), "smg_get_object_cloud")
+        xyz = np.zeros((max(n, 1), 3), np.float32)
+        seq = np.zeros(max(n, 1), np.uint32)
+        lib().smg_get_object_cloud(self.h, m, i, _ptr(xyz), _ptr(seq), n)
+        return xyz[:n], seq[:n]
+
+    def assoc(self, m: int = 0):
+        cap = self.max_det
+        oid = np.zeros(cap, np.uint32)
+        nv = np.zeros(cap, np.int32)
+        ar = np.zeros(cap, np.float32)
+        dm = np.zeros(cap, np.float32)
+        n = _check(lib().smg_get_assoc(self.h, m, _ptr(oid), _ptr(nv), _ptr(ar), _ptr(dm), cap), "smg_get_assoc")
+        return dict(obj_id=oid[:n], n_valid=nv[:n], area_px=ar[:n], depth_med=dm[:n])
+
+    def stats(self, m: int = 0) -> dict:
+        s = np.zeros(16, np.int64)
+        _check(lib().smg_get_stats(self.h, m, _ptr(s)), "smg_get_stats")
+        return {k: int(v) for k, v in zip(STAT_FIELDS, s)}
+
+    def events(self, m: int = 0):
+        cap = 1024
+        t = np.zeros(cap, np.float64)
+        i = np.zeros(cap, np.uint32)
+        k = np.zeros(cap, np.int32)
+        n = _check(lib().smg_get_events(self.h, m, _ptr(t), _ptr(i), _ptr(k), cap), "smg_get_events")
+        return list(zip(t[:n].tolist(), i[:n].tolist(), k[:n].tolist()))
+
+    def grid_cells(self, m: int = 0):
+        gw, gh, x0, y0 = self.grid
+        L = np.zeros((gh, gw), np.int16)
+        seen = np.zeros((gh, gw), np.uint8)
+        c8 = np.zeros((gh, gw), np.int8)
+        _check(lib().smg_get_grid(self.h, m, _ptr(L), _ptr(seen), _ptr(c8)), "smg_get_grid")
+        return dict(x0=x0, y0=y0, w=gw, h=gh, L=L, seen=seen, c8=c8)
+
+    def keyframe(self, m: int = 0):
+        o = np.zeros(3, np.int32)
+        _check(lib().smg_get_keyframe(self.h, m, _ptr(o)), "smg_get_keyframe")
+        return dict(inserted=int(o[0]), changed=int(o[1]), n_hits=int(o[2]))
+
+    def error_word(self) -> int:
+        return _check(lib().smg_error_word(self.h), "smg_error_word")
+
+    def launches(self) -> int:
+        return int(lib().smg_kernel_launches(self.h))

@@ -1,0 +1,124 @@
+"""Seeded synthetic frames for the scenemap objprob configurations (ctypes over libsynth.so).
+
+The generator itself is C (``synth/synth.h``, ``synth/synth_host.cpp``); this module only
+wraps it and assembles per-frame input dictionaries that both the B200 path and the CPU
+reference consume, so that both see byte-identical inputs.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(os.path.dirname(_HERE), "synth", "libsynth.so")
+
+SY_MAX_BOXES = 64
+
+
+class SyBox(C.Structure):
+    _fields_ = [("lo", C.c_double * 3), ("hi", C.c_double * 3)]
+
+
+class SyScene(C.Structure):
+    _fields_ = [("seed", C.c_uint64), ("room", C.c_double * 3), ("n_boxes", C.c_int),
+                ("box", SyBox * SY_MAX_BOXES), ("noise_k", C.c_float)]
+
+
+class SyCamera(C.Structure):
+    _fields_ = [("w", C.c_int), ("h", C.c_int), ("fx", C.c_float), ("fy", C.c_float),
+                ("cx", C.c_float), ("cy", C.c_float)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            raise RuntimeError(f"libsynth.so not built ({_LIB_PATH}); run __graft_entry__.build()")
+        L = C.CDLL(_LIB_PATH)
+        P = C.POINTER
+        L.sy_scene_make.argtypes = [C.c_uint64, C.c_int, C.c_double, C.c_double, C.c_double, C.c_float,
+                                    C.c_double, C.c_double, C.c_double, C.c_double, P(SyScene)]
+        L.sy_traj.argtypes = [P(SyScene), C.c_int, C.c_double, C.c_double, C.c_double, P(C.c_double)]
+        L.sy_rig_T_bc.argtypes = [C.c_float, C.c_float, C.c_float, P(C.c_float)]
+        L.sy_T_mc.argtypes = [P(C.c_double), P(C.c_float), P(C.c_double)]
+        L.sy_render.argtypes = [P(SyScene), P(SyCamera), P(C.c_double), C.c_uint64, P(C.c_float), P(C.c_uint16)]
+        L.sy_dets.argtypes = [P(C.c_uint16), C.c_int, C.c_int, C.c_int, C.c_int, P(C.c_uint16), P(C.c_float),
+                              P(C.c_int32), P(C.c_float)]
+        L.sy_dets.restype = C.c_int
+        L.sy_embed.argtypes = [P(SyScene), C.c_uint64, C.c_int, P(C.c_uint16), C.c_int, C.c_double, C.c_int, P(C.c_float)]
+        _lib = L
+    return _lib
+
+
+def _p(a, t):
+    return a.ctypes.data_as(C.POINTER(t))
+
+
+def map_seed(base: int, index: int) -> int:
+    """Per-map seed: splitmix64 of base xor map index."""
+    z = (base ^ index) & 0xFFFFFFFFFFFFFFFF
+    z = (z + 0x9E3779B97F4A7C15) & 0xFFFFFFFFFFFFFFFF
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & 0xFFFFFFFFFFFFFFFF
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & 0xFFFFFFFFFFFFFFFF
+    return z ^ (z >> 31)
+
+
+class BoxRoom:
+    """Config 0/1/4 generator: 6x5x2.6 m room, 20 boxes, pinhole camera on a moving base."""
+
+    def __init__(self, seed: int, n_boxes: int = 20, room=(6.0, 5.0, 2.6), noise_k: float = 0.005,
+                 size=(0.2, 0.6), height=(0.15, 0.9), w: int = 640, h: int = 480, fx: float = 525.0,
+                 fy: float = 525.0, cx: float = 319.5, cy: float = 239.5, dt: float = 0.1, speed: float = 0.3,
+                 n_frames: int = 300, D: int = 1152, bf16: bool = False, emb_sigma: float = 0.05,
+                 min_px: int = 64, max_det: int = 24, cam_height: float = 0.9, pitch_deg: float = 20.0):
+        L = lib()
+        self.seed = seed
+        self.scene = SyScene()
+        L.sy_scene_make(seed, n_boxes, room[0], room[1], room[2], noise_k, size[0], size[1], height[0], height[1],
+                        C.byref(self.scene))
+        self.cam = SyCamera(w, h, fx, fy, cx, cy)
+        self.w, self.h, self.fx, self.fy, self.cx, self.cy = w, h, fx, fy, cx, cy
+        self.dt, self.n_frames, self.D, self.bf16, self.emb_sigma = dt, n_frames, D, bf16, emb_sigma
+        self.min_px, self.max_det = min_px, max_det
+        self.poses = np.zeros((n_frames, 3), np.float64)
+        L.sy_traj(C.byref(self.scene), n_frames, dt, speed, 0.5, _p(self.poses, C.c_double))
+        self.T_bc = np.zeros(12, np.float32)
+        L.sy_rig_T_bc(0.1, cam_height, pitch_deg, _p(self.T_bc, C.c_float))
+        # hands: far from everything (the synthetic rig has no arm)
+        self.eef = np.full((2, 3), 1000.0, np.float64)
+        self.eef_base = np.tile(np.array([-0.05, 0.0, 0.25], np.float32), (2, 1))
+
+    def T_mc(self, f: int) -> np.ndarray:
+        out = np.zeros(12, np.float64)
+        pose = np.ascontiguousarray(self.poses[f])
+        lib().sy_T_mc(_p(pose, C.c_double), _p(self.T_bc, C.c_float), _p(out, C.c_double))
+        return out
+
+    def frame(self, f: int) -> dict:
+        L = lib()
+        T = self.T_mc(f)
+        depth = np.zeros((self.h, self.w), np.float32)
+        label = np.zeros((self.h, self.w), np.uint16)
+        key = f + 1
+        L.sy_render(C.byref(self.scene), C.byref(self.cam), _p(T, C.c_double), key, _p(depth, C.c_float),
+                    _p(label, C.c_uint16))
+        md = self.max_det
+        det_label = np.zeros(md, np.uint16)
+        box = np.zeros((md, 4), np.float32)
+        cls = np.zeros(md, np.int32)
+        score = np.zeros(md, np.float32)
+        n = L.sy_dets(_p(label, C.c_uint16), self.w, self.h, self.min_px, md, _p(det_label, C.c_uint16),
+                      _p(box, C.c_float), _p(cls, C.c_int32), _p(score, C.c_float))
+        emb = np.zeros((max(n, 1), self.D), np.float32)
+        if n:
+            L.sy_embed(C.byref(self.scene), key, n, _p(det_label, C.c_uint16), self.D, self.emb_sigma,
+                       1 if self.bf16 else 0, _p(emb, C.c_float))
+        return dict(stamp=f * self.dt, w=self.w, h=self.h, depth=depth, label=label, fx=self.fx, fy=self.fy,
+                    cx=self.cx, cy=self.cy, T_mc=T, T_bc=self.T_bc, base=self.poses[f].copy(), eef=self.eef,
+                    eef_base=self.eef_base, n_det=n, det_label=det_label[:n].copy(), box=box[:n].copy(),
+                    cls=cls[:n].copy(), score=score[:n].copy(), emb=emb[:n].copy(), emb_dim=self.D)
