@@ -1,0 +1,358 @@
+#!/usr/bin/env python
+"""Benchmark: map-frames/s of the scenemap objprob keyframe update.
+
+Workload (per GPU): 64 independent box-room maps (config-0 generator, per-map seeds), 640x480
+fp32 depth + uint16 labels, 8-24 detections per frame, 1152-d bf16 embeddings, 512x512 grid.
+A step = one keyframe of every map (Mapper2D::keyframe + ObjectMap::update + addPoints).
+The maps first run `--preroll` untimed frames (so the timed window sees a populated memory),
+then W warm-up steps, then K timed steps.  Each step reads fresh frames (118 MB of new input
+per step at 64 maps; the timed window reads K x that from HBM), so no L2 flush is inserted.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Multi-GPU (torchrun): every rank owns its own 64 maps (weak scaling, no collective on the
+path); per-map ApStats are gathered to rank 0 with NCCL after the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "robot-agent_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+METRIC = "map-frames/s of scenemap objprob update"
+UNIT = "map-frames/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--preroll", type=int, default=100)
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--maps", type=int, default=64)
+    ap.add_argument("--max-objects", type=int, default=512)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-frames", type=int, default=30, help="CPU baseline: frames per map (untimed lead-in + timed)")
+    ap.add_argument("--cpu-timed", type=int, default=10, help="CPU baseline: timed frames per map")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    def __init__(self, gpu_index: int, path: str):
+        self.path = path
+        self.proc = None
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}", "--format=csv,noheader",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1].split()[0]))
+                mx = float(p[2].split()[0])
+            except ValueError:
+                continue
+            for name, v in zip(["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"], p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline (reference scenemap code)
+def cpu_reference(M_sample: int, frames: int, timed: int, threads: int, base_seed: int = 1000):
+    """The reference scenemap (oracle/_ref, compiled from the reference sources) on the host cores:
+    one map per thread; each map runs `frames` keyframes, the last `timed` of which are timed.
+    Inputs come from the same generator (device renderer when a GPU is present, else host)."""
+    from oracle import ref
+    from scenemap_b200 import synth
+    if not ref.available():
+        return None
+    gen_dev = False
+    try:
+        import torch
+        gen_dev = torch.cuda.is_available()
+    except Exception:
+        pass
+    inputs = []   # per map: list of frame dicts (host numpy)
+    if gen_dev:
+        from scenemap_b200.workload import RoomBatch
+        wl = RoomBatch(M_sample, base_seed, frames, D=1152, bf16=True, max_det=24)
+        for f0 in range(0, frames, 10):
+            nf = min(10, frames - f0)
+            R = wl.render(f0, nf)
+            for fi in range(nf):
+                hf = wl.host_frames(R, fi)
+                for m in range(M_sample):
+                    if len(inputs) <= m:
+                        inputs.append([])
+                    inputs[m].append(hf[m])
+    else:
+        for m in range(M_sample):
+            g = synth.BoxRoom(seed=synth.map_seed(base_seed, m), n_frames=frames, bf16=True, max_det=24)
+            inputs.append([g.frame(f) for f in range(frames)])
+    t_timed = [0.0] * M_sample
+    lead = frames - timed
+
+    def work(m):
+        R = ref.RefMap()
+        for f in range(frames):
+            if f == lead:
+                t0 = time.perf_counter()
+            R.frame(inputs[m][f])
+        t_timed[m] = time.perf_counter() - t0
+
+    ths = []
+    for start in range(0, M_sample, threads):
+        batch = [threading.Thread(target=work, args=(m,)) for m in range(start, min(M_sample, start + threads))]
+        t0 = time.perf_counter()
+        for t in batch:
+            t.start()
+        for t in batch:
+            t.join()
+        ths.append(time.perf_counter() - t0)
+    # throughput: timed map-frames over the slowest thread's timed span, per concurrent wave
+    waves = [t_timed[i:i + threads] for i in range(0, M_sample, threads)]
+    value = sum(len(w) * timed for w in waves) / sum(max(w) for w in waves)
+    return dict(value=value, unit=UNIT, cores=threads, kind="reference",
+                sample=f"{M_sample} maps x frames {lead}..{frames - 1} (timed {timed} per map), one map per thread, "
+                       f"reference scenemap C++ (-O2) from oracle/_ref")
+
+
+# ------------------------------------------------------------------ B200 arm
+def k_obs_bytes(wl, R, fi):
+    """Algorithmic bytes of one k_obs launch: depth (4 B) at every scanned pixel and the label
+    (2 B) of the pixel and its 4 erosion neighbours (each label pixel once when sk == 1)."""
+    tot = 0
+    for m in range(wl.M):
+        d = R["dets"][fi * wl.M + m]
+        for k in range(d["n"]):
+            b = d["box"][k]
+            u0, u1 = max(0, int(b[0]) - 1), min(wl.w - 1, int(b[2]) + 1)
+            v0, v1 = max(0, int(b[1]) - 1), min(wl.h - 1, int(b[3]) + 1)
+            box_px = max(0, u1 - u0 + 1) * max(0, v1 - v0 + 1)
+            sk = max(1, int(np.ceil(np.sqrt(box_px / 6000.0))))
+            npx = ((u1 - u0) // sk + 1) * ((v1 - v0) // sk + 1)
+            tot += npx * 4 + (npx * 2 if sk == 1 else npx * 10)
+    return tot
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    from scenemap_b200 import smg
+    from scenemap_b200.workload import RoomBatch
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    M = args.maps
+    n_total = args.preroll + args.warmup + args.steps + args.e2e_steps
+    wl = RoomBatch(M, 1000, n_total, D=1152, bf16=True, max_det=24, map_offset=rank * M, device=str(dev))
+    B = smg.Batch(M, max_objects=args.max_objects, emb_dim=1152, max_w=640, max_h=480, max_det=24,
+                  grid=(512, 512, -256 + 60, -256 + 50), dev=local_rank)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    f = 0
+    # untimed pre-roll + warm-up
+    while f < args.preroll + args.warmup:
+        nf = min(16, args.preroll + args.warmup - f)
+        R = wl.render(f, nf, sp)
+        for fi in range(nf):
+            keep = []
+            B.push(None, smg.SMG_MEM_DEVICE, structs=wl.structs(R, fi, keep), stream=sp)
+        f += nf
+    torch.cuda.synchronize()
+    assert B.error_word() == 0, "device error word set during warm-up"
+    # timed window: inputs resident in HBM before the clock starts
+    R = wl.render(f, args.steps, sp)
+    keep = []
+    structs = [wl.structs(R, fi, keep) for fi in range(args.steps)]
+    obs_bytes = [k_obs_bytes(wl, R, fi) for fi in range(args.steps)]
+    B.timing_read()
+    B.timing(True)
+    launches0 = B.launches()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clk = Clocks(local_rank, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
+                                          f"clocks_r{rank}.csv"))
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for fi in range(args.steps):
+        B.push(None, smg.SMG_MEM_DEVICE, structs=structs[fi], stream=sp)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = clk.stop()
+    t = e0.elapsed_time(e1) / 1e3
+    launches = B.launches() - launches0
+    kt = B.timing_read()
+    B.timing(False)
+    err = B.error_word()
+    f += args.steps
+    del R, structs
+    # e2e: host (pinned) inputs through the C ABI, association read back every step
+    E = args.e2e_steps
+    R = wl.render(f, E, sp)
+    depth_h = torch.empty((E, M, 480, 640), dtype=torch.float32, pin_memory=True)
+    label_h = torch.empty((E, M, 480, 640), dtype=torch.int16, pin_memory=True)
+    emb_h = torch.empty(R["emb"].shape, dtype=torch.int16, pin_memory=True)
+    depth_h.copy_(R["depth"])
+    label_h.copy_(R["label"].view(torch.int16))
+    emb_h.copy_(R["emb"].view(torch.int16))
+    torch.cuda.synchronize()
+    e_structs, keep2 = [], []
+    h2d = 0
+    for fi in range(E):
+        arr = (smg.SmgFrame * M)()
+        for m in range(M):
+            fd = wl.frame_dict(R, fi, m)
+            d = R["dets"][fi * M + m]
+            ptrs = dict(depth=depth_h[fi, m].data_ptr(), label=label_h[fi, m].data_ptr(),
+                        emb=emb_h.data_ptr() + d["emb_off"] * 1152 * 2 if d["n"] else None)
+            arr[m] = smg.Batch.frame_struct(fd, keep2, smg.SMG_EMB_BF16, ptrs=ptrs)
+            h2d += 640 * 480 * 6 + d["n"] * 1152 * 2
+        e_structs.append(arr)
+    h2d //= E
+    d2h = M * 24 * 16
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for fi in range(E):
+        B.push(None, smg.SMG_MEM_HOST, structs=e_structs[fi], stream=sp)
+        B.assoc_all()
+    torch.cuda.synchronize()
+    t_e2e = time.perf_counter() - t0
+    if world > 1:
+        torch.distributed.barrier()
+    err |= B.error_word()
+    # per-map statistics gathered to rank 0 (NCCL over NVLink when world > 1)
+    stats = np.zeros((M, 16), np.int64)
+    for m in range(M):
+        s = B.stats(m)
+        stats[m] = list(s.values())
+    st_t = torch.from_numpy(stats).to(dev)
+    if world > 1:
+        gathered = [torch.empty_like(st_t) for _ in range(world)]
+        torch.distributed.all_gather(gathered, st_t)
+        all_stats = torch.cat(gathered).cpu().numpy()
+        tt = torch.tensor([t, t_e2e], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        t, t_e2e = float(tt[0]), float(tt[1])
+    else:
+        all_stats = stats
+    n_obj = [len(B.objects(m)) for m in range(min(M, 4))]
+    B.close()
+    return dict(t=t, t_e2e=t_e2e, kt=kt, launches=launches, err=err, clocks=clocks, obs_bytes=obs_bytes,
+                stats=all_stats, h2d=h2d, d2h=d2h, n_obj=n_obj)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = {"workload": "config 1: 64 box-room maps per GPU, 640x480 fp32 depth + u16 labels, 8-24 dets, "
+                       "1152-d bf16 embeddings, <=512 object slots, 512x512 grid",
+           "maps_per_gpu": args.maps, "frames_timed": f"{args.preroll + args.warmup}..{args.preroll + args.warmup + args.steps - 1}",
+           "l2": "fresh frames every step (118 MB/step at 64 maps), no flush", "parallelism": f"dp{world} (maps)"}
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cores = os.cpu_count() or 1
+        cb = cpu_reference(min(max(cores, 8), 64), args.cpu_frames, args.cpu_timed, min(cores, 64))
+        if cb is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libscenemap_ref.so not built"}))
+            return
+        print(json.dumps({"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.cpu_timed,
+                          "warmup": args.cpu_frames - args.cpu_timed, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "f64/f32", "data": "synthetic", "config": cfg, "impl": "reference",
+                          "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                          "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+    if world > 1:
+        import datetime
+        import torch
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    r = run_b200(args, rank, world, local_rank)
+    if world > 1:
+        import torch
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    K, M = args.steps, args.maps
+    value = M * world * K / r["t"]
+    e2e = M * world * args.e2e_steps / r["t_e2e"]
+    # roofline of the dominant kernel
+    kt = r["kt"]
+    dom = max(kt, key=lambda k: kt[k][0])
+    ms, n = kt[dom]
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    roof = None
+    if dom == "k_obs":
+        avg_s = ms / n / 1e3
+        alg = float(np.mean(r["obs_bytes"]))
+        roof = {"kernel": dom, "bound": "hbm", "achieved": alg / avg_s / 1e9, "peak": hbm, "unit": "GB/s",
+                "frac": alg / avg_s / 1e9 / hbm, "traffic": None, "alg_bytes_per_launch": alg,
+                "avg_launch_ms": ms / n, "peak_source": "MEASURED_PEAKS.json" if peaks else "fallback"}
+    else:
+        roof = {"kernel": dom, "bound": "hbm", "achieved": None, "peak": hbm, "unit": "GB/s", "frac": None,
+                "traffic": None, "avg_launch_ms": ms / n}
+    cb = None
+    if not args.no_cpu_baseline and world == 1:
+        cores = os.cpu_count() or 1
+        cb = cpu_reference(min(max(cores, 8), 64), args.cpu_frames, args.cpu_timed, min(cores, 64))
+    out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+           "ms_per_step": 1e3 * r["t"] / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "f64/f32 (bf16 embeddings)", "data": "synthetic", "config": cfg,
+           "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+           "gpu_launches": r["launches"], "roofline": roof, "clocks": r["clocks"],
+           "kernel_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in kt.items()},
+           "device_error_word": r["err"], "objects_first_maps": r["n_obj"],
+           "stats_sum": {k: int(v) for k, v in zip(["n_through", "n_obs", "n_wall", "n_wall_name", "n_ceil", "n_floor",
+                                                     "n_assoc", "n_new", "n_merge", "n_obj_struct", "n_reenc_req",
+                                                     "n_reenc_done", "n_blocked", "n_wall_tall", "n_so_big", "n_bridge"],
+                                                    r["stats"].sum(0))}}
+    if cb is not None:
+        out["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

@@ -179,6 +179,14 @@ int smg_get_events(smg_batch* b, int m, double* t, uint32_t* id, int32_t* kind, 
 int smg_get_grid(smg_batch* b, int m, int16_t* L, uint8_t* seen, int8_t* c8);
 /* Keyframe stats of the last frame of map m: inserted, changed_cells, n_hits (KeyframeStats). */
 int smg_get_keyframe(smg_batch* b, int m, int32_t* out3);
+/* Association of all maps in one read: obj_id[m * max_det + k] (0 = no object). */
+int smg_get_assoc_all(smg_batch* b, uint32_t* obj_id);
+/* Per-kernel device time with CUDA events on the launch stream (instrumentation, off by
+ * default).  smg_timing_read fills ms[k] (total milliseconds) and n[k] (launches) for the
+ * SMG_NUM_KERNELS kernels of the keyframe chain and resets the counters; names[k] is static. */
+#define SMG_NUM_KERNELS 14
+int smg_timing_enable(smg_batch* b, int on);
+int smg_timing_read(smg_batch* b, double* ms, int64_t* n, const char** names);
 /* Device error word (0 = none) and a static description of the last host-side error. */
 int smg_error_word(smg_batch* b);
 const char* smg_last_error(void);

@@ -46,14 +46,40 @@ struct smg_batch {
   int dev;
   int max_w, max_h;
   std::vector<void*> allocs;
-  FrameDev* h_frames = nullptr;   // pinned
+  static const int kRing = 4;
+  FrameDev* h_ring = nullptr;     // pinned, kRing x M descriptors
+  cudaEvent_t ring_ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  bool ring_used[4] = {false, false, false, false};
+  long long n_push = 0;
+  FrameDev* h_frames = nullptr;   // current ring slot
   float* d_depth = nullptr;       // staging for SMG_MEM_HOST
   uint16_t* d_label = nullptr;
   unsigned char* d_emb = nullptr;
   std::vector<double> last_cam_t, last_cam_fwd;
   long long launches = 0;
   cudaStream_t last_stream = nullptr;
+  // per-kernel event timing
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_pool;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> ev_used;
+  double k_ms[SMG_NUM_KERNELS] = {0};
+  long long k_n[SMG_NUM_KERNELS] = {0};
 };
+
+static const char* k_names[SMG_NUM_KERNELS] = {"k_begin", "k_merge_pairs", "k_merge_apply", "k_obs", "k_obs_finalize", "k_assoc",
+                                               "k_update", "k_absent", "k_relink", "k_struct", "k_prune", "k_markview",
+                                               "k_cloud_add", "k_grid"};
+
+static cudaEvent_t ev_get(smg_batch* b) {
+  if (b->ev_pool.empty()) {
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    return e;
+  }
+  cudaEvent_t e = b->ev_pool.back();
+  b->ev_pool.pop_back();
+  return e;
+}
 
 extern "C" int smg_destroy(smg_batch* b);
 template <class T>
@@ -200,8 +226,11 @@ int smg_params_apply(smg_params* p, const char* kv) {
 
 int smg_destroy(smg_batch* b) {
   if (!b) return SMG_ERR_ARGS;
+  for (auto& u : b->ev_used) { cudaEventDestroy(u.second.first); cudaEventDestroy(u.second.second); }
+  for (auto e : b->ev_pool) cudaEventDestroy(e);
   for (void* p : b->allocs) cudaFree(p);
-  if (b->h_frames) cudaFreeHost(b->h_frames);
+  if (b->h_ring) cudaFreeHost(b->h_ring);
+  for (auto e : b->ring_ev) if (e) cudaEventDestroy(e);
   delete b;
   return SMG_OK;
 }
@@ -383,7 +412,8 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   k_fill_i8<<<256, 256>>>(B.gc8, G, (int8_t)-1);
   b->launches += 3;
   CK(cudaGetLastError());
-  CK(cudaMallocHost(&b->h_frames, sizeof(FrameDev) * M));
+  CK(cudaMallocHost(&b->h_ring, sizeof(FrameDev) * M * smg_batch::kRing));
+  for (int r = 0; r < smg_batch::kRing; ++r) CK(cudaEventCreateWithFlags(&b->ring_ev[r], cudaEventDisableTiming));
   b->last_cam_t.assign(M, -1e300);
   b->last_cam_fwd.assign(3 * (size_t)M, 0.0);
   // kernels with large dynamic shared memory
@@ -434,6 +464,10 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
         (f.n_det > 0 && (!f.label || !f.det_label || !f.box || !f.cls)) || (f.emb && f.emb_dtype != SMG_EMB_F32 && f.emb_dtype != SMG_EMB_BF16))
       return fail(SMG_ERR_ARGS, "smg_push_frames: bad frame");
   }
+  // pinned descriptor ring: wait until the copy that last read this slot has run
+  const int slot = (int)(b->n_push++ % smg_batch::kRing);
+  if (b->ring_used[slot]) CK(cudaEventSynchronize(b->ring_ev[slot]));
+  b->h_frames = b->h_ring + (size_t)slot * B.M;
   const size_t WH = (size_t)b->max_w * b->max_h;
   const size_t esz = 4;
   for (int m = 0; m < B.M; ++m) {
@@ -516,21 +550,51 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     }
   }
   CK(cudaMemcpyAsync(B.frames, b->h_frames, sizeof(FrameDev) * B.M, cudaMemcpyHostToDevice, st));
+  CK(cudaEventRecord(b->ring_ev[slot], st));
+  b->ring_used[slot] = true;
   const int M = B.M;
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_begin<<<M, 128, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({0, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_merge_pairs<<<dim3(MP_CTAS, M), 256, 8 * (B.D + 3 * MP_SPW) * 4, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({1, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_merge_apply<<<M, 512, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({2, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_obs<<<dim3(B.max_det, M), OBS_THREADS, OBS_HASH * 12, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({3, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_obs_finalize<<<M, 32, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({4, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_assoc<<<dim3(B.max_det, M), ASSOC_THREADS, ((B.D * 4 + SP_MAX * 12 + 7) & ~7) + B.O * 8, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({5, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_update<<<M, UPD_THREADS, B.D * 4, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({6, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_absent<<<dim3(4, M), 256, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({7, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_relink<<<M, 256, 8 * B.D * 4, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({8, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_struct<<<dim3(WORK_SLOTS, M), 256, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({9, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_prune<<<M, 32, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({10, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_markview<<<M, 256, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({11, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_cloud_add<<<dim3(WORK_SLOTS, M), 512, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({12, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_grid<<<M, GRID_THREADS, 0, st>>>(B);
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({13, {e0, e1}}); } }
   b->launches += 14;
   CK(cudaGetLastError());
   return SMG_OK;
@@ -707,6 +771,45 @@ int smg_get_keyframe(smg_batch* b, int m, int32_t* out3) {
   out3[0] = R.kf_inserted;
   out3[1] = R.kf_changed;
   out3[2] = R.kf_hits;
+  return SMG_OK;
+}
+
+int smg_get_assoc_all(smg_batch* b, uint32_t* obj_id) {
+  if (!b || !obj_id) return fail(SMG_ERR_ARGS, "smg_get_assoc_all: bad arguments");
+  const Batch& B = b->B;
+  std::vector<AssocRec> a((size_t)B.M * B.max_det);
+  CK(cudaSetDevice(b->dev));
+  CK(cudaMemcpyAsync(a.data(), B.assoc, sizeof(AssocRec) * a.size(), cudaMemcpyDeviceToHost, b->last_stream));
+  CK(cudaStreamSynchronize(b->last_stream));
+  for (size_t i = 0; i < a.size(); ++i) obj_id[i] = a[i].obj_id;
+  return SMG_OK;
+}
+
+int smg_timing_enable(smg_batch* b, int on) {
+  if (!b) return SMG_ERR_ARGS;
+  b->timing = on != 0;
+  return SMG_OK;
+}
+
+int smg_timing_read(smg_batch* b, double* ms, int64_t* n, const char** names) {
+  if (!b) return fail(SMG_ERR_ARGS, "smg_timing_read: bad arguments");
+  if (int r = sync_b(b)) return r;
+  for (auto& u : b->ev_used) {
+    float t = 0;
+    CK(cudaEventElapsedTime(&t, u.second.first, u.second.second));
+    b->k_ms[u.first] += t;
+    b->k_n[u.first] += 1;
+    b->ev_pool.push_back(u.second.first);
+    b->ev_pool.push_back(u.second.second);
+  }
+  b->ev_used.clear();
+  for (int k = 0; k < SMG_NUM_KERNELS; ++k) {
+    if (ms) ms[k] = b->k_ms[k];
+    if (n) n[k] = b->k_n[k];
+    if (names) names[k] = k_names[k];
+    b->k_ms[k] = 0;
+    b->k_n[k] = 0;
+  }
   return SMG_OK;
 }
 

@@ -66,6 +66,9 @@ def lib():
         L.smg_get_keyframe.argtypes = [vp, C.c_int, vp]
         L.smg_error_word.argtypes = [vp]
         L.smg_last_error.restype = C.c_char_p
+        L.smg_get_assoc_all.argtypes = [vp, vp]
+        L.smg_timing_enable.argtypes = [vp, C.c_int]
+        L.smg_timing_read.argtypes = [vp, vp, vp, vp]
         L.smg_kernel_launches.restype = C.c_int64
         L.smg_kernel_launches.argtypes = [vp]
         _lib = L
@@ -75,7 +78,9 @@ def lib():
 EXPORTED = ["smg_params_size", "smg_params_default", "smg_params_apply", "smg_create", "smg_destroy", "smg_push_frames",
             "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
             "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
-            "smg_kernel_launches"]
+            "smg_kernel_launches", "smg_get_assoc_all", "smg_timing_enable", "smg_timing_read"]
+
+NUM_KERNELS = 14
 
 
 def _ptr(a):
@@ -243,6 +248,21 @@ class Batch:
         o = np.zeros(3, np.int32)
         _check(lib().smg_get_keyframe(self.h, m, _ptr(o)), "smg_get_keyframe")
         return dict(inserted=int(o[0]), changed=int(o[1]), n_hits=int(o[2]))
+
+    def assoc_all(self) -> np.ndarray:
+        out = np.zeros(self.n_maps * self.max_det, np.uint32)
+        _check(lib().smg_get_assoc_all(self.h, _ptr(out)), "smg_get_assoc_all")
+        return out.reshape(self.n_maps, self.max_det)
+
+    def timing(self, on: bool = True):
+        _check(lib().smg_timing_enable(self.h, 1 if on else 0), "smg_timing_enable")
+
+    def timing_read(self) -> dict:
+        ms = np.zeros(NUM_KERNELS, np.float64)
+        n = np.zeros(NUM_KERNELS, np.int64)
+        names = (C.c_char_p * NUM_KERNELS)()
+        _check(lib().smg_timing_read(self.h, _ptr(ms), _ptr(n), names), "smg_timing_read")
+        return {names[k].decode(): (float(ms[k]), int(n[k])) for k in range(NUM_KERNELS)}
 
     def error_word(self) -> int:
         return _check(lib().smg_error_word(self.h), "smg_error_word")

@@ -1,25 +1,117 @@
-// Device renderer of the synthetic box room (synth.h): the same per-pixel function as the
-// host generator, for producing benchmark inputs directly in HBM.  Not on the measured path.
+// Device side of the synthetic generator (synth.h): renders frames, label statistics and
+// detection embeddings directly in HBM, for benchmark inputs.  Not on the measured path.
+// The per-pixel render is the same function as the host generator; embeddings normalise with
+// a block reduction (the host sums sequentially), so a device embedding can differ from the
+// host one in the last float bit.
 #include <stdint.h>
 
 #include "synth.h"
 
-__global__ void sy_render_kernel(sy_scene S, sy_camera Cm, const double* __restrict__ T_all, const uint64_t* __restrict__ keys,
-                                 int n_frames, float* __restrict__ depth, uint16_t* __restrict__ label) {
-  const int f = blockIdx.y;
-  if (f >= n_frames) return;
+#define SY_NLAB (1 + 3 * SY_MAX_BOXES)
+
+// frames f of maps m: T_all[(f*M + m)*12], keys[f*M + m]; output image (f*M + m)
+__global__ void sy_render_batch_kernel(const sy_scene* __restrict__ scenes, sy_camera Cm, const double* __restrict__ T_all,
+                                       const uint64_t* __restrict__ keys, int M, int n_img, float* __restrict__ depth,
+                                       uint16_t* __restrict__ label) {
+  const int img = blockIdx.y;
+  if (img >= n_img) return;
+  const sy_scene* S = &scenes[img % M];
   const size_t WH = (size_t)Cm.w * Cm.h;
   double T[12];
-  for (int k = 0; k < 12; ++k) T[k] = T_all[12 * f + k];
+  for (int k = 0; k < 12; ++k) T[k] = T_all[12 * (size_t)img + k];
   for (size_t p = blockIdx.x * (size_t)blockDim.x + threadIdx.x; p < WH; p += (size_t)gridDim.x * blockDim.x) {
     const int u = (int)(p % Cm.w), v = (int)(p / Cm.w);
-    sy_pixel(&S, &Cm, T, keys[f], u, v, depth + f * WH + p, label + f * WH + p);
+    sy_pixel(S, &Cm, T, keys[img], u, v, depth + img * WH + p, label + img * WH + p);
   }
 }
 
-extern "C" int sy_render_device(const sy_scene* S, const sy_camera* C, const double* T_dev, const uint64_t* keys_dev, int n_frames,
-                                float* depth_dev, uint16_t* label_dev, void* stream) {
-  dim3 grid(148, n_frames);
-  sy_render_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(*S, *C, T_dev, keys_dev, n_frames, depth_dev, label_dev);
+// per image and label: count, umin, vmin, umax, vmax (stats[img][SY_NLAB][5])
+__global__ void sy_label_stats_kernel(const uint16_t* __restrict__ label, int w, int h, int n_img, int* __restrict__ stats) {
+  __shared__ int s[SY_NLAB * 5];
+  const int img = blockIdx.y;
+  if (img >= n_img) return;
+  for (int i = threadIdx.x; i < SY_NLAB; i += blockDim.x) {
+    s[5 * i] = 0; s[5 * i + 1] = w; s[5 * i + 2] = h; s[5 * i + 3] = -1; s[5 * i + 4] = -1;
+  }
+  __syncthreads();
+  const size_t WH = (size_t)w * h;
+  const uint16_t* L = label + img * WH;
+  for (size_t p = blockIdx.x * (size_t)blockDim.x + threadIdx.x; p < WH; p += (size_t)gridDim.x * blockDim.x) {
+    const int l = L[p];
+    if (l <= 0 || l >= SY_NLAB) continue;
+    const int u = (int)(p % w), v = (int)(p / w);
+    atomicAdd(&s[5 * l], 1);
+    atomicMin(&s[5 * l + 1], u); atomicMin(&s[5 * l + 2], v);
+    atomicMax(&s[5 * l + 3], u); atomicMax(&s[5 * l + 4], v);
+  }
+  __syncthreads();
+  int* o = stats + (size_t)img * SY_NLAB * 5;
+  for (int i = threadIdx.x; i < SY_NLAB; i += blockDim.x) {
+    atomicAdd(&o[5 * i], s[5 * i]);
+    atomicMin(&o[5 * i + 1], s[5 * i + 1]); atomicMin(&o[5 * i + 2], s[5 * i + 2]);
+    atomicMax(&o[5 * i + 3], s[5 * i + 3]); atomicMax(&o[5 * i + 4], s[5 * i + 4]);
+  }
+}
+
+__global__ void sy_stats_init_kernel(int* stats, int n_img, int w, int h) {
+  const size_t n = (size_t)n_img * SY_NLAB;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    stats[5 * i] = 0; stats[5 * i + 1] = w; stats[5 * i + 2] = h; stats[5 * i + 3] = -1; stats[5 * i + 4] = -1;
+  }
+}
+
+// one block per detection: desc[4*j] = map, box, det slot k, frame key (as two ints: lo, hi)
+__global__ void sy_embed_kernel(const sy_scene* __restrict__ scenes, const int* __restrict__ desc, int n, int D, double sigma,
+                                int bf16, void* __restrict__ out) {
+  const int j = blockIdx.x;
+  if (j >= n) return;
+  const int m = desc[5 * j], box = desc[5 * j + 1], k = desc[5 * j + 2];
+  const uint64_t key = (uint64_t)(uint32_t)desc[5 * j + 3] | ((uint64_t)(uint32_t)desc[5 * j + 4] << 32);
+  const uint64_t seed = scenes[m].seed;
+  __shared__ double red[32];
+  double s = 0;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const double v = sy_emb_raw(seed, box, key, k, i, sigma);
+    s += v * v;
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const double inv = 1.0 / sqrt(red[0]);
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float f = (float)(sy_emb_raw(seed, box, key, k, i, sigma) * inv);
+    if (bf16) ((uint16_t*)out)[(size_t)j * D + i] = (uint16_t)(__float_as_uint(sy_bf16_round(f)) >> 16);
+    else ((float*)out)[(size_t)j * D + i] = f;
+  }
+}
+
+extern "C" {
+
+int sy_render_batch_device(const sy_scene* scenes_dev, const sy_camera* C, const double* T_dev, const uint64_t* keys_dev, int M,
+                           int n_img, float* depth_dev, uint16_t* label_dev, void* stream) {
+  dim3 grid(296, n_img);
+  sy_render_batch_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(scenes_dev, *C, T_dev, keys_dev, M, n_img, depth_dev, label_dev);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
+
+int sy_label_stats_device(const uint16_t* label_dev, int w, int h, int n_img, int* stats_dev, void* stream) {
+  sy_stats_init_kernel<<<256, 256, 0, (cudaStream_t)stream>>>(stats_dev, n_img, w, h);
+  sy_label_stats_kernel<<<dim3(16, n_img), 512, 0, (cudaStream_t)stream>>>(label_dev, w, h, n_img, stats_dev);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int sy_embed_device(const sy_scene* scenes_dev, const int* desc_dev, int n, int D, double sigma, int bf16, void* out_dev, void* stream) {
+  if (n <= 0) return 0;
+  sy_embed_kernel<<<n, 256, 0, (cudaStream_t)stream>>>(scenes_dev, desc_dev, n, D, sigma, bf16, out_dev);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int sy_nlab(void) { return SY_NLAB; }
+
+}  // extern "C"
