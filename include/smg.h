@@ -125,6 +125,9 @@ int smg_params_default(smg_params* p);
  * of unknown keys (0 = all known), or SMG_ERR_ARGS. */
 int smg_params_apply(smg_params* p, const char* kv);
 
+/* ObjectMap::setCloudParams (scenemap objmap.hpp:255-258): voxel > 0 and cap > 0 override. */
+int smg_params_set_cloud(smg_params* p, double voxel, int cap);
+
 /* Create M maps on device `dev`.  max_objects: object slots per map; emb_dim: embedding width
  * (<= 2048); max_w/max_h: largest frame; max_det: detections per frame (<= 64);
  * grid_w/grid_h and grid_x0/grid_y0: the fixed occupancy window in global cell indices.
@@ -187,6 +190,9 @@ int smg_get_assoc_all(smg_batch* b, uint32_t* obj_id);
 #define SMG_NUM_KERNELS 14
 int smg_timing_enable(smg_batch* b, int on);
 int smg_timing_read(smg_batch* b, double* ms, int64_t* n, const char** names);
+/* First failed self-check of a -DSMG_CHECKS build: (site, index, bound); all zero when none
+ * (always zero in the production build). */
+int smg_debug_check(smg_batch* b, uint64_t* out3);
 /* Device error word (0 = none) and a static description of the last host-side error. */
 int smg_error_word(smg_batch* b);
 const char* smg_last_error(void);

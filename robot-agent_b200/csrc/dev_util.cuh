@@ -10,6 +10,22 @@
 
 #define DEV __device__ __forceinline__
 
+// Self-checks (built with -DSMG_CHECKS): an index outside [0, n) records (site, index, bound) of
+// the first failure in smg_chk and the access is skipped.  Without SMG_CHECKS they compile away.
+__device__ unsigned long long smg_chk[3];
+#ifdef SMG_CHECKS
+__device__ __noinline__ bool smg_chk_fail(int site, long long i, long long n) {
+  if (atomicCAS(&smg_chk[0], 0ull, (unsigned long long)site) == 0ull) {
+    smg_chk[1] = (unsigned long long)i;
+    smg_chk[2] = (unsigned long long)n;
+  }
+  return false;
+}
+#define INB(i, n, site) (((long long)(i) >= 0 && (long long)(i) < (long long)(n)) ? true : smg_chk_fail(site, (long long)(i), (long long)(n)))
+#else
+#define INB(i, n, site) true
+#endif
+
 // ---------------------------------------------------------------- block primitives
 // All helpers assume blockDim.x is a multiple of 32 and <= 1024, and that every thread of the
 // block calls them (they contain __syncthreads).
@@ -123,7 +139,7 @@ DEV int block_excl_scan(int flag, int* total, BlockScratch& s) {
     if (lane >= o) x += y;
   }
   __syncthreads();
-  if (lane == 31) s.i[wid] = x;
+  if (lane == 31 && INB(wid, 33, 131)) s.i[wid] = x;
   __syncthreads();
   if (wid == 0) {
     int w = lane < nw ? s.i[lane] : 0;
@@ -163,6 +179,9 @@ DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& 
       const uint64_t key = d_ord(a[i]);
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
     }
+#ifdef SMG_CHECKS
+    if (threadIdx.x == 0 && (k < 0 || k >= n)) smg_chk_fail(130, k, n);
+#endif
     __syncthreads();
     if (threadIdx.x < 32) {
       const int lane = threadIdx.x;

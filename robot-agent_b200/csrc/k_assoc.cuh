@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
   if (!F.active || a >= R.n_obs) return;
   const smg_params& P = B.p;
   const int det = B.obs_list[(size_t)m * B.max_det + a];
+  if (!INB(det, B.max_det, 203)) return;
   ObsRec* O = &B.obs[(size_t)m * B.max_det + det];
   const bool has_z = F.emb != nullptr;
   for (int i = tid; i < B.D; i += blockDim.x) zs[i] = has_z ? emb_at(F.emb, F.emb_dtype, B.D, det, i) : 0.f;
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
       const double g = smax3(0.0, O->lo[k] - ob.hi[k], ob.lo[k] - O->hi[k]);
       g2 += g * g;
     }
+    if (!INB(b, B.O, 201) || !INB(slot, B.O, 202)) continue;
     if (g2 > gate2) {
       if (lane == 0) pp[b] = -1.0;
       continue;

@@ -98,7 +98,7 @@ DEV void cloud_trim(const Batch& B, size_t cs, const Work& W, int* hist, BlockSc
     const int k = i < n && (W.scr[i] > cut || (is_eq && eq_seen + peq >= eq_drop));
     int tot;
     const int pos = block_excl_scan(k, &tot, bs);
-    if (k) { W.t4[w + pos] = pts[i]; W.tc[w + pos] = col[i]; }
+    if (k && INB(w + pos, B.work_n, 404)) { W.t4[w + pos] = pts[i]; W.tc[w + pos] = col[i]; }
     w += tot;
     eq_seen += toteq;
   }
@@ -179,7 +179,7 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
     if (i < n) W.dst[i] = -1;
     if (last >= 0) {
       const int d = isnew ? base + added + pos : old;
-      if (d < B.cap) {
+      if (d < B.cap && INB(d, B.cap, 401) && INB(last, n, 402)) {
         const float x = (float)((double)xyz[3 * last] - sh_org[0]), y = (float)((double)xyz[3 * last + 1] - sh_org[1]),
                     z = (float)((double)xyz[3 * last + 2] - sh_org[2]);
         pts[d] = make_float4(x, y, z, __uint_as_float(sh_seq));
@@ -191,7 +191,7 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
   }
   __syncthreads();
   for (int i = tid; i < n; i += blockDim.x)
-    if (W.dst[i] >= 0) voxel_insert(B, cs, sh_vgen, W.keys[i], (uint32_t)W.dst[i]);
+    if (W.dst[i] >= 0 && INB(W.dst[i], B.cap, 403)) voxel_insert(B, cs, sh_vgen, W.keys[i], (uint32_t)W.dst[i]);
   __syncthreads();
   if (tid == 0) {
     C.n = base + added;
@@ -264,12 +264,16 @@ __global__ void __launch_bounds__(512) k_cloud_add(Batch B) {
   const MapRec& R = B.maps[m];
   const Work W = work_at(B, m, blockIdx.x);
   for (int j = blockIdx.x; j < R.n_targets; j += gridDim.x) {
+    if (!INB(j, B.O, 405)) break;
     const int slot = B.tgt_slot[(size_t)m * B.O + j];
+    if (!INB(slot, B.O, 406)) continue;
     const ObjRec& o = B.objs[oglob(B, m, slot)];
     const size_t cs = (size_t)m * B.O + o.cloud_slot;
     for (int e = 0; e < R.n_pts; ++e) {
+      if (!INB(e, B.max_det, 407)) break;
       const PtsRec& pr = B.ptsl[(size_t)m * B.max_det + e];
       if (pr.obj_id != o.id) continue;
+      if (!INB(pr.det, B.max_det, 408) || !INB(pr.n, B.pmax + 1, 409)) continue;
       const float* xyz = B.cxyz + ((size_t)m * B.max_det + pr.det) * 3 * B.pmax;
       cloud_add(B, m, cs, xyz, nullptr, pr.n, F.stamp, W, hist, bs);
     }

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   const int step = max(1, (int)llround(F.w / 160.0));
   const int gw = (F.w + step - 1) / step, gh = (F.h + step - 1) / step, ng = gw * gh;
   if (ng > B.scan_pmax) {
-    if (tid == 0) set_err(R, SMG_E_CAP_GRID);
+    if (tid == 0) { set_err(R, SMG_E_CAP_GRID); R->kf_inserted = 0; R->kf_changed = 0; }
     return;
   }
   float4* SP = B.sP + (size_t)m * B.scan_pmax;
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   }
   __syncthreads();
   for (int i = tid; i < MH_SLOTS; i += blockDim.x)
-    if (HKY[i] != INT64_MIN) CF[HF[i]] = 1;
+    if (HKY[i] != INT64_MIN && INB(HF[i], ng, 702)) CF[HF[i]] = 1;
   __syncthreads();
   // rank of each cell = number of cells whose first pixel comes earlier (ordered scan)
   int nrank = 0;
@@ -182,7 +182,8 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     const int64_t key = MK[c];
     if (key == INT64_MIN) continue;
     uint32_t h = (uint32_t)(((uint64_t)key * 0x9E3779B97F4A7C15ull) >> 50) & (MH_SLOTS - 1);
-    while (HKY[h] != key) h = (h + 1) & (MH_SLOTS - 1);
+    for (int probe = 0; probe < MH_SLOTS && HKY[h] != key; ++probe) h = (h + 1) & (MH_SLOTS - 1);
+    if (HKY[h] != key) { set_err(R, SMG_E_CAP_GRID); MK[c] = -1; continue; }
     const int r = HC[h];
     MK[c] = r < ncell ? r : -1;   // reuse: rank or -1
     if (r < ncell) atomicAdd(&CC[r], 1);
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     const long long r = MK[c];
     if (r < 0 || MK[c] == INT64_MIN) continue;
     const int slot = atomicAdd(&CO[r], 1);
-    CPX[slot] = c;
+    if (INB(slot, ng, 701)) CPX[slot] = c;
   }
   __syncthreads();
   float* OUT = B.sc_pts + (size_t)m * (2 * SMG_BINS_MAX + SMG_MATCH_CELLS) * 4;
@@ -245,7 +246,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     int th, tf;
     const int ph = block_excl_scan(ish, &th, bs);
     const int pf = block_excl_scan(isf, &tf, bs);
-    if (ish) { const float4 q = SP[pix]; HOUT[4 * (nh + ph)] = q.x; HOUT[4 * (nh + ph) + 1] = q.y; }
+    if (ish && INB(pix, ng, 705)) { const float4 q = SP[pix]; HOUT[4 * (nh + ph)] = q.x; HOUT[4 * (nh + ph) + 1] = q.y; }
     if (isf) {
       FOUT[4 * (nf + pf)] = T[3] + fr * B.bin_cos[k];
       FOUT[4 * (nf + pf) + 1] = T[7] + fr * B.bin_sin[k];
@@ -276,6 +277,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     sh_ins = R->kf_first || nudged || changed || R->kf_last_changed > 0 || R->kf_since >= P.still_every;
     R->kf_hits = P.dense ? ncell : nh;
     R->kf_inserted = sh_ins;
+    if (!sh_ins) R->kf_changed = 0;
     sh_n[0] = ncell; sh_n[1] = nh; sh_n[2] = nf;
   }
   __syncthreads();
@@ -331,6 +333,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
       for (;;) {
         const bool end = xx == x1 && yy == y1;
         if (end && !is_free) break;
+        if (!INB(xx - X0, GW, 703) || !INB(yy - Y0, GH, 704)) break;
         const size_t ci = (size_t)(yy - Y0) * GW + (xx - X0);
         const unsigned long long key = sk | 0x80000000ull | ((unsigned long long)r << 12) | (stepi & 0xfffu);
         if (pass == 0) {

@@ -44,7 +44,8 @@ DEV int absent_evidence_warp(const Batch& B, int m, const ObjRec& o, const Frame
   for (int s = lane; s < ns; s += 32) {
     double p[3];
     if (nc >= 8) {
-      const float4 q = pts[(size_t)s * stride];
+      if (!INB((size_t)s * stride, nc, 504)) continue;
+    const float4 q = pts[(size_t)s * stride];
       p[0] = C.org[0] + (double)q.x; p[1] = C.org[1] + (double)q.y; p[2] = C.org[2] + (double)q.z;
     } else {
       const int a = s / 9, b = (s / 3) % 3, c = s % 3;
@@ -126,8 +127,9 @@ DEV void erase_pos(const Batch& B, int m, int pos, bool keep_cloud) {
   int32_t* ord = B.order + (size_t)m * B.O;
   const int slot = ord[pos];
   const ObjRec& o = B.objs[oglob(B, m, slot)];
-  if (!keep_cloud) B.cfreel[(size_t)m * B.O + R->n_cfree++] = o.cloud_slot;
-  B.freel[(size_t)m * B.O + R->n_free++] = slot;
+  if (!INB(pos, R->n_obj, 501)) return;
+  if (!keep_cloud) { if (INB(R->n_cfree, B.O, 502)) B.cfreel[(size_t)m * B.O + R->n_cfree++] = o.cloud_slot; }
+  if (INB(R->n_free, B.O, 503)) B.freel[(size_t)m * B.O + R->n_free++] = slot;
   for (int i = pos + 1; i < R->n_obj; ++i) ord[i - 1] = ord[i];
   --R->n_obj;
 }
@@ -258,6 +260,7 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
     const ObjRec& no = B.objs[oglob(B, m, slot_at(B, m, ni))];
     for (int k = 0; k < 3; ++k) { mo.pos[k] = no.pos[k]; mo.ext[k] = no.ext[k]; mo.lo[k] = no.lo[k]; mo.hi[k] = no.hi[k]; }
     // m takes n's cloud (m.cloud = n.cloud; version = n.version + 1); m's old cloud slot is freed
+    if (mi < 0 || ni < 0 || !INB(R->n_cfree, B.O, 505)) continue;
     B.cfreel[(size_t)m * B.O + R->n_cfree++] = mo.cloud_slot;
     mo.cloud_slot = no.cloud_slot;
     ++B.clouds[(size_t)m * B.O + mo.cloud_slot].version;
@@ -301,6 +304,7 @@ __global__ void __launch_bounds__(256) k_struct(Batch B) {
     const size_t stp = (size_t)C.n / 800 > 1 ? (size_t)C.n / 800 : 1;
     const int n = (int)(((size_t)C.n + stp - 1) / stp);
     const float4* pts = B.cpts + cs * B.cap;
+    if (!INB(3 * n, 4 * B.work_n, 508)) continue;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       const float4 q = pts[(size_t)i * stp];
       Pt[3 * i] = (float)(C.org[0] + (double)q.x);
@@ -356,7 +360,7 @@ __global__ void k_prune(Batch B) {
     const int slot = slot_at(B, m, pos);
     bool seen = false;
     for (int q = 0; q < nt; ++q) seen = seen || B.tgt_slot[(size_t)m * B.O + q] == slot;
-    if (!seen) B.tgt_slot[(size_t)m * B.O + nt++] = slot;
+    if (!seen && INB(nt, B.O, 506)) B.tgt_slot[(size_t)m * B.O + nt++] = slot;
   }
   for (int b = 0; b < R->n_obj; ++b) {
     const int slot = slot_at(B, m, b);
@@ -365,7 +369,7 @@ __global__ void k_prune(Batch B) {
     if (C.cver == C.version || C.n == 0) continue;
     bool seen = false;
     for (int q = 0; q < nt; ++q) seen = seen || B.tgt_slot[(size_t)m * B.O + q] == slot;
-    if (!seen) B.tgt_slot[(size_t)m * B.O + nt++] = slot;
+    if (!seen && INB(nt, B.O, 507)) B.tgt_slot[(size_t)m * B.O + nt++] = slot;
   }
   R->n_targets = nt;
 }

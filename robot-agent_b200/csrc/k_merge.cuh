@@ -184,6 +184,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
     const int nb = Cb.n;
     const float4* pb = B.cpts + csb * B.cap;
     const uint32_t* colb = B.crgb + csb * B.cap;
+    if (!INB(3 * nb, 3 * B.max_det * B.pmax, 601)) continue;
     for (int i = tid; i < nb; i += blockDim.x) {
       const float4 p = pb[i];
       xyz[3 * i] = (float)(Cb.org[0] + (double)p.x);
@@ -230,6 +231,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
     __syncthreads();
     for (int v = 0; v < nkeep; ++v) {
       if (vsrc[v] != 1) continue;
+      if (!INB(vphys[v], B.topk + 1, 602) || !INB(dstp[v], B.topk + 1, 603)) continue;
       const uint16_t* src = B.views + (ogb * (B.topk + 1) + vphys[v]) * B.D;
       uint16_t* dst = B.views + (oga * (B.topk + 1) + dstp[v]) * B.D;
       for (int i = tid; i < B.D; i += blockDim.x) dst[i] = src[i];
@@ -262,7 +264,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
       a.wall_like = a.wall_like && b.wall_like;
       a.confirmed = a.confirmed || b.confirmed;
       ++R->st.n_merge;
-      erase_pos(B, m, find_pos(B, m, b.id), false);
+      { const int pe = find_pos(B, m, b.id); if (INB(pe, R->n_obj, 604)) erase_pos(B, m, pe, false); }
       push_event(B, m, t, a, 7, (1u << 24) | (uint32_t)R->n_evn++);
     }
     __syncthreads();

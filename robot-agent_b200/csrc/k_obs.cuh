@@ -15,6 +15,9 @@
 
 #define OBS_THREADS 512
 #define OBS_HASH 8192
+#define RANSAC_MAX 256
+// nsamp = ceil(n / max(1, n / min(n, 256))) <= 511, and cnt <= nsamp (objprob.cpp:135-158)
+#define NEED_N 512
 
 struct PlaneOut {
   int ok;
@@ -86,54 +89,76 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     __syncthreads();
     return;
   }
-  if (tid < 32) {
-    const int lane = tid;
+  // RANSAC (objprob.cpp:133-163).  The index triples do not depend on the inlier counts, so
+  // thread 0 draws all of them in the reference's splitmix sequence, every warp scores
+  // hypotheses in parallel, and thread 0 replays the sequential best/adaptive-stop logic.
+  __shared__ int h_id[RANSAC_MAX][3];
+  __shared__ int h_cnt[RANSAC_MAX];
+  __shared__ double h_pl[RANSAC_MAX][4];
+  const int iters = max_iters < RANSAC_MAX ? max_iters : RANSAC_MAX;
+  const int ns = n < 256 ? n : 256;
+  const int sstep = n / ns > 1 ? n / ns : 1;
+  const int nsamp = (n + sstep - 1) / sstep;
+  if (tid == 0) {
     uint64_t rs = seed ^ ((uint64_t)n << 32);
-    const int ns = n < 256 ? n : 256;
-    const int sstep = n / ns > 1 ? n / ns : 1;
-    const int nsamp = (n + sstep - 1) / sstep;
-    double best[4] = {0, 0, 1, 0};
-    int best_c = -1;
-    int need = max_iters > 1 ? max_iters : 1;
-    for (int it = 0; it < need && it < max_iters; ++it) {
-      int id0 = 0, id1 = 0, id2 = 0;
-      if (lane == 0) {
-        id0 = (int)(splitmix(rs) % (uint64_t)n);
-        do id1 = (int)(splitmix(rs) % (uint64_t)n); while (id1 == id0);
-        do id2 = (int)(splitmix(rs) % (uint64_t)n); while (id2 == id0 || id2 == id1);
-      }
-      id0 = __shfl_sync(0xffffffffu, id0, 0);
-      id1 = __shfl_sync(0xffffffffu, id1, 0);
-      id2 = __shfl_sync(0xffffffffu, id2, 0);
-      const float* a = xyz + 3 * id0;
-      const float* b = xyz + 3 * id1;
-      const float* c = xyz + 3 * id2;
+    for (int it = 0; it < iters; ++it) {
+      const int id0 = (int)(splitmix(rs) % (uint64_t)n);
+      int id1, id2;
+      do id1 = (int)(splitmix(rs) % (uint64_t)n); while (id1 == id0);
+      do id2 = (int)(splitmix(rs) % (uint64_t)n); while (id2 == id0 || id2 == id1);
+      h_id[it][0] = id0; h_id[it][1] = id1; h_id[it][2] = id2;
+    }
+  }
+  __syncthreads();
+  {
+    const int lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+    for (int it = wid; it < iters; it += nw) {
+      if (!INB(h_id[it][0], n, 105) || !INB(h_id[it][1], n, 105) || !INB(h_id[it][2], n, 105)) { if (lane == 0) h_cnt[it] = -1; continue; }
+      const float* a = xyz + 3 * h_id[it][0];
+      const float* b = xyz + 3 * h_id[it][1];
+      const float* c = xyz + 3 * h_id[it][2];
       const double u[3] = {(double)(b[0] - a[0]), (double)(b[1] - a[1]), (double)(b[2] - a[2])};
       const double v[3] = {(double)(c[0] - a[0]), (double)(c[1] - a[1]), (double)(c[2] - a[2])};
       double nn[3] = {u[1] * v[2] - u[2] * v[1], u[2] * v[0] - u[0] * v[2], u[0] * v[1] - u[1] * v[0]};
       const double L = sqrt(nn[0] * nn[0] + nn[1] * nn[1] + nn[2] * nn[2]);
-      if (L < 1e-6) continue;
+      if (L < 1e-6) {   // nearly collinear: the reference skips the iteration
+        if (lane == 0) h_cnt[it] = -1;
+        continue;
+      }
       for (int k = 0; k < 3; ++k) nn[k] /= L;
       const double d0 = -(nn[0] * (double)a[0] + nn[1] * (double)a[1] + nn[2] * (double)a[2]);
       int cnt = 0;
       for (int s = lane; s < nsamp; s += 32) {
         const int i = s * sstep;
+        if (!INB(i, n, 119)) break;
         cnt += fabs(nn[0] * (double)xyz[3 * i] + nn[1] * (double)xyz[3 * i + 1] + nn[2] * (double)xyz[3 * i + 2] + d0) <= tau;
       }
       cnt = warp_sum_i(cnt);
+      if (lane == 0) {
+        h_cnt[it] = cnt;
+        h_pl[it][0] = nn[0]; h_pl[it][1] = nn[1]; h_pl[it][2] = nn[2]; h_pl[it][3] = d0;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double best[4] = {0, 0, 1, 0};
+    int best_c = -1;
+    int need = max_iters > 1 ? max_iters : 1;
+    for (int it = 0; it < need && it < iters; ++it) {
+      const int cnt = h_cnt[it];
+      if (cnt < 0) continue;
       if (cnt > best_c) {
         best_c = cnt;
-        best[0] = nn[0]; best[1] = nn[1]; best[2] = nn[2]; best[3] = d0;
+        for (int k = 0; k < 4; ++k) best[k] = h_pl[it][k];
         const double w = (double)cnt / (double)nsamp;
         const double pw = w * w * w;
         if (pw > 0.999999) break;
-        if (pw > 1e-9) need = need_tab[nsamp * 257 + cnt];
+        if (pw > 1e-9 && INB(nsamp * NEED_N + cnt, NEED_N * NEED_N, 120)) need = need_tab[nsamp * NEED_N + cnt];
       }
     }
-    if (lane == 0) {
-      sh_bestc = best_c;
-      for (int k = 0; k < 4; ++k) sh_best[k] = best[k];
-    }
+    sh_bestc = best_c;
+    for (int k = 0; k < 4; ++k) sh_best[k] = best[k];
   }
   __syncthreads();
   if (sh_bestc < 3) {
@@ -210,6 +235,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
     if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) {
       const int q = atomicAdd(&sh_cnt, 1);
+      if (!INB(q, cap, 104)) continue;
       zs[q] = z;
       hsp[q] = (x - m0) * hc + (y - m1) * hs;
     }
@@ -236,13 +262,15 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
 // subsample (objmap.cpp:37-42) of v[0..n) into S (<= SMG_SUB values); returns its size
 DEV int subsample_to(const double* v, int n, double* S) {
   const int nS = n <= SMG_SUB ? n : SMG_SUB;
-  for (int i = threadIdx.x; i < nS; i += blockDim.x) S[i] = n <= SMG_SUB ? v[i] : v[(size_t)i * (size_t)n / SMG_SUB];
+  for (int i = threadIdx.x; i < nS; i += blockDim.x)
+    if (INB(i, SMG_SUB, 117) && INB(n <= SMG_SUB ? i : (size_t)i * (size_t)n / SMG_SUB, n, 118))
+      S[i] = n <= SMG_SUB ? v[i] : v[(size_t)i * (size_t)n / SMG_SUB];
   __syncthreads();
   return nS;
 }
 
 DEV bool lab_is(const uint16_t* label, int W, int H, int u, int v, uint16_t L) {
-  return u >= 0 && v >= 0 && u < W && v < H && label[(size_t)v * W + u] == L;
+  return u >= 0 && v >= 0 && u < W && v < H && INB((size_t)v * W + u, (size_t)W * H, 116) && label[(size_t)v * W + u] == L;
 }
 
 __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
@@ -262,6 +290,12 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
   }
   const smg_params& P = B.p;
   const int W = F.w, H = F.h;
+#ifdef SMG_CHECKS
+  if (F.depth == nullptr || F.label == nullptr || W <= 0 || H <= 0 || W > B.W || H > B.H || m >= B.M) {
+    if (tid == 0) smg_chk_fail(110, (long long)(size_t)F.depth, (long long)(size_t)F.label);
+    return;
+  }
+#endif
   const size_t slot = (size_t)m * B.max_det + k;
   double* X = B.px + slot * 4 * B.pmax;
   double* Y = X + B.pmax;
@@ -304,7 +338,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
       // mask cell (i, j) = pixel (u, v); 1-cell erosion; rows j < 1 or j >= MH-1 are skipped
       if (vv >= 1 && vv < H - 1 && lab_is(F.label, W, H, uu, vv, L) && lab_is(F.label, W, H, uu - 1, vv, L) &&
           lab_is(F.label, W, H, uu + 1, vv, L) && lab_is(F.label, W, H, uu, vv - 1, L) && lab_is(F.label, W, H, uu, vv + 1, L)) {
-        const float z = F.depth[(size_t)vv * W + uu];
+        const float z = INB((size_t)vv * W + uu, (size_t)W * H, 111) ? F.depth[(size_t)vv * W + uu] : 0.f;
         if (z > P.zmin && z < P.zmax) {
           const double xc = (double)(((float)uu - F.cx) / F.fx * z), yc = (double)(((float)vv - F.cy) / F.fy * z);
           const double zd = (double)z;
@@ -318,7 +352,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
     }
     int tot;
     const int pos = block_excl_scan(ok, &tot, bs);
-    if (ok) {
+    if (ok && INB(n + pos, B.pmax, 101)) {
       X[n + pos] = px; Y[n + pos] = py; Z[n + pos] = pz; ZC[n + pos] = zz;
       PU[n + pos] = uu; PV[n + pos] = vv;
     }
@@ -349,7 +383,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
     const int i = c0 + tid;
     int keep = 0;
     if (i < n) {
-      keep = !(fabs(ZC[i] - zmed) > band);
+      keep = INB(i, B.pmax, 112) && !(fabs(ZC[i] - zmed) > band);
       if (keep) {
         const double x = X[i], y = Y[i], z = Z[i];
         const double d0 = (x - E0[0]) * (x - E0[0]) + (y - E0[1]) * (y - E0[1]) + (z - E0[2]) * (z - E0[2]);
@@ -370,7 +404,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
     }
     int tot;
     const int pos = block_excl_scan(keep, &tot, bs);
-    if (keep) { XK[w + pos] = X[i]; YK[w + pos] = Y[i]; ZK[w + pos] = Z[i]; }
+    if (keep && INB(w + pos, B.pmax, 102)) { XK[w + pos] = X[i]; YK[w + pos] = Y[i]; ZK[w + pos] = Z[i]; }
     w += tot;
   }
   const int near_hand = block_sum_i(near_local, bs);
@@ -380,7 +414,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
   for (int c0 = 0; c0 < n; c0 += blockDim.x) {
     const int i = c0 + tid;
     int emit = 0;
-    if (i < n && !(fabs(ZC[i] - zmed) > band)) {
+    if (i < n && INB(i, B.pmax, 113) && !(fabs(ZC[i] - zmed) > band)) {
       const double x = X[i], y = Y[i], z = Z[i];
       const double d0 = (x - E0[0]) * (x - E0[0]) + (y - E0[1]) * (y - E0[1]) + (z - E0[2]) * (z - E0[2]);
       const double d1 = (x - E1[0]) * (x - E1[0]) + (y - E1[1]) * (y - E1[1]) + (z - E1[2]) * (z - E1[2]);
@@ -390,6 +424,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
         const uint64_t key = voxel_key((float)x, (float)y, (float)z, B.inv_vox);
         uint32_t h = hmix(key) & (OBS_HASH - 1);
         for (int probe = 0; probe < OBS_HASH; ++probe) {
+          if (!INB(h, OBS_HASH, 114)) break;
           if (hkey[h] == key) { emit = hidx[h] == (uint32_t)i; break; }
           h = (h + 1) & (OBS_HASH - 1);
         }
@@ -397,7 +432,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
     }
     int tot;
     const int pos = block_excl_scan(emit, &tot, bs);
-    if (emit) {
+    if (emit && INB(nc + pos, B.pmax, 103)) {
       CX[3 * (nc + pos)] = (float)X[i];
       CX[3 * (nc + pos) + 1] = (float)Y[i];
       CX[3 * (nc + pos) + 2] = (float)Z[i];
@@ -449,7 +484,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
   }
   // 5. plane fit of the cloud candidates (apObsStructural, objmap.cpp:565-575)
   double c0s = 0, c1s = 0, c2s = 0;
-  for (int i = tid; i < nc; i += blockDim.x) { c0s += CX[3 * i]; c1s += CX[3 * i + 1]; c2s += CX[3 * i + 2]; }
+  for (int i = tid; i < nc && INB(3 * i + 2, 3 * B.pmax, 115); i += blockDim.x) { c0s += CX[3 * i]; c1s += CX[3 * i + 1]; c2s += CX[3 * i + 2]; }
   const double cen0 = block_sum_d(c0s, bs), cen1 = block_sum_d(c1s, bs), cen2 = block_sum_d(c2s, bs);
   if (nc >= 8) {
     const double dc = hypot3(cen0 / nc - T[3], cen1 / nc - T[7], cen2 / nc - T[11]);

@@ -78,7 +78,7 @@ DEV void ap_add_view(const Batch& B, size_t og, const float* z_sh, double kappa,
     sh_k = k;
     // free physical view slot: the one of 0..topk not referenced by the current views
     int used = 0;
-    for (int v = 0; v < o.n_views; ++v) used |= 1 << o.view_slot[v];
+    for (int v = 0; v < o.n_views; ++v) if (INB(o.view_slot[v], B.topk + 1, 301)) used |= 1 << o.view_slot[v];
     int f = 0;
     while (used & (1 << f)) ++f;
     sh_free = f;
@@ -118,6 +118,7 @@ DEV void ap_add_view(const Batch& B, size_t og, const float* z_sh, double kappa,
 DEV int new_object_slot(const Batch& B, int m, int* cslot) {
   MapRec* R = &B.maps[m];
   if (R->n_free <= 0 || R->n_cfree <= 0 || R->n_obj >= B.O) { set_err(R, SMG_E_CAP_OBJ); return -1; }
+  if (!INB(R->n_free - 1, B.O, 303) || !INB(R->n_cfree - 1, B.O, 303)) return -1;
   const int slot = B.freel[(size_t)m * B.O + --R->n_free];
   *cslot = B.cfreel[(size_t)m * B.O + --R->n_cfree];
   B.order[(size_t)m * B.O + R->n_obj++] = slot;
@@ -190,7 +191,7 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
       as.area_px = (float)o.n * o.sk * o.sk;
       as.depth_med = (float)o.zmed;
       sh_act = 0;
-      if (o.obs_to >= 0) {
+      if (o.obs_to >= 0 && INB(o.obs_to, R->n_obj, 302)) {
         sh_act = 1;
         sh_slot = slot_at(B, m, o.obs_to);
         as.obj_id = B.objs[oglob(B, m, sh_slot)].id;

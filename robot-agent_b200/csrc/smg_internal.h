@@ -237,7 +237,7 @@ typedef struct {
   int64_t* vkey;         // [M*view_slots], INT64_MIN = empty
   double* vfirst;        // [M*view_slots*5]
   // RANSAC adaptive iteration table need[nsamp][cnt] (objprob.cpp:161), host libm
-  int32_t* need_tab;     // [257*257]
+  int32_t* need_tab;     // [NEED_N*NEED_N]
   // occupancy grid
   int16_t* gL;           // [M*gw*gh]
   int8_t* gc8;

@@ -13,7 +13,7 @@ import os
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(os.path.dirname(_HERE), "libsmg.so")
+LIB_PATH = os.environ.get("SMG_LIB") or os.path.join(os.path.dirname(_HERE), "libsmg.so")
 
 SMG_MEM_DEVICE, SMG_MEM_HOST = 0, 1
 SMG_EMB_F32, SMG_EMB_BF16 = 0, 1
@@ -53,6 +53,7 @@ def lib():
         L.smg_params_size.restype = C.c_int
         L.smg_params_default.argtypes = [vp]
         L.smg_params_apply.argtypes = [vp, C.c_char_p]
+        L.smg_params_set_cloud.argtypes = [vp, C.c_double, C.c_int]
         L.smg_create.argtypes = [vp] + [C.c_int] * 11 + [P(vp)]
         L.smg_destroy.argtypes = [vp]
         L.smg_push_frames.argtypes = [vp, P(SmgFrame), C.c_int, C.c_int, vp]
@@ -67,6 +68,7 @@ def lib():
         L.smg_error_word.argtypes = [vp]
         L.smg_last_error.restype = C.c_char_p
         L.smg_get_assoc_all.argtypes = [vp, vp]
+        L.smg_debug_check.argtypes = [vp, vp]
         L.smg_timing_enable.argtypes = [vp, C.c_int]
         L.smg_timing_read.argtypes = [vp, vp, vp, vp]
         L.smg_kernel_launches.restype = C.c_int64
@@ -75,10 +77,10 @@ def lib():
     return _lib
 
 
-EXPORTED = ["smg_params_size", "smg_params_default", "smg_params_apply", "smg_create", "smg_destroy", "smg_push_frames",
+EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "smg_params_apply", "smg_create", "smg_destroy", "smg_push_frames",
             "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
             "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
-            "smg_kernel_launches", "smg_get_assoc_all", "smg_timing_enable", "smg_timing_read"]
+            "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read"]
 
 NUM_KERNELS = 14
 
@@ -112,9 +114,12 @@ class Params:
 
 class Batch:
     def __init__(self, n_maps: int, max_objects: int = 256, emb_dim: int = 1152, max_w: int = 640, max_h: int = 480,
-                 max_det: int = 32, grid=(512, 512, -256 + 60, -256 + 50), params: Params | None = None, dev: int = 0):
+                 max_det: int = 32, grid=(512, 512, -256 + 60, -256 + 50), params: Params | None = None, dev: int = 0,
+                 cloud_cap: int | None = None):
         L = lib()
         self.params = params or Params()
+        if cloud_cap is not None:   # ObjectMap::setCloudParams (objmap.hpp:255-258)
+            _check(L.smg_params_set_cloud(self.params.buf, 0.0, int(cloud_cap)), "smg_params_set_cloud")
         self.n_maps, self.max_objects, self.D, self.max_det = n_maps, max_objects, emb_dim, max_det
         self.grid = grid
         h = C.c_void_p()
@@ -263,6 +268,11 @@ class Batch:
         names = (C.c_char_p * NUM_KERNELS)()
         _check(lib().smg_timing_read(self.h, _ptr(ms), _ptr(n), names), "smg_timing_read")
         return {names[k].decode(): (float(ms[k]), int(n[k])) for k in range(NUM_KERNELS)}
+
+    def debug_check(self):
+        out = np.zeros(3, np.uint64)
+        _check(lib().smg_debug_check(self.h, _ptr(out)), "smg_debug_check")
+        return [int(v) for v in out]
 
     def error_word(self) -> int:
         return _check(lib().smg_error_word(self.h), "smg_error_word")

@@ -57,3 +57,24 @@ def test_parity_config0_full():
     _need()
     n = int(os.environ.get("SMG_PARITY_FRAMES", "300"))
     _run(n, 1234, bf16=False, deep_every=25)
+
+
+def test_parity_batch_maps():
+    """Several maps in one batch: each map must match its own reference instance."""
+    _need()
+    from oracle import ref
+    from scenemap_b200 import smg, synth
+    M, N, D = 4, 25, 1152
+    gens = [synth.BoxRoom(seed=synth.map_seed(4242, i), n_frames=N, D=D, bf16=True) for i in range(M)]
+    refs = [ref.RefMap() for _ in range(M)]
+    B = smg.Batch(M, max_objects=128, emb_dim=D, max_det=32)
+    for f in range(N):
+        frs = [g.frame(f) for g in gens]
+        for R, fr in zip(refs, frs):
+            R.frame(fr)
+        B.push(frs, smg.SMG_MEM_HOST, smg.SMG_EMB_BF16)
+        for m in range(M):
+            errs = compare_frame(refs[m], B, m, D, deep=(f % 8 == 0 or f == N - 1))
+            assert not errs, f"map {m} frame {f}: " + "\n".join(errs[:20])
+    assert B.error_word() == 0
+    B.close()
