@@ -128,6 +128,26 @@ DEV double block_min_d(double v, BlockScratch& s) {
   return r;
 }
 
+// N sums in one reduction (deterministic tree); buf: N*32 shared doubles.
+template <int N>
+DEV void block_sum_multi(double (&v)[N], double* buf) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int k = 0; k < N; ++k) v[k] = warp_sum_d(v[k]);
+  __syncthreads();
+  if (lane == 0)
+    for (int k = 0; k < N; ++k) buf[k * 32 + wid] = v[k];
+  __syncthreads();
+  if (wid == 0)
+    for (int k = 0; k < N; ++k) {
+      double r = lane < nw ? buf[k * 32 + lane] : 0.0;
+      r = warp_sum_d(r);
+      if (lane == 0) buf[k * 32] = r;
+    }
+  __syncthreads();
+  for (int k = 0; k < N; ++k) v[k] = buf[k * 32];
+  __syncthreads();
+}
+
 // Exclusive scan of a 0/1 (or small int) flag across the block; returns the prefix for this
 // thread and writes the block total to *total.  Order = thread order (used for ordered
 // stream compaction: chunk c covers elements c*blockDim .. c*blockDim+blockDim-1).
@@ -211,6 +231,60 @@ DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& 
     mask |= 0xffull << shift;
   }
   return d_unord(prefix);
+}
+
+// Up to SEL_MAXQ exact selections in one set of 8 radix passes: value q = the k[q]-th smallest
+// of a[q][0..n[q]).  hist: SEL_MAXQ*256 ints (shared).  All threads must call it.
+#define SEL_MAXQ 9
+DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s) {
+  __shared__ unsigned long long sh_prefix[SEL_MAXQ];
+  __shared__ int sh_k[SEL_MAXQ];
+#ifdef SMG_CHECKS
+  if (threadIdx.x == 0 && (nq > SEL_MAXQ || nq > (int)(blockDim.x >> 5))) smg_chk_fail(132, nq, SEL_MAXQ);
+#endif
+  if (threadIdx.x < nq) { sh_prefix[threadIdx.x] = 0; sh_k[threadIdx.x] = kq[threadIdx.x]; }
+  uint64_t mask = 0;
+  for (int pass = 0; pass < 8; ++pass) {
+    const int shift = 56 - 8 * pass;
+    for (int i = threadIdx.x; i < nq * 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int q = 0; q < nq; ++q) {
+      const uint64_t pre = sh_prefix[q];
+      const double* aq = a[q];
+      for (int i = threadIdx.x; i < n[q]; i += blockDim.x) {
+        const uint64_t key = d_ord(aq[i]);
+        if ((key & mask) == pre) atomicAdd(&hist[q * 256 + ((key >> shift) & 255u)], 1);
+      }
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
+    if (wq < nq) {
+      const int* hq = hist + wq * 256;
+      int c[8], tot = 0;
+      for (int j = 0; j < 8; ++j) { c[j] = hq[lane * 8 + j]; tot += c[j]; }
+      int incl = tot;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int excl = incl - tot;
+      const int k = sh_k[wq];
+      if (k >= excl && k < incl) {
+        int kk = k - excl, b = 0;
+        for (int j = 0; j < 8; ++j) {
+          if (kk < c[j]) { b = j; break; }
+          kk -= c[j];
+        }
+        sh_prefix[wq] |= (unsigned long long)(lane * 8 + b) << shift;
+        sh_k[wq] = kk;
+      }
+    }
+    __syncthreads();
+    mask |= 0xffull << shift;
+  }
+  if (threadIdx.x < nq) out[threadIdx.x] = d_unord(sh_prefix[threadIdx.x]);
+  __syncthreads();
+  (void)s;
 }
 
 // ---------------------------------------------------------------- hashing / keys

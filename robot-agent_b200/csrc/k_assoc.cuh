@@ -42,10 +42,49 @@ DEV int contact_hits_warp(const Batch& B, size_t cs, const float* sp, int n, dou
     const long long a = (long long)floor((double)sp[3 * i] * inv), b = (long long)floor((double)sp[3 * i + 1] * inv),
                     c = (long long)floor((double)sp[3 * i + 2] * inv);
     if (a < C.clo[0] - 1 || a > C.chi[0] + 1 || b < C.clo[1] - 1 || b > C.chi[1] + 1 || c < C.clo[2] - 1 || c > C.chi[2] + 1) continue;
+    if (C.cb_ok) {   // dilated bitset: the cell itself carries the 27-neighbourhood
+      const uint32_t* D = B.cbits + cs * 2 * CB_WORDS + CB_WORDS;
+      const int x = (int)(a - (C.clo[0] - 1)), y = (int)(b - (C.clo[1] - 1)), z = (int)(c - (C.clo[2] - 1));
+      const size_t w = ((size_t)z * C.cb_dy + y) * C.cb_wpr + (x >> 5);
+      if (!INB(w, CB_WORDS, 210)) continue;
+      hit += (D[w] >> (x & 31)) & 1u;
+      continue;
+    }
     bool h = false;
     for (int dx = -1; dx <= 1 && !h; ++dx)
       for (int dy = -1; dy <= 1 && !h; ++dy)
         for (int dz = -1; dz <= 1 && !h; ++dz) h = contact_has(B, cs, C.cgen, cell_key3(a + dx, b + dy, c + dz));
+    hit += h;
+  }
+  return warp_sum_i(hit);
+}
+
+// apContact with the sample taken on the fly: every stp-th point of cloud `css` (map frame,
+// float(org + p), objmap.cpp:1107-1114) against the contact cells of cloud `cst`.  Warp-level.
+DEV int contact_hits_cloud_warp(const Batch& B, size_t cst, size_t css, int stp, int n, double cell) {
+  const CloudRec& C = B.clouds[cst];
+  const CloudRec& S = B.clouds[css];
+  if (n <= 0 || C.cn <= 0) return 0;
+  const double inv = 1.0 / cell;
+  const float4* pts = B.cpts + css * B.cap;
+  const uint32_t* Dbits = B.cbits + cst * 2 * CB_WORDS + CB_WORDS;
+  int hit = 0;
+  for (int q = threadIdx.x & 31; q < n; q += 32) {
+    const float4 p = pts[(size_t)q * stp];
+    const float x = (float)(S.org[0] + (double)p.x), y = (float)(S.org[1] + (double)p.y), z = (float)(S.org[2] + (double)p.z);
+    const long long a = (long long)floor((double)x * inv), b = (long long)floor((double)y * inv), c = (long long)floor((double)z * inv);
+    if (a < C.clo[0] - 1 || a > C.chi[0] + 1 || b < C.clo[1] - 1 || b > C.chi[1] + 1 || c < C.clo[2] - 1 || c > C.chi[2] + 1) continue;
+    if (C.cb_ok) {
+      const int xi = (int)(a - (C.clo[0] - 1)), yi = (int)(b - (C.clo[1] - 1)), zi = (int)(c - (C.clo[2] - 1));
+      const size_t w = ((size_t)zi * C.cb_dy + yi) * C.cb_wpr + (xi >> 5);
+      if (!INB(w, CB_WORDS, 211)) continue;
+      hit += (Dbits[w] >> (xi & 31)) & 1u;
+      continue;
+    }
+    bool h = false;
+    for (int dx = -1; dx <= 1 && !h; ++dx)
+      for (int dy = -1; dy <= 1 && !h; ++dy)
+        for (int dz = -1; dz <= 1 && !h; ++dz) h = contact_has(B, cst, C.cgen, cell_key3(a + dx, b + dy, c + dz));
     hit += h;
   }
   return warp_sum_i(hit);
@@ -56,23 +95,47 @@ DEV const uint16_t* view_of(const Batch& B, size_t og, int phys) { return B.view
 
 // apCosMax of object o against the fp32 vector z (shared or global), warp-level: the fragment
 // mean direction r_frag/|r_frag| and each stored fp16 view; returns the max on every lane.
-DEV double cos_max_warp(const Batch& B, size_t og, const ObjRec& o, const float* z) {
-  const int lane = threadIdx.x & 31, D = B.D;
-  double best = -1;
-  if (o.nrm_frag > 0) {
-    const float* r = rfrag_of(B, og);
-    double dot = 0;
-    for (int i = lane; i < D; i += 32) dot += (double)r[i] * (double)z[i];
-    dot = warp_sum_d(dot);
-    best = smax(best, dot / sqrt(o.nrm_frag));
+// Every product float*float (or fp16*float) is exact in double; the sums are warp trees.
+// When D is a multiple of 128 each lane streams float4 / 4 x fp16 chunks (more loads in flight).
+DEV double dot_f32_warp(const float* a, const float* z, int D) {
+  const int lane = threadIdx.x & 31;
+  double dot = 0;
+  if ((D & 127) == 0 && ((((uintptr_t)a) | ((uintptr_t)z)) & 15) == 0) {
+    const float4* a4 = (const float4*)a;
+    const float4* z4 = (const float4*)z;
+#pragma unroll 3
+    for (int i = lane; i < D / 4; i += 32) {
+      const float4 x = a4[i], y = z4[i];
+      dot += (double)x.x * (double)y.x + (double)x.y * (double)y.y + (double)x.z * (double)y.z + (double)x.w * (double)y.w;
+    }
+  } else {
+    for (int i = lane; i < D; i += 32) dot += (double)a[i] * (double)z[i];
   }
-  for (int v = 0; v < o.n_views; ++v) {
-    const uint16_t* q = view_of(B, og, o.view_slot[v]);
-    double dot = 0;
+  return warp_sum_d(dot);
+}
+DEV double dot_f16_warp(const uint16_t* q, const float* z, int D) {
+  const int lane = threadIdx.x & 31;
+  double dot = 0;
+  if ((D & 127) == 0 && ((((uintptr_t)q) & 7) | (((uintptr_t)z) & 15)) == 0) {
+    const uint2* q4 = (const uint2*)q;
+    const float4* z4 = (const float4*)z;
+#pragma unroll 3
+    for (int i = lane; i < D / 4; i += 32) {
+      const uint2 h = q4[i];
+      const float4 y = z4[i];
+      dot += (double)ref_h2f((uint16_t)(h.x & 0xffffu)) * (double)y.x + (double)ref_h2f((uint16_t)(h.x >> 16)) * (double)y.y +
+             (double)ref_h2f((uint16_t)(h.y & 0xffffu)) * (double)y.z + (double)ref_h2f((uint16_t)(h.y >> 16)) * (double)y.w;
+    }
+  } else {
     for (int i = lane; i < D; i += 32) dot += (double)ref_h2f(q[i]) * (double)z[i];
-    dot = warp_sum_d(dot);
-    best = smax(best, dot);
   }
+  return warp_sum_d(dot);
+}
+DEV double cos_max_warp(const Batch& B, size_t og, const ObjRec& o, const float* z) {
+  const int D = B.D;
+  double best = -1;
+  if (o.nrm_frag > 0) best = smax(best, dot_f32_warp(rfrag_of(B, og), z, D) / sqrt(o.nrm_frag));
+  for (int v = 0; v < o.n_views; ++v) best = smax(best, dot_f16_warp(view_of(B, og, o.view_slot[v]), z, D));
   return best;
 }
 
@@ -119,6 +182,15 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
   __syncthreads();
   const int nobj = R.n_obj;
   const int lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  // frame-grouping dot products dot(z_b, z_a) with the later observations b (objmap.cpp:992)
+  if (has_z)
+    for (int b2 = a + 1 + wid; b2 < R.n_obs; b2 += nw) {
+      const int det2 = B.obs_list[(size_t)m * B.max_det + b2];
+      double dot = 0;
+      for (int i = lane; i < B.D; i += 32) dot += (double)emb_at(F.emb, F.emb_dtype, B.D, det2, i) * (double)zs[i];
+      dot = warp_sum_d(dot);
+      if (lane == 0) B.gdot[((size_t)m * B.max_det + a) * B.max_det + b2] = dot;
+    }
   const double gate2 = P.gate * P.gate;
   for (int b = wid; b < nobj; b += nw) {
     const int slot = slot_at(B, m, b);

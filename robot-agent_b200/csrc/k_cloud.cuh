@@ -207,47 +207,101 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
 }
 
 // apBuildContact over the cloud's map-frame points float(org + p) (objmap.cpp:1090-1103).
-// Keys are a set: a racing duplicate of one key only costs a slot.
+// Two representations of the same cell set: a dilated occupancy bitset over the cell box
+// [lo-1, hi+1] (bit = some cloud cell within the 27-neighbourhood, so a contact test is one bit)
+// when the box fits CB_WORDS words, else a generation-tagged hash set (racing duplicates of one
+// key only cost a slot).
 DEV void contact_rebuild(const Batch& B, size_t cs, BlockScratch& bs) {
   CloudRec& C = B.clouds[cs];
-  __shared__ uint32_t sh_gen;
-  if (threadIdx.x == 0) sh_gen = ++C.cgen;
-  __syncthreads();
-  const uint32_t gen = sh_gen;
   const int n = C.n;
   const double inv = 1.0 / B.p.contact_cell;
   const float4* pts = B.cpts + cs * B.cap;
-  uint64_t* K = B.ckey + cs * B.HCC;
-  uint32_t* G = B.cgen + cs * B.HCC;
-  double lo[3] = {1e300, 1e300, 1e300}, hi[3] = {-1e300, -1e300, -1e300};
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  auto cell = [&](int i, long long c[3]) {
     const float4 p = pts[i];
     const float q[3] = {(float)(C.org[0] + (double)p.x), (float)(C.org[1] + (double)p.y), (float)(C.org[2] + (double)p.z)};
+    for (int k = 0; k < 3; ++k) c[k] = (long long)floor((double)q[k] * inv);
+  };
+  double lo[3] = {1e300, 1e300, 1e300}, hi[3] = {-1e300, -1e300, -1e300};
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
     long long c[3];
-    for (int k = 0; k < 3; ++k) {
-      c[k] = (long long)floor((double)q[k] * inv);
-      lo[k] = fmin(lo[k], (double)c[k]);
-      hi[k] = fmax(hi[k], (double)c[k]);
-    }
-    const uint64_t key = cell_key3(c[0], c[1], c[2]);
-    uint32_t h = hmix(key) & (uint32_t)(B.HCC - 1);
-    for (int probe = 0; probe < B.HCC; ++probe) {
-      const uint32_t g = G[h];
-      if (g == gen) {
-        if (K[h] == key) break;
-      } else if (atomicCAS(&G[h], g, gen) == g) {
-        K[h] = key;
-        break;
-      } else {
-        continue;   // lost the slot to another writer: look at it again
-      }
-      h = (h + 1) & (uint32_t)(B.HCC - 1);
-    }
+    cell(i, c);
+    for (int k = 0; k < 3; ++k) { lo[k] = fmin(lo[k], (double)c[k]); hi[k] = fmax(hi[k], (double)c[k]); }
   }
+  long long L[3], H[3];
   for (int k = 0; k < 3; ++k) {
-    const double l = block_min_d(lo[k], bs), u = block_max_d(hi[k], bs);
-    if (threadIdx.x == 0 && n > 0) { C.clo[k] = (long long)l; C.chi[k] = (long long)u; }
+    L[k] = (long long)block_min_d(lo[k], bs);
+    H[k] = (long long)block_max_d(hi[k], bs);
   }
+  const long long dx = H[0] - L[0] + 3, dy = H[1] - L[1] + 3, dz = H[2] - L[2] + 3;
+  const long long wpr = (dx + 31) / 32;
+  const bool fits = n > 0 && wpr * dy * dz <= CB_WORDS;
+  __shared__ uint32_t sh_gen;
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < 3; ++k) { C.clo[k] = n > 0 ? L[k] : 0; C.chi[k] = n > 0 ? H[k] : -1; }
+    C.cb_ok = fits;
+    C.cb_dy = (int)dy;
+    C.cb_dz = (int)dz;
+    C.cb_wpr = (int)wpr;
+    sh_gen = fits ? C.cgen : ++C.cgen;
+  }
+  __syncthreads();
+  if (fits) {
+    uint32_t* O = B.cbits + cs * 2 * CB_WORDS;
+    uint32_t* D = O + CB_WORDS;
+    const int words = (int)(wpr * dy * dz);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) { O[i] = 0; D[i] = 0; }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      long long c[3];
+      cell(i, c);
+      const int x = (int)(c[0] - L[0] + 1), y = (int)(c[1] - L[1] + 1), z = (int)(c[2] - L[2] + 1);
+      const size_t w = ((size_t)z * dy + y) * wpr + (x >> 5);
+      if (INB(w, (size_t)words, 420)) atomicOr(&O[w], 1u << (x & 31));
+    }
+    __syncthreads();
+    // dilate along x (with carries across words), then y, then z
+    for (int i = threadIdx.x; i < words; i += blockDim.x) {
+      const int wx = (int)(i % wpr);
+      const uint32_t w = O[i];
+      const uint32_t prev = wx > 0 ? O[i - 1] : 0u, next = wx + 1 < wpr ? O[i + 1] : 0u;
+      D[i] = w | (w << 1) | (w >> 1) | (prev >> 31) | (next << 31);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < words; i += blockDim.x) {
+      const long long row = i / wpr, y = row % dy;
+      const uint32_t up = y > 0 ? D[i - wpr] : 0u, dn = y + 1 < dy ? D[i + wpr] : 0u;
+      O[i] = D[i] | up | dn;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < words; i += blockDim.x) {
+      const long long z = i / (wpr * dy);
+      const uint32_t below = z > 0 ? O[i - wpr * dy] : 0u, above = z + 1 < dz ? O[i + wpr * dy] : 0u;
+      D[i] = O[i] | below | above;
+    }
+  } else {
+    const uint32_t gen = sh_gen;
+    uint64_t* K = B.ckey + cs * B.HCC;
+    uint32_t* G = B.cgen + cs * B.HCC;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      long long c[3];
+      cell(i, c);
+      const uint64_t key = cell_key3(c[0], c[1], c[2]);
+      uint32_t h = hmix(key) & (uint32_t)(B.HCC - 1);
+      for (int probe = 0; probe < B.HCC; ++probe) {
+        const uint32_t g = G[h];
+        if (g == gen) {
+          if (K[h] == key) break;
+        } else if (atomicCAS(&G[h], g, gen) == g) {
+          K[h] = key;
+          break;
+        } else {
+          continue;   // lost the slot to another writer: look at it again
+        }
+        h = (h + 1) & (uint32_t)(B.HCC - 1);
+      }
+    }
+  }
+  __syncthreads();
   if (threadIdx.x == 0) { C.cn = n; C.cver = C.version; }
   __syncthreads();
 }

@@ -152,6 +152,7 @@ DEV void remap_id(const Batch& B, int m, uint32_t from, uint32_t to) {
 }
 
 #define RELINK_MAXC 256
+#define RELINK_STAGE 1024
 // relink (objmap.cpp:321-385), per map: candidate pairs pass the scalar tests, a warp per pair
 // evaluates the embedding cosine of n's mean direction against m, then pairs are applied nearest
 // first.  Also emits the cloud-candidate list of the update (objmap.cpp:1010-1019) beforehand.
@@ -161,8 +162,12 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
   __shared__ int np_;
   __shared__ double pd_[RELINK_MAXC];
   __shared__ uint32_t pm_[RELINK_MAXC], pn_[RELINK_MAXC];
+  __shared__ int s_state[RELINK_STAGE], s_nobs[RELINK_STAGE], s_cls[RELINK_STAGE];
+  __shared__ unsigned char s_flags[RELINK_STAGE];
+  __shared__ double s_first[RELINK_STAGE], s_last[RELINK_STAGE];
   extern __shared__ unsigned char smem_raw[];
-  float* mu = (float*)smem_raw;   // D per warp
+  double* s_pos = (double*)smem_raw;   // 3 per object
+  float* mu = (float*)(s_pos + 3 * RELINK_STAGE);   // D per warp
   const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
@@ -183,24 +188,40 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
       pr.n = nc;
     }
     R->n_pts = e;
-    // scalar tests of the relink candidates
+  }
+  // stage the scalars of the relink tests (objmap.cpp:323-346) in shared memory
+  const int nobj = R->n_obj;
+  const bool staged = nobj <= RELINK_STAGE;
+  for (int i = tid; i < nobj && staged; i += blockDim.x) {
+    const ObjRec& o = obj_at(B, m, i);
+    s_state[i] = o.state;
+    s_flags[i] = (o.appeared ? 1 : 0) | (o.confirmed ? 2 : 0) | (o.moved ? 4 : 0);
+    s_nobs[i] = (int)o.n_obs;
+    s_cls[i] = o.cls;
+    s_first[i] = o.first_seen;
+    s_last[i] = o.last_seen;
+    for (int k = 0; k < 3; ++k) s_pos[3 * i + k] = o.pos[k];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    if (!staged) set_err(R, SMG_E_CAP_OBJ);
+    // scalar tests of the relink candidates (a pair needs a gone object m)
     cn_ = 0;
-    for (int i = 0; i < R->n_obj; ++i) {
-      const ObjRec& n = obj_at(B, m, i);
-      if (!n.appeared || !n.confirmed || n.state == 1 || (int)n.n_obs < P.link_min_obs) continue;
-      if (t - n.first_seen > P.link_window_s) continue;
-      for (int j = 0; j < R->n_obj; ++j) {
-        const ObjRec& mm = obj_at(B, m, j);
-        if (j == i || mm.state != 1 || !mm.confirmed || (!mm.moved && (int)mm.n_obs < P.spurious_obs)) continue;
-        if (!(n.first_seen > mm.last_seen)) continue;
-        const double d = dist3(n.pos, mm.pos);
-        if (d > smin(P.link_max_d, P.link_d0 + P.link_v * (n.first_seen - mm.last_seen))) continue;
+    bool any_gone = false;
+    for (int i = 0; staged && i < nobj && !any_gone; ++i) any_gone = s_state[i] == 1;
+    for (int i = 0; any_gone && i < nobj; ++i) {
+      if (!(s_flags[i] & 1) || !(s_flags[i] & 2) || s_state[i] == 1 || s_nobs[i] < P.link_min_obs) continue;
+      if (t - s_first[i] > P.link_window_s) continue;
+      for (int j = 0; j < nobj; ++j) {
+        if (j == i || s_state[j] != 1 || !(s_flags[j] & 2) || (!(s_flags[j] & 4) && s_nobs[j] < P.spurious_obs)) continue;
+        if (!(s_first[i] > s_last[j])) continue;
+        const double d = dist3(&s_pos[3 * i], &s_pos[3 * j]);
+        if (d > smin(P.link_max_d, P.link_d0 + P.link_v * (s_first[i] - s_last[j]))) continue;
         bool wait = false;
-        if (t - n.first_seen < P.link_wait_s)
-          for (int q = 0; q < R->n_obj; ++q) {
-            const ObjRec& qq = obj_at(B, m, q);
-            if (q == i || q == j || !qq.confirmed || qq.state == 1 || qq.cls != n.cls) continue;
-            if (qq.last_seen < n.first_seen && dist3(qq.pos, n.pos) < d) { wait = true; break; }
+        if (t - s_first[i] < P.link_wait_s)
+          for (int q = 0; q < nobj; ++q) {
+            if (q == i || q == j || !(s_flags[q] & 2) || s_state[q] == 1 || s_cls[q] != s_cls[i]) continue;
+            if (s_last[q] < s_first[i] && dist3(&s_pos[3 * q], &s_pos[3 * i]) < d) { wait = true; break; }
           }
         if (wait) continue;
         if (cn_ < RELINK_MAXC) { cm_[cn_] = j; cnn_[cn_] = i; cd_[cn_] = d; ++cn_; }
@@ -256,11 +277,12 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
     used[nused++] = pm_[p];
     used[nused++] = pn_[p];
     const int mi = find_pos(B, m, pm_[p]), ni = find_pos(B, m, pn_[p]);
+    if (mi < 0 || ni < 0) continue;
     ObjRec& mo = B.objs[oglob(B, m, slot_at(B, m, mi))];
     const ObjRec& no = B.objs[oglob(B, m, slot_at(B, m, ni))];
     for (int k = 0; k < 3; ++k) { mo.pos[k] = no.pos[k]; mo.ext[k] = no.ext[k]; mo.lo[k] = no.lo[k]; mo.hi[k] = no.hi[k]; }
     // m takes n's cloud (m.cloud = n.cloud; version = n.version + 1); m's old cloud slot is freed
-    if (mi < 0 || ni < 0 || !INB(R->n_cfree, B.O, 505)) continue;
+    if (!INB(R->n_cfree, B.O, 505)) continue;
     B.cfreel[(size_t)m * B.O + R->n_cfree++] = mo.cloud_slot;
     mo.cloud_slot = no.cloud_slot;
     ++B.clouds[(size_t)m * B.O + mo.cloud_slot].version;
@@ -286,15 +308,16 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
 // segments and no text model, so only geo 1 (wall-size vertical plane) / 2 (ceiling) matter.
 __global__ void __launch_bounds__(256) k_struct(Batch B) {
   __shared__ BlockScratch bs;
-  __shared__ int hist[256];
+  __shared__ int hist[SEL_MAXQ * 256];
   __shared__ PlaneOut pout;
   const int m = blockIdx.y;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const MapRec& R = B.maps[m];
   const smg_params& P = B.p;
-  const Work W = work_at(B, m, blockIdx.x);
-  float* Pt = (float*)W.t4;
+  double* sel = B.sel + ((size_t)m * B.max_det + blockIdx.x) * 4 * B.pmax;
+  float* Pt = (float*)sel;                  // <= 2*800 points
+  double* scr = sel + 4096;                 // plane-fit scratch: 2 x 4096 doubles
   for (int b = blockIdx.x; b < R.n_obj; b += gridDim.x) {
     ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
     const size_t cs = (size_t)m * B.O + o.cloud_slot;
@@ -304,7 +327,7 @@ __global__ void __launch_bounds__(256) k_struct(Batch B) {
     const size_t stp = (size_t)C.n / 800 > 1 ? (size_t)C.n / 800 : 1;
     const int n = (int)(((size_t)C.n + stp - 1) / stp);
     const float4* pts = B.cpts + cs * B.cap;
-    if (!INB(3 * n, 4 * B.work_n, 508)) continue;
+    if (!INB(3 * n, 2 * 4096, 508)) continue;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       const float4 q = pts[(size_t)i * stp];
       Pt[3 * i] = (float)(C.org[0] + (double)q.x);
@@ -312,7 +335,7 @@ __global__ void __launch_bounds__(256) k_struct(Batch B) {
       Pt[3 * i + 2] = (float)(C.org[2] + (double)q.z);
     }
     __syncthreads();
-    plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, W.scr, B.work_n / 2, hist, bs,
+    plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, scr, 4096, hist, bs,
               &pout);
     int up = 0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) up += (double)Pt[3 * i + 2] > R.ceil_est - P.ceil_band;
@@ -335,42 +358,73 @@ __global__ void __launch_bounds__(256) k_struct(Batch B) {
 }
 
 // drop + prune (objmap.cpp:1064-1073), then the cloud-addition targets (objects named by this
-// frame's cloud lists, first appearance order, plus objects whose cloud moved)
-__global__ void k_prune(Batch B) {
-  const int m = blockIdx.x;
+// frame's cloud lists, first appearance order, plus objects whose cloud moved).  The list is
+// staged in shared memory; removal flags are evaluated in parallel, the ordered compaction and
+// the target list by thread 0.
+#define PRUNE_MAX 4096
+__global__ void __launch_bounds__(256) k_prune(Batch B) {
+  __shared__ int s_slot[PRUNE_MAX];
+  __shared__ uint32_t s_id[PRUNE_MAX];
+  __shared__ unsigned char s_rm[PRUNE_MAX], s_dirty[PRUNE_MAX];
+  __shared__ BlockScratch bs;
+  const int m = blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
-  if (!F.active || threadIdx.x != 0) return;
+  if (!F.active) return;
   MapRec* R = &B.maps[m];
   const smg_params& P = B.p;
-  for (int b = 0; b < R->n_obj;) {
-    ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
+  const int n = R->n_obj;
+  if (n > PRUNE_MAX) {
+    if (tid == 0) set_err(R, SMG_E_CAP_OBJ);
+    return;
+  }
+  int nstruct = 0;
+  for (int b = tid; b < n; b += blockDim.x) {
+    const int slot = slot_at(B, m, b);
+    ObjRec& o = B.objs[oglob(B, m, slot)];
     o.hide = 0;
     o.drop = o.geo == 1 || o.geo == 2;
     bool rm;
-    if (o.drop) { ++R->st.n_obj_struct; rm = true; }
+    if (o.drop) { ++nstruct; rm = true; }
     else if (!o.confirmed) rm = F.stamp - o.last_seen > P.prune_s;
     else rm = o.state == 1 && !o.moved && (int)o.n_obs < P.spurious_obs;
-    if (rm) erase_pos(B, m, b, false);
-    else ++b;
-  }
-  int nt = 0;
-  for (int e = 0; e < R->n_pts; ++e) {
-    const int pos = find_pos(B, m, B.ptsl[(size_t)m * B.max_det + e].obj_id);
-    if (pos < 0) continue;
-    const int slot = slot_at(B, m, pos);
-    bool seen = false;
-    for (int q = 0; q < nt; ++q) seen = seen || B.tgt_slot[(size_t)m * B.O + q] == slot;
-    if (!seen && INB(nt, B.O, 506)) B.tgt_slot[(size_t)m * B.O + nt++] = slot;
-  }
-  for (int b = 0; b < R->n_obj; ++b) {
-    const int slot = slot_at(B, m, b);
-    const ObjRec& o = B.objs[oglob(B, m, slot)];
     const CloudRec& C = B.clouds[(size_t)m * B.O + o.cloud_slot];
-    if (C.cver == C.version || C.n == 0) continue;
-    bool seen = false;
-    for (int q = 0; q < nt; ++q) seen = seen || B.tgt_slot[(size_t)m * B.O + q] == slot;
-    if (!seen && INB(nt, B.O, 507)) B.tgt_slot[(size_t)m * B.O + nt++] = slot;
+    s_slot[b] = slot;
+    s_id[b] = o.id;
+    s_rm[b] = rm;
+    s_dirty[b] = C.cver != C.version && C.n > 0;
   }
+  nstruct = block_sum_i(nstruct, bs);
+  if (tid != 0) return;
+  R->st.n_obj_struct += nstruct;
+  int32_t* ord = B.order + (size_t)m * B.O;
+  int w = 0;
+  for (int b = 0; b < n; ++b) {
+    if (s_rm[b]) {
+      const ObjRec& o = B.objs[oglob(B, m, s_slot[b])];
+      if (INB(R->n_cfree, B.O, 510)) B.cfreel[(size_t)m * B.O + R->n_cfree++] = o.cloud_slot;
+      if (INB(R->n_free, B.O, 511)) B.freel[(size_t)m * B.O + R->n_free++] = s_slot[b];
+      continue;
+    }
+    s_slot[w] = s_slot[b];
+    s_id[w] = s_id[b];
+    s_dirty[w] = s_dirty[b];
+    ord[w] = s_slot[b];
+    ++w;
+  }
+  R->n_obj = w;
+  int nt = 0;
+  unsigned char* taken = s_rm;   // reuse as "already a target" flags
+  for (int b = 0; b < w; ++b) taken[b] = 0;
+  for (int e = 0; e < R->n_pts; ++e) {
+    const uint32_t id = B.ptsl[(size_t)m * B.max_det + e].obj_id;
+    for (int b = 0; b < w; ++b)
+      if (s_id[b] == id) {
+        if (!taken[b]) { taken[b] = 1; B.tgt_slot[(size_t)m * B.O + nt++] = s_slot[b]; }
+        break;
+      }
+  }
+  for (int b = 0; b < w; ++b)
+    if (s_dirty[b] && !taken[b]) { taken[b] = 1; B.tgt_slot[(size_t)m * B.O + nt++] = s_slot[b]; }
   R->n_targets = nt;
 }
 

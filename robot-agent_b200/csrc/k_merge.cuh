@@ -13,84 +13,101 @@
 #pragma once
 #include "k_life.cuh"
 
-#define MP_CTAS 8
-#define MP_SPW 640
+#define MP_CTAS 4
+#define MP_GL 8192   // gated pairs per CTA
+#define MP_SMEM(O) ((size_t)(O) * (6 * 8 + 2 * 4) + MP_GL * 4)
+
+// p-th pair (i < j) of n objects in row-major order of the upper triangle
+DEV void pair_of(long long p, int n, int* pi, int* pj) {
+  auto rowstart = [&](long long i) { return i * (2LL * n - i - 1) / 2; };
+  long long i = (long long)((2.0 * n - 1 - sqrt((2.0 * n - 1) * (2.0 * n - 1) - 8.0 * (double)p)) / 2.0);
+  if (i < 0) i = 0;
+  while (i > 0 && rowstart(i) > p) --i;
+  while (i + 1 < n && rowstart(i + 1) <= p) ++i;
+  *pi = (int)i;
+  *pj = (int)(p - rowstart(i) + i + 1);
+}
 
 __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
   extern __shared__ unsigned char smem_raw[];
+  __shared__ int ngl;
   const int m = blockIdx.y, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const MapRec& R = B.maps[m];
   const smg_params& P = B.p;
-  float* mu = (float*)smem_raw + (size_t)wid * (B.D + 3 * MP_SPW);
-  float* sp = mu + B.D;
   const int n = R.n_obj;
+  if (n < 2) return;
+  double* slo = (double*)smem_raw;
+  double* shi = slo + 3 * (size_t)B.O;
+  int* scn = (int*)(shi + 3 * (size_t)B.O);
+  int* sst = scn + B.O;
+  int* gl = sst + B.O;
+  // 1. stage the gate inputs of every object (parallel loads)
+  for (int b = tid; b < n; b += blockDim.x) {
+    const ObjRec& o = obj_at(B, m, b);
+    for (int k = 0; k < 3; ++k) { slo[3 * b + k] = o.lo[k]; shi[3 * b + k] = o.hi[k]; }
+    scn[b] = B.clouds[(size_t)m * B.O + o.cloud_slot].n;
+    sst[b] = o.state;
+  }
+  if (tid == 0) ngl = 0;
+  __syncthreads();
+  // 2. box-gap and size gates of all pairs (objmap.cpp:1160-1173); this CTA takes every
+  //    MP_CTAS-th pair
   const double gate2 = P.gate * P.gate;
-  for (int i = blockIdx.x * nw + wid; i < n; i += gridDim.x * nw) {
-    const int si = slot_at(B, m, i);
-    const ObjRec& a = B.objs[oglob(B, m, si)];
-    if (a.state == 1) continue;
-    for (int j = i + 1; j < n; ++j) {
-      const int sj = slot_at(B, m, j);
-      const ObjRec& b = B.objs[oglob(B, m, sj)];
-      if (b.state == 1) continue;
-      double g2 = 0;
-      bool too_big = false;
-      for (int k = 0; k < 3; ++k) {
-        const double g = smax3(0.0, a.lo[k] - b.hi[k], b.lo[k] - a.hi[k]);
-        g2 += g * g;
-        too_big = too_big || smax(a.hi[k], b.hi[k]) - smin(a.lo[k], b.lo[k]) > P.max_ext;
-      }
-      if (g2 > gate2 || too_big) continue;
-      const size_t csa = (size_t)m * B.O + a.cloud_slot, csb = (size_t)m * B.O + b.cloud_slot;
-      const bool a_small = B.clouds[csa].n <= B.clouds[csb].n;
-      const ObjRec& sm = a_small ? a : b;
-      const ObjRec& lg = a_small ? b : a;
-      const size_t css = a_small ? csa : csb, csl = a_small ? csb : csa;
-      // cloudSample(sm, contact_samples) (objmap.cpp:1107-1114)
-      const CloudRec& Cs = B.clouds[css];
-      const int cn = Cs.n;
-      const int stp = max(1, cn / max(1, P.contact_samples));
-      const int nsp = cn > 0 ? (cn + stp - 1) / stp : 0;
-      if (nsp > MP_SPW) { if (lane == 0) set_err(&B.maps[m], SMG_E_ARGS); continue; }
-      const float4* pts = B.cpts + css * B.cap;
-      for (int q = lane; q < nsp; q += 32) {
-        const float4 p = pts[(size_t)q * stp];
-        sp[3 * q] = (float)(Cs.org[0] + (double)p.x);
-        sp[3 * q + 1] = (float)(Cs.org[1] + (double)p.y);
-        sp[3 * q + 2] = (float)(Cs.org[2] + (double)p.z);
-      }
-      __syncwarp();
-      double cs = -2;
-      for (int dir = 0; dir < 2; ++dir) {
-        const ObjRec& x = dir == 0 ? a : b;
-        const size_t ogx = oglob(B, m, dir == 0 ? si : sj), ogy = oglob(B, m, dir == 0 ? sj : si);
-        if (!(x.nrm_frag > 0)) continue;
-        const double nn = sqrt(x.nrm_frag);
-        const float* r = B.rfrag + ogx * B.D;
-        for (int q = lane; q < B.D; q += 32) mu[q] = (float)((double)r[q] / nn);
-        __syncwarp();
-        cs = smax(cs, cos_max_warp(B, ogy, B.objs[ogy], mu));
-        __syncwarp();
-      }
-      const int hits = contact_hits_warp(B, csl, sp, nsp, P.contact_cell);
-      if (lane == 0) {
-        const double contact = (nsp > 0 && B.clouds[csl].cn > 0) ? (double)hits / (double)nsp : 0.0;
-        const double p = pair_p(sm.lo, sm.hi, sm.pos, contact, lg.lo, lg.hi, lg.pos, cs, P, true, nullptr);
-        if (p >= P.merge_p) {
-          const int c = atomicAdd(&B.mcand_n[m], 1);
-          if (c < B.O * 8) {
-            B.mcand_p[(size_t)m * B.O * 8 + c] = p;
-            B.mcand_ab[((size_t)m * B.O * 8 + c) * 2] = a.id;
-            B.mcand_ab[((size_t)m * B.O * 8 + c) * 2 + 1] = b.id;
-          } else {
-            set_err(&B.maps[m], SMG_E_ARGS);
-          }
+  const long long npair = (long long)n * (n - 1) / 2;
+  for (long long p = (long long)blockIdx.x * blockDim.x + tid; p < npair; p += (long long)gridDim.x * blockDim.x) {
+    int i, j;
+    pair_of(p, n, &i, &j);
+    if (sst[i] == 1 || sst[j] == 1) continue;
+    double g2 = 0;
+    bool too_big = false;
+    for (int k = 0; k < 3; ++k) {
+      const double g = smax3(0.0, slo[3 * i + k] - shi[3 * j + k], slo[3 * j + k] - shi[3 * i + k]);
+      g2 += g * g;
+      too_big = too_big || smax(shi[3 * i + k], shi[3 * j + k]) - smin(slo[3 * i + k], slo[3 * j + k]) > P.max_ext;
+    }
+    if (g2 > gate2 || too_big) continue;
+    const int q = atomicAdd(&ngl, 1);
+    if (q < MP_GL) gl[q] = i << 16 | j;
+    else set_err(&B.maps[m], SMG_E_ARGS);
+  }
+  __syncthreads();
+  // 3. apPairObj of the gated pairs (objmap.cpp:1118-1135), one warp per pair
+  const int ng = min(ngl, MP_GL);
+  for (int g = wid; g < ng; g += nw) {
+    const int i = gl[g] >> 16, j = gl[g] & 0xffff;
+    const int si = slot_at(B, m, i), sj = slot_at(B, m, j);
+    const size_t ogi = oglob(B, m, si), ogj = oglob(B, m, sj);
+    const ObjRec& a = B.objs[ogi];
+    const ObjRec& b = B.objs[ogj];
+    const bool a_small = scn[i] <= scn[j];
+    const ObjRec& sm = a_small ? a : b;
+    const ObjRec& lg = a_small ? b : a;
+    const size_t css = (size_t)m * B.O + sm.cloud_slot, csl = (size_t)m * B.O + lg.cloud_slot;
+    const int cn = a_small ? scn[i] : scn[j];
+    const int stp = max(1, cn / max(1, P.contact_samples));
+    const int nsp = cn > 0 ? (cn + stp - 1) / stp : 0;
+    double cs = -2;
+    if (a.nrm_frag > 0) cs = smax(cs, cos_max_warp(B, ogj, b, B.mu + ogi * B.D));
+    if (b.nrm_frag > 0) cs = smax(cs, cos_max_warp(B, ogi, a, B.mu + ogj * B.D));
+    const int hits = contact_hits_cloud_warp(B, csl, css, stp, nsp, P.contact_cell);
+    if (lane == 0) {
+      const double contact = (nsp > 0 && B.clouds[csl].cn > 0) ? (double)hits / (double)nsp : 0.0;
+      const double p = pair_p(sm.lo, sm.hi, sm.pos, contact, lg.lo, lg.hi, lg.pos, cs, P, true, nullptr);
+      if (p >= P.merge_p) {
+        const int c = atomicAdd(&B.mcand_n[m], 1);
+        if (c < B.O * 8) {
+          B.mcand_p[(size_t)m * B.O * 8 + c] = p;
+          B.mcand_ab[((size_t)m * B.O * 8 + c) * 2] = a.id;
+          B.mcand_ab[((size_t)m * B.O * 8 + c) * 2 + 1] = b.id;
+          B.mcand_key[(size_t)m * B.O * 8 + c] = (uint32_t)i << 16 | (uint32_t)j;
+        } else {
+          set_err(&B.maps[m], SMG_E_ARGS);
         }
       }
-      __syncwarp();
     }
+    __syncwarp();
   }
 }
 
@@ -108,15 +125,21 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
   const int nc = min(B.mcand_n[m], B.O * 8);
   double* cp = B.mcand_p + (size_t)m * B.O * 8;
   uint32_t* cab = B.mcand_ab + (size_t)m * B.O * 8 * 2;
+  uint32_t* ckey = B.mcand_key + (size_t)m * B.O * 8;
   if (tid == 0) {
     R->n_evn = 0;
     nused = 0;
-    for (int i = 1; i < nc; ++i) {   // descending P (stable for equal P)
+    // descending P; equal P keep the reference's enumeration order (pairs i < j in list order),
+    // which is what its std::sort leaves for lists of up to 16 candidates (insertion sort)
+    for (int i = 1; i < nc; ++i) {
       const double p = cp[i];
-      const uint32_t x = cab[2 * i], y = cab[2 * i + 1];
+      const uint32_t x = cab[2 * i], y = cab[2 * i + 1], kk = ckey[i];
       int j = i;
-      while (j > 0 && cp[j - 1] < p) { cp[j] = cp[j - 1]; cab[2 * j] = cab[2 * j - 2]; cab[2 * j + 1] = cab[2 * j - 1]; --j; }
-      cp[j] = p; cab[2 * j] = x; cab[2 * j + 1] = y;
+      while (j > 0 && (cp[j - 1] < p || (cp[j - 1] == p && ckey[j - 1] > kk))) {
+        cp[j] = cp[j - 1]; cab[2 * j] = cab[2 * j - 2]; cab[2 * j + 1] = cab[2 * j - 1]; ckey[j] = ckey[j - 1];
+        --j;
+      }
+      cp[j] = p; cab[2 * j] = x; cab[2 * j + 1] = y; ckey[j] = kk;
     }
   }
   __syncthreads();

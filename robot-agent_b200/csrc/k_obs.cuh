@@ -83,6 +83,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   __shared__ double sh_best[4];
   __shared__ int sh_bestc;
   __shared__ double sh_m[3], sh_V[3][3], sh_ev[3];
+  __shared__ double red[6 * 32];
   const int tid = threadIdx.x;
   if (n < 8 || !(tau > 0)) {
     if (tid == 0) out->ok = 0;
@@ -172,20 +173,20 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   int ni = 0;
   for (int pass = 0; pass < 2; ++pass) {
     for (int k = 0; k < 4; ++k) mp[k] = pl[k];
-    double s0 = 0, s1 = 0, s2 = 0;
-    int cnt = 0;
+    double sm[4] = {0, 0, 0, 0};   // count, sum x, sum y, sum z
     for (int i = tid; i < n; i += blockDim.x) {
       const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
-      if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) { s0 += x; s1 += y; s2 += z; ++cnt; }
+      if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) { sm[0] += 1.0; sm[1] += x; sm[2] += y; sm[3] += z; }
     }
-    ni = block_sum_i(cnt, bs);
+    block_sum_multi<4>(sm, red);
+    ni = (int)sm[0];
     if (ni < 3) {
       if (tid == 0) out->ok = 0;
       __syncthreads();
       return;
     }
     const double inv = 1.0 / (double)(ni > 1 ? ni : 1);
-    double m[3] = {block_sum_d(s0, bs), block_sum_d(s1, bs), block_sum_d(s2, bs)};
+    double m[3] = {sm[1], sm[2], sm[3]};
     for (int k = 0; k < 3; ++k) m[k] *= inv;
     double c[6] = {0, 0, 0, 0, 0, 0};
     for (int i = tid; i < n; i += blockDim.x) {
@@ -196,9 +197,10 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
         c[3] += d[1] * d[1]; c[4] += d[1] * d[2]; c[5] += d[2] * d[2];
       }
     }
+    block_sum_multi<6>(c, red);
     double C[3][3];
-    C[0][0] = block_sum_d(c[0], bs) * inv; C[0][1] = block_sum_d(c[1], bs) * inv; C[0][2] = block_sum_d(c[2], bs) * inv;
-    C[1][1] = block_sum_d(c[3], bs) * inv; C[1][2] = block_sum_d(c[4], bs) * inv; C[2][2] = block_sum_d(c[5], bs) * inv;
+    C[0][0] = c[0] * inv; C[0][1] = c[1] * inv; C[0][2] = c[2] * inv;
+    C[1][1] = c[3] * inv; C[1][2] = c[4] * inv; C[2][2] = c[5] * inv;
     C[1][0] = C[0][1]; C[2][0] = C[0][2]; C[2][1] = C[1][2];
     if (tid == 0) {
       double ev[3], V[3][3];
@@ -223,7 +225,9 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
       a0 += dx * dx; a1 += dx * dy; a2 += dy * dy;
     }
   }
-  const double sxx = block_sum_d(a0, bs), sxy = block_sum_d(a1, bs), syy = block_sum_d(a2, bs);
+  double hs3[3] = {a0, a1, a2};
+  block_sum_multi<3>(hs3, red);
+  const double sxx = hs3[0], sxy = hs3[1], syy = hs3[2];
   const double th = 0.5 * atan2(2 * sxy, sxx - syy), hc = cos(th), hs = sin(th);
   // z and horizontal-span projections of the inliers -> exact percentiles (objprob.cpp:193-206)
   __shared__ int sh_cnt;
@@ -241,11 +245,14 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     }
   }
   __syncthreads();
-  const double h9 = block_select(hsp, ni, pct_index(ni, 0.9), hist, bs);
-  const double h1 = block_select(hsp, ni, pct_index(ni, 0.1), hist, bs);
-  const double zlo = block_select(zs, ni, pct_index(ni, 0.1), hist, bs);
-  const double zhi = block_select(zs, ni, pct_index(ni, 0.9), hist, bs);
-  const double zmd = block_select(zs, ni, pct_index(ni, 0.5), hist, bs);
+  __shared__ double sel5[5];
+  {
+    const double* arr[5] = {hsp, hsp, zs, zs, zs};
+    const int nn[5] = {ni, ni, ni, ni, ni};
+    const int kk[5] = {pct_index(ni, 0.9), pct_index(ni, 0.1), pct_index(ni, 0.1), pct_index(ni, 0.9), pct_index(ni, 0.5)};
+    block_select_multi(arr, nn, kk, sel5, 5, hist, bs);
+  }
+  const double h9 = sel5[0], h1 = sel5[1], zlo = sel5[2], zhi = sel5[3], zmd = sel5[4];
   if (tid == 0) {
     out->ok = 1;
     for (int k = 0; k < 3; ++k) out->n[k] = sh_V[k][0];
@@ -446,14 +453,21 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
     return;
   }
   __syncthreads();
-  // 4. 10/50/90 percentiles per axis (objmap.cpp:730-738)
+  // 4. 10/50/90 percentiles per axis (objmap.cpp:730-738): nine order statistics, one sweep
   double lo[3], md[3], hi[3];
-  const double* AX[3] = {XK, YK, ZK};
-  for (int a = 0; a < 3; ++a) {
-    nS = subsample_to(AX[a], np, S);
-    md[a] = block_select(S, nS, pct_index(nS, 0.5), hist, bs);
-    lo[a] = block_select(S, nS, pct_index(nS, 0.1), hist, bs);
-    hi[a] = block_select(S, nS, pct_index(nS, 0.9), hist, bs);
+  {
+    const double* AX[3] = {XK, YK, ZK};
+    double* SB[3] = {S, S + SMG_SUB, S + 2 * SMG_SUB};
+    int* mh = (int*)(S + 3 * SMG_SUB);
+    int nS3 = 0;
+    for (int a = 0; a < 3; ++a) nS3 = subsample_to(AX[a], np, SB[a]);
+    const double* arr[9] = {SB[0], SB[0], SB[0], SB[1], SB[1], SB[1], SB[2], SB[2], SB[2]};
+    const int nn[9] = {nS3, nS3, nS3, nS3, nS3, nS3, nS3, nS3, nS3};
+    const int kk[9] = {pct_index(nS3, 0.5), pct_index(nS3, 0.1), pct_index(nS3, 0.9), pct_index(nS3, 0.5), pct_index(nS3, 0.1),
+                       pct_index(nS3, 0.9), pct_index(nS3, 0.5), pct_index(nS3, 0.1), pct_index(nS3, 0.9)};
+    __shared__ double sel9[9];
+    block_select_multi(arr, nn, kk, sel9, 9, mh, bs);
+    for (int a = 0; a < 3; ++a) { md[a] = sel9[3 * a]; lo[a] = sel9[3 * a + 1]; hi[a] = sel9[3 * a + 2]; }
     __syncthreads();
   }
   const int trunc = (b[0] <= 2 || b[1] <= 2 || b[2] >= W - 3 || b[3] >= H - 3);
@@ -490,7 +504,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
     const double dc = hypot3(cen0 / nc - T[3], cen1 / nc - T[7], cen2 / nc - T[11]);
     const double tau = smin(P.ransac_tau_max, P.ransac_tau0 + P.ransac_tau_k * dc * dc);
     const uint64_t sb = (uint64_t)__double_as_longlong(F.stamp);
-    plane_fit(CX, nc, tau, ap_seed(sb, (uint64_t)k), P.ransac_iters, B.need_tab, SCR, B.pmax, hist, bs, &pout);
+    plane_fit(CX, nc, tau, ap_seed(sb, (uint64_t)k), P.ransac_iters, B.need_tab, SCR, B.pmax, (int*)smem_raw, bs, &pout);
   } else if (tid == 0) {
     pout.ok = 0;
   }

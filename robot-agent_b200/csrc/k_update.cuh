@@ -10,6 +10,7 @@
 #include "k_assoc.cuh"
 
 #define UPD_THREADS 256
+#define UPD_SMEM(B) ((size_t)(B).D * 4 + (size_t)(B).max_det * sizeof(ObsRec) + sizeof(ObjRec) + 16)
 
 DEV size_t cslot_glob(const Batch& B, int m, const ObjRec& o) { return (size_t)m * B.O + o.cloud_slot; }
 
@@ -36,24 +37,48 @@ DEV double first_view(const Batch& B, int m, double x, double y, double range) {
   return 1e300;
 }
 
-// |r_frag|^2 refresh (ApState mu cache, objprob.cpp:228-240), block-wide
+// |r_frag|^2 and the mean direction mu = float(r / |r|) (ApState mu cache, objprob.cpp:228-240),
+// block-wide, after every change of r_frag
 DEV void refresh_nrm(const Batch& B, size_t og, BlockScratch& bs) {
   const float* r = B.rfrag + og * B.D;
   double s = 0;
   for (int i = threadIdx.x; i < B.D; i += blockDim.x) s += (double)r[i] * (double)r[i];
   s = block_sum_d(s, bs);
   if (threadIdx.x == 0) B.objs[og].nrm_frag = s;
+  const double nn = sqrt(s);
+  float* mu = B.mu + og * B.D;
+  for (int i = threadIdx.x; i < B.D; i += blockDim.x) mu[i] = s > 0 ? (float)((double)r[i] / nn) : 0.f;
+  __syncthreads();
+}
+
+// refresh_nrm writing |r|^2 into the given (shared) record
+DEV void refresh_nrm_into(const Batch& B, ObjRec& o, size_t og, BlockScratch& bs) {
+  const float* r = B.rfrag + og * B.D;
+  double s = 0;
+  for (int i = threadIdx.x; i < B.D; i += blockDim.x) s += (double)r[i] * (double)r[i];
+  s = block_sum_d(s, bs);
+  if (threadIdx.x == 0) o.nrm_frag = s;
+  const double nn = sqrt(s);
+  float* mu = B.mu + og * B.D;
+  for (int i = threadIdx.x; i < B.D; i += blockDim.x) mu[i] = s > 0 ? (float)((double)r[i] / nn) : 0.f;
+  __syncthreads();
+}
+
+// block copy of an object record between global and shared memory
+DEV void rec_copy(ObjRec* dst, const ObjRec* src) {
+  const uint32_t* s = (const uint32_t*)src;
+  uint32_t* d = (uint32_t*)dst;
+  for (int i = threadIdx.x; i < (int)(sizeof(ObjRec) / 4); i += blockDim.x) d[i] = s[i];
   __syncthreads();
 }
 
 // apAddView (scenemap objprob.cpp:312-356) for a detection fragment (whole = false), no text
 // model.  Block-wide; z is the fp32 embedding (global).  Returns nothing (tempered kappa is only
 // used for the label terms, absent here).
-DEV void ap_add_view(const Batch& B, size_t og, const float* z_sh, double kappa, double stamp, const double cam[6],
+DEV void ap_add_view(const Batch& B, ObjRec& o, size_t og, const float* z_sh, double kappa, double stamp, const double cam[6],
                      BlockScratch& bs) {
   __shared__ double sh_k;
   __shared__ int sh_free;
-  ObjRec& o = B.objs[og];
   const int tid = threadIdx.x, D = B.D;
   if (tid == 0) {
     double k = kappa;
@@ -111,7 +136,7 @@ DEV void ap_add_view(const Batch& B, size_t og, const float* z_sh, double kappa,
     if (o.n_views > B.topk) o.n_views = B.topk;
   }
   __syncthreads();
-  refresh_nrm(B, og, bs);
+  refresh_nrm_into(B, o, og, bs);
 }
 
 // allocate an object slot + cloud slot for a new object (appended at list position n_obj)
@@ -126,10 +151,12 @@ DEV int new_object_slot(const Batch& B, int m, int* cslot) {
 }
 
 __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
-  extern __shared__ unsigned char smem_raw[];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   float* zs = (float*)smem_raw;   // D
+  ObsRec* OBs = (ObsRec*)(smem_raw + (((size_t)B.D * 4 + 15) & ~(size_t)15));   // staged observations
+  ObjRec* MO = (ObjRec*)(OBs + B.max_det);                                         // staged object record
   __shared__ BlockScratch bs;
-  __shared__ int sh_act, sh_slot, sh_cslot, sh_go;
+  __shared__ int sh_act, sh_slot, sh_cslot;
   __shared__ int head[SMG_MAX_DET];
   __shared__ int evn;
   const int m = blockIdx.x, tid = threadIdx.x;
@@ -140,8 +167,14 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
   const double* T = F.T_mc;
   const int nobs = R->n_obs;
   const bool has_z = F.emb != nullptr;
-  ObsRec* OB = B.obs + (size_t)m * B.max_det;
+  ObsRec* OB = OBs;
+  {
+    const uint32_t* src = (const uint32_t*)(B.obs + (size_t)m * B.max_det);
+    uint32_t* dst = (uint32_t*)OBs;
+    for (int i = tid; i < (int)(B.max_det * sizeof(ObsRec) / 4); i += blockDim.x) dst[i] = src[i];
+  }
   const int32_t* OL = B.obs_list + (size_t)m * B.max_det;
+  const double* GD = B.gdot + (size_t)m * B.max_det * B.max_det;
   const double cam6[6] = {T[3], T[7], T[11], T[2], T[6], T[10]};
   if (tid == 0) {
     evn = 0;
@@ -210,9 +243,10 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
     __syncthreads();
     const size_t og = oglob(B, m, sh_slot);
     if (act == 1) {
-      if (has_z) ap_add_view(B, og, zs, o.kappa, F.stamp, cam6, bs);
+      rec_copy(MO, &B.objs[og]);
+      if (has_z) ap_add_view(B, *MO, og, zs, o.kappa, F.stamp, cam6, bs);
       if (tid == 0) {
-        ObjRec& mo = B.objs[og];
+        ObjRec& mo = *MO;
         ++mo.n_ap_obs;
         mo.wall_like = 2 * mo.n_wall_obs >= mo.n_ap_obs;
         if (!o.sec) {
@@ -300,9 +334,11 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
           }
         }
       }
+      __syncthreads();
+      rec_copy(&B.objs[og], MO);
     } else if (act == 2) {
       if (tid == 0) {   // new candidate (objmap.cpp:951-978)
-        ObjRec& mo = B.objs[og];
+        ObjRec& mo = *MO;
         const int cs = sh_cslot;
         memset(&mo, 0, sizeof(ObjRec));
         mo.id = R->next_id++;
@@ -345,48 +381,36 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
         for (int i = tid; i < B.D; i += blockDim.x) r[i] = 0.f;
         __syncthreads();
       }
-      if (has_z) ap_add_view(B, og, zs, o.kappa, F.stamp, cam6, bs);
+      if (has_z) ap_add_view(B, *MO, og, zs, o.kappa, F.stamp, cam6, bs);
       if (tid == 0) {
-        ObjRec& mo = B.objs[og];
+        ObjRec& mo = *MO;
         mo.n_ap_obs = 1;
         mo.n_wall_obs = 0;
         mo.n_struct_look = 0;
         mo.wall_like = 0;
         ++R->st.n_new;
       }
-      // frame grouping (objmap.cpp:980-995): later unmatched fragments touching this one
-      if (P.frame_group) {
+      // frame grouping (objmap.cpp:980-995): later unmatched fragments touching this one, with
+      // the dot products computed by k_assoc
+      if (P.frame_group && tid == 0) {
         for (int b2 = a + 1; b2 < nobs; ++b2) {
-          if (tid == 0) {
-            const ObsRec& q = OB[OL[b2]];
-            sh_go = 0;
-            if (q.obs_to == -1 && has_z) {
-              double g2 = 0;
-              for (int k = 0; k < 3; ++k) {
-                const double g = smax3(0.0, q.lo[k] - o.hi[k], o.lo[k] - q.hi[k]);
-                g2 += g * g;
-              }
-              sh_go = !(g2 > 0.02 * 0.02);
-            }
+          ObsRec& q = OB[OL[b2]];
+          if (q.obs_to != -1 || !has_z) continue;
+          double g2 = 0;
+          for (int k = 0; k < 3; ++k) {
+            const double g = smax3(0.0, q.lo[k] - o.hi[k], o.lo[k] - q.hi[k]);
+            g2 += g * g;
           }
-          __syncthreads();
-          if (sh_go) {
-            const ObsRec& q = OB[OL[b2]];
-            double dot = 0;
-            for (int i = tid; i < B.D; i += blockDim.x)
-              dot += (double)emb_at(F.emb, F.emb_dtype, B.D, q.det, i) * (double)zs[i];
-            dot = block_sum_d(dot, bs);
-            if (tid == 0) {
-              double f[7] = {0, 0, 0, 0, 0, 0, 0};
-              pair_geo(q.lo, q.hi, q.pos, o.lo, o.hi, o.pos, dot, P.cos0, f);
-              f[0] = 1.0;
-              if (1.0 / (1.0 + exp(-same_logit(P.w, f))) >= P.same_p) OB[OL[b2]].obs_to = R->n_obj - 1;
-            }
-          }
-          __syncthreads();
+          if (g2 > 0.02 * 0.02) continue;
+          double f[7] = {0, 0, 0, 0, 0, 0, 0};
+          pair_geo(q.lo, q.hi, q.pos, o.lo, o.hi, o.pos, GD[(size_t)a * B.max_det + b2], P.cos0, f);
+          f[0] = 1.0;
+          if (1.0 / (1.0 + exp(-same_logit(P.w, f))) >= P.same_p) q.obs_to = R->n_obj - 1;
         }
       }
-      if (tid == 0) push_event(B, m, F.stamp, B.objs[og], 0, (2u << 24) | (uint32_t)evn++);
+      if (tid == 0) push_event(B, m, F.stamp, *MO, 0, (2u << 24) | (uint32_t)evn++);
+      __syncthreads();
+      rec_copy(&B.objs[og], MO);
     }
     __syncthreads();
   }

@@ -259,7 +259,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
                int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out) {
   if (!p || !out || n_maps <= 0 || max_objects <= 0 || emb_dim <= 0 || emb_dim > 2048 || max_w <= 0 || max_h <= 0 || max_det <= 0 ||
       max_det > SMG_MAX_DET || grid_w <= 0 || grid_h <= 0 || p->topk <= 0 || p->topk > SMG_TOPK_MAX || p->bins <= 0 ||
-      p->bins > SMG_BINS_MAX || p->cloud_cap <= 0 || p->voxel <= 0 || p->ransac_iters > RANSAC_MAX)
+      p->bins > SMG_BINS_MAX || max_objects > PRUNE_MAX || p->cloud_cap <= 0 || p->voxel <= 0 || p->ransac_iters > RANSAC_MAX)
     return fail(SMG_ERR_ARGS, "smg_create: bad arguments");
   *out = nullptr;
   int ndev = 0;
@@ -310,6 +310,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.cfreel, MO);
   DA(B.assoc, (size_t)M * max_det);
   DA(B.rfrag, MO * D);
+  DA(B.mu, MO * D);
   DA(B.views, MO * (B.topk + 1) * D);
   DA(B.clouds, MO);
   DA(B.cpts, MO * B.cap);
@@ -317,6 +318,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.chkey, MO * B.HC);
   DA(B.chidx, MO * B.HC);
   DA(B.chgen, MO * B.HC);
+  DA(B.cbits, MO * 2 * CB_WORDS);
   DA(B.ckey, MO * B.HCC);
   DA(B.cgen, MO * B.HCC);
   const size_t MD = (size_t)M * max_det;
@@ -331,10 +333,12 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.touched, MO + max_det);
   DA(B.obj_hit, MO + max_det);
   DA(B.ptsl, MD);
+  DA(B.gdot, MD * max_det);
   DA(B.tgt_slot, MO);
   DA(B.events, (size_t)M * SMG_MAX_EVENTS);
   DA(B.mcand_p, MO * 8);
   DA(B.mcand_ab, MO * 8 * 2);
+  DA(B.mcand_key, MO * 8);
   DA(B.mcand_n, M);
   DA(B.vkey, (size_t)M * B.view_slots);
   DA(B.vfirst, (size_t)M * B.view_slots * SMG_VIEW_BANDS);
@@ -438,8 +442,9 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   {
     const int sm_assoc = ((D * 4 + SP_MAX * 12 + 7) & ~7) + O * 8;
     CK(cudaFuncSetAttribute(k_assoc, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_assoc));
-    CK(cudaFuncSetAttribute(k_merge_pairs, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * (D + 3 * MP_SPW) * 4));
-    CK(cudaFuncSetAttribute(k_relink, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * D * 4));
+    CK(cudaFuncSetAttribute(k_merge_pairs, cudaFuncAttributeMaxDynamicSharedMemorySize, MP_SMEM(O)));
+    CK(cudaFuncSetAttribute(k_relink, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 8 * RELINK_STAGE + 8 * D * 4));
+    CK(cudaFuncSetAttribute(k_update, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UPD_SMEM(B)));
   }
   CK(cudaDeviceSynchronize());
   *out = b;
@@ -582,7 +587,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   if (b->timing) { cudaEventRecord(e1, b->s_grid); b->ev_used.push_back({13, {e0, e1}}); } }
   CK(cudaEventRecord(b->ev_join, b->s_grid));
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_merge_pairs<<<dim3(MP_CTAS, M), 256, 8 * (B.D + 3 * MP_SPW) * 4, st>>>(B);
+  k_merge_pairs<<<dim3(MP_CTAS, M), 256, MP_SMEM(B.O), st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({1, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
@@ -602,7 +607,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({5, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_update<<<M, UPD_THREADS, B.D * 4, st>>>(B);
+  k_update<<<M, UPD_THREADS, UPD_SMEM(B), st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({6, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
@@ -610,15 +615,15 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({7, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_relink<<<M, 256, 8 * B.D * 4, st>>>(B);
+  k_relink<<<M, 256, 3 * 8 * RELINK_STAGE + 8 * B.D * 4, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({8, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_struct<<<dim3(WORK_SLOTS, M), 256, 0, st>>>(B);
+  k_struct<<<dim3(B.max_det, M), 256, 0, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({9, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_prune<<<M, 32, 0, st>>>(B);
+  k_prune<<<M, 256, 0, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({10, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }

@@ -29,7 +29,8 @@
 #define SMG_MAX_EVENTS 1024   // per map per frame
 #define SMG_BINS_MAX 1440
 #define SMG_MATCH_CELLS 12288 // kH * 3 / 4 (scenemap scan.cpp:319, :399)
-#define WORK_SLOTS 8          // per-map work areas (cloud add / struct CTAs per map)
+#define WORK_SLOTS 16         // per-map work areas (cloud add CTAs per map)
+#define CB_WORDS 16384        // contact bitset budget per cloud (words of 32 cells)
 
 // error word bits
 #define SMG_E_CAP_OBJ 1
@@ -129,6 +130,8 @@ typedef struct {
   uint32_t cgen;
   int32_t cn;
   int64_t clo[3], chi[3];
+  // dilated occupancy bitset of the contact cells over [clo-1, chi+1] (cb_ok = 1 when it fits)
+  int32_t cb_ok, cb_dy, cb_dz, cb_wpr;
 } CloudRec;
 
 typedef struct {
@@ -204,6 +207,7 @@ typedef struct {
   int32_t* cfreel;       // [M*O] free cloud-slot stack
   AssocRec* assoc;       // [M*max_det]
   float* rfrag;          // [M*O*D]
+  float* mu;             // [M*O*D] float(r_frag / |r_frag|) (ApState mu_c), refreshed with r_frag
   uint16_t* views;       // [M*O*(topk+1)*D]
   CloudRec* clouds;      // [M*O]
   float4* cpts;          // [M*O*cap]
@@ -211,6 +215,7 @@ typedef struct {
   uint64_t* chkey;       // [M*O*HC]
   uint32_t* chidx;       // [M*O*HC]
   uint32_t* chgen;       // [M*O*HC]
+  uint32_t* cbits;       // [M*O*2*CB_WORDS] occupancy + dilated bitsets
   uint64_t* ckey;        // [M*O*HCC]
   uint32_t* cgen;        // [M*O*HCC]
   // per-frame scratch
@@ -224,7 +229,7 @@ typedef struct {
   int32_t* obs_list;     // [M*max_det] detection index of observation a
   uint8_t* touched;      // [M*O]  by list position
   uint8_t* obj_hit;      // [M*O]
-  double* pairp;         // [M*max_det*O] association P per (obs, object position)
+  double* gdot;          // [M*max_det*max_det] dot(z_b, z_a) of observations a < b (frame grouping)
   PtsRec* ptsl;          // [M*max_det]
   int32_t* tgt_slot;     // [M*O] cloud-addition targets (object slots)
   unsigned char* work;   // [M*WORK_SLOTS*work_stride]
@@ -232,6 +237,7 @@ typedef struct {
   // merge pass scratch
   double* mcand_p;       // [M*O*8] candidate P
   uint32_t* mcand_ab;    // [M*O*8*2]
+  uint32_t* mcand_key;   // [M*O*8] list positions i << 16 | j (the reference's enumeration order)
   int32_t* mcand_n;      // [M]
   // view-first hash (markView)
   int64_t* vkey;         // [M*view_slots], INT64_MIN = empty
