@@ -32,6 +32,64 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 METRIC = "map-frames/s of scenemap objprob update"
+D_EMB = 1152
+
+
+def alg_bytes(work, D):
+    """Algorithmic HBM bytes per step from the work counters: the per-unit terms of the path's
+    byte count (depth fp32 + label u16 per scanned pixel, bf16 detection embeddings, memory
+    vectors read by association, r_frag fp32 read + write and one fp16 view per update, 20-byte
+    cloud points, int16 log-odds read + write per updated cell, 12-byte scan points, depth
+    pixels read by makeScan).  Per kernel: the terms that kernel moves."""
+    w = work
+    per = {
+        "k_obs": 6 * w["obs_px"],
+        "k_assoc": 2 * D * (w["det"] + w["vec16"]),
+        "k_update": 10 * D * w["upd"],
+        "k_cloud_add": 20 * w["cloud_pts"],
+        "k_grid": 4 * w["scan_px"] + 12 * w["scan_pts"] + 4 * w["cells"],
+    }
+    return per, float(sum(per.values()))
+
+
+def ncu_traffic():
+    """DRAM bytes per launch from the committed ncu summary (profiles/ncu_traffic.txt:
+    '<kernel> <bytes per launch>' lines), or {} when absent."""
+    out = {}
+    pth = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    if os.path.exists(pth):
+        for line in open(pth):
+            f = line.split()
+            if len(f) >= 2 and not line.startswith("#"):
+                try:
+                    out[f[0]] = float(f[1])
+                except ValueError:
+                    pass
+    return out
+
+
+def rooflines(kt, work, step_s, D):
+    peaks_p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_p)) if os.path.exists(peaks_p) else {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    src = "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback 6650 GB/s"
+    per, tot = alg_bytes(work, D)
+    traffic = ncu_traffic()
+    allk = {}
+    for k, b in per.items():
+        if k not in kt or kt[k][1] == 0:
+            continue
+        avg_s = kt[k][0] / kt[k][1] / 1e3
+        allk[k] = {"alg_bytes_per_launch": b, "avg_launch_ms": avg_s * 1e3, "achieved_gbs": b / avg_s / 1e9,
+                   "frac": b / avg_s / 1e9 / hbm}
+    dom = max(allk, key=lambda k: allk[k]["avg_launch_ms"])
+    d = allk[dom]
+    roof = {"kernel": dom, "bound": "hbm", "achieved": d["achieved_gbs"], "peak": hbm, "unit": "GB/s",
+            "frac": d["frac"], "traffic": traffic.get(dom), "alg_bytes_per_launch": d["alg_bytes_per_launch"],
+            "avg_launch_ms": d["avg_launch_ms"], "peak_source": src}
+    step = {"kernel": "whole keyframe chain (all kernels of a step)", "bound": "hbm", "achieved": tot / step_s / 1e9,
+            "peak": hbm, "unit": "GB/s", "frac": tot / step_s / 1e9 / hbm, "alg_bytes_per_step": tot}
+    return roof, step, allk
 UNIT = "map-frames/s"
 
 
@@ -43,7 +101,7 @@ def parse():
     ap.add_argument("--preroll", type=int, default=100)
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--maps", type=int, default=64)
-    ap.add_argument("--max-objects", type=int, default=512)
+    ap.add_argument("--max-objects", type=int, default=1024)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-frames", type=int, default=30, help="CPU baseline: frames per map (untimed lead-in + timed)")
     ap.add_argument("--cpu-timed", type=int, default=10, help="CPU baseline: timed frames per map")
@@ -153,23 +211,6 @@ def cpu_reference(M_sample: int, frames: int, timed: int, threads: int, base_see
 
 
 # ------------------------------------------------------------------ B200 arm
-def k_obs_bytes(wl, R, fi):
-    """Algorithmic bytes of one k_obs launch: depth (4 B) at every scanned pixel and the label
-    (2 B) of the pixel and its 4 erosion neighbours (each label pixel once when sk == 1)."""
-    tot = 0
-    for m in range(wl.M):
-        d = R["dets"][fi * wl.M + m]
-        for k in range(d["n"]):
-            b = d["box"][k]
-            u0, u1 = max(0, int(b[0]) - 1), min(wl.w - 1, int(b[2]) + 1)
-            v0, v1 = max(0, int(b[1]) - 1), min(wl.h - 1, int(b[3]) + 1)
-            box_px = max(0, u1 - u0 + 1) * max(0, v1 - v0 + 1)
-            sk = max(1, int(np.ceil(np.sqrt(box_px / 6000.0))))
-            npx = ((u1 - u0) // sk + 1) * ((v1 - v0) // sk + 1)
-            tot += npx * 4 + (npx * 2 if sk == 1 else npx * 10)
-    return tot
-
-
 def run_b200(args, rank, world, local_rank):
     import torch
     from scenemap_b200 import smg
@@ -198,9 +239,9 @@ def run_b200(args, rank, world, local_rank):
     R = wl.render(f, args.steps, sp)
     keep = []
     structs = [wl.structs(R, fi, keep) for fi in range(args.steps)]
-    obs_bytes = [k_obs_bytes(wl, R, fi) for fi in range(args.steps)]
     B.timing_read()
     B.timing(True)
+    work0 = B.work()
     launches0 = B.launches()
     if world > 1:
         torch.distributed.barrier()
@@ -221,6 +262,8 @@ def run_b200(args, rank, world, local_rank):
     launches = B.launches() - launches0
     kt = B.timing_read()
     B.timing(False)
+    work1 = B.work()
+    work = {k: (work1[k] - work0[k]) / args.steps for k in work0}   # per step (all maps of this GPU)
     err = B.error_word()
     f += args.steps
     del R, structs
@@ -277,7 +320,7 @@ def run_b200(args, rank, world, local_rank):
         all_stats = stats
     n_obj = [len(B.objects(m)) for m in range(min(M, 4))]
     B.close()
-    return dict(t=t, t_e2e=t_e2e, kt=kt, launches=launches, err=err, clocks=clocks, obs_bytes=obs_bytes,
+    return dict(t=t, t_e2e=t_e2e, kt=kt, launches=launches, err=err, clocks=clocks, work=work,
                 stats=all_stats, h2d=h2d, d2h=d2h, n_obj=n_obj)
 
 
@@ -287,7 +330,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     cfg = {"workload": "config 1: 64 box-room maps per GPU, 640x480 fp32 depth + u16 labels, 8-24 dets, "
-                       "1152-d bf16 embeddings, <=512 object slots, 512x512 grid",
+                       f"1152-d bf16 embeddings, <={args.max_objects} object slots, 512x512 grid",
            "maps_per_gpu": args.maps, "frames_timed": f"{args.preroll + args.warmup}..{args.preroll + args.warmup + args.steps - 1}",
            "l2": "fresh frames every step (118 MB/step at 64 maps), no flush", "parallelism": f"dp{world} (maps)"}
     if args.impl == "reference":
@@ -317,23 +360,8 @@ def main():
     K, M = args.steps, args.maps
     value = M * world * K / r["t"]
     e2e = M * world * args.e2e_steps / r["t_e2e"]
-    # roofline of the dominant kernel
-    kt = r["kt"]
-    dom = max(kt, key=lambda k: kt[k][0])
-    ms, n = kt[dom]
-    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
-        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
-    hbm = peaks.get("hbm_gbs", 6650.0)
-    roof = None
-    if dom == "k_obs":
-        avg_s = ms / n / 1e3
-        alg = float(np.mean(r["obs_bytes"]))
-        roof = {"kernel": dom, "bound": "hbm", "achieved": alg / avg_s / 1e9, "peak": hbm, "unit": "GB/s",
-                "frac": alg / avg_s / 1e9 / hbm, "traffic": None, "alg_bytes_per_launch": alg,
-                "avg_launch_ms": ms / n, "peak_source": "MEASURED_PEAKS.json" if peaks else "fallback"}
-    else:
-        roof = {"kernel": dom, "bound": "hbm", "achieved": None, "peak": hbm, "unit": "GB/s", "frac": None,
-                "traffic": None, "avg_launch_ms": ms / n}
+    # roofline: algorithmic bytes from the device work counters (one launch per kernel per step)
+    roof, roof_step, roof_all = rooflines(r["kt"], r["work"], r["t"] / K, D_EMB)
     cb = None
     if not args.no_cpu_baseline and world == 1:
         cores = os.cpu_count() or 1
@@ -342,8 +370,9 @@ def main():
            "ms_per_step": 1e3 * r["t"] / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "f64/f32 (bf16 embeddings)", "data": "synthetic", "config": cfg,
            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
-           "gpu_launches": r["launches"], "roofline": roof, "clocks": r["clocks"],
-           "kernel_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in kt.items()},
+           "gpu_launches": r["launches"], "roofline": roof, "roofline_step": roof_step,
+           "roofline_kernels": roof_all, "work_per_step": r["work"], "clocks": r["clocks"],
+           "kernel_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in r["kt"].items()},
            "device_error_word": r["err"], "objects_first_maps": r["n_obj"],
            "stats_sum": {k: int(v) for k, v in zip(["n_through", "n_obs", "n_wall", "n_wall_name", "n_ceil", "n_floor",
                                                      "n_assoc", "n_new", "n_merge", "n_obj_struct", "n_reenc_req",

@@ -198,6 +198,12 @@ int smg_error_word(smg_batch* b);
 const char* smg_last_error(void);
 /* Number of kernels the library has launched since creation (instrumentation). */
 int64_t smg_kernel_launches(smg_batch* b);
+/* Cumulative work counters summed over the maps of the batch (instrumentation, no reference
+ * counterpart): out[0] pixels scanned by the detection back-projection, [1] detections,
+ * [2] memory vectors read by association in units of D fp16 values (an fp32 r_frag counts 2),
+ * [3] object vector updates, [4] cloud points written, [5] depth pixels read by makeScan,
+ * [6] scan points inserted, [7] occupancy cells updated.  Returns the number of counters. */
+int smg_get_work(smg_batch* b, int64_t* out, int n);
 
 #ifdef __cplusplus
 }

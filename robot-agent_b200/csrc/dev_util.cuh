@@ -479,6 +479,9 @@ DEV double dist3(const double* a, const double* b) {
 }
 
 DEV void set_err(MapRec* m, int bit) { atomicOr(&m->err, bit); }
+DEV void wk_add(MapRec* m, int k, long long v) {
+  if (v) atomicAdd((unsigned long long*)&m->wk[k], (unsigned long long)v);
+}
 
 // event in program order: key = phase << 24 | position
 DEV void push_event(const Batch& B, int map, double t, const ObjRec& o, int kind, uint32_t key) {

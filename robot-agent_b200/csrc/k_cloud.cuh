@@ -161,6 +161,9 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
   float4* pts = B.cpts + cs * B.cap;
   uint32_t* col = B.crgb + cs * B.cap;
   int added = 0;
+  __shared__ int sh_nw;
+  if (tid == 0) sh_nw = 0;
+  __syncthreads();
   for (int c0 = 0; c0 < n; c0 += blockDim.x) {
     const int i = c0 + tid;
     int isnew = 0, last = -1, old = -1;
@@ -184,6 +187,7 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
                     z = (float)((double)xyz[3 * last + 2] - sh_org[2]);
         pts[d] = make_float4(x, y, z, __uint_as_float(sh_seq));
         col[d] = pack_rgb(rgb, last);
+        atomicAdd(&sh_nw, 1);
         if (isnew) W.dst[i] = d;
       }
     }
@@ -194,6 +198,7 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
     if (W.dst[i] >= 0 && INB(W.dst[i], B.cap, 403)) voxel_insert(B, cs, sh_vgen, W.keys[i], (uint32_t)W.dst[i]);
   __syncthreads();
   if (tid == 0) {
+    wk_add(&B.maps[m], SMG_WK_CLOUD, sh_nw);
     C.n = base + added;
     if (C.n > B.cap) { C.n = B.cap; set_err(&B.maps[m], SMG_E_CAP_PTS); }
   }

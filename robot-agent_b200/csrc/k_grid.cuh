@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   const int GW = B.gw_grid, GH = B.gh_grid, X0 = B.gx0, Y0 = B.gy0;
   const size_t gbase = (size_t)m * GW * GH;
   unsigned long long* TOUCH = B.gtouch + gbase;
-  if (tid == 0) ++R->scan_id;
+  if (tid == 0) { ++R->scan_id; wk_add(R, SMG_WK_SCAN_PX, ng); wk_add(R, SMG_WK_SCAN_PTS, npt); }
   __syncthreads();
   const unsigned long long sk = (unsigned long long)(0xffffffffu - R->scan_id) << 32;
   int bad = 0;
@@ -318,6 +318,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   }
   // rays: laser hits (end excluded), free rays (end included) — Bresenham (grid.cpp:236-256)
   const int nray = nhh + nff;
+  int applied_l = 0;
   for (int pass = 0; pass < 2; ++pass) {
     int changed_l = 0;
     for (int r = tid; r < nray; r += blockDim.x) {
@@ -345,6 +346,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
           const int nL = max((int)L + B.q_miss, (int)B.q_min);
           const bool was_seen = *fl & 1;
           *fl |= 1;
+          ++applied_l;
           if (!(nL == L && was_seen)) {
             ++changed_l;
             *Lp = (int16_t)nL;
@@ -382,6 +384,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
         int16_t* Lp = B.gL + gbase + ci;
         uint8_t* fl = B.gflags + gbase + ci;
         const int16_t L = *Lp;
+        ++applied_l;
         const int nL = min((int)L + B.q_hit, (int)B.q_max);
         const bool was_seen = *fl & 1;
         *fl |= 3;
@@ -414,6 +417,8 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     }
     __syncthreads();
   }
+  applied_l = block_sum_i(applied_l, bs);
+  if (tid == 0) wk_add(R, SMG_WK_CELLS, applied_l);
   int16_t* ISw = B.ins_sig + (size_t)m * nb;
   for (int k = tid; k < nb; k += blockDim.x) ISw[k] = SIG[k];
 }

@@ -330,6 +330,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
     if (tid == 0) { O->valid = 0; O->stage = 0; set_err(&B.maps[m], SMG_E_CAP_PTS); }
     return;
   }
+  if (tid == 0) { wk_add(&B.maps[m], SMG_WK_OBS_PX, npix); wk_add(&B.maps[m], SMG_WK_DET, 1); }
   const double* T = F.T_mc;
   // 1. back-projection in raster order (objmap.cpp:667-688), ordered compaction
   int n = 0;

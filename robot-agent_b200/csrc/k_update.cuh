@@ -110,6 +110,7 @@ DEV void ap_add_view(const Batch& B, ObjRec& o, size_t og, const float* z_sh, do
   }
   __syncthreads();
   const double k = sh_k;
+  if (tid == 0) wk_add(&B.maps[og / B.O], SMG_WK_UPD, 1);
   float* r = B.rfrag + og * D;
   uint16_t* vz = B.views + (og * (B.topk + 1) + sh_free) * D;
   for (int i = tid; i < D; i += blockDim.x) {

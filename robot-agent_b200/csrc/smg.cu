@@ -876,4 +876,17 @@ int smg_error_word(smg_batch* b) {
 
 int64_t smg_kernel_launches(smg_batch* b) { return b ? b->launches : -1; }
 
+int smg_get_work(smg_batch* b, int64_t* out, int n) {
+  if (!b || !out || n <= 0) return fail(SMG_ERR_ARGS, "smg_get_work: bad arguments");
+  if (int r = sync_b(b)) return r;
+  std::vector<MapRec> maps((size_t)b->B.M);
+  CK(cudaMemcpy(maps.data(), b->B.maps, sizeof(MapRec) * maps.size(), cudaMemcpyDeviceToHost));
+  for (int k = 0; k < n; ++k) {
+    out[k] = 0;
+    if (k < SMG_WORK_N)
+      for (const MapRec& r : maps) out[k] += r.wk[k];
+  }
+  return SMG_WORK_N;
+}
+
 }  // extern "C"

@@ -147,6 +147,17 @@ typedef struct {
   int32_t pad;
 } EventRec;
 
+// work counters, summed by smg_get_work: the per-unit terms of the algorithmic byte count
+#define SMG_WK_OBS_PX 0      // pixels scanned by the per-detection back-projection (depth + label)
+#define SMG_WK_DET 1         // detections processed
+#define SMG_WK_VEC16 2       // memory vectors read by association, in units of D fp16 values
+#define SMG_WK_UPD 3         // object vector updates (r_frag read + write, one view written)
+#define SMG_WK_CLOUD 4       // cloud points written
+#define SMG_WK_SCAN_PX 5     // depth pixels read by makeScan
+#define SMG_WK_SCAN_PTS 6    // scan points inserted (match cells + laser hits + free rays)
+#define SMG_WK_CELLS 7       // occupancy cells updated (one update per cell per scan)
+#define SMG_WORK_N 8
+
 typedef struct {
   uint32_t next_id;
   int32_t n_obj;
@@ -166,6 +177,8 @@ typedef struct {
   double kf_last_ins[3];
   uint32_t scan_id;
   int32_t view_n;
+  // cumulative work counters (algorithmic traffic of the path; see SMG_WK_*)
+  long long wk[SMG_WORK_N];
 } MapRec;
 
 // ObjectMap::lastAssoc entry (DetAssoc, objmap.hpp:194-199)

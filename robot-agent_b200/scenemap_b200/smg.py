@@ -73,6 +73,7 @@ def lib():
         L.smg_timing_read.argtypes = [vp, vp, vp, vp]
         L.smg_kernel_launches.restype = C.c_int64
         L.smg_kernel_launches.argtypes = [vp]
+        L.smg_get_work.argtypes = [vp, C.POINTER(C.c_int64), C.c_int]
         _lib = L
     return _lib
 
@@ -80,7 +81,8 @@ def lib():
 EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "smg_params_apply", "smg_create", "smg_destroy", "smg_push_frames",
             "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
             "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
-            "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read"]
+            "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
+           "smg_get_work"]
 
 NUM_KERNELS = 14
 
@@ -279,3 +281,11 @@ class Batch:
 
     def launches(self) -> int:
         return int(lib().smg_kernel_launches(self.h))
+
+    WORK_KEYS = ("obs_px", "det", "vec16", "upd", "cloud_pts", "scan_px", "scan_pts", "cells")
+
+    def work(self) -> dict:
+        """Cumulative work counters (smg_get_work) as a dict keyed by WORK_KEYS."""
+        out = (C.c_int64 * len(self.WORK_KEYS))()
+        _check(lib().smg_get_work(self.h, out, len(self.WORK_KEYS)), "smg_get_work")
+        return dict(zip(self.WORK_KEYS, (int(v) for v in out)))
