@@ -205,6 +205,18 @@ int64_t smg_kernel_launches(smg_batch* b);
  * [6] scan points inserted, [7] occupancy cells updated.  Returns the number of counters. */
 int smg_get_work(smg_batch* b, int64_t* out, int n);
 
+/* Batched plane fit: replaces scenemap::apPlaneFit (objprob.hpp:204, objprob.cpp:130-209), one
+ * call per point set there.  Set s is the float (x, y, z) points xyz[3*off[s] .. 3*off[s+1]),
+ * fitted with distance tau and RANSAC seed seeds[s] (apSeed values), at most max_iters
+ * (1..256) hypotheses.  out[10*s .. 10*s+9] = ok, n[0..2], thick, inl, zmed, zlo, zhi, hspan;
+ * an unfitted set gets the reference's ApPlane defaults (ok 0, n = (0,0,1), thick 1, rest 0)
+ * and a set with malformed offsets gets ok = -1.  n_points = off[n_sets].  xyz, off, seeds and
+ * out are device memory; the call is asynchronous on `stream`.  Scratch of 16 bytes per point
+ * is allocated and freed stream-ordered (cudaMallocAsync) inside the call, and a 1 MB
+ * iteration table is allocated once per device on first use. */
+int smg_plane_fit(const float* xyz, const int32_t* off, int n_sets, int n_points, double tau, const uint64_t* seeds,
+                  int max_iters, double* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -258,3 +258,70 @@ class RefMap:
         c8 = np.zeros((h, w), np.int8)
         L.ref_grid_cells(self._h, _p(Lq, C.c_int16), _p(seen, C.c_uint8), _p(c8, C.c_int8))
         return dict(x0=x0, y0=y0, w=w, h=h, L=Lq, seen=seen, c8=c8)
+
+
+# ---------------------------------------------------------------- C restatement (port/)
+_port = None
+
+
+def port_available() -> bool:
+    return os.path.exists(PORT_SO)
+
+
+def port_lib():
+    global _port
+    if _port is None:
+        L = C.CDLL(PORT_SO)
+        P = C.POINTER
+        L.op_ap_seed.restype = C.c_uint64
+        L.op_ap_seed.argtypes = [C.c_uint64, C.c_uint64]
+        L.op_f2h.restype = C.c_uint16
+        L.op_f2h.argtypes = [C.c_float]
+        L.op_h2f.restype = C.c_float
+        L.op_h2f.argtypes = [C.c_uint16]
+        L.op_to_f16.argtypes = [P(C.c_float), P(C.c_uint16), C.c_int]
+        L.op_voxel_key.restype = C.c_uint64
+        L.op_voxel_key.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
+        L.op_contact.restype = C.c_double
+        L.op_contact.argtypes = [P(C.c_float), C.c_int, P(C.c_float), C.c_int, C.c_double]
+        L.op_plane_fit.argtypes = [P(C.c_float), C.c_int, C.c_double, C.c_uint64, C.c_int, P(C.c_double)]
+        L.op_fast_atan2.restype = C.c_float
+        L.op_fast_atan2.argtypes = [C.c_float, C.c_float]
+        _port = L
+    return _port
+
+
+def plane_fit(xyz, tau: float, seed: int, max_iters: int = 64, impl: str = "port") -> np.ndarray:
+    """apPlaneFit of an (n, 3) float32 cloud: 10 doubles (ok, n0, n1, n2, thick, inl, zmed, zlo,
+    zhi, hspan) from the restatement (impl="port") or the compiled reference (impl="ref")."""
+    a = np.ascontiguousarray(xyz, np.float32).reshape(-1, 3)
+    out = np.zeros(10, np.float64)
+    if impl == "port":
+        port_lib().op_plane_fit(_p(a, C.c_float), len(a), tau, seed, max_iters, _p(out, C.c_double))
+    else:
+        ref_lib().ref_plane_fit(_p(a, C.c_float), len(a), tau, seed, max_iters, _p(out, C.c_double))
+    return out
+
+
+def ap_seed(a: int, b: int, impl: str = "port") -> int:
+    return int(port_lib().op_ap_seed(a, b) if impl == "port" else ref_lib().ref_ap_seed(a, b))
+
+
+def contact(cloud, pts, cell: float, impl: str = "port") -> float:
+    c = np.ascontiguousarray(cloud, np.float32).reshape(-1, 3)
+    p = np.ascontiguousarray(pts, np.float32).reshape(-1, 3)
+    fn = port_lib().op_contact if impl == "port" else ref_lib().ref_contact
+    return float(fn(_p(c, C.c_float), len(c), _p(p, C.c_float), len(p), cell))
+
+
+def to_f16(x, impl: str = "port") -> np.ndarray:
+    a = np.ascontiguousarray(x, np.float32).reshape(-1)
+    out = np.zeros(len(a), np.uint16)
+    fn = port_lib().op_to_f16 if impl == "port" else ref_lib().ref_to_f16
+    fn(_p(a, C.c_float), _p(out, C.c_uint16), len(a))
+    return out
+
+
+def voxel_key(x: float, y: float, z: float, inv: float, impl: str = "port") -> int:
+    fn = port_lib().op_voxel_key if impl == "port" else ref_lib().ref_voxel_key
+    return int(fn(x, y, z, inv))

@@ -167,24 +167,30 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     __syncthreads();
     return;
   }
-  // two PCA refits (objprob.cpp:166-180); mp = plane whose inliers the last pass used
+  // two PCA refits (objprob.cpp:166-180); mp = plane whose inliers the last pass used.
+  // Sums are block trees.  Where the outcome is ill-conditioned in the reference's own rounding
+  // (a point within 1e-11 of the tau boundary, a near-double smallest eigenvalue or a near-zero
+  // one, a nearly isotropic horizontal spread), thread 0 replays the whole refit with the
+  // reference's sequential sums in index order, so the result is the reference's bit for bit.
+  __shared__ int sh_deg, sh_ni, sh_ok;
+  __shared__ double sh_mp[4], sh_hc, sh_hs;
+  if (tid == 0) sh_deg = 0;
   double pl[4] = {sh_best[0], sh_best[1], sh_best[2], sh_best[3]};
   double mp[4];
   int ni = 0;
   for (int pass = 0; pass < 2; ++pass) {
     for (int k = 0; k < 4; ++k) mp[k] = pl[k];
-    double sm[4] = {0, 0, 0, 0};   // count, sum x, sum y, sum z
+    double sm[5] = {0, 0, 0, 0, 0};   // count, sum x, sum y, sum z, near-boundary points
     for (int i = tid; i < n; i += blockDim.x) {
       const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
-      if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) { sm[0] += 1.0; sm[1] += x; sm[2] += y; sm[3] += z; }
+      const double dd = fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]);
+      if (dd <= tau) { sm[0] += 1.0; sm[1] += x; sm[2] += y; sm[3] += z; }
+      if (fabs(dd - tau) <= 1e-11) sm[4] += 1.0;
     }
-    block_sum_multi<4>(sm, red);
+    block_sum_multi<5>(sm, red);
     ni = (int)sm[0];
-    if (ni < 3) {
-      if (tid == 0) out->ok = 0;
-      __syncthreads();
-      return;
-    }
+    if (sm[4] > 0 && tid == 0) sh_deg = 1;
+    if (ni < 3) break;
     const double inv = 1.0 / (double)(ni > 1 ? ni : 1);
     double m[3] = {sm[1], sm[2], sm[3]};
     for (int k = 0; k < 3; ++k) m[k] *= inv;
@@ -210,25 +216,98 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
         sh_m[i] = m[i];
         for (int j = 0; j < 3; ++j) sh_V[i][j] = V[i][j];
       }
+      if (ev[1] - ev[0] <= 1e-3 * ev[2] || ev[0] <= 1e-12 * ev[2]) sh_deg = 1;
     }
     __syncthreads();
     pl[0] = sh_V[0][0]; pl[1] = sh_V[1][0]; pl[2] = sh_V[2][0];
     pl[3] = -(pl[0] * sh_m[0] + pl[1] * sh_m[1] + pl[2] * sh_m[2]);
   }
-  const double m0 = sh_m[0], m1 = sh_m[1];
-  // horizontal principal direction of the inliers (objprob.cpp:187-192)
-  double a0 = 0, a1 = 0, a2 = 0;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
-    if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) {
-      const double dx = x - m0, dy = y - m1;
-      a0 += dx * dx; a1 += dx * dy; a2 += dy * dy;
+  double th_hc = 0, th_hs = 0;
+  if (ni >= 3) {
+    const double m0 = sh_m[0], m1 = sh_m[1];
+    // horizontal principal direction of the inliers (objprob.cpp:187-192)
+    double a3[3] = {0, 0, 0};
+    for (int i = tid; i < n; i += blockDim.x) {
+      const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
+      if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) {
+        const double dx = x - m0, dy = y - m1;
+        a3[0] += dx * dx; a3[1] += dx * dy; a3[2] += dy * dy;
+      }
     }
+    block_sum_multi<3>(a3, red);
+    const double sxx = a3[0], sxy = a3[1], syy = a3[2];
+    if (tid == 0 && 2 * fabs(sxy) + fabs(sxx - syy) <= 1e-3 * (sxx + syy)) sh_deg = 1;
+    const double th = 0.5 * atan2(2 * sxy, sxx - syy);
+    th_hc = cos(th);
+    th_hs = sin(th);
   }
-  double hs3[3] = {a0, a1, a2};
-  block_sum_multi<3>(hs3, red);
-  const double sxx = hs3[0], sxy = hs3[1], syy = hs3[2];
-  const double th = 0.5 * atan2(2 * sxy, sxx - syy), hc = cos(th), hs = sin(th);
+  __syncthreads();
+  if (sh_deg) {   // exact replay in the reference's order (pcaOf objprob.cpp:101-114, :166-192)
+    if (tid == 0) {
+      double q[4] = {sh_best[0], sh_best[1], sh_best[2], sh_best[3]}, qm[4] = {0, 0, 0, 0};
+      double m[3] = {0, 0, 0}, ev[3] = {0, 0, 0}, V[3][3];
+      int nin = 0;
+      for (int pass = 0; pass < 2 && (pass == 0 || nin >= 3); ++pass) {
+        for (int k = 0; k < 4; ++k) qm[k] = q[k];
+        nin = 0;
+        m[0] = m[1] = m[2] = 0;
+        for (int i = 0; i < n; ++i)
+          if (fabs(qm[0] * xyz[3 * i] + qm[1] * xyz[3 * i + 1] + qm[2] * xyz[3 * i + 2] + qm[3]) <= tau) {
+            ++nin;
+            for (int k = 0; k < 3; ++k) m[k] += xyz[3 * i + k];
+          }
+        if (nin < 3) break;
+        const double inv = 1.0 / (double)(nin > 1 ? nin : 1);
+        for (int k = 0; k < 3; ++k) m[k] *= inv;
+        double C[3][3] = {{0, 0, 0}, {0, 0, 0}, {0, 0, 0}};
+        for (int i = 0; i < n; ++i)
+          if (fabs(qm[0] * xyz[3 * i] + qm[1] * xyz[3 * i + 1] + qm[2] * xyz[3 * i + 2] + qm[3]) <= tau) {
+            const double d[3] = {xyz[3 * i] - m[0], xyz[3 * i + 1] - m[1], xyz[3 * i + 2] - m[2]};
+            for (int r = 0; r < 3; ++r)
+              for (int cc = 0; cc < 3; ++cc) C[r][cc] += d[r] * d[cc];
+          }
+        for (int r = 0; r < 3; ++r)
+          for (int cc = 0; cc < 3; ++cc) C[r][cc] *= inv;
+        eig_sym3(C, ev, V);
+        q[0] = V[0][0]; q[1] = V[1][0]; q[2] = V[2][0];
+        q[3] = -(q[0] * m[0] + q[1] * m[1] + q[2] * m[2]);
+      }
+      sh_ok = nin >= 3;
+      sh_ni = nin;
+      if (nin >= 3) {
+        double sxx = 0, sxy = 0, syy = 0;
+        for (int i = 0; i < n; ++i)
+          if (fabs(qm[0] * xyz[3 * i] + qm[1] * xyz[3 * i + 1] + qm[2] * xyz[3 * i + 2] + qm[3]) <= tau) {
+            const double dx = xyz[3 * i] - m[0], dy = xyz[3 * i + 1] - m[1];
+            sxx += dx * dx; sxy += dx * dy; syy += dy * dy;
+          }
+        const double th = 0.5 * atan2(2 * sxy, sxx - syy);
+        sh_hc = cos(th);
+        sh_hs = sin(th);
+        for (int i = 0; i < 3; ++i) {
+          sh_ev[i] = ev[i];
+          sh_m[i] = m[i];
+          for (int j = 0; j < 3; ++j) sh_V[i][j] = V[i][j];
+        }
+        for (int k = 0; k < 4; ++k) sh_mp[k] = qm[k];
+      }
+    }
+    __syncthreads();
+    if (!sh_ok) {
+      if (tid == 0) out->ok = 0;
+      __syncthreads();
+      return;
+    }
+    ni = sh_ni;
+    for (int k = 0; k < 4; ++k) mp[k] = sh_mp[k];
+    th_hc = sh_hc;
+    th_hs = sh_hs;
+  } else if (ni < 3) {
+    if (tid == 0) out->ok = 0;
+    __syncthreads();
+    return;
+  }
+  const double m0 = sh_m[0], m1 = sh_m[1], hc = th_hc, hs = th_hs;
   // z and horizontal-span projections of the inliers -> exact percentiles (objprob.cpp:193-206)
   __shared__ int sh_cnt;
   if (tid == 0) sh_cnt = 0;

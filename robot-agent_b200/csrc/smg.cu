@@ -22,10 +22,13 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <vector>
 
 #include "k_grid.cuh"
+
+#define PF_THREADS 256   // CTA size of the batched plane fit (the block sums' tree follows it)
 
 static thread_local std::string g_err;
 static int fail(int code, const char* msg) {
@@ -249,6 +252,21 @@ int smg_destroy(smg_batch* b) {
   return SMG_OK;
 }
 
+// RANSAC adaptive-iteration table (host libm, like the reference): need = max(8,
+// ceil(log(0.01) / log(1 - w^3))) for w = cnt / nsamp; 0 where the reference does not update it.
+static const std::vector<int32_t>& need_table() {
+  static const std::vector<int32_t> tab = [] {
+    std::vector<int32_t> need((size_t)NEED_N * NEED_N, 0);
+    for (int ns = 1; ns < NEED_N; ++ns)
+      for (int c = 0; c <= ns; ++c) {
+        const double w = double(c) / double(ns), pw = w * w * w;
+        need[(size_t)ns * NEED_N + c] = pw > 1e-9 && pw <= 0.999999 ? std::max(8, int(std::ceil(std::log(0.01) / std::log(1.0 - pw)))) : 0;
+      }
+    return need;
+  }();
+  return tab;
+}
+
 static int pow2_at_least(long long n) {
   int v = 1;
   while (v < n) v <<= 1;
@@ -395,13 +413,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
     std::vector<CloudRec> cl(MO);
     for (auto& c : cl) { memset(&c, 0, sizeof(c)); c.vgen = 1; c.cgen = 1; c.cver = 0xffffffffu; }
     CK(cudaMemcpy(B.clouds, cl.data(), sizeof(CloudRec) * MO, cudaMemcpyHostToDevice));
-    // RANSAC adaptive-iteration table: need = max(8, ceil(log(0.01)/log(1-w^3))) for w = cnt/nsamp
-    std::vector<int32_t> need((size_t)NEED_N * NEED_N, 0);
-    for (int ns = 1; ns < NEED_N; ++ns)
-      for (int c = 0; c <= ns; ++c) {
-        const double w = double(c) / double(ns), pw = w * w * w;
-        need[(size_t)ns * NEED_N + c] = pw > 1e-9 && pw <= 0.999999 ? std::max(8, int(std::ceil(std::log(0.01) / std::log(1.0 - pw)))) : 0;
-      }
+    const std::vector<int32_t>& need = need_table();
     CK(cudaMemcpy(B.need_tab, need.data(), sizeof(int32_t) * need.size(), cudaMemcpyHostToDevice));
     // export8 / probability LUTs (grid.cpp:118-123)
     std::vector<int8_t> l8(nlut);
@@ -875,6 +887,80 @@ int smg_error_word(smg_batch* b) {
 }
 
 int64_t smg_kernel_launches(smg_batch* b) { return b ? b->launches : -1; }
+
+// ------------------------------------------------------------------ batched apPlaneFit
+// One CTA per point set; the set's scratch (z and horizontal-projection lists of its inliers,
+// 2 doubles per point) starts at 2 * off[s] doubles.  Output row (10 doubles): ok, n[3], thick,
+// inl, zmed, zlo, zhi, hspan; a set that is not fitted gets the reference's ApPlane defaults.
+__global__ void __launch_bounds__(PF_THREADS) k_plane_sets(const float* xyz, const int32_t* off, int n_sets, int n_points,
+                                                            double tau, const uint64_t* seeds, int max_iters,
+                                                            const int32_t* need_tab, double* scr, double* out) {
+  __shared__ BlockScratch bs;
+  __shared__ int hist[SEL_MAXQ * 256];
+  __shared__ PlaneOut po;
+  const int s = blockIdx.x;
+  if (s >= n_sets) return;
+  const int a = off[s], e = off[s + 1];
+  double* o = out + 10 * (size_t)s;
+  if (a < 0 || e < a || e > n_points) {   // malformed offsets: ok = -1
+    if (threadIdx.x == 0) { o[0] = -1; for (int k = 1; k < 10; ++k) o[k] = 0; }
+    return;
+  }
+  const int n = e - a;
+  plane_fit(xyz + 3 * (size_t)a, n, tau, seeds[s], max_iters, need_tab, scr + 2 * (size_t)a, n, hist, bs, &po);
+  if (threadIdx.x == 0) {
+    const double dflt[10] = {0, 0, 0, 1, 1, 0, 0, 0, 0, 0};
+    if (!po.ok) {
+      for (int k = 0; k < 10; ++k) o[k] = dflt[k];
+    } else {
+      o[0] = 1; o[1] = po.n[0]; o[2] = po.n[1]; o[3] = po.n[2]; o[4] = po.thick; o[5] = po.inl;
+      o[6] = po.zmed; o[7] = po.zlo; o[8] = po.zhi; o[9] = po.hspan;
+    }
+  }
+}
+
+static int plane_args(const float* xyz, const int32_t* off, int n_sets, int n_points, double tau, const uint64_t* seeds,
+                      int max_iters, double* out, const char* who) {
+  if (!xyz || !off || !seeds || !out || n_sets <= 0 || n_points < 0 || !(tau > 0) || max_iters < 1)
+    return fail(SMG_ERR_ARGS, (std::string(who) + ": bad arguments").c_str());
+  if (max_iters > RANSAC_MAX)
+    return fail(SMG_ERR_ARGS, (std::string(who) + ": max_iters above " + std::to_string(RANSAC_MAX)).c_str());
+  return SMG_OK;
+}
+
+// Per-device RANSAC table for smg_plane_fit, allocated once and kept until exit.
+static int plane_need_table(int dev, const int32_t** out) {
+  static std::mutex mu;
+  static std::vector<int32_t*> tabs;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)tabs.size() <= dev) tabs.resize((size_t)dev + 1, nullptr);
+  if (!tabs[(size_t)dev]) {
+    const std::vector<int32_t>& need = need_table();
+    int32_t* p = nullptr;
+    CK(cudaMalloc(&p, sizeof(int32_t) * need.size()));
+    CK(cudaMemcpy(p, need.data(), sizeof(int32_t) * need.size(), cudaMemcpyHostToDevice));
+    tabs[(size_t)dev] = p;
+  }
+  *out = tabs[(size_t)dev];
+  return SMG_OK;
+}
+
+int smg_plane_fit(const float* xyz, const int32_t* off, int n_sets, int n_points, double tau, const uint64_t* seeds,
+                  int max_iters, double* out, void* stream) {
+  if (int r = plane_args(xyz, off, n_sets, n_points, tau, seeds, max_iters, out, "smg_plane_fit")) return r;
+  cudaStream_t st = (cudaStream_t)stream;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const int32_t* need = nullptr;
+  if (int r = plane_need_table(dev, &need)) return r;
+  double* scr = nullptr;
+  CK(cudaMallocAsync(&scr, sizeof(double) * 2 * (size_t)std::max(n_points, 1), st));
+  k_plane_sets<<<n_sets, PF_THREADS, 0, st>>>(xyz, off, n_sets, n_points, tau, seeds, max_iters, need, scr, out);
+  const cudaError_t le = cudaGetLastError();
+  CK(cudaFreeAsync(scr, st));
+  CK(le);
+  return SMG_OK;
+}
 
 int smg_get_work(smg_batch* b, int64_t* out, int n) {
   if (!b || !out || n <= 0) return fail(SMG_ERR_ARGS, "smg_get_work: bad arguments");

@@ -74,6 +74,7 @@ def lib():
         L.smg_kernel_launches.restype = C.c_int64
         L.smg_kernel_launches.argtypes = [vp]
         L.smg_get_work.argtypes = [vp, C.POINTER(C.c_int64), C.c_int]
+        L.smg_plane_fit.argtypes = [vp, vp, C.c_int, C.c_int, C.c_double, vp, C.c_int, vp, vp]
         _lib = L
     return _lib
 
@@ -82,7 +83,7 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
             "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
             "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
             "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
-           "smg_get_work"]
+           "smg_get_work", "smg_plane_fit"]
 
 NUM_KERNELS = 14
 
@@ -289,3 +290,26 @@ class Batch:
         out = (C.c_int64 * len(self.WORK_KEYS))()
         _check(lib().smg_get_work(self.h, out, len(self.WORK_KEYS)), "smg_get_work")
         return dict(zip(self.WORK_KEYS, (int(v) for v in out)))
+
+
+def plane_fit(clouds, tau, seeds, max_iters=64, device="cuda:0", entry="smg_plane_fit"):
+    """apPlaneFit on a list of (n, 3) float32 point sets through the batched C entry point.
+
+    Returns an (n_sets, 10) float64 array: ok, n0, n1, n2, thick, inl, zmed, zlo, zhi, hspan.
+    `entry` names the C entry point (same signature)."""
+    import numpy as np
+    import torch
+    dev = torch.device(device)
+    pts = [np.ascontiguousarray(c, dtype=np.float32).reshape(-1, 3) for c in clouds]
+    off = np.zeros(len(pts) + 1, np.int32)
+    off[1:] = np.cumsum([len(p) for p in pts])
+    xyz = torch.from_numpy(np.concatenate(pts) if pts else np.zeros((0, 3), np.float32)).to(dev)
+    off_d = torch.from_numpy(off).to(dev)
+    seeds_d = torch.from_numpy(np.asarray(seeds, np.uint64).view(np.int64)).to(dev)
+    out = torch.empty((len(pts), 10), dtype=torch.float64, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    fn = getattr(lib(), entry)
+    _check(fn(C.c_void_p(xyz.data_ptr()), C.c_void_p(off_d.data_ptr()), len(pts), int(off[-1]), float(tau),
+              C.c_void_p(seeds_d.data_ptr()), int(max_iters), C.c_void_p(out.data_ptr()), C.c_void_p(st)), entry)
+    torch.cuda.synchronize(dev)
+    return out.cpu().numpy()
