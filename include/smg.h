@@ -217,6 +217,22 @@ int smg_get_work(smg_batch* b, int64_t* out, int n);
 int smg_plane_fit(const float* xyz, const int32_t* off, int n_sets, int n_points, double tau, const uint64_t* seeds,
                   int max_iters, double* out, void* stream);
 
+/* smg_plane_fit without any device allocation.  No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory while they run, such as a robot's real-time frame
+ * loop that reserves all of its GPU memory at start-up (cudaMalloc and cudaMallocAsync can
+ * block, synchronise or fail against a fixed memory budget in the middle of a frame) or a
+ * plugin host whose per-frame step forbids allocation.  Same arguments and results as
+ * smg_plane_fit; the caller still provides xyz, off, seeds and out in device memory.
+ * Limit: n_points <= 65536 per call (SMG_ERR_CAPACITY with a message otherwise).  The scratch
+ * (1 MiB) and the iteration table (1 MiB) are static device arrays of the library, held on
+ * every GPU that loads it until the process exits.  The first call on each device does a
+ * one-time set-up on that device (address look-up and a synchronous table copy), so make that
+ * first call before any stream capture.  All calls share the one scratch array: calls that
+ * can overlap on the GPU (other streams, other host threads) race and must be serialised by
+ * the caller.  Nothing in the scratch needs to start at zero, so no call clears it. */
+int smg_plane_fit_noalloc(const float* xyz, const int32_t* off, int n_sets, int n_points, double tau,
+                          const uint64_t* seeds, int max_iters, double* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -962,6 +962,65 @@ int smg_plane_fit(const float* xyz, const int32_t* off, int n_sets, int n_points
   return SMG_OK;
 }
 
+// ------------------------------------------------------------------ plane fit, no allocation
+// smg_plane_fit_noalloc runs k_plane_sets on scratch that lives in this module's own static
+// device memory, for callers that must not allocate device memory while they run.  The arrays
+// exist on every GPU where the library is loaded, from load until process exit.  In host code
+// their names are host-side shadows, not device addresses, so the kernel receives addresses
+// obtained with cudaGetSymbolAddress on the current device.
+#define SMG_PF_STATIC_POINTS 65536
+static __device__ __align__(256) double g_pf_scratch[2 * SMG_PF_STATIC_POINTS];   // 1 MiB
+static __device__ __align__(256) int32_t g_pf_need[NEED_N * NEED_N];              // 1 MiB
+
+struct PfStaticDevice {
+  bool ready = false;
+  double* scratch = nullptr;
+  int32_t* need = nullptr;
+};
+
+// Once per device, with that device current: resolve the device addresses of the static
+// arrays and fill the constant iteration table (a synchronous copy, no allocation).
+static int pf_static_setup(int dev, PfStaticDevice* out) {
+  static std::mutex mu;
+  static std::vector<PfStaticDevice> devs;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)devs.size() <= dev) devs.resize((size_t)dev + 1);
+  PfStaticDevice& d = devs[(size_t)dev];
+  if (!d.ready) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_pf_scratch);
+    if (e != cudaSuccess) return fail(SMG_ERR_DEVICE, (std::string("smg_plane_fit_noalloc: cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e)).c_str());
+    d.scratch = (double*)p;
+    e = cudaGetSymbolAddress(&p, g_pf_need);
+    if (e != cudaSuccess) return fail(SMG_ERR_DEVICE, (std::string("smg_plane_fit_noalloc: cudaGetSymbolAddress(table): ") + cudaGetErrorString(e)).c_str());
+    d.need = (int32_t*)p;
+    const std::vector<int32_t>& need = need_table();
+    CK(cudaMemcpyToSymbol(g_pf_need, need.data(), sizeof(int32_t) * need.size()));
+    d.ready = true;
+  }
+  *out = d;
+  return SMG_OK;
+}
+
+int smg_plane_fit_noalloc(const float* xyz, const int32_t* off, int n_sets, int n_points, double tau,
+                          const uint64_t* seeds, int max_iters, double* out, void* stream) {
+  if (int r = plane_args(xyz, off, n_sets, n_points, tau, seeds, max_iters, out, "smg_plane_fit_noalloc")) return r;
+  if (n_points > SMG_PF_STATIC_POINTS)
+    return fail(SMG_ERR_CAPACITY, ("smg_plane_fit_noalloc: n_points " + std::to_string(n_points) +
+                                   " exceeds the static scratch limit of " + std::to_string(SMG_PF_STATIC_POINTS) +
+                                   " points per call (use smg_plane_fit)").c_str());
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  PfStaticDevice d;
+  if (int r = pf_static_setup(dev, &d)) return r;
+  // Nothing in the scratch has to start at zero: every entry a set reads (its inliers' z and
+  // horizontal projections) is written earlier in the same launch, so no clearing is needed.
+  k_plane_sets<<<n_sets, PF_THREADS, 0, (cudaStream_t)stream>>>(xyz, off, n_sets, n_points, tau, seeds, max_iters, d.need,
+                                                                  d.scratch, out);
+  CK(cudaGetLastError());
+  return SMG_OK;
+}
+
 int smg_get_work(smg_batch* b, int64_t* out, int n) {
   if (!b || !out || n <= 0) return fail(SMG_ERR_ARGS, "smg_get_work: bad arguments");
   if (int r = sync_b(b)) return r;

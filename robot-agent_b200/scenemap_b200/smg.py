@@ -75,6 +75,7 @@ def lib():
         L.smg_kernel_launches.argtypes = [vp]
         L.smg_get_work.argtypes = [vp, C.POINTER(C.c_int64), C.c_int]
         L.smg_plane_fit.argtypes = [vp, vp, C.c_int, C.c_int, C.c_double, vp, C.c_int, vp, vp]
+        L.smg_plane_fit_noalloc.argtypes = [vp, vp, C.c_int, C.c_int, C.c_double, vp, C.c_int, vp, vp]
         _lib = L
     return _lib
 
@@ -83,7 +84,7 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
             "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
             "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
             "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
-           "smg_get_work", "smg_plane_fit"]
+           "smg_get_work", "smg_plane_fit", "smg_plane_fit_noalloc"]
 
 NUM_KERNELS = 14
 
@@ -296,7 +297,8 @@ def plane_fit(clouds, tau, seeds, max_iters=64, device="cuda:0", entry="smg_plan
     """apPlaneFit on a list of (n, 3) float32 point sets through the batched C entry point.
 
     Returns an (n_sets, 10) float64 array: ok, n0, n1, n2, thick, inl, zmed, zlo, zhi, hspan.
-    `entry` names the C entry point (same signature)."""
+    `entry` names the C entry point: "smg_plane_fit" (stream-ordered scratch allocation) or
+    "smg_plane_fit_noalloc" (static scratch, no device allocation, <= 65536 points)."""
     import numpy as np
     import torch
     dev = torch.device(device)
