@@ -205,6 +205,61 @@ int64_t smg_kernel_launches(smg_batch* b);
  * [6] scan points inserted, [7] occupancy cells updated.  Returns the number of counters. */
 int smg_get_work(smg_batch* b, int64_t* out, int n);
 
+/* ---- standalone occupancy grid + correlative scan matching ---- */
+/* GridParams (scenemap grid.hpp:18-21) plus the probability clamp of OccGrid::prob
+ * (grid.hpp:75: pmin 0.1, pmax 0.9; unseen cells read pmin). */
+typedef struct smg_occ_params {
+  float res, l_hit, l_miss, l_min, l_max, pmin, pmax;
+} smg_occ_params;
+
+/* Scan2 (scenemap scan.hpp:50-58), host memory: sensor origin, match points (+ optional
+ * normals), laser hits (ray end excluded from the misses) and free-ray ends (included), all in
+ * the base frame.  Only the laser hits take part in scan matching. */
+typedef struct smg_scan2 {
+  float ox, oy;
+  int32_t n_match;
+  const float *mx, *my, *mnx, *mny;
+  int32_t n_hit;
+  const float *hx, *hy;
+  int32_t n_free;
+  const float *fx, *fy;
+} smg_scan2;
+
+/* Real-time correlative search (the reference configures Cartographer's, slam_carto/config/
+ * carto_2d.lua:17-21): offsets of -W..W in x and y in steps of linear_step (must equal the
+ * grid resolution: offsets are whole cells), rotations -A..A in steps of angular_step (rad),
+ * candidate weight exp(-(|t| * translation_weight + |dth| * rotation_weight)^2). */
+typedef struct smg_csm_params {
+  double linear_window, angular_window, linear_step, angular_step, translation_weight, rotation_weight;
+} smg_csm_params;
+
+typedef struct smg_occ smg_occ;
+
+/* n_maps independent grids, each a fixed window of grid_w x grid_h cells (<= 4096 per side)
+ * starting at global cell (grid_x0, grid_y0).  Replaces `OccGrid(p)` (grid.hpp:23), which
+ * grows on demand: here a point outside the window fails that grid's insert.  max_points
+ * bounds match + hit + free points per scan (<= 65536). */
+int smg_occ_create(const smg_occ_params* p, int n_maps, int grid_w, int grid_h, int grid_x0, int grid_y0, int max_points,
+                   int dev, smg_occ** out);
+int smg_occ_destroy(smg_occ* o);
+/* OccGrid::insert(scan, pose) (grid.cpp:195-259) for grids 0..n-1; poses = n x (x, y, th).
+ * changed_out (n, or NULL): the reference's return value (cells whose log-odds or seen flag
+ * changed), -1 if the scan left the window (the grid is then unchanged).  With changed_out
+ * NULL the call is asynchronous on `stream`. */
+int smg_occ_insert(smg_occ* o, const smg_scan2* scans, const double* poses, int n, int32_t* changed_out, void* stream);
+/* Correlative scan match of each scan's hits around pose0 (n x (x, y, th)) against the
+ * current grid: best pose (n x 3), candidate index ((rotation * n_x + x offset) * n_y + y
+ * offset, lowest index on ties) and weighted score.  Replaces Cartographer's
+ * RealTimeCorrelativeScanMatcher2D::Match as configured by the reference. */
+int smg_occ_match(smg_occ* o, const smg_scan2* scans, const double* pose0, const smg_csm_params* c, int n, double* pose_out,
+                  int32_t* index_out, double* score_out, void* stream);
+/* Match, then insert each scan at its matched pose (one scan-matching front-end step). */
+int smg_occ_track(smg_occ* o, const smg_scan2* scans, const double* pose0, const smg_csm_params* c, int n, double* pose_out,
+                  int32_t* index_out, double* score_out, int32_t* changed_out, void* stream);
+/* Cells of grid m (row-major grid_w x grid_h): log-odds x 256, seen, export8 value (-1
+ * unknown, 0..100), and the matcher's quantised probability; any pointer may be NULL. */
+int smg_occ_get_cells(smg_occ* o, int m, int16_t* L, uint8_t* seen, int8_t* c8, uint16_t* q);
+
 /* Batched plane fit: replaces scenemap::apPlaneFit (objprob.hpp:204, objprob.cpp:130-209), one
  * call per point set there.  Set s is the float (x, y, z) points xyz[3*off[s] .. 3*off[s+1]),
  * fitted with distance tau and RANSAC seed seeds[s] (apSeed values), at most max_iters

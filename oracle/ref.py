@@ -325,3 +325,75 @@ def to_f16(x, impl: str = "port") -> np.ndarray:
 def voxel_key(x: float, y: float, z: float, inv: float, impl: str = "port") -> int:
     fn = port_lib().op_voxel_key if impl == "port" else ref_lib().ref_voxel_key
     return int(fn(x, y, z, inv))
+
+
+# ---------------------------------------------------------------- config 3: grid + matcher
+def _lround(x: np.ndarray) -> np.ndarray:
+    """C lround for x >= 0 (halves away from zero), exact: floor, then compare the remainder."""
+    r = np.floor(x)
+    return (r + (x - r >= 0.5)).astype(np.int64)
+
+
+class RefOcc:
+    """The reference OccGrid (grid.cpp), compiled in place, with the config-3 parameters."""
+
+    def __init__(self, res=0.05, l_hit=0.85, l_miss=-0.4, l_min=-5.0, l_max=5.0):
+        g5 = np.array([res, l_hit, l_miss, l_min, l_max], np.float32)
+        self.res = res
+        self.g = ref_lib().ref_occ_create(_p(g5, C.c_float))
+
+    def __del__(self):
+        if getattr(self, "g", None):
+            ref_lib().ref_occ_destroy(self.g)
+            self.g = None
+
+    def insert(self, hits, free, pose, match=None, normals=None, origin=(0.0, 0.0)) -> int:
+        def xy(a):
+            a = np.zeros((0, 2), np.float32) if a is None else np.ascontiguousarray(a, np.float32).reshape(-1, 2)
+            return np.ascontiguousarray(a[:, 0]), np.ascontiguousarray(a[:, 1]), len(a)
+        hx, hy, nh = xy(hits)
+        fx, fy, nf = xy(free)
+        mx, my, nm = xy(match)
+        mnx, mny, _ = xy(normals) if normals is not None else (None, None, 0)
+        P = np.ascontiguousarray(pose, np.float64)
+        fp = lambda a: _p(a, C.c_float) if a is not None else None
+        return int(ref_lib().ref_occ_insert(self.g, origin[0], origin[1], fp(hx), fp(hy), nh, fp(fx), fp(fy), nf, fp(mx),
+                                            fp(my), fp(mnx), fp(mny), nm, _p(P, C.c_double)))
+
+    def cells(self) -> dict:
+        g4 = np.zeros(4, np.int32)
+        ref_lib().ref_occ_geom(self.g, _p(g4, C.c_int32))
+        x0, y0, w, h = (int(v) for v in g4)
+        n = w * h
+        L, seen, c8, prob = np.zeros(n, np.int16), np.zeros(n, np.uint8), np.zeros(n, np.int8), np.zeros(n, np.float32)
+        if n:
+            ref_lib().ref_occ_cells(self.g, _p(L, C.c_int16), _p(seen, C.c_uint8), _p(c8, C.c_int8), _p(prob, C.c_float))
+        q = _lround(prob.astype(np.float64) * 65535.0).astype(np.uint16)
+        sh = (h, w)
+        return {"L": L.reshape(sh), "seen": seen.reshape(sh), "c8": c8.reshape(sh), "prob": prob.reshape(sh),
+                "q": q.reshape(sh), "x0": x0, "y0": y0}
+
+
+def csm(cells: dict, hits, pose0, lin_half=6, ang_half=20, ang_step=None, w_t=10.0, w_r=0.1, res=0.05, pmin=0.1):
+    """Restated correlative scan match (oracle/port/csm_port.c) on a grid snapshot from
+    RefOcc.cells(): (best index, best score, best pose)."""
+    import math
+    L = port_lib()
+    P = C.POINTER
+    if not getattr(L, "_csm_ready", False):
+        L.op_csm.argtypes = [P(C.c_uint16), C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint16, C.c_float, P(C.c_float),
+                             P(C.c_float), C.c_int, P(C.c_double), C.c_int, C.c_int, C.c_double, C.c_double, C.c_double,
+                             P(C.c_int32), P(C.c_double), P(C.c_double)]
+        L._csm_ready = True
+    ang_step = math.radians(0.5) if ang_step is None else ang_step
+    q = np.ascontiguousarray(cells["q"], np.uint16)
+    h, w = q.shape
+    a = np.ascontiguousarray(hits, np.float32).reshape(-1, 2)
+    hx, hy = np.ascontiguousarray(a[:, 0]), np.ascontiguousarray(a[:, 1])
+    p0 = np.ascontiguousarray(pose0, np.float64)
+    bi, bs, bp = np.zeros(1, np.int32), np.zeros(1), np.zeros(3)
+    q_out = int(_lround(np.array([float(np.float32(pmin)) * 65535.0]))[0])
+    L.op_csm(_p(q, C.c_uint16) if q.size else None, w, h, cells["x0"], cells["y0"], q_out, res, _p(hx, C.c_float),
+             _p(hy, C.c_float), len(a), _p(p0, C.c_double), lin_half, ang_half, ang_step, w_t, w_r, _p(bi, C.c_int32),
+             _p(bs, C.c_double), _p(bp, C.c_double))
+    return int(bi[0]), float(bs[0]), bp

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "k_grid.cuh"
+#include "k_occ.cuh"
 
 #define PF_THREADS 256   // CTA size of the batched plane fit (the block sums' tree follows it)
 
@@ -960,6 +961,326 @@ int smg_plane_fit(const float* xyz, const int32_t* off, int n_sets, int n_points
   CK(cudaFreeAsync(scr, st));
   CK(le);
   return SMG_OK;
+}
+
+// ------------------------------------------------------------------ standalone occupancy + CSM
+int smg_occ_destroy(smg_occ* o);
+struct smg_occ {
+  OccDev G;
+  int dev = 0;
+  int max_hits = 0;
+  std::vector<void*> allocs;
+  // pinned staging of one call's inputs
+  float2* h_pts = nullptr;
+  float2* h_mn = nullptr;
+  int32_t* h_n = nullptr;
+  float2* h_org = nullptr;
+  double* h_pose = nullptr;    // [M][5]
+  double* h_pose0 = nullptr;   // [M][3]
+  double* h_rot = nullptr;     // [M][n_rot][2]
+  double* h_out = nullptr;     // [M][5 pose + score] readback
+  int32_t* h_iout = nullptr;   // [M][2] best, changed
+  cudaEvent_t staged = nullptr;
+  bool staged_used = false;
+  // current matcher geometry (cand_w depends on it)
+  double csm_key[6] = {0, 0, 0, 0, 0, 0};
+  double* d_cand_w = nullptr;
+};
+
+static int oalloc(smg_occ* o, void** p, size_t bytes, int fill) {
+  void* q = nullptr;
+  CK(cudaMalloc(&q, std::max<size_t>(bytes, 1)));
+  o->allocs.push_back(q);
+  CK(cudaMemset(q, fill, std::max<size_t>(bytes, 1)));
+  *p = q;
+  return SMG_OK;
+}
+#define OA(ptr, n, fill)                                                               \
+  do {                                                                                 \
+    void* q_ = nullptr;                                                                \
+    int r_ = oalloc(o, &q_, sizeof(*(ptr)) * (size_t)(n), fill);                       \
+    if (r_) { smg_occ_destroy(o); return r_; }                                         \
+    *(void**)&(ptr) = q_;                                                              \
+  } while (0)
+
+int smg_occ_destroy(smg_occ* o) {
+  if (!o) return fail(SMG_ERR_ARGS, "smg_occ_destroy: null");
+  cudaSetDevice(o->dev);
+  for (void* p : o->allocs) cudaFree(p);
+  for (void* p : {(void*)o->h_pts, (void*)o->h_mn, (void*)o->h_n, (void*)o->h_org, (void*)o->h_pose, (void*)o->h_pose0,
+                  (void*)o->h_rot, (void*)o->h_out, (void*)o->h_iout})
+    if (p) cudaFreeHost(p);
+  if (o->staged) cudaEventDestroy(o->staged);
+  delete o;
+  return SMG_OK;
+}
+
+int smg_occ_create(const smg_occ_params* p, int n_maps, int grid_w, int grid_h, int grid_x0, int grid_y0, int max_points,
+                   int dev, smg_occ** out) {
+  if (!p || !out || n_maps <= 0 || grid_w <= 0 || grid_h <= 0 || grid_w > 4096 || grid_h > 4096 || max_points <= 0 ||
+      max_points > 65536 || !(p->res > 0) || p->l_min > 0 || p->l_max < 0)
+    return fail(SMG_ERR_ARGS, "smg_occ_create: bad arguments");
+  *out = nullptr;
+  CK(cudaSetDevice(dev));
+  smg_occ* o = new smg_occ();
+  o->dev = dev;
+  OccDev& G = o->G;
+  memset(&G, 0, sizeof(G));
+  const int M = n_maps;
+  G.M = M; G.W = grid_w; G.H = grid_h; G.X0 = grid_x0; G.Y0 = grid_y0; G.res = p->res;
+  // OccGrid::OccGrid (grid.cpp:8-22): fixed-point steps and the LUTs, host libm
+  const int kQ = 256;
+  G.q_hit = (int)std::lround(p->l_hit * kQ);
+  G.q_miss = (int)std::lround(p->l_miss * kQ);
+  G.q_min = (int)std::lround(p->l_min * kQ);
+  G.q_max = (int)std::lround(p->l_max * kQ);
+  G.lut_off = -G.q_min;
+  const int nlut = G.q_max - G.q_min + 1;
+  std::vector<int8_t> l8(nlut);
+  std::vector<uint16_t> lq(nlut);
+  for (int k = 0; k < nlut; ++k) {
+    const float L = float(k - G.lut_off) / kQ;
+    const float pr = 1.f / (1.f + std::exp(-L));
+    l8[k] = int8_t(std::lround(100.f * pr));
+    const float pc = std::min(std::max(pr, p->pmin), p->pmax);   // OccGrid::prob clamp
+    lq[k] = (uint16_t)std::lround((double)pc * 65535.0);
+  }
+  G.q_unseen = (uint16_t)std::lround((double)p->pmin * 65535.0);
+  G.max_pts = max_points;
+  const size_t cells = (size_t)M * grid_w * grid_h;
+  OA(G.L, cells, 0);
+  OA(G.c8, cells, 0xff);
+  OA(G.flags, cells, 0);
+  OA(G.cold, cells, 0);
+  OA(G.cnt, cells, 0);
+  OA(G.touch, cells, 0xff);
+  OA(G.Q, cells, 0);
+  int8_t* lut8 = nullptr;
+  uint16_t* qlut = nullptr;
+  OA(lut8, nlut, 0);
+  OA(qlut, nlut, 0);
+  CK(cudaMemcpy(lut8, l8.data(), nlut, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(qlut, lq.data(), nlut * 2, cudaMemcpyHostToDevice));
+  G.lut8 = lut8;
+  G.qlut = qlut;
+  {   // unseen cells read pmin
+    std::vector<uint16_t> q0((size_t)grid_w * grid_h, G.q_unseen);
+    for (int m = 0; m < M; ++m)
+      CK(cudaMemcpy(G.Q + (size_t)m * grid_w * grid_h, q0.data(), q0.size() * 2, cudaMemcpyHostToDevice));
+  }
+  OA(G.scan_id, M, 0);
+  OA(G.changed, M, 0);
+  OA(G.err, M, 0);
+  OA(G.pts, (size_t)M * 3 * max_points, 0);
+  OA(G.mn, (size_t)M * max_points, 0);
+  OA(G.nmhf, (size_t)M * 3, 0);
+  OA(G.origin, M, 0);
+  OA(G.pose, (size_t)M * 5, 0);
+  OA(G.rot, (size_t)M * CSM_MAX_ROT * 2, 0);
+  OA(G.pose0, (size_t)M * 3, 0);
+  OA(G.score, (size_t)M * CSM_MAX_ROT * CSM_MAX_LIN * CSM_MAX_LIN, 0);
+  OA(G.best, M, 0);
+  OA(G.best_score, M, 0);
+  OA(o->d_cand_w, (size_t)CSM_MAX_ROT * CSM_MAX_LIN * CSM_MAX_LIN, 0);
+  G.cand_w = o->d_cand_w;
+  CK(cudaMallocHost(&o->h_pts, sizeof(float2) * (size_t)M * 3 * max_points));
+  CK(cudaMallocHost(&o->h_mn, sizeof(float2) * (size_t)M * max_points));
+  CK(cudaMallocHost(&o->h_n, sizeof(int32_t) * (size_t)M * 3));
+  CK(cudaMallocHost(&o->h_org, sizeof(float2) * M));
+  CK(cudaMallocHost(&o->h_pose, sizeof(double) * (size_t)M * 5));
+  CK(cudaMallocHost(&o->h_pose0, sizeof(double) * (size_t)M * 3));
+  CK(cudaMallocHost(&o->h_rot, sizeof(double) * (size_t)M * CSM_MAX_ROT * 2));
+  CK(cudaMallocHost(&o->h_out, sizeof(double) * (size_t)M * 6));
+  CK(cudaMallocHost(&o->h_iout, sizeof(int32_t) * (size_t)M * 2));
+  CK(cudaEventCreateWithFlags(&o->staged, cudaEventDisableTiming));
+  CK(cudaFuncSetAttribute(k_csm_score, cudaFuncAttributeMaxDynamicSharedMemorySize, CSM_WIN_CELLS * 2));
+  *out = o;
+  return SMG_OK;
+}
+
+// stage the scans of the first n maps (host memory) into pinned buffers and copy them in
+static int occ_stage(smg_occ* o, const smg_scan2* scans, int n, bool need_hits, cudaStream_t st) {
+  OccDev& G = o->G;
+  if (o->staged_used) CK(cudaEventSynchronize(o->staged));
+  int mx = 0;
+  for (int m = 0; m < G.M; ++m) {
+    int* c = o->h_n + 3 * m;
+    c[0] = c[1] = c[2] = 0;
+    o->h_org[m] = make_float2(0.f, 0.f);
+    if (m >= n) continue;
+    const smg_scan2& s = scans[m];
+    if (s.n_match < 0 || s.n_hit < 0 || s.n_free < 0 || s.n_match + s.n_hit + s.n_free > G.max_pts ||
+        (s.n_match && (!s.mx || !s.my)) || (s.n_hit && (!s.hx || !s.hy)) || (s.n_free && (!s.fx || !s.fy)))
+      return fail(SMG_ERR_ARGS, "smg_occ: bad scan (counts, pointers or more than max_points points)");
+    c[0] = s.n_match; c[1] = s.n_hit; c[2] = s.n_free;
+    o->h_org[m] = make_float2(s.ox, s.oy);
+    float2* P = o->h_pts + (size_t)m * 3 * G.max_pts;
+    float2* N = o->h_mn + (size_t)m * G.max_pts;
+    for (int k = 0; k < s.n_match; ++k) {
+      P[k] = make_float2(s.mx[k], s.my[k]);
+      N[k] = (s.mnx && s.mny) ? make_float2(s.mnx[k], s.mny[k]) : make_float2(0.f, 0.f);
+    }
+    for (int k = 0; k < s.n_hit; ++k) P[s.n_match + k] = make_float2(s.hx[k], s.hy[k]);
+    for (int k = 0; k < s.n_free; ++k) P[s.n_match + s.n_hit + k] = make_float2(s.fx[k], s.fy[k]);
+    mx = std::max(mx, s.n_hit);
+  }
+  (void)need_hits;
+  o->max_hits = mx;
+  for (int m = 0; m < G.M; ++m) {
+    const int* c = o->h_n + 3 * m;
+    const size_t np = (size_t)(c[0] + c[1] + c[2]);
+    if (np) CK(cudaMemcpyAsync(G.pts + (size_t)m * 3 * G.max_pts, o->h_pts + (size_t)m * 3 * G.max_pts, np * sizeof(float2),
+                               cudaMemcpyHostToDevice, st));
+    if (c[0]) CK(cudaMemcpyAsync(G.mn + (size_t)m * G.max_pts, o->h_mn + (size_t)m * G.max_pts, (size_t)c[0] * sizeof(float2),
+                                 cudaMemcpyHostToDevice, st));
+  }
+  CK(cudaMemcpyAsync(G.nmhf, o->h_n, sizeof(int32_t) * 3 * G.M, cudaMemcpyHostToDevice, st));
+  CK(cudaMemcpyAsync(G.origin, o->h_org, sizeof(float2) * G.M, cudaMemcpyHostToDevice, st));
+  return SMG_OK;
+}
+
+static int occ_matcher_setup(smg_occ* o, const smg_csm_params* c, const double* pose0, int n, cudaStream_t st) {
+  OccDev& G = o->G;
+  if (!c || !(c->linear_step > 0) || !(c->angular_step > 0) || c->linear_window < 0 || c->angular_window < 0)
+    return fail(SMG_ERR_ARGS, "smg_occ: bad matcher parameters");
+  const int lh = (int)std::lround(c->linear_window / c->linear_step), ah = (int)std::lround(c->angular_window / c->angular_step);
+  if (2 * lh + 1 > CSM_MAX_LIN || 2 * ah + 1 > CSM_MAX_ROT)
+    return fail(SMG_ERR_ARGS, "smg_occ: search window too large (at most 13 offsets per axis and 81 rotations)");
+  if (std::fabs(c->linear_step - (double)G.res) > 1e-6 * (double)G.res)
+    return fail(SMG_ERR_ARGS, "smg_occ: linear_step must equal the grid resolution (offsets are whole cells)");
+  G.lin_half = lh;
+  G.n_lin = 2 * lh + 1;
+  G.n_rot = 2 * ah + 1;
+  G.lin_step = (double)G.res;
+  G.ang_step = c->angular_step;
+  const double key[6] = {(double)lh, (double)ah, c->angular_step, c->translation_weight, c->rotation_weight, (double)G.res};
+  if (memcmp(key, o->csm_key, sizeof key) != 0) {
+    // candidate weights exp(-(|t| w_t + |dth| w_r)^2), host libm, candidate order (j, kx, ky)
+    std::vector<double> w((size_t)G.n_rot * G.n_lin * G.n_lin);
+    for (int j = 0; j < G.n_rot; ++j)
+      for (int kx = -lh; kx <= lh; ++kx)
+        for (int ky = -lh; ky <= lh; ++ky) {
+          const double t = std::hypot((double)kx * G.lin_step, (double)ky * G.lin_step);
+          const double a = std::fabs((double)(j - ah) * c->angular_step);
+          const double e = t * c->translation_weight + a * c->rotation_weight;
+          w[((size_t)j * G.n_lin + (kx + lh)) * G.n_lin + (ky + lh)] = std::exp(-(e * e));
+        }
+    CK(cudaMemcpy(o->d_cand_w, w.data(), sizeof(double) * w.size(), cudaMemcpyHostToDevice));
+    memcpy(o->csm_key, key, sizeof key);
+  }
+  for (int m = 0; m < G.M; ++m) {
+    const double* P = m < n ? pose0 + 3 * m : nullptr;
+    for (int k = 0; k < 3; ++k) o->h_pose0[3 * m + k] = P ? P[k] : 0.0;
+    for (int j = 0; j < G.n_rot; ++j) {
+      const double th = o->h_pose0[3 * m + 2] + (double)(j - ah) * c->angular_step;
+      o->h_rot[((size_t)m * G.n_rot + j) * 2] = std::cos(th);
+      o->h_rot[((size_t)m * G.n_rot + j) * 2 + 1] = std::sin(th);
+    }
+  }
+  CK(cudaMemcpyAsync(G.pose0, o->h_pose0, sizeof(double) * 3 * G.M, cudaMemcpyHostToDevice, st));
+  CK(cudaMemcpyAsync(G.rot, o->h_rot, sizeof(double) * 2 * G.n_rot * G.M, cudaMemcpyHostToDevice, st));
+  return SMG_OK;
+}
+
+static int occ_launch_match(smg_occ* o, cudaStream_t st) {
+  OccDev& G = o->G;
+  const int sectors = std::max(CSM_SECTORS, (o->max_hits + 1023) / 1024);
+  k_csm_score<<<dim3(sectors, G.n_rot, G.M), OCC_THREADS, CSM_WIN_CELLS * 2, st>>>(G);
+  k_csm_best<<<G.M, OCC_THREADS, 0, st>>>(G);
+  CK(cudaGetLastError());
+  return SMG_OK;
+}
+
+static int occ_launch_insert(smg_occ* o, cudaStream_t st) {
+  OccDev& G = o->G;
+  int mx = 0;
+  for (int m = 0; m < G.M; ++m) mx = std::max(mx, o->h_n[3 * m] + o->h_n[3 * m + 1] + o->h_n[3 * m + 2]);
+  const int blocks = std::max(1, std::min(64, (mx + 63) / 64));
+  k_occ_begin<<<(G.M + 127) / 128, 128, 0, st>>>(G);
+  k_occ_keys<<<dim3(blocks, G.M), OCC_THREADS, 0, st>>>(G);
+  k_occ_apply<<<dim3(blocks, G.M), OCC_THREADS, 0, st>>>(G);
+  CK(cudaGetLastError());
+  return SMG_OK;
+}
+
+static int occ_finish(smg_occ* o, int n, double* pose_out, int32_t* index_out, double* score_out, int32_t* changed_out,
+                      cudaStream_t st) {
+  OccDev& G = o->G;
+  CK(cudaEventRecord(o->staged, st));
+  o->staged_used = true;
+  if (!pose_out && !index_out && !score_out && !changed_out) return SMG_OK;
+  // readback: h_out = [M][5] poses then [M] scores; h_iout = [M] best then [M] changed
+  CK(cudaMemcpyAsync(o->h_out, G.pose, sizeof(double) * 5 * G.M, cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(o->h_out + 5 * G.M, G.best_score, sizeof(double) * G.M, cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(o->h_iout, G.best, sizeof(int32_t) * G.M, cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(o->h_iout + G.M, G.changed, sizeof(int32_t) * G.M, cudaMemcpyDeviceToHost, st));
+  std::vector<int32_t> err(G.M);
+  CK(cudaMemcpyAsync(err.data(), G.err, sizeof(int32_t) * G.M, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  for (int m = 0; m < n; ++m) {
+    if (pose_out) for (int k = 0; k < 3; ++k) pose_out[3 * m + k] = o->h_out[5 * m + k];
+    if (index_out) index_out[m] = o->h_iout[m];
+    if (score_out) score_out[m] = o->h_out[5 * G.M + m];
+    if (changed_out) changed_out[m] = err[m] ? -1 : o->h_iout[G.M + m];
+  }
+  return SMG_OK;
+}
+
+int smg_occ_insert(smg_occ* o, const smg_scan2* scans, const double* poses, int n, int32_t* changed_out, void* stream) {
+  if (!o || !scans || !poses || n <= 0 || n > o->G.M) return fail(SMG_ERR_ARGS, "smg_occ_insert: bad arguments");
+  CK(cudaSetDevice(o->dev));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (int r = occ_stage(o, scans, n, false, st)) return r;
+  OccDev& G = o->G;
+  for (int m = 0; m < G.M; ++m) {   // the insert pose and its host-libm cos/sin (grid.cpp:201)
+    double* q = o->h_pose + 5 * m;
+    const double* P = m < n ? poses + 3 * m : nullptr;
+    q[0] = P ? P[0] : 0; q[1] = P ? P[1] : 0; q[2] = P ? P[2] : 0;
+    q[3] = std::cos(q[2]); q[4] = std::sin(q[2]);
+  }
+  CK(cudaMemcpyAsync(G.pose, o->h_pose, sizeof(double) * 5 * G.M, cudaMemcpyHostToDevice, st));
+  if (int r = occ_launch_insert(o, st)) return r;
+  return occ_finish(o, n, nullptr, nullptr, nullptr, changed_out, st);
+}
+
+int smg_occ_match(smg_occ* o, const smg_scan2* scans, const double* pose0, const smg_csm_params* c, int n, double* pose_out,
+                  int32_t* index_out, double* score_out, void* stream) {
+  if (!o || !scans || !pose0 || n <= 0 || n > o->G.M) return fail(SMG_ERR_ARGS, "smg_occ_match: bad arguments");
+  CK(cudaSetDevice(o->dev));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (int r = occ_stage(o, scans, n, true, st)) return r;
+  if (int r = occ_matcher_setup(o, c, pose0, n, st)) return r;
+  if (int r = occ_launch_match(o, st)) return r;
+  return occ_finish(o, n, pose_out, index_out, score_out, nullptr, st);
+}
+
+int smg_occ_track(smg_occ* o, const smg_scan2* scans, const double* pose0, const smg_csm_params* c, int n, double* pose_out,
+                  int32_t* index_out, double* score_out, int32_t* changed_out, void* stream) {
+  if (!o || !scans || !pose0 || n <= 0 || n > o->G.M) return fail(SMG_ERR_ARGS, "smg_occ_track: bad arguments");
+  CK(cudaSetDevice(o->dev));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (int r = occ_stage(o, scans, n, true, st)) return r;
+  if (int r = occ_matcher_setup(o, c, pose0, n, st)) return r;
+  if (int r = occ_launch_match(o, st)) return r;
+  if (int r = occ_launch_insert(o, st)) return r;
+  return occ_finish(o, n, pose_out, index_out, score_out, changed_out, st);
+}
+
+int smg_occ_get_cells(smg_occ* o, int m, int16_t* L, uint8_t* seen, int8_t* c8, uint16_t* q) {
+  if (!o || m < 0 || m >= o->G.M) return fail(SMG_ERR_ARGS, "smg_occ_get_cells: bad arguments");
+  CK(cudaSetDevice(o->dev));
+  CK(cudaDeviceSynchronize());
+  const OccDev& G = o->G;
+  const size_t n = (size_t)G.W * G.H, b = (size_t)m * n;
+  if (L) CK(cudaMemcpy(L, G.L + b, n * 2, cudaMemcpyDeviceToHost));
+  if (c8) CK(cudaMemcpy(c8, G.c8 + b, n, cudaMemcpyDeviceToHost));
+  if (q) CK(cudaMemcpy(q, G.Q + b, n * 2, cudaMemcpyDeviceToHost));
+  if (seen) {
+    std::vector<uint8_t> f(n);
+    CK(cudaMemcpy(f.data(), G.flags + b, n, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < n; ++i) seen[i] = f[i] & 1;
+  }
+  return (int)n;
 }
 
 // ------------------------------------------------------------------ plane fit, no allocation

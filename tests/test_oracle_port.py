@@ -101,3 +101,45 @@ def test_primitives_port_vs_reference():
         xyz = plane_clouds._plane_cloud(rng, n, float(rng.uniform(0.001, 0.05)), float(rng.uniform(0, 0.7)))
         tau, seed = float(rng.uniform(0.01, 0.06)), int(rng.integers(1, 2**62))
         assert np.array_equal(ref.plane_fit(xyz, tau, seed), ref.plane_fit(xyz, tau, seed, impl="ref")), k
+
+
+def _csm_numpy(q, x0, y0, q_out, res, hits, pose0, lh, ah, step, wt, wr):
+    """Direct statement of the matcher's definition (independent of oracle/port/csm_port.c)."""
+    import math
+    h, w = q.shape
+    n = len(hits)
+    best, bi = -1.0, -1
+    rd = float(np.float32(res))
+    for j in range(2 * ah + 1):
+        th = pose0[2] + (j - ah) * step
+        c, s = math.cos(th), math.sin(th)
+        cells = [(math.floor((pose0[0] + c * float(px) - s * float(py)) / rd),
+                  math.floor((pose0[1] + s * float(px) + c * float(py)) / rd)) for px, py in hits]
+        for kx in range(-lh, lh + 1):
+            for ky in range(-lh, lh + 1):
+                tot = 0
+                for ix, iy in cells:
+                    X, Y = ix + kx - x0, iy + ky - y0
+                    tot += int(q[Y, X]) if 0 <= X < w and 0 <= Y < h else q_out
+                e = math.hypot(kx * rd, ky * rd) * wt + abs((j - ah) * step) * wr
+                v = (tot / (n * 65535.0)) * math.exp(-(e * e))
+                if v > best:
+                    best, bi = v, (j * (2 * lh + 1) + kx + lh) * (2 * lh + 1) + ky + lh
+    return bi, best
+
+
+def test_csm_port_matches_definition():
+    ref = _port()
+    rng = np.random.default_rng(3)
+    for trial in range(6):
+        q = rng.integers(0, 65536, (40, 50)).astype(np.uint16)
+        if trial == 0:
+            q[:] = 6554                       # flat grid: every offset ties, the weights decide
+        hits = rng.uniform(-0.8, 0.8, (int(rng.integers(1, 30)), 2)).astype(np.float32)
+        pose0 = np.array([float(rng.uniform(0.8, 1.5)), float(rng.uniform(0.8, 1.2)), float(rng.uniform(-3, 3))])
+        cells = {"q": q, "x0": -3, "y0": -2}
+        bi, bs, bp = ref.csm(cells, hits, pose0, lin_half=2, ang_half=3, ang_step=0.02, w_t=10.0, w_r=0.1)
+        want = _csm_numpy(q, -3, -2, 6554, 0.05, hits, pose0, 2, 3, 0.02, 10.0, 0.1)
+        assert (bi, bs) == want, (trial, bi, bs, want)
+        if trial == 0:
+            assert bi == (3 * 5 + 2) * 5 + 2  # centre candidate
