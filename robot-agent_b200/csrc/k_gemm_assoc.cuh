@@ -1,0 +1,341 @@
+// Association stress path: detections x memory bank on the tcgen05 tensor
+// cores, with the association decision fused into the epilogue.
+//
+// Score of (detection d, memory j) = dot(z_d, m_j) of the bf16 L2-normalised embeddings, fp32
+// accumulation in TMEM.  A pair takes part only if the 3D boxes overlap with IoU > iou_min
+// (float arithmetic, the same operation order as the CPU restatement).  Decision per
+// detection: the gated memory with the largest score if that score is >= cos_min, the lowest
+// memory index on ties, else no match -- evaluated on the fp64 dot products of the same bf16
+// values summed in index order (the restatement's definition).
+//
+// The tensor-core scores differ from those fp64 values by at most `delta` (fp32 accumulation
+// of K exact bf16 products of unit vectors: K * 2^-23 bounds it; the host passes a margin
+// above that).  The epilogue keeps, per detection and tile, the best and second-best gated
+// scores; k_assoc_decide certifies a decision when the best is clear of the threshold and of
+// the runner-up by more than the error margin, and otherwise recomputes that detection's gated
+// candidates in fp64, in index order, so every decision equals the restatement's.
+//
+// GEMM: A = detections [n_det][K], B = memories [n_mem][K], both K-major bf16, loaded by TMA
+// (128-byte swizzle, 64-element K blocks) into a 4-stage shared-memory ring; one elected
+// thread issues tcgen05.mma (M = 128, N = 256, K = 16) into a 128 x 256 fp32 TMEM
+// accumulator; the four warps read it back with tcgen05.ld (warp w owns TMEM lanes 32w..32w+31,
+// i.e. detections), apply the gate and keep the top-2 per detection.  Every mbarrier wait is
+// bounded by a %globaltimer limit; a timeout sets the error word and the CTA still waits
+// (bounded) for its tensor-core work and frees its TMEM before returning.
+#pragma once
+#include <cuda.h>
+#include "dev_util.cuh"
+
+#define AG_BM 128
+#define AG_BN 256
+#define AG_BK 64
+#define AG_STAGES 4
+#define AG_THREADS 128
+#define AG_A_BYTES (AG_BM * AG_BK * 2)
+#define AG_B_BYTES (AG_BN * AG_BK * 2)
+#define AG_TMEM_COLS 256
+#define AG_SMEM (AG_STAGES * (AG_A_BYTES + AG_B_BYTES) + 1024 + 256 + AG_BN * 6 * 4)
+#define AG_WAIT_NS 200000000ull   // 0.2 s per wait
+
+// instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1), B bf16
+// (bits 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28
+#define AG_IDESC ((1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(AG_BN >> 3) << 17) | ((uint32_t)(AG_BM >> 4) << 24))
+
+struct AssocArgs {
+  int n_det, n_mem, dim, n_tiles;
+  const float* det_box;   // n_det x 6: lo xyz, hi xyz
+  const float* mem_box;   // n_mem x 6
+  const uint16_t* det;    // n_det x dim bf16
+  const uint16_t* mem;    // n_mem x dim bf16
+  float iou_min;
+  double cos_min, delta;
+  float* t_best;          // [n_det][n_tiles]
+  float* t_second;
+  int32_t* t_idx;
+  float* scores;          // optional [n_det][n_mem]
+  int32_t* match;         // [n_det]
+  double* score;          // [n_det]
+  int32_t* certified;     // [n_det] 1 = decided from the tensor-core scores, 0 = recomputed
+  int32_t* err;           // [1]
+};
+
+DEV uint32_t ag_smem(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+DEV uint64_t ag_now() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+DEV void ag_mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(ag_smem(b)), "r"(count) : "memory");
+}
+
+DEV void ag_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(ag_smem(b)), "r"(bytes) : "memory");
+}
+
+DEV bool ag_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(ag_smem(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// bounded wait on phase `parity`; false after AG_WAIT_NS
+DEV bool ag_wait(uint64_t* b, uint32_t parity) {
+  const uint64_t t0 = ag_now();
+  for (uint32_t i = 0;; ++i) {
+    if (ag_try_wait(b, parity)) return true;
+    if ((i & 255u) == 255u && ag_now() - t0 > AG_WAIT_NS) return false;
+  }
+}
+
+DEV void ag_tma_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          ag_smem(dst)),
+      "l"((uint64_t)map), "r"(ag_smem(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 bytes apart
+DEV uint64_t ag_desc(const void* tile) {
+  const uint32_t a = ag_smem(tile);
+  uint64_t d = (uint64_t)((a >> 4) & 0x3fffu);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+DEV void ag_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+      "l"(da), "l"(db), "r"(AG_IDESC), "r"(accum));
+}
+
+DEV void ag_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(ag_smem(bar)) : "memory");
+}
+
+DEV void ag_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+DEV void ag_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+DEV void ag_tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 3D AABB IoU > tmin, float, fixed operation order (the restatement uses the same)
+DEV bool ag_gate(const float* a, float avol, const float* b, float tmin) {
+  float inter = 1.f;
+  for (int k = 0; k < 3; ++k) {
+    const float lo = fmaxf(a[k], b[k]), hi = fminf(a[3 + k], b[3 + k]);
+    const float e = hi - lo;
+    if (!(e > 0.f)) return false;
+    inter = inter * e;
+  }
+  const float bvol = ((b[3] - b[0]) * (b[4] - b[1])) * (b[5] - b[2]);
+  const float uni = (avol + bvol) - inter;
+  return inter > tmin * uni;
+}
+
+__global__ void __launch_bounds__(AG_THREADS, 1)
+    k_assoc_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, AssocArgs g) {
+  extern __shared__ unsigned char ag_raw[];
+  unsigned char* base = (unsigned char*)(((uintptr_t)ag_raw + 1023) & ~(uintptr_t)1023);
+  unsigned char* sA = base;
+  unsigned char* sB = base + AG_STAGES * AG_A_BYTES;
+  uint64_t* full = (uint64_t*)(sB + AG_STAGES * AG_B_BYTES);
+  uint64_t* empty = full + AG_STAGES;
+  uint64_t* done = empty + AG_STAGES;
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
+  float* mbox = (float*)(base + AG_STAGES * (AG_A_BYTES + AG_B_BYTES) + 256);
+  __shared__ int sh_fail;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * AG_BN, m0 = blockIdx.y * AG_BM;
+  const int nk = g.dim / AG_BK;
+  if (tid == 0) {
+    for (int s = 0; s < AG_STAGES; ++s) {
+      ag_mbar_init(&full[s], 1);
+      ag_mbar_init(&empty[s], 1);
+    }
+    ag_mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    sh_fail = 0;
+  }
+  for (int i = tid; i < AG_BN * 6; i += blockDim.x) {
+    const int j = n0 + i / 6;
+    mbox[i] = j < g.n_mem ? g.mem_box[(size_t)j * 6 + i % 6] : 0.f;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ag_smem(tmem_slot)),
+                 "r"(AG_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  ag_fence_before();
+  __syncthreads();
+  ag_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {   // TMA producer
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % AG_STAGES;
+      const uint32_t ph = (uint32_t)(kb / AG_STAGES) & 1u;
+      if (!ag_wait(&empty[s], ph ^ 1u)) { sh_fail = 1; break; }
+      ag_expect_tx(&full[s], AG_A_BYTES + AG_B_BYTES);
+      ag_tma_2d(&tmA, &full[s], sA + s * AG_A_BYTES, kb * AG_BK, m0);
+      ag_tma_2d(&tmB, &full[s], sB + s * AG_B_BYTES, kb * AG_BK, n0);
+    }
+  } else if (warp == 1 && lane == 0) {   // MMA issuer
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % AG_STAGES;
+      const uint32_t ph = (uint32_t)(kb / AG_STAGES) & 1u;
+      if (!ag_wait(&full[s], ph)) { sh_fail = 1; break; }
+      ag_fence_after();
+      const uint64_t da = ag_desc(sA + s * AG_A_BYTES), db = ag_desc(sB + s * AG_B_BYTES);
+#pragma unroll
+      for (int k = 0; k < AG_BK / 16; ++k) ag_mma(tmem, da + 2 * k, db + 2 * k, (kb | k) != 0);
+      ag_commit(&empty[s]);
+    }
+    ag_commit(done);   // also on failure: arrives once every issued MMA has completed
+  }
+  __syncwarp();
+  bool ok = ag_wait(done, 0);
+  if (warp == 0 && lane == 0) {   // drain: the last loads issued must have landed before exit
+    for (int kb = nk - AG_STAGES > 0 ? nk - AG_STAGES : 0; kb < nk; ++kb)
+      ok = ag_wait(&full[kb % AG_STAGES], (uint32_t)(kb / AG_STAGES) & 1u) && ok;
+  }
+  ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  ag_fence_after();
+  const int r = warp * 32 + lane, d = m0 + r;
+  float bx[6] = {0, 0, 0, 0, 0, 0};
+  if (d < g.n_det)
+    for (int k = 0; k < 6; ++k) bx[k] = g.det_box[(size_t)d * 6 + k];
+  const float avol = ((bx[3] - bx[0]) * (bx[4] - bx[1])) * (bx[5] - bx[2]);
+  float b1 = -INFINITY, b2 = -INFINITY;
+  int i1 = -1;
+  if (ok) {
+    for (int c0 = 0; c0 < AG_BN; c0 += 32) {
+      uint32_t v[32];
+      ag_tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int j = n0 + c0 + c;
+        const float sc = __uint_as_float(v[c]);
+        if (d >= g.n_det || j >= g.n_mem) continue;
+        if (g.scores) g.scores[(size_t)d * g.n_mem + j] = sc;
+        if (!ag_gate(bx, avol, &mbox[(c0 + c) * 6], g.iou_min)) continue;
+        if (sc > b1) { b2 = b1; b1 = sc; i1 = j; }
+        else if (sc > b2) b2 = sc;
+      }
+    }
+  }
+  if (d < g.n_det) {
+    const size_t t = (size_t)d * g.n_tiles + blockIdx.x;
+    g.t_best[t] = b1;
+    g.t_second[t] = b2;
+    g.t_idx[t] = i1;
+  }
+  ag_fence_before();
+  __syncthreads();
+  if (tid == 0 && (sh_fail || !ok)) atomicOr(g.err, 1);
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(AG_TMEM_COLS) : "memory");
+  }
+}
+
+// fp64 dot of two bf16 rows summed in index order (the restatement's definition)
+DEV double ag_dot_seq(const uint16_t* a, const uint16_t* b, int D) {
+  double s = 0.0;
+  for (int k = 0; k < D; ++k) s += (double)__uint_as_float((uint32_t)a[k] << 16) * (double)__uint_as_float((uint32_t)b[k] << 16);
+  return s;
+}
+
+// one warp per detection: combine the tiles, certify, or recompute in fp64
+__global__ void __launch_bounds__(256) k_assoc_decide(AssocArgs g) {
+  const int lane = threadIdx.x & 31;
+  const int d = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (d >= g.n_det) return;
+  float b1 = -INFINITY, o1 = -INFINITY;   // best, and the best of the other candidates
+  int i1 = 0x7fffffff;
+  for (int t = lane; t < g.n_tiles; t += 32) {
+    const size_t q = (size_t)d * g.n_tiles + t;
+    const float tb = g.t_best[q], ts = g.t_second[q];
+    const int ti = g.t_idx[q];
+    if (ti >= 0 && (tb > b1 || (tb == b1 && ti < i1))) {
+      o1 = fmaxf(o1, fmaxf(b1, ts));
+      b1 = tb;
+      i1 = ti;
+    } else {
+      o1 = fmaxf(o1, fmaxf(tb, ts));
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const float b2 = __shfl_xor_sync(0xffffffffu, b1, off), p2 = __shfl_xor_sync(0xffffffffu, o1, off);
+    const int j2 = __shfl_xor_sync(0xffffffffu, i1, off);
+    if (j2 != 0x7fffffff && (b2 > b1 || (b2 == b1 && j2 < i1))) {
+      o1 = fmaxf(p2, fmaxf(o1, b1));
+      b1 = b2;
+      i1 = j2;
+    } else {
+      o1 = fmaxf(o1, fmaxf(p2, b2));
+    }
+  }
+  const double best = (double)b1, other = (double)o1, thr = g.cos_min, dl = g.delta;
+  int decided = -2;   // -2 = undecided
+  if (i1 == 0x7fffffff || best < thr - dl) decided = -1;
+  else if (best >= thr + dl && other < best - 2 * dl) decided = i1;
+  if (decided != -2) {
+    double s = 0.0;
+    if (decided >= 0) {   // fp64 score of the chosen pair (lane-parallel partial sums)
+      const uint16_t* a = g.det + (size_t)d * g.dim;
+      const uint16_t* b = g.mem + (size_t)decided * g.dim;
+      for (int k = lane; k < g.dim; k += 32)
+        s += (double)__uint_as_float((uint32_t)a[k] << 16) * (double)__uint_as_float((uint32_t)b[k] << 16);
+      s = warp_sum_d(s);
+    }
+    if (lane == 0) { g.match[d] = decided; g.score[d] = s; g.certified[d] = 1; }
+    return;
+  }
+  // recompute: every gated memory, fp64 in index order, one lane per candidate
+  float bx[6];
+  for (int k = 0; k < 6; ++k) bx[k] = g.det_box[(size_t)d * 6 + k];
+  const float avol = ((bx[3] - bx[0]) * (bx[4] - bx[1])) * (bx[5] - bx[2]);
+  double bs = -1e300;
+  int bj = 0x7fffffff;
+  const uint16_t* a = g.det + (size_t)d * g.dim;
+  for (int j = lane; j < g.n_mem; j += 32) {
+    if (!ag_gate(bx, avol, g.mem_box + (size_t)j * 6, g.iou_min)) continue;
+    const double s = ag_dot_seq(a, g.mem + (size_t)j * g.dim, g.dim);
+    if (s >= thr && (s > bs || (s == bs && j < bj))) { bs = s; bj = j; }
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const double s2 = __shfl_xor_sync(0xffffffffu, bs, off);
+    const int j2 = __shfl_xor_sync(0xffffffffu, bj, off);
+    if (s2 > bs || (s2 == bs && j2 < bj)) { bs = s2; bj = j2; }
+  }
+  if (lane == 0) {
+    g.match[d] = bj == 0x7fffffff ? -1 : bj;
+    g.score[d] = bj == 0x7fffffff ? 0.0 : bs;
+    g.certified[d] = 0;
+  }
+}

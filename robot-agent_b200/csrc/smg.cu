@@ -28,6 +28,9 @@
 
 #include "k_grid.cuh"
 #include "k_occ.cuh"
+#include "k_gemm_assoc.cuh"
+
+#include <cudaTypedefs.h>
 
 #define PF_THREADS 256   // CTA size of the batched plane fit (the block sums' tree follows it)
 
@@ -1281,6 +1284,109 @@ int smg_occ_get_cells(smg_occ* o, int m, int16_t* L, uint8_t* seen, int8_t* c8, 
     for (size_t i = 0; i < n; ++i) seen[i] = f[i] & 1;
   }
   return (int)n;
+}
+
+// ------------------------------------------------------------------ association stress (config 2)
+struct smg_assoc {
+  int dev = 0, max_det = 0, max_mem = 0, dim = 0;
+  float* t_best = nullptr;
+  float* t_second = nullptr;
+  int32_t* t_idx = nullptr;
+  int32_t* err = nullptr;
+};
+
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// 2D bf16 [rows][dim] K-major, box = 64 x box_rows, 128-byte swizzle, zero fill outside
+static int encode_rows(CUtensorMap* m, const void* ptr, int rows, int dim, int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = tmap_encoder();
+  if (!fn) return fail(SMG_ERR_DEVICE, "smg_assoc: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t gdim[2] = {(cuuint64_t)dim, (cuuint64_t)rows};
+  const cuuint64_t gstr[1] = {(cuuint64_t)dim * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)AG_BK, (cuuint32_t)box_rows};
+  const cuuint32_t est[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), gdim, gstr, box, est,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SMG_ERR_ARGS, ("smg_assoc: tensor map encoding failed (" + std::to_string((int)r) + ")").c_str());
+  return SMG_OK;
+}
+
+int smg_assoc_destroy(smg_assoc* a) {
+  if (!a) return fail(SMG_ERR_ARGS, "smg_assoc_destroy: null");
+  cudaSetDevice(a->dev);
+  cudaFree(a->t_best);
+  cudaFree(a->t_second);
+  cudaFree(a->t_idx);
+  cudaFree(a->err);
+  delete a;
+  return SMG_OK;
+}
+
+int smg_assoc_create(int max_det, int max_mem, int dim, int dev, smg_assoc** out) {
+  if (!out || max_det <= 0 || max_mem <= 0 || dim <= 0 || dim % AG_BK != 0)
+    return fail(SMG_ERR_ARGS, "smg_assoc_create: bad arguments (dim must be a positive multiple of 64)");
+  *out = nullptr;
+  CK(cudaSetDevice(dev));
+  smg_assoc* a = new smg_assoc();
+  a->dev = dev; a->max_det = max_det; a->max_mem = max_mem; a->dim = dim;
+  const size_t nt = (size_t)(max_mem + AG_BN - 1) / AG_BN;
+  if (cudaMalloc(&a->t_best, sizeof(float) * max_det * nt) != cudaSuccess ||
+      cudaMalloc(&a->t_second, sizeof(float) * max_det * nt) != cudaSuccess ||
+      cudaMalloc(&a->t_idx, sizeof(int32_t) * max_det * nt) != cudaSuccess || cudaMalloc(&a->err, sizeof(int32_t)) != cudaSuccess) {
+    smg_assoc_destroy(a);
+    return fail(SMG_ERR_DEVICE, "smg_assoc_create: out of device memory");
+  }
+  CK(cudaMemset(a->err, 0, sizeof(int32_t)));
+  CK(cudaFuncSetAttribute(k_assoc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, AG_SMEM));
+  *out = a;
+  return SMG_OK;
+}
+
+int smg_assoc_match(smg_assoc* a, const uint16_t* det, const float* det_box, int n_det, const uint16_t* mem, const float* mem_box,
+                    int n_mem, float iou_min, double cos_min, int32_t* match, double* score, int32_t* certified,
+                    float* scores, void* stream) {
+  if (!a || !det || !det_box || !mem || !mem_box || !match || !score || !certified || n_det <= 0 || n_mem <= 0 ||
+      n_det > a->max_det || n_mem > a->max_mem)
+    return fail(SMG_ERR_ARGS, "smg_assoc_match: bad arguments");
+  if ((((uintptr_t)det) | ((uintptr_t)mem)) & 15) return fail(SMG_ERR_ARGS, "smg_assoc_match: embeddings must be 16-byte aligned");
+  CK(cudaSetDevice(a->dev));
+  cudaStream_t st = (cudaStream_t)stream;
+  CUtensorMap tA, tB;
+  if (int r = encode_rows(&tA, det, n_det, a->dim, AG_BM)) return r;
+  if (int r = encode_rows(&tB, mem, n_mem, a->dim, AG_BN)) return r;
+  AssocArgs g;
+  memset(&g, 0, sizeof(g));
+  g.n_det = n_det; g.n_mem = n_mem; g.dim = a->dim; g.n_tiles = (n_mem + AG_BN - 1) / AG_BN;
+  g.det_box = det_box; g.mem_box = mem_box; g.det = det; g.mem = mem;
+  g.iou_min = iou_min; g.cos_min = cos_min;
+  g.delta = (double)a->dim * std::ldexp(1.0, -22);   // > K * 2^-23 (fp32 accumulation, |z| <= 1.01)
+  g.t_best = a->t_best; g.t_second = a->t_second; g.t_idx = a->t_idx;
+  g.scores = scores; g.match = match; g.score = score; g.certified = certified; g.err = a->err;
+  const dim3 grid(g.n_tiles, (n_det + AG_BM - 1) / AG_BM);
+  k_assoc_gemm<<<grid, AG_THREADS, AG_SMEM, st>>>(tA, tB, g);
+  k_assoc_decide<<<(n_det + 7) / 8, 256, 0, st>>>(g);
+  CK(cudaGetLastError());
+  return SMG_OK;
+}
+
+int smg_assoc_error(smg_assoc* a) {
+  if (!a) return fail(SMG_ERR_ARGS, "smg_assoc_error: null");
+  CK(cudaSetDevice(a->dev));
+  int32_t e = 0;
+  CK(cudaMemcpy(&e, a->err, sizeof(e), cudaMemcpyDeviceToHost));
+  return e;
 }
 
 // ------------------------------------------------------------------ plane fit, no allocation
