@@ -260,6 +260,31 @@ int smg_occ_track(smg_occ* o, const smg_scan2* scans, const double* pose0, const
  * unknown, 0..100), and the matcher's quantised probability; any pointer may be NULL. */
 int smg_occ_get_cells(smg_occ* o, int m, int16_t* L, uint8_t* seen, int8_t* c8, uint16_t* q);
 
+/* ---- association stress ---- */
+/* The association step of ObjectMap::update (scenemap objmap.cpp:774-810: box gate, best
+ * cosine above the threshold, top-1) in its dense stress form: every detection against a bank
+ * of memory vectors.  Embeddings are bf16 (raw uint16 bits), L2-normalised, dim a multiple of
+ * 64, rows 16-byte aligned; boxes are float (lo x, y, z, hi x, y, z). */
+typedef struct smg_assoc smg_assoc;
+int smg_assoc_create(int max_det, int max_mem, int dim, int dev, smg_assoc** out);
+int smg_assoc_destroy(smg_assoc* a);
+/* For each detection d: the memory j with 3D IoU(box_d, box_j) > iou_min and the largest
+ * fp64 dot product (bf16 values, summed in index order) >= cos_min, lowest j on ties, else -1
+ * (match[d]); score[d] = that dot product; certified[d] = 1 when the decision was read off the
+ * tensor-core scores, 0 when it was recomputed exactly (near the threshold or a near tie).
+ * scores (optional, n_det x n_mem fp32): the raw tensor-core dot products.  All pointers are
+ * device memory; asynchronous on `stream`. */
+int smg_assoc_match(smg_assoc* a, const uint16_t* det, const float* det_box, int n_det, const uint16_t* mem, const float* mem_box,
+                    int n_mem, float iou_min, double cos_min, int32_t* match, double* score, int32_t* certified,
+                    float* scores, void* stream);
+/* Device error word of the batch of matches so far (1 = a pipeline wait timed out). */
+int smg_assoc_error(smg_assoc* a);
+/* Instrumentation: enable = 1 makes the following matches record %globaltimer at 16 points of
+ * one CTA (0 start, 1 TMEM ready, 2 first loads issued, 3 first stage landed, 4 last stage
+ * landed, 5 all MMAs done, 6 epilogue done, 7 exit, 8-11 epilogue steps); out16 (or NULL)
+ * receives the last record. */
+int smg_assoc_stamps(smg_assoc* a, int enable, int64_t* out16);
+
 /* Batched plane fit: replaces scenemap::apPlaneFit (objprob.hpp:204, objprob.cpp:130-209), one
  * call per point set there.  Set s is the float (x, y, z) points xyz[3*off[s] .. 3*off[s+1]),
  * fitted with distance tau and RANSAC seed seeds[s] (apSeed values), at most max_iters

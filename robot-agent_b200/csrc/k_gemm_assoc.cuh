@@ -30,11 +30,12 @@
 #define AG_BN 256
 #define AG_BK 64
 #define AG_STAGES 4
-#define AG_THREADS 128
+#define AG_THREADS 512   // 16 warps: warps w, w+4, w+8, w+12 read the same TMEM lanes, a quarter of the columns each
+#define AG_GROUPS (AG_THREADS / 128)
 #define AG_A_BYTES (AG_BM * AG_BK * 2)
 #define AG_B_BYTES (AG_BN * AG_BK * 2)
 #define AG_TMEM_COLS 256
-#define AG_SMEM (AG_STAGES * (AG_A_BYTES + AG_B_BYTES) + 1024 + 256 + AG_BN * 6 * 4)
+#define AG_SMEM (AG_STAGES * (AG_A_BYTES + AG_B_BYTES) + 1024 + 256 + AG_BN * 8 * 4 + AG_GROUPS * AG_BM * 3 * 4)
 #define AG_WAIT_NS 200000000ull   // 0.2 s per wait
 
 // instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A bf16 (bits 7-9 = 1), B bf16
@@ -57,6 +58,7 @@ struct AssocArgs {
   double* score;          // [n_det]
   int32_t* certified;     // [n_det] 1 = decided from the tensor-core scores, 0 = recomputed
   int32_t* err;           // [1]
+  unsigned long long* stamps;   // optional: %globaltimer at 16 points of CTA (0, 0) (instrumentation)
 };
 
 DEV uint32_t ag_smem(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -143,6 +145,16 @@ DEV void ag_tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+DEV void ag_tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // 3D AABB IoU > tmin, float, fixed operation order (the restatement uses the same)
 DEV bool ag_gate(const float* a, float avol, const float* b, float tmin) {
   float inter = 1.f;
@@ -172,7 +184,10 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n0 = blockIdx.x * AG_BN, m0 = blockIdx.y * AG_BM;
   const int nk = g.dim / AG_BK;
-  if (tid == 0) {
+  const bool stamp = g.stamps && blockIdx.x == 0 && blockIdx.y == 0;
+  if (stamp && tid == 0) g.stamps[0] = ag_now();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (tid == 0) {   // barriers, then the first AG_STAGES loads go out before anything else
     for (int s = 0; s < AG_STAGES; ++s) {
       ag_mbar_init(&full[s], 1);
       ag_mbar_init(&empty[s], 1);
@@ -180,10 +195,23 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
     ag_mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sh_fail = 0;
+    for (int kb = 0; kb < AG_STAGES && kb < nk; ++kb) {
+      ag_expect_tx(&full[kb], AG_A_BYTES + AG_B_BYTES);
+      ag_tma_2d(&tmA, &full[kb], sA + kb * AG_A_BYTES, kb * AG_BK, m0);
+      ag_tma_2d(&tmB, &full[kb], sB + kb * AG_B_BYTES, kb * AG_BK, n0);
+    }
+    if (stamp) g.stamps[2] = ag_now();
   }
-  for (int i = tid; i < AG_BN * 6; i += blockDim.x) {
-    const int j = n0 + i / 6;
-    mbox[i] = j < g.n_mem ? g.mem_box[(size_t)j * 6 + i % 6] : 0.f;
+  // memory boxes of the tile: lo xyz, hi xyz, volume ((dx * dy) * dz), pad
+  for (int c = tid; c < AG_BN; c += blockDim.x) {
+    const int j = n0 + c;
+    float b[6] = {0, 0, 0, 0, 0, 0};
+    if (j < g.n_mem)
+      for (int k = 0; k < 6; ++k) b[k] = g.mem_box[(size_t)j * 6 + k];
+    float* o = mbox + 8 * c;
+    for (int k = 0; k < 6; ++k) o[k] = b[k];
+    o[6] = ((b[3] - b[0]) * (b[4] - b[1])) * (b[5] - b[2]);
+    o[7] = 0.f;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ag_smem(tmem_slot)),
@@ -195,9 +223,10 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
   __syncthreads();
   ag_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (stamp && tid == 0) g.stamps[1] = ag_now();
 
-  if (warp == 0 && lane == 0) {   // TMA producer
-    for (int kb = 0; kb < nk; ++kb) {
+  if (warp == 0 && lane == 0) {   // TMA producer (the first AG_STAGES loads are already out)
+    for (int kb = AG_STAGES; kb < nk; ++kb) {
       const int s = kb % AG_STAGES;
       const uint32_t ph = (uint32_t)(kb / AG_STAGES) & 1u;
       if (!ag_wait(&empty[s], ph ^ 1u)) { sh_fail = 1; break; }
@@ -210,6 +239,8 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
       const int s = kb % AG_STAGES;
       const uint32_t ph = (uint32_t)(kb / AG_STAGES) & 1u;
       if (!ag_wait(&full[s], ph)) { sh_fail = 1; break; }
+      if (stamp && kb == 0) g.stamps[3] = ag_now();
+      if (stamp && kb == nk - 1) g.stamps[4] = ag_now();
       ag_fence_after();
       const uint64_t da = ag_desc(sA + s * AG_A_BYTES), db = ag_desc(sB + s * AG_B_BYTES);
 #pragma unroll
@@ -225,42 +256,97 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
       ok = ag_wait(&full[kb % AG_STAGES], (uint32_t)(kb / AG_STAGES) & 1u) && ok;
   }
   ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  if (stamp && tid == 0) g.stamps[5] = ag_now();
   ag_fence_after();
-  const int r = warp * 32 + lane, d = m0 + r;
+  const int quarter = warp & 3, grp = warp >> 2;   // TMEM lane quarter, column group
+  const int r = quarter * 32 + lane, d = m0 + r;
   float bx[6] = {0, 0, 0, 0, 0, 0};
   if (d < g.n_det)
     for (int k = 0; k < 6; ++k) bx[k] = g.det_box[(size_t)d * 6 + k];
   const float avol = ((bx[3] - bx[0]) * (bx[4] - bx[1])) * (bx[5] - bx[2]);
+  if (stamp && tid == 0) g.stamps[8] = ag_now();
+  const float tmin = g.iou_min;
+  const float4* mb4 = (const float4*)mbox;
   float b1 = -INFINITY, b2 = -INFINITY;
   int i1 = -1;
+  const int jlim = g.n_mem - n0;   // columns c < jlim are real memories
+  constexpr int CW = AG_BN / AG_GROUPS;
   if (ok) {
-    for (int c0 = 0; c0 < AG_BN; c0 += 32) {
-      uint32_t v[32];
-      ag_tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+    for (int c0 = grp * CW; c0 < (grp + 1) * CW; c0 += 16) {
+      uint32_t v[16];
+      ag_tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+      if (stamp && tid == 0 && c0 == 0) g.stamps[9] = ag_now();
+      if (g.scores && d < g.n_det) {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int j = n0 + c0 + c;
-        const float sc = __uint_as_float(v[c]);
-        if (d >= g.n_det || j >= g.n_mem) continue;
-        if (g.scores) g.scores[(size_t)d * g.n_mem + j] = sc;
-        if (!ag_gate(bx, avol, &mbox[(c0 + c) * 6], g.iou_min)) continue;
-        if (sc > b1) { b2 = b1; b1 = sc; i1 = j; }
-        else if (sc > b2) b2 = sc;
+        for (int c = 0; c < 16; ++c)
+          if (c0 + c < jlim) g.scores[(size_t)d * g.n_mem + n0 + c0 + c] = __uint_as_float(v[c]);
+      }
+      // pass 1: x and y overlap (a superset of the gate), one bit per column; the warp's OR
+      uint32_t mine = 0;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const float4 p = mb4[2 * (c0 + c)], q = mb4[2 * (c0 + c) + 1];   // lo xyz hi.x | hi.y hi.z vol pad
+        const float e0 = fminf(bx[3], p.w) - fmaxf(bx[0], p.x);
+        const float e1 = fminf(bx[4], q.x) - fmaxf(bx[1], p.y);
+        mine |= (uint32_t)(e0 > 0.f && e1 > 0.f && c0 + c < jlim) << c;
+      }
+      const uint32_t any = __reduce_or_sync(0xffffffffu, mine);
+      if (!any) continue;
+      // pass 2: the full gate (the same float operations as ag_gate and the restatement) and the
+      // top-2 update, only on columns some lane of the warp still has; columns in increasing
+      // order, so the first maximum keeps the lowest index
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        if (!((any >> c) & 1u)) continue;
+        const float4 p = mb4[2 * (c0 + c)], q = mb4[2 * (c0 + c) + 1];
+        const float e0 = fminf(bx[3], p.w) - fmaxf(bx[0], p.x);
+        const float e1 = fminf(bx[4], q.x) - fmaxf(bx[1], p.y);
+        const float e2 = fminf(bx[5], q.y) - fmaxf(bx[2], p.z);
+        const float inter = (e0 * e1) * e2;
+        const float uni = (avol + q.z) - inter;
+        const bool pass = ((mine >> c) & 1u) && e2 > 0.f && inter > tmin * uni;
+        const float sc = pass ? __uint_as_float(v[c]) : -INFINITY;
+        const bool gt = sc > b1;
+        b2 = gt ? b1 : fmaxf(b2, sc);
+        i1 = gt ? n0 + c0 + c : i1;
+        b1 = gt ? sc : b1;
       }
     }
   }
-  if (d < g.n_det) {
-    const size_t t = (size_t)d * g.n_tiles + blockIdx.x;
-    g.t_best[t] = b1;
-    g.t_second[t] = b2;
-    g.t_idx[t] = i1;
+  if (stamp && tid == 0) g.stamps[10] = ag_now();
+  // merge the column groups of each row in column order (ties keep the lower index)
+  float* xb = (float*)(mbox + 8 * AG_BN);   // groups x 128 rows x (b1, b2, i1)
+  if (grp > 0) {
+    float* o = xb + 3 * ((size_t)grp * AG_BM + r);
+    o[0] = b1;
+    o[1] = b2;
+    ((int*)o)[2] = i1;
   }
+  __syncthreads();
+  if (stamp && tid == 0) g.stamps[11] = ag_now();
+  if (grp == 0) {
+    for (int q2 = 1; q2 < AG_GROUPS; ++q2) {
+      const float* o = xb + 3 * ((size_t)q2 * AG_BM + r);
+      const float c1 = o[0], c2 = o[1];
+      const int ci = ((const int*)o)[2];
+      if (ci >= 0 && c1 > b1) { b2 = fmaxf(b1, c2); b1 = c1; i1 = ci; }
+      else b2 = fmaxf(b2, c1);
+    }
+    if (d < g.n_det) {
+      const size_t t = (size_t)d * g.n_tiles + blockIdx.x;
+      g.t_best[t] = i1 >= 0 ? b1 : -INFINITY;
+      g.t_second[t] = b2;
+      g.t_idx[t] = i1;
+    }
+  }
+  if (stamp && tid == 0) g.stamps[6] = ag_now();
   ag_fence_before();
   __syncthreads();
   if (tid == 0 && (sh_fail || !ok)) atomicOr(g.err, 1);
   if (warp == 0) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(AG_TMEM_COLS) : "memory");
   }
+  if (stamp && tid == 0) g.stamps[7] = ag_now();
 }
 
 // fp64 dot of two bf16 rows summed in index order (the restatement's definition)
@@ -272,6 +358,7 @@ DEV double ag_dot_seq(const uint16_t* a, const uint16_t* b, int D) {
 
 // one warp per detection: combine the tiles, certify, or recompute in fp64
 __global__ void __launch_bounds__(256) k_assoc_decide(AssocArgs g) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // the GEMM grid has completed (launched with PDL)
   const int lane = threadIdx.x & 31;
   const int d = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (d >= g.n_det) return;

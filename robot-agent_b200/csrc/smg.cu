@@ -1289,6 +1289,8 @@ int smg_occ_get_cells(smg_occ* o, int m, int16_t* L, uint8_t* seen, int8_t* c8, 
 // ------------------------------------------------------------------ association stress (config 2)
 struct smg_assoc {
   int dev = 0, max_det = 0, max_mem = 0, dim = 0;
+  unsigned long long* stamps = nullptr;   // instrumentation (smg_assoc_stamps)
+  bool stamping = false;
   float* t_best = nullptr;
   float* t_second = nullptr;
   int32_t* t_idx = nullptr;
@@ -1330,6 +1332,7 @@ int smg_assoc_destroy(smg_assoc* a) {
   cudaFree(a->t_second);
   cudaFree(a->t_idx);
   cudaFree(a->err);
+  cudaFree(a->stamps);
   delete a;
   return SMG_OK;
 }
@@ -1374,10 +1377,37 @@ int smg_assoc_match(smg_assoc* a, const uint16_t* det, const float* det_box, int
   g.delta = (double)a->dim * std::ldexp(1.0, -22);   // > K * 2^-23 (fp32 accumulation, |z| <= 1.01)
   g.t_best = a->t_best; g.t_second = a->t_second; g.t_idx = a->t_idx;
   g.scores = scores; g.match = match; g.score = score; g.certified = certified; g.err = a->err;
+  g.stamps = a->stamping ? a->stamps : nullptr;
   const dim3 grid(g.n_tiles, (n_det + AG_BM - 1) / AG_BM);
   k_assoc_gemm<<<grid, AG_THREADS, AG_SMEM, st>>>(tA, tB, g);
-  k_assoc_decide<<<(n_det + 7) / 8, 256, 0, st>>>(g);
+  {   // programmatic dependent launch: the decide grid is scheduled while the GEMM drains
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((n_det + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    CK(cudaLaunchKernelEx(&cfg, k_assoc_decide, g));
+  }
   CK(cudaGetLastError());
+  return SMG_OK;
+}
+
+int smg_assoc_stamps(smg_assoc* a, int enable, int64_t* out16) {
+  if (!a) return fail(SMG_ERR_ARGS, "smg_assoc_stamps: null");
+  CK(cudaSetDevice(a->dev));
+  if (!a->stamps) {
+    CK(cudaMalloc(&a->stamps, 16 * sizeof(unsigned long long)));
+    CK(cudaMemset(a->stamps, 0, 16 * sizeof(unsigned long long)));
+  }
+  if (out16) {
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(out16, a->stamps, 16 * sizeof(int64_t), cudaMemcpyDeviceToHost));
+  }
+  a->stamping = enable != 0;
   return SMG_OK;
 }
 

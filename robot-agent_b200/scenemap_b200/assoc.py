@@ -26,6 +26,7 @@ def _lib():
         L.smg_assoc_destroy.argtypes = [vp]
         L.smg_assoc_match.argtypes = [vp, vp, vp, C.c_int, vp, vp, C.c_int, C.c_float, C.c_double, vp, vp, vp, vp, vp]
         L.smg_assoc_error.argtypes = [vp]
+        L.smg_assoc_stamps.argtypes = [vp, C.c_int, C.POINTER(C.c_int64)]
         _ready = True
     return L
 
@@ -109,6 +110,12 @@ class AssocGPU:
                                       vp(c.data_ptr()), vp(scores.data_ptr() if scores is not None else 0), vp(stream)),
                "smg_assoc_match")
         return m, s, c
+
+    def stamps(self, enable: bool):
+        """Enable phase timestamps; returns the last record (8 x ns, %globaltimer)."""
+        out = (C.c_int64 * 16)()
+        _check(_lib().smg_assoc_stamps(self.h, 1 if enable else 0, out), "smg_assoc_stamps")
+        return [int(v) for v in out]
 
     def error(self) -> int:
         return _check(_lib().smg_assoc_error(self.h), "smg_assoc_error")

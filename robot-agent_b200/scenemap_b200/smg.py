@@ -84,7 +84,9 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
             "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
             "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
             "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
-           "smg_get_work", "smg_plane_fit", "smg_plane_fit_noalloc"]
+           "smg_get_work", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
+           "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
+           "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps"]
 
 NUM_KERNELS = 14
 
