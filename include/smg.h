@@ -260,6 +260,39 @@ int smg_occ_track(smg_occ* o, const smg_scan2* scans, const double* pose0, const
  * unknown, 0..100), and the matcher's quantised probability; any pointer may be NULL. */
 int smg_occ_get_cells(smg_occ* o, int m, int16_t* L, uint8_t* seen, int8_t* c8, uint16_t* q);
 
+/* ---- text model: label log-likelihoods and names ---- */
+/* ApText (scenemap objprob.hpp:40-54), device pointers: rows x dim L2-normalised text
+ * embeddings, the label of each row, SigLIP logit scale/bias, and the optional per-label
+ * log prior, log-size Gaussian (mu, sd; sd <= 0 = unused) and hypernym parent (-1 = none). */
+typedef struct smg_text {
+  int32_t dim, n_labels, rows;
+  const float* text;
+  const int32_t* row_label;
+  float scale, bias;
+  const float* log_prior;
+  const float* ls_mu;
+  const float* ls_sd;
+  const int32_t* parent;
+  int32_t object_label;
+} smg_text;
+/* apLabelLogLik (objprob.cpp:287-310) for n embeddings z (n x dim, device): out (n x n_labels,
+ * device) = per-label log sigma(scale * max row cosine + bias), normalised over the labels;
+ * labels without a text row get -1e30.  n_labels <= 1024.  Asynchronous on `stream`. */
+int smg_label_loglik(const smg_text* t, const float* z, int n, float* out, void* stream);
+/* ApParams naming fields (objprob.hpp:84-87). */
+typedef struct smg_name_params {
+  double whole_w, name_wmax, size_w, name_tau;
+} smg_name_params;
+/* apName (objprob.cpp:396-455) for n_obj objects (device arrays, n_obj x n_labels for the L
+ * vectors; NULL = that vector is empty in the reference's ApState): Sigma w log p from fragment
+ * and whole views (lw_* = their weights), external and geometric log-likelihoods, object size
+ * (longest side, m).  Outputs: post (n_obj x n_labels), lab3 = {name_lab, top_lab, rolled} and
+ * val3 = {name_p, top_p, name_H} per object; name_lab = -2 when the object has no image
+ * evidence (the reference then leaves its name unchanged). */
+int smg_name(const smg_text* t, const smg_name_params* p, int n_obj, const float* L_frag, const double* lw_frag,
+             const float* L_whole, const double* lw_whole, const float* L_ext, const float* L_geo, const double* size,
+             float* post, int32_t* lab3, float* val3, void* stream);
+
 /* ---- association stress ---- */
 /* The association step of ObjectMap::update (scenemap objmap.cpp:774-810: box gate, best
  * cosine above the threshold, top-1) in its dense stress form: every detection against a bank

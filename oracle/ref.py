@@ -397,3 +397,47 @@ def csm(cells: dict, hits, pose0, lin_half=6, ang_half=20, ang_step=None, w_t=10
              _p(hy, C.c_float), len(a), _p(p0, C.c_double), lin_half, ang_half, ang_step, w_t, w_r, _p(bi, C.c_int32),
              _p(bs, C.c_double), _p(bp, C.c_double))
     return int(bi[0]), float(bs[0]), bp
+
+
+# ---------------------------------------------------------------- text model (apLabelLogLik, apName)
+def label_loglik(text, row_label, n_labels, scale, bias, z):
+    L = ref_lib()
+    P = C.POINTER
+    L.ref_label_loglik.argtypes = [C.c_int, C.c_int, C.c_int, P(C.c_float), P(C.c_int32), C.c_float, C.c_float,
+                                   P(C.c_float), C.c_int, P(C.c_float)]
+    t = np.ascontiguousarray(text, np.float32)
+    rl = np.ascontiguousarray(row_label, np.int32)
+    zz = np.ascontiguousarray(z, np.float32).reshape(-1, t.shape[1])
+    out = np.zeros((len(zz), n_labels), np.float32)
+    L.ref_label_loglik(t.shape[1], n_labels, len(t), _p(t, C.c_float), _p(rl, C.c_int32), scale, bias, _p(zz, C.c_float),
+                       len(zz), _p(out, C.c_float))
+    return out
+
+
+def name(text, row_label, n_labels, scale, bias, log_prior, ls_mu, ls_sd, parent, object_label, whole_w, name_wmax,
+         size_w, name_tau, L_frag, lw_frag, L_whole, lw_whole, L_ext, L_geo, size):
+    """apName of one object (ref_name): (post, name_lab, name_p, top_lab, top_p, name_H, rolled, named)."""
+    L = ref_lib()
+    P = C.POINTER
+    L.ref_name.argtypes = [C.c_int, C.c_int, C.c_int, P(C.c_float), P(C.c_int32), C.c_float, C.c_float, P(C.c_float),
+                           P(C.c_float), P(C.c_float), P(C.c_int32), C.c_int, C.c_double, C.c_double, C.c_double,
+                           C.c_double, P(C.c_float), C.c_double, P(C.c_float), C.c_double, P(C.c_float), P(C.c_float),
+                           C.c_double, P(C.c_float), P(C.c_double)]
+    f = lambda a: None if a is None else _p(np.ascontiguousarray(a, np.float32), C.c_float)
+    keep = [np.ascontiguousarray(a, np.float32) for a in (text, log_prior, ls_mu, ls_sd, L_frag, L_whole, L_ext, L_geo)
+            if a is not None]
+    t = np.ascontiguousarray(text, np.float32)
+    rl = np.ascontiguousarray(row_label, np.int32)
+    par = None if parent is None else np.ascontiguousarray(parent, np.int32)
+    arrs = {}
+    for k, a in (("lp", log_prior), ("mu", ls_mu), ("sd", ls_sd), ("lf", L_frag), ("lwh", L_whole), ("le", L_ext), ("lg", L_geo)):
+        arrs[k] = None if a is None else np.ascontiguousarray(a, np.float32)
+    fp = lambda k: None if arrs[k] is None else _p(arrs[k], C.c_float)
+    post = np.zeros(n_labels, np.float32)
+    f6 = np.zeros(6)
+    named = L.ref_name(t.shape[1], n_labels, len(t), _p(t, C.c_float), _p(rl, C.c_int32), scale, bias, fp("lp"), fp("mu"),
+                       fp("sd"), None if par is None else _p(par, C.c_int32), object_label, whole_w, name_wmax, size_w,
+                       name_tau, fp("lf"), lw_frag, fp("lwh"), lw_whole, fp("le"), fp("lg"), size, _p(post, C.c_float),
+                       _p(f6, C.c_double))
+    del keep
+    return post, int(f6[0]), float(f6[1]), int(f6[2]), float(f6[3]), float(f6[4]), int(f6[5]), bool(named)

@@ -427,4 +427,53 @@ double ref_contact(const float* cloud, int nc, const float* pts, int np, double 
   return apContact(pts, np, idx, cell);
 }
 
+// ---- text model: apLabelLogLik and apName (objprob.cpp:287-310, :396-455) ----
+static ApText make_text(int dim, int n_labels, int rows, const float* text, const int32_t* row_label, float scale, float bias,
+                        const float* log_prior, const float* ls_mu, const float* ls_sd, const int32_t* parent, int object_label) {
+  ApText T;
+  T.dim = dim;
+  T.n_labels = n_labels;
+  T.text.assign(text, text + size_t(rows) * dim);
+  T.row_label.assign(row_label, row_label + rows);
+  T.scale = scale;
+  T.bias = bias;
+  if (log_prior) T.log_prior.assign(log_prior, log_prior + n_labels);
+  if (ls_mu && ls_sd) { T.ls_mu.assign(ls_mu, ls_mu + n_labels); T.ls_sd.assign(ls_sd, ls_sd + n_labels); }
+  if (parent) T.parent.assign(parent, parent + n_labels);
+  T.object_label = object_label;
+  return T;
+}
+
+void ref_label_loglik(int dim, int n_labels, int rows, const float* text, const int32_t* row_label, float scale, float bias,
+                      const float* z, int n, float* out) {
+  const ApText T = make_text(dim, n_labels, rows, text, row_label, scale, bias, nullptr, nullptr, nullptr, nullptr, -1);
+  std::vector<float> ll;
+  for (int i = 0; i < n; ++i) {
+    apLabelLogLik(T, z + size_t(i) * dim, &ll);
+    for (int l = 0; l < n_labels; ++l) out[size_t(i) * n_labels + l] = ll[size_t(l)];
+  }
+}
+
+// apName of one object; L arrays of n_labels (NULL = empty vector).  out: post[n_labels],
+// f6 = {name_lab, name_p, top_lab, top_p, name_H, rolled}; returns 1 if apName produced a name.
+int ref_name(int dim, int n_labels, int rows, const float* text, const int32_t* row_label, float scale, float bias,
+             const float* log_prior, const float* ls_mu, const float* ls_sd, const int32_t* parent, int object_label,
+             double whole_w, double name_wmax, double size_w, double name_tau, const float* L_frag, double lw_frag,
+             const float* L_whole, double lw_whole, const float* L_ext, const float* L_geo, double size, float* post, double* f6) {
+  const ApText T = make_text(dim, n_labels, rows, text, row_label, scale, bias, log_prior, ls_mu, ls_sd, parent, object_label);
+  ApParams p;
+  p.whole_w = whole_w; p.name_wmax = name_wmax; p.size_w = size_w; p.name_tau = name_tau;
+  ApState s;
+  if (L_frag) s.L_frag.assign(L_frag, L_frag + n_labels);
+  if (L_whole) s.L_whole.assign(L_whole, L_whole + n_labels);
+  if (L_ext) s.L_ext.assign(L_ext, L_ext + n_labels);
+  if (L_geo) s.L_geo.assign(L_geo, L_geo + n_labels);
+  s.lw_frag = lw_frag;
+  s.lw_whole = lw_whole;
+  apName(s, T, p, size);
+  for (int l = 0; l < n_labels; ++l) post[l] = size_t(l) < s.post.size() ? s.post[size_t(l)] : 0.f;
+  f6[0] = s.name_lab; f6[1] = s.name_p; f6[2] = s.top_lab; f6[3] = s.top_p; f6[4] = s.name_H; f6[5] = s.rolled;
+  return !s.post.empty();
+}
+
 }  // extern "C"

@@ -29,6 +29,7 @@
 #include "k_grid.cuh"
 #include "k_occ.cuh"
 #include "k_gemm_assoc.cuh"
+#include "k_text.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -1417,6 +1418,47 @@ int smg_assoc_error(smg_assoc* a) {
   int32_t e = 0;
   CK(cudaMemcpy(&e, a->err, sizeof(e), cudaMemcpyDeviceToHost));
   return e;
+}
+
+// ------------------------------------------------------------------ text model (apLabelLogLik, apName)
+static int text_dev(const smg_text* t, TextDev* T, const char* who) {
+  if (!t || t->dim <= 0 || t->n_labels <= 0 || t->n_labels > TXT_MAX_LABELS || t->rows <= 0 || !t->text || !t->row_label ||
+      (!t->ls_mu) != (!t->ls_sd))
+    return fail(SMG_ERR_ARGS, (std::string(who) + ": bad text model").c_str());
+  T->dim = t->dim; T->n_labels = t->n_labels; T->rows = t->rows; T->text = t->text; T->row_label = t->row_label;
+  T->scale = t->scale; T->bias = t->bias; T->log_prior = t->log_prior; T->ls_mu = t->ls_mu; T->ls_sd = t->ls_sd;
+  T->parent = t->parent; T->object_label = t->object_label;
+  return SMG_OK;
+}
+
+int smg_label_loglik(const smg_text* t, const float* z, int n, float* out, void* stream) {
+  TextDev T;
+  if (int r = text_dev(t, &T, "smg_label_loglik")) return r;
+  if (!z || !out || n <= 0) return fail(SMG_ERR_ARGS, "smg_label_loglik: bad arguments");
+  const size_t sm = sizeof(float) * ((size_t)T.dim + T.n_labels);
+  if (sm > 200 * 1024) return fail(SMG_ERR_ARGS, "smg_label_loglik: dim + n_labels too large");
+  if (sm > 48 * 1024) CK(cudaFuncSetAttribute(k_label_loglik, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  k_label_loglik<<<n, 256, sm, (cudaStream_t)stream>>>(T, z, n, out);
+  CK(cudaGetLastError());
+  return SMG_OK;
+}
+
+int smg_name(const smg_text* t, const smg_name_params* p, int n_obj, const float* L_frag, const double* lw_frag,
+             const float* L_whole, const double* lw_whole, const float* L_ext, const float* L_geo, const double* size,
+             float* post, int32_t* lab3, float* val3, void* stream) {
+  TextDev T;
+  if (int r = text_dev(t, &T, "smg_name")) return r;
+  if (!p || n_obj <= 0 || !size || !post || !lab3 || !val3 || (L_frag && !lw_frag) || (L_whole && !lw_whole))
+    return fail(SMG_ERR_ARGS, "smg_name: bad arguments");
+  NameArgs a;
+  a.n_obj = n_obj; a.whole_w = p->whole_w; a.name_wmax = p->name_wmax; a.size_w = p->size_w; a.name_tau = p->name_tau;
+  a.L_frag = L_frag; a.lw_frag = lw_frag; a.L_whole = L_whole; a.lw_whole = lw_whole; a.L_ext = L_ext; a.L_geo = L_geo;
+  a.size = size; a.post = post; a.lab = lab3; a.val = val3;
+  const size_t sm = sizeof(double) * 2 * (size_t)T.n_labels * 8;
+  if (sm > 48 * 1024) CK(cudaFuncSetAttribute(k_name, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  k_name<<<(n_obj + 7) / 8, 256, sm, (cudaStream_t)stream>>>(T, a);
+  CK(cudaGetLastError());
+  return SMG_OK;
 }
 
 // ------------------------------------------------------------------ plane fit, no allocation

@@ -86,7 +86,7 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
             "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
            "smg_get_work", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
-           "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps"]
+           "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name"]
 
 NUM_KERNELS = 14
 
