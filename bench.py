@@ -223,7 +223,9 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     M = args.maps
     n_total = args.preroll + args.warmup + args.steps + args.e2e_steps
-    wl = RoomBatch(M, 1000, n_total, D=1152, bf16=True, max_det=24, map_offset=rank * M, device=str(dev))
+    from scenemap_b200 import dist
+    wl = RoomBatch(M, 1000, n_total, D=1152, bf16=True, max_det=24, map_offset=dist.rank_maps(rank, world, M)[0],
+                   device=str(dev))
     B = smg.Batch(M, max_objects=args.max_objects, emb_dim=1152, max_w=640, max_h=480, max_det=24,
                   grid=(512, 512, -256 + 60, -256 + 50), dev=local_rank)
     stream = torch.cuda.current_stream(dev)
@@ -312,16 +314,9 @@ def run_b200(args, rank, world, local_rank):
     for m in range(M):
         s = B.stats(m)
         stats[m] = list(s.values())
-    st_t = torch.from_numpy(stats).to(dev)
-    if world > 1:
-        gathered = [torch.empty_like(st_t) for _ in range(world)]
-        torch.distributed.all_gather(gathered, st_t)
-        all_stats = torch.cat(gathered).cpu().numpy()
-        tt = torch.tensor([t, t_e2e], dtype=torch.float64, device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        t, t_e2e = float(tt[0]), float(tt[1])
-    else:
-        all_stats = stats
+    from scenemap_b200 import dist
+    all_stats = dist.gather_stats(stats, world, dev)          # NCCL all_gather when world > 1
+    t, t_e2e = dist.max_over_ranks([t, t_e2e], world, dev)   # device times: max over ranks
     n_obj = [len(B.objects(m)) for m in range(min(M, 4))]
     B.close()
     return dict(t=t, t_e2e=t_e2e, kt=kt, launches=launches, err=err, clocks=clocks, work=work,
