@@ -176,6 +176,30 @@ DEV int block_excl_scan(int flag, int* total, BlockScratch& s) {
   return before + x - flag;
 }
 
+// Exclusive scan like block_excl_scan with one barrier: the per-warp totals go to one of two
+// buffers chosen by the caller's running call count `it`, so the next call (which writes the
+// other buffer after its own barrier) cannot race with this call's reads.  Consecutive calls
+// must pass consecutive `it` values.
+DEV int block_scan_db(int flag, int* total, int (*buf)[33], int it) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = flag;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  int* b = buf[it & 1];
+  if (lane == 31) b[wid] = x;
+  __syncthreads();
+  int before = 0, tot = 0;
+  for (int w = 0; w < nw; ++w) {
+    const int v = b[w];
+    before += w < wid ? v : 0;
+    tot += v;
+  }
+  *total = tot;
+  return before + x - flag;
+}
+
 // order-preserving double <-> uint64 map (total order, -0.0 < +0.0)
 DEV uint64_t d_ord(double v) {
   const uint64_t u = (uint64_t)__double_as_longlong(v);

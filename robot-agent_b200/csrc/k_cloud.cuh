@@ -90,14 +90,16 @@ DEV void cloud_trim(const Batch& B, size_t cs, const Work& W, int* hist, BlockSc
   for (int i = threadIdx.x; i < n; i += blockDim.x) lt += W.scr[i] < cut;
   const int eq_drop = drop - block_sum_i(lt, bs);
   int w = 0, eq_seen = 0;
+  __shared__ int trim_db[2][33];
+  int trim_it = 0;
   for (int c0 = 0; c0 < n; c0 += blockDim.x) {
     const int i = c0 + threadIdx.x;
     const int is_eq = i < n && W.scr[i] == cut;
     int toteq;
-    const int peq = block_excl_scan(is_eq, &toteq, bs);
+    const int peq = block_scan_db(is_eq, &toteq, trim_db, trim_it++);
     const int k = i < n && (W.scr[i] > cut || (is_eq && eq_seen + peq >= eq_drop));
     int tot;
-    const int pos = block_excl_scan(k, &tot, bs);
+    const int pos = block_scan_db(k, &tot, trim_db, trim_it++);
     if (k && INB(w + pos, B.work_n, 404)) { W.t4[w + pos] = pts[i]; W.tc[w + pos] = col[i]; }
     w += tot;
     eq_seen += toteq;
@@ -162,6 +164,8 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
   uint32_t* col = B.crgb + cs * B.cap;
   int added = 0;
   __shared__ int sh_nw;
+  __shared__ int add_db[2][33];
+  int add_it = 0;
   if (tid == 0) sh_nw = 0;
   __syncthreads();
   for (int c0 = 0; c0 < n; c0 += blockDim.x) {
@@ -178,7 +182,7 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
       }
     }
     int tot;
-    const int pos = block_excl_scan(isnew, &tot, bs);
+    const int pos = block_scan_db(isnew, &tot, add_db, add_it++);
     if (i < n) W.dst[i] = -1;
     if (last >= 0) {
       const int d = isnew ? base + added + pos : old;

@@ -309,6 +309,7 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
 __global__ void __launch_bounds__(256) k_struct(Batch B) {
   __shared__ BlockScratch bs;
   __shared__ int hist[SEL_MAXQ * 256];
+  __shared__ int draws[RANSAC_DRAWS];
   __shared__ PlaneOut pout;
   const int m = blockIdx.y;
   const FrameDev& F = B.frames[m];
@@ -335,8 +336,8 @@ __global__ void __launch_bounds__(256) k_struct(Batch B) {
       Pt[3 * i + 2] = (float)(C.org[2] + (double)q.z);
     }
     __syncthreads();
-    plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, scr, 4096, hist, bs,
-              &pout);
+    plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, scr, 4096, hist, draws,
+              bs, &pout);
     int up = 0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) up += (double)Pt[3 * i + 2] > R.ceil_est - P.ceil_band;
     up = block_sum_i(up, bs);

@@ -16,6 +16,7 @@
 #define OBS_THREADS 512
 #define OBS_HASH 8192
 #define RANSAC_MAX 256
+#define RANSAC_DRAWS (3 * RANSAC_MAX + 64)
 // nsamp = ceil(n / max(1, n / min(n, 256))) <= 511, and cnt <= nsamp (objprob.cpp:135-158)
 #define NEED_N 512
 
@@ -79,7 +80,7 @@ DEV int pct_index(int n, double q) {   // min(n-1, size_t(q*(n-1) + 0.5)) (objma
 // draws, same adaptive stop; the stop count comes from a host-libm table).  Inlier sums are
 // block reductions (deterministic tree).  span1/span2 are not produced (no caller reads them).
 DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_iters, const int32_t* need_tab, double* scr, int cap,
-                   int* hist, BlockScratch& bs, PlaneOut* out) {
+                   int* hist, int* h_draw, BlockScratch& bs, PlaneOut* out) {
   __shared__ double sh_best[4];
   __shared__ int sh_bestc;
   __shared__ double sh_m[3], sh_V[3][3], sh_ev[3];
@@ -100,13 +101,31 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   const int ns = n < 256 ? n : 256;
   const int sstep = n / ns > 1 ? n / ns : 1;
   const int nsamp = (n + sstep - 1) / sstep;
+  // The splitmix state only advances by a constant, so draw k is mix(rs0 + (k + 1) * gamma):
+  // all draws (and their 64-bit remainders, the expensive part) are computed in parallel, and
+  // thread 0 then walks them with the reference's rejections (objprob.cpp:140-142), falling
+  // back to drawing in sequence if the rejections outrun the precomputed draws.
+  const uint64_t rs0 = seed ^ ((uint64_t)n << 32);   // h_draw: RANSAC_DRAWS shared ints of the caller
+  const int ndraw = 3 * iters + 64 < RANSAC_DRAWS ? 3 * iters + 64 : RANSAC_DRAWS;
+  for (int k = tid; k < ndraw; k += blockDim.x) {
+    uint64_t s = rs0 + (uint64_t)k * 0x9E3779B97F4A7C15ull;
+    h_draw[k] = (int)(splitmix(s) % (uint64_t)n);
+  }
+  __syncthreads();
   if (tid == 0) {
-    uint64_t rs = seed ^ ((uint64_t)n << 32);
+    int pos = 0;
+    uint64_t rs = rs0;
+    auto draw = [&]() -> int {
+      if (pos < ndraw) { ++pos; return h_draw[pos - 1]; }
+      if (pos == ndraw) rs = rs0 + (uint64_t)ndraw * 0x9E3779B97F4A7C15ull;
+      ++pos;
+      return (int)(splitmix(rs) % (uint64_t)n);
+    };
     for (int it = 0; it < iters; ++it) {
-      const int id0 = (int)(splitmix(rs) % (uint64_t)n);
+      const int id0 = draw();
       int id1, id2;
-      do id1 = (int)(splitmix(rs) % (uint64_t)n); while (id1 == id0);
-      do id2 = (int)(splitmix(rs) % (uint64_t)n); while (id2 == id0 || id2 == id1);
+      do id1 = draw(); while (id1 == id0);
+      do id2 = draw(); while (id2 == id0 || id2 == id1);
       h_id[it][0] = id0; h_id[it][1] = id1; h_id[it][2] = id2;
     }
   }
@@ -169,9 +188,11 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   }
   // two PCA refits (objprob.cpp:166-180); mp = plane whose inliers the last pass used.
   // Sums are block trees.  Where the outcome is ill-conditioned in the reference's own rounding
-  // (a point within 1e-11 of the tau boundary, a near-double smallest eigenvalue or a near-zero
-  // one, a nearly isotropic horizontal spread), thread 0 replays the whole refit with the
-  // reference's sequential sums in index order, so the result is the reference's bit for bit.
+  // (a point within 1e-11 of the tau boundary, a near-double smallest eigenvalue, a nearly
+  // isotropic horizontal spread), thread 0 replays the whole refit with the reference's
+  // sequential sums in index order, so the result is the reference's bit for bit.  A near-zero
+  // smallest eigenvalue (exactly planar points) is well-conditioned for the normal; only the
+  // thickness sqrt(ev0) then differs, by at most ~sqrt(1e-16 * ev2).
   __shared__ int sh_deg, sh_ni, sh_ok;
   __shared__ double sh_mp[4], sh_hc, sh_hs;
   if (tid == 0) sh_deg = 0;
@@ -216,7 +237,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
         sh_m[i] = m[i];
         for (int j = 0; j < 3; ++j) sh_V[i][j] = V[i][j];
       }
-      if (ev[1] - ev[0] <= 1e-3 * ev[2] || ev[0] <= 1e-12 * ev[2]) sh_deg = 1;
+      if (ev[1] - ev[0] <= 1e-3 * ev[2]) sh_deg = 1;   // near-double smallest eigenvalue: the normal is ill-defined
     }
     __syncthreads();
     pl[0] = sh_V[0][0]; pl[1] = sh_V[1][0]; pl[2] = sh_V[2][0];
@@ -359,7 +380,7 @@ DEV bool lab_is(const uint16_t* label, int W, int H, int u, int v, uint16_t L) {
   return u >= 0 && v >= 0 && u < W && v < H && INB((size_t)v * W + u, (size_t)W * H, 116) && label[(size_t)v * W + u] == L;
 }
 
-__global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
+__global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs per SM: <= 64 registers
   extern __shared__ unsigned char smem_raw[];
   uint64_t* hkey = (uint64_t*)smem_raw;                         // OBS_HASH keys
   uint32_t* hidx = (uint32_t*)(smem_raw + OBS_HASH * 8);        // OBS_HASH first index
@@ -411,6 +432,8 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
   }
   if (tid == 0) { wk_add(&B.maps[m], SMG_WK_OBS_PX, npix); wk_add(&B.maps[m], SMG_WK_DET, 1); }
   const double* T = F.T_mc;
+  __shared__ int scan_db[2][33];
+  int scan_it = 0;
   // 1. back-projection in raster order (objmap.cpp:667-688), ordered compaction
   int n = 0;
   for (int c0 = 0; c0 < npix; c0 += blockDim.x) {
@@ -438,7 +461,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
       }
     }
     int tot;
-    const int pos = block_excl_scan(ok, &tot, bs);
+    const int pos = block_scan_db(ok, &tot, scan_db, scan_it++);
     if (ok && INB(n + pos, B.pmax, 101)) {
       X[n + pos] = px; Y[n + pos] = py; Z[n + pos] = pz; ZC[n + pos] = zz;
       PU[n + pos] = uu; PV[n + pos] = vv;
@@ -490,7 +513,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
       }
     }
     int tot;
-    const int pos = block_excl_scan(keep, &tot, bs);
+    const int pos = block_scan_db(keep, &tot, scan_db, scan_it++);
     if (keep && INB(w + pos, B.pmax, 102)) { XK[w + pos] = X[i]; YK[w + pos] = Y[i]; ZK[w + pos] = Z[i]; }
     w += tot;
   }
@@ -518,7 +541,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
       }
     }
     int tot;
-    const int pos = block_excl_scan(emit, &tot, bs);
+    const int pos = block_scan_db(emit, &tot, scan_db, scan_it++);
     if (emit && INB(nc + pos, B.pmax, 103)) {
       CX[3 * (nc + pos)] = (float)X[i];
       CX[3 * (nc + pos) + 1] = (float)Y[i];
@@ -584,7 +607,8 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs(Batch B) {
     const double dc = hypot3(cen0 / nc - T[3], cen1 / nc - T[7], cen2 / nc - T[11]);
     const double tau = smin(P.ransac_tau_max, P.ransac_tau0 + P.ransac_tau_k * dc * dc);
     const uint64_t sb = (uint64_t)__double_as_longlong(F.stamp);
-    plane_fit(CX, nc, tau, ap_seed(sb, (uint64_t)k), P.ransac_iters, B.need_tab, SCR, B.pmax, (int*)smem_raw, bs, &pout);
+    plane_fit(CX, nc, tau, ap_seed(sb, (uint64_t)k), P.ransac_iters, B.need_tab, SCR, B.pmax, (int*)smem_raw,
+              (int*)smem_raw + SEL_MAXQ * 256, bs, &pout);
   } else if (tid == 0) {
     pout.ok = 0;
   }

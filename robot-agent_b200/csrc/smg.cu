@@ -902,6 +902,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_plane_sets(const float* xyz, con
                                                             const int32_t* need_tab, double* scr, double* out) {
   __shared__ BlockScratch bs;
   __shared__ int hist[SEL_MAXQ * 256];
+  __shared__ int draws[RANSAC_DRAWS];
   __shared__ PlaneOut po;
   const int s = blockIdx.x;
   if (s >= n_sets) return;
@@ -912,7 +913,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_plane_sets(const float* xyz, con
     return;
   }
   const int n = e - a;
-  plane_fit(xyz + 3 * (size_t)a, n, tau, seeds[s], max_iters, need_tab, scr + 2 * (size_t)a, n, hist, bs, &po);
+  plane_fit(xyz + 3 * (size_t)a, n, tau, seeds[s], max_iters, need_tab, scr + 2 * (size_t)a, n, hist, draws, bs, &po);
   if (threadIdx.x == 0) {
     const double dflt[10] = {0, 0, 0, 1, 1, 0, 0, 0, 0, 0};
     if (!po.ok) {

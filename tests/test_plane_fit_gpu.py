@@ -5,7 +5,8 @@ of tests/plane_clouds.py, all fitted in ONE call (one CTA per set).  Expected ou
 reference's, stored in tests/golden/plane_fit.json.  The RANSAC hypotheses, inlier counts and
 percentile selections are exact, so ok, inl, zmed, zlo and zhi must be identical; the PCA
 sums are tree reductions on the device instead of the reference's sequential sums, so the
-normal, thickness and horizontal span are compared within 1e-9 absolute.
+normal and horizontal span are compared within 1e-9 absolute and the thickness (a square root
+of the smallest eigenvalue) within 1e-7.
 """
 import json
 import os
@@ -26,12 +27,17 @@ def _golden():
     return {k: np.array([float.fromhex(v) for v in c["out"]]) for k, c in g["cases"].items()}
 
 
+ATOL_THICK = 1e-7   # thick = sqrt(ev0): for exactly planar points ev0 ~ 1e-17 and the square root
+                    # turns a 1e-16 difference of the covariance sums into ~1e-8
+
+
 def _compare(name, o, g):
     assert o[0] == g[0], f"{name}: ok {o[0]} vs {g[0]}"
     exact = [5, 6, 7, 8]           # inl, zmed, zlo, zhi
     assert np.array_equal(o[exact], g[exact]), f"{name}: {o[exact]} vs {g[exact]}"
-    fp = [1, 2, 3, 4, 9]           # n0..n2, thick, hspan
+    fp = [1, 2, 3, 9]              # n0..n2, hspan
     assert np.allclose(o[fp], g[fp], rtol=0, atol=ATOL_FP), f"{name}: {o[fp]} vs {g[fp]}"
+    assert abs(o[4] - g[4]) <= ATOL_THICK, f"{name}: thick {o[4]} vs {g[4]}"
 
 
 def test_plane_fit_batch_matches_reference():
