@@ -13,7 +13,7 @@
 #pragma once
 #include "k_life.cuh"
 
-#define MP_CTAS 4
+#define MP_CTAS 8
 #define MP_GL 8192   // gated pairs per CTA
 #define MP_SMEM(O) ((size_t)(O) * (6 * 8 + 2 * 4) + MP_GL * 4)
 
@@ -88,12 +88,27 @@ __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
     const int cn = a_small ? scn[i] : scn[j];
     const int stp = max(1, cn / max(1, P.contact_samples));
     const int nsp = cn > 0 ? (cn + stp - 1) / stp : 0;
-    double cs = -2;
-    if (a.nrm_frag > 0) cs = smax(cs, cos_max_warp(B, ogj, b, B.mu + ogi * B.D));
-    if (b.nrm_frag > 0) cs = smax(cs, cos_max_warp(B, ogi, a, B.mu + ogj * B.D));
-    const int hits = contact_hits_cloud_warp(B, csl, css, stp, nsp, P.contact_cell);
+    // cached cosine and contact of an unchanged pair
+    const uint32_t ca = B.clouds[(size_t)m * B.O + a.cloud_slot].version, cb = B.clouds[(size_t)m * B.O + b.cloud_slot].version;
+    PairCacheRec& pc = B.pcache[(size_t)m * PCACHE_SLOTS + (hmix(((uint64_t)a.id << 32) | b.id) & (PCACHE_SLOTS - 1))];
+    const bool hit = pc.ida == a.id && pc.idb == b.id && pc.va == a.ver && pc.vb == b.ver && pc.ca == ca && pc.cb == cb;
+    double cs = -2, contact = 0.0;
+    if (hit) {
+      cs = pc.cs;
+      contact = pc.contact;
+    } else {
+      if (a.nrm_frag > 0) cs = smax(cs, cos_max_warp(B, ogj, b, B.mu + ogi * B.D));
+      if (b.nrm_frag > 0) cs = smax(cs, cos_max_warp(B, ogi, a, B.mu + ogj * B.D));
+      const int hits = contact_hits_cloud_warp(B, csl, css, stp, nsp, P.contact_cell);
+      contact = (nsp > 0 && B.clouds[csl].cn > 0) ? (double)hits / (double)nsp : 0.0;
+      __syncwarp();
+      if (lane == 0) {
+        pc.ida = a.id; pc.idb = b.id; pc.va = a.ver; pc.vb = b.ver; pc.ca = ca; pc.cb = cb;
+        pc.cs = cs;
+        pc.contact = contact;
+      }
+    }
     if (lane == 0) {
-      const double contact = (nsp > 0 && B.clouds[csl].cn > 0) ? (double)hits / (double)nsp : 0.0;
       const double p = pair_p(sm.lo, sm.hi, sm.pos, contact, lg.lo, lg.hi, lg.pos, cs, P, true, nullptr);
       if (p >= P.merge_p) {
         const int c = atomicAdd(&B.mcand_n[m], 1);

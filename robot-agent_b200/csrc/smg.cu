@@ -363,6 +363,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.mcand_ab, MO * 8 * 2);
   DA(B.mcand_key, MO * 8);
   DA(B.mcand_n, M);
+  DA(B.pcache, (size_t)M * PCACHE_SLOTS);
   DA(B.vkey, (size_t)M * B.view_slots);
   DA(B.vfirst, (size_t)M * B.view_slots * SMG_VIEW_BANDS);
   DA(B.need_tab, NEED_N * NEED_N);

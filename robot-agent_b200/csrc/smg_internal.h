@@ -158,6 +158,16 @@ typedef struct {
 #define SMG_WK_CELLS 7       // occupancy cells updated (one update per cell per scan)
 #define SMG_WORK_N 8
 
+// Merge-pass cache (the reference keeps one too, objmap.cpp:1137-1150): the embedding cosine and
+// the contact fraction of an object pair depend only on the two objects' vectors (ver) and
+// clouds (cloud version), so a pair whose four versions are unchanged reuses them.  Direct
+// mapped; a collision only costs a recomputation.
+#define PCACHE_SLOTS 8192
+struct PairCacheRec {
+  uint32_t ida, idb, va, vb, ca, cb;
+  double cs, contact;
+};
+
 typedef struct {
   uint32_t next_id;
   int32_t n_obj;
@@ -252,6 +262,7 @@ typedef struct {
   uint32_t* mcand_ab;    // [M*O*8*2]
   uint32_t* mcand_key;   // [M*O*8] list positions i << 16 | j (the reference's enumeration order)
   int32_t* mcand_n;      // [M]
+  struct PairCacheRec* pcache;   // [M * PCACHE_SLOTS] merge-pass pair features of unchanged pairs
   // view-first hash (markView)
   int64_t* vkey;         // [M*view_slots], INT64_MIN = empty
   double* vfirst;        // [M*view_slots*5]
