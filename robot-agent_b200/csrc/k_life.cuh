@@ -152,6 +152,9 @@ DEV void remap_id(const Batch& B, int m, uint32_t from, uint32_t to) {
 }
 
 #define RELINK_MAXC 256
+#define STRUCT_CTAS 64
+#define STRUCT_LIST 64
+#define STRUCT_SCR (4096 + 2 * 4096)   // doubles per CTA: points (as floats) + plane-fit scratch
 #define RELINK_STAGE 1024
 // relink (objmap.cpp:321-385), per map: candidate pairs pass the scalar tests, a warp per pair
 // evaluates the embedding cosine of n's mean direction against m, then pairs are applied nearest
@@ -205,30 +208,33 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
   __syncthreads();
   if (tid == 0) {
     if (!staged) set_err(R, SMG_E_CAP_OBJ);
-    // scalar tests of the relink candidates (a pair needs a gone object m)
     cn_ = 0;
-    bool any_gone = false;
-    for (int i = 0; staged && i < nobj && !any_gone; ++i) any_gone = s_state[i] == 1;
-    for (int i = 0; any_gone && i < nobj; ++i) {
-      if (!(s_flags[i] & 1) || !(s_flags[i] & 2) || s_state[i] == 1 || s_nobs[i] < P.link_min_obs) continue;
-      if (t - s_first[i] > P.link_window_s) continue;
-      for (int j = 0; j < nobj; ++j) {
-        if (j == i || s_state[j] != 1 || !(s_flags[j] & 2) || (!(s_flags[j] & 4) && s_nobs[j] < P.spurious_obs)) continue;
-        if (!(s_first[i] > s_last[j])) continue;
-        const double d = dist3(&s_pos[3 * i], &s_pos[3 * j]);
-        if (d > smin(P.link_max_d, P.link_d0 + P.link_v * (s_first[i] - s_last[j]))) continue;
-        bool wait = false;
-        if (t - s_first[i] < P.link_wait_s)
-          for (int q = 0; q < nobj; ++q) {
-            if (q == i || q == j || !(s_flags[q] & 2) || s_state[q] == 1 || s_cls[q] != s_cls[i]) continue;
-            if (s_last[q] < s_first[i] && dist3(&s_pos[3 * q], &s_pos[3 * i]) < d) { wait = true; break; }
-          }
-        if (wait) continue;
-        if (cn_ < RELINK_MAXC) { cm_[cn_] = j; cnn_[cn_] = i; cd_[cn_] = d; ++cn_; }
-        else set_err(R, SMG_E_ARGS);
-      }
+  }
+  __syncthreads();
+  // scalar tests of the relink candidates (a pair needs a gone object m), one thread per n;
+  // the candidates are sorted by (distance, m id, n id) below, so their list order is free
+  for (int i = tid; staged && i < nobj; i += blockDim.x) {
+    if (!(s_flags[i] & 1) || !(s_flags[i] & 2) || s_state[i] == 1 || s_nobs[i] < P.link_min_obs) continue;
+    if (t - s_first[i] > P.link_window_s) continue;
+    for (int j = 0; j < nobj; ++j) {
+      if (j == i || s_state[j] != 1 || !(s_flags[j] & 2) || (!(s_flags[j] & 4) && s_nobs[j] < P.spurious_obs)) continue;
+      if (!(s_first[i] > s_last[j])) continue;
+      const double d = dist3(&s_pos[3 * i], &s_pos[3 * j]);
+      if (d > smin(P.link_max_d, P.link_d0 + P.link_v * (s_first[i] - s_last[j]))) continue;
+      bool wait = false;
+      if (t - s_first[i] < P.link_wait_s)
+        for (int q = 0; q < nobj; ++q) {
+          if (q == i || q == j || !(s_flags[q] & 2) || s_state[q] == 1 || s_cls[q] != s_cls[i]) continue;
+          if (s_last[q] < s_first[i] && dist3(&s_pos[3 * q], &s_pos[3 * i]) < d) { wait = true; break; }
+        }
+      if (wait) continue;
+      const int c = atomicAdd(&cn_, 1);
+      if (c < RELINK_MAXC) { cm_[c] = j; cnn_[c] = i; cd_[c] = d; }
+      else set_err(R, SMG_E_ARGS);
     }
   }
+  __syncthreads();
+  if (tid == 0 && cn_ > RELINK_MAXC) cn_ = RELINK_MAXC;
   __syncthreads();
   // apCosMax(m, mu(n)) >= link_cos (mu = r_frag / |r_frag| as float, objprob.cpp:233-239)
   float* myu = mu + (size_t)wid * B.D;
@@ -311,29 +317,55 @@ __global__ void __launch_bounds__(256) k_struct(Batch B) {
   __shared__ int hist[SEL_MAXQ * 256];
   __shared__ int draws[RANSAC_DRAWS];
   __shared__ PlaneOut pout;
+  __shared__ int mine[STRUCT_LIST];
+  __shared__ int nmine;
+  __shared__ int scan_db[2][33];
   const int m = blockIdx.y;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const MapRec& R = B.maps[m];
   const smg_params& P = B.p;
-  double* sel = B.sel + ((size_t)m * B.max_det + blockIdx.x) * 4 * B.pmax;
+  double* sel = B.sscr + ((size_t)m * gridDim.x + blockIdx.x) * STRUCT_SCR;
   float* Pt = (float*)sel;                  // <= 2*800 points
   double* scr = sel + 4096;                 // plane-fit scratch: 2 x 4096 doubles
-  for (int b = blockIdx.x; b < R.n_obj; b += gridDim.x) {
+  // the objects whose cloud changed, in list order; CTA c takes every gridDim.x-th of them
+  if (threadIdx.x == 0) nmine = 0;
+  int before = 0, it = 0;
+  for (int c0 = 0; c0 < R.n_obj; c0 += blockDim.x) {
+    const int b = c0 + threadIdx.x;
+    int need = 0;
+    if (b < R.n_obj) {
+      const ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
+      const CloudRec& C = B.clouds[(size_t)m * B.O + o.cloud_slot];
+      need = o.geo_ver != C.version && C.n >= 30;
+    }
+    int tot;
+    const int rank = before + block_scan_db(need, &tot, scan_db, it++);
+    if (need && rank % (int)gridDim.x == (int)blockIdx.x) {
+      const int q = atomicAdd(&nmine, 1);
+      if (q < STRUCT_LIST) mine[q] = b;
+    }
+    before += tot;
+  }
+  __syncthreads();
+  const int nm = nmine < STRUCT_LIST ? nmine : STRUCT_LIST;
+  if (threadIdx.x == 0 && nmine > STRUCT_LIST) set_err(&B.maps[m], SMG_E_ARGS);
+  // the list came out of an unordered append; objects are independent, so order is free
+  for (int q = 0; q < nm; ++q) {
+    const int b = mine[q];
     ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
     const size_t cs = (size_t)m * B.O + o.cloud_slot;
     const CloudRec& C = B.clouds[cs];
-    if (o.geo_ver == C.version || C.n < 30) continue;
     // cloudSample(m, 800) (objmap.cpp:1107-1114)
     const size_t stp = (size_t)C.n / 800 > 1 ? (size_t)C.n / 800 : 1;
     const int n = (int)(((size_t)C.n + stp - 1) / stp);
     const float4* pts = B.cpts + cs * B.cap;
     if (!INB(3 * n, 2 * 4096, 508)) continue;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const float4 q = pts[(size_t)i * stp];
-      Pt[3 * i] = (float)(C.org[0] + (double)q.x);
-      Pt[3 * i + 1] = (float)(C.org[1] + (double)q.y);
-      Pt[3 * i + 2] = (float)(C.org[2] + (double)q.z);
+      const float4 qp = pts[(size_t)i * stp];
+      Pt[3 * i] = (float)(C.org[0] + (double)qp.x);
+      Pt[3 * i + 1] = (float)(C.org[1] + (double)qp.y);
+      Pt[3 * i + 2] = (float)(C.org[2] + (double)qp.z);
     }
     __syncthreads();
     plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, scr, 4096, hist, draws,

@@ -364,6 +364,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.mcand_key, MO * 8);
   DA(B.mcand_n, M);
   DA(B.pcache, (size_t)M * PCACHE_SLOTS);
+  DA(B.sscr, (size_t)M * STRUCT_CTAS * STRUCT_SCR);
   DA(B.vkey, (size_t)M * B.view_slots);
   DA(B.vfirst, (size_t)M * B.view_slots * SMG_VIEW_BANDS);
   DA(B.need_tab, NEED_N * NEED_N);
@@ -637,7 +638,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({8, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_struct<<<dim3(B.max_det, M), 256, 0, st>>>(B);
+  k_struct<<<dim3(STRUCT_CTAS, M), 256, 0, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({9, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }

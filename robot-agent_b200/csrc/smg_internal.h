@@ -263,6 +263,7 @@ typedef struct {
   uint32_t* mcand_key;   // [M*O*8] list positions i << 16 | j (the reference's enumeration order)
   int32_t* mcand_n;      // [M]
   struct PairCacheRec* pcache;   // [M * PCACHE_SLOTS] merge-pass pair features of unchanged pairs
+  double* sscr;          // [M * STRUCT_CTAS * STRUCT_SCR] k_struct scratch
   // view-first hash (markView)
   int64_t* vkey;         // [M*view_slots], INT64_MIN = empty
   double* vfirst;        // [M*view_slots*5]
