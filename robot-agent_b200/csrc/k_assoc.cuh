@@ -12,6 +12,7 @@
 
 #define ASSOC_THREADS 256
 #define SP_MAX 1024
+#define ASSOC_GATED 1024
 
 DEV const ObjRec& obj_at(const Batch& B, int m, int pos) { return B.objs[(size_t)m * B.O + B.order[(size_t)m * B.O + pos]]; }
 DEV int slot_at(const Batch& B, int m, int pos) { return B.order[(size_t)m * B.O + pos]; }
@@ -192,20 +193,38 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
       if (lane == 0) B.gdot[((size_t)m * B.max_det + a) * B.max_det + b2] = dot;
     }
   const double gate2 = P.gate * P.gate;
-  for (int b = wid; b < nobj; b += nw) {
+  // box-gap gate of every object, one thread per object; the gated ones go to a list that the
+  // warps then work through (the top-1 below reads pp in list order, so the list order is free)
+  __shared__ int gl[ASSOC_GATED];
+  __shared__ int ngl;
+  if (tid == 0) ngl = 0;
+  __syncthreads();
+  {
+    double olo[3], ohi[3];
+    for (int k = 0; k < 3; ++k) { olo[k] = O->lo[k]; ohi[k] = O->hi[k]; }
+    for (int b = tid; b < nobj; b += blockDim.x) {
+      if (!INB(b, B.O, 201)) continue;
+      const ObjRec& ob = B.objs[oglob(B, m, slot_at(B, m, b))];
+      double g2 = 0;
+      for (int k = 0; k < 3; ++k) {
+        const double g = smax3(0.0, olo[k] - ob.hi[k], ob.lo[k] - ohi[k]);
+        g2 += g * g;
+      }
+      pp[b] = -1.0;
+      if (g2 > gate2) continue;
+      const int q = atomicAdd(&ngl, 1);
+      if (q < ASSOC_GATED) gl[q] = b;
+      else set_err(&B.maps[m], SMG_E_ARGS);
+    }
+  }
+  __syncthreads();
+  const int ng = ngl < ASSOC_GATED ? ngl : ASSOC_GATED;
+  for (int gi = wid; gi < ng; gi += nw) {
+    const int b = gl[gi];
     const int slot = slot_at(B, m, b);
     const size_t og = oglob(B, m, slot);
     const ObjRec& ob = B.objs[og];
-    double g2 = 0;
-    for (int k = 0; k < 3; ++k) {
-      const double g = smax3(0.0, O->lo[k] - ob.hi[k], ob.lo[k] - O->hi[k]);
-      g2 += g * g;
-    }
-    if (!INB(b, B.O, 201) || !INB(slot, B.O, 202)) continue;
-    if (g2 > gate2) {
-      if (lane == 0) pp[b] = -1.0;
-      continue;
-    }
+    if (!INB(slot, B.O, 202)) continue;
     const double cs = has_z ? cos_max_warp(B, og, ob, zs) : -2.0;
     if (has_z && lane == 0) wk_add(&B.maps[m], SMG_WK_VEC16, (ob.nrm_frag > 0 ? 2 : 0) + ob.n_views);
     const size_t cslot = oglob(B, m, ob.cloud_slot);
