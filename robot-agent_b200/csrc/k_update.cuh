@@ -1,16 +1,18 @@
-// Object update of one keyframe, one CTA per map (scenemap src/objmap.cpp:807-1019).
+// Object update of one keyframe (scenemap src/objmap.cpp:807-1019) in two kernels.
 //
 // The reference's update is a sequence over observations whose later steps depend on the
 // earlier ones (fragments fuse into the first, largest one; new objects are appended mid-loop
-// and can capture later fragments).  That order is kept: thread 0 walks the observations and
-// takes every scalar decision; the whole block joins for the D-length work (r_frag += k z in
-// fp32, fp16 view encoding, the frame-grouping dot product, |r_frag|^2).  Parallelism comes from
-// the batch of maps (one CTA each).
+// and can capture later fragments).  k_update keeps that order: one CTA per map, thread 0 walks
+// the observations and takes every scalar decision, including the scalar half of apAddView
+// (tempering, camera ring, view list), and records each embedding's D-length work as a job.
+// k_update_vec then runs one CTA per target object and applies its jobs in observation order
+// (r_frag += k z in fp32, the fp16 view copy, |r_frag|^2 and mu); the objects are independent.
+// The frame-grouping dot products were computed by k_assoc.
 #pragma once
 #include "k_assoc.cuh"
 
 #define UPD_THREADS 256
-#define UPD_SMEM(B) ((size_t)(B).D * 4 + (size_t)(B).max_det * sizeof(ObsRec) + sizeof(ObjRec) + 16)
+#define UPD_SMEM(B) ((size_t)(B).max_det * sizeof(ObsRec) + sizeof(ObjRec) + 16)
 
 DEV size_t cslot_glob(const Batch& B, int m, const ObjRec& o) { return (size_t)m * B.O + o.cloud_slot; }
 
@@ -73,74 +75,75 @@ DEV void rec_copy(ObjRec* dst, const ObjRec* src) {
 }
 
 // apAddView (scenemap objprob.cpp:312-356) for a detection fragment (whole = false), no text
-// model.  Block-wide; z is the fp32 embedding (global).  Returns nothing (tempered kappa is only
-// used for the label terms, absent here).
-DEV void ap_add_view(const Batch& B, ObjRec& o, size_t og, const float* z_sh, double kappa, double stamp, const double cam[6],
-                     BlockScratch& bs) {
-  __shared__ double sh_k;
-  __shared__ int sh_free;
-  const int tid = threadIdx.x, D = B.D;
-  if (tid == 0) {
-    double k = kappa;
-    const double cmin = B.cos_temper;
-    for (int c = 0; c < o.n_cams; ++c) {
-      const double* cc = o.cams[c];
-      if (fabs(cc[6] - stamp) < 1e-6) continue;
-      const double dd = hypot3(cc[0] - cam[0], cc[1] - cam[1], cc[2] - cam[2]);
-      const double ca = cc[3] * cam[3] + cc[4] * cam[4] + cc[5] * cam[5];
-      if (dd < B.p.temper_d && ca > cmin) { k = kappa * B.p.temper; break; }
-    }
-    if (o.n_cams >= SMG_CAMS) {   // keep the newest 32 (push, then erase the front)
-      for (int c = 1; c < SMG_CAMS; ++c)
-        for (int j = 0; j < 7; ++j) o.cams[c - 1][j] = o.cams[c][j];
-      o.n_cams = SMG_CAMS - 1;
-    }
-    for (int j = 0; j < 6; ++j) o.cams[o.n_cams][j] = cam[j];
-    o.cams[o.n_cams][6] = stamp;
-    ++o.n_cams;
-    ++o.ver;
-    o.k_frag += k;
-    sh_k = k;
-    // free physical view slot: the one of 0..topk not referenced by the current views
-    int used = 0;
-    for (int v = 0; v < o.n_views; ++v) if (INB(o.view_slot[v], B.topk + 1, 301)) used |= 1 << o.view_slot[v];
-    int f = 0;
-    while (used & (1 << f)) ++f;
-    sh_free = f;
+// model: the scalar part, run by one thread -- view tempering against the camera ring
+// (similar view at another stamp: kappa * temper), the ring of the newest 32 cameras, ver and
+// k_frag, the physical view slot the fp16 copy goes to and the view list kept sorted by kappa
+// (stable, top-k).  The D-length part (r_frag += k z, the fp16 copy, |r|^2, mu) is recorded as
+// a job for k_update_vec.
+DEV void ap_add_view_plan(const Batch& B, ObjRec& o, double kappa, double stamp, const double cam[6], double* k_out, int* phys_out) {
+  double k = kappa;
+  const double cmin = B.cos_temper;
+  for (int c = 0; c < o.n_cams; ++c) {
+    const double* cc = o.cams[c];
+    if (fabs(cc[6] - stamp) < 1e-6) continue;
+    const double dd = hypot3(cc[0] - cam[0], cc[1] - cam[1], cc[2] - cam[2]);
+    const double ca = cc[3] * cam[3] + cc[4] * cam[4] + cc[5] * cam[5];
+    if (dd < B.p.temper_d && ca > cmin) { k = kappa * B.p.temper; break; }
   }
-  __syncthreads();
-  const double k = sh_k;
-  if (tid == 0) wk_add(&B.maps[og / B.O], SMG_WK_UPD, 1);
-  float* r = B.rfrag + og * D;
-  uint16_t* vz = B.views + (og * (B.topk + 1) + sh_free) * D;
-  for (int i = tid; i < D; i += blockDim.x) {
-    const float zi = z_sh[i];
-    r[i] += (float)(k * (double)zi);
-    vz[i] = ref_f2h(zi);
+  if (o.n_cams >= SMG_CAMS) {   // keep the newest 32 (push, then erase the front)
+    for (int c = 1; c < SMG_CAMS; ++c)
+      for (int j = 0; j < 7; ++j) o.cams[c - 1][j] = o.cams[c][j];
+    o.n_cams = SMG_CAMS - 1;
   }
-  __syncthreads();
-  if (tid == 0) {
-    // stable sort by (whole desc, kappa desc): every view is a fragment, so insert after the
-    // views whose kappa is >= the new one, then keep the top-k
-    const float kv = (float)kappa;
-    int pos = o.n_views;
-    while (pos > 0 && o.vkappa[pos - 1] < kv) --pos;
-    for (int v = o.n_views; v > pos; --v) {
-      o.view_slot[v] = o.view_slot[v - 1];
-      o.vkappa[v] = o.vkappa[v - 1];
-      o.vstamp[v] = o.vstamp[v - 1];
-    }
-    o.view_slot[pos] = sh_free;
-    o.vkappa[pos] = kv;
-    o.vstamp[pos] = stamp;
-    ++o.n_views;
-    if (o.n_views > B.topk) o.n_views = B.topk;
+  for (int j = 0; j < 6; ++j) o.cams[o.n_cams][j] = cam[j];
+  o.cams[o.n_cams][6] = stamp;
+  ++o.n_cams;
+  ++o.ver;
+  o.k_frag += k;
+  // free physical view slot: the one of 0..topk not referenced by the current views
+  int used = 0;
+  for (int v = 0; v < o.n_views; ++v) if (INB(o.view_slot[v], B.topk + 1, 301)) used |= 1 << o.view_slot[v];
+  int f = 0;
+  while (used & (1 << f)) ++f;
+  // stable sort by (whole desc, kappa desc): every view is a fragment, so insert after the
+  // views whose kappa is >= the new one, then keep the top-k
+  const float kv = (float)kappa;
+  int pos = o.n_views;
+  while (pos > 0 && o.vkappa[pos - 1] < kv) --pos;
+  for (int v = o.n_views; v > pos; --v) {
+    o.view_slot[v] = o.view_slot[v - 1];
+    o.vkappa[v] = o.vkappa[v - 1];
+    o.vstamp[v] = o.vstamp[v - 1];
   }
-  __syncthreads();
-  refresh_nrm_into(B, o, og, bs);
+  o.view_slot[pos] = f;
+  o.vkappa[pos] = kv;
+  o.vstamp[pos] = stamp;
+  ++o.n_views;
+  if (o.n_views > B.topk) o.n_views = B.topk;
+  *k_out = k;
+  *phys_out = f;
 }
 
-// allocate an object slot + cloud slot for a new object (appended at list position n_obj)
+// record one vector job (objmap.cpp:848, :970 -> apAddView) for object `og`
+DEV void upd_job(const Batch& B, int m, int* njobs, int* ntg, size_t og, int det, double k, int phys, int zero) {
+  const size_t base = (size_t)m * B.max_det;
+  int tg = -1;
+  for (int c = 0; c < *ntg; ++c)
+    if (B.upd_tg[base + c] == (int64_t)og) { tg = c; break; }
+  if (tg < 0) {
+    if (!INB(*ntg, B.max_det, 304)) return;
+    tg = (*ntg)++;
+    B.upd_tg[base + tg] = (int64_t)og;
+  }
+  if (!INB(*njobs, B.max_det, 305)) return;
+  UpdJob& j = B.upd_job[base + (*njobs)++];
+  j.tg = tg;
+  j.det = det;
+  j.phys = phys;
+  j.zero = zero;
+  j.k = k;
+}
+
 DEV int new_object_slot(const Batch& B, int m, int* cslot) {
   MapRec* R = &B.maps[m];
   if (R->n_free <= 0 || R->n_cfree <= 0 || R->n_obj >= B.O) { set_err(R, SMG_E_CAP_OBJ); return -1; }
@@ -153,13 +156,11 @@ DEV int new_object_slot(const Batch& B, int m, int* cslot) {
 
 __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* zs = (float*)smem_raw;   // D
-  ObsRec* OBs = (ObsRec*)(smem_raw + (((size_t)B.D * 4 + 15) & ~(size_t)15));   // staged observations
+  ObsRec* OBs = (ObsRec*)smem_raw;   // staged observations
   ObjRec* MO = (ObjRec*)(OBs + B.max_det);                                         // staged object record
-  __shared__ BlockScratch bs;
   __shared__ int sh_act, sh_slot, sh_cslot;
   __shared__ int head[SMG_MAX_DET];
-  __shared__ int evn;
+  __shared__ int evn, njobs, ntg;
   const int m = blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
@@ -179,6 +180,8 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
   const double cam6[6] = {T[3], T[7], T[11], T[2], T[6], T[10]};
   if (tid == 0) {
     evn = 0;
+    njobs = 0;
+    ntg = 0;
     // association bookkeeping (objmap.cpp:807-809)
     for (int a = 0; a < nobs; ++a) {
       ObsRec& o = OB[OL[a]];
@@ -238,16 +241,17 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
     __syncthreads();
     const int act = sh_act;
     ObsRec& o = OB[OL[a]];
-    if (act != 0 && has_z) {
-      for (int i = tid; i < B.D; i += blockDim.x) zs[i] = emb_at(F.emb, F.emb_dtype, B.D, o.det, i);
-    }
-    __syncthreads();
     const size_t og = oglob(B, m, sh_slot);
     if (act == 1) {
       rec_copy(MO, &B.objs[og]);
-      if (has_z) ap_add_view(B, *MO, og, zs, o.kappa, F.stamp, cam6, bs);
       if (tid == 0) {
         ObjRec& mo = *MO;
+        if (has_z) {
+          double k;
+          int phys;
+          ap_add_view_plan(B, mo, o.kappa, F.stamp, cam6, &k, &phys);
+          upd_job(B, m, &njobs, &ntg, og, o.det, k, phys, 0);
+        }
         ++mo.n_ap_obs;
         mo.wall_like = 2 * mo.n_wall_obs >= mo.n_ap_obs;
         if (!o.sec) {
@@ -376,15 +380,14 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
         B.touched[(size_t)m * B.O + R->n_obj - 1] = 1;
         B.obj_hit[(size_t)m * B.O + R->n_obj - 1] = 1;
       }
-      __syncthreads();
-      {   // a recycled slot starts from an empty r_frag (objprob.cpp:329 assigns zeros)
-        float* r = B.rfrag + og * B.D;
-        for (int i = tid; i < B.D; i += blockDim.x) r[i] = 0.f;
-        __syncthreads();
-      }
-      if (has_z) ap_add_view(B, *MO, og, zs, o.kappa, F.stamp, cam6, bs);
       if (tid == 0) {
         ObjRec& mo = *MO;
+        if (has_z) {   // a recycled slot starts from an empty r_frag (objprob.cpp:329 assigns zeros)
+          double k;
+          int phys;
+          ap_add_view_plan(B, mo, o.kappa, F.stamp, cam6, &k, &phys);
+          upd_job(B, m, &njobs, &ntg, og, o.det, k, phys, 1);
+        }
         mo.n_ap_obs = 1;
         mo.n_wall_obs = 0;
         mo.n_struct_look = 0;
@@ -415,5 +418,39 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
     }
     __syncthreads();
   }
-  if (tid == 0) R->n_evn = evn;
+  if (tid == 0) {
+    R->n_evn = evn;
+    B.upd_n[2 * m] = njobs;
+    B.upd_n[2 * m + 1] = ntg;
+  }
+}
+
+// The D-length part of apAddView for every target object of the frame: one CTA per object
+// applies that object's jobs in observation order (r_frag += float(k z), the fp16 view copy),
+// then |r_frag|^2 and mu (objprob.cpp:228-240).  Objects are independent, so they run in
+// parallel; each thread owns the same elements across jobs, so the jobs need no barrier.
+__global__ void __launch_bounds__(UPD_THREADS) k_update_vec(Batch B) {
+  __shared__ BlockScratch bs;
+  const int c = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+  const FrameDev& F = B.frames[m];
+  if (!F.active || c >= B.upd_n[2 * m + 1]) return;
+  const size_t base = (size_t)m * B.max_det;
+  const size_t og = (size_t)B.upd_tg[base + c];
+  const int nj = B.upd_n[2 * m];
+  float* r = B.rfrag + og * B.D;
+  int nmine = 0;
+  for (int jj = 0; jj < nj; ++jj) {
+    const UpdJob j = B.upd_job[base + jj];
+    if (j.tg != c) continue;
+    ++nmine;
+    uint16_t* vz = B.views + (og * (B.topk + 1) + j.phys) * B.D;
+    for (int i = tid; i < B.D; i += blockDim.x) {
+      const float zi = emb_at(F.emb, F.emb_dtype, B.D, j.det, i);
+      r[i] = (j.zero ? 0.f : r[i]) + (float)(j.k * (double)zi);
+      vz[i] = ref_f2h(zi);
+    }
+  }
+  if (tid == 0) wk_add(&B.maps[m], SMG_WK_UPD, nmine);
+  __syncthreads();
+  refresh_nrm(B, og, bs);
 }

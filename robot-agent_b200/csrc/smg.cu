@@ -365,6 +365,9 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.mcand_n, M);
   DA(B.pcache, (size_t)M * PCACHE_SLOTS);
   DA(B.sscr, (size_t)M * STRUCT_CTAS * STRUCT_SCR);
+  DA(B.upd_job, MD);
+  DA(B.upd_tg, MD);
+  DA(B.upd_n, (size_t)M * 2);
   DA(B.vkey, (size_t)M * B.view_slots);
   DA(B.vfirst, (size_t)M * B.view_slots * SMG_VIEW_BANDS);
   DA(B.need_tab, NEED_N * NEED_N);
@@ -627,6 +630,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({5, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_update<<<M, UPD_THREADS, UPD_SMEM(B), st>>>(B);
+  k_update_vec<<<dim3(B.max_det, M), UPD_THREADS, 0, st>>>(B);   // timed together with k_update
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({6, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
@@ -654,7 +658,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({12, {e0, e1}}); } }
   CK(cudaStreamWaitEvent(st, b->ev_join, 0));   // join
-  b->launches += 14;
+  b->launches += 15;
   CK(cudaGetLastError());
   return SMG_OK;
 }

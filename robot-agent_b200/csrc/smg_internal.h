@@ -163,6 +163,11 @@ typedef struct {
 // clouds (cloud version), so a pair whose four versions are unchanged reuses them.  Direct
 // mapped; a collision only costs a recomputation.
 #define PCACHE_SLOTS 8192
+// one apAddView vector job of the keyframe (target object index tg of the frame's list)
+struct UpdJob {
+  int32_t tg, det, phys, zero;
+  double k;
+};
 struct PairCacheRec {
   uint32_t ida, idb, va, vb, ca, cb;
   double cs, contact;
@@ -264,6 +269,9 @@ typedef struct {
   int32_t* mcand_n;      // [M]
   struct PairCacheRec* pcache;   // [M * PCACHE_SLOTS] merge-pass pair features of unchanged pairs
   double* sscr;          // [M * STRUCT_CTAS * STRUCT_SCR] k_struct scratch
+  struct UpdJob* upd_job;  // [M * max_det] vector jobs of k_update, observation order
+  int64_t* upd_tg;         // [M * max_det] target objects (global slot) of those jobs
+  int32_t* upd_n;          // [M * 2] jobs, targets
   // view-first hash (markView)
   int64_t* vkey;         // [M*view_slots], INT64_MIN = empty
   double* vfirst;        // [M*view_slots*5]
