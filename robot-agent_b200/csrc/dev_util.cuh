@@ -213,101 +213,125 @@ DEV double d_unord(uint64_t k) {
 // Exact k-th smallest (0-based) of a[0..n) by MSB-first radix selection on the ordered bit
 // pattern: returns exactly the value std::nth_element leaves at position k.
 // hist: 256 shared ints.  All threads of the block must call it.
+DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s);
 DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& s) {
-  uint64_t prefix = 0, mask = 0;
-  for (int pass = 0; pass < 8; ++pass) {
-    const int shift = 56 - 8 * pass;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint64_t key = d_ord(a[i]);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
-    }
-#ifdef SMG_CHECKS
-    if (threadIdx.x == 0 && (k < 0 || k >= n)) smg_chk_fail(130, k, n);
-#endif
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      const int lane = threadIdx.x;
-      int c[8], tot = 0;
-      for (int j = 0; j < 8; ++j) { c[j] = hist[lane * 8 + j]; tot += c[j]; }
-      int incl = tot;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const int excl = incl - tot;
-      if (k >= excl && k < incl) {
-        int kk = k - excl, b = 0;
-        for (int j = 0; j < 8; ++j) {
-          if (kk < c[j]) { b = j; break; }
-          kk -= c[j];
-        }
-        s.i[0] = lane * 8 + b;
-        s.i[1] = kk;
-      }
-    }
-    __syncthreads();
-    const int sel = s.i[0];
-    k = s.i[1];
-    __syncthreads();
-    prefix |= (uint64_t)sel << shift;
-    mask |= 0xffull << shift;
-  }
-  return d_unord(prefix);
+  __shared__ double sel1;
+  const double* arr[1] = {a};
+  const int nn[1] = {n}, kk[1] = {k};
+  block_select_multi(arr, nn, kk, &sel1, 1, hist, s);
+  return sel1;
 }
 
-// Up to SEL_MAXQ exact selections in one set of 8 radix passes: value q = the k[q]-th smallest
-// of a[q][0..n[q]).  hist: SEL_MAXQ*256 ints (shared).  All threads must call it.
+// Up to SEL_MAXQ exact selections at once: value q = the k[q]-th smallest of a[q][0..n[q]).
+// Each query walks the key bytes MSB first (one histogram of the keys that share the decided
+// prefix per round); histogram increments are aggregated per warp over the lanes with the same
+// byte as the warp's first active lane, so the first bytes (shared by most keys) do not
+// serialise on one counter.  Once the chosen byte holds at most SEL_GATHER keys, those keys are
+// gathered and ranked by one warp instead of running the remaining byte rounds.  Two barriers
+// per round.
+// hist: SEL_MAXQ*256 ints (shared).  Needs nq <= warps of the block.  All threads must call it.
 #define SEL_MAXQ 9
+#define SEL_GATHER 32
 DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s) {
   __shared__ unsigned long long sh_prefix[SEL_MAXQ];
-  __shared__ int sh_k[SEL_MAXQ];
+  __shared__ unsigned long long sh_g[SEL_MAXQ][SEL_GATHER];
+  __shared__ int sh_k[SEL_MAXQ], sh_dec[SEL_MAXQ], sh_mode[SEL_MAXQ], sh_gn[SEL_MAXQ], sh_live;
+  const int tid = threadIdx.x, lane = tid & 31, wq = tid >> 5;
 #ifdef SMG_CHECKS
-  if (threadIdx.x == 0 && (nq > SEL_MAXQ || nq > (int)(blockDim.x >> 5))) smg_chk_fail(132, nq, SEL_MAXQ);
+  if (tid == 0 && (nq > SEL_MAXQ || nq > (int)(blockDim.x >> 5))) smg_chk_fail(132, nq, SEL_MAXQ);
+  if (tid < nq && (kq[tid] < 0 || kq[tid] >= n[tid])) smg_chk_fail(130, kq[tid], n[tid]);
 #endif
-  if (threadIdx.x < nq) { sh_prefix[threadIdx.x] = 0; sh_k[threadIdx.x] = kq[threadIdx.x]; }
-  uint64_t mask = 0;
-  for (int pass = 0; pass < 8; ++pass) {
-    const int shift = 56 - 8 * pass;
-    for (int i = threadIdx.x; i < nq * 256; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
-    for (int q = 0; q < nq; ++q) {
-      const uint64_t pre = sh_prefix[q];
-      const double* aq = a[q];
-      for (int i = threadIdx.x; i < n[q]; i += blockDim.x) {
-        const uint64_t key = d_ord(aq[i]);
-        if ((key & mask) == pre) atomicAdd(&hist[q * 256 + ((key >> shift) & 255u)], 1);
-      }
-    }
-    __syncthreads();
-    const int lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
-    if (wq < nq) {
-      const int* hq = hist + wq * 256;
-      int c[8], tot = 0;
-      for (int j = 0; j < 8; ++j) { c[j] = hq[lane * 8 + j]; tot += c[j]; }
-      int incl = tot;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const int excl = incl - tot;
-      const int k = sh_k[wq];
-      if (k >= excl && k < incl) {
-        int kk = k - excl, b = 0;
-        for (int j = 0; j < 8; ++j) {
-          if (kk < c[j]) { b = j; break; }
-          kk -= c[j];
-        }
-        sh_prefix[wq] |= (unsigned long long)(lane * 8 + b) << shift;
-        sh_k[wq] = kk;
-      }
-    }
-    __syncthreads();
-    mask |= 0xffull << shift;
-  }
-  if (threadIdx.x < nq) out[threadIdx.x] = d_unord(sh_prefix[threadIdx.x]);
+  for (int i = tid; i < nq * 256; i += blockDim.x) hist[i] = 0;
+  if (tid < nq) { sh_prefix[tid] = 0; sh_k[tid] = kq[tid]; sh_dec[tid] = 0; sh_mode[tid] = 0; sh_gn[tid] = 0; }
+  if (tid == 0) sh_live = nq;
   __syncthreads();
+  for (int round = 0; round < 10; ++round) {
+    // A: histogram (mode 0) or gather (mode 1) of the keys under each query's prefix
+    for (int q = 0; q < nq; ++q) {
+      const int mode = sh_mode[q];
+      if (mode == 2) continue;
+      const int dec = sh_dec[q];
+      const uint64_t pre = sh_prefix[q], msk = dec == 0 ? 0ull : ~0ull << (64 - dec);
+      const int shift = 56 - dec;
+      const double* aq = a[q];
+      const int nqq = n[q];
+      for (int i0 = 0; i0 < nqq; i0 += blockDim.x) {
+        const int i = i0 + tid;
+        const uint64_t key = i < nqq ? d_ord(aq[i]) : 0ull;
+        const bool act = i < nqq && (key & msk) == pre;
+        if (mode == 0) {
+          // the lanes sharing the first active lane's byte add with one atomic
+          const unsigned am = __ballot_sync(0xffffffffu, act);
+          const unsigned bin = (unsigned)(key >> shift) & 255u;
+          const int src = am ? __ffs(am) - 1 : 0;
+          const unsigned b0 = __shfl_sync(0xffffffffu, bin, src);
+          const unsigned same = __ballot_sync(0xffffffffu, act && bin == b0);
+          if (am && lane == src) atomicAdd(&hist[q * 256 + b0], __popc(same));
+          else if (act && bin != b0) atomicAdd(&hist[q * 256 + bin], 1);
+        } else if (act) {
+          const int slot = atomicAdd(&sh_gn[q], 1);
+          if (INB(slot, SEL_GATHER, 133)) sh_g[q][slot] = key;
+        }
+      }
+    }
+    __syncthreads();
+    // B: warp q picks the byte holding rank k (and clears its counters), or ranks the gathered keys
+    if (wq < nq && sh_mode[wq] != 2) {
+      const int k = sh_k[wq];
+      if (sh_mode[wq] == 0) {
+        int* hq = hist + wq * 256;
+        int c[8], tot = 0;
+        for (int j = 0; j < 8; ++j) { c[j] = hq[lane * 8 + j]; hq[lane * 8 + j] = 0; tot += c[j]; }
+        int incl = tot;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const int excl = incl - tot;
+        const int all = __shfl_sync(0xffffffffu, incl, 31);
+        if (k >= excl && k < incl) {
+          int kk = k - excl, b = 0;
+          for (int j = 0; j < 8; ++j) {
+            if (kk < c[j]) { b = j; break; }
+            kk -= c[j];
+          }
+          const int dec = sh_dec[wq] + 8;
+          sh_prefix[wq] |= (unsigned long long)(lane * 8 + b) << (64 - dec);
+          sh_k[wq] = kk;
+          sh_dec[wq] = dec;
+          if (dec == 64) {
+            out[wq] = d_unord(sh_prefix[wq]);
+            sh_mode[wq] = 2;
+            atomicSub(&sh_live, 1);
+          } else if (c[b] <= SEL_GATHER) {
+            sh_mode[wq] = 1;
+          }
+        } else if (lane == 0 && !(k >= 0 && k < all)) {   // rank outside the keys: no selection
+          out[wq] = d_unord(sh_prefix[wq]);
+          sh_mode[wq] = 2;
+          atomicSub(&sh_live, 1);
+        }
+      } else {
+        const int gn = sh_gn[wq] < SEL_GATHER ? sh_gn[wq] : SEL_GATHER;
+        const uint64_t g = lane < gn ? sh_g[wq][lane] : 0ull;
+        int lt = 0, eq = 0;
+        for (int j = 0; j < gn; ++j) {
+          const uint64_t h = sh_g[wq][j];
+          lt += h < g;
+          eq += h == g;
+        }
+        const bool hit = lane < gn && lt <= k && k < lt + eq;
+        const unsigned hm = __ballot_sync(0xffffffffu, hit);
+        if (lane == (hm ? __ffs(hm) - 1 : 0)) {
+          out[wq] = d_unord(hm ? g : sh_prefix[wq]);
+          sh_mode[wq] = 2;
+          atomicSub(&sh_live, 1);
+        }
+      }
+    }
+    __syncthreads();
+    if (sh_live == 0) break;
+  }
   (void)s;
 }
 
@@ -508,6 +532,22 @@ DEV void wk_add(MapRec* m, int k, long long v) {
 }
 
 // event in program order: key = phase << 24 | position
+// camera ring of an object (the newest SMG_CAMS cameras, oldest first): entry i, and an append
+// that drops the oldest when full (push, then erase the front)
+DEV double* cam_at(ObjRec& o, int i) { return o.cams[(o.cam_head + i) & (SMG_CAMS - 1)]; }
+DEV const double* cam_at(const ObjRec& o, int i) { return o.cams[(o.cam_head + i) & (SMG_CAMS - 1)]; }
+DEV void cam_push(ObjRec& o, const double c[7]) {
+  double* d;
+  if (o.n_cams >= SMG_CAMS) {
+    d = o.cams[o.cam_head & (SMG_CAMS - 1)];
+    o.cam_head = (o.cam_head + 1) & (SMG_CAMS - 1);
+    o.n_cams = SMG_CAMS;
+  } else {
+    d = cam_at(o, o.n_cams++);
+  }
+  for (int j = 0; j < 7; ++j) d[j] = c[j];
+}
+
 DEV void push_event(const Batch& B, int map, double t, const ObjRec& o, int kind, uint32_t key) {
   MapRec* M = &B.maps[map];
   const int e = atomicAdd(&M->n_events, 1);

@@ -312,10 +312,9 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
 
 // apStructObject geometry (objmap.cpp:1255-1319) for objects whose cloud changed; no wall
 // segments and no text model, so only geo 1 (wall-size vertical plane) / 2 (ceiling) matter.
-__global__ void __launch_bounds__(256) k_struct(Batch B) {
+__global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
   __shared__ BlockScratch bs;
-  __shared__ int hist[SEL_MAXQ * 256];
-  __shared__ int draws[RANSAC_DRAWS];
+  __shared__ PlaneSmem ps;
   __shared__ PlaneOut pout;
   __shared__ int mine[STRUCT_LIST];
   __shared__ int nmine;
@@ -368,8 +367,8 @@ __global__ void __launch_bounds__(256) k_struct(Batch B) {
       Pt[3 * i + 2] = (float)(C.org[2] + (double)qp.z);
     }
     __syncthreads();
-    plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, scr, 4096, hist, draws,
-              bs, &pout);
+    plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, scr, 4096, &ps, bs,
+              &pout);
     int up = 0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) up += (double)Pt[3 * i + 2] > R.ceil_est - P.ceil_band;
     up = block_sum_i(up, bs);

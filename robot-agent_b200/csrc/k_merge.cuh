@@ -284,17 +284,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
       a.whole_kappa = 0;
       a.need_whole = 1;
       // cams: append b's, keep the newest 32
-      int nc2 = a.n_cams;
-      for (int q = 0; q < b.n_cams; ++q) {
-        if (nc2 == SMG_CAMS) {
-          for (int r = 1; r < SMG_CAMS; ++r)
-            for (int j = 0; j < 7; ++j) a.cams[r - 1][j] = a.cams[r][j];
-          --nc2;
-        }
-        for (int j = 0; j < 7; ++j) a.cams[nc2][j] = b.cams[q][j];
-        ++nc2;
-      }
-      a.n_cams = nc2;
+      for (int q = 0; q < b.n_cams; ++q) cam_push(a, cam_at(b, q));
       for (int k = 0; k < 3; ++k) a.P[k] = merge_var(a.P[k], b.P[k]);
       a.n_wall_obs += b.n_wall_obs;
       a.n_ap_obs += b.n_ap_obs;

@@ -15,10 +15,23 @@
 
 #define OBS_THREADS 512
 #define OBS_HASH 8192
+#define OBS_SMEM (OBS_HASH * 12)   // k_obs dynamic shared memory: the voxel hash, reused by later phases
+#define OBS_PPT 4      // raster pixels per thread in the back-projection
 #define RANSAC_MAX 256
 #define RANSAC_DRAWS (3 * RANSAC_MAX + 64)
+#define RANSAC_DBUF (2 * RANSAC_DRAWS)   // draw buffer a caller of plane_fit provides (ints)
 // nsamp = ceil(n / max(1, n / min(n, 256))) <= 511, and cnt <= nsamp (objprob.cpp:135-158)
 #define NEED_N 512
+
+// Shared-memory working set of plane_fit, provided by the caller (a kernel whose dynamic
+// shared memory is free at that point passes a slice of it).
+struct PlaneSmem {
+  double pl[RANSAC_MAX][4];   // hypothesis planes
+  int hist[SEL_MAXQ * 256];   // selection histograms
+  int draws[RANSAC_DBUF];     // RANSAC draws + next-triple table
+  int id[RANSAC_MAX][3];      // hypothesis index triples
+  int cnt[RANSAC_MAX];        // hypothesis inlier counts
+};
 
 struct PlaneOut {
   int ok;
@@ -80,7 +93,7 @@ DEV int pct_index(int n, double q) {   // min(n-1, size_t(q*(n-1) + 0.5)) (objma
 // draws, same adaptive stop; the stop count comes from a host-libm table).  Inlier sums are
 // block reductions (deterministic tree).  span1/span2 are not produced (no caller reads them).
 DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_iters, const int32_t* need_tab, double* scr, int cap,
-                   int* hist, int* h_draw, BlockScratch& bs, PlaneOut* out) {
+                   PlaneSmem* ps, BlockScratch& bs, PlaneOut* out) {
   __shared__ double sh_best[4];
   __shared__ int sh_bestc;
   __shared__ double sh_m[3], sh_V[3][3], sh_ev[3];
@@ -94,9 +107,11 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   // RANSAC (objprob.cpp:133-163).  The index triples do not depend on the inlier counts, so
   // thread 0 draws all of them in the reference's splitmix sequence, every warp scores
   // hypotheses in parallel, and thread 0 replays the sequential best/adaptive-stop logic.
-  __shared__ int h_id[RANSAC_MAX][3];
-  __shared__ int h_cnt[RANSAC_MAX];
-  __shared__ double h_pl[RANSAC_MAX][4];
+  int (*h_id)[3] = ps->id;
+  int* h_cnt = ps->cnt;
+  double (*h_pl)[4] = ps->pl;
+  int* h_draw = ps->draws;
+  int* hist = ps->hist;
   const int iters = max_iters < RANSAC_MAX ? max_iters : RANSAC_MAX;
   const int ns = n < 256 ? n : 256;
   const int sstep = n / ns > 1 ? n / ns : 1;
@@ -105,23 +120,42 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   // all draws (and their 64-bit remainders, the expensive part) are computed in parallel, and
   // thread 0 then walks them with the reference's rejections (objprob.cpp:140-142), falling
   // back to drawing in sequence if the rejections outrun the precomputed draws.
-  const uint64_t rs0 = seed ^ ((uint64_t)n << 32);   // h_draw: RANSAC_DRAWS shared ints of the caller
+  const uint64_t rs0 = seed ^ ((uint64_t)n << 32);
   const int ndraw = 3 * iters + 64 < RANSAC_DRAWS ? 3 * iters + 64 : RANSAC_DRAWS;
+  int* h_qr = h_draw + RANSAC_DRAWS;
   for (int k = tid; k < ndraw; k += blockDim.x) {
     uint64_t s = rs0 + (uint64_t)k * 0x9E3779B97F4A7C15ull;
     h_draw[k] = (int)(splitmix(s) % (uint64_t)n);
   }
   __syncthreads();
+  // For every start position p: the positions q, r of the second and third index the
+  // reference's rejection loops take from there (packed q | r << 16; -1 past the precomputed
+  // draws).  The walk over the iterations is then one dependent load per iteration.
+  for (int p = tid; p < ndraw; p += blockDim.x) {
+    const int i0 = h_draw[p];
+    int q = p + 1;
+    while (q < ndraw && h_draw[q] == i0) ++q;
+    int r = q + 1;
+    while (r < ndraw && (h_draw[r] == i0 || h_draw[r] == h_draw[q])) ++r;
+    h_qr[p] = r < ndraw ? q | (r << 16) : -1;
+  }
+  __syncthreads();
   if (tid == 0) {
-    int pos = 0;
+    int pos = 0, it = 0;
+    for (; it < iters && pos < ndraw; ++it) {
+      const int e = h_qr[pos];
+      if (e < 0) break;
+      h_id[it][0] = h_draw[pos]; h_id[it][1] = h_draw[e & 0xffff]; h_id[it][2] = h_draw[e >> 16];
+      pos = (e >> 16) + 1;
+    }
     uint64_t rs = rs0;
-    auto draw = [&]() -> int {
+    auto draw = [&]() -> int {   // the rest in sequence: precomputed draws, then fresh ones
       if (pos < ndraw) { ++pos; return h_draw[pos - 1]; }
       if (pos == ndraw) rs = rs0 + (uint64_t)ndraw * 0x9E3779B97F4A7C15ull;
       ++pos;
       return (int)(splitmix(rs) % (uint64_t)n);
     };
-    for (int it = 0; it < iters; ++it) {
+    for (; it < iters; ++it) {
       const int id0 = draw();
       int id1, id2;
       do id1 = draw(); while (id1 == id0);
@@ -366,26 +400,34 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   __syncthreads();
 }
 
-// subsample (objmap.cpp:37-42) of v[0..n) into S (<= SMG_SUB values); returns its size
+// subsample (objmap.cpp:37-42) of v[0..n) into S (<= SMG_SUB values); returns its size.
+// Each thread issues its (up to 4) loads before storing any.  No barrier: the caller syncs.
 DEV int subsample_to(const double* v, int n, double* S) {
   const int nS = n <= SMG_SUB ? n : SMG_SUB;
-  for (int i = threadIdx.x; i < nS; i += blockDim.x)
-    if (INB(i, SMG_SUB, 117) && INB(n <= SMG_SUB ? i : (size_t)i * (size_t)n / SMG_SUB, n, 118))
-      S[i] = n <= SMG_SUB ? v[i] : v[(size_t)i * (size_t)n / SMG_SUB];
-  __syncthreads();
+  for (int c0 = 0; c0 < nS; c0 += 4 * blockDim.x) {
+    double t[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = c0 + j * blockDim.x + threadIdx.x;
+      const size_t src = n <= SMG_SUB ? (size_t)i : (size_t)i * (size_t)n / SMG_SUB;
+      t[j] = i < nS && INB(src, n, 118) ? v[src] : 0.0;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = c0 + j * blockDim.x + threadIdx.x;
+      if (i < nS && INB(i, SMG_SUB, 117)) S[i] = t[j];
+    }
+  }
   return nS;
 }
 
-DEV bool lab_is(const uint16_t* label, int W, int H, int u, int v, uint16_t L) {
-  return u >= 0 && v >= 0 && u < W && v < H && INB((size_t)v * W + u, (size_t)W * H, 116) && label[(size_t)v * W + u] == L;
-}
 
 __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs per SM: <= 64 registers
-  extern __shared__ unsigned char smem_raw[];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   uint64_t* hkey = (uint64_t*)smem_raw;                         // OBS_HASH keys
   uint32_t* hidx = (uint32_t*)(smem_raw + OBS_HASH * 8);        // OBS_HASH first index
   double* S = (double*)smem_raw;                                // SMG_SUB values (aliases the hash)
-  __shared__ int hist[256];
+  int* hist = (int*)(S + SMG_SUB);                              // MAD selection histogram
   __shared__ BlockScratch bs;
   __shared__ PlaneOut pout;
   const int m = blockIdx.y, k = blockIdx.x, tid = threadIdx.x;
@@ -434,37 +476,49 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   const double* T = F.T_mc;
   __shared__ int scan_db[2][33];
   int scan_it = 0;
-  // 1. back-projection in raster order (objmap.cpp:667-688), ordered compaction
+  // 1. back-projection in raster order (objmap.cpp:667-688), ordered compaction.  Each thread
+  // takes OBS_PPT consecutive raster pixels and issues all their label and depth loads before
+  // using any, so one round trip to memory covers them.
   int n = 0;
-  for (int c0 = 0; c0 < npix; c0 += blockDim.x) {
-    const int idx = c0 + tid;
-    int ok = 0;
-    double px = 0, py = 0, pz = 0, zz = 0;
-    int uu = 0, vv = 0;
-    if (idx < npix) {
-      const int r = idx / ncols, cc = idx - r * ncols;
-      uu = u0 + cc * sk;
-      vv = v0 + r * sk;
-      // mask cell (i, j) = pixel (u, v); 1-cell erosion; rows j < 1 or j >= MH-1 are skipped
-      if (vv >= 1 && vv < H - 1 && lab_is(F.label, W, H, uu, vv, L) && lab_is(F.label, W, H, uu - 1, vv, L) &&
-          lab_is(F.label, W, H, uu + 1, vv, L) && lab_is(F.label, W, H, uu, vv - 1, L) && lab_is(F.label, W, H, uu, vv + 1, L)) {
-        const float z = INB((size_t)vv * W + uu, (size_t)W * H, 111) ? F.depth[(size_t)vv * W + uu] : 0.f;
-        if (z > P.zmin && z < P.zmax) {
-          const double xc = (double)(((float)uu - F.cx) / F.fx * z), yc = (double)(((float)vv - F.cy) / F.fy * z);
-          const double zd = (double)z;
-          px = T[0] * xc + T[1] * yc + T[2] * zd + T[3];
-          py = T[4] * xc + T[5] * yc + T[6] * zd + T[7];
-          pz = T[8] * xc + T[9] * yc + T[10] * zd + T[11];
-          zz = zd;
-          ok = 1;
+  for (int c0 = 0; c0 < npix; c0 += blockDim.x * OBS_PPT) {
+    const int i0 = c0 + tid * OBS_PPT;
+    float zv[OBS_PPT];
+    int okm = 0;
+#pragma unroll
+    for (int j = 0; j < OBS_PPT; ++j) {
+      const int idx = i0 + j;
+      zv[j] = 0.f;
+      if (idx < npix) {
+        const int r = idx / ncols, cc = idx - r * ncols;
+        const int uu = u0 + cc * sk, vv = v0 + r * sk;
+        // mask cell (i, j) = pixel (u, v); 1-cell erosion; rows j < 1 or j >= MH-1 are skipped
+        if (vv >= 1 && vv < H - 1 && INB((size_t)vv * W + uu, (size_t)W * H, 111)) {
+          const size_t at = (size_t)vv * W + uu;
+          const uint16_t* lp = F.label + at;
+          const bool lm = (lp[0] == L) & (uu > 0 && lp[-1] == L) & (uu + 1 < W && lp[1] == L) & (lp[-W] == L) & (lp[W] == L);
+          const float z = F.depth[at];
+          if (lm && z > P.zmin && z < P.zmax) { okm |= 1 << j; zv[j] = z; }
         }
       }
     }
     int tot;
-    const int pos = block_scan_db(ok, &tot, scan_db, scan_it++);
-    if (ok && INB(n + pos, B.pmax, 101)) {
-      X[n + pos] = px; Y[n + pos] = py; Z[n + pos] = pz; ZC[n + pos] = zz;
-      PU[n + pos] = uu; PV[n + pos] = vv;
+    int o = n + block_scan_db(__popc(okm), &tot, scan_db, scan_it++);
+#pragma unroll
+    for (int j = 0; j < OBS_PPT; ++j) {
+      if (!((okm >> j) & 1)) continue;
+      const int idx = i0 + j, r = idx / ncols, cc = idx - r * ncols;
+      const int uu = u0 + cc * sk, vv = v0 + r * sk;
+      const float z = zv[j];
+      const double xc = (double)(((float)uu - F.cx) / F.fx * z), yc = (double)(((float)vv - F.cy) / F.fy * z);
+      const double zd = (double)z;
+      if (INB(o, B.pmax, 101)) {
+        X[o] = T[0] * xc + T[1] * yc + T[2] * zd + T[3];
+        Y[o] = T[4] * xc + T[5] * yc + T[6] * zd + T[7];
+        Z[o] = T[8] * xc + T[9] * yc + T[10] * zd + T[11];
+        ZC[o] = zd;
+        PU[o] = uu; PV[o] = vv;
+      }
+      ++o;
     }
     n += tot;
   }
@@ -475,6 +529,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   __syncthreads();
   // 2. MAD depth band (objmap.cpp:692-695)
   int nS = subsample_to(ZC, n, S);
+  __syncthreads();
   const int kmed = pct_index(nS, 0.5);
   const double zmed = block_select(S, nS, kmed, hist, bs);
   for (int i = tid; i < nS; i += blockDim.x) S[i] = fabs(S[i] - zmed);
@@ -489,9 +544,10 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   const double* E0 = F.eef[0];
   const double* E1 = F.eef[1];
   int near_local = 0, w = 0;
+  int32_t* HS = (int32_t*)SCR;   // per point: its voxel's hash slot, -1 when it enters no voxel
   for (int c0 = 0; c0 < n; c0 += blockDim.x) {
     const int i = c0 + tid;
-    int keep = 0;
+    int keep = 0, hs = -1;
     if (i < n) {
       keep = INB(i, B.pmax, 112) && !(fabs(ZC[i] - zmed) > band);
       if (keep) {
@@ -506,11 +562,12 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
           uint32_t h = hmix(key) & (OBS_HASH - 1);
           for (int probe = 0; probe < OBS_HASH; ++probe) {
             const unsigned long long prev = atomicCAS((unsigned long long*)&hkey[h], ~0ull, (unsigned long long)key);
-            if (prev == ~0ull || prev == key) { atomicMin(&hidx[h], (uint32_t)i); break; }
+            if (prev == ~0ull || prev == key) { atomicMin(&hidx[h], (uint32_t)i); hs = (int)h; break; }
             h = (h + 1) & (OBS_HASH - 1);
           }
         }
       }
+      if (INB(i, B.pmax, 112)) HS[i] = hs;
     }
     int tot;
     const int pos = block_scan_db(keep, &tot, scan_db, scan_it++);
@@ -519,26 +576,14 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   }
   const int near_hand = block_sum_i(near_local, bs);
   const int np = w;
-  // emit the first point of each voxel, raster order
+  // emit the first point of each voxel, raster order (same thread per point as the pass above)
   int nc = 0;
   for (int c0 = 0; c0 < n; c0 += blockDim.x) {
     const int i = c0 + tid;
     int emit = 0;
-    if (i < n && INB(i, B.pmax, 113) && !(fabs(ZC[i] - zmed) > band)) {
-      const double x = X[i], y = Y[i], z = Z[i];
-      const double d0 = (x - E0[0]) * (x - E0[0]) + (y - E0[1]) * (y - E0[1]) + (z - E0[2]) * (z - E0[2]);
-      const double d1 = (x - E1[0]) * (x - E1[0]) + (y - E1[1]) * (y - E1[1]) + (z - E1[2]) * (z - E1[2]);
-      const double dh2 = smin(d0, d1);
-      const double bx = x - F.base[0], by = y - F.base[1];
-      if (dh2 >= chand2 && bx * bx + by * by >= body2) {
-        const uint64_t key = voxel_key((float)x, (float)y, (float)z, B.inv_vox);
-        uint32_t h = hmix(key) & (OBS_HASH - 1);
-        for (int probe = 0; probe < OBS_HASH; ++probe) {
-          if (!INB(h, OBS_HASH, 114)) break;
-          if (hkey[h] == key) { emit = hidx[h] == (uint32_t)i; break; }
-          h = (h + 1) & (OBS_HASH - 1);
-        }
-      }
+    if (i < n && INB(i, B.pmax, 113)) {
+      const int hs = HS[i];
+      emit = hs >= 0 && INB(hs, OBS_HASH, 114) && hidx[hs] == (uint32_t)i;
     }
     int tot;
     const int pos = block_scan_db(emit, &tot, scan_db, scan_it++);
@@ -564,6 +609,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     int* mh = (int*)(S + 3 * SMG_SUB);
     int nS3 = 0;
     for (int a = 0; a < 3; ++a) nS3 = subsample_to(AX[a], np, SB[a]);
+    __syncthreads();
     const double* arr[9] = {SB[0], SB[0], SB[0], SB[1], SB[1], SB[1], SB[2], SB[2], SB[2]};
     const int nn[9] = {nS3, nS3, nS3, nS3, nS3, nS3, nS3, nS3, nS3};
     const int kk[9] = {pct_index(nS3, 0.5), pct_index(nS3, 0.1), pct_index(nS3, 0.9), pct_index(nS3, 0.5), pct_index(nS3, 0.1),
@@ -607,8 +653,16 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     const double dc = hypot3(cen0 / nc - T[3], cen1 / nc - T[7], cen2 / nc - T[11]);
     const double tau = smin(P.ransac_tau_max, P.ransac_tau0 + P.ransac_tau_k * dc * dc);
     const uint64_t sb = (uint64_t)__double_as_longlong(F.stamp);
-    plane_fit(CX, nc, tau, ap_seed(sb, (uint64_t)k), P.ransac_iters, B.need_tab, SCR, B.pmax, (int*)smem_raw,
-              (int*)smem_raw + SEL_MAXQ * 256, bs, &pout);
+    // the hash is dead: plane-fit working set, then the points when they fit
+    PlaneSmem* ps = (PlaneSmem*)smem_raw;
+    const float* PX = CX;
+    if ((size_t)nc * 12 + sizeof(PlaneSmem) <= OBS_SMEM) {
+      float* PXs = (float*)(smem_raw + sizeof(PlaneSmem));
+      for (int i = tid; i < 3 * nc; i += blockDim.x) PXs[i] = CX[i];
+      __syncthreads();
+      PX = PXs;
+    }
+    plane_fit(PX, nc, tau, ap_seed(sb, (uint64_t)k), P.ransac_iters, B.need_tab, SCR, B.pmax, ps, bs, &pout);
   } else if (tid == 0) {
     pout.ok = 0;
   }

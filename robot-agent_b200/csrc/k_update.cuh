@@ -12,7 +12,7 @@
 #include "k_assoc.cuh"
 
 #define UPD_THREADS 256
-#define UPD_SMEM(B) ((size_t)(B).max_det * sizeof(ObsRec) + sizeof(ObjRec) + 16)
+#define UPD_SMEM(B) ((size_t)(B).max_det * (sizeof(ObsRec) + sizeof(ObjRec)))
 
 DEV size_t cslot_glob(const Batch& B, int m, const ObjRec& o) { return (size_t)m * B.O + o.cloud_slot; }
 
@@ -66,14 +66,6 @@ DEV void refresh_nrm_into(const Batch& B, ObjRec& o, size_t og, BlockScratch& bs
   __syncthreads();
 }
 
-// block copy of an object record between global and shared memory
-DEV void rec_copy(ObjRec* dst, const ObjRec* src) {
-  const uint32_t* s = (const uint32_t*)src;
-  uint32_t* d = (uint32_t*)dst;
-  for (int i = threadIdx.x; i < (int)(sizeof(ObjRec) / 4); i += blockDim.x) d[i] = s[i];
-  __syncthreads();
-}
-
 // apAddView (scenemap objprob.cpp:312-356) for a detection fragment (whole = false), no text
 // model: the scalar part, run by one thread -- view tempering against the camera ring
 // (similar view at another stamp: kappa * temper), the ring of the newest 32 cameras, ver and
@@ -83,21 +75,23 @@ DEV void rec_copy(ObjRec* dst, const ObjRec* src) {
 DEV void ap_add_view_plan(const Batch& B, ObjRec& o, double kappa, double stamp, const double cam[6], double* k_out, int* phys_out) {
   double k = kappa;
   const double cmin = B.cos_temper;
+  const double td = B.p.temper_d, td2 = td * td;
   for (int c = 0; c < o.n_cams; ++c) {
-    const double* cc = o.cams[c];
+    const double* cc = cam_at(o, c);
     if (fabs(cc[6] - stamp) < 1e-6) continue;
-    const double dd = hypot3(cc[0] - cam[0], cc[1] - cam[1], cc[2] - cam[2]);
     const double ca = cc[3] * cam[3] + cc[4] * cam[4] + cc[5] * cam[5];
-    if (dd < B.p.temper_d && ca > cmin) { k = kappa * B.p.temper; break; }
+    if (!(ca > cmin)) continue;
+    // hypot(d) < temper_d: the squared norm decides it unless it lies within rounding of the
+    // bound, where the 3-argument hypot itself is evaluated
+    const double dx = cc[0] - cam[0], dy = cc[1] - cam[1], dz = cc[2] - cam[2];
+    const double s2 = dx * dx + dy * dy + dz * dz;
+    const bool close = fabs(s2 - td2) <= 1e-12 * td2 ? hypot3(dx, dy, dz) < td : s2 < td2;
+    if (close) { k = kappa * B.p.temper; break; }
   }
-  if (o.n_cams >= SMG_CAMS) {   // keep the newest 32 (push, then erase the front)
-    for (int c = 1; c < SMG_CAMS; ++c)
-      for (int j = 0; j < 7; ++j) o.cams[c - 1][j] = o.cams[c][j];
-    o.n_cams = SMG_CAMS - 1;
+  {   // keep the newest 32 (push, then erase the front)
+    const double c7[7] = {cam[0], cam[1], cam[2], cam[3], cam[4], cam[5], stamp};
+    cam_push(o, c7);
   }
-  for (int j = 0; j < 6; ++j) o.cams[o.n_cams][j] = cam[j];
-  o.cams[o.n_cams][6] = stamp;
-  ++o.n_cams;
   ++o.ver;
   o.k_frag += k;
   // free physical view slot: the one of 0..topk not referenced by the current views
@@ -124,16 +118,18 @@ DEV void ap_add_view_plan(const Batch& B, ObjRec& o, double kappa, double stamp,
   *phys_out = f;
 }
 
-// record one vector job (objmap.cpp:848, :970 -> apAddView) for object `og`
-DEV void upd_job(const Batch& B, int m, int* njobs, int* ntg, size_t og, int det, double k, int phys, int zero) {
+// record one vector job (objmap.cpp:848, :970 -> apAddView) for object `og`; tg: the frame's
+// target objects (shared memory)
+DEV void upd_job(const Batch& B, int64_t* tg_og, int* njobs, int* ntg, size_t og, int det, double k, int phys, int zero) {
+  const int m = blockIdx.x;
   const size_t base = (size_t)m * B.max_det;
   int tg = -1;
   for (int c = 0; c < *ntg; ++c)
-    if (B.upd_tg[base + c] == (int64_t)og) { tg = c; break; }
+    if (tg_og[c] == (int64_t)og) { tg = c; break; }
   if (tg < 0) {
     if (!INB(*ntg, B.max_det, 304)) return;
     tg = (*ntg)++;
-    B.upd_tg[base + tg] = (int64_t)og;
+    tg_og[tg] = (int64_t)og;
   }
   if (!INB(*njobs, B.max_det, 305)) return;
   UpdJob& j = B.upd_job[base + (*njobs)++];
@@ -144,61 +140,94 @@ DEV void upd_job(const Batch& B, int m, int* njobs, int* ntg, size_t og, int det
   j.k = k;
 }
 
-DEV int new_object_slot(const Batch& B, int m, int* cslot) {
-  MapRec* R = &B.maps[m];
-  if (R->n_free <= 0 || R->n_cfree <= 0 || R->n_obj >= B.O) { set_err(R, SMG_E_CAP_OBJ); return -1; }
-  if (!INB(R->n_free - 1, B.O, 303) || !INB(R->n_cfree - 1, B.O, 303)) return -1;
-  const int slot = B.freel[(size_t)m * B.O + --R->n_free];
-  *cslot = B.cfreel[(size_t)m * B.O + --R->n_cfree];
-  B.order[(size_t)m * B.O + R->n_obj++] = slot;
-  return slot;
+// push_event with the map's event count held by the caller (ev_base at entry, *evl added since)
+DEV void push_event_l(const Batch& B, int map, double t, const ObjRec& o, int kind, uint32_t key, int ev_base, int* evl) {
+  const int e = ev_base + (*evl)++;
+  if (e >= SMG_MAX_EVENTS) { set_err(&B.maps[map], SMG_E_CAP_EVENTS); return; }
+  EventRec& r = B.events[(size_t)map * SMG_MAX_EVENTS + e];
+  r.t = t;
+  r.id = o.id;
+  r.kind = kind;
+  r.key = key;
 }
+
 
 __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  ObsRec* OBs = (ObsRec*)smem_raw;   // staged observations
-  ObjRec* MO = (ObjRec*)(OBs + B.max_det);                                         // staged object record
-  __shared__ int sh_act, sh_slot, sh_cslot;
+  ObjRec* REC = (ObjRec*)smem_raw;                 // staged object records, indexed by observation
+  ObsRec* OB = (ObsRec*)(REC + B.max_det);         // staged observations
+  __shared__ int OL[SMG_MAX_DET];                  // observation list (detection order)
+  __shared__ int rec_slot[SMG_MAX_DET];            // object slot of record a (-1: record unused)
+  __shared__ int obs_rec[SMG_MAX_DET];             // record of each listed observation (-1: none)
   __shared__ int head[SMG_MAX_DET];
-  __shared__ int evn, njobs, ntg;
+  __shared__ int fl[SMG_MAX_DET], cfl[SMG_MAX_DET];   // the free-list entries new objects pop, in order
+  __shared__ int64_t tg_og[SMG_MAX_DET];           // target objects of the vector jobs
+  __shared__ int n_book[3], njobs, ntg;
   const int m = blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   MapRec* R = &B.maps[m];
   const smg_params& P = B.p;
   const double* T = F.T_mc;
-  const int nobs = R->n_obs;
+  const int nobs = R->n_obs, n_obj0 = R->n_obj, n_free0 = R->n_free, n_cfree0 = R->n_cfree;
   const bool has_z = F.emb != nullptr;
-  ObsRec* OB = OBs;
   {
     const uint32_t* src = (const uint32_t*)(B.obs + (size_t)m * B.max_det);
-    uint32_t* dst = (uint32_t*)OBs;
+    uint32_t* dst = (uint32_t*)OB;
     for (int i = tid; i < (int)(B.max_det * sizeof(ObsRec) / 4); i += blockDim.x) dst[i] = src[i];
+    for (int i = tid; i < nobs; i += blockDim.x) OL[i] = B.obs_list[(size_t)m * B.max_det + i];
+    if (tid < 3) n_book[tid] = 0;
   }
-  const int32_t* OL = B.obs_list + (size_t)m * B.max_det;
   const double* GD = B.gdot + (size_t)m * B.max_det * B.max_det;
   const double cam6[6] = {T[3], T[7], T[11], T[2], T[6], T[10]};
+  __syncthreads();
+  // association bookkeeping (objmap.cpp:807-809), one thread per observation
+  if (tid < nobs) {
+    ObsRec& o = OB[OL[tid]];
+    if (P.bridge_drop && o.n_same >= 2 && o.obs_to >= 0) { o.obs_to = -2; atomicAdd(&n_book[0], 1); }
+    else if (o.obs_to >= 0) { B.obj_hit[(size_t)m * B.O + o.obs_to] = 1; atomicAdd(&n_book[1], 1); }
+    else if (o.blocked) { o.obs_to = -2; atomicAdd(&n_book[2], 1); }
+  }
+  __syncthreads();
+  // per observation: its fusion head (the first fragment of its target with the most points,
+  // objmap.cpp:812-820) and its staged record (the target's first observation)
+  if (tid < nobs) {
+    const int b = OB[OL[tid]].obs_to;
+    int h = -1, first = -1;
+    if (b >= 0)
+      for (int a2 = 0; a2 < nobs; ++a2) {
+        const ObsRec& q = OB[OL[a2]];
+        if (q.obs_to != b) continue;
+        if (first < 0) first = a2;
+        if (h < 0 || q.n > OB[OL[h]].n) h = a2;
+      }
+    head[tid] = h;
+    const bool valid = b >= 0 && INB(b, n_obj0, 302);
+    obs_rec[tid] = valid ? first : -1;
+    rec_slot[tid] = valid && first == tid ? slot_at(B, m, b) : -1;
+    fl[tid] = tid < n_free0 && INB(n_free0 - 1 - tid, B.O, 303) ? B.freel[(size_t)m * B.O + n_free0 - 1 - tid] : -1;
+    cfl[tid] = tid < n_cfree0 && INB(n_cfree0 - 1 - tid, B.O, 303) ? B.cfreel[(size_t)m * B.O + n_cfree0 - 1 - tid] : -1;
+  }
+  __syncthreads();
+  {
+    const int wpr = (int)(sizeof(ObjRec) / 4);
+    for (int i = tid; i < nobs * wpr; i += blockDim.x) {
+      const int r = i / wpr, w = i - r * wpr;
+      if (rec_slot[r] >= 0) ((uint32_t*)&REC[r])[w] = ((const uint32_t*)&B.objs[oglob(B, m, rec_slot[r])])[w];
+    }
+  }
+  __syncthreads();
+  // The per-observation walk below runs on thread 0 against the staged copies, with the map
+  // scalars in registers: it waits on no global load.
+  uint32_t next_id = 0;
+  int n_obj = n_obj0, n_free = n_free0, n_cfree = n_cfree0, n_pop = 0, evn = 0, evl = 0, ev_base = 0;
+  long long n_new = 0;
   if (tid == 0) {
-    evn = 0;
+    next_id = R->next_id;
+    ev_base = R->n_events;
     njobs = 0;
     ntg = 0;
-    // association bookkeeping (objmap.cpp:807-809)
-    for (int a = 0; a < nobs; ++a) {
-      ObsRec& o = OB[OL[a]];
-      if (P.bridge_drop && o.n_same >= 2 && o.obs_to >= 0) { o.obs_to = -2; ++R->st.n_bridge; continue; }
-      if (o.obs_to >= 0) { B.obj_hit[(size_t)m * B.O + o.obs_to] = 1; ++R->st.n_assoc; }
-      else if (o.blocked) { o.obs_to = -2; ++R->st.n_blocked; }
-    }
-    // fragment fusion (objmap.cpp:812-835): head = first fragment with the most points
-    for (int a = 0; a < nobs; ++a) {
-      head[a] = -1;
-      const int b = OB[OL[a]].obs_to;
-      if (b < 0) continue;
-      int h = -1;
-      for (int a2 = 0; a2 < nobs; ++a2)
-        if (OB[OL[a2]].obs_to == b && (h < 0 || OB[OL[a2]].n > OB[OL[h]].n)) h = a2;
-      head[a] = h;
-    }
+    // fragment fusion (objmap.cpp:821-835) into each head, in observation order
     for (int a = 0; a < nobs; ++a) {
       ObsRec& o = OB[OL[a]];
       const int b = o.obs_to;
@@ -218,39 +247,42 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
       o.sec = 1;
     }
   }
-  __syncthreads();
   // update loop (objmap.cpp:837-997)
-  for (int a = 0; a < nobs; ++a) {
-    if (tid == 0) {
+  if (tid == 0) {
+    for (int a = 0; a < nobs; ++a) {
       ObsRec& o = OB[OL[a]];
       AssocRec& as = B.assoc[(size_t)m * B.max_det + o.det];
       as.n_valid = o.n;
       as.area_px = (float)o.n * o.sk * o.sk;
       as.depth_med = (float)o.zmed;
-      sh_act = 0;
-      if (o.obs_to >= 0 && INB(o.obs_to, R->n_obj, 302)) {
-        sh_act = 1;
-        sh_slot = slot_at(B, m, o.obs_to);
-        as.obj_id = B.objs[oglob(B, m, sh_slot)].id;
-      } else if (o.obs_to == -1) {
-        int cs = -1;
-        const int s = new_object_slot(B, m, &cs);
-        if (s >= 0) { sh_act = 2; sh_slot = s; sh_cslot = cs; }
+      int act = 0, r = -1, cs = -1;
+      if (o.obs_to >= 0 && INB(o.obs_to, n_obj, 302) && obs_rec[a] >= 0) {
+        act = 1;
+        r = obs_rec[a];
+        as.obj_id = REC[r].id;
+      } else if (o.obs_to == -1) {   // ObjectMap slot allocation (new object)
+        if (n_free <= 0 || n_cfree <= 0 || n_obj >= B.O || !INB(n_pop, nobs, 303) || fl[n_pop] < 0 || cfl[n_pop] < 0) {
+          set_err(R, SMG_E_CAP_OBJ);
+        } else {
+          const int slot = fl[n_pop];
+          cs = cfl[n_pop];
+          ++n_pop;
+          --n_free;
+          --n_cfree;
+          B.order[(size_t)m * B.O + n_obj++] = slot;
+          act = 2;
+          r = a;   // an unmatched observation's own record is free
+          rec_slot[r] = slot;
+        }
       }
-    }
-    __syncthreads();
-    const int act = sh_act;
-    ObsRec& o = OB[OL[a]];
-    const size_t og = oglob(B, m, sh_slot);
-    if (act == 1) {
-      rec_copy(MO, &B.objs[og]);
-      if (tid == 0) {
-        ObjRec& mo = *MO;
+      const size_t og = act ? oglob(B, m, rec_slot[r]) : 0;
+      if (act == 1) {
+        ObjRec& mo = REC[r];
         if (has_z) {
           double k;
           int phys;
           ap_add_view_plan(B, mo, o.kappa, F.stamp, cam6, &k, &phys);
-          upd_job(B, m, &njobs, &ntg, og, o.det, k, phys, 0);
+          upd_job(B, tg_og, &njobs, &ntg, og, o.det, k, phys, 0);
         }
         ++mo.n_ap_obs;
         mo.wall_like = 2 * mo.n_wall_obs >= mo.n_ap_obs;
@@ -331,22 +363,17 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
           mo.misses = 0;
           if (mo.state == 1) {
             mo.state = mo.moved ? 2 : 0;
-            push_event(B, m, F.stamp, mo, 6, (2u << 24) | (uint32_t)evn++);
+            push_event_l(B, m, F.stamp, mo, 6, (2u << 24) | (uint32_t)evn++, ev_base, &evl);
           }
           if (!mo.confirmed && (int)mo.n_obs >= P.confirm) {
             mo.confirmed = 1;
-            push_event(B, m, F.stamp, mo, 1, (2u << 24) | (uint32_t)evn++);
+            push_event_l(B, m, F.stamp, mo, 1, (2u << 24) | (uint32_t)evn++, ev_base, &evl);
           }
         }
-      }
-      __syncthreads();
-      rec_copy(&B.objs[og], MO);
-    } else if (act == 2) {
-      if (tid == 0) {   // new candidate (objmap.cpp:951-978)
-        ObjRec& mo = *MO;
-        const int cs = sh_cslot;
+      } else if (act == 2) {   // new candidate (objmap.cpp:951-978)
+        ObjRec& mo = REC[r];
         memset(&mo, 0, sizeof(ObjRec));
-        mo.id = R->next_id++;
+        mo.id = next_id++;
         mo.cls = o.cls;
         for (int k = 0; k < 3; ++k) { mo.pos[k] = mo.first_pos[k] = o.pos[k]; mo.ext[k] = o.ext[k]; mo.lo[k] = o.lo[k]; mo.hi[k] = o.hi[k]; }
         mo.n_obs = 1;
@@ -377,51 +404,62 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
         ++C.cgen;
         ++C.vgen;
         C.cver = 0xffffffffu;
-        B.touched[(size_t)m * B.O + R->n_obj - 1] = 1;
-        B.obj_hit[(size_t)m * B.O + R->n_obj - 1] = 1;
-      }
-      if (tid == 0) {
-        ObjRec& mo = *MO;
+        B.touched[(size_t)m * B.O + n_obj - 1] = 1;
+        B.obj_hit[(size_t)m * B.O + n_obj - 1] = 1;
         if (has_z) {   // a recycled slot starts from an empty r_frag (objprob.cpp:329 assigns zeros)
           double k;
           int phys;
           ap_add_view_plan(B, mo, o.kappa, F.stamp, cam6, &k, &phys);
-          upd_job(B, m, &njobs, &ntg, og, o.det, k, phys, 1);
+          upd_job(B, tg_og, &njobs, &ntg, og, o.det, k, phys, 1);
         }
         mo.n_ap_obs = 1;
         mo.n_wall_obs = 0;
         mo.n_struct_look = 0;
         mo.wall_like = 0;
-        ++R->st.n_new;
-      }
-      // frame grouping (objmap.cpp:980-995): later unmatched fragments touching this one, with
-      // the dot products computed by k_assoc
-      if (P.frame_group && tid == 0) {
-        for (int b2 = a + 1; b2 < nobs; ++b2) {
-          ObsRec& q = OB[OL[b2]];
-          if (q.obs_to != -1 || !has_z) continue;
-          double g2 = 0;
-          for (int k = 0; k < 3; ++k) {
-            const double g = smax3(0.0, q.lo[k] - o.hi[k], o.lo[k] - q.hi[k]);
-            g2 += g * g;
+        ++n_new;
+        // frame grouping (objmap.cpp:980-995): later unmatched fragments touching this one, with
+        // the dot products computed by k_assoc
+        if (P.frame_group) {
+          for (int b2 = a + 1; b2 < nobs; ++b2) {
+            ObsRec& q = OB[OL[b2]];
+            if (q.obs_to != -1 || !has_z) continue;
+            double g2 = 0;
+            for (int k = 0; k < 3; ++k) {
+              const double g = smax3(0.0, q.lo[k] - o.hi[k], o.lo[k] - q.hi[k]);
+              g2 += g * g;
+            }
+            if (g2 > 0.02 * 0.02) continue;
+            double f[7] = {0, 0, 0, 0, 0, 0, 0};
+            pair_geo(q.lo, q.hi, q.pos, o.lo, o.hi, o.pos, GD[(size_t)a * B.max_det + b2], P.cos0, f);
+            f[0] = 1.0;
+            if (1.0 / (1.0 + exp(-same_logit(P.w, f))) >= P.same_p) { q.obs_to = n_obj - 1; obs_rec[b2] = r; }
           }
-          if (g2 > 0.02 * 0.02) continue;
-          double f[7] = {0, 0, 0, 0, 0, 0, 0};
-          pair_geo(q.lo, q.hi, q.pos, o.lo, o.hi, o.pos, GD[(size_t)a * B.max_det + b2], P.cos0, f);
-          f[0] = 1.0;
-          if (1.0 / (1.0 + exp(-same_logit(P.w, f))) >= P.same_p) q.obs_to = R->n_obj - 1;
         }
+        push_event_l(B, m, F.stamp, mo, 0, (2u << 24) | (uint32_t)evn++, ev_base, &evl);
       }
-      if (tid == 0) push_event(B, m, F.stamp, *MO, 0, (2u << 24) | (uint32_t)evn++);
-      __syncthreads();
-      rec_copy(&B.objs[og], MO);
     }
-    __syncthreads();
-  }
-  if (tid == 0) {
+    R->next_id = next_id;
+    R->n_obj = n_obj;
+    R->n_free = n_free;
+    R->n_cfree = n_cfree;
+    R->n_events = ev_base + evl;
+    R->st.n_bridge += n_book[0];
+    R->st.n_assoc += n_book[1];
+    R->st.n_blocked += n_book[2];
+    R->st.n_new += n_new;
     R->n_evn = evn;
     B.upd_n[2 * m] = njobs;
     B.upd_n[2 * m + 1] = ntg;
+  }
+  __syncthreads();
+  // write back every staged record and the job targets
+  {
+    const int wpr = (int)(sizeof(ObjRec) / 4);
+    for (int i = tid; i < nobs * wpr; i += blockDim.x) {
+      const int r = i / wpr, w = i - r * wpr;
+      if (rec_slot[r] >= 0) ((uint32_t*)&B.objs[oglob(B, m, rec_slot[r])])[w] = ((const uint32_t*)&REC[r])[w];
+    }
+    for (int c = tid; c < ntg; c += blockDim.x) B.upd_tg[(size_t)m * B.max_det + c] = tg_og[c];
   }
 }
 

@@ -460,7 +460,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   b->last_cam_t.assign(M, -1e300);
   b->last_cam_fwd.assign(3 * (size_t)M, 0.0);
   // kernels with large dynamic shared memory
-  CK(cudaFuncSetAttribute(k_obs, cudaFuncAttributeMaxDynamicSharedMemorySize, OBS_HASH * 12));
+  CK(cudaFuncSetAttribute(k_obs, cudaFuncAttributeMaxDynamicSharedMemorySize, OBS_SMEM));
   {
     const int sm_assoc = ((D * 4 + SP_MAX * 12 + 7) & ~7) + O * 8;
     CK(cudaFuncSetAttribute(k_assoc, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_assoc));
@@ -617,7 +617,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({2, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_obs<<<dim3(B.max_det, M), OBS_THREADS, OBS_HASH * 12, st>>>(B);
+  k_obs<<<dim3(B.max_det, M), OBS_THREADS, OBS_SMEM, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({3, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
@@ -907,8 +907,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_plane_sets(const float* xyz, con
                                                             double tau, const uint64_t* seeds, int max_iters,
                                                             const int32_t* need_tab, double* scr, double* out) {
   __shared__ BlockScratch bs;
-  __shared__ int hist[SEL_MAXQ * 256];
-  __shared__ int draws[RANSAC_DRAWS];
+  __shared__ PlaneSmem ps;
   __shared__ PlaneOut po;
   const int s = blockIdx.x;
   if (s >= n_sets) return;
@@ -919,7 +918,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_plane_sets(const float* xyz, con
     return;
   }
   const int n = e - a;
-  plane_fit(xyz + 3 * (size_t)a, n, tau, seeds[s], max_iters, need_tab, scr + 2 * (size_t)a, n, hist, draws, bs, &po);
+  plane_fit(xyz + 3 * (size_t)a, n, tau, seeds[s], max_iters, need_tab, scr + 2 * (size_t)a, n, &ps, bs, &po);
   if (threadIdx.x == 0) {
     const double dflt[10] = {0, 0, 0, 1, 1, 0, 0, 0, 0, 0};
     if (!po.ok) {

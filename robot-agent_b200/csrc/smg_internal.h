@@ -105,7 +105,7 @@ typedef struct {
   int32_t view_slot[SMG_TOPK_MAX + 1];
   float vkappa[SMG_TOPK_MAX + 1];
   double vstamp[SMG_TOPK_MAX + 1];
-  int32_t n_cams;
+  int32_t n_cams, cam_head;   // camera ring: n_cams newest, oldest at cams[cam_head]
   double cams[SMG_CAMS][7];
   int32_t n_wall_obs, n_ap_obs, n_struct_look;
   double whole_kappa;
