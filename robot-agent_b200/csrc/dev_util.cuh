@@ -212,7 +212,7 @@ DEV double d_unord(uint64_t k) {
 
 // Exact k-th smallest (0-based) of a[0..n) by MSB-first radix selection on the ordered bit
 // pattern: returns exactly the value std::nth_element leaves at position k.
-// hist: 256 shared ints.  All threads of the block must call it.
+// hist: SEL_HIST(1) shared ints.  All threads of the block must call it.
 DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s);
 DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& s) {
   __shared__ double sel1;
@@ -223,65 +223,102 @@ DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& 
 }
 
 // Up to SEL_MAXQ exact selections at once: value q = the k[q]-th smallest of a[q][0..n[q]).
-// Each query walks the key bytes MSB first (one histogram of the keys that share the decided
-// prefix per round); histogram increments are aggregated per warp over the lanes with the same
-// byte as the warp's first active lane, so the first bytes (shared by most keys) do not
-// serialise on one counter.  Once the chosen byte holds at most SEL_GATHER keys, those keys are
-// gathered and ranked by one warp instead of running the remaining byte rounds.  Two barriers
-// per round.
-// hist: SEL_MAXQ*256 ints (shared).  Needs nq <= warps of the block.  All threads must call it.
+// Keys are the ordered bit patterns.  The bits every key of an array shares (its minimum and
+// maximum agree on them) are decided first; then each query walks the remaining bits MSB first,
+// 8 per round, with one histogram of the keys under its decided prefix per round.  Queries on
+// the same array share the first histogram (their prefixes only part after it).  Once the
+// chosen digit holds at most SEL_GATHER keys, those are gathered and ranked by one warp instead
+// of running the remaining rounds.  Two barriers per round.
+// hist: SEL_HIST(nq) shared ints.  Needs nq <= warps of the block.  All threads must call it.
 #define SEL_MAXQ 9
 #define SEL_GATHER 32
+#define SEL_HIST(nq) (2 * (nq) * 256)
 DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s) {
-  __shared__ unsigned long long sh_prefix[SEL_MAXQ];
+  __shared__ unsigned long long sh_prefix[SEL_MAXQ], sh_mn[SEL_MAXQ], sh_mx[SEL_MAXQ];
   __shared__ unsigned long long sh_g[SEL_MAXQ][SEL_GATHER];
-  __shared__ int sh_k[SEL_MAXQ], sh_dec[SEL_MAXQ], sh_mode[SEL_MAXQ], sh_gn[SEL_MAXQ], sh_live;
+  __shared__ int sh_k[SEL_MAXQ], sh_dec[SEL_MAXQ], sh_mode[SEL_MAXQ], sh_gn[SEL_MAXQ], sh_first[SEL_MAXQ], sh_ld[SEL_MAXQ], sh_live;
   const int tid = threadIdx.x, lane = tid & 31, wq = tid >> 5;
+  int* hist0 = hist + nq * 256;   // first histogram of each group leader (queries on one array share it)
 #ifdef SMG_CHECKS
   if (tid == 0 && (nq > SEL_MAXQ || nq > (int)(blockDim.x >> 5))) smg_chk_fail(132, nq, SEL_MAXQ);
   if (tid < nq && (kq[tid] < 0 || kq[tid] >= n[tid])) smg_chk_fail(130, kq[tid], n[tid]);
 #endif
-  for (int i = tid; i < nq * 256; i += blockDim.x) hist[i] = 0;
-  if (tid < nq) { sh_prefix[tid] = 0; sh_k[tid] = kq[tid]; sh_dec[tid] = 0; sh_mode[tid] = 0; sh_gn[tid] = 0; }
+  for (int i = tid; i < 2 * nq * 256; i += blockDim.x) hist[i] = 0;
+  if (tid < nq) {
+    int ld = tid;
+    for (int q = 0; q < tid; ++q)
+      if (a[q] == a[tid] && n[q] == n[tid]) { ld = q; break; }
+    sh_ld[tid] = ld;
+    sh_k[tid] = kq[tid]; sh_mode[tid] = 0; sh_gn[tid] = 0; sh_first[tid] = 1; sh_mn[tid] = ~0ull; sh_mx[tid] = 0ull;
+  }
   if (tid == 0) sh_live = nq;
   __syncthreads();
+  // the bits every key of an array shares (its minimum and maximum agree on them) are decided first
+  for (int q = 0; q < nq; ++q) {
+    if (sh_ld[q] != q) continue;
+    unsigned long long mn = ~0ull, mx = 0ull;
+    for (int i = tid; i < n[q]; i += blockDim.x) {
+      const unsigned long long key = d_ord(a[q][i]);
+      mn = key < mn ? key : mn;
+      mx = key > mx ? key : mx;
+    }
+    // warp min / max of the 64-bit keys as two 32-bit reductions (high word, then low word)
+    const unsigned hmn = __reduce_min_sync(0xffffffffu, (unsigned)(mn >> 32));
+    const unsigned lmn = __reduce_min_sync(0xffffffffu, (unsigned)(mn >> 32) == hmn ? (unsigned)mn : 0xffffffffu);
+    const unsigned hmx = __reduce_max_sync(0xffffffffu, (unsigned)(mx >> 32));
+    const unsigned lmx = __reduce_max_sync(0xffffffffu, (unsigned)(mx >> 32) == hmx ? (unsigned)mx : 0u);
+    if (lane == 0) {
+      atomicMin(&sh_mn[q], ((unsigned long long)hmn << 32) | lmn);
+      atomicMax(&sh_mx[q], ((unsigned long long)hmx << 32) | lmx);
+    }
+  }
+  __syncthreads();
+  if (tid < nq) {
+    const unsigned long long mn = sh_mn[sh_ld[tid]], d = mn ^ sh_mx[sh_ld[tid]];
+    const int dec = d ? __clzll((long long)d) : 64;
+    sh_dec[tid] = dec;
+    sh_prefix[tid] = dec == 0 ? 0ull : mn & (~0ull << (64 - dec));
+    if (dec == 64 || n[tid] <= 0) {   // all keys equal (or none)
+      out[tid] = d_unord(mn);
+      sh_mode[tid] = 2;
+      atomicSub(&sh_live, 1);
+    }
+  }
+  __syncthreads();
   for (int round = 0; round < 10; ++round) {
-    // A: histogram (mode 0) or gather (mode 1) of the keys under each query's prefix
+    // A: histogram (mode 0) or gather (mode 1) of the keys under each query's prefix; the first
+    // histogram of a group is taken by its leader alone
     for (int q = 0; q < nq; ++q) {
-      const int mode = sh_mode[q];
-      if (mode == 2) continue;
+      const int mode = sh_mode[q], first = sh_first[q];
+      if (mode == 2 || (mode == 0 && first && sh_ld[q] != q)) continue;
       const int dec = sh_dec[q];
       const uint64_t pre = sh_prefix[q], msk = dec == 0 ? 0ull : ~0ull << (64 - dec);
-      const int shift = 56 - dec;
+      const int wdt = 64 - dec < 8 ? 64 - dec : 8, shift = 64 - dec - wdt;   // next digit: bits [shift, shift + wdt)
+      int* hq = (first ? hist0 : hist) + q * 256;
       const double* aq = a[q];
       const int nqq = n[q];
-      for (int i0 = 0; i0 < nqq; i0 += blockDim.x) {
-        const int i = i0 + tid;
-        const uint64_t key = i < nqq ? d_ord(aq[i]) : 0ull;
-        const bool act = i < nqq && (key & msk) == pre;
+      for (int i = tid; i < nqq; i += blockDim.x) {
+        const uint64_t key = d_ord(aq[i]);
+        if ((key & msk) != pre) continue;
         if (mode == 0) {
-          // the lanes sharing the first active lane's byte add with one atomic
-          const unsigned am = __ballot_sync(0xffffffffu, act);
-          const unsigned bin = (unsigned)(key >> shift) & 255u;
-          const int src = am ? __ffs(am) - 1 : 0;
-          const unsigned b0 = __shfl_sync(0xffffffffu, bin, src);
-          const unsigned same = __ballot_sync(0xffffffffu, act && bin == b0);
-          if (am && lane == src) atomicAdd(&hist[q * 256 + b0], __popc(same));
-          else if (act && bin != b0) atomicAdd(&hist[q * 256 + bin], 1);
-        } else if (act) {
+          atomicAdd(&hq[(unsigned)(key >> shift) & ((1u << wdt) - 1u)], 1);
+        } else {
           const int slot = atomicAdd(&sh_gn[q], 1);
           if (INB(slot, SEL_GATHER, 133)) sh_g[q][slot] = key;
         }
       }
     }
     __syncthreads();
-    // B: warp q picks the byte holding rank k (and clears its counters), or ranks the gathered keys
+    // B: warp q picks the digit holding rank k (clearing its own counters), or ranks the gathered keys
     if (wq < nq && sh_mode[wq] != 2) {
       const int k = sh_k[wq];
       if (sh_mode[wq] == 0) {
-        int* hq = hist + wq * 256;
+        const int first = sh_first[wq];
+        int* hq = first ? hist0 + sh_ld[wq] * 256 : hist + wq * 256;
         int c[8], tot = 0;
-        for (int j = 0; j < 8; ++j) { c[j] = hq[lane * 8 + j]; hq[lane * 8 + j] = 0; tot += c[j]; }
+        for (int j = 0; j < 8; ++j) { c[j] = hq[lane * 8 + j]; tot += c[j]; }
+        if (!first)
+          for (int j = 0; j < 8; ++j) hq[lane * 8 + j] = 0;
         int incl = tot;
         for (int o = 1; o < 32; o <<= 1) {
           const int y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -289,13 +326,14 @@ DEV void block_select_multi(const double* const* a, const int* n, const int* kq,
         }
         const int excl = incl - tot;
         const int all = __shfl_sync(0xffffffffu, incl, 31);
+        if (lane == 0) sh_first[wq] = 0;
         if (k >= excl && k < incl) {
           int kk = k - excl, b = 0;
           for (int j = 0; j < 8; ++j) {
             if (kk < c[j]) { b = j; break; }
             kk -= c[j];
           }
-          const int dec = sh_dec[wq] + 8;
+          const int d0 = sh_dec[wq], wdt = 64 - d0 < 8 ? 64 - d0 : 8, dec = d0 + wdt;
           sh_prefix[wq] |= (unsigned long long)(lane * 8 + b) << (64 - dec);
           sh_k[wq] = kk;
           sh_dec[wq] = dec;

@@ -320,7 +320,7 @@ DEV void contact_rebuild(const Batch& B, size_t cs, BlockScratch& bs) {
 // rebuilds its contact index.  Targets also include objects whose cloud moved (translate).
 __global__ void __launch_bounds__(512) k_cloud_add(Batch B) {
   __shared__ BlockScratch bs;
-  __shared__ int hist[256];
+  __shared__ int hist[SEL_HIST(1)];
   const int m = blockIdx.y;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;

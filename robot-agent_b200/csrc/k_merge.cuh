@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
 
 __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
   __shared__ BlockScratch bs;
-  __shared__ int hist[256];
+  __shared__ int hist[SEL_HIST(1)];
   __shared__ int sh_go, sh_ka, sh_kb, nused;
   __shared__ uint32_t used[2 * 256];
   const int m = blockIdx.x, tid = threadIdx.x;

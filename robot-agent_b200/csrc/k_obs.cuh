@@ -27,7 +27,7 @@
 // shared memory is free at that point passes a slice of it).
 struct PlaneSmem {
   double pl[RANSAC_MAX][4];   // hypothesis planes
-  int hist[SEL_MAXQ * 256];   // selection histograms
+  int hist[SEL_HIST(SEL_MAXQ)];   // selection histograms
   int draws[RANSAC_DBUF];     // RANSAC draws + next-triple table
   int id[RANSAC_MAX][3];      // hypothesis index triples
   int cnt[RANSAC_MAX];        // hypothesis inlier counts

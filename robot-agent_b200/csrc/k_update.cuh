@@ -14,6 +14,22 @@
 #define UPD_THREADS 256
 #define UPD_SMEM(B) ((size_t)(B).max_det * (sizeof(ObsRec) + sizeof(ObjRec)))
 
+// one warp copies an object record in 16-byte words, all of a lane's loads issued first
+static_assert(sizeof(ObjRec) % 16 == 0, "ObjRec is copied in 16-byte words");
+DEV void rec_load(ObjRec* dst, const ObjRec* src) {
+  constexpr int NW = (int)(sizeof(ObjRec) / 16), PER = (NW + 31) / 32;
+  const int lane = threadIdx.x & 31;
+  const uint4* s = (const uint4*)src;
+  uint4* d = (uint4*)dst;
+  uint4 t[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+    if (j * 32 + lane < NW) t[j] = s[j * 32 + lane];
+#pragma unroll
+  for (int j = 0; j < PER; ++j)
+    if (j * 32 + lane < NW) d[j * 32 + lane] = t[j];
+}
+
 DEV size_t cslot_glob(const Batch& B, int m, const ObjRec& o) { return (size_t)m * B.O + o.cloud_slot; }
 
 // ObjectMap::firstView (objmap.cpp:247-252) over the view-first hash
@@ -209,13 +225,8 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
     cfl[tid] = tid < n_cfree0 && INB(n_cfree0 - 1 - tid, B.O, 303) ? B.cfreel[(size_t)m * B.O + n_cfree0 - 1 - tid] : -1;
   }
   __syncthreads();
-  {
-    const int wpr = (int)(sizeof(ObjRec) / 4);
-    for (int i = tid; i < nobs * wpr; i += blockDim.x) {
-      const int r = i / wpr, w = i - r * wpr;
-      if (rec_slot[r] >= 0) ((uint32_t*)&REC[r])[w] = ((const uint32_t*)&B.objs[oglob(B, m, rec_slot[r])])[w];
-    }
-  }
+  for (int r = tid >> 5; r < nobs; r += blockDim.x >> 5)
+    if (rec_slot[r] >= 0) rec_load(&REC[r], &B.objs[oglob(B, m, rec_slot[r])]);
   __syncthreads();
   // The per-observation walk below runs on thread 0 against the staged copies, with the map
   // scalars in registers: it waits on no global load.
@@ -453,14 +464,9 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
   }
   __syncthreads();
   // write back every staged record and the job targets
-  {
-    const int wpr = (int)(sizeof(ObjRec) / 4);
-    for (int i = tid; i < nobs * wpr; i += blockDim.x) {
-      const int r = i / wpr, w = i - r * wpr;
-      if (rec_slot[r] >= 0) ((uint32_t*)&B.objs[oglob(B, m, rec_slot[r])])[w] = ((const uint32_t*)&REC[r])[w];
-    }
-    for (int c = tid; c < ntg; c += blockDim.x) B.upd_tg[(size_t)m * B.max_det + c] = tg_og[c];
-  }
+  for (int r = tid >> 5; r < nobs; r += blockDim.x >> 5)
+    if (rec_slot[r] >= 0) rec_load(&B.objs[oglob(B, m, rec_slot[r])], &REC[r]);
+  for (int c = tid; c < ntg; c += blockDim.x) B.upd_tg[(size_t)m * B.max_det + c] = tg_og[c];
 }
 
 // The D-length part of apAddView for every target object of the frame: one CTA per object

@@ -82,7 +82,7 @@ typedef struct {
   int32_t obs_to, n_same, blocked, sec;
 } ObsRec;
 
-typedef struct {
+typedef struct __align__(16) {   // 16-byte aligned: staged in shared memory in 16-byte words
   uint32_t id;
   int32_t cls;
   double pos[3], ext[3], first_pos[3], lo[3], hi[3];
