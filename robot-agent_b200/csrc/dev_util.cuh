@@ -133,18 +133,14 @@ template <int N>
 DEV void block_sum_multi(double (&v)[N], double* buf) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int k = 0; k < N; ++k) v[k] = warp_sum_d(v[k]);
-  __syncthreads();
   if (lane == 0)
     for (int k = 0; k < N; ++k) buf[k * 32 + wid] = v[k];
   __syncthreads();
-  if (wid == 0)
-    for (int k = 0; k < N; ++k) {
-      double r = lane < nw ? buf[k * 32 + lane] : 0.0;
-      r = warp_sum_d(r);
-      if (lane == 0) buf[k * 32] = r;
-    }
-  __syncthreads();
-  for (int k = 0; k < N; ++k) v[k] = buf[k * 32];
+  for (int k = 0; k < N; ++k) {   // every thread adds the warp sums in warp order
+    double r = 0.0;
+    for (int w = 0; w < nw; ++w) r += buf[k * 32 + w];
+    v[k] = r;
+  }
   __syncthreads();
 }
 

@@ -38,49 +38,88 @@ struct PlaneOut {
   double n[3], thick, inl, zmed, zlo, zhi, hspan;
 };
 
+// cos and sin of th = atan2(y, x) / 2, th in (-pi/2, pi/2], from the half-angle identities
+// (cos 2th = x / r, sin 2th = y / r, r = |(x, y)|): the larger of the two comes from its square
+// root and the other from sin 2th = 2 s c, so both keep full relative precision (within 2 ulps
+// of cos/sin of the libm angle).  Reciprocal square roots keep the dependent chain short.
+DEV void jacobi_cs(double y, double x, double* c, double* s) {
+  const double r2 = x * x + y * y;
+  if (!(r2 > 0)) { *c = 1.0; *s = 0.0; return; }
+  const double ri = rsqrt(r2);
+  if (x >= 0) {
+    const double t = 0.5 + 0.5 * (x * ri), rt = rsqrt(t);
+    *c = t * rt;
+    *s = (0.5 * y * ri) * rt;
+  } else {
+    const double t = 0.5 - 0.5 * (x * ri), rt = rsqrt(t);
+    *s = copysign(t * rt, y);
+    *c = (0.5 * y * ri) * copysign(rt, y);
+  }
+}
+
+// one Jacobi rotation in the (p, q) plane: A <- R^T A R, V <- V R (indices fixed at compile
+// time so A and V stay in registers)
+template <int p, int q>
+DEV void jacobi_rot(double (&A)[3][3], double (&V)[3][3], double c, double s) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const double akp = A[k][p], akq = A[k][q];
+    A[k][p] = c * akp - s * akq;
+    A[k][q] = s * akp + c * akq;
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const double apk = A[p][k], aqk = A[q][k];
+    A[p][k] = c * apk - s * aqk;
+    A[q][k] = s * apk + c * aqk;
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const double vkp = V[k][p], vkq = V[k][q];
+    V[k][p] = c * vkp - s * vkq;
+    V[k][q] = s * vkp + c * vkq;
+  }
+}
+
 // 3x3 symmetric Jacobi eigen-decomposition (scenemap objprob.cpp:50-84): ascending ev, columns V.
+// Each step rotates away the largest off-diagonal entry (first of (0,1), (0,2), (1,2) on ties)
+// until it is below 1e-12, at most 32 steps.
 DEV void eig_sym3(double A[3][3], double ev[3], double V[3][3]) {
+  double a[3][3], v[3][3];
+#pragma unroll
   for (int i = 0; i < 3; ++i)
-    for (int j = 0; j < 3; ++j) V[i][j] = i == j;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) { a[i][j] = A[i][j]; v[i][j] = i == j; }
   for (int it = 0; it < 32; ++it) {
-    int p = 0, q = 1;
-    double best = fabs(A[0][1]);
-    if (fabs(A[0][2]) > best) { best = fabs(A[0][2]); p = 0; q = 2; }
-    if (fabs(A[1][2]) > best) { best = fabs(A[1][2]); p = 1; q = 2; }
+    int sel = 0;
+    double best = fabs(a[0][1]);
+    if (fabs(a[0][2]) > best) { best = fabs(a[0][2]); sel = 1; }
+    if (fabs(a[1][2]) > best) { best = fabs(a[1][2]); sel = 2; }
     if (best < 1e-12) break;
-    const double th = 0.5 * atan2(2 * A[p][q], A[q][q] - A[p][p]);
-    const double c = cos(th), s = sin(th);
-    for (int k = 0; k < 3; ++k) {
-      const double akp = A[k][p], akq = A[k][q];
-      A[k][p] = c * akp - s * akq;
-      A[k][q] = s * akp + c * akq;
-    }
-    for (int k = 0; k < 3; ++k) {
-      const double apk = A[p][k], aqk = A[q][k];
-      A[p][k] = c * apk - s * aqk;
-      A[q][k] = s * apk + c * aqk;
-    }
-    for (int k = 0; k < 3; ++k) {
-      const double vkp = V[k][p], vkq = V[k][q];
-      V[k][p] = c * vkp - s * vkq;
-      V[k][q] = s * vkp + c * vkq;
-    }
+    double c, s;
+    if (sel == 0) { jacobi_cs(2 * a[0][1], a[1][1] - a[0][0], &c, &s); jacobi_rot<0, 1>(a, v, c, s); }
+    else if (sel == 1) { jacobi_cs(2 * a[0][2], a[2][2] - a[0][0], &c, &s); jacobi_rot<0, 2>(a, v, c, s); }
+    else { jacobi_cs(2 * a[1][2], a[2][2] - a[1][1], &c, &s); jacobi_rot<1, 2>(a, v, c, s); }
   }
   // stable ascending order of the diagonal (insertion sort, like std::sort on 3 elements)
-  int o[3] = {0, 1, 2};
-  for (int i = 1; i < 3; ++i) {
-    const int v = o[i];
-    int j = i;
-    while (j > 0 && A[v][v] < A[o[j - 1]][o[j - 1]]) { o[j] = o[j - 1]; --j; }
-    o[j] = v;
+  const double d[3] = {a[0][0], a[1][1], a[2][2]};
+  int o0 = 0, o1 = 1, o2 = 2;
+  if (d[o1] < d[o0]) { const int t = o0; o0 = o1; o1 = t; }
+  if (d[o2] < d[o1]) {
+    const int t = o1; o1 = o2; o2 = t;
+    if (d[o1] < d[o0]) { const int u = o0; o0 = o1; o1 = u; }
   }
-  double W[3][3];
+  const int o[3] = {o0, o1, o2};
+#pragma unroll
   for (int k = 0; k < 3; ++k) {
-    ev[k] = A[o[k]][o[k]];
-    for (int i = 0; i < 3; ++i) W[i][k] = V[i][o[k]];
+    ev[k] = o[k] == 0 ? d[0] : (o[k] == 1 ? d[1] : d[2]);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) V[i][k] = o[k] == 0 ? v[i][0] : (o[k] == 1 ? v[i][1] : v[i][2]);
   }
+#pragma unroll
   for (int i = 0; i < 3; ++i)
-    for (int j = 0; j < 3; ++j) V[i][j] = W[i][j];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) A[i][j] = a[i][j];
 }
 
 DEV int pct_index(int n, double q) {   // min(n-1, size_t(q*(n-1) + 0.5)) (objmap.cpp:17, objprob.cpp:87)
@@ -224,7 +263,8 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   // Sums are block trees.  Where the outcome is ill-conditioned in the reference's own rounding
   // (a point within 1e-11 of the tau boundary, a near-double smallest eigenvalue, a nearly
   // isotropic horizontal spread), thread 0 replays the whole refit with the reference's
-  // sequential sums in index order, so the result is the reference's bit for bit.  A near-zero
+  // sequential sums in index order, so inlier sets and sums are the reference's (the Jacobi
+  // rotations come from half-angle identities, within a few ulps of libm's trigonometry).  A near-zero
   // smallest eigenvalue (exactly planar points) is well-conditioned for the normal; only the
   // thickness sqrt(ev0) then differs, by at most ~sqrt(1e-16 * ev2).
   __shared__ int sh_deg, sh_ni, sh_ok;
@@ -292,9 +332,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     block_sum_multi<3>(a3, red);
     const double sxx = a3[0], sxy = a3[1], syy = a3[2];
     if (tid == 0 && 2 * fabs(sxy) + fabs(sxx - syy) <= 1e-3 * (sxx + syy)) sh_deg = 1;
-    const double th = 0.5 * atan2(2 * sxy, sxx - syy);
-    th_hc = cos(th);
-    th_hs = sin(th);
+    jacobi_cs(2 * sxy, sxx - syy, &th_hc, &th_hs);
   }
   __syncthreads();
   if (sh_deg) {   // exact replay in the reference's order (pcaOf objprob.cpp:101-114, :166-192)
@@ -336,9 +374,10 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
             const double dx = xyz[3 * i] - m[0], dy = xyz[3 * i + 1] - m[1];
             sxx += dx * dx; sxy += dx * dy; syy += dy * dy;
           }
-        const double th = 0.5 * atan2(2 * sxy, sxx - syy);
-        sh_hc = cos(th);
-        sh_hs = sin(th);
+        double hc, hs;
+        jacobi_cs(2 * sxy, sxx - syy, &hc, &hs);
+        sh_hc = hc;
+        sh_hs = hs;
         for (int i = 0; i < 3; ++i) {
           sh_ev[i] = ev[i];
           sh_m[i] = m[i];
