@@ -3,6 +3,7 @@
 // restated for the device.  Compiled with --fmad=false so that every float/double expression
 // rounds exactly like the reference's host build (baseline x86-64, no FMA contraction).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -428,25 +429,9 @@ DEV uint16_t ref_f2h(float f) {
   return (uint16_t)(sign | ((uint32_t)e << 10) | (m >> 13));
 }
 // fp16 bits -> float (scenemap objprob.cpp:31-47; exact widening)
-DEV float ref_h2f(uint16_t h) {
-  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
-  uint32_t e = (h >> 10) & 0x1f, m = h & 0x3ffu, x;
-  if (e == 0) {
-    if (m == 0) {
-      x = sign;
-    } else {
-      e = 127 - 15 + 1;
-      while (!(m & 0x400u)) { m <<= 1; --e; }
-      m &= 0x3ffu;
-      x = sign | (e << 23) | (m << 13);
-    }
-  } else if (e == 31) {
-    x = sign | 0x7f800000u | (m << 13);
-  } else {
-    x = sign | ((e + 127 - 15) << 23) | (m << 13);
-  }
-  return __uint_as_float(x);
-}
+// fp16 -> fp32 is exact for every finite value and infinity (what the reference's bitwise
+// widening computes); the hardware conversion gives the same floats, NaN stays NaN.
+DEV float ref_h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 DEV float emb_at(const void* emb, int dtype, int D, int k, int i) {
   if (dtype == SMG_EMB_BF16) {
