@@ -206,18 +206,33 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     if (INB(slot, ng, 701)) CPX[slot] = c;
   }
   __syncthreads();
+  // raster order within each cell: a bucketed pixel's place is the number of pixels of its
+  // cell with a smaller index (every slot counts over its own bucket, in parallel)
+  int32_t* SPX = CF;   // the per-pixel first flags are dead here: sorted buckets
+  for (int a = tid; a < off; a += blockDim.x) {
+    const int v = CPX[a];
+    const long long r = MK[v];
+    if (r < 0 || r >= ncell) continue;
+    const int e = CO[r], s0 = e - CC[r];
+    int pos = 0;
+    for (int b = s0; b < e; ++b) pos += CPX[b] < v;
+    if (INB(s0 + pos, ng, 706)) SPX[s0 + pos] = v;
+  }
+  __syncthreads();
   float* OUT = B.sc_pts + (size_t)m * (2 * SMG_BINS_MAX + SMG_MATCH_CELLS) * 4;
   for (int r = tid; r < ncell; r += blockDim.x) {
     const int n = CC[r], e = CO[r], s0 = e - n;
-    for (int a = s0 + 1; a < e; ++a) {   // raster order within the cell
-      const int v = CPX[a];
-      int b = a;
-      while (b > s0 && CPX[b - 1] > v) { CPX[b] = CPX[b - 1]; --b; }
-      CPX[b] = v;
-    }
     float sx = 0, sy = 0, snx = 0, sny = 0;
-    for (int a = s0; a < e; ++a) {
-      const float4 w = MV[CPX[a]];
+    int a = s0;
+    for (; a + 4 <= e; a += 4) {   // four loads in flight, added in order
+      const float4 w0 = MV[SPX[a]], w1 = MV[SPX[a + 1]], w2 = MV[SPX[a + 2]], w3 = MV[SPX[a + 3]];
+      sx += w0.x; sy += w0.y; snx += w0.z; sny += w0.w;
+      sx += w1.x; sy += w1.y; snx += w1.z; sny += w1.w;
+      sx += w2.x; sy += w2.y; snx += w2.z; sny += w2.w;
+      sx += w3.x; sy += w3.y; snx += w3.z; sny += w3.w;
+    }
+    for (; a < e; ++a) {
+      const float4 w = MV[SPX[a]];
       sx += w.x; sy += w.y; snx += w.z; sny += w.w;
     }
     const float nn = sqrtf(snx * snx + sny * sny);
