@@ -100,6 +100,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--preroll", type=int, default=100)
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--kt-steps", type=int, default=10, help="steps of the separate per-kernel timing pass")
     ap.add_argument("--maps", type=int, default=None, help="maps per GPU (default 64 for objprob, 1 for occ)")
     ap.add_argument("--max-objects", type=int, default=1024)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
@@ -222,7 +223,7 @@ def run_b200(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     M = args.maps
-    n_total = args.preroll + args.warmup + args.steps + args.e2e_steps
+    n_total = args.preroll + args.warmup + args.steps + args.kt_steps + args.e2e_steps
     from scenemap_b200 import dist
     wl = RoomBatch(M, 1000, n_total, D=1152, bf16=True, max_det=24, map_offset=dist.rank_maps(rank, world, M)[0],
                    device=str(dev))
@@ -245,8 +246,6 @@ def run_b200(args, rank, world, local_rank):
     R = wl.render(f, args.steps, sp)
     keep = []
     structs = [wl.structs(R, fi, keep) for fi in range(args.steps)]
-    B.timing_read()
-    B.timing(True)
     work0 = B.work()
     launches0 = B.launches()
     if world > 1:
@@ -266,12 +265,25 @@ def run_b200(args, rank, world, local_rank):
     clocks = clk.stop()
     t = e0.elapsed_time(e1) / 1e3
     launches = B.launches() - launches0
-    kt = B.timing_read()
-    B.timing(False)
     work1 = B.work()
     work = {k: (work1[k] - work0[k]) / args.steps for k in work0}   # per step (all maps of this GPU)
     err = B.error_word()
     f += args.steps
+    del R, structs
+    # per-kernel breakdown: a separate pass with event timing around every launch (the chain
+    # then runs as one stream group, so each kernel's time is its own)
+    R = wl.render(f, args.kt_steps, sp)
+    keep = []
+    structs = [wl.structs(R, fi, keep) for fi in range(args.kt_steps)]
+    torch.cuda.synchronize()
+    B.timing_read()
+    B.timing(True)
+    for fi in range(args.kt_steps):
+        B.push(None, smg.SMG_MEM_DEVICE, structs=structs[fi], stream=sp)
+    torch.cuda.synchronize()
+    kt = B.timing_read()
+    B.timing(False)
+    f += args.kt_steps
     del R, structs
     # e2e: host (pinned) inputs through the C ABI, association read back every step
     E = args.e2e_steps

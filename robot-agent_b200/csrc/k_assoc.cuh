@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
   float* sp = zs + B.D;                           // 3 * SP_MAX
   double* pp = (double*)(smem_raw + (((size_t)B.D * 4 + SP_MAX * 12 + 7) & ~(size_t)7));   // O
   __shared__ BlockScratch bs;
-  const int a = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+  const int a = blockIdx.x, m = B.map0 + blockIdx.y, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   const MapRec& R = B.maps[m];
   if (!F.active || a >= R.n_obs) return;

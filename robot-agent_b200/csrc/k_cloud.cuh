@@ -321,7 +321,7 @@ DEV void contact_rebuild(const Batch& B, size_t cs, BlockScratch& bs) {
 __global__ void __launch_bounds__(512) k_cloud_add(Batch B) {
   __shared__ BlockScratch bs;
   __shared__ int hist[SEL_HIST(1)];
-  const int m = blockIdx.y;
+  const int m = B.map0 + blockIdx.y;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const MapRec& R = B.maps[m];

@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   __shared__ BlockScratch bs;
   __shared__ int sh_n[4];
   __shared__ int sh_ins;
-  const int m = blockIdx.x, tid = threadIdx.x;
+  const int m = B.map0 + blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   MapRec* R = &B.maps[m];

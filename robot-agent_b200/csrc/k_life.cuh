@@ -80,7 +80,7 @@ DEV bool is_big(const smg_params& P, const ObjRec& o) {
 
 // absence and misses (objmap.cpp:1021-1061), one warp per object in list order
 __global__ void __launch_bounds__(256) k_absent(Batch B) {
-  const int m = blockIdx.y;
+  const int m = B.map0 + blockIdx.y;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   MapRec* R = &B.maps[m];
@@ -152,7 +152,7 @@ DEV void remap_id(const Batch& B, int m, uint32_t from, uint32_t to) {
 }
 
 #define RELINK_MAXC 256
-#define STRUCT_CTAS 64
+#define STRUCT_CTAS 32
 #define STRUCT_LIST 64
 #define STRUCT_SCR (4096 + 2 * 4096)   // doubles per CTA: points (as floats) + plane-fit scratch
 #define RELINK_STAGE 1024
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
   extern __shared__ unsigned char smem_raw[];
   double* s_pos = (double*)smem_raw;   // 3 per object
   float* mu = (float*)(s_pos + 3 * RELINK_STAGE);   // D per warp
-  const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const int m = B.map0 + blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   MapRec* R = &B.maps[m];
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
   __shared__ int mine[STRUCT_LIST];
   __shared__ int nmine;
   __shared__ int scan_db[2][33];
-  const int m = blockIdx.y;
+  const int m = B.map0 + blockIdx.y;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const MapRec& R = B.maps[m];
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
   __shared__ uint32_t s_id[PRUNE_MAX];
   __shared__ unsigned char s_rm[PRUNE_MAX], s_dirty[PRUNE_MAX];
   __shared__ BlockScratch bs;
-  const int m = blockIdx.x, tid = threadIdx.x;
+  const int m = B.map0 + blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   MapRec* R = &B.maps[m];
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
 // markView (objmap.cpp:219-245): sparse depth samples, horizontal camera->point segments, first
 // time each 2D cell was seen per range band.  Fresh cells are pre-filled with "never".
 __global__ void __launch_bounds__(256) k_markview(Batch B) {
-  const int m = blockIdx.x;
+  const int m = B.map0 + blockIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const smg_params& P = B.p;

@@ -31,7 +31,7 @@ DEV void pair_of(long long p, int n, int* pi, int* pj) {
 __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ int ngl;
-  const int m = blockIdx.y, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const int m = B.map0 + blockIdx.y, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const MapRec& R = B.maps[m];
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
   __shared__ int hist[SEL_HIST(1)];
   __shared__ int sh_go, sh_ka, sh_kb, nused;
   __shared__ uint32_t used[2 * 256];
-  const int m = blockIdx.x, tid = threadIdx.x;
+  const int m = B.map0 + blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   MapRec* R = &B.maps[m];

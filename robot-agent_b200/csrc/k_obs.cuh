@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   int* hist = (int*)(S + SMG_SUB);                              // MAD selection histogram
   __shared__ BlockScratch bs;
   __shared__ PlaneOut pout;
-  const int m = blockIdx.y, k = blockIdx.x, tid = threadIdx.x;
+  const int m = B.map0 + blockIdx.y, k = blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   ObsRec* O = &B.obs[(size_t)m * B.max_det + k];
   if (!F.active || k >= F.n_det) {
@@ -723,7 +723,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
 // Structural decision and observation list, in detection order (objmap.cpp:741-765 and the
 // apObsStructural branches at :576-621 with no wall segments and no text model).
 __global__ void k_obs_finalize(Batch B) {
-  const int m = blockIdx.x;
+  const int m = B.map0 + blockIdx.x;
   if (threadIdx.x != 0) return;
   const FrameDev& F = B.frames[m];
   MapRec* R = &B.maps[m];

@@ -137,7 +137,7 @@ DEV void ap_add_view_plan(const Batch& B, ObjRec& o, double kappa, double stamp,
 // record one vector job (objmap.cpp:848, :970 -> apAddView) for object `og`; tg: the frame's
 // target objects (shared memory)
 DEV void upd_job(const Batch& B, int64_t* tg_og, int* njobs, int* ntg, size_t og, int det, double k, int phys, int zero) {
-  const int m = blockIdx.x;
+  const int m = B.map0 + blockIdx.x;
   const size_t base = (size_t)m * B.max_det;
   int tg = -1;
   for (int c = 0; c < *ntg; ++c)
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
   __shared__ int fl[SMG_MAX_DET], cfl[SMG_MAX_DET];   // the free-list entries new objects pop, in order
   __shared__ int64_t tg_og[SMG_MAX_DET];           // target objects of the vector jobs
   __shared__ int n_book[3], njobs, ntg;
-  const int m = blockIdx.x, tid = threadIdx.x;
+  const int m = B.map0 + blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   MapRec* R = &B.maps[m];
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
 // parallel; each thread owns the same elements across jobs, so the jobs need no barrier.
 __global__ void __launch_bounds__(UPD_THREADS) k_update_vec(Batch B) {
   __shared__ BlockScratch bs;
-  const int c = blockIdx.x, m = blockIdx.y, tid = threadIdx.x;
+  const int c = blockIdx.x, m = B.map0 + blockIdx.y, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active || c >= B.upd_n[2 * m + 1]) return;
   const size_t base = (size_t)m * B.max_det;

@@ -60,8 +60,13 @@ struct smg_batch {
   bool ring_used[4] = {false, false, false, false};
   long long n_push = 0;
   FrameDev* h_frames = nullptr;   // current ring slot
-  cudaStream_t s_grid = nullptr;  // occupancy work runs beside the object chain
-  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  // stream groups: the maps are split into `groups` ranges, each with its own chain stream (the
+  // caller's for group 0) and occupancy side stream; host inputs arrive on s_copy
+  static constexpr int kGroupsMax = 8;
+  int groups = 1;
+  cudaStream_t s_grp[kGroupsMax] = {}, s_gridg[kGroupsMax] = {}, s_copy = nullptr;
+  cudaEvent_t ev_fork[kGroupsMax] = {}, ev_join[kGroupsMax] = {}, ev_copied[kGroupsMax] = {}, ev_gdone[kGroupsMax] = {};
+  cudaEvent_t ev_up = nullptr, ev_done = nullptr;
   bool dbg_sync = getenv("SMG_DEBUG_SYNC") != nullptr;   // synchronise + check after every launch
   long long dbg_last = 0;
   float* d_depth = nullptr;       // staging for SMG_MEM_HOST
@@ -250,9 +255,12 @@ int smg_destroy(smg_batch* b) {
   for (void* p : b->allocs) cudaFree(p);
   if (b->h_ring) cudaFreeHost(b->h_ring);
   for (auto e : b->ring_ev) if (e) cudaEventDestroy(e);
-  if (b->ev_fork) cudaEventDestroy(b->ev_fork);
-  if (b->ev_join) cudaEventDestroy(b->ev_join);
-  if (b->s_grid) cudaStreamDestroy(b->s_grid);
+  for (int g = 0; g < smg_batch::kGroupsMax; ++g) {
+    for (cudaEvent_t e : {b->ev_fork[g], b->ev_join[g], b->ev_copied[g], b->ev_gdone[g]}) if (e) cudaEventDestroy(e);
+    for (cudaStream_t q : {b->s_grp[g], b->s_gridg[g]}) if (q) cudaStreamDestroy(q);
+  }
+  for (cudaEvent_t e : {b->ev_up, b->ev_done}) if (e) cudaEventDestroy(e);
+  if (b->s_copy) cudaStreamDestroy(b->s_copy);
   delete b;
   return SMG_OK;
 }
@@ -298,7 +306,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   Batch& B = b->B;
   memset(&B, 0, sizeof(B));
   const int M = n_maps, O = max_objects, D = emb_dim;
-  B.M = M; B.O = O; B.D = D; B.topk = p->topk; B.max_det = max_det; B.W = max_w; B.H = max_h;
+  B.M = M; B.O = O; B.D = D; B.topk = p->topk; B.max_det = max_det; B.W = max_w; B.H = max_h; B.map0 = 0;
   B.p = *p;
   B.cap = 2 * p->cloud_cap;
   B.HC = pow2_at_least(2LL * B.cap);
@@ -454,9 +462,20 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   CK(cudaGetLastError());
   CK(cudaMallocHost(&b->h_ring, sizeof(FrameDev) * M * smg_batch::kRing));
   for (int r = 0; r < smg_batch::kRing; ++r) CK(cudaEventCreateWithFlags(&b->ring_ev[r], cudaEventDisableTiming));
-  CK(cudaStreamCreateWithFlags(&b->s_grid, cudaStreamNonBlocking));
-  CK(cudaEventCreateWithFlags(&b->ev_fork, cudaEventDisableTiming));
-  CK(cudaEventCreateWithFlags(&b->ev_join, cudaEventDisableTiming));
+  {
+    const char* ge = getenv("SMG_STREAM_GROUPS");   // maps per launch = M / groups
+    b->groups = std::max(1, std::min(smg_batch::kGroupsMax, ge ? atoi(ge) : (M >= 32 ? 4 : 1)));
+    for (int g = 0; g < smg_batch::kGroupsMax; ++g) {
+      if (g > 0) CK(cudaStreamCreateWithFlags(&b->s_grp[g], cudaStreamNonBlocking));
+      CK(cudaStreamCreateWithFlags(&b->s_gridg[g], cudaStreamNonBlocking));
+      for (cudaEvent_t* e : {&b->ev_fork[g], &b->ev_join[g], &b->ev_copied[g], &b->ev_gdone[g]})
+        CK(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    }
+    CK(cudaStreamCreateWithFlags(&b->s_copy, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&b->ev_up, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&b->ev_done, cudaEventDisableTiming));
+    CK(cudaEventRecord(b->ev_done, 0));
+  }
   b->last_cam_t.assign(M, -1e300);
   b->last_cam_fwd.assign(3 * (size_t)M, 0.0);
   // kernels with large dynamic shared memory
@@ -474,7 +493,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
 }
 
 __global__ void k_begin(Batch B) {
-  const int m = blockIdx.x;
+  const int m = B.map0 + blockIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   for (int k = threadIdx.x; k < B.max_det; k += blockDim.x) {
@@ -490,6 +509,76 @@ __global__ void k_begin(Batch B) {
     R->n_targets = 0;
     B.mcand_n[m] = 0;
   }
+}
+
+// The keyframe chain of one group of maps (B.map0 .. B.map0 + Mg - 1) on stream st, with the
+// occupancy kernel on the side stream sgrid (forked after k_begin, joined at the end).
+static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, cudaStream_t sgrid, cudaEvent_t efork,
+                        cudaEvent_t ejoin) {
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_begin<<<Mg, 128, 0, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({0, {e0, e1}}); } }
+  // fork: the occupancy grid (Mapper2D::keyframe) is independent of the object chain
+  CK(cudaEventRecord(efork, st));
+  CK(cudaStreamWaitEvent(sgrid, efork, 0));
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, sgrid); }
+  k_grid<<<Mg, GRID_THREADS, 0, sgrid>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(sgrid); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after k_grid: ") + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } }
+  if (b->timing) { cudaEventRecord(e1, sgrid); b->ev_used.push_back({13, {e0, e1}}); } }
+  CK(cudaEventRecord(ejoin, sgrid));
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_merge_pairs<<<dim3(MP_CTAS, Mg), 256, MP_SMEM(B.O), st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({1, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_merge_apply<<<Mg, 512, 0, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({2, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_obs<<<dim3(B.max_det, Mg), OBS_THREADS, OBS_SMEM, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({3, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_obs_finalize<<<Mg, 32, 0, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({4, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_assoc<<<dim3(B.max_det, Mg), ASSOC_THREADS, ((B.D * 4 + SP_MAX * 12 + 7) & ~7) + B.O * 8, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({5, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_update<<<Mg, UPD_THREADS, UPD_SMEM(B), st>>>(B);
+  k_update_vec<<<dim3(B.max_det, Mg), UPD_THREADS, 0, st>>>(B);   // timed together with k_update
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({6, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_absent<<<dim3(4, Mg), 256, 0, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({7, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_relink<<<Mg, 256, 3 * 8 * RELINK_STAGE + 8 * B.D * 4, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({8, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_struct<<<dim3(STRUCT_CTAS, Mg), 256, 0, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({9, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_prune<<<Mg, 256, 0, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({10, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_markview<<<Mg, 256, 0, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({11, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_cloud_add<<<dim3(WORK_SLOTS, Mg), 512, 0, st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({12, {e0, e1}}); } }
+  CK(cudaStreamWaitEvent(st, ejoin, 0));   // join
+  b->launches += 15;
+  return SMG_OK;
 }
 
 int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, void* stream) {
@@ -512,7 +601,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   if (b->ring_used[slot]) CK(cudaEventSynchronize(b->ring_ev[slot]));
   b->h_frames = b->h_ring + (size_t)slot * B.M;
   const size_t WH = (size_t)b->max_w * b->max_h;
-  const size_t esz = 4;
+  size_t emb_off = 0;   // host embeddings are staged packed, frame after frame
   for (int m = 0; m < B.M; ++m) {
     FrameDev& d = b->h_frames[m];
     memset(&d, 0, sizeof(d));
@@ -543,7 +632,8 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     } else {
       d.depth = b->d_depth + (size_t)m * WH;
       d.label = b->d_label + (size_t)m * WH;
-      d.emb = f.emb ? (const void*)(b->d_emb + (size_t)m * B.max_det * B.D * esz) : nullptr;
+      d.emb = f.emb && f.n_det > 0 ? (const void*)(b->d_emb + emb_off) : nullptr;
+      if (d.emb) emb_off += (size_t)f.n_det * B.D * (f.emb_dtype == SMG_EMB_BF16 ? 2 : 4);
     }
     // host-libm scalars (objmap.cpp:520-531, bestview.cpp:77-81, grid.cpp:202)
     const double* T = f.T_mc;
@@ -562,103 +652,66 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     d.cos_th = std::cos(f.base[2]);
     d.sin_th = std::sin(f.base[2]);
   }
-  if (where == SMG_MEM_HOST) {
-    // contiguous host inputs (map i at base + i*stride) go in one copy each
-    auto contiguous = [&](auto get, size_t stride) {
-      for (int i = 1; i < n; ++i)
-        if ((const char*)get(i) != (const char*)get(0) + i * stride) return false;
-      return true;
-    };
-    const smg_frame& f0 = frames[0];
-    const bool same_size = [&] {
-      for (int i = 1; i < n; ++i) if (frames[i].w != f0.w || frames[i].h != f0.h) return false;
-      return true;
-    }();
-    const size_t px = (size_t)f0.w * f0.h;
-    if (same_size && px == WH && contiguous([&](int i) { return (const void*)frames[i].depth; }, px * 4) &&
-        contiguous([&](int i) { return (const void*)frames[i].label; }, px * 2)) {
-      CK(cudaMemcpyAsync(b->d_depth, f0.depth, px * 4 * n, cudaMemcpyHostToDevice, st));
-      if (f0.label) CK(cudaMemcpyAsync(b->d_label, f0.label, px * 2 * n, cudaMemcpyHostToDevice, st));
-    } else {
-      for (int i = 0; i < n; ++i) {
-        const size_t pi = (size_t)frames[i].w * frames[i].h;
-        CK(cudaMemcpyAsync(b->d_depth + i * WH, frames[i].depth, pi * 4, cudaMemcpyHostToDevice, st));
-        if (frames[i].label) CK(cudaMemcpyAsync(b->d_label + i * WH, frames[i].label, pi * 2, cudaMemcpyHostToDevice, st));
-      }
-    }
-    for (int i = 0; i < n; ++i) {
-      if (!frames[i].emb || frames[i].n_det <= 0) continue;
-      const size_t eb = (size_t)frames[i].n_det * B.D * (frames[i].emb_dtype == SMG_EMB_BF16 ? 2 : 4);
-      CK(cudaMemcpyAsync(b->d_emb + (size_t)i * B.max_det * B.D * esz, frames[i].emb, eb, cudaMemcpyHostToDevice, st));
-    }
-  }
+  // Stream groups: maps [g*M/G, (g+1)*M/G) run their chain on stream g (the caller's stream
+  // for g = 0), so the groups' kernels overlap; with host inputs, group g's chain starts as soon
+  // as its own inputs have arrived on the copy stream.
+  const int G = (b->timing || b->dbg_sync) ? 1 : std::max(1, std::min(b->groups, B.M));
+  auto gbeg = [&](int g) { return (int)((long long)B.M * g / G); };
   CK(cudaMemcpyAsync(B.frames, b->h_frames, sizeof(FrameDev) * B.M, cudaMemcpyHostToDevice, st));
   CK(cudaEventRecord(b->ring_ev[slot], st));
   b->ring_used[slot] = true;
-  const int M = B.M;
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_begin<<<M, 128, 0, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({0, {e0, e1}}); } }
-  // fork: the occupancy grid (Mapper2D::keyframe) is independent of the object chain
-  CK(cudaEventRecord(b->ev_fork, st));
-  CK(cudaStreamWaitEvent(b->s_grid, b->ev_fork, 0));
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, b->s_grid); }
-  k_grid<<<M, GRID_THREADS, 0, b->s_grid>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(b->s_grid); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after k_grid: ") + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } }
-  if (b->timing) { cudaEventRecord(e1, b->s_grid); b->ev_used.push_back({13, {e0, e1}}); } }
-  CK(cudaEventRecord(b->ev_join, b->s_grid));
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_merge_pairs<<<dim3(MP_CTAS, M), 256, MP_SMEM(B.O), st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({1, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_merge_apply<<<M, 512, 0, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({2, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_obs<<<dim3(B.max_det, M), OBS_THREADS, OBS_SMEM, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({3, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_obs_finalize<<<M, 32, 0, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({4, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_assoc<<<dim3(B.max_det, M), ASSOC_THREADS, ((B.D * 4 + SP_MAX * 12 + 7) & ~7) + B.O * 8, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({5, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_update<<<M, UPD_THREADS, UPD_SMEM(B), st>>>(B);
-  k_update_vec<<<dim3(B.max_det, M), UPD_THREADS, 0, st>>>(B);   // timed together with k_update
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({6, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_absent<<<dim3(4, M), 256, 0, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({7, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_relink<<<M, 256, 3 * 8 * RELINK_STAGE + 8 * B.D * 4, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({8, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_struct<<<dim3(STRUCT_CTAS, M), 256, 0, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({9, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_prune<<<M, 256, 0, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({10, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_markview<<<M, 256, 0, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({11, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_cloud_add<<<dim3(WORK_SLOTS, M), 512, 0, st>>>(B);
-  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
-  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({12, {e0, e1}}); } }
-  CK(cudaStreamWaitEvent(st, b->ev_join, 0));   // join
-  b->launches += 15;
+  CK(cudaEventRecord(b->ev_up, st));
+  if (where == SMG_MEM_HOST) {
+    // the staging buffers are free once the previous chain is done
+    CK(cudaStreamWaitEvent(b->s_copy, b->ev_done, 0));
+    for (int g = 0; g < G; ++g) {
+      const int m0 = std::min(gbeg(g), n), m1 = std::min(gbeg(g + 1), n);
+      // depth and labels: one copy per run of maps that lie back to back in host memory
+      for (int i = m0; i < m1;) {
+        const size_t pi = (size_t)frames[i].w * frames[i].h;
+        int j = i + 1;
+        while (j < m1 && pi == WH && (size_t)frames[j].w * frames[j].h == WH &&
+               (const char*)frames[j].depth == (const char*)frames[i].depth + (j - i) * WH * 4 &&
+               (const char*)frames[j].label == (const char*)frames[i].label + (j - i) * WH * 2 && frames[i].label)
+          ++j;
+        const size_t run = j - i > 1 ? (size_t)(j - i) * WH : pi;
+        CK(cudaMemcpyAsync(b->d_depth + i * WH, frames[i].depth, run * 4, cudaMemcpyHostToDevice, b->s_copy));
+        if (frames[i].label) CK(cudaMemcpyAsync(b->d_label + i * WH, frames[i].label, run * 2, cudaMemcpyHostToDevice, b->s_copy));
+        i = j;
+      }
+      // embeddings: packed on the device; one copy per run that is packed on the host too
+      for (int i = m0; i < m1;) {
+        if (!frames[i].emb || frames[i].n_det <= 0) { ++i; continue; }
+        const char* d0 = (const char*)b->h_frames[i].emb;
+        const char* h0 = (const char*)frames[i].emb;
+        size_t bytes = 0;
+        int j = i;
+        while (j < m1 && frames[j].emb && frames[j].n_det > 0 && (const char*)frames[j].emb == h0 + bytes &&
+               (const char*)b->h_frames[j].emb == d0 + bytes) {
+          bytes += (size_t)frames[j].n_det * B.D * (frames[j].emb_dtype == SMG_EMB_BF16 ? 2 : 4);
+          ++j;
+        }
+        CK(cudaMemcpyAsync((void*)d0, h0, bytes, cudaMemcpyHostToDevice, b->s_copy));
+        i = j;
+      }
+      CK(cudaEventRecord(b->ev_copied[g], b->s_copy));
+    }
+  }
+  for (int g = 0; g < G; ++g) {
+    Batch Bg = B;
+    Bg.map0 = gbeg(g);
+    const int Mg = gbeg(g + 1) - gbeg(g);
+    cudaStream_t sg = g == 0 ? st : b->s_grp[g];
+    if (g > 0) CK(cudaStreamWaitEvent(sg, b->ev_up, 0));
+    if (where == SMG_MEM_HOST) CK(cudaStreamWaitEvent(sg, b->ev_copied[g], 0));
+    if (Mg > 0)
+      if (int r = launch_group(b, Bg, Mg, sg, b->s_gridg[g], b->ev_fork[g], b->ev_join[g])) return r;
+    if (g > 0) {
+      CK(cudaEventRecord(b->ev_gdone[g], sg));
+      CK(cudaStreamWaitEvent(st, b->ev_gdone[g], 0));
+    }
+  }
+  CK(cudaEventRecord(b->ev_done, st));
   CK(cudaGetLastError());
   return SMG_OK;
 }

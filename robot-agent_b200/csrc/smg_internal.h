@@ -213,6 +213,7 @@ typedef struct {
 typedef struct {
   // sizes
   int32_t M, O, D, topk, cap, HC, HCC, pmax, max_det, W, H;
+  int32_t map0;                         // first map of the launch (maps are split into stream groups)
   int32_t work_n;                       // points per work area
   size_t work_stride;                   // bytes per work area
   int32_t gw_grid, gh_grid, gx0, gy0;   // occupancy window
