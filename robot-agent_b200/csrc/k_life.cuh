@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
 __global__ void __launch_bounds__(256) k_prune(Batch B) {
   __shared__ int s_slot[PRUNE_MAX];
   __shared__ uint32_t s_id[PRUNE_MAX];
-  __shared__ unsigned char s_rm[PRUNE_MAX], s_dirty[PRUNE_MAX];
+  __shared__ unsigned char s_rm[PRUNE_MAX], s_dirty[PRUNE_MAX], s_fe[PRUNE_MAX];
   __shared__ BlockScratch bs;
   const int m = B.map0 + blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
@@ -426,38 +426,67 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
     s_dirty[b] = C.cver != C.version && C.n > 0;
   }
   nstruct = block_sum_i(nstruct, bs);
-  if (tid != 0) return;
-  R->st.n_obj_struct += nstruct;
+  // everything below is list-ordered compaction, done with block scans: kept objects to the
+  // list, removed ones to the free lists (in list order), then the cloud targets
+  const int nfree0 = R->n_free, ncfree0 = R->n_cfree, npts = min(R->n_pts, B.max_det);
+  __shared__ uint32_t s_pid[SMG_MAX_DET];
+  __shared__ int s_byE[SMG_MAX_DET];
+  __shared__ int pr_db[2][33];
+  for (int e = tid; e < npts; e += blockDim.x) { s_pid[e] = B.ptsl[(size_t)m * B.max_det + e].obj_id; s_byE[e] = -1; }
+  __syncthreads();
   int32_t* ord = B.order + (size_t)m * B.O;
-  int w = 0;
-  for (int b = 0; b < n; ++b) {
-    if (s_rm[b]) {
-      const ObjRec& o = B.objs[oglob(B, m, s_slot[b])];
-      if (INB(R->n_cfree, B.O, 510)) B.cfreel[(size_t)m * B.O + R->n_cfree++] = o.cloud_slot;
-      if (INB(R->n_free, B.O, 511)) B.freel[(size_t)m * B.O + R->n_free++] = s_slot[b];
-      continue;
+  int it = 0, kept = 0, rmd = 0;
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int b = c0 + tid;
+    const int rm = b < n && s_rm[b], keep = b < n && !s_rm[b];
+    int tk, tr;
+    const int pk = block_scan_db(keep, &tk, pr_db, it++);
+    const int pr = block_scan_db(rm, &tr, pr_db, it++);
+    if (keep) {
+      ord[kept + pk] = s_slot[b];
+      // first cloud list of this object (each list names one object)
+      int fe = 255;
+      for (int e = 0; e < npts; ++e)
+        if (s_pid[e] == s_id[b]) { fe = e; break; }
+      s_fe[b] = (unsigned char)fe;
+      if (fe < 255) s_byE[fe] = b;
     }
-    s_slot[w] = s_slot[b];
-    s_id[w] = s_id[b];
-    s_dirty[w] = s_dirty[b];
-    ord[w] = s_slot[b];
-    ++w;
+    if (rm) {
+      const ObjRec& o = B.objs[oglob(B, m, s_slot[b])];
+      if (INB(ncfree0 + rmd + pr, B.O, 510)) B.cfreel[(size_t)m * B.O + ncfree0 + rmd + pr] = o.cloud_slot;
+      if (INB(nfree0 + rmd + pr, B.O, 511)) B.freel[(size_t)m * B.O + nfree0 + rmd + pr] = s_slot[b];
+    }
+    kept += tk;
+    rmd += tr;
   }
-  R->n_obj = w;
-  int nt = 0;
-  unsigned char* taken = s_rm;   // reuse as "already a target" flags
-  for (int b = 0; b < w; ++b) taken[b] = 0;
-  for (int e = 0; e < R->n_pts; ++e) {
-    const uint32_t id = B.ptsl[(size_t)m * B.max_det + e].obj_id;
-    for (int b = 0; b < w; ++b)
-      if (s_id[b] == id) {
-        if (!taken[b]) { taken[b] = 1; B.tgt_slot[(size_t)m * B.O + nt++] = s_slot[b]; }
-        break;
-      }
+  __syncthreads();
+  // targets: the objects of the cloud lists in list order, then the kept objects whose contact
+  // index is stale, in object-list order
+  int32_t* TG = B.tgt_slot + (size_t)m * B.O;
+  __shared__ int s_na;
+  if (tid == 0) {
+    int na = 0;
+    for (int e = 0; e < npts; ++e)
+      if (s_byE[e] >= 0) TG[na++] = s_slot[s_byE[e]];
+    s_na = na;
   }
-  for (int b = 0; b < w; ++b)
-    if (s_dirty[b] && !taken[b]) { taken[b] = 1; B.tgt_slot[(size_t)m * B.O + nt++] = s_slot[b]; }
-  R->n_targets = nt;
+  __syncthreads();
+  int nt = s_na;
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int b = c0 + tid;
+    const int f = b < n && !s_rm[b] && s_dirty[b] && s_fe[b] == 255;
+    int tot;
+    const int pos = block_scan_db(f, &tot, pr_db, it++);
+    if (f && INB(nt + pos, B.O, 512)) TG[nt + pos] = s_slot[b];
+    nt += tot;
+  }
+  if (tid == 0) {
+    R->st.n_obj_struct += nstruct;
+    R->n_cfree = ncfree0 + rmd <= B.O ? ncfree0 + rmd : B.O;
+    R->n_free = nfree0 + rmd <= B.O ? nfree0 + rmd : B.O;
+    R->n_obj = kept;
+    R->n_targets = nt;
+  }
 }
 
 // markView (objmap.cpp:219-245): sparse depth samples, horizontal camera->point segments, first

@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
 __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
   __shared__ BlockScratch bs;
   __shared__ int hist[SEL_HIST(1)];
-  __shared__ int sh_go, sh_ka, sh_kb, nused;
+  __shared__ int sh_go, sh_ka, sh_kb, sh_pkb, nused, sh_pa, sh_pb;
   __shared__ uint32_t used[2 * 256];
   const int m = B.map0 + blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
@@ -162,12 +162,21 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
   float* xyz = B.cxyz + (size_t)m * B.max_det * 3 * B.pmax;
   uint8_t* rgb = (uint8_t*)(B.cpx + (size_t)m * B.max_det * 2 * B.pmax);
   for (int c = 0; c < nc; ++c) {
+    // list positions of the pair's objects (findPos), searched by the whole block
+    const uint32_t ia = cab[2 * c], ib = cab[2 * c + 1];
+    if (tid == 0) { sh_pa = 0x7fffffff; sh_pb = 0x7fffffff; }
+    __syncthreads();
+    for (int i = tid; i < R->n_obj; i += blockDim.x) {
+      const uint32_t id = obj_at(B, m, i).id;
+      if (id == ia) atomicMin(&sh_pa, i);
+      if (id == ib) atomicMin(&sh_pb, i);
+    }
+    __syncthreads();
     if (tid == 0) {
       sh_go = 0;
-      const uint32_t ia = cab[2 * c], ib = cab[2 * c + 1];
       bool u = false;
       for (int q = 0; q < nused; ++q) u = u || used[q] == ia || used[q] == ib;
-      const int pa = find_pos(B, m, ia), pb = find_pos(B, m, ib);
+      const int pa = sh_pa == 0x7fffffff ? -1 : sh_pa, pb = sh_pb == 0x7fffffff ? -1 : sh_pb;
       if (!u && pa >= 0 && pb >= 0 && nused + 2 <= 2 * 256) {
         int ka = pa, kb = pb;
         const ObjRec& A = obj_at(B, m, pa);
@@ -177,6 +186,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
         used[nused++] = ib;
         sh_ka = slot_at(B, m, ka);
         sh_kb = slot_at(B, m, kb);
+        sh_pkb = kb;
         sh_go = 1;
         // da::absorb scalar part (merge.cpp:33-62)
         ObjRec& a = B.objs[oglob(B, m, sh_ka)];
@@ -292,7 +302,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
       a.wall_like = a.wall_like && b.wall_like;
       a.confirmed = a.confirmed || b.confirmed;
       ++R->st.n_merge;
-      { const int pe = find_pos(B, m, b.id); if (INB(pe, R->n_obj, 604)) erase_pos(B, m, pe, false); }
+      { const int pe = sh_pkb; if (INB(pe, R->n_obj, 604)) erase_pos(B, m, pe, false); }   // b's position (findPos)
       push_event(B, m, t, a, 7, (1u << 24) | (uint32_t)R->n_evn++);
     }
     __syncthreads();

@@ -162,6 +162,8 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   const uint64_t rs0 = seed ^ ((uint64_t)n << 32);
   const int ndraw = 3 * iters + 64 < RANSAC_DRAWS ? 3 * iters + 64 : RANSAC_DRAWS;
   int* h_qr = h_draw + RANSAC_DRAWS;
+  __shared__ int sh_fb;   // first iteration whose triple is not the next three draws
+  if (tid == 0) sh_fb = iters;
   for (int k = tid; k < ndraw; k += blockDim.x) {
     uint64_t s = rs0 + (uint64_t)k * 0x9E3779B97F4A7C15ull;
     h_draw[k] = (int)(splitmix(s) % (uint64_t)n);
@@ -169,7 +171,8 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   __syncthreads();
   // For every start position p: the positions q, r of the second and third index the
   // reference's rejection loops take from there (packed q | r << 16; -1 past the precomputed
-  // draws).  The walk over the iterations is then one dependent load per iteration.
+  // draws).  Iterations before the first rejection are filled in parallel; from there the
+  // walk is one dependent load per iteration.
   for (int p = tid; p < ndraw; p += blockDim.x) {
     const int i0 = h_draw[p];
     int q = p + 1;
@@ -177,10 +180,16 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     int r = q + 1;
     while (r < ndraw && (h_draw[r] == i0 || h_draw[r] == h_draw[q])) ++r;
     h_qr[p] = r < ndraw ? q | (r << 16) : -1;
+    if (p % 3 == 0 && p / 3 < iters && !(q == p + 1 && r == p + 2 && r < ndraw)) atomicMin(&sh_fb, p / 3);
   }
   __syncthreads();
+  // until the first rejection, iteration it draws positions 3it, 3it+1, 3it+2
+  const int fb = sh_fb;
+  for (int it = tid; it < fb; it += blockDim.x) {
+    h_id[it][0] = h_draw[3 * it]; h_id[it][1] = h_draw[3 * it + 1]; h_id[it][2] = h_draw[3 * it + 2];
+  }
   if (tid == 0) {
-    int pos = 0, it = 0;
+    int pos = 3 * fb, it = fb;
     for (; it < iters && pos < ndraw; ++it) {
       const int e = h_qr[pos];
       if (e < 0) break;
