@@ -177,20 +177,33 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
   MapRec* R = &B.maps[m];
   const smg_params& P = B.p;
   const double t = F.stamp;
-  if (tid == 0) {
-    // cloud candidates in observation order (objmap.cpp:1010-1019)
+  if (wid == 0) {
+    // cloud candidates in observation order (objmap.cpp:1010-1019): warp 0 loads 32
+    // observations at a time and places the kept ones by a ballot prefix
+    const int nobs = min(R->n_obs, B.max_det);
     int e = 0;
-    for (int a = 0; a < R->n_obs; ++a) {
-      const int det = B.obs_list[(size_t)m * B.max_det + a];
-      const uint32_t id = B.assoc[(size_t)m * B.max_det + det].obj_id;
-      const int nc = B.obs[(size_t)m * B.max_det + det].nc;
-      if (!id || nc <= 0) continue;
-      PtsRec& pr = B.ptsl[(size_t)m * B.max_det + e++];
-      pr.obj_id = id;
-      pr.det = det;
-      pr.n = nc;
+    for (int a0 = 0; a0 < nobs; a0 += 32) {
+      const int a = a0 + lane;
+      int det = 0, nc = 0;
+      uint32_t id = 0;
+      if (a < nobs) {
+        det = B.obs_list[(size_t)m * B.max_det + a];
+        if (INB(det, B.max_det, 513)) {
+          id = B.assoc[(size_t)m * B.max_det + det].obj_id;
+          nc = B.obs[(size_t)m * B.max_det + det].nc;
+        }
+      }
+      const bool keep = a < nobs && id && nc > 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, keep);
+      if (keep) {
+        PtsRec& pr = B.ptsl[(size_t)m * B.max_det + e + __popc(bal & ((1u << lane) - 1u))];
+        pr.obj_id = id;
+        pr.det = det;
+        pr.n = nc;
+      }
+      e += __popc(bal);
     }
-    R->n_pts = e;
+    if (lane == 0) R->n_pts = e;
   }
   // stage the scalars of the relink tests (objmap.cpp:323-346) in shared memory
   const int nobj = R->n_obj;
@@ -491,8 +504,10 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
 
 // markView (objmap.cpp:219-245): sparse depth samples, horizontal camera->point segments, first
 // time each 2D cell was seen per range band.  Fresh cells are pre-filled with "never".
+#define MV_CTAS 24    // k_markview CTAs per map
+#define MV_SPLIT 8    // threads per sampled pixel: each marches every MV_SPLIT-th step of its ray
 __global__ void __launch_bounds__(256) k_markview(Batch B) {
-  const int m = B.map0 + blockIdx.x;
+  const int m = B.map0 + blockIdx.y;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const smg_params& P = B.p;
@@ -501,7 +516,10 @@ __global__ void __launch_bounds__(256) k_markview(Batch B) {
   const int stp = max(1, F.w / 32);
   const int nu = (F.w - stp / 2 + stp - 1) / stp, nv = (F.h - stp / 2 + stp - 1) / stp;
   int64_t* K = B.vkey + (size_t)m * B.view_slots;
-  for (int s = threadIdx.x; s < nu * nv; s += blockDim.x) {
+  // the view cells a ray covers and their first stamps do not depend on the order of the steps
+  // (every write of the frame stores the same stamp), so the steps are split across threads
+  for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < nu * nv * MV_SPLIT; g += gridDim.x * blockDim.x) {
+    const int s = g / MV_SPLIT, j = g - s * MV_SPLIT;
     const int u = stp / 2 + (s % nu) * stp, v = stp / 2 + (s / nu) * stp;
     const float z = F.depth[(size_t)v * F.w + u];
     if (!(z > P.zmin && z < P.zmax)) continue;
@@ -513,7 +531,7 @@ __global__ void __launch_bounds__(256) k_markview(Batch B) {
     const double L = sqrt(dx * dx + dy * dy), Lm = smin(L, (double)SMG_VIEW_BANDS);
     if (L < 1e-6) continue;
     const int ns = (int)ceil(Lm / (0.5 * cell));
-    for (int q = 0; q <= ns; ++q) {
+    for (int q = j; q <= ns; q += MV_SPLIT) {
       const double r = Lm * q / (double)max(1, ns);
       const int64_t key = view_cell_key(T[3] + r / L * dx, T[7] + r / L * dy, cell);
       uint32_t h = hmix((uint64_t)key) & (uint32_t)(B.view_slots - 1);

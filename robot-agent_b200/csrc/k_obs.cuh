@@ -733,51 +733,76 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
 // apObsStructural branches at :576-621 with no wall segments and no text model).
 __global__ void k_obs_finalize(Batch B) {
   const int m = B.map0 + blockIdx.x;
-  if (threadIdx.x != 0) return;
   const FrameDev& F = B.frames[m];
-  MapRec* R = &B.maps[m];
   if (!F.active) return;
+  // the fields the decision reads, staged by the warp; the walk then waits on no global load
+  struct Fin {
+    int valid, stage, nc, pl_ok;
+    double inl, thick, nz, zmed, zhi, zlo, hspan;
+  };
+  __shared__ Fin fs[SMG_MAX_DET];
+  const int nd = min(F.n_det, B.max_det);
+  for (int k = threadIdx.x; k < nd; k += blockDim.x) {
+    const ObsRec* O = &B.obs[(size_t)m * B.max_det + k];
+    Fin f;
+    f.valid = O->valid; f.stage = O->stage; f.nc = O->nc; f.pl_ok = O->pl_ok;
+    f.inl = O->pl_inl; f.thick = O->pl_thick; f.nz = fabs(O->pl_n[2]); f.zmed = O->pl_zmed;
+    f.zhi = O->pl_zhi; f.zlo = O->pl_zlo; f.hspan = O->pl_hspan;
+    fs[k] = f;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  MapRec* R = &B.maps[m];
   const smg_params& P = B.p;
+  long long st_obs = 0, st_floor = 0, st_ceil = 0, st_wall_tall = 0;
+  int n_ceil = R->n_ceil;
+  double ceil_est = R->ceil_est;
   int n = 0;
-  for (int k = 0; k < F.n_det; ++k) {
-    ObsRec* O = &B.obs[(size_t)m * B.max_det + k];
-    if (!O->valid) {
-      if (O->stage == 3) ++R->st.n_floor;
+  for (int k = 0; k < nd; ++k) {
+    const Fin& O = fs[k];
+    if (!O.valid) {
+      if (O.stage == 3) ++st_floor;
       continue;
     }
-    ++R->st.n_obs;
+    ++st_obs;
     bool drop = false;
-    if (O->nc >= 8 && O->pl_ok && !(O->pl_inl < P.plane_inl) && !(O->pl_thick > P.plane_thick)) {
-      const double nz = fabs(O->pl_n[2]);
+    if (O.nc >= 8 && O.pl_ok && !(O.inl < P.plane_inl) && !(O.thick > P.plane_thick)) {
+      const double nz = O.nz;
       if (nz > P.horiz) {
-        if (O->pl_zmed > 1.8) {
-          if (R->n_ceil >= SMG_CEIL_OBS) {
-            for (int i = 1; i < R->n_ceil; ++i) R->ceil_obs[i - 1] = R->ceil_obs[i];
-            --R->n_ceil;
+        if (O.zmed > 1.8) {
+          if (n_ceil >= SMG_CEIL_OBS) {
+            for (int i = 1; i < n_ceil; ++i) R->ceil_obs[i - 1] = R->ceil_obs[i];
+            --n_ceil;
           }
-          R->ceil_obs[R->n_ceil++] = O->pl_zmed;
-          if (R->n_ceil >= 20) {   // nth_element value at size/2
-            const int kk = R->n_ceil / 2;
+          R->ceil_obs[n_ceil++] = O.zmed;
+          if (n_ceil >= 20) {   // nth_element value at size/2
+            const int kk = n_ceil / 2;
             double val = 0;
-            for (int i = 0; i < R->n_ceil; ++i) {
+            for (int i = 0; i < n_ceil; ++i) {
               int less = 0, eq = 0;
-              for (int j = 0; j < R->n_ceil; ++j) { less += R->ceil_obs[j] < R->ceil_obs[i]; eq += R->ceil_obs[j] == R->ceil_obs[i]; }
+              for (int j = 0; j < n_ceil; ++j) { less += R->ceil_obs[j] < R->ceil_obs[i]; eq += R->ceil_obs[j] == R->ceil_obs[i]; }
               if (less <= kk && kk < less + eq) { val = R->ceil_obs[i]; break; }
             }
-            R->ceil_est = val;
+            ceil_est = val;
           }
         }
-        const double cz = R->ceil_est > 0 ? smin(P.ceil_z, R->ceil_est - P.ceil_band) : P.ceil_z;
-        if (O->pl_zmed > cz) { ++R->st.n_ceil; drop = true; }
-        else if (O->pl_zhi < P.floor_z) { ++R->st.n_floor; drop = true; }
+        const double cz = ceil_est > 0 ? smin(P.ceil_z, ceil_est - P.ceil_band) : P.ceil_z;
+        if (O.zmed > cz) { ++st_ceil; drop = true; }
+        else if (O.zhi < P.floor_z) { ++st_floor; drop = true; }
       } else if (!(nz > P.wall_vert)) {
-        const double cz = R->ceil_est > 0 ? R->ceil_est : P.ceil_z + 0.4;
-        const bool tall = O->pl_zhi - O->pl_zlo >= P.tall_h || (O->pl_zlo <= P.tall_floor && O->pl_zhi >= cz - P.tall_ceil);
-        const bool wide = O->pl_hspan >= P.tall_w_any;   // structure probability -1 < tall_ps
-        if (tall && wide) { ++R->st.n_wall_tall; drop = true; }
+        const double cz = ceil_est > 0 ? ceil_est : P.ceil_z + 0.4;
+        const bool tall = O.zhi - O.zlo >= P.tall_h || (O.zlo <= P.tall_floor && O.zhi >= cz - P.tall_ceil);
+        const bool wide = O.hspan >= P.tall_w_any;   // structure probability -1 < tall_ps
+        if (tall && wide) { ++st_wall_tall; drop = true; }
       }
     }
     if (!drop) B.obs_list[(size_t)m * B.max_det + n++] = k;
   }
+  R->st.n_obs += st_obs;
+  R->st.n_floor += st_floor;
+  R->st.n_ceil += st_ceil;
+  R->st.n_wall_tall += st_wall_tall;
+  R->n_ceil = n_ceil;
+  R->ceil_est = ceil_est;
   R->n_obs = n;
 }
