@@ -45,8 +45,10 @@ DEV int voxel_lookup(const Batch& B, size_t cs, uint32_t gen, uint64_t key) {
   const uint32_t* I = B.chidx + cs * B.HC;
   uint32_t h = hmix(key) & (uint32_t)(B.HC - 1);
   for (int probe = 0; probe < B.HC; ++probe) {
-    if (G[h] != gen) return -1;
-    if (K[h] == key) return (int)I[h];
+    const uint32_t g = G[h], ix = I[h];   // the slot's three words in one round trip
+    const uint64_t k = K[h];
+    if (g != gen) return -1;
+    if (k == key) return (int)ix;
     h = (h + 1) & (uint32_t)(B.HC - 1);
   }
   return -1;
