@@ -2,9 +2,12 @@
 //
 // The reference's update is a sequence over observations whose later steps depend on the
 // earlier ones (fragments fuse into the first, largest one; new objects are appended mid-loop
-// and can capture later fragments).  k_update keeps that order: one CTA per map, thread 0 walks
-// the observations and takes every scalar decision, including the scalar half of apAddView
-// (tempering, camera ring, view list), and records each embedding's D-length work as a job.
+// and can capture later fragments).  k_update keeps that order where it matters: one CTA per
+// map; thread 0 walks the observations for the decisions that cross objects (actions, slots and
+// ids, frame grouping, job places, event numbers), and each staged object then applies its own
+// observations in order on its own thread (the scalar half of apAddView -- tempering, camera
+// ring, view list -- and the Kalman/tracking/state update), recording each embedding's D-length
+// work as a job.
 // k_update_vec then runs one CTA per target object and applies its jobs in observation order
 // (r_frag += k z in fp32, the fp16 view copy, |r_frag|^2 and mu); the objects are independent.
 // The frame-grouping dot products were computed by k_assoc.
@@ -134,28 +137,6 @@ DEV void ap_add_view_plan(const Batch& B, ObjRec& o, double kappa, double stamp,
   *phys_out = f;
 }
 
-// record one vector job (objmap.cpp:848, :970 -> apAddView) for object `og`; tg: the frame's
-// target objects (shared memory)
-DEV void upd_job(const Batch& B, int64_t* tg_og, int* njobs, int* ntg, size_t og, int det, double k, int phys, int zero) {
-  const int m = B.map0 + blockIdx.x;
-  const size_t base = (size_t)m * B.max_det;
-  int tg = -1;
-  for (int c = 0; c < *ntg; ++c)
-    if (tg_og[c] == (int64_t)og) { tg = c; break; }
-  if (tg < 0) {
-    if (!INB(*ntg, B.max_det, 304)) return;
-    tg = (*ntg)++;
-    tg_og[tg] = (int64_t)og;
-  }
-  if (!INB(*njobs, B.max_det, 305)) return;
-  UpdJob& j = B.upd_job[base + (*njobs)++];
-  j.tg = tg;
-  j.det = det;
-  j.phys = phys;
-  j.zero = zero;
-  j.k = k;
-}
-
 // push_event with the map's event count held by the caller (ev_base at entry, *evl added since)
 DEV void push_event_l(const Batch& B, int map, double t, const ObjRec& o, int kind, uint32_t key, int ev_base, int* evl) {
   const int e = ev_base + (*evl)++;
@@ -258,7 +239,16 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
       o.sec = 1;
     }
   }
-  // update loop (objmap.cpp:837-997)
+  // update loop (objmap.cpp:837-997), in three steps.  P1 (thread 0, observation order): the
+  // association record, the action (update a staged object or create one), slot and id
+  // allocation, the frame grouping of later fragments and the vector jobs' places.  P2 (one
+  // thread per staged record, its observations in order): the object's own update -- the
+  // scalar half of apAddView, Kalman, tracking, state -- which reads and writes no other
+  // object.  P3 (thread 0): the events, numbered in observation order.
+  __shared__ signed char s_act[SMG_MAX_DET], s_evf[SMG_MAX_DET];
+  __shared__ int s_job[SMG_MAX_DET], s_cs[SMG_MAX_DET];
+  __shared__ uint32_t s_newid[SMG_MAX_DET];
+  const size_t jbase = (size_t)m * B.max_det;
   if (tid == 0) {
     for (int a = 0; a < nobs; ++a) {
       ObsRec& o = OB[OL[a]];
@@ -266,17 +256,19 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
       as.n_valid = o.n;
       as.area_px = (float)o.n * o.sk * o.sk;
       as.depth_med = (float)o.zmed;
-      int act = 0, r = -1, cs = -1;
+      int act = 0, r = -1;
+      s_evf[a] = 0;
+      s_job[a] = -1;
       if (o.obs_to >= 0 && INB(o.obs_to, n_obj, 302) && obs_rec[a] >= 0) {
         act = 1;
         r = obs_rec[a];
-        as.obj_id = REC[r].id;
+        as.obj_id = s_act[r] == 2 && r < a ? s_newid[r] : REC[r].id;   // a grouped fragment's object is built in P2
       } else if (o.obs_to == -1) {   // ObjectMap slot allocation (new object)
         if (n_free <= 0 || n_cfree <= 0 || n_obj >= B.O || !INB(n_pop, nobs, 303) || fl[n_pop] < 0 || cfl[n_pop] < 0) {
           set_err(R, SMG_E_CAP_OBJ);
         } else {
           const int slot = fl[n_pop];
-          cs = cfl[n_pop];
+          s_cs[a] = cfl[n_pop];
           ++n_pop;
           --n_free;
           --n_cfree;
@@ -284,107 +276,64 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
           act = 2;
           r = a;   // an unmatched observation's own record is free
           rec_slot[r] = slot;
+          obs_rec[a] = r;
+          s_newid[a] = next_id++;
+          as.obj_id = s_newid[a];
+          B.touched[(size_t)m * B.O + n_obj - 1] = 1;
+          B.obj_hit[(size_t)m * B.O + n_obj - 1] = 1;
+          ++n_new;
+          // frame grouping (objmap.cpp:980-995): later unmatched fragments touching this one, with
+          // the dot products computed by k_assoc
+          if (P.frame_group) {
+            for (int b2 = a + 1; b2 < nobs; ++b2) {
+              ObsRec& q = OB[OL[b2]];
+              if (q.obs_to != -1 || !has_z) continue;
+              double g2 = 0;
+              for (int k = 0; k < 3; ++k) {
+                const double g = smax3(0.0, q.lo[k] - o.hi[k], o.lo[k] - q.hi[k]);
+                g2 += g * g;
+              }
+              if (g2 > 0.02 * 0.02) continue;
+              double f[7] = {0, 0, 0, 0, 0, 0, 0};
+              pair_geo(q.lo, q.hi, q.pos, o.lo, o.hi, o.pos, GD[(size_t)a * B.max_det + b2], P.cos0, f);
+              f[0] = 1.0;
+              if (1.0 / (1.0 + exp(-same_logit(P.w, f))) >= P.same_p) { q.obs_to = n_obj - 1; obs_rec[b2] = r; }
+            }
+          }
         }
       }
-      const size_t og = act ? oglob(B, m, rec_slot[r]) : 0;
-      if (act == 1) {
-        ObjRec& mo = REC[r];
-        if (has_z) {
-          double k;
-          int phys;
-          ap_add_view_plan(B, mo, o.kappa, F.stamp, cam6, &k, &phys);
-          upd_job(B, tg_og, &njobs, &ntg, og, o.det, k, phys, 0);
+      s_act[a] = (signed char)act;
+      // the vector job's place (objmap.cpp:848, :970 -> apAddView): jobs in observation order,
+      // targets numbered by first appearance; k and the view slot come in P2
+      if (act && has_z) {
+        const int64_t og = (int64_t)oglob(B, m, rec_slot[r]);
+        int tg = -1;
+        for (int c = 0; c < ntg; ++c)
+          if (tg_og[c] == og) { tg = c; break; }
+        if (tg < 0 && INB(ntg, B.max_det, 304)) { tg = ntg++; tg_og[tg] = og; }
+        if (tg >= 0 && INB(njobs, B.max_det, 305)) {
+          UpdJob& j = B.upd_job[jbase + njobs];
+          j.tg = tg;
+          j.det = o.det;
+          j.zero = act == 2;
+          s_job[a] = njobs++;
         }
-        ++mo.n_ap_obs;
-        mo.wall_like = 2 * mo.n_wall_obs >= mo.n_ap_obs;
-        if (!o.sec) {
-          const double dt_seen = F.stamp - mo.last_seen;
-          if (mo.last_kf != F.stamp) ++mo.n_obs;
-          mo.last_kf = F.stamp;
-          const bool big = smax(smax(mo.hi[0] - mo.lo[0], mo.hi[1] - mo.lo[1]), smax(o.ext[0], o.ext[1])) > P.big;
-          bool snap = false;
-          if (P.move_n > 0 && mo.trk_t > 0 && !o.trunc && F.cam_steady) {
-            const double dt = F.stamp - mo.trk_t;
-            const double sx = o.pos[0] - mo.trk_pos[0], sy = o.pos[1] - mo.trk_pos[1];
-            const double sp = dt > 1e-6 && dt <= 0.6 ? sqrt(sx * sx + sy * sy) / dt : 0.0;
-            const bool same_dir = sx * mo.trk_step[0] + sy * mo.trk_step[1] > 0;
-            mo.mv_cnt = sp > P.move_v && (same_dir || mo.mv_cnt == 0) ? mo.mv_cnt + 1 : 0;
-            mo.trk_step[0] = sx;
-            mo.trk_step[1] = sy;
-            const double rx = o.pos[0] - mo.pos[0], ry = o.pos[1] - mo.pos[1];
-            const double away = sqrt(rx * rx + ry * ry);
-            const bool moving = F.stamp - mo.moving_t < 1.0;
-            const bool left = away > smax(P.move_min_d, 0.5 * smax(o.ext[0], o.ext[1])) &&
-                              box_overlap(o.lo, o.hi, mo.lo, mo.hi, P.merge_min_ext) < 0.1;
-            if (mo.mv_cnt >= P.move_n && (moving || left)) {
-              if (!moving) mo.move_from_t = F.stamp;
-              mo.moving_t = F.stamp;
-              snap = true;
-            } else if (moving && sp > 0.5 * P.move_v) {
-              snap = true;
-              mo.moving_t = F.stamp;
-            }
-          }
-          if (!o.trunc) {
-            for (int k = 0; k < 3; ++k) mo.trk_pos[k] = o.pos[k];
-            mo.trk_t = F.stamp;
-          }
-          if (snap) {
-            double d3[3];
-            for (int k = 0; k < 3; ++k) {
-              d3[k] = o.pos[k] - mo.pos[k];
-              mo.pos[k] = o.pos[k]; mo.ext[k] = o.ext[k]; mo.lo[k] = o.lo[k]; mo.hi[k] = o.hi[k];
-            }
-            CloudRec& C = B.clouds[cslot_glob(B, m, mo)];
-            if (C.n > 0 && !(d3[0] == 0 && d3[1] == 0 && d3[2] == 0)) {   // ObjCloud::translate (cloud.cpp:79-84)
-              for (int k = 0; k < 3; ++k) C.org[k] += d3[k];
-              ++C.version;
-              C.stamp = F.stamp;
-            }
-            if (dist3(mo.pos, mo.first_pos) > P.moved_d) mo.moved = 1;
-            if (mo.moved && mo.state == 0) mo.state = 2;
-          }
-          const bool fresh = mo.first_seen == F.stamp;
-          for (int k = 0; k < 3 && !snap; ++k) {
-            if (fresh) {
-              mo.lo[k] = smin(mo.lo[k], o.lo[k]);
-              mo.hi[k] = smax(mo.hi[k], o.hi[k]);
-              mo.pos[k] = 0.5 * (mo.lo[k] + mo.hi[k]);
-              mo.ext[k] = mo.hi[k] - mo.lo[k];
-              continue;
-            }
-            if (big) {
-              const double lo = smax(smin(mo.lo[k], o.lo[k]), mo.lo[k] - P.grow_max);
-              const double hi = smin(smax(mo.hi[k], o.hi[k]), mo.hi[k] + P.grow_max);
-              if (hi - lo <= P.max_ext) { mo.lo[k] = lo; mo.hi[k] = hi; }
-              mo.pos[k] = 0.5 * (mo.lo[k] + mo.hi[k]);
-              mo.ext[k] = mo.hi[k] - mo.lo[k];
-            } else {
-              const double K = kalman_gain(mo.P[k], P.ap_q_pos, dt_seen, kalman_R(P.ap_r0, P.ap_r1, o.zmed, o.trunc, o.ext[k]));
-              mo.pos[k] += K * (o.pos[k] - mo.pos[k]);
-              mo.lo[k] += K * (o.lo[k] - mo.lo[k]);
-              mo.hi[k] += K * (o.hi[k] - mo.hi[k]);
-              mo.ext[k] = mo.hi[k] - mo.lo[k];
-            }
-            if (big) kalman_big(mo.P[k], P.ap_q_pos, dt_seen, P.ap_r0 + P.ap_r1 * o.zmed, mo.ext[k]);
-          }
-          mo.score = (mo.score < o.score) ? o.score : mo.score;
-          mo.max_det_z = smax(mo.max_det_z, o.zmed);
-          mo.last_seen = F.stamp;
-          mo.misses = 0;
-          if (mo.state == 1) {
-            mo.state = mo.moved ? 2 : 0;
-            push_event_l(B, m, F.stamp, mo, 6, (2u << 24) | (uint32_t)evn++, ev_base, &evl);
-          }
-          if (!mo.confirmed && (int)mo.n_obs >= P.confirm) {
-            mo.confirmed = 1;
-            push_event_l(B, m, F.stamp, mo, 1, (2u << 24) | (uint32_t)evn++, ev_base, &evl);
-          }
-        }
-      } else if (act == 2) {   // new candidate (objmap.cpp:951-978)
-        ObjRec& mo = REC[r];
+      }
+    }
+  }
+  __syncthreads();
+  // P2: every staged record walks its own observations in order, one record per warp (lane 0):
+  // the records' paths differ, so records sharing a warp would run one after the other
+  for (int r = tid >> 5; (tid & 31) == 0 && r < nobs; r += blockDim.x >> 5) {
+    if (rec_slot[r] < 0) continue;
+    ObjRec& mo = REC[r];
+    for (int a = 0; a < nobs; ++a) {
+      const int act = s_act[a];
+      if (!act || obs_rec[a] != r) continue;
+      const ObsRec& o = OB[OL[a]];
+      if (act == 2) {   // new candidate (objmap.cpp:951-978)
         memset(&mo, 0, sizeof(ObjRec));
-        mo.id = next_id++;
+        mo.id = s_newid[a];
         mo.cls = o.cls;
         for (int k = 0; k < 3; ++k) { mo.pos[k] = mo.first_pos[k] = o.pos[k]; mo.ext[k] = o.ext[k]; mo.lo[k] = o.lo[k]; mo.hi[k] = o.hi[k]; }
         mo.n_obs = 1;
@@ -399,13 +348,12 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
           mo.appeared = first_view(B, m, o.pos[0], o.pos[1], sqrt(hx * hx + hy * hy) + P.view_cell) < F.stamp - P.link_view_gap_s;
         }
         mo.confirmed = P.confirm <= 1;
-        B.assoc[(size_t)m * B.max_det + o.det].obj_id = mo.id;
-        mo.cloud_slot = cs;
+        mo.cloud_slot = s_cs[a];
         mo.need_whole = 1;
         mo.geo_ver = 0xffffffffu;
         const double sd = P.ap_r0 + P.ap_r1 * o.zmed;
         for (int k = 0; k < 3; ++k) mo.P[k] = sd * sd + (o.trunc ? 0.25 * o.ext[k] * o.ext[k] : 0.0);
-        CloudRec& C = B.clouds[(size_t)m * B.O + cs];
+        CloudRec& C = B.clouds[(size_t)m * B.O + s_cs[a]];
         C.has_org = 0;
         C.n = 0;
         C.version = 0;
@@ -415,38 +363,123 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
         ++C.cgen;
         ++C.vgen;
         C.cver = 0xffffffffu;
-        B.touched[(size_t)m * B.O + n_obj - 1] = 1;
-        B.obj_hit[(size_t)m * B.O + n_obj - 1] = 1;
-        if (has_z) {   // a recycled slot starts from an empty r_frag (objprob.cpp:329 assigns zeros)
-          double k;
-          int phys;
-          ap_add_view_plan(B, mo, o.kappa, F.stamp, cam6, &k, &phys);
-          upd_job(B, tg_og, &njobs, &ntg, og, o.det, k, phys, 1);
-        }
         mo.n_ap_obs = 1;
         mo.n_wall_obs = 0;
         mo.n_struct_look = 0;
         mo.wall_like = 0;
-        ++n_new;
-        // frame grouping (objmap.cpp:980-995): later unmatched fragments touching this one, with
-        // the dot products computed by k_assoc
-        if (P.frame_group) {
-          for (int b2 = a + 1; b2 < nobs; ++b2) {
-            ObsRec& q = OB[OL[b2]];
-            if (q.obs_to != -1 || !has_z) continue;
-            double g2 = 0;
-            for (int k = 0; k < 3; ++k) {
-              const double g = smax3(0.0, q.lo[k] - o.hi[k], o.lo[k] - q.hi[k]);
-              g2 += g * g;
-            }
-            if (g2 > 0.02 * 0.02) continue;
-            double f[7] = {0, 0, 0, 0, 0, 0, 0};
-            pair_geo(q.lo, q.hi, q.pos, o.lo, o.hi, o.pos, GD[(size_t)a * B.max_det + b2], P.cos0, f);
-            f[0] = 1.0;
-            if (1.0 / (1.0 + exp(-same_logit(P.w, f))) >= P.same_p) { q.obs_to = n_obj - 1; obs_rec[b2] = r; }
-          }
+      }
+      if (has_z) {   // a recycled slot starts from an empty r_frag (objprob.cpp:329 assigns zeros)
+        double k;
+        int phys;
+        ap_add_view_plan(B, mo, o.kappa, F.stamp, cam6, &k, &phys);
+        if (s_job[a] >= 0) {
+          UpdJob& j = B.upd_job[jbase + s_job[a]];
+          j.k = k;
+          j.phys = phys;
         }
+      }
+      if (act == 1) {
+          ++mo.n_ap_obs;
+          mo.wall_like = 2 * mo.n_wall_obs >= mo.n_ap_obs;
+          if (!o.sec) {
+            const double dt_seen = F.stamp - mo.last_seen;
+            if (mo.last_kf != F.stamp) ++mo.n_obs;
+            mo.last_kf = F.stamp;
+            const bool big = smax(smax(mo.hi[0] - mo.lo[0], mo.hi[1] - mo.lo[1]), smax(o.ext[0], o.ext[1])) > P.big;
+            bool snap = false;
+            if (P.move_n > 0 && mo.trk_t > 0 && !o.trunc && F.cam_steady) {
+              const double dt = F.stamp - mo.trk_t;
+              const double sx = o.pos[0] - mo.trk_pos[0], sy = o.pos[1] - mo.trk_pos[1];
+              const double sp = dt > 1e-6 && dt <= 0.6 ? sqrt(sx * sx + sy * sy) / dt : 0.0;
+              const bool same_dir = sx * mo.trk_step[0] + sy * mo.trk_step[1] > 0;
+              mo.mv_cnt = sp > P.move_v && (same_dir || mo.mv_cnt == 0) ? mo.mv_cnt + 1 : 0;
+              mo.trk_step[0] = sx;
+              mo.trk_step[1] = sy;
+              const double rx = o.pos[0] - mo.pos[0], ry = o.pos[1] - mo.pos[1];
+              const double away = sqrt(rx * rx + ry * ry);
+              const bool moving = F.stamp - mo.moving_t < 1.0;
+              const bool left = away > smax(P.move_min_d, 0.5 * smax(o.ext[0], o.ext[1])) &&
+                                box_overlap(o.lo, o.hi, mo.lo, mo.hi, P.merge_min_ext) < 0.1;
+              if (mo.mv_cnt >= P.move_n && (moving || left)) {
+                if (!moving) mo.move_from_t = F.stamp;
+                mo.moving_t = F.stamp;
+                snap = true;
+              } else if (moving && sp > 0.5 * P.move_v) {
+                snap = true;
+                mo.moving_t = F.stamp;
+              }
+            }
+            if (!o.trunc) {
+              for (int k = 0; k < 3; ++k) mo.trk_pos[k] = o.pos[k];
+              mo.trk_t = F.stamp;
+            }
+            if (snap) {
+              double d3[3];
+              for (int k = 0; k < 3; ++k) {
+                d3[k] = o.pos[k] - mo.pos[k];
+                mo.pos[k] = o.pos[k]; mo.ext[k] = o.ext[k]; mo.lo[k] = o.lo[k]; mo.hi[k] = o.hi[k];
+              }
+              CloudRec& C = B.clouds[cslot_glob(B, m, mo)];
+              if (C.n > 0 && !(d3[0] == 0 && d3[1] == 0 && d3[2] == 0)) {   // ObjCloud::translate (cloud.cpp:79-84)
+                for (int k = 0; k < 3; ++k) C.org[k] += d3[k];
+                ++C.version;
+                C.stamp = F.stamp;
+              }
+              if (dist3(mo.pos, mo.first_pos) > P.moved_d) mo.moved = 1;
+              if (mo.moved && mo.state == 0) mo.state = 2;
+            }
+            const bool fresh = mo.first_seen == F.stamp;
+            for (int k = 0; k < 3 && !snap; ++k) {
+              if (fresh) {
+                mo.lo[k] = smin(mo.lo[k], o.lo[k]);
+                mo.hi[k] = smax(mo.hi[k], o.hi[k]);
+                mo.pos[k] = 0.5 * (mo.lo[k] + mo.hi[k]);
+                mo.ext[k] = mo.hi[k] - mo.lo[k];
+                continue;
+              }
+              if (big) {
+                const double lo = smax(smin(mo.lo[k], o.lo[k]), mo.lo[k] - P.grow_max);
+                const double hi = smin(smax(mo.hi[k], o.hi[k]), mo.hi[k] + P.grow_max);
+                if (hi - lo <= P.max_ext) { mo.lo[k] = lo; mo.hi[k] = hi; }
+                mo.pos[k] = 0.5 * (mo.lo[k] + mo.hi[k]);
+                mo.ext[k] = mo.hi[k] - mo.lo[k];
+              } else {
+                const double K = kalman_gain(mo.P[k], P.ap_q_pos, dt_seen, kalman_R(P.ap_r0, P.ap_r1, o.zmed, o.trunc, o.ext[k]));
+                mo.pos[k] += K * (o.pos[k] - mo.pos[k]);
+                mo.lo[k] += K * (o.lo[k] - mo.lo[k]);
+                mo.hi[k] += K * (o.hi[k] - mo.hi[k]);
+                mo.ext[k] = mo.hi[k] - mo.lo[k];
+              }
+              if (big) kalman_big(mo.P[k], P.ap_q_pos, dt_seen, P.ap_r0 + P.ap_r1 * o.zmed, mo.ext[k]);
+            }
+            mo.score = (mo.score < o.score) ? o.score : mo.score;
+            mo.max_det_z = smax(mo.max_det_z, o.zmed);
+            mo.last_seen = F.stamp;
+            mo.misses = 0;
+            if (mo.state == 1) {
+              mo.state = mo.moved ? 2 : 0;
+              s_evf[a] |= 1;   // state event, numbered in P3
+            }
+            if (!mo.confirmed && (int)mo.n_obs >= P.confirm) {
+              mo.confirmed = 1;
+              s_evf[a] |= 2;   // confirmation event, numbered in P3
+            }
+          }
+      }
+    }
+  }
+  __syncthreads();
+  // P3: events in observation order (new object: 0; update: state change 6, confirmation 1)
+  if (tid == 0) {
+    for (int a = 0; a < nobs; ++a) {
+      const int act = s_act[a];
+      if (!act) continue;
+      const ObjRec& mo = REC[obs_rec[a]];
+      if (act == 2) {
         push_event_l(B, m, F.stamp, mo, 0, (2u << 24) | (uint32_t)evn++, ev_base, &evl);
+      } else {
+        if (s_evf[a] & 1) push_event_l(B, m, F.stamp, mo, 6, (2u << 24) | (uint32_t)evn++, ev_base, &evl);
+        if (s_evf[a] & 2) push_event_l(B, m, F.stamp, mo, 1, (2u << 24) | (uint32_t)evn++, ev_base, &evl);
       }
     }
     R->next_id = next_id;
