@@ -325,9 +325,13 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
 
 // apStructObject geometry (objmap.cpp:1255-1319) for objects whose cloud changed; no wall
 // segments and no text model, so only geo 1 (wall-size vertical plane) / 2 (ceiling) matter.
+#define STRUCT_PTS 1600   // cloudSample(800) keeps ceil(n / max(1, n / 800)) < 1600 points
+#define STRUCT_SMEM (sizeof(PlaneSmem) + 3 * STRUCT_PTS * sizeof(float))   // dynamic: plane-fit working set + sample
 __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
+  extern __shared__ __align__(16) unsigned char st_raw[];
+  PlaneSmem& ps = *(PlaneSmem*)st_raw;
+  float* Pt = (float*)(st_raw + sizeof(PlaneSmem));   // cloudSample(800) points (shared)
   __shared__ BlockScratch bs;
-  __shared__ PlaneSmem ps;
   __shared__ PlaneOut pout;
   __shared__ int mine[STRUCT_LIST];
   __shared__ int nmine;
@@ -338,7 +342,6 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
   const MapRec& R = B.maps[m];
   const smg_params& P = B.p;
   double* sel = B.sscr + ((size_t)m * gridDim.x + blockIdx.x) * STRUCT_SCR;
-  float* Pt = (float*)sel;                  // <= 2*800 points
   double* scr = sel + 4096;                 // plane-fit scratch: 2 x 4096 doubles
   // the objects whose cloud changed, in list order; CTA c takes every gridDim.x-th of them
   if (threadIdx.x == 0) nmine = 0;
@@ -372,7 +375,7 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
     const size_t stp = (size_t)C.n / 800 > 1 ? (size_t)C.n / 800 : 1;
     const int n = (int)(((size_t)C.n + stp - 1) / stp);
     const float4* pts = B.cpts + cs * B.cap;
-    if (!INB(3 * n, 2 * 4096, 508)) continue;
+    if (!INB(n, STRUCT_PTS, 508)) continue;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       const float4 qp = pts[(size_t)i * stp];
       Pt[3 * i] = (float)(C.org[0] + (double)qp.x);
