@@ -202,7 +202,9 @@ int64_t smg_kernel_launches(smg_batch* b);
  * counterpart): out[0] pixels scanned by the detection back-projection, [1] detections,
  * [2] memory vectors read by association in units of D fp16 values (an fp32 r_frag counts 2),
  * [3] object vector updates, [4] cloud points written, [5] depth pixels read by makeScan,
- * [6] scan points inserted, [7] occupancy cells updated.  Returns the number of counters. */
+ * [6] scan points inserted, [7] occupancy cells updated, [8] bytes of host inputs moved to the
+ * device by pushes of SMG_MEM_HOST frames (copies plus in-place reads of pinned frames).
+ * Returns the number of counters. */
 int smg_get_work(smg_batch* b, int64_t* out, int n);
 
 /* ---- standalone occupancy grid + correlative scan matching ---- */

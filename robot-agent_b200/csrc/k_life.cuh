@@ -59,7 +59,7 @@ DEV int absent_evidence_warp(const Batch& B, int m, const ObjRec& o, const Frame
     const double uf = (double)F.fx * c[0] / c[2] + (double)F.cx, vf = (double)F.fy * c[1] / c[2] + (double)F.cy;
     const int u = (int)uf, v = (int)vf;
     if (u < 2 || v < 2 || u >= F.w - 2 || v >= F.h - 2) continue;
-    const float d = F.depth[(size_t)v * F.w + u];
+    const float d = (F.depth_host ? F.depth_host : F.depth)[(size_t)v * F.w + u];   // host frame when gathered
     if (!(d > 0)) continue;
     if ((double)d < c[2] - P.occl) continue;
     ++vis;

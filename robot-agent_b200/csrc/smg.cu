@@ -30,6 +30,7 @@
 #include "k_occ.cuh"
 #include "k_gemm_assoc.cuh"
 #include "k_text.cuh"
+#include "k_gather.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -64,6 +65,7 @@ struct smg_batch {
   // caller's for group 0) and occupancy side stream; host inputs arrive on s_copy
   static constexpr int kGroupsMax = 8;
   int groups = 1;
+  bool host_gather = getenv("SMG_HOST_GATHER") == nullptr || atoi(getenv("SMG_HOST_GATHER")) != 0;
   cudaStream_t s_grp[kGroupsMax] = {}, s_gridg[kGroupsMax] = {}, s_copy = nullptr;
   cudaEvent_t ev_fork[kGroupsMax] = {}, ev_join[kGroupsMax] = {}, ev_copied[kGroupsMax] = {}, ev_gdone[kGroupsMax] = {};
   cudaEvent_t ev_up = nullptr, ev_done = nullptr;
@@ -74,6 +76,7 @@ struct smg_batch {
   unsigned char* d_emb = nullptr;
   std::vector<double> last_cam_t, last_cam_fwd;
   long long launches = 0;
+  long long h2d_host = 0;   // host-input bytes copied by the copy engines
   cudaStream_t last_stream = nullptr;
   // per-kernel event timing
   bool timing = false;
@@ -603,6 +606,28 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   b->h_frames = b->h_ring + (size_t)slot * B.M;
   const size_t WH = (size_t)b->max_w * b->max_h;
   size_t emb_off = 0;   // host embeddings are staged packed, frame after frame
+  // Host frames in pinned (device-accessible) memory are read in place: k_gather fetches only
+  // the pixels the chain reads.  Any other host memory goes through whole-frame copies.
+  bool gather = where == SMG_MEM_HOST && b->host_gather && b->max_w <= GATHER_WMAX;
+  auto dev_ptr = [](const void* p, size_t bytes) -> const void* {
+    cudaPointerAttributes a0, a1;
+    if (cudaPointerGetAttributes(&a0, p) != cudaSuccess || cudaPointerGetAttributes(&a1, (const char*)p + bytes - 1) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    if (a0.type != cudaMemoryTypeHost || a1.type != cudaMemoryTypeHost || !a0.devicePointer || !a1.devicePointer) return nullptr;
+    return a0.devicePointer;
+  };
+  std::vector<const void*> dh(gather ? 2 * (size_t)n : 0, nullptr);
+  for (int i = 0; i < n && gather; ++i) {
+    const size_t pi = (size_t)frames[i].w * frames[i].h;
+    dh[2 * i] = dev_ptr(frames[i].depth, pi * 4);
+    if (!dh[2 * i]) gather = false;
+    if (frames[i].label) {
+      dh[2 * i + 1] = dev_ptr(frames[i].label, pi * 2);
+      if (!dh[2 * i + 1]) gather = false;
+    }
+  }
   for (int m = 0; m < B.M; ++m) {
     FrameDev& d = b->h_frames[m];
     memset(&d, 0, sizeof(d));
@@ -633,6 +658,10 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     } else {
       d.depth = b->d_depth + (size_t)m * WH;
       d.label = b->d_label + (size_t)m * WH;
+      if (gather) {
+        d.depth_host = (const float*)dh[2 * m];
+        d.label_host = (const uint16_t*)dh[2 * m + 1];
+      }
       d.emb = f.emb && f.n_det > 0 ? (const void*)(b->d_emb + emb_off) : nullptr;
       if (d.emb) emb_off += (size_t)f.n_det * B.D * (f.emb_dtype == SMG_EMB_BF16 ? 2 : 4);
     }
@@ -659,16 +688,19 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   const int G = (b->timing || b->dbg_sync) ? 1 : std::max(1, std::min(b->groups, B.M));
   auto gbeg = [&](int g) { return (int)((long long)B.M * g / G); };
   CK(cudaMemcpyAsync(B.frames, b->h_frames, sizeof(FrameDev) * B.M, cudaMemcpyHostToDevice, st));
+  if (where == SMG_MEM_HOST) b->h2d_host += (long long)(sizeof(FrameDev) * B.M);
   CK(cudaEventRecord(b->ring_ev[slot], st));
   b->ring_used[slot] = true;
   CK(cudaEventRecord(b->ev_up, st));
   if (where == SMG_MEM_HOST) {
-    // the staging buffers are free once the previous chain is done
+    // the staging buffers are free once the previous chain is done; the gather reads the
+    // descriptors uploaded above
     CK(cudaStreamWaitEvent(b->s_copy, b->ev_done, 0));
+    if (gather) CK(cudaStreamWaitEvent(b->s_copy, b->ev_up, 0));
     for (int g = 0; g < G; ++g) {
       const int m0 = std::min(gbeg(g), n), m1 = std::min(gbeg(g + 1), n);
       // depth and labels: one copy per run of maps that lie back to back in host memory
-      for (int i = m0; i < m1;) {
+      for (int i = m0; i < m1 && !gather;) {
         const size_t pi = (size_t)frames[i].w * frames[i].h;
         int j = i + 1;
         while (j < m1 && pi == WH && (size_t)frames[j].w * frames[j].h == WH &&
@@ -678,6 +710,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
         const size_t run = j - i > 1 ? (size_t)(j - i) * WH : pi;
         CK(cudaMemcpyAsync(b->d_depth + i * WH, frames[i].depth, run * 4, cudaMemcpyHostToDevice, b->s_copy));
         if (frames[i].label) CK(cudaMemcpyAsync(b->d_label + i * WH, frames[i].label, run * 2, cudaMemcpyHostToDevice, b->s_copy));
+        b->h2d_host += (long long)run * (frames[i].label ? 6 : 4);
         i = j;
       }
       // embeddings: packed on the device; one copy per run that is packed on the host too
@@ -693,7 +726,14 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
           ++j;
         }
         CK(cudaMemcpyAsync((void*)d0, h0, bytes, cudaMemcpyHostToDevice, b->s_copy));
+        b->h2d_host += (long long)bytes;
         i = j;
+      }
+      if (gather && gbeg(g + 1) > gbeg(g)) {   // group g's pixels, while group g-1 computes
+        Batch Bg = B;
+        Bg.map0 = gbeg(g);
+        k_gather<<<dim3(b->max_h, gbeg(g + 1) - gbeg(g)), GATHER_THREADS, 0, b->s_copy>>>(Bg);
+        b->launches += 1;
       }
       CK(cudaEventRecord(b->ev_copied[g], b->s_copy));
     }
@@ -1589,6 +1629,7 @@ int smg_get_work(smg_batch* b, int64_t* out, int n) {
     out[k] = 0;
     if (k < SMG_WORK_N)
       for (const MapRec& r : maps) out[k] += r.wk[k];
+    if (k == SMG_WK_H2D) out[k] += b->h2d_host;
   }
   return SMG_WORK_N;
 }

@@ -46,6 +46,10 @@ typedef struct {
   int32_t w, h;
   const float* depth;
   const uint16_t* label;
+  // host inputs the device reads in place (pinned, device-accessible), or null: the staging
+  // images then hold only the pixels the chain reads, gathered by k_gather
+  const float* depth_host;
+  const uint16_t* label_host;
   float fx, fy, cx, cy;
   double T_mc[12];
   float T_bc[12];
@@ -156,7 +160,8 @@ typedef struct {
 #define SMG_WK_SCAN_PX 5     // depth pixels read by makeScan
 #define SMG_WK_SCAN_PTS 6    // scan points inserted (match cells + laser hits + free rays)
 #define SMG_WK_CELLS 7       // occupancy cells updated (one update per cell per scan)
-#define SMG_WORK_N 8
+#define SMG_WK_H2D 8         // host-input bytes the device read in place (pinned frames, k_gather)
+#define SMG_WORK_N 9
 
 // Merge-pass cache (the reference keeps one too, objmap.cpp:1137-1150): the embedding cosine and
 // the contact fraction of an object pair depend only on the two objects' vectors (ver) and

@@ -286,7 +286,7 @@ class Batch:
     def launches(self) -> int:
         return int(lib().smg_kernel_launches(self.h))
 
-    WORK_KEYS = ("obs_px", "det", "vec16", "upd", "cloud_pts", "scan_px", "scan_pts", "cells")
+    WORK_KEYS = ("obs_px", "det", "vec16", "upd", "cloud_pts", "scan_px", "scan_pts", "cells", "h2d")
 
     def work(self) -> dict:
         """Cumulative work counters (smg_get_work) as a dict keyed by WORK_KEYS."""

@@ -12,7 +12,21 @@ from conftest import has_gpu
 pytestmark = pytest.mark.gpu
 
 
-def _run(groups: int, M: int, N: int, D: int):
+def _pinned(fr: dict) -> dict:
+    """The frame with its images in pinned host memory (the device reads them in place)."""
+    import torch
+    out = dict(fr)
+    for k in ("depth", "label"):
+        a = np.ascontiguousarray(fr[k])
+        t = torch.empty(a.shape, dtype=torch.float32 if a.dtype == np.float32 else torch.int16, pin_memory=True)
+        v = t.numpy().view(a.dtype)
+        v[...] = a
+        out[k] = v
+        out["_keep_" + k] = t
+    return out
+
+
+def _run(groups: int, M: int, N: int, D: int, pinned: bool = False):
     from scenemap_b200 import smg, synth
     os.environ["SMG_STREAM_GROUPS"] = str(groups)
     try:
@@ -23,6 +37,8 @@ def _run(groups: int, M: int, N: int, D: int):
     trace = []
     for f in range(N):
         frs = [g.frame(f) for g in gens]
+        if pinned:
+            frs = [_pinned(fr) for fr in frs]
         B.push(frs, smg.SMG_MEM_HOST, smg.SMG_EMB_BF16)   # host inputs: copied group by group
         trace.append(B.assoc_all().copy())
     out = {"assoc": trace, "err": B.error_word()}
@@ -62,3 +78,15 @@ def test_stream_groups_match_one_chain():
     _same(one, four)
     three = _run(3, M, N, D)   # uneven ranges (3, 2, 3 maps)
     _same(one, three)
+
+
+def test_pinned_host_frames_gathered():
+    """Pinned host frames are read in place, only the pixels the chain reads (k_gather); the
+    results must equal those of whole-frame copies of pageable frames."""
+    if not has_gpu():
+        pytest.skip("no GPU")
+    M, N, D = 8, 24, 1152
+    paged = _run(4, M, N, D)
+    pinned = _run(4, M, N, D, pinned=True)
+    assert paged["err"] == 0 and pinned["err"] == 0
+    _same(paged, pinned)
