@@ -6,6 +6,8 @@
 //    (objmap.cpp:648-652, the same expressions as k_obs);
 //  - k_grid: the depth rows v = j * step (makeScan's grid, scan.cpp:233-251);
 //  - k_markview: the depth rows v = stp/2 + j * stp (objmap.cpp:219-245).
+// Those whole rows travel by strided copies on the copy engines, beside this kernel; the kernel
+// moves the box pixels of the other rows and every label pixel.
 // k_absent reads depth at the projections of object clouds, which depend on the map state; it
 // reads those few pixels from the host frame directly (FrameDev::depth_host).
 // One CTA per (image row, map): the row's pixel masks are built from the boxes in shared memory,
@@ -23,11 +25,11 @@ __global__ void __launch_bounds__(GATHER_THREADS) k_gather(Batch B) {
   if (!F.active || !F.depth_host || v >= F.h) return;
   const int W = F.w, H = F.h, nw = (W + 31) >> 5;
   if (W > GATHER_WMAX) return;   // rejected on the host
-  // whole rows: makeScan's sample rows and markView's sample rows
+  // whole rows (copied by the copy engines): makeScan's and markView's sample rows
   const int step = max(1, (int)llround(F.w / 160.0));
   const int stp = max(1, F.w / 32);
   const bool full = v % step == 0 || (v >= stp / 2 && (v - stp / 2) % stp == 0);
-  for (int i = tid; i < nw; i += blockDim.x) { dmask[i] = full ? 0xffffffffu : 0u; lmask[i] = 0u; }
+  for (int i = tid; i < nw; i += blockDim.x) { dmask[i] = 0u; lmask[i] = 0u; }   // whole rows come by copy
   __syncthreads();
   // detection boxes: depth over [u0, u1] on rows [v0, v1], labels one pixel wider on both axes
   auto set_bits = [](uint32_t* mask, int lo, int hi) {   // bits lo..hi, a word at a time

@@ -66,8 +66,9 @@ struct smg_batch {
   static constexpr int kGroupsMax = 8;
   int groups = 1;
   bool host_gather = getenv("SMG_HOST_GATHER") == nullptr || atoi(getenv("SMG_HOST_GATHER")) != 0;
-  cudaStream_t s_grp[kGroupsMax] = {}, s_gridg[kGroupsMax] = {}, s_copy = nullptr;
-  cudaEvent_t ev_fork[kGroupsMax] = {}, ev_join[kGroupsMax] = {}, ev_copied[kGroupsMax] = {}, ev_gdone[kGroupsMax] = {};
+  cudaStream_t s_grp[kGroupsMax] = {}, s_gridg[kGroupsMax] = {}, s_copy = nullptr, s_dma = nullptr;
+  cudaEvent_t ev_fork[kGroupsMax] = {}, ev_join[kGroupsMax] = {}, ev_copied[kGroupsMax] = {}, ev_gdone[kGroupsMax] = {},
+              ev_dma[kGroupsMax] = {};
   cudaEvent_t ev_up = nullptr, ev_done = nullptr;
   bool dbg_sync = getenv("SMG_DEBUG_SYNC") != nullptr;   // synchronise + check after every launch
   long long dbg_last = 0;
@@ -259,11 +260,12 @@ int smg_destroy(smg_batch* b) {
   if (b->h_ring) cudaFreeHost(b->h_ring);
   for (auto e : b->ring_ev) if (e) cudaEventDestroy(e);
   for (int g = 0; g < smg_batch::kGroupsMax; ++g) {
-    for (cudaEvent_t e : {b->ev_fork[g], b->ev_join[g], b->ev_copied[g], b->ev_gdone[g]}) if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : {b->ev_fork[g], b->ev_join[g], b->ev_copied[g], b->ev_gdone[g], b->ev_dma[g]}) if (e) cudaEventDestroy(e);
     for (cudaStream_t q : {b->s_grp[g], b->s_gridg[g]}) if (q) cudaStreamDestroy(q);
   }
   for (cudaEvent_t e : {b->ev_up, b->ev_done}) if (e) cudaEventDestroy(e);
   if (b->s_copy) cudaStreamDestroy(b->s_copy);
+  if (b->s_dma) cudaStreamDestroy(b->s_dma);
   delete b;
   return SMG_OK;
 }
@@ -471,10 +473,11 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
     for (int g = 0; g < smg_batch::kGroupsMax; ++g) {
       if (g > 0) CK(cudaStreamCreateWithFlags(&b->s_grp[g], cudaStreamNonBlocking));
       CK(cudaStreamCreateWithFlags(&b->s_gridg[g], cudaStreamNonBlocking));
-      for (cudaEvent_t* e : {&b->ev_fork[g], &b->ev_join[g], &b->ev_copied[g], &b->ev_gdone[g]})
+      for (cudaEvent_t* e : {&b->ev_fork[g], &b->ev_join[g], &b->ev_copied[g], &b->ev_gdone[g], &b->ev_dma[g]})
         CK(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
     }
     CK(cudaStreamCreateWithFlags(&b->s_copy, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&b->s_dma, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&b->ev_up, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&b->ev_done, cudaEventDisableTiming));
     CK(cudaEventRecord(b->ev_done, 0));
@@ -696,7 +699,23 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     // the staging buffers are free once the previous chain is done; the gather reads the
     // descriptors uploaded above
     CK(cudaStreamWaitEvent(b->s_copy, b->ev_done, 0));
-    if (gather) CK(cudaStreamWaitEvent(b->s_copy, b->ev_up, 0));
+    if (gather) {
+      CK(cudaStreamWaitEvent(b->s_copy, b->ev_up, 0));
+      CK(cudaStreamWaitEvent(b->s_dma, b->ev_done, 0));
+    }
+    // in gather mode the copy engines move the embeddings and the whole sample rows (makeScan's
+    // rows v = j * step, markView's rows v = stp/2 + j * stp) on s_dma, beside the SMs' gather
+    cudaStream_t sdma = gather ? b->s_dma : b->s_copy;
+    auto rows2d = [&](int i, int j, int first, int pitch) -> int {   // maps i..j-1, same size, back to back
+      const int w = frames[i].w, h = frames[i].h;
+      const size_t spitch = (size_t)pitch * w * 4;
+      const size_t nrow = j - i > 1 ? (size_t)(j - i) * h / pitch : (size_t)(h - first + pitch - 1) / pitch;
+      if (nrow == 0) return 0;
+      CK(cudaMemcpy2DAsync(b->d_depth + i * WH + (size_t)first * w, spitch, frames[i].depth + (size_t)first * w, spitch,
+                           (size_t)w * 4, nrow, cudaMemcpyHostToDevice, sdma));
+      b->h2d_host += (long long)(nrow * w * 4);
+      return 0;
+    };
     for (int g = 0; g < G; ++g) {
       const int m0 = std::min(gbeg(g), n), m1 = std::min(gbeg(g + 1), n);
       // depth and labels: one copy per run of maps that lie back to back in host memory
@@ -725,10 +744,22 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
           bytes += (size_t)frames[j].n_det * B.D * (frames[j].emb_dtype == SMG_EMB_BF16 ? 2 : 4);
           ++j;
         }
-        CK(cudaMemcpyAsync((void*)d0, h0, bytes, cudaMemcpyHostToDevice, b->s_copy));
+        CK(cudaMemcpyAsync((void*)d0, h0, bytes, cudaMemcpyHostToDevice, sdma));
         b->h2d_host += (long long)bytes;
         i = j;
       }
+      for (int i = m0; i < m1 && gather;) {
+        const int w = frames[i].w, h = frames[i].h;
+        const int step = std::max(1, (int)std::llround(w / 160.0)), stp = std::max(1, w / 32);
+        int j = i + 1;
+        while (j < m1 && (size_t)w * h == WH && frames[j].w == w && frames[j].h == h && h % step == 0 && h % stp == 0 &&
+               frames[j].depth == frames[i].depth + (size_t)(j - i) * WH)
+          ++j;
+        if (int r = rows2d(i, j, 0, step)) return r;
+        if (int r = rows2d(i, j, stp / 2, stp)) return r;
+        i = j;
+      }
+      if (gather) CK(cudaEventRecord(b->ev_dma[g], b->s_dma));
       if (gather && gbeg(g + 1) > gbeg(g)) {   // group g's pixels, while group g-1 computes
         Batch Bg = B;
         Bg.map0 = gbeg(g);
@@ -745,6 +776,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     cudaStream_t sg = g == 0 ? st : b->s_grp[g];
     if (g > 0) CK(cudaStreamWaitEvent(sg, b->ev_up, 0));
     if (where == SMG_MEM_HOST) CK(cudaStreamWaitEvent(sg, b->ev_copied[g], 0));
+    if (gather) CK(cudaStreamWaitEvent(sg, b->ev_dma[g], 0));
     if (Mg > 0)
       if (int r = launch_group(b, Bg, Mg, sg, b->s_gridg[g], b->ev_fork[g], b->ev_join[g])) return r;
     if (g > 0) {
