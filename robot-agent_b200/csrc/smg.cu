@@ -622,14 +622,21 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     return a0.devicePointer;
   };
   std::vector<const void*> dh(gather ? 2 * (size_t)n : 0, nullptr);
-  for (int i = 0; i < n && gather; ++i) {
+  for (int i = 0; i < n && gather;) {
+    // a run of frames that lie back to back (depth and labels) is checked at its two ends
     const size_t pi = (size_t)frames[i].w * frames[i].h;
-    dh[2 * i] = dev_ptr(frames[i].depth, pi * 4);
-    if (!dh[2 * i]) gather = false;
-    if (frames[i].label) {
-      dh[2 * i + 1] = dev_ptr(frames[i].label, pi * 2);
-      if (!dh[2 * i + 1]) gather = false;
+    int j = i + 1;
+    while (j < n && (size_t)frames[j].w * frames[j].h == pi && frames[j].depth == frames[i].depth + (j - i) * pi &&
+           (frames[i].label ? frames[j].label == frames[i].label + (j - i) * pi : frames[j].label == nullptr))
+      ++j;
+    const char* d0 = (const char*)dev_ptr(frames[i].depth, (size_t)(j - i) * pi * 4);
+    const char* l0 = frames[i].label ? (const char*)dev_ptr(frames[i].label, (size_t)(j - i) * pi * 2) : nullptr;
+    if (!d0 || (frames[i].label && !l0)) { gather = false; break; }
+    for (int k = i; k < j; ++k) {
+      dh[2 * k] = d0 + (size_t)(k - i) * pi * 4;
+      dh[2 * k + 1] = l0 ? l0 + (size_t)(k - i) * pi * 2 : nullptr;
     }
+    i = j;
   }
   for (int m = 0; m < B.M; ++m) {
     FrameDev& d = b->h_frames[m];
