@@ -2,10 +2,11 @@
 // 1154-1225, apPairObj :1118-1135, da::absorbObject da/src/merge.cpp:32-82, apMerge
 // objprob.cpp:358-394).
 //
-// k_merge_pairs: warps take the rows i of the object list and test every j > i: box-gap and
-// size gates, then for surviving pairs the contact fraction of a <= 2*contact_samples sample of
-// the smaller cloud against the larger cloud's contact set, and the symmetric embedding cosine
-// (each object's mean direction against the other's vectors).  Pairs with P >= merge_p go to a
+// k_merge_gate tests every pair i < j (box-gap and size gates) and lists the survivors;
+// k_merge_pairs then evaluates them, a warp per pair taken from the map's list: the contact
+// fraction of a <= 2*contact_samples sample of the smaller cloud against the larger cloud's
+// contact set, and the symmetric embedding cosine (each object's mean direction against the
+// other's vectors).  Pairs with P >= merge_p go to a
 // per-map candidate list.  (The reference's pair cache only skips recomputing identical inputs,
 // so evaluating every gated pair gives the same P.)
 // k_merge_apply: one CTA per map sorts the candidates by P and merges greedily, each object at
@@ -14,8 +15,8 @@
 #include "k_life.cuh"
 
 #define MP_CTAS 8
-#define MP_GL 8192   // gated pairs per CTA
-#define MP_SMEM(O) ((size_t)(O) * (6 * 8 + 2 * 4) + MP_GL * 4)
+#define MGL_CAP 65536   // gated pairs per map and frame
+#define MP_SMEM(O) ((size_t)(O) * (6 * 8 + 4))   // k_merge_gate: boxes and states
 
 // p-th pair (i < j) of n objects in row-major order of the upper triangle
 DEV void pair_of(long long p, int n, int* pi, int* pj) {
@@ -28,10 +29,10 @@ DEV void pair_of(long long p, int n, int* pi, int* pj) {
   *pj = (int)(p - rowstart(i) + i + 1);
 }
 
-__global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
+// Pair gating: the 8 CTAs of a map share the pairs and append the gated ones to the map's list.
+__global__ void __launch_bounds__(256) k_merge_gate(Batch B) {
   extern __shared__ unsigned char smem_raw[];
-  __shared__ int ngl;
-  const int m = B.map0 + blockIdx.y, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const int m = B.map0 + blockIdx.y, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   const MapRec& R = B.maps[m];
@@ -40,17 +41,13 @@ __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
   if (n < 2) return;
   double* slo = (double*)smem_raw;
   double* shi = slo + 3 * (size_t)B.O;
-  int* scn = (int*)(shi + 3 * (size_t)B.O);
-  int* sst = scn + B.O;
-  int* gl = sst + B.O;
+  int* sst = (int*)(shi + 3 * (size_t)B.O);
   // 1. stage the gate inputs of every object (parallel loads)
   for (int b = tid; b < n; b += blockDim.x) {
     const ObjRec& o = obj_at(B, m, b);
     for (int k = 0; k < 3; ++k) { slo[3 * b + k] = o.lo[k]; shi[3 * b + k] = o.hi[k]; }
-    scn[b] = B.clouds[(size_t)m * B.O + o.cloud_slot].n;
     sst[b] = o.state;
   }
-  if (tid == 0) ngl = 0;
   __syncthreads();
   // 2. box-gap and size gates of all pairs (objmap.cpp:1160-1173); this CTA takes every
   //    MP_CTAS-th pair
@@ -68,24 +65,39 @@ __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
       too_big = too_big || smax(shi[3 * i + k], shi[3 * j + k]) - smin(slo[3 * i + k], slo[3 * j + k]) > P.max_ext;
     }
     if (g2 > gate2 || too_big) continue;
-    const int q = atomicAdd(&ngl, 1);
-    if (q < MP_GL) gl[q] = i << 16 | j;
+    const int q = atomicAdd(&B.mgl_n[m], 1);
+    if (q < MGL_CAP) B.mgl[(size_t)m * MGL_CAP + q] = i << 16 | j;
     else set_err(&B.maps[m], SMG_E_ARGS);
   }
-  __syncthreads();
-  // 3. apPairObj of the gated pairs (objmap.cpp:1118-1135), one warp per pair
-  const int ng = min(ngl, MP_GL);
-  for (int g = wid; g < ng; g += nw) {
-    const int i = gl[g] >> 16, j = gl[g] & 0xffff;
+}
+
+// Pair evaluation: every warp of the map's CTAs takes the next gated pair of the map's list, so
+// a slow pair (cosines against all views, contact test) holds one warp, not a CTA's share.
+__global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
+  const int m = B.map0 + blockIdx.y, lane = threadIdx.x & 31;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  const MapRec& R = B.maps[m];
+  const smg_params& P = B.p;
+  if (R.n_obj < 2) return;
+  const int ng = min(B.mgl_n[m], MGL_CAP);
+  for (;;) {
+    int g = 0;
+    if (lane == 0) g = atomicAdd(&B.mgl_n[B.M + m], 1);
+    g = __shfl_sync(0xffffffffu, g, 0);
+    if (g >= ng) break;
+    const int key = B.mgl[(size_t)m * MGL_CAP + g];
+    const int i = key >> 16, j = key & 0xffff;
     const int si = slot_at(B, m, i), sj = slot_at(B, m, j);
     const size_t ogi = oglob(B, m, si), ogj = oglob(B, m, sj);
     const ObjRec& a = B.objs[ogi];
     const ObjRec& b = B.objs[ogj];
-    const bool a_small = scn[i] <= scn[j];
+    const int scn_i = B.clouds[(size_t)m * B.O + a.cloud_slot].n, scn_j = B.clouds[(size_t)m * B.O + b.cloud_slot].n;
+    const bool a_small = scn_i <= scn_j;
     const ObjRec& sm = a_small ? a : b;
     const ObjRec& lg = a_small ? b : a;
     const size_t css = (size_t)m * B.O + sm.cloud_slot, csl = (size_t)m * B.O + lg.cloud_slot;
-    const int cn = a_small ? scn[i] : scn[j];
+    const int cn = a_small ? scn_i : scn_j;
     const int stp = max(1, cn / max(1, P.contact_samples));
     const int nsp = cn > 0 ? (cn + stp - 1) / stp : 0;
     // cached cosine and contact of an unchanged pair

@@ -376,6 +376,8 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.mcand_ab, MO * 8 * 2);
   DA(B.mcand_key, MO * 8);
   DA(B.mcand_n, M);
+  DA(B.mgl, (size_t)M * MGL_CAP);
+  DA(B.mgl_n, 2 * (size_t)M);
   DA(B.pcache, (size_t)M * PCACHE_SLOTS);
   DA(B.sscr, (size_t)M * STRUCT_CTAS * STRUCT_SCR);
   DA(B.upd_job, MD);
@@ -489,7 +491,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   {
     const int sm_assoc = ((D * 4 + SP_MAX * 12 + 7) & ~7) + O * 8;
     CK(cudaFuncSetAttribute(k_assoc, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_assoc));
-    CK(cudaFuncSetAttribute(k_merge_pairs, cudaFuncAttributeMaxDynamicSharedMemorySize, MP_SMEM(O)));
+    CK(cudaFuncSetAttribute(k_merge_gate, cudaFuncAttributeMaxDynamicSharedMemorySize, MP_SMEM(O)));
     CK(cudaFuncSetAttribute(k_relink, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 8 * RELINK_STAGE + 8 * D * 4));
     CK(cudaFuncSetAttribute(k_update, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UPD_SMEM(B)));
     CK(cudaFuncSetAttribute(k_struct, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)STRUCT_SMEM));
@@ -515,6 +517,8 @@ __global__ void k_begin(Batch B) {
     R->n_pts = 0;
     R->n_targets = 0;
     B.mcand_n[m] = 0;
+    B.mgl_n[m] = 0;
+    B.mgl_n[B.M + m] = 0;
   }
 }
 
@@ -535,7 +539,8 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   if (b->timing) { cudaEventRecord(e1, sgrid); b->ev_used.push_back({13, {e0, e1}}); } }
   CK(cudaEventRecord(ejoin, sgrid));
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_merge_pairs<<<dim3(MP_CTAS, Mg), 256, MP_SMEM(B.O), st>>>(B);
+  k_merge_gate<<<dim3(MP_CTAS, Mg), 256, MP_SMEM(B.O), st>>>(B);
+  k_merge_pairs<<<dim3(MP_CTAS, Mg), 256, 0, st>>>(B);   // timed together with k_merge_gate
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({1, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
@@ -584,7 +589,7 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({12, {e0, e1}}); } }
   CK(cudaStreamWaitEvent(st, ejoin, 0));   // join
-  b->launches += 15;
+  b->launches += 16;
   return SMG_OK;
 }
 

@@ -273,6 +273,8 @@ typedef struct {
   uint32_t* mcand_ab;    // [M*O*8*2]
   uint32_t* mcand_key;   // [M*O*8] list positions i << 16 | j (the reference's enumeration order)
   int32_t* mcand_n;      // [M]
+  int32_t* mgl;          // [M*MGL_CAP] gated merge pairs of the frame, i << 16 | j
+  int32_t* mgl_n;        // [M] gated pairs; [M] next pair a warp takes (mgl_n + M)
   struct PairCacheRec* pcache;   // [M * PCACHE_SLOTS] merge-pass pair features of unchanged pairs
   double* sscr;          // [M * STRUCT_CTAS * STRUCT_SCR] k_struct scratch
   struct UpdJob* upd_job;  // [M * max_det] vector jobs of k_update, observation order
