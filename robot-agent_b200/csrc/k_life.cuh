@@ -170,7 +170,6 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
   __shared__ double s_first[RELINK_STAGE], s_last[RELINK_STAGE];
   extern __shared__ unsigned char smem_raw[];
   double* s_pos = (double*)smem_raw;   // 3 per object
-  float* mu = (float*)(s_pos + 3 * RELINK_STAGE);   // D per warp
   const int m = B.map0 + blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
@@ -249,19 +248,15 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
   __syncthreads();
   if (tid == 0 && cn_ > RELINK_MAXC) cn_ = RELINK_MAXC;
   __syncthreads();
-  // apCosMax(m, mu(n)) >= link_cos (mu = r_frag / |r_frag| as float, objprob.cpp:233-239)
-  float* myu = mu + (size_t)wid * B.D;
+  // apCosMax(m, mu(n)) >= link_cos (mu = r_frag / |r_frag| as float, objprob.cpp:233-239): the
+  // object's mu cache (kept current with r_frag by k_update_vec and the merge pass) is that vector
   for (int c = wid; c < cn_; c += nw) {
     const ObjRec& n = obj_at(B, m, cnn_[c]);
     const size_t ogn = oglob(B, m, slot_at(B, m, cnn_[c]));
     double cs = -3.0;
     if (n.nrm_frag > 0) {
-      const double nn = sqrt(n.nrm_frag);
-      const float* r = B.rfrag + ogn * B.D;
-      for (int i = lane; i < B.D; i += 32) myu[i] = (float)((double)r[i] / nn);
-      __syncwarp();
       const size_t ogm = oglob(B, m, slot_at(B, m, cm_[c]));
-      cs = cos_max_warp(B, ogm, B.objs[ogm], myu);
+      cs = cos_max_warp(B, ogm, B.objs[ogm], B.mu + ogn * B.D);
     }
     if (lane == 0) ccos_[c] = cs;
     __syncwarp();

@@ -492,7 +492,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
     const int sm_assoc = ((D * 4 + SP_MAX * 12 + 7) & ~7) + O * 8;
     CK(cudaFuncSetAttribute(k_assoc, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_assoc));
     CK(cudaFuncSetAttribute(k_merge_gate, cudaFuncAttributeMaxDynamicSharedMemorySize, MP_SMEM(O)));
-    CK(cudaFuncSetAttribute(k_relink, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 8 * RELINK_STAGE + 8 * D * 4));
+    CK(cudaFuncSetAttribute(k_relink, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 8 * RELINK_STAGE));
     CK(cudaFuncSetAttribute(k_update, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UPD_SMEM(B)));
     CK(cudaFuncSetAttribute(k_struct, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)STRUCT_SMEM));
   }
@@ -569,7 +569,7 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({7, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
-  k_relink<<<Mg, 256, 3 * 8 * RELINK_STAGE + 8 * B.D * 4, st>>>(B);
+  k_relink<<<Mg, 256, 3 * 8 * RELINK_STAGE, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({8, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
