@@ -87,6 +87,10 @@ typedef struct smg_params {
   int32_t bins;
   float self_r, eef_r, arm_r, shoulder[2][3], match_hi, vert_nz, match_cell;
   int32_t dense, change_bins, change_cells, still_every;
+  /* ApParams re-encode requests (objprob.hpp:90-93) */
+  int32_t reenc_max;
+  double reenc_gain, reenc_min_vis;
+  int32_t reenc_min_px;
 } smg_params;
 
 /* One frame of one map.  depth/label/emb/dets live in device memory (SMG_MEM_DEVICE) or in
@@ -138,7 +142,8 @@ int smg_destroy(smg_batch* b);
 
 /* One keyframe for each of the first n maps (frames[i] -> map i).  Replaces, per map,
  * the keyframe block of sm_push_image_rgb (scenemap src/capi.cpp:811-992):
- * Mapper2D::keyframe, ObjectMap::update, ObjectMap::addPoints.  `stream` is a cudaStream_t
+ * Mapper2D::keyframe, ObjectMap::update, ObjectMap::addPoints, and on frames that carry
+ * detection embeddings ObjectMap::buildReencode (capi.cpp:1002-1010).  `stream` is a cudaStream_t
  * (NULL = the legacy default stream).  Returns before the device work finishes; results
  * are read with the getters below (which synchronise the stream). */
 int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, void* stream);
@@ -184,10 +189,26 @@ int smg_get_grid(smg_batch* b, int m, int16_t* L, uint8_t* seen, int8_t* c8);
 int smg_get_keyframe(smg_batch* b, int m, int32_t* out3);
 /* Association of all maps in one read: obj_id[m * max_det + k] (0 = no object). */
 int smg_get_assoc_all(smg_batch* b, uint32_t* obj_id);
+/* Whole-object re-encode request (sm_reenc_req, scenemap include/scenemap.h:407, plus the
+ * request's camera and mask grid; ReencReq, objmap.hpp:142-148): object id, crop box in image
+ * pixels (x0 y0 x1 y1), the view kappa the whole view will carry, the camera position and
+ * optical axis (map frame) at request time, and the mask grid (= the frame's image grid). */
+typedef struct smg_reenc_req {
+  uint32_t id;
+  float box[4];
+  float kappa;
+  double cam[6];
+  int32_t mask_w, mask_h;
+} smg_reenc_req;
+/* Re-encode requests of map m from its last keyframe (sm_reencode_requests, scenemap.h:408),
+ * best first.  bits (may be NULL) receives the projected mask of request r at
+ * bits + r * ceil(max_w * max_h / 32): ceil(mask_w * mask_h / 32) words, bit q = pixel q of
+ * the row-major mask grid, LSB first.  Returns the number of requests (up to cap copied). */
+int smg_get_reencode(smg_batch* b, int m, smg_reenc_req* reqs, uint32_t* bits, int cap);
 /* Per-kernel device time with CUDA events on the launch stream (instrumentation, off by
  * default).  smg_timing_read fills ms[k] (total milliseconds) and n[k] (launches) for the
  * SMG_NUM_KERNELS kernels of the keyframe chain and resets the counters; names[k] is static. */
-#define SMG_NUM_KERNELS 14
+#define SMG_NUM_KERNELS 15
 int smg_timing_enable(smg_batch* b, int on);
 int smg_timing_read(smg_batch* b, double* ms, int64_t* n, const char** names);
 /* First failed self-check of a -DSMG_CHECKS build: (site, index, bound); all zero when none

@@ -81,6 +81,9 @@ def ref_lib():
         L.ref_n_events.argtypes = [C.c_void_p]
         L.ref_events.argtypes = [C.c_void_p, P(C.c_double), P(C.c_uint32), P(C.c_int32), C.c_int]
         L.ref_kf.argtypes = [C.c_void_p, P(C.c_int32)]
+        L.ref_reenc.argtypes = [C.c_void_p, P(C.c_uint32), P(C.c_float), P(C.c_float), P(C.c_double), P(C.c_uint32),
+                                C.c_int]
+        L.ref_reenc_words.argtypes = [C.c_void_p]
         L.ref_grid_geom.argtypes = [C.c_void_p, P(C.c_int32)]
         L.ref_grid_cells.argtypes = [C.c_void_p, P(C.c_int16), P(C.c_uint8), P(C.c_int8)]
         L.ref_occ_create.restype = C.c_void_p
@@ -241,6 +244,21 @@ class RefMap:
         k = np.zeros(max(n, 1), np.int32)
         L.ref_events(self._h, _p(t, C.c_double), _p(i, C.c_uint32), _p(k, C.c_int32), n)
         return list(zip(t[:n].tolist(), i[:n].tolist(), k[:n].tolist()))
+
+    def reenc(self) -> dict:
+        """Re-encode requests of the last keyframe (ObjectMap::buildReencode), best first."""
+        L = ref_lib()
+        n = L.ref_reenc(self._h, None, None, None, None, None, 0)
+        nw = L.ref_reenc_words(self._h)
+        k = max(n, 1)
+        ids = np.zeros(k, np.uint32)
+        box = np.zeros((k, 4), np.float32)
+        kap = np.zeros(k, np.float32)
+        cam = np.zeros((k, 6), np.float64)
+        bits = np.zeros((k, max(nw, 1)), np.uint32)
+        L.ref_reenc(self._h, _p(ids, C.c_uint32), _p(box, C.c_float), _p(kap, C.c_float), _p(cam, C.c_double),
+                    _p(bits, C.c_uint32), n)
+        return dict(id=ids[:n], box=box[:n], kappa=kap[:n], cam=cam[:n], bits=bits[:n, :nw])
 
     def kf(self):
         o = np.zeros(3, np.int32)

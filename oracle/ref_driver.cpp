@@ -5,8 +5,9 @@
 //   Mapper2D::keyframe (scenemap src/mapper2d.cpp:100)  -> makeScan + OccGrid::insert
 //   ObjectMap::update   (scenemap src/objmap.cpp:516)    -> the objprob per-frame update
 //   ObjectMap::addPoints(scenemap src/objmap.cpp:508)    -> ObjCloud::add (cloud.cpp:86)
-// in the order the reference's keyframe glue runs them (scenemap src/capi.cpp:811-992),
-// minus robot FK, best-view crops and re-encode requests (outside the hot path).
+//   ObjectMap::buildReencode (scenemap src/objmap.cpp:1371) -> whole-object re-encode requests
+// in the order the reference's keyframe glue runs them (scenemap src/capi.cpp:811-1010),
+// minus robot FK and best-view crops (outside the hot path).
 // The label image is turned into the sm_detections bit masks the reference consumes
 // (scenemap include/scenemap.h:20-34), with the mask grid equal to the image grid.
 #include <math.h>
@@ -85,6 +86,8 @@ struct RefMap {
   KeyframeStats kf;
   std::vector<uint32_t> bits;
   std::vector<ObsPoints> pts;   // copy of lastPoints() as handed to addPoints
+  std::vector<ReencReq> reenc;  // re-encode requests of the last keyframe
+  int reenc_words = 0;
   explicit RefMap(const ObjParams& p) : om(p) {}
 };
 
@@ -128,6 +131,7 @@ int ref_frame(void* h, const rf_frame* f) {
     Pose2 known{f->base[0], f->base[1], f->base[2]};
     m->kf = m->mapper->keyframe(dv, b, known, nullptr);
   }
+  m->reenc.clear();
   if (f->grid_only) return 0;
   // label image -> sm_detections (mask grid = image grid)
   const int n = f->n_det;
@@ -173,8 +177,30 @@ int ref_frame(void* h, const rf_frame* f) {
   // cloud points, uncoloured (capi.cpp:986-992 with no RGB source)
   m->pts = m->om.lastPoints();
   for (const ObsPoints& q : m->pts) m->om.addPoints(q.obj_id, q.xyz.data(), nullptr, int(q.px.size() / 2), f->stamp);
+  // whole-object re-encode requests on frames with detection embeddings (capi.cpp:1002-1005),
+  // the mask grid being the image grid
+  if (n > 0 && f->emb) m->om.buildReencode(F, f->w, f->h, f->w, f->h, 1.f, 1.f, 0.f, 0.f, &m->reenc);
+  m->reenc_words = int((size_t(f->w) * f->h + 31) / 32);
   return 0;
 }
+
+// Re-encode requests of the last keyframe: id, box (4), kappa, cam (6) and the mask bits
+// (words_per_request words each, consecutive).  Returns the count; copies up to cap.
+int ref_reenc(void* h, uint32_t* id, float* box, float* kappa, double* cam, uint32_t* bits, int cap) {
+  RefMap* m = static_cast<RefMap*>(h);
+  const int n = int(m->reenc.size());
+  for (int r = 0; r < n && r < cap; ++r) {
+    const ReencReq& q = m->reenc[r];
+    if (id) id[r] = q.id;
+    if (box) for (int k = 0; k < 4; ++k) box[4 * r + k] = q.box[k];
+    if (kappa) kappa[r] = q.kappa;
+    if (cam) for (int k = 0; k < 6; ++k) cam[6 * r + k] = q.cam[k];
+    if (bits)
+      for (int k = 0; k < m->reenc_words; ++k) bits[size_t(r) * m->reenc_words + k] = k < int(q.bits.size()) ? q.bits[k] : 0u;
+  }
+  return n;
+}
+int ref_reenc_words(void* h) { return static_cast<RefMap*>(h)->reenc_words; }
 
 int ref_n_objects(void* h) { return int(static_cast<RefMap*>(h)->om.objects().size()); }
 

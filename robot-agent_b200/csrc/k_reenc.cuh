@@ -1,0 +1,310 @@
+// Whole-object re-encode requests of a keyframe (ObjectMap::buildReencode, scenemap
+// src/objmap.cpp:1371-1458), run after the keyframe's cloud additions as the reference's push
+// does (capi.cpp:1002-1010) on every frame that carries detection embeddings.
+//
+// For each confirmed object seen this keyframe with at least 30 cloud points, every stp-th cloud
+// point (stp = max(1, n / 3000)) is projected into the frame.  A point in front of the depth
+// surface (depth > 0 and depth >= z - 0.08) is visible: it paints a voxel-sized square
+// (0.6 voxel at its depth) into the mask grid and its depth joins the median.  The painted mask
+// is closed once (an empty cell with >= 3 painted neighbours of its 8 is filled), and the view
+// kappa of the closed mask (sqrt(area) as size, median depth, visible fraction, truncation)
+// decides the request.  Requests are ranked by priority (objects that never had a whole view
+// first, then kappa over the best whole-view kappa) and the first reenc_max are kept.
+//
+// Layout: one CTA per (candidate slot, map).  Candidates are the objects that pass the cheap
+// tests, numbered in list order; CTA x takes candidates x, x + gridDim.x, ...  The painted mask
+// is a bitset in shared memory with rows padded to whole 32-bit words; the closing runs on
+// whole words (the eight neighbour words are shifted copies of three rows, counted by a
+// saturating bit-sliced adder) and writes the closed mask straight to the candidate's output
+// slot, row-padded, so no second mask is held on chip.  The median depth is an exact radix
+// selection over the visible depths kept in shared memory.  The last CTA of a map to finish
+// ranks the candidates: priority descending, list order on equal priority (the reference's
+// std::sort leaves the order of equal priorities unspecified).
+#pragma once
+#include "dev_util.cuh"
+
+#define RE_THREADS 256
+#define RE_CTAS 8       // CTAs per map
+#define RE_ZMAX 6000    // sampled points per object: ceil(n / max(1, n / 3000)) < 6000 for every n
+// dynamic shared memory: the row-padded mask of the largest frame plus the visible depths
+#define RE_SMEM(B) ((size_t)(B).H * ((((B).W) + 31) >> 5) * 4 + (size_t)RE_ZMAX * 4)
+
+// order-preserving unsigned keys of floats
+DEV uint32_t f_ord(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+DEV float f_unord(uint32_t k) { return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k); }
+
+// k-th smallest (0-based, 0 <= k < n) of n floats: four most-significant-digit radix rounds of
+// 8 bits; exact, so it is the value std::nth_element leaves at position k.
+DEV float block_select_f(const float* a, int n, int k, int* hist, int* s_pick) {
+  const int tid = threadIdx.x;
+  uint32_t prefix = 0, pmask = 0;
+  for (int sh = 24; sh >= 0; sh -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) {
+      const uint32_t key = f_ord(a[i]);
+      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> sh) & 255u], 1);
+    }
+    __syncthreads();
+    if (tid < 32) {   // warp 0: the bin holding rank k (eight bins per lane)
+      int c[8], sum = 0;
+      for (int q = 0; q < 8; ++q) { c[q] = hist[tid * 8 + q]; sum += c[q]; }
+      int incl = sum;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += y;
+      }
+      int before = incl - sum;
+      if (k >= before && k < incl) {
+        int q = 0;
+        while (q < 7 && k >= before + c[q]) { before += c[q]; ++q; }
+        s_pick[0] = tid * 8 + q;
+        s_pick[1] = k - before;
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)s_pick[0] << sh;
+    pmask |= 255u << sh;
+    k = s_pick[1];
+    __syncthreads();
+  }
+  return f_unord(prefix);
+}
+
+// the cheap tests of objmap.cpp:1383 (every object here is an objprob object and none is held)
+DEV bool reenc_candidate(const Batch& B, int m, const ObjRec& o, double stamp) {
+  return o.confirmed && o.state != 1 && o.last_kf == stamp && B.clouds[(size_t)m * B.O + o.cloud_slot].n >= 30;
+}
+
+// viewKappa (bestview.cpp:77-81, objprob_math.h:78-87) with a visible fraction; the camera blur
+// factor exp(-cam_w / blur_w) comes computed by the host libm
+DEV double view_kappa_vis(const smg_params& P, double size_px, bool trunc, double depth, double vis, double blur_fac) {
+  const double s = dmax2(0.0, size_px), d = dmax2(0.0, depth);
+  double k = P.kap_k0 * s / (s + P.kap_s0);
+  if (trunc) k *= P.kap_trunc;
+  k /= 1.0 + (d / P.kap_d0) * (d / P.kap_d0);
+  const double v = vis < 0 ? 0.0 : (vis > 1 ? 1.0 : vis);
+  k *= P.kap_occ == 1.0 ? v : pow(v, P.kap_occ);
+  if (P.kap_blur_w > 0) k *= blur_fac;
+  return dmax2(k, 1e-3);
+}
+
+// Depth at pixel (u, v).  A device-resident frame is read directly.  For a host frame read in
+// place (k_gather), the staging image holds the sample rows and each detection's scan box;
+// any other pixel is read from the host frame.
+DEV float reenc_depth(const FrameDev& F, int u, int v, int step, int stp, int& host_reads) {
+  const size_t i = (size_t)v * F.w + u;
+  if (!F.depth_host) return F.depth[i];
+  if (v % step == 0 || (v >= stp / 2 && (v - stp / 2) % stp == 0)) return F.depth[i];
+  for (int k = 0; k < F.n_det; ++k) {
+    const float* b = F.box[k];
+    const int u0 = max(0, (int)(b[0]) - 1), u1 = min(F.w - 1, (int)(b[2]) + 1);
+    const int v0 = max(0, (int)(b[1]) - 1), v1 = min(F.h - 1, (int)(b[3]) + 1);
+    if (u >= u0 && u <= u1 && v >= v0 && v <= v1) return F.depth[i];
+  }
+  ++host_reads;
+  return F.depth_host[i];
+}
+
+__global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
+  extern __shared__ __align__(16) unsigned char re_smem[];
+  __shared__ BlockScratch bs;
+  __shared__ int s_cand[RE_CAND];
+  __shared__ int s_vis, s_last;
+  __shared__ int s_hist[256], s_pick[2];
+  const int m = B.map0 + blockIdx.y, tid = threadIdx.x;
+  const FrameDev& F = B.frames[m];
+  if (!F.active) return;
+  MapRec* R = &B.maps[m];
+  if (!(F.emb != nullptr && F.n_det > 0)) {   // not an objprob keyframe: no requests
+    if (blockIdx.x == 0 && tid == 0) R->re_n = 0;
+    return;
+  }
+  const smg_params& P = B.p;
+  const double* T = F.T_mc;
+  // the mask grid is the image grid (smg_frame): mask_w = img_w = w, scale 1, offset 0
+  const int mw = F.w, mh = F.h, img_w = F.w, img_h = F.h;
+  const float msx = 1.f, msy = 1.f;
+  const int wpr = (mw + 31) >> 5, nwords = mh * wpr;
+  const int step = max(1, (int)llround(F.w / 160.0)), stp_mv = max(1, F.w / 32);
+  uint32_t* g = (uint32_t*)re_smem;
+  float* zs = (float*)(re_smem + (size_t)B.H * ((B.W + 31) >> 5) * 4);
+
+  // candidates in list order; this CTA keeps its own
+  const int nobj = R->n_obj;
+  int ncand = 0;
+  for (int b0 = 0; b0 < nobj; b0 += blockDim.x) {
+    const int b = b0 + tid;
+    int c = 0;
+    if (b < nobj) c = reenc_candidate(B, m, B.objs[oglob(B, m, slot_at(B, m, b))], F.stamp);
+    int tot;
+    const int j = ncand + block_excl_scan(c, &tot, bs);
+    if (c && j < RE_CAND && j % (int)gridDim.x == (int)blockIdx.x) s_cand[j / gridDim.x] = b;
+    ncand += tot;
+  }
+  if (ncand > RE_CAND && blockIdx.x == 0 && tid == 0) set_err(R, SMG_E_CAP_REENC);
+  const int nc = min(ncand, RE_CAND);
+  __syncthreads();
+
+  ReencRec* recs = B.reenc + (size_t)m * RE_CAND;
+  int host_reads = 0;
+  for (int q = 0; (int)blockIdx.x + q * (int)gridDim.x < nc; ++q) {
+    const int j = blockIdx.x + q * gridDim.x;
+    const int b = s_cand[q];
+    const ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
+    const size_t cs = (size_t)m * B.O + o.cloud_slot;
+    const CloudRec& C = B.clouds[cs];
+    const float4* pts = B.cpts + cs * B.cap;
+    const int n = C.n;
+    const int stp = max(1, n / 3000);
+    const int tot = (n + stp - 1) / stp;
+    for (int i = tid; i < nwords; i += blockDim.x) g[i] = 0u;
+    if (tid == 0) s_vis = 0;
+    __syncthreads();
+    double u0 = 1e9, v0 = 1e9, u1 = -1e9, v1 = -1e9;
+    int trunc = 0;
+    // each thread takes a run of consecutive points: neighbouring cloud points paint the same
+    // words, which the thread then finds painted already, and the lanes of a warp work on
+    // distant parts of the cloud instead of contending for one word
+    const int per = (tot + (int)blockDim.x - 1) / (int)blockDim.x;
+    for (int s = tid * per, s_end = min(tot, s + per); s < s_end; ++s) {
+      if (!INB((size_t)s * stp, n, 801)) continue;
+      const float4 pt = pts[(size_t)s * stp];
+      const double p0 = C.org[0] + (double)pt.x - T[3], p1 = C.org[1] + (double)pt.y - T[7],
+                   p2 = C.org[2] + (double)pt.z - T[11];
+      const double cx = T[0] * p0 + T[4] * p1 + T[8] * p2, cy = T[1] * p0 + T[5] * p1 + T[9] * p2,
+                   cz = T[2] * p0 + T[6] * p1 + T[10] * p2;
+      if (cz < 0.15) continue;
+      const double ud = (double)F.fx * cx / cz + (double)F.cx, vd = (double)F.fy * cy / cz + (double)F.cy;
+      if (ud < 0 || vd < 0 || ud >= F.w || vd >= F.h) { trunc = 1; continue; }
+      const float d = reenc_depth(F, (int)ud, (int)vd, step, stp_mv, host_reads);
+      if (!(d > 0) || d < cz - 0.08) continue;
+      {   // append the depth: one shared-memory atomic per warp
+        const unsigned am = __activemask();
+        const int lane = tid & 31, lead = __ffs(am) - 1;
+        int zb = 0;
+        if (lane == lead) zb = atomicAdd(&s_vis, __popc(am));
+        const int zi = __shfl_sync(am, zb, lead) + __popc(am & ((1u << lane) - 1u));
+        if (INB(zi, RE_ZMAX, 802)) zs[zi] = (float)cz;
+      }
+      // detection pixel -> mask cells, painted over the voxel's footprint.  The reference divides
+      // by the detection/depth scale and the mask scale and subtracts the mask offset; with the
+      // mask grid equal to the image grid those are divisions by 1.0 and subtractions of 0.0,
+      // exact identities, so they are left out.
+      const double ui = ud, vi = vd;
+      const double rpx = 0.6 * P.voxel * (double)F.fx / cz;
+      const int i0 = (int)floor(ui - rpx), i1 = (int)floor(ui + rpx);
+      const int j0 = (int)floor(vi - rpx), j1 = (int)floor(vi + rpx);
+      const int ia = max(0, i0), ib = min(mw - 1, i1);
+      for (int jj = max(0, j0); jj <= min(mh - 1, j1); ++jj) {
+        uint32_t* row = g + (size_t)jj * wpr;
+        for (int u = ia; u <= ib;) {
+          const int w = u >> 5, e = min(ib, (w << 5) + 31);
+          const uint32_t bits = (e - u == 31) ? 0xffffffffu : (((1u << (e - u + 1)) - 1u) << (u & 31));
+          if ((row[w] & bits) != bits) atomicOr(&row[w], bits);
+          u = e + 1;
+        }
+      }
+      u0 = fmin(u0, ui); u1 = fmax(u1, ui); v0 = fmin(v0, vi); v1 = fmax(v1, vi);
+      if (ui <= 2 || vi <= 2 || ui >= img_w - 3 || vi >= img_h - 3) trunc = 1;
+    }
+    trunc = __syncthreads_or(trunc);
+    const int vis = s_vis;
+    u0 = block_min_d(u0, bs); u1 = block_max_d(u1, bs);
+    v0 = block_min_d(v0, bs); v1 = block_max_d(v1, bs);
+    bool ok = tot > 0 && vis >= 12;
+    const double vfrac = ok ? (double)vis / tot : 0.0;
+    ok = ok && !(vfrac < P.reenc_min_vis);
+    double size_px = 0;
+    if (ok) {   // closing by one cell, written to the candidate's output slot; area of the result
+      uint32_t* out = B.reenc_bits + ((size_t)m * RE_CAND + j) * B.re_words;
+      const uint32_t tail = (mw & 31) ? (1u << (mw & 31)) - 1u : 0xffffffffu;
+      long long area = 0;
+      for (int t = tid; t < nwords; t += blockDim.x) {
+        const int r = t / wpr, w = t - r * wpr;
+        uint32_t s0 = 0, s1 = 0, s2 = 0;
+        auto add = [&](uint32_t x) { const uint32_t c0 = s0 & x; s0 ^= x; const uint32_t c1 = s1 & c0; s1 ^= c0; s2 |= c1; };
+        for (int dr = -1; dr <= 1; ++dr) {
+          const int rr = r + dr;
+          if (rr < 0 || rr >= mh) continue;
+          const uint32_t* row = g + (size_t)rr * wpr;
+          const uint32_t c = row[w], l = w > 0 ? row[w - 1] : 0u, h = w + 1 < wpr ? row[w + 1] : 0u;
+          add((c << 1) | (l >> 31));   // left neighbour (column - 1)
+          add((c >> 1) | (h << 31));   // right neighbour (column + 1)
+          if (dr != 0) add(c);
+        }
+        uint32_t g2 = g[t] | s2 | (s1 & s0);   // painted, or >= 3 painted neighbours
+        if (w == wpr - 1) g2 &= tail;
+        out[t] = g2;
+        area += __popc(g2);
+      }
+      area = block_sum_ll(area, bs);
+      size_px = sqrt((double)area * (double)msx * (double)msy);
+      ok = !(size_px < (double)P.reenc_min_px);
+    }
+    float zmed = 0.f;
+    if (ok) zmed = block_select_f(zs, min(vis, RE_ZMAX), vis / 2, s_hist, s_pick);
+    if (tid == 0) {
+      ReencRec rc;
+      rc.id = o.id;
+      rc.ok = 0;
+      rc.prio = 0;
+      rc.kappa = 0.f;
+      rc.mask_w = mw;
+      rc.mask_h = mh;
+      if (ok) {
+        // ViewQuality holds float fields (bestview.hpp:58-64)
+        const float size_f = (float)size_px, vis_f = (float)vfrac;
+        const double kap = view_kappa_vis(P, (double)fmaxf(0.f, size_f), trunc != 0, (double)fmaxf(0.f, zmed), (double)vis_f, F.blur_fac);
+        const bool need = o.need_whole != 0;
+        if (need || !(kap < P.reenc_gain * o.whole_kappa)) {
+          rc.ok = 1;
+          rc.prio = (need ? 1e6 : 0.0) + kap / dmax2(1.0, o.whole_kappa);
+          rc.kappa = (float)kap;
+          rc.box[0] = (float)dmax2(0.0, u0 - 2);
+          rc.box[1] = (float)dmax2(0.0, v0 - 2);
+          rc.box[2] = (float)dmin2((double)img_w, u1 + 2);
+          rc.box[3] = (float)dmin2((double)img_h, v1 + 2);
+          for (int k = 0; k < 6; ++k) rc.cam[k] = k < 3 ? T[4 * k + 3] : T[4 * (k - 3) + 2];
+        }
+      }
+      recs[j] = rc;
+    }
+    __syncthreads();
+  }
+  host_reads = __reduce_add_sync(0xffffffffu, host_reads);
+  if ((tid & 31) == 0 && host_reads) wk_add(R, SMG_WK_H2D, 4LL * host_reads);
+
+  // the last CTA of the map ranks the candidates
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(&R->re_done, 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  int n_ok = 0;
+  for (int j = tid; j < nc; j += blockDim.x) {
+    if (!__ldcg(&recs[j].ok)) continue;
+    ++n_ok;
+    const double pj = __ldcg(&recs[j].prio);
+    int rank = 0;
+    for (int k = 0; k < nc; ++k) {
+      if (k == j || !__ldcg(&recs[k].ok)) continue;
+      const double pk = __ldcg(&recs[k].prio);
+      rank += pk > pj || (pk == pj && k < j);
+    }
+    if (rank < P.reenc_max && INB(rank, RE_CAND, 803)) R->re_rank[rank] = j;
+  }
+  n_ok = block_sum_i(n_ok, bs);
+  if (tid == 0) {
+    const int nreq = min(n_ok, max(0, P.reenc_max));
+    R->re_n = nreq;
+    R->st.n_reenc_req += nreq;
+    R->re_done = 0;
+  }
+}

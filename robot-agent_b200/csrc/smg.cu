@@ -31,6 +31,7 @@
 #include "k_gemm_assoc.cuh"
 #include "k_text.cuh"
 #include "k_gather.cuh"
+#include "k_reenc.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -89,7 +90,7 @@ struct smg_batch {
 
 static const char* k_names[SMG_NUM_KERNELS] = {"k_begin", "k_merge_pairs", "k_merge_apply", "k_obs", "k_obs_finalize", "k_assoc",
                                                "k_update", "k_absent", "k_relink", "k_struct", "k_prune", "k_markview",
-                                               "k_cloud_add", "k_grid"};
+                                               "k_cloud_add", "k_grid", "k_reenc"};
 
 static cudaEvent_t ev_get(smg_batch* b) {
   if (b->ev_pool.empty()) {
@@ -183,6 +184,7 @@ int smg_params_default(smg_params* p) {
   for (int s = 0; s < 2; ++s) { p->shoulder[s][0] = -0.05f; p->shoulder[s][1] = 0.f; p->shoulder[s][2] = 0.25f; }
   p->match_hi = 3.0f; p->vert_nz = 0.7f; p->match_cell = 0.025f; p->dense = 1;
   p->change_bins = 2; p->change_cells = 1; p->still_every = 50;
+  p->reenc_max = 8; p->reenc_gain = 1.3; p->reenc_min_vis = 0.5; p->reenc_min_px = 24;   // objprob.hpp:90-93
   return SMG_OK;
 }
 
@@ -209,8 +211,8 @@ int smg_params_apply(smg_params* p, const char* kv) {
       {"ap_same_p", &p->same_p, 0}, {"ap_merge_p", &p->merge_p, 0}, {"ap_gate", &p->gate, 0}, {"ap_name_tau", &sink_d, 0},
       {"ap_name_wmax", &sink_d, 0}, {"ap_size_w", &sink_d, 0}, {"ap_kappa_ref", &p->kappa_ref, 0}, {"ap_temper", &p->temper, 0},
       {"ap_wall_big", &sink_d, 0}, {"ap_struct_p", &sink_d, 0}, {"ap_ceil_z", &p->ceil_z, 0}, {"ap_struct_obj_p", &p->struct_obj_p, 0},
-      {"ap_obj_wall_span", &p->obj_wall_span, 0}, {"ap_obj_wall_top", &p->obj_wall_top, 0}, {"ap_reenc_max", 0, &sink_i},
-      {"ap_reenc_gain", &sink_d, 0}, {"ap_link_cos", &p->link_cos, 0}, {"ap_whole_w", &sink_d, 0}, {"ap_export_named", 0, &sink_i},
+      {"ap_obj_wall_span", &p->obj_wall_span, 0}, {"ap_obj_wall_top", &p->obj_wall_top, 0}, {"ap_reenc_max", 0, &p->reenc_max},
+      {"ap_reenc_gain", &p->reenc_gain, 0}, {"ap_link_cos", &p->link_cos, 0}, {"ap_whole_w", &sink_d, 0}, {"ap_export_named", 0, &sink_i},
       {"ap_guard_obj", &p->guard_obj, 0}, {"ap_guard_obs", &p->guard_obs, 0}, {"ap_geo_w", &sink_d, 0},
       {"ap_name_veto", &p->name_veto, 0}, {"ap_through_d", &sink_d, 0}, {"ap_bridge_max", &sink_d, 0},
       {"ap_frame_group", 0, &p->frame_group}, {"ap_struct_obj_min_views", 0, &p->struct_obj_min_views},
@@ -295,7 +297,8 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
                int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out) {
   if (!p || !out || n_maps <= 0 || max_objects <= 0 || emb_dim <= 0 || emb_dim > 2048 || max_w <= 0 || max_h <= 0 || max_det <= 0 ||
       max_det > SMG_MAX_DET || grid_w <= 0 || grid_h <= 0 || p->topk <= 0 || p->topk > SMG_TOPK_MAX || p->bins <= 0 ||
-      p->bins > SMG_BINS_MAX || max_objects > PRUNE_MAX || p->cloud_cap <= 0 || p->voxel <= 0 || p->ransac_iters > RANSAC_MAX)
+      p->bins > SMG_BINS_MAX || max_objects > PRUNE_MAX || p->cloud_cap <= 0 || p->voxel <= 0 || p->ransac_iters > RANSAC_MAX ||
+      (size_t)max_h * ((max_w + 31) / 32) * 4 + RE_ZMAX * 4 > 227 * 1024)   // re-encode mask held in shared memory
     return fail(SMG_ERR_ARGS, "smg_create: bad arguments");
   *out = nullptr;
   int ndev = 0;
@@ -378,6 +381,9 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.mcand_n, M);
   DA(B.mgl, (size_t)M * MGL_CAP);
   DA(B.mgl_n, 2 * (size_t)M);
+  B.re_words = (size_t)max_h * ((max_w + 31) >> 5);
+  DA(B.reenc, (size_t)M * RE_CAND);
+  DA(B.reenc_bits, (size_t)M * RE_CAND * B.re_words);
   DA(B.pcache, (size_t)M * PCACHE_SLOTS);
   DA(B.sscr, (size_t)M * STRUCT_CTAS * STRUCT_SCR);
   DA(B.upd_job, MD);
@@ -495,6 +501,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
     CK(cudaFuncSetAttribute(k_relink, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 8 * RELINK_STAGE));
     CK(cudaFuncSetAttribute(k_update, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UPD_SMEM(B)));
     CK(cudaFuncSetAttribute(k_struct, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)STRUCT_SMEM));
+    CK(cudaFuncSetAttribute(k_reenc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)RE_SMEM(B)));
   }
   CK(cudaDeviceSynchronize());
   *out = b;
@@ -588,8 +595,12 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   k_cloud_add<<<dim3(WORK_SLOTS, Mg), 512, 0, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({12, {e0, e1}}); } }
+  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  k_reenc<<<dim3(RE_CTAS, Mg), RE_THREADS, RE_SMEM(B), st>>>(B);
+  if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
+  if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({14, {e0, e1}}); } }
   CK(cudaStreamWaitEvent(st, ejoin, 0));   // join
-  b->launches += 16;
+  b->launches += 17;
   return SMG_OK;
 }
 
@@ -810,6 +821,48 @@ static int sync_b(smg_batch* b) {
 static int read_map(smg_batch* b, int m, MapRec* R) {
   CK(cudaMemcpy(R, b->B.maps + m, sizeof(MapRec), cudaMemcpyDeviceToHost));
   return SMG_OK;
+}
+
+int smg_get_reencode(smg_batch* b, int m, smg_reenc_req* reqs, uint32_t* bits, int cap) {
+  if (!b || m < 0 || m >= b->B.M || cap < 0) return fail(SMG_ERR_ARGS, "smg_get_reencode: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  const int n = std::max(0, std::min(R.re_n, RE_CAND));
+  const size_t ostride = ((size_t)b->max_w * b->max_h + 31) / 32;
+  std::vector<uint32_t> pad(B.re_words);
+  for (int r = 0; r < n && r < cap; ++r) {
+    const int j = R.re_rank[r];
+    if (j < 0 || j >= RE_CAND) return fail(SMG_ERR_DEVICE, "smg_get_reencode: bad rank");
+    ReencRec rc;
+    CK(cudaMemcpy(&rc, B.reenc + (size_t)m * RE_CAND + j, sizeof(rc), cudaMemcpyDeviceToHost));
+    if (reqs) {
+      smg_reenc_req& q = reqs[r];
+      q.id = rc.id;
+      for (int k = 0; k < 4; ++k) q.box[k] = rc.box[k];
+      q.kappa = rc.kappa;
+      for (int k = 0; k < 6; ++k) q.cam[k] = rc.cam[k];
+      q.mask_w = rc.mask_w;
+      q.mask_h = rc.mask_h;
+    }
+    if (bits) {   // rows padded to whole words on the device -> one row-major bit string
+      const int mw = rc.mask_w, mh = rc.mask_h, wpr = (mw + 31) >> 5;
+      if (mw <= 0 || mh <= 0 || (size_t)mh * wpr > B.re_words) return fail(SMG_ERR_DEVICE, "smg_get_reencode: bad mask size");
+      CK(cudaMemcpy(pad.data(), B.reenc_bits + ((size_t)m * RE_CAND + j) * B.re_words, sizeof(uint32_t) * (size_t)mh * wpr,
+                    cudaMemcpyDeviceToHost));
+      uint32_t* o = bits + (size_t)r * ostride;
+      const size_t nw = ((size_t)mw * mh + 31) / 32;
+      std::fill(o, o + nw, 0u);
+      for (int y = 0; y < mh; ++y)
+        for (int x = 0; x < mw; ++x)
+          if ((pad[(size_t)y * wpr + (x >> 5)] >> (x & 31)) & 1u) {
+            const size_t q = (size_t)y * mw + x;
+            o[q >> 5] |= 1u << (q & 31);
+          }
+    }
+  }
+  return n;
 }
 
 int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap) {

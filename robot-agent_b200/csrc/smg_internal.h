@@ -21,6 +21,7 @@
 #include "../../include/smg.h"
 
 #define SMG_MAX_DET 64
+#define RE_CAND SMG_MAX_DET   // re-encode candidates per keyframe: objects seen this keyframe (<= detections)
 #define SMG_TOPK_MAX 8
 #define SMG_CAMS 32
 #define SMG_CEIL_OBS 400
@@ -39,6 +40,7 @@
 #define SMG_E_CAP_VIEW 8
 #define SMG_E_CAP_EVENTS 16
 #define SMG_E_ARGS 32
+#define SMG_E_CAP_REENC 64   // more re-encode candidates in a keyframe than RE_CAND
 
 // Per (map, frame) input descriptor on the device (smg_frame + host-derived scalars).
 typedef struct {
@@ -199,7 +201,21 @@ typedef struct {
   int32_t view_n;
   // cumulative work counters (algorithmic traffic of the path; see SMG_WK_*)
   long long wk[SMG_WORK_N];
+  // whole-object re-encode requests of the last keyframe (k_reenc): count, candidate of each rank
+  int32_t re_n, re_done;
+  int32_t re_rank[RE_CAND];
 } MapRec;
+
+// Whole-object re-encode candidate of a keyframe (ReencReq, scenemap objmap.hpp:142-148, plus
+// the ranking key); the mask bits live in Batch::reenc_bits, rows padded to whole words.
+typedef struct {
+  uint32_t id;
+  int32_t ok;            // passed every test of buildReencode
+  double prio;
+  float kappa, box[4];
+  double cam[6];
+  int32_t mask_w, mask_h;
+} ReencRec;
 
 // ObjectMap::lastAssoc entry (DetAssoc, objmap.hpp:194-199)
 typedef struct {
@@ -274,6 +290,9 @@ typedef struct {
   uint32_t* mcand_key;   // [M*O*8] list positions i << 16 | j (the reference's enumeration order)
   int32_t* mcand_n;      // [M]
   int32_t* mgl;          // [M*MGL_CAP] gated merge pairs of the frame, i << 16 | j
+  ReencRec* reenc;       // [M*RE_CAND]
+  uint32_t* reenc_bits;  // [M*RE_CAND*re_words] closed masks, rows padded to whole words
+  size_t re_words;       // H * ceil(W / 32)
   int32_t* mgl_n;        // [M] gated pairs; [M] next pair a warp takes (mgl_n + M)
   struct PairCacheRec* pcache;   // [M * PCACHE_SLOTS] merge-pass pair features of unchanged pairs
   double* sscr;          // [M * STRUCT_CTAS * STRUCT_SCR] k_struct scratch

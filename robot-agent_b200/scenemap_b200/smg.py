@@ -29,6 +29,11 @@ class SmgFrame(C.Structure):
                 ("score", C.c_void_p), ("emb", C.c_void_p), ("emb_dtype", C.c_int32)]
 
 
+class SmgReencReq(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("box", C.c_float * 4), ("kappa", C.c_float), ("cam", C.c_double * 6),
+                ("mask_w", C.c_int32), ("mask_h", C.c_int32)]
+
+
 class SmgObject(C.Structure):
     _fields_ = [("id", C.c_uint32), ("cls", C.c_int32), ("pos", C.c_double * 3), ("ext", C.c_double * 3),
                 ("first_pos", C.c_double * 3), ("lo", C.c_double * 3), ("hi", C.c_double * 3), ("n_obs", C.c_uint32),
@@ -68,6 +73,7 @@ def lib():
         L.smg_error_word.argtypes = [vp]
         L.smg_last_error.restype = C.c_char_p
         L.smg_get_assoc_all.argtypes = [vp, vp]
+        L.smg_get_reencode.argtypes = [vp, C.c_int, vp, vp, C.c_int]
         L.smg_debug_check.argtypes = [vp, vp]
         L.smg_timing_enable.argtypes = [vp, C.c_int]
         L.smg_timing_read.argtypes = [vp, vp, vp, vp]
@@ -86,9 +92,9 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
             "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
            "smg_get_work", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
-           "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name"]
+           "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode"]
 
-NUM_KERNELS = 14
+NUM_KERNELS = 15
 
 
 def _ptr(a):
@@ -127,6 +133,7 @@ class Batch:
         if cloud_cap is not None:   # ObjectMap::setCloudParams (objmap.hpp:255-258)
             _check(L.smg_params_set_cloud(self.params.buf, 0.0, int(cloud_cap)), "smg_params_set_cloud")
         self.n_maps, self.max_objects, self.D, self.max_det = n_maps, max_objects, emb_dim, max_det
+        self.max_w, self.max_h = max_w, max_h
         self.grid = grid
         h = C.c_void_p()
         _check(L.smg_create(self.params.buf, n_maps, max_objects, emb_dim, max_w, max_h, max_det, grid[0], grid[1],
@@ -259,6 +266,23 @@ class Batch:
         o = np.zeros(3, np.int32)
         _check(lib().smg_get_keyframe(self.h, m, _ptr(o)), "smg_get_keyframe")
         return dict(inserted=int(o[0]), changed=int(o[1]), n_hits=int(o[2]))
+
+    def reencode(self, m: int = 0) -> dict:
+        """Whole-object re-encode requests of map m's last keyframe (smg_get_reencode), best first:
+        id, box, kappa, cam and the row-major mask bits (ceil(w * h / 32) words per request)."""
+        L = lib()
+        n = _check(L.smg_get_reencode(self.h, m, None, None, 0), "smg_get_reencode")
+        k = max(n, 1)
+        stride = (self.max_w * self.max_h + 31) // 32
+        reqs = (SmgReencReq * k)()
+        bits = np.zeros((k, stride), np.uint32)
+        _check(L.smg_get_reencode(self.h, m, reqs, _ptr(bits), n), "smg_get_reencode")
+        nw = (reqs[0].mask_w * reqs[0].mask_h + 31) // 32 if n else 0
+        return dict(id=np.array([reqs[r].id for r in range(n)], np.uint32),
+                    box=np.array([list(reqs[r].box) for r in range(n)], np.float32).reshape(n, 4),
+                    kappa=np.array([reqs[r].kappa for r in range(n)], np.float32),
+                    cam=np.array([list(reqs[r].cam) for r in range(n)], np.float64).reshape(n, 6),
+                    bits=bits[:n, :nw])
 
     def assoc_all(self) -> np.ndarray:
         out = np.zeros(self.n_maps * self.max_det, np.uint32)

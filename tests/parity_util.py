@@ -79,6 +79,13 @@ def compare_frame(ref, gpu, m: int, D: int, deep: bool = False) -> list:
         errs.append(f"events ref={re_new} gpu={ge}")
     ro, go = ref.objects(), gpu.objects(m)
     errs += compare_objects(ro, go)
+    rr, gr = ref.reenc(), gpu.reencode(m)   # buildReencode requests, best first
+    if not np.array_equal(rr["id"], gr["id"]):
+        errs.append(f"reencode ids ref={rr['id'].tolist()} gpu={gr['id'].tolist()}")
+    else:
+        for k in ("box", "kappa", "cam", "bits"):
+            if len(rr["id"]) and not np.array_equal(rr[k], gr[k]):
+                errs.append(f"reencode {k} differs")
     rk, gk = ref.kf(), gpu.keyframe(m)
     if rk != gk:
         errs.append(f"keyframe ref={rk} gpu={gk}")

@@ -41,6 +41,7 @@ def _run(groups: int, M: int, N: int, D: int, pinned: bool = False):
             frs = [_pinned(fr) for fr in frs]
         B.push(frs, smg.SMG_MEM_HOST, smg.SMG_EMB_BF16)   # host inputs: copied group by group
         trace.append(B.assoc_all().copy())
+        trace.append([B.reencode(m) for m in range(M)])   # re-encode masks read host depth when gathered
     out = {"assoc": trace, "err": B.error_word()}
     for m in range(M):
         out[f"obj{m}"] = B.objects(m)
