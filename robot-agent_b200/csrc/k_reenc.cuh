@@ -16,7 +16,9 @@
 // is a bitset in shared memory with rows padded to whole 32-bit words; the closing runs on
 // whole words (the eight neighbour words are shifted copies of three rows, counted by a
 // saturating bit-sliced adder) and writes the closed mask straight to the candidate's output
-// slot, row-padded, so no second mask is held on chip.  The median depth is an exact radix
+// slot, row-padded, so no second mask is held on chip.  Only the window of painted cells plus a
+// one-cell ring is closed and written (no cell outside it has a painted neighbour); the window
+// goes with the request and the reader zero-fills the rest.  The median depth is an exact radix
 // selection over the visible depths kept in shared memory.  The last CTA of a map to finish
 // ranks the candidates: priority descending, list order on equal priority (the reference's
 // std::sort leaves the order of equal priorities unspecified).
@@ -24,7 +26,7 @@
 #include "dev_util.cuh"
 
 #define RE_THREADS 256
-#define RE_CTAS 8       // CTAs per map
+#define RE_CTAS 16      // CTAs per map (a keyframe has about one candidate per detection)
 #define RE_ZMAX 6000    // sampled points per object: ceil(n / max(1, n / 3000)) < 6000 for every n
 // dynamic shared memory: the row-padded mask of the largest frame plus the visible depths
 #define RE_SMEM(B) ((size_t)(B).H * ((((B).W) + 31) >> 5) * 4 + (size_t)RE_ZMAX * 4)
@@ -44,9 +46,14 @@ DEV float block_select_f(const float* a, int n, int k, int* hist, int* s_pick) {
   for (int sh = 24; sh >= 0; sh -= 8) {
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) {
-      const uint32_t key = f_ord(a[i]);
-      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> sh) & 255u], 1);
+    for (int base = 0; base < n; base += blockDim.x) {   // one atomic per distinct bin of a warp
+      const int i = base + tid;
+      uint32_t key = 0;
+      bool in = false;
+      if (i < n) { key = f_ord(a[i]); in = (key & pmask) == prefix; }
+      const uint32_t bin = (key >> sh) & 255u;
+      const unsigned grp = __match_any_sync(0xffffffffu, in ? bin : 256u + (tid & 31));
+      if (in && (tid & 31) == __ffs(grp) - 1) atomicAdd(&hist[bin], __popc(grp));
     }
     __syncthreads();
     if (tid < 32) {   // warp 0: the bin holding rank k (eight bins per lane)
@@ -151,6 +158,8 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
 
   ReencRec* recs = B.reenc + (size_t)m * RE_CAND;
   int host_reads = 0;
+  for (int i = tid; i < nwords; i += blockDim.x) g[i] = 0u;   // later candidates clear their window
+  __syncthreads();
   for (int q = 0; (int)blockIdx.x + q * (int)gridDim.x < nc; ++q) {
     const int j = blockIdx.x + q * gridDim.x;
     const int b = s_cand[q];
@@ -161,11 +170,11 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
     const int n = C.n;
     const int stp = max(1, n / 3000);
     const int tot = (n + stp - 1) / stp;
-    for (int i = tid; i < nwords; i += blockDim.x) g[i] = 0u;
     if (tid == 0) s_vis = 0;
     __syncthreads();
     double u0 = 1e9, v0 = 1e9, u1 = -1e9, v1 = -1e9;
     int trunc = 0;
+    int pi0 = INT_MAX, pi1 = -1, pj0 = INT_MAX, pj1 = -1;   // painted cells of this thread
     // each thread takes a run of consecutive points: neighbouring cloud points paint the same
     // words, which the thread then finds painted already, and the lanes of a warp work on
     // distant parts of the cloud instead of contending for one word
@@ -198,8 +207,9 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
       const double rpx = 0.6 * P.voxel * (double)F.fx / cz;
       const int i0 = (int)floor(ui - rpx), i1 = (int)floor(ui + rpx);
       const int j0 = (int)floor(vi - rpx), j1 = (int)floor(vi + rpx);
-      const int ia = max(0, i0), ib = min(mw - 1, i1);
-      for (int jj = max(0, j0); jj <= min(mh - 1, j1); ++jj) {
+      const int ia = max(0, i0), ib = min(mw - 1, i1), ja = max(0, j0), jb = min(mh - 1, j1);
+      if (ia <= ib && ja <= jb) { pi0 = min(pi0, ia); pi1 = max(pi1, ib); pj0 = min(pj0, ja); pj1 = max(pj1, jb); }
+      for (int jj = ja; jj <= jb; ++jj) {
         uint32_t* row = g + (size_t)jj * wpr;
         for (int u = ia; u <= ib;) {
           const int w = u >> 5, e = min(ib, (w << 5) + 31);
@@ -215,6 +225,13 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
     const int vis = s_vis;
     u0 = block_min_d(u0, bs); u1 = block_max_d(u1, bs);
     v0 = block_min_d(v0, bs); v1 = block_max_d(v1, bs);
+    // window of the closing: painted cells plus a one-cell ring, in whole words
+    pi0 = (int)block_min_d((double)pi0, bs); pi1 = (int)block_max_d((double)pi1, bs);
+    pj0 = (int)block_min_d((double)pj0, bs); pj1 = (int)block_max_d((double)pj1, bs);
+    const bool painted = pi1 >= 0;
+    const int r0 = painted ? max(0, pj0 - 1) : 0, r1 = painted ? min(mh - 1, pj1 + 1) : -1;
+    const int w0 = painted ? max(0, pi0 - 1) >> 5 : 0, w1 = painted ? min(mw - 1, pi1 + 1) >> 5 : -1;
+    const int nww = w1 - w0 + 1, nwin = painted ? (r1 - r0 + 1) * nww : 0;
     bool ok = tot > 0 && vis >= 12;
     const double vfrac = ok ? (double)vis / tot : 0.0;
     ok = ok && !(vfrac < P.reenc_min_vis);
@@ -223,8 +240,8 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
       uint32_t* out = B.reenc_bits + ((size_t)m * RE_CAND + j) * B.re_words;
       const uint32_t tail = (mw & 31) ? (1u << (mw & 31)) - 1u : 0xffffffffu;
       long long area = 0;
-      for (int t = tid; t < nwords; t += blockDim.x) {
-        const int r = t / wpr, w = t - r * wpr;
+      for (int t = tid; t < nwin; t += blockDim.x) {
+        const int r = r0 + t / nww, w = w0 + t % nww;
         uint32_t s0 = 0, s1 = 0, s2 = 0;
         auto add = [&](uint32_t x) { const uint32_t c0 = s0 & x; s0 ^= x; const uint32_t c1 = s1 & c0; s1 ^= c0; s2 |= c1; };
         for (int dr = -1; dr <= 1; ++dr) {
@@ -236,9 +253,9 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
           add((c >> 1) | (h << 31));   // right neighbour (column + 1)
           if (dr != 0) add(c);
         }
-        uint32_t g2 = g[t] | s2 | (s1 & s0);   // painted, or >= 3 painted neighbours
+        uint32_t g2 = g[(size_t)r * wpr + w] | s2 | (s1 & s0);   // painted, or >= 3 painted neighbours
         if (w == wpr - 1) g2 &= tail;
-        out[t] = g2;
+        out[(size_t)r * wpr + w] = g2;
         area += __popc(g2);
       }
       area = block_sum_ll(area, bs);
@@ -255,6 +272,7 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
       rc.kappa = 0.f;
       rc.mask_w = mw;
       rc.mask_h = mh;
+      rc.win[0] = r0; rc.win[1] = r1; rc.win[2] = w0; rc.win[3] = w1;
       if (ok) {
         // ViewQuality holds float fields (bestview.hpp:58-64)
         const float size_f = (float)size_px, vis_f = (float)vfrac;
@@ -273,6 +291,7 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
       }
       recs[j] = rc;
     }
+    for (int t = tid; t < nwin; t += blockDim.x) g[(size_t)(r0 + t / nww) * wpr + w0 + t % nww] = 0u;   // painted cells lie inside
     __syncthreads();
   }
   host_reads = __reduce_add_sync(0xffffffffu, host_reads);

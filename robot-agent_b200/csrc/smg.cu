@@ -854,8 +854,11 @@ int smg_get_reencode(smg_batch* b, int m, smg_reenc_req* reqs, uint32_t* bits, i
       uint32_t* o = bits + (size_t)r * ostride;
       const size_t nw = ((size_t)mw * mh + 31) / 32;
       std::fill(o, o + nw, 0u);
-      for (int y = 0; y < mh; ++y)
-        for (int x = 0; x < mw; ++x)
+      // only the closing window was written (every other cell is zero)
+      const int y0 = std::max(0, rc.win[0]), y1 = std::min(mh - 1, rc.win[1]);
+      const int x0 = std::max(0, rc.win[2] * 32), x1 = std::min(mw - 1, rc.win[3] * 32 + 31);
+      for (int y = y0; y <= y1; ++y)
+        for (int x = x0; x <= x1; ++x)
           if ((pad[(size_t)y * wpr + (x >> 5)] >> (x & 31)) & 1u) {
             const size_t q = (size_t)y * mw + x;
             o[q >> 5] |= 1u << (q & 31);

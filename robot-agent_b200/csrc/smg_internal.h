@@ -215,6 +215,7 @@ typedef struct {
   float kappa, box[4];
   double cam[6];
   int32_t mask_w, mask_h;
+  int32_t win[4];        // rows r0..r1 and words w0..w1 written to the mask slot (zero elsewhere)
 } ReencRec;
 
 // ObjectMap::lastAssoc entry (DetAssoc, objmap.hpp:194-199)
