@@ -489,6 +489,7 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     cfg = {"workload": "config 1: 64 box-room maps per GPU, 640x480 fp32 depth + u16 labels, 8-24 dets, "
                        f"1152-d bf16 embeddings, <={args.max_objects} object slots, 512x512 grid",
+           "keyframe": "Mapper2D::keyframe + ObjectMap::update + addPoints + buildReencode (capi.cpp:811-1010)",
            "maps_per_gpu": args.maps, "frames_timed": f"{args.preroll + args.warmup}..{args.preroll + args.warmup + args.steps - 1}",
            "l2": "fresh frames every step (118 MB/step at 64 maps), no flush", "parallelism": f"dp{world} (maps)"}
     if args.impl == "reference":
