@@ -84,6 +84,7 @@ def ref_lib():
         L.ref_reenc.argtypes = [C.c_void_p, P(C.c_uint32), P(C.c_float), P(C.c_float), P(C.c_double), P(C.c_uint32),
                                 C.c_int]
         L.ref_reenc_words.argtypes = [C.c_void_p]
+        L.ref_add_whole_views.argtypes = [C.c_void_p, P(C.c_uint32), P(C.c_float), C.c_int, C.c_int, C.c_double]
         L.ref_grid_geom.argtypes = [C.c_void_p, P(C.c_int32)]
         L.ref_grid_cells.argtypes = [C.c_void_p, P(C.c_int16), P(C.c_uint8), P(C.c_int8)]
         L.ref_occ_create.restype = C.c_void_p
@@ -259,6 +260,13 @@ class RefMap:
         L.ref_reenc(self._h, _p(ids, C.c_uint32), _p(box, C.c_float), _p(kap, C.c_float), _p(cam, C.c_double),
                     _p(bits, C.c_uint32), n)
         return dict(id=ids[:n], box=box[:n], kappa=kap[:n], cam=cam[:n], bits=bits[:n, :nw])
+
+    def add_whole_views(self, ids, emb, stamp: float) -> int:
+        """Answer the last keyframe's requests (sm_set_object_embeddings): one L2 embedding per id."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        emb = np.ascontiguousarray(emb, np.float32)
+        return ref_lib().ref_add_whole_views(self._h, _p(ids, C.c_uint32), _p(emb, C.c_float), len(ids),
+                                             emb.shape[1] if emb.ndim == 2 else 0, stamp)
 
     def kf(self):
         o = np.zeros(3, np.int32)

@@ -202,6 +202,22 @@ int ref_reenc(void* h, uint32_t* id, float* box, float* kappa, double* cam, uint
 }
 int ref_reenc_words(void* h) { return static_cast<RefMap*>(h)->reenc_words; }
 
+// The caller's answer to the requests (sm_set_object_embeddings, scenemap capi.cpp:1825-1835):
+// whole-object embedding i of object ids[i] is added with the kappa and camera of its request,
+// at the request frame's stamp; ids without a request are skipped.  Returns the number added.
+int ref_add_whole_views(void* h, const uint32_t* ids, const float* emb, int n, int dim, double stamp) {
+  RefMap* m = static_cast<RefMap*>(h);
+  int added = 0;
+  for (int i = 0; i < n; ++i) {
+    const ReencReq* r = nullptr;
+    for (const ReencReq& q : m->reenc) if (q.id == ids[i]) { r = &q; break; }
+    if (!r) continue;
+    m->om.addWholeView(ids[i], emb + size_t(i) * dim, dim, r->kappa, stamp, r->cam);
+    ++added;
+  }
+  return added;
+}
+
 int ref_n_objects(void* h) { return int(static_cast<RefMap*>(h)->om.objects().size()); }
 
 int ref_objects(void* h, rf_obj* out, int cap) {
