@@ -22,6 +22,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -104,13 +105,19 @@ def parse():
     ap.add_argument("--maps", type=int, default=None, help="maps per GPU (default 64 for objprob, 1 for occ)")
     ap.add_argument("--max-objects", type=int, default=1024)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-frames", type=int, default=30, help="CPU baseline: frames per map (untimed lead-in + timed)")
-    ap.add_argument("--cpu-timed", type=int, default=10, help="CPU baseline: timed frames per map")
+    ap.add_argument("--cpu-timed", type=int, default=10,
+                    help="CPU baseline: timed keyframes per map (the first of the device arm's timed frames)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="objprob", choices=["objprob", "occ", "assoc"],
                     help="objprob = config 1 (headline); occ = config 3 (grid insert + correlative scan matching); "
                          "assoc = config 2 (association GEMM)")
     ap.add_argument("--scans", type=int, default=5000, help="config 3: scans per map")
+    ap.add_argument("--check-run", type=int, default=0, metavar="FRAMES",
+                    help="checked run instead of the benchmark: push --maps maps (device-resident config-1 frames, "
+                         "--max-objects slots) for FRAMES keyframes; after every 16 frames print the device error word "
+                         "and the first failed bounds check (nonzero only in a -DSMG_CHECKS library, chosen with the "
+                         "SMG_LIB environment variable) and stop at the first nonzero one.  Also the small case that "
+                         "ncu captures are taken on")
     return ap.parse_args()
 
 
@@ -156,63 +163,59 @@ class Clocks:
 
 
 # ------------------------------------------------------------------ CPU baseline (reference scenemap code)
-def cpu_reference(M_sample: int, frames: int, timed: int, threads: int, base_seed: int = 1000):
+def cpu_reference(M_sample: int, lead: int, timed: int, threads: int, base_seed: int = 1000, obj_kv: str = ""):
     """The reference scenemap (oracle/_ref, compiled from the reference sources) on the host cores:
-    one map per thread; each map runs `frames` keyframes, the last `timed` of which are timed.
-    Inputs come from the same generator (device renderer when a GPU is present, else host)."""
+    one map per thread.  Every map runs `lead` untimed keyframes, then `timed` timed ones: the
+    same frames (same seeds, same frame indices) the device arm pre-rolls and times.  Inputs come
+    from the same generator (the device renderer when a GPU is present, else the host one, which
+    renders the same bytes) in chunks of 10 frames; the threads meet at every chunk, and the
+    timed span is the sum over chunks of the slowest thread's timed work in that chunk."""
     from oracle import ref
     from scenemap_b200 import synth
     if not ref.available():
         return None
+    M_sample = min(M_sample, threads)
+    frames = lead + timed
     gen_dev = False
     try:
         import torch
         gen_dev = torch.cuda.is_available()
     except Exception:
         pass
-    inputs = []   # per map: list of frame dicts (host numpy)
     if gen_dev:
         from scenemap_b200.workload import RoomBatch
-        wl = RoomBatch(M_sample, base_seed, frames, D=1152, bf16=True, max_det=24)
-        for f0 in range(0, frames, 10):
-            nf = min(10, frames - f0)
-            R = wl.render(f0, nf)
-            for fi in range(nf):
-                hf = wl.host_frames(R, fi)
-                for m in range(M_sample):
-                    if len(inputs) <= m:
-                        inputs.append([])
-                    inputs[m].append(hf[m])
+        wl = RoomBatch(M_sample, base_seed, frames, D=D_EMB, bf16=True, max_det=24)
     else:
-        for m in range(M_sample):
-            g = synth.BoxRoom(seed=synth.map_seed(base_seed, m), n_frames=frames, bf16=True, max_det=24)
-            inputs.append([g.frame(f) for f in range(frames)])
-    t_timed = [0.0] * M_sample
-    lead = frames - timed
+        gens = [synth.BoxRoom(seed=synth.map_seed(base_seed, m), n_frames=frames, bf16=True, max_det=24)
+                for m in range(M_sample)]
+    maps = [ref.RefMap(obj_kv) for _ in range(M_sample)]
+    span = 0.0
+    for f0 in range(0, frames, 10):
+        nf = min(10, frames - f0)
+        if gen_dev:
+            R = wl.render(f0, nf)
+            chunk = [wl.host_frames(R, fi) for fi in range(nf)]
+        else:
+            chunk = [[g.frame(f0 + fi) for g in gens] for fi in range(nf)]
+        t_m = [0.0] * M_sample
 
-    def work(m):
-        R = ref.RefMap()
-        for f in range(frames):
-            if f == lead:
+        def work(m):
+            for fi in range(nf):
                 t0 = time.perf_counter()
-            R.frame(inputs[m][f])
-        t_timed[m] = time.perf_counter() - t0
+                maps[m].frame(chunk[fi][m])
+                if f0 + fi >= lead:
+                    t_m[m] += time.perf_counter() - t0
 
-    ths = []
-    for start in range(0, M_sample, threads):
-        batch = [threading.Thread(target=work, args=(m,)) for m in range(start, min(M_sample, start + threads))]
-        t0 = time.perf_counter()
-        for t in batch:
+        ths = [threading.Thread(target=work, args=(m,)) for m in range(M_sample)]
+        for t in ths:
             t.start()
-        for t in batch:
+        for t in ths:
             t.join()
-        ths.append(time.perf_counter() - t0)
-    # throughput: timed map-frames over the slowest thread's timed span, per concurrent wave
-    waves = [t_timed[i:i + threads] for i in range(0, M_sample, threads)]
-    value = sum(len(w) * timed for w in waves) / sum(max(w) for w in waves)
-    return dict(value=value, unit=UNIT, cores=threads, kind="reference",
-                sample=f"{M_sample} maps x frames {lead}..{frames - 1} (timed {timed} per map), one map per thread, "
-                       f"reference scenemap C++ (-O2) from oracle/_ref")
+        span += max(t_m)
+    value = M_sample * timed / span
+    return dict(value=value, unit=UNIT, cores=M_sample, kind="reference", frames_timed=f"{lead}..{frames - 1}",
+                sample=f"{M_sample} maps, keyframes {lead}..{frames - 1} timed after {lead} untimed, one map per host "
+                       f"thread, reference scenemap C++ (-O2) from oracle/_ref")
 
 
 # ------------------------------------------------------------------ B200 arm
@@ -251,8 +254,7 @@ def run_b200(args, rank, world, local_rank):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    clk = Clocks(local_rank, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else ".",
-                                          f"clocks_r{rank}.csv"))
+    clk = Clocks(local_rank, os.path.join(tempfile.gettempdir(), f"smg_bench_clocks_{os.getpid()}_r{rank}.csv"))
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -338,6 +340,32 @@ def run_b200(args, rank, world, local_rank):
     B.close()
     return dict(t=t, t_e2e=t_e2e, kt=kt, launches=launches, err=err, clocks=clocks, work=work,
                 stats=all_stats, h2d=h2d, h2d_input=h2d_input, d2h=d2h, n_obj=n_obj)
+
+
+def check_run(args, local_rank):
+    """Checked run of the config-1 workload (see --check-run)."""
+    import torch
+    from scenemap_b200 import smg
+    from scenemap_b200.workload import RoomBatch
+    torch.cuda.set_device(local_rank)
+    M, NF = args.maps, args.check_run
+    wl = RoomBatch(M, 1000, NF, D=D_EMB, bf16=True, max_det=24, device=f"cuda:{local_rank}")
+    B = smg.Batch(M, max_objects=args.max_objects, emb_dim=D_EMB, max_w=640, max_h=480, max_det=24,
+                  grid=(512, 512, -256 + 60, -256 + 50), dev=local_rank)
+    for f0 in range(0, NF, 16):
+        nf = min(16, NF - f0)
+        R = wl.render(f0, nf, 0)
+        for fi in range(nf):
+            keep = []
+            B.push(None, smg.SMG_MEM_DEVICE, structs=wl.structs(R, fi, keep), stream=0)
+        torch.cuda.synchronize()
+        err, chk = B.error_word(), B.debug_check()
+        print("frames", f0, f0 + nf, "err", err, "chk", chk, flush=True)
+        if err or any(chk):
+            B.close()
+            sys.exit(1)
+    print("work", B.work())
+    B.close()
 
 
 def run_occ(args, rank, world, local_rank):
@@ -487,6 +515,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.check_run:
+        check_run(args, local_rank)
+        return
     cfg = {"workload": "config 1: 64 box-room maps per GPU, 640x480 fp32 depth + u16 labels, 8-24 dets, "
                        f"1152-d bf16 embeddings, <={args.max_objects} object slots, 512x512 grid",
            "keyframe": "Mapper2D::keyframe + ObjectMap::update + addPoints + buildReencode (capi.cpp:811-1010)",
@@ -496,16 +527,17 @@ def main():
         if rank != 0:
             return
         cores = os.cpu_count() or 1
-        # K timed keyframes per map after an untimed lead-in of at least W keyframes (the maps
-        # fill up with objects first, as the device arm's pre-roll does)
-        lead = max(args.warmup, args.cpu_frames - args.cpu_timed)
-        cb = cpu_reference(min(max(cores, 8), 64), lead + args.steps, args.steps, min(cores, 64))
+        # the same keyframes the device arm times: frames preroll+W .. preroll+W+K-1 of the same
+        # maps, after the same untimed pre-roll and warm-up frames
+        lead = args.preroll + args.warmup
+        cb = cpu_reference(min(cores, 64), lead, args.steps, min(cores, 64))
         if cb is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libscenemap_ref.so not built"}))
             return
         print(json.dumps({"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-                          "warmup": lead, "higher_is_better": True, "scaling": "weak",
+                          "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
                           "vs_baseline": None, "dtype": "f64/f32", "data": "synthetic", "config": cfg, "impl": "reference",
+                          "frames_timed": cb["frames_timed"],
                           "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                           "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
@@ -574,7 +606,7 @@ def main():
     cb = None
     if not args.no_cpu_baseline and world == 1:
         cores = os.cpu_count() or 1
-        cb = cpu_reference(min(max(cores, 8), 64), args.cpu_frames, args.cpu_timed, min(cores, 64))
+        cb = cpu_reference(min(cores, 64), args.preroll + args.warmup, args.cpu_timed, min(cores, 64))
     out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
            "ms_per_step": 1e3 * r["t"] / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "f64/f32 (bf16 embeddings)", "data": "synthetic", "config": cfg,

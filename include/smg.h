@@ -3,7 +3,7 @@
  * One `smg_batch` holds M independent maps on one GPU: each map is one scenemap
  * (ObjectMap + Mapper2D occupancy grid).  A call to smg_push_frames runs, for every map,
  * the reference keyframe path for one depth frame:
- *   Mapper2D::keyframe  (scenemap src/mapper2d.cpp:100-160: makeScan + OccGrid::insert)
+ *   Mapper2D::keyframe  (scenemap src/mapper2d.cpp:27-87: makeScan + OccGrid::insert)
  *   ObjectMap::update   (scenemap src/objmap.cpp:516-1086)
  *   ObjectMap::addPoints for every emitted observation cloud (scenemap src/capi.cpp:986-992)
  * entirely on the device, on the caller's stream.  Nothing falls back to the CPU: without a
@@ -28,6 +28,7 @@ enum {
   SMG_ERR_PARAM = -2,      /* unknown parameter key */
   SMG_ERR_CAPACITY = -3,   /* an object / point / cell capacity would be exceeded */
   SMG_ERR_DEVICE = -4,     /* CUDA error, or the device error word was set */
+  SMG_ERR_UNSUPPORTED = -5,/* a known reference input or parameter this build does not implement */
 };
 
 enum { SMG_MEM_DEVICE = 0, SMG_MEM_HOST = 1 };
@@ -126,7 +127,13 @@ int smg_params_size(void);
  * scan.hpp:37-48, mapper2d.hpp:14-26). */
 int smg_params_default(smg_params* p);
 /* ObjectMap::applyParams (scenemap src/objmap.cpp:132-205): "key=val,...".  Returns the number
- * of unknown keys (0 = all known), or SMG_ERR_ARGS. */
+ * of unknown keys (0 = all known), or SMG_ERR_ARGS.  Keys of reference features this build does
+ * not run (text-model naming and structural-name rules, wall segments, inspect, the export
+ * filter: ap_name_tau, ap_name_wmax, ap_size_w, ap_wall_big, ap_struct_p, ap_whole_w,
+ * ap_export_named, ap_geo_w, ap_through_d, ap_bridge_max, ap_so_*, ap_wallhug_*,
+ * ap_struct_look_block, ap_flat_max_w, ap_big_vinl, inspect) are accepted at their reference
+ * default only; any other value makes the call return SMG_ERR_UNSUPPORTED (all other keys are
+ * still applied) and smg_last_error names them. */
 int smg_params_apply(smg_params* p, const char* kv);
 
 /* ObjectMap::setCloudParams (scenemap objmap.hpp:255-258): voxel > 0 and cap > 0 override. */
@@ -265,7 +272,7 @@ typedef struct smg_occ smg_occ;
 int smg_occ_create(const smg_occ_params* p, int n_maps, int grid_w, int grid_h, int grid_x0, int grid_y0, int max_points,
                    int dev, smg_occ** out);
 int smg_occ_destroy(smg_occ* o);
-/* OccGrid::insert(scan, pose) (grid.cpp:195-259) for grids 0..n-1; poses = n x (x, y, th).
+/* OccGrid::insert(scan, pose) (grid.cpp:95-159) for grids 0..n-1; poses = n x (x, y, th).
  * changed_out (n, or NULL): the reference's return value (cells whose log-odds or seen flag
  * changed), -1 if the scan left the window (the grid is then unchanged).  With changed_out
  * NULL the call is asynchronous on `stream`. */
@@ -363,7 +370,7 @@ int smg_plane_fit(const float* xyz, const int32_t* off, int n_sets, int n_points
  * (1 MiB) and the iteration table (1 MiB) are static device arrays of the library, held on
  * every GPU that loads it until the process exits.  The first call on each device does a
  * one-time set-up on that device (address look-up and a synchronous table copy), so make that
- * first call before any stream capture.  All calls share the one scratch array: calls that
+ * first call before any stream capture; after a cudaDeviceReset the next call repeats it.  All calls share the one scratch array: calls that
  * can overlap on the GPU (other streams, other host threads) race and must be serialised by
  * the caller.  Nothing in the scratch needs to start at zero, so no call clears it. */
 int smg_plane_fit_noalloc(const float* xyz, const int32_t* off, int n_sets, int n_points, double tau,

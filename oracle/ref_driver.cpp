@@ -2,7 +2,7 @@
 //
 // Drives the reference scenemap C++ code, compiled in place from the reference sources by
 // oracle/Makefile into oracle/_ref/libscenemap_ref.so, through its C++ API:
-//   Mapper2D::keyframe (scenemap src/mapper2d.cpp:100)  -> makeScan + OccGrid::insert
+//   Mapper2D::keyframe (scenemap src/mapper2d.cpp:27-87)  -> makeScan + OccGrid::insert
 //   ObjectMap::update   (scenemap src/objmap.cpp:516)    -> the objprob per-frame update
 //   ObjectMap::addPoints(scenemap src/objmap.cpp:508)    -> ObjCloud::add (cloud.cpp:86)
 //   ObjectMap::buildReencode (scenemap src/objmap.cpp:1371) -> whole-object re-encode requests

@@ -1,5 +1,5 @@
 // 2D occupancy of a keyframe: makeScan (scenemap src/scan.cpp:222-451), the Mapper2D insert
-// policy (mapper2d.cpp:118-146) and OccGrid::insert (grid.cpp:195-259).  One CTA per map.
+// policy (mapper2d.cpp:46-72) and OccGrid::insert (grid.cpp:95-159).  One CTA per map.
 //
 // makeScan: per-pixel base-frame points at stride `step`; per-bin nearest in-band hit = the
 // first raster pixel with the smallest squared range (64-bit atomicMin of (rr2 bits, pixel));
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     nf += tf;
   }
   __syncthreads();
-  // 5. insert policy (mapper2d.cpp:118-146)
+  // 5. insert policy (mapper2d.cpp:46-72)
   const int th_c = P.change_cells;
   int nd_l = 0;
   const int16_t* IS = B.ins_sig + (size_t)m * nb;
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   }
   __syncthreads();
   if (!sh_ins) return;
-  // 6. OccGrid::insert (grid.cpp:195-259)
+  // 6. OccGrid::insert (grid.cpp:95-159)
   const double c = F.cos_th, sn = F.sin_th;
   const double* pose = F.base;
   const float res = P.grid_res;

@@ -1,6 +1,6 @@
 // Standalone 2D occupancy + correlative scan matching.
 //
-// OccGrid::insert (scenemap src/grid.cpp:195-259, hit/miss :157-193) for M independent grids,
+// OccGrid::insert (scenemap src/grid.cpp:95-159, hit/miss :57-93) for M independent grids,
 // spread over many CTAs per grid: a first pass takes, per cell, the minimum of a first-touch
 // key (scan id in the high word, then hits in point order before every ray cell, rays in
 // order, cells along a ray in step order) with atomicMin; the second pass lets only the

@@ -15,7 +15,7 @@
 //   k_prune         drop / prune, cloud targets        (objmap.cpp:1066-1073)
 //   k_markview      seen cells                         (objmap.cpp:1084)
 //   k_cloud_add     ObjectMap::addPoints + contact     (capi.cpp:986-992, cloud.cpp:86-127)
-//   k_grid          makeScan + insert policy + insert  (mapper2d.cpp:100-160)
+//   k_grid          makeScan + insert policy + insert  (mapper2d.cpp:27-87)
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdio.h>
@@ -188,48 +188,56 @@ int smg_params_default(smg_params* p) {
   return SMG_OK;
 }
 
-// ObjectMap::applyParams key table (scenemap src/objmap.cpp:135-180).  Keys of features this
-// build does not run (text model, wall segments, re-encode, inspect) are accepted and stored
-// nowhere, like a field the caller never reads.
+// ObjectMap::applyParams key table (scenemap src/objmap.cpp:135-180).  Keys whose feature the
+// device path does not run (the text model's naming and structural-name rules, wall segments,
+// the inspect pass, the export filter) only ever take the reference default here: any other
+// value is reported as unsupported, so a parameter file cannot change the reference's
+// behaviour and leave this one unchanged without an error.
 int smg_params_apply(smg_params* p, const char* kv) {
   if (!p) return SMG_ERR_ARGS;
   if (!kv || !*kv) return 0;
-  struct K { const char* n; double* d; int32_t* i; };
-  static double sink_d;
-  static int32_t sink_i;
+  // d/i: the field the key sets; dflt: for keys of features this build does not run (d == i ==
+  // null), the reference default (objprob.hpp:84-136, inspect.hpp:19), the only value accepted
+  struct K { const char* n; double* d; int32_t* i; double dflt; };
   const K keys[] = {
-      {"floor_h", &p->floor_h, 0}, {"absent_samples", 0, &p->absent_samples}, {"absent_vis", &p->absent_vis, 0},
-      {"absent_min_px", &p->absent_min_px, 0}, {"absent_det_k", &p->absent_det_k, 0}, {"gone_misses", 0, &p->gone_misses},
-      {"gone_min_s", &p->gone_min_s, 0}, {"gone_misses_big", 0, &p->gone_misses_big}, {"gone_min_s_big", &p->gone_min_s_big, 0},
-      {"gone_view_d", &p->gone_view_d, 0}, {"gone_eps", &p->gone_eps, 0}, {"gone_step_d", &p->gone_step_d, 0},
-      {"gone_step_deg", &p->gone_step_deg, 0}, {"spurious_obs", 0, &p->spurious_obs}, {"link_v", &p->link_v, 0},
-      {"link_d0", &p->link_d0, 0}, {"link_max_d", &p->link_max_d, 0}, {"link_min_obs", 0, &p->link_min_obs},
-      {"link_wait_s", &p->link_wait_s, 0}, {"link_window_s", &p->link_window_s, 0}, {"link_view_gap_s", &p->link_view_gap_s, 0},
-      {"view_cell", &p->view_cell, 0}, {"confirm", 0, &p->confirm}, {"move_v", &p->move_v, 0}, {"move_n", 0, &p->move_n},
-      {"move_min_d", &p->move_min_d, 0}, {"move_max_cam_w", &p->move_max_cam_w, 0}, {"self_pad", &p->self_pad, 0},
-      {"inspect", 0, &sink_i},
-      {"ap_same_p", &p->same_p, 0}, {"ap_merge_p", &p->merge_p, 0}, {"ap_gate", &p->gate, 0}, {"ap_name_tau", &sink_d, 0},
-      {"ap_name_wmax", &sink_d, 0}, {"ap_size_w", &sink_d, 0}, {"ap_kappa_ref", &p->kappa_ref, 0}, {"ap_temper", &p->temper, 0},
-      {"ap_wall_big", &sink_d, 0}, {"ap_struct_p", &sink_d, 0}, {"ap_ceil_z", &p->ceil_z, 0}, {"ap_struct_obj_p", &p->struct_obj_p, 0},
-      {"ap_obj_wall_span", &p->obj_wall_span, 0}, {"ap_obj_wall_top", &p->obj_wall_top, 0}, {"ap_reenc_max", 0, &p->reenc_max},
-      {"ap_reenc_gain", &p->reenc_gain, 0}, {"ap_link_cos", &p->link_cos, 0}, {"ap_whole_w", &sink_d, 0}, {"ap_export_named", 0, &sink_i},
-      {"ap_guard_obj", &p->guard_obj, 0}, {"ap_guard_obs", &p->guard_obs, 0}, {"ap_geo_w", &sink_d, 0},
-      {"ap_name_veto", &p->name_veto, 0}, {"ap_through_d", &sink_d, 0}, {"ap_bridge_max", &sink_d, 0},
-      {"ap_frame_group", 0, &p->frame_group}, {"ap_struct_obj_min_views", 0, &p->struct_obj_min_views},
-      {"ap_plane_inl", &p->plane_inl, 0}, {"ap_obj_plane_inl", &p->obj_plane_inl, 0}, {"ap_ransac_tau0", &p->ransac_tau0, 0},
-      {"ap_ransac_tau_k", &p->ransac_tau_k, 0}, {"ap_obj_tau", &p->obj_tau, 0}, {"ap_ransac_iters", 0, &p->ransac_iters},
-      {"ap_so_dw_w", &sink_d, 0}, {"ap_so_dw_thick", &sink_d, 0}, {"ap_so_max_h", &sink_d, 0}, {"ap_so_pillar", &sink_d, 0},
-      {"ap_so_stairs", &sink_d, 0}, {"ap_wallhug_frac", &sink_d, 0}, {"ap_wallhug_w", &sink_d, 0},
-      {"ap_struct_look_block", 0, &sink_i}, {"ap_flat_max_w", &sink_d, 0}, {"ap_tall_h", &p->tall_h, 0}, {"ap_tall_w", &p->tall_w, 0},
-      {"ap_tall_ps", &p->tall_ps, 0}, {"ap_tall_w_any", &p->tall_w_any, 0}, {"ap_big_vinl", &sink_d, 0}, {"ap_so_dw_min", &sink_d, 0},
-      {"ap_so_hide_k", &sink_d, 0},
-      {"ap_w0", &p->w[0], 0}, {"ap_w1", &p->w[1], 0}, {"ap_w2", &p->w[2], 0}, {"ap_w3", &p->w[3], 0}, {"ap_w4", &p->w[4], 0},
-      {"ap_w5", &p->w[5], 0}, {"ap_w6", &p->w[6], 0}, {"ap_w7", &p->w[7], 0},
-      {"ap_wm0", &p->wm[0], 0}, {"ap_wm1", &p->wm[1], 0}, {"ap_wm2", &p->wm[2], 0}, {"ap_wm3", &p->wm[3], 0}, {"ap_wm4", &p->wm[4], 0},
-      {"ap_wm5", &p->wm[5], 0}, {"ap_wm6", &p->wm[6], 0}, {"ap_wm7", &p->wm[7], 0},
-      {"ap_cos0", &p->cos0, 0}, {"ap_bridge_drop", 0, &p->bridge_drop},
-      {"kap_k0", &p->kap_k0, 0}, {"kap_s0", &p->kap_s0, 0}, {"kap_trunc", &p->kap_trunc, 0}, {"kap_d0", &p->kap_d0, 0}};
+      {"floor_h", &p->floor_h, 0, 0}, {"absent_samples", 0, &p->absent_samples, 0}, {"absent_vis", &p->absent_vis, 0, 0},
+      {"absent_min_px", &p->absent_min_px, 0, 0}, {"absent_det_k", &p->absent_det_k, 0, 0}, {"gone_misses", 0, &p->gone_misses, 0},
+      {"gone_min_s", &p->gone_min_s, 0, 0}, {"gone_misses_big", 0, &p->gone_misses_big, 0}, {"gone_min_s_big", &p->gone_min_s_big, 0, 0},
+      {"gone_view_d", &p->gone_view_d, 0, 0}, {"gone_eps", &p->gone_eps, 0, 0}, {"gone_step_d", &p->gone_step_d, 0, 0},
+      {"gone_step_deg", &p->gone_step_deg, 0, 0}, {"spurious_obs", 0, &p->spurious_obs, 0}, {"link_v", &p->link_v, 0, 0},
+      {"link_d0", &p->link_d0, 0, 0}, {"link_max_d", &p->link_max_d, 0, 0}, {"link_min_obs", 0, &p->link_min_obs, 0},
+      {"link_wait_s", &p->link_wait_s, 0, 0}, {"link_window_s", &p->link_window_s, 0, 0}, {"link_view_gap_s", &p->link_view_gap_s, 0, 0},
+      {"view_cell", &p->view_cell, 0, 0}, {"confirm", 0, &p->confirm, 0}, {"move_v", &p->move_v, 0, 0}, {"move_n", 0, &p->move_n, 0},
+      {"move_min_d", &p->move_min_d, 0, 0}, {"move_max_cam_w", &p->move_max_cam_w, 0, 0}, {"self_pad", &p->self_pad, 0, 0},
+      {"inspect", 0, 0, 0},
+      {"ap_same_p", &p->same_p, 0, 0}, {"ap_merge_p", &p->merge_p, 0, 0}, {"ap_gate", &p->gate, 0, 0}, {"ap_name_tau", 0, 0, 0.5},
+      {"ap_name_wmax", 0, 0, 6.0}, {"ap_size_w", 0, 0, 1.0}, {"ap_kappa_ref", &p->kappa_ref, 0, 0}, {"ap_temper", &p->temper, 0, 0},
+      {"ap_wall_big", 0, 0, 1.0}, {"ap_struct_p", 0, 0, 0.5}, {"ap_ceil_z", &p->ceil_z, 0, 0}, {"ap_struct_obj_p", &p->struct_obj_p, 0, 0},
+      {"ap_obj_wall_span", &p->obj_wall_span, 0, 0}, {"ap_obj_wall_top", &p->obj_wall_top, 0, 0}, {"ap_reenc_max", 0, &p->reenc_max, 0},
+      {"ap_reenc_gain", &p->reenc_gain, 0, 0}, {"ap_link_cos", &p->link_cos, 0, 0}, {"ap_whole_w", 0, 0, 1.0},
+      {"ap_export_named", 0, 0, 1}, {"ap_guard_obj", &p->guard_obj, 0, 0}, {"ap_guard_obs", &p->guard_obs, 0, 0},
+      {"ap_geo_w", 0, 0, 3.0}, {"ap_name_veto", &p->name_veto, 0, 0}, {"ap_through_d", 0, 0, 0.20}, {"ap_bridge_max", 0, 0, 0.0},
+      {"ap_frame_group", 0, &p->frame_group, 0}, {"ap_struct_obj_min_views", 0, &p->struct_obj_min_views, 0},
+      {"ap_plane_inl", &p->plane_inl, 0, 0}, {"ap_obj_plane_inl", &p->obj_plane_inl, 0, 0}, {"ap_ransac_tau0", &p->ransac_tau0, 0, 0},
+      {"ap_ransac_tau_k", &p->ransac_tau_k, 0, 0}, {"ap_obj_tau", &p->obj_tau, 0, 0}, {"ap_ransac_iters", 0, &p->ransac_iters, 0},
+      {"ap_so_dw_w", 0, 0, 2.2}, {"ap_so_dw_thick", 0, 0, 0.45}, {"ap_so_max_h", 0, 0, 2.8}, {"ap_so_pillar", 0, 0, 1.0},
+      {"ap_so_stairs", 0, 0, 6.0}, {"ap_wallhug_frac", 0, 0, 0.75}, {"ap_wallhug_w", 0, 0, 2.0},
+      {"ap_struct_look_block", 0, 0, 1}, {"ap_flat_max_w", 0, 0, 2.2}, {"ap_tall_h", &p->tall_h, 0, 0}, {"ap_tall_w", &p->tall_w, 0, 0},
+      {"ap_tall_ps", &p->tall_ps, 0, 0}, {"ap_tall_w_any", &p->tall_w_any, 0, 0}, {"ap_big_vinl", 0, 0, 0.5}, {"ap_so_dw_min", 0, 0, 0.3},
+      {"ap_so_hide_k", 0, 0, 1.5},
+      {"ap_w0", &p->w[0], 0, 0}, {"ap_w1", &p->w[1], 0, 0}, {"ap_w2", &p->w[2], 0, 0}, {"ap_w3", &p->w[3], 0, 0}, {"ap_w4", &p->w[4], 0, 0},
+      {"ap_w5", &p->w[5], 0, 0}, {"ap_w6", &p->w[6], 0, 0}, {"ap_w7", &p->w[7], 0, 0},
+      {"ap_wm0", &p->wm[0], 0, 0}, {"ap_wm1", &p->wm[1], 0, 0}, {"ap_wm2", &p->wm[2], 0, 0}, {"ap_wm3", &p->wm[3], 0, 0},
+      {"ap_wm4", &p->wm[4], 0, 0}, {"ap_wm5", &p->wm[5], 0, 0}, {"ap_wm6", &p->wm[6], 0, 0}, {"ap_wm7", &p->wm[7], 0, 0},
+      {"ap_cos0", &p->cos0, 0, 0}, {"ap_bridge_drop", 0, &p->bridge_drop, 0},
+      {"kap_k0", &p->kap_k0, 0, 0}, {"kap_s0", &p->kap_s0, 0, 0}, {"kap_trunc", &p->kap_trunc, 0, 0}, {"kap_d0", &p->kap_d0, 0, 0}};
+  // boolean keys (bool fields in the reference: v != 0)
+  auto is_bool = [](const char* n) {
+    return !strcmp(n, "ap_frame_group") || !strcmp(n, "ap_bridge_drop") || !strcmp(n, "inspect") || !strcmp(n, "ap_export_named") ||
+           !strcmp(n, "ap_struct_look_block");
+  };
   int n_bad = 0;
+  std::string unsupported;
   std::string s(kv);
   size_t a = 0;
   while (a < s.size()) {
@@ -244,14 +252,23 @@ int smg_params_apply(smg_params* p, const char* kv) {
     bool ok = false;
     for (const K& x : keys)
       if (k == x.n) {
-        if (x.d) *x.d = v;
-        if (x.i) *x.i = (x.i == &p->bridge_drop || x.i == &p->frame_group) ? (v != 0) : (int32_t)v;
         ok = true;
+        if (x.d) *x.d = v;
+        else if (x.i) *x.i = is_bool(x.n) ? (v != 0) : (int32_t)v;
+        else if (is_bool(x.n) ? ((v != 0) != (x.dflt != 0)) : v != x.dflt)
+          unsupported += (unsupported.empty() ? "" : ",") + k;
       }
     if (!ok) ++n_bad;
   }
-  if (n_bad) g_err = "unknown parameter key";
-  return n_bad;
+  if (n_bad) {
+    g_err = "unknown parameter key";
+    return n_bad;
+  }
+  if (!unsupported.empty()) {
+    g_err = "parameter keys of features this build does not run, set away from the reference default: " + unsupported;
+    return SMG_ERR_UNSUPPORTED;
+  }
+  return 0;
 }
 
 int smg_destroy(smg_batch* b) {
@@ -1673,19 +1690,46 @@ static __device__ __align__(256) int32_t g_pf_need[NEED_N * NEED_N];            
 
 struct PfStaticDevice {
   bool ready = false;
+  unsigned long long ctx_id = 0;   // the context the set-up ran in (cuCtxGetId)
   double* scratch = nullptr;
   int32_t* need = nullptr;
 };
 
-// Once per device, with that device current: resolve the device addresses of the static
-// arrays and fill the constant iteration table (a synchronous copy, no allocation).
+// Unique id of the calling thread's current context (0 when none can be read).  A device reset
+// destroys the context that held the static arrays' contents; the next context has a new id.
+static unsigned long long current_ctx_id() {
+  typedef CUresult (*PfnCtxGetCurrent)(CUcontext*);
+  typedef CUresult (*PfnCtxGetId)(CUcontext, unsigned long long*);
+  static PfnCtxGetCurrent get_cur = nullptr;
+  static PfnCtxGetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_cur = (PfnCtxGetCurrent)p;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_id = (PfnCtxGetId)p;
+  });
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (!get_cur || !get_id || get_cur(&c) != CUDA_SUCCESS || !c || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Once per device and context, with that device current: resolve the device addresses of the
+// static arrays and fill the constant iteration table (a synchronous copy, no allocation).  The
+// set-up is repeated when the device's context has changed since (after a cudaDeviceReset), so
+// no stale address or empty table is used.
 static int pf_static_setup(int dev, PfStaticDevice* out) {
   static std::mutex mu;
   static std::vector<PfStaticDevice> devs;
   std::lock_guard<std::mutex> lk(mu);
   if ((int)devs.size() <= dev) devs.resize((size_t)dev + 1);
   PfStaticDevice& d = devs[(size_t)dev];
-  if (!d.ready) {
+  const unsigned long long ctx = current_ctx_id();
+  if (!d.ready || ctx == 0 || ctx != d.ctx_id) {
+    d.ready = false;
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_pf_scratch);
     if (e != cudaSuccess) return fail(SMG_ERR_DEVICE, (std::string("smg_plane_fit_noalloc: cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e)).c_str());
@@ -1695,6 +1739,7 @@ static int pf_static_setup(int dev, PfStaticDevice* out) {
     d.need = (int32_t*)p;
     const std::vector<int32_t>& need = need_table();
     CK(cudaMemcpyToSymbol(g_pf_need, need.data(), sizeof(int32_t) * need.size()));
+    d.ctx_id = current_ctx_id();
     d.ready = true;
   }
   *out = d;

@@ -194,7 +194,7 @@ typedef struct {
   int32_t n_targets;     // objects receiving cloud points / contact rebuilds this frame
   StatsRec st;
   double ceil_obs[SMG_CEIL_OBS];
-  // Mapper2D insert policy (mapper2d.cpp:118-146)
+  // Mapper2D insert policy (mapper2d.cpp:46-72)
   int32_t kf_first, kf_since, kf_last_changed, kf_inserted, kf_changed, kf_hits, kf_sig_n;
   double kf_last_ins[3];
   uint32_t scan_id;

@@ -17,6 +17,7 @@ LIB_PATH = os.environ.get("SMG_LIB") or os.path.join(os.path.dirname(_HERE), "li
 
 SMG_MEM_DEVICE, SMG_MEM_HOST = 0, 1
 SMG_EMB_F32, SMG_EMB_BF16 = 0, 1
+SMG_OK, SMG_ERR_ARGS, SMG_ERR_PARAM, SMG_ERR_CAPACITY, SMG_ERR_DEVICE, SMG_ERR_UNSUPPORTED = 0, -1, -2, -3, -4, -5
 STAT_FIELDS = ["n_through", "n_obs", "n_wall", "n_wall_name", "n_ceil", "n_floor", "n_assoc", "n_new", "n_merge",
                "n_obj_struct", "n_reenc_req", "n_reenc_done", "n_blocked", "n_wall_tall", "n_so_big", "n_bridge"]
 
@@ -119,9 +120,10 @@ class Params:
         self.buf = C.create_string_buffer(L.smg_params_size())
         _check(L.smg_params_default(self.buf), "smg_params_default")
         if kv:
-            n_bad = L.smg_params_apply(self.buf, kv.encode())
-            if n_bad:
+            rc = L.smg_params_apply(self.buf, kv.encode())
+            if rc > 0:
                 raise SmgError(f"unknown parameter keys in {kv!r}")
+            _check(rc, "smg_params_apply")
 
 
 class Batch:

@@ -15,6 +15,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(os.path.dirname(_HERE), "synth", "libsynth.so")
 
 SY_MAX_BOXES = 64
+SY_SHELL_LABEL0 = 1 + 3 * SY_MAX_BOXES   # first room-face label (synth.h)
 
 
 class SyBox(C.Structure):
@@ -23,7 +24,14 @@ class SyBox(C.Structure):
 
 class SyScene(C.Structure):
     _fields_ = [("seed", C.c_uint64), ("room", C.c_double * 3), ("n_boxes", C.c_int),
-                ("box", SyBox * SY_MAX_BOXES), ("noise_k", C.c_float)]
+                ("box", SyBox * SY_MAX_BOXES), ("noise_k", C.c_float), ("shell_labels", C.c_int32)]
+
+
+def obj_of_label(label):
+    """The object a label belongs to (synth.h sy_obj_of_label): box b for its three face labels,
+    SY_MAX_BOXES + face for the room faces.  Works on ints and integer numpy arrays."""
+    label = np.asarray(label, np.int64)
+    return np.where(label < SY_SHELL_LABEL0, (label - 1) // 3, SY_MAX_BOXES + (label - SY_SHELL_LABEL0))
 
 
 class SyCamera(C.Structure):
@@ -69,18 +77,39 @@ def map_seed(base: int, index: int) -> int:
 
 
 class BoxRoom:
-    """Config 0/1/4 generator: 6x5x2.6 m room, 20 boxes, pinhole camera on a moving base."""
+    """Config 0/1/4 generator: 6x5x2.6 m room, 20 boxes, pinhole camera on a moving base.
+
+    Variants (parity cases for rules the default room never reaches):
+      shell_labels  the room's walls, floor and ceiling come back as detections of their own;
+      box_moves     [(frame, box, (dx, dy, dz)), ...]: from that frame on the box is translated
+                    (cumulatively); a translation far outside the room makes it vanish;
+      box_extra     [(lo, hi), ...]: boxes added after the seeded ones (their placement is the
+                    caller's, e.g. small graspable boxes or boxes that only enter through a move);
+      hands         callable f -> (eef (2, 3) map frame, grip (2,)): the robot hand's point and
+                    gripper value per frame (default: far away, open).
+    """
 
     def __init__(self, seed: int, n_boxes: int = 20, room=(6.0, 5.0, 2.6), noise_k: float = 0.005,
                  size=(0.2, 0.6), height=(0.15, 0.9), w: int = 640, h: int = 480, fx: float = 525.0,
                  fy: float = 525.0, cx: float = 319.5, cy: float = 239.5, dt: float = 0.1, speed: float = 0.3,
                  n_frames: int = 300, D: int = 1152, bf16: bool = False, emb_sigma: float = 0.05,
-                 min_px: int = 64, max_det: int = 24, cam_height: float = 0.9, pitch_deg: float = 20.0):
+                 min_px: int = 64, max_det: int = 24, cam_height: float = 0.9, pitch_deg: float = 20.0,
+                 shell_labels: bool = False, box_moves=(), box_extra=(), hands=None):
         L = lib()
         self.seed = seed
         self.scene = SyScene()
         L.sy_scene_make(seed, n_boxes, room[0], room[1], room[2], noise_k, size[0], size[1], height[0], height[1],
                         C.byref(self.scene))
+        for lo, hi in box_extra:
+            b = self.scene.n_boxes
+            assert b < SY_MAX_BOXES
+            for k in range(3):
+                self.scene.box[b].lo[k] = lo[k]
+                self.scene.box[b].hi[k] = hi[k]
+            self.scene.n_boxes = b + 1
+        self.scene.shell_labels = 1 if shell_labels else 0
+        self.box_moves = sorted(box_moves, key=lambda e: e[0])
+        self.hands = hands
         self.cam = SyCamera(w, h, fx, fy, cx, cy)
         self.w, self.h, self.fx, self.fy, self.cx, self.cy = w, h, fx, fy, cx, cy
         self.dt, self.n_frames, self.D, self.bf16, self.emb_sigma = dt, n_frames, D, bf16, emb_sigma
@@ -99,13 +128,27 @@ class BoxRoom:
         lib().sy_T_mc(_p(pose, C.c_double), _p(self.T_bc, C.c_float), _p(out, C.c_double))
         return out
 
+    def scene_at(self, f: int) -> SyScene:
+        """The scene of frame f: the seeded boxes with every move of frames <= f applied."""
+        if not self.box_moves:
+            return self.scene
+        S = SyScene.from_buffer_copy(self.scene)
+        for fm, b, d in self.box_moves:
+            if fm > f:
+                break
+            for k in range(3):
+                S.box[b].lo[k] += d[k]
+                S.box[b].hi[k] += d[k]
+        return S
+
     def frame(self, f: int) -> dict:
         L = lib()
         T = self.T_mc(f)
         depth = np.zeros((self.h, self.w), np.float32)
         label = np.zeros((self.h, self.w), np.uint16)
         key = f + 1
-        L.sy_render(C.byref(self.scene), C.byref(self.cam), _p(T, C.c_double), key, _p(depth, C.c_float),
+        S = self.scene_at(f)
+        L.sy_render(C.byref(S), C.byref(self.cam), _p(T, C.c_double), key, _p(depth, C.c_float),
                     _p(label, C.c_uint16))
         md = self.max_det
         det_label = np.zeros(md, np.uint16)
@@ -116,9 +159,10 @@ class BoxRoom:
                       _p(box, C.c_float), _p(cls, C.c_int32), _p(score, C.c_float))
         emb = np.zeros((max(n, 1), self.D), np.float32)
         if n:
-            L.sy_embed(C.byref(self.scene), key, n, _p(det_label, C.c_uint16), self.D, self.emb_sigma,
+            L.sy_embed(C.byref(S), key, n, _p(det_label, C.c_uint16), self.D, self.emb_sigma,
                        1 if self.bf16 else 0, _p(emb, C.c_float))
+        eef, grip = (self.eef, np.ones(2, np.float32)) if self.hands is None else self.hands(f)
         return dict(stamp=f * self.dt, w=self.w, h=self.h, depth=depth, label=label, fx=self.fx, fy=self.fy,
-                    cx=self.cx, cy=self.cy, T_mc=T, T_bc=self.T_bc, base=self.poses[f].copy(), eef=self.eef,
-                    eef_base=self.eef_base, n_det=n, det_label=det_label[:n].copy(), box=box[:n].copy(),
+                    cx=self.cx, cy=self.cy, T_mc=T, T_bc=self.T_bc, base=self.poses[f].copy(),
+                    eef=np.asarray(eef, np.float64), grip=np.asarray(grip, np.float32), eef_base=self.eef_base, n_det=n, det_label=det_label[:n].copy(), box=box[:n].copy(),
                     cls=cls[:n].copy(), score=score[:n].copy(), emb=emb[:n].copy(), emb_dim=self.D)

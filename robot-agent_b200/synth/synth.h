@@ -10,8 +10,11 @@
 // optical depth plus a uint16 instance-label image.  Each visible box face is its own
 // label (1 + 3*box + axis, axis 0/1/2 = x/y/z-facing face), so one box yields up to
 // three detection fragments, like a segmenter that splits objects into parts; 0 is the
-// background (walls, floor, ceiling).  Depth noise is sigma = k*z^2 times a unit-variance
-// Irwin-Hall(12) draw (sum of 12 uniforms minus 6), which is reproducible bit for bit.
+// background (walls, floor, ceiling) unless the scene's shell_labels flag is set: the six
+// room faces then get labels of their own (SY_SHELL_LABEL0 + face, face = -x, +x, -y, +y,
+// floor, ceiling), like a segmenter that also returns wall, floor and ceiling segments.
+// Depth noise is sigma = k*z^2 times a unit-variance Irwin-Hall(12) draw (sum of 12 uniforms
+// minus 6), which is reproducible bit for bit.
 #pragma once
 #include <stdint.h>
 
@@ -22,6 +25,8 @@
 #endif
 
 #define SY_MAX_BOXES 64
+#define SY_SHELL_LABEL0 (1 + 3 * SY_MAX_BOXES)   // first room-face label
+#define SY_NLAB (SY_SHELL_LABEL0 + 6)             // label values 0 .. SY_NLAB-1
 
 typedef struct {
   double lo[3], hi[3];
@@ -33,7 +38,14 @@ typedef struct {
   int n_boxes;
   sy_box box[SY_MAX_BOXES];
   float noise_k;   // depth noise sigma = noise_k * z^2
+  int32_t shell_labels;   // 1: room faces carry labels SY_SHELL_LABEL0 + face (else 0)
 } sy_scene;
+
+// The object a label belongs to: box b for its three face labels, SY_MAX_BOXES + face for the
+// room faces.  Embeddings (per-object base vector) and classes are keyed by it.
+SY_HD int sy_obj_of_label(int label) {
+  return label < SY_SHELL_LABEL0 ? (label - 1) / 3 : SY_MAX_BOXES + (label - SY_SHELL_LABEL0);
+}
 
 typedef struct {
   int w, h;
@@ -64,20 +76,22 @@ SY_HD double sy_gauss(uint64_t seed, uint64_t a, uint64_t b, uint64_t c) {
 }
 
 // Ray (origin o, direction d, not normalised) against the scene: returns the ray parameter of
-// the first hit (> 1e-9) and its label (0 = room shell, 1 + 3*box + axis for box faces).
+// the first hit (> 1e-9) and its label (room shell: 0, or SY_SHELL_LABEL0 + face with
+// shell_labels; 1 + 3*box + axis for box faces).
 SY_HD double sy_cast(const sy_scene* S, const double o[3], const double d[3], int* label) {
   // room shell: the exit point of the interior
   double t_best = 1e300;
+  int face = 0;
   for (int k = 0; k < 3; ++k) {
     if (d[k] > 0.0) {
       const double t = (S->room[k] - o[k]) / d[k];
-      if (t < t_best) t_best = t;
+      if (t < t_best) { t_best = t; face = 2 * k + 1; }
     } else if (d[k] < 0.0) {
       const double t = (0.0 - o[k]) / d[k];
-      if (t < t_best) t_best = t;
+      if (t < t_best) { t_best = t; face = 2 * k; }
     }
   }
-  int lab = 0;
+  int lab = S->shell_labels ? SY_SHELL_LABEL0 + face : 0;
   for (int b = 0; b < S->n_boxes; ++b) {
     const sy_box* B = &S->box[b];
     double t0 = -1e300, t1 = 1e300;

@@ -1,13 +1,11 @@
 // Device side of the synthetic generator (synth.h): renders frames, label statistics and
 // detection embeddings directly in HBM, for benchmark inputs.  Not on the measured path.
-// The per-pixel render is the same function as the host generator; embeddings normalise with
-// a block reduction (the host sums sequentially), so a device embedding can differ from the
-// host one in the last float bit.
+// The per-pixel render is the same function as the host generator, and embeddings are
+// normalised with the host's sum order (one thread adds the squares in index order), so the
+// device renders bit for bit the frames the host generator renders.
 #include <stdint.h>
 
 #include "synth.h"
-
-#define SY_NLAB (1 + 3 * SY_MAX_BOXES)
 
 // frames f of maps m: T_all[(f*M + m)*12], keys[f*M + m]; output image (f*M + m)
 __global__ void sy_render_batch_kernel(const sy_scene* __restrict__ scenes, sy_camera Cm, const double* __restrict__ T_all,
@@ -60,7 +58,11 @@ __global__ void sy_stats_init_kernel(int* stats, int n_img, int w, int h) {
   }
 }
 
-// one block per detection: desc[4*j] = map, box, det slot k, frame key (as two ints: lo, hi)
+// one block per detection: desc[5*j] = map, object (sy_obj_of_label), det slot k, frame key
+// (as two ints: lo, hi).  The raw values are staged in shared memory and their squares summed in
+// index order by one thread, as the host generator does, so the normalised values are the same
+// floats.
+#define SY_EMB_DMAX 2048
 __global__ void sy_embed_kernel(const sy_scene* __restrict__ scenes, const int* __restrict__ desc, int n, int D, double sigma,
                                 int bf16, void* __restrict__ out) {
   const int j = blockIdx.x;
@@ -68,24 +70,18 @@ __global__ void sy_embed_kernel(const sy_scene* __restrict__ scenes, const int* 
   const int m = desc[5 * j], box = desc[5 * j + 1], k = desc[5 * j + 2];
   const uint64_t key = (uint64_t)(uint32_t)desc[5 * j + 3] | ((uint64_t)(uint32_t)desc[5 * j + 4] << 32);
   const uint64_t seed = scenes[m].seed;
-  __shared__ double red[32];
-  double s = 0;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    const double v = sy_emb_raw(seed, box, key, k, i, sigma);
-    s += v * v;
-  }
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __shared__ double v[SY_EMB_DMAX];
+  __shared__ double inv;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) v[i] = sy_emb_raw(seed, box, key, k, i, sigma);
   __syncthreads();
-  if (threadIdx.x < 32) {
-    double t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
-    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (threadIdx.x == 0) red[0] = t;
+  if (threadIdx.x == 0) {
+    double s = 0;
+    for (int i = 0; i < D; ++i) s += v[i] * v[i];
+    inv = 1.0 / sqrt(s);
   }
   __syncthreads();
-  const double inv = 1.0 / sqrt(red[0]);
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    const float f = (float)(sy_emb_raw(seed, box, key, k, i, sigma) * inv);
+    const float f = (float)(v[i] * inv);
     if (bf16) ((uint16_t*)out)[(size_t)j * D + i] = (uint16_t)(__float_as_uint(sy_bf16_round(f)) >> 16);
     else ((float*)out)[(size_t)j * D + i] = f;
   }
@@ -108,6 +104,7 @@ int sy_label_stats_device(const uint16_t* label_dev, int w, int h, int n_img, in
 
 int sy_embed_device(const sy_scene* scenes_dev, const int* desc_dev, int n, int D, double sigma, int bf16, void* out_dev, void* stream) {
   if (n <= 0) return 0;
+  if (D <= 0 || D > SY_EMB_DMAX) return -1;
   sy_embed_kernel<<<n, 256, 0, (cudaStream_t)stream>>>(scenes_dev, desc_dev, n, D, sigma, bf16, out_dev);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

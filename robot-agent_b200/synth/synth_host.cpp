@@ -117,7 +117,7 @@ void sy_render(const sy_scene* S, const sy_camera* C, const double T_mc[12], uin
 // Detections from a label image: one per label value with >= min_px pixels, ordered by pixel
 // count (descending, ties by label).  box = [umin, vmin, umax + 1, vmax + 1] in pixels.
 int sy_dets(const uint16_t* label, int w, int h, int min_px, int max_det, uint16_t* det_label, float* box, int32_t* cls, float* score) {
-  const int L = 1 + 3 * SY_MAX_BOXES;
+  const int L = SY_NLAB;
   std::vector<int> cnt(L, 0), u0(L, w), v0(L, h), u1(L, -1), v1(L, -1);
   for (int v = 0; v < h; ++v)
     for (int u = 0; u < w; ++u) {
@@ -138,7 +138,7 @@ int sy_dets(const uint16_t* label, int w, int h, int min_px, int max_det, uint16
     box[4 * k + 1] = (float)v0[l];
     box[4 * k + 2] = (float)(u1[l] + 1);
     box[4 * k + 3] = (float)(v1[l] + 1);
-    cls[k] = ((l - 1) / 3) % 16;
+    cls[k] = sy_obj_of_label(l) % 16;
     score[k] = 0.5f + 0.5f * std::min(1.f, (float)cnt[l] / 20000.f);
   }
   return n;
@@ -149,7 +149,7 @@ int sy_dets(const uint16_t* label, int w, int h, int min_px, int max_det, uint16
 void sy_embed(const sy_scene* S, uint64_t frame_key, int n, const uint16_t* det_label, int D, double sigma, int bf16, float* out) {
   std::vector<double> v((size_t)D);
   for (int k = 0; k < n; ++k) {
-    const int box = (det_label[k] - 1) / 3;
+    const int box = sy_obj_of_label(det_label[k]);
     double s = 0;
     for (int i = 0; i < D; ++i) {
       v[(size_t)i] = sy_emb_raw(S->seed, box, frame_key, k, i, sigma);

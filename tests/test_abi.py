@@ -49,6 +49,31 @@ def test_params_default_and_apply():
         smg.Params("no_such_key=1")
 
 
+# engine parameter file of the reference (tools/realbag/objprob_params/yolo26n-seg-obj-416.json,
+# its "obj_params" string): every key it sets is implemented on the device
+YOLO26N_OBJ_PARAMS = ("ap_w0=-4.235,ap_w1=5.063,ap_w2=-5.289,ap_w3=-0.3241,ap_w4=5.02,ap_w5=1.417,ap_w6=-0.013,ap_w7=0,"
+                      "ap_wm0=-2.671,ap_wm1=1.209,ap_wm2=-4.964,ap_wm3=-0.3121,ap_wm4=6.248,ap_wm5=1.648,ap_wm6=-0.5892,"
+                      "ap_wm7=2.04,ap_same_p=0.5,ap_merge_p=0.7,ap_cos0=0.75,kap_k0=4369,kap_s0=40,kap_trunc=1,kap_d0=100")
+
+
+def test_params_unsupported_keys_are_not_silent():
+    """Keys of features the device does not run are accepted at the reference default only."""
+    from scenemap_b200 import smg
+    L = smg.lib()
+    p = smg.Params()
+    assert L.smg_params_apply(p.buf, YOLO26N_OBJ_PARAMS.encode()) == 0
+    # the reference defaults of inert keys are accepted (a full parameter dump stays loadable)
+    assert L.smg_params_apply(p.buf, b"ap_through_d=0.2,ap_wall_big=1,ap_export_named=1,inspect=0,ap_so_dw_w=2.2") == 0
+    before = p.buf.raw
+    rc = L.smg_params_apply(p.buf, b"ap_same_p=0.55,ap_through_d=0.5,ap_wallhug_w=3")
+    assert rc == smg.SMG_ERR_UNSUPPORTED
+    msg = L.smg_last_error().decode()
+    assert "ap_through_d" in msg and "ap_wallhug_w" in msg and "ap_same_p" not in msg
+    assert p.buf.raw != before                      # the supported key was still applied
+    with pytest.raises(smg.SmgError):
+        smg.Params("inspect=1")
+
+
 def test_bad_arguments_fail_cleanly_without_gpu():
     from scenemap_b200 import smg
     L = smg.lib()

@@ -1,0 +1,65 @@
+"""B200 objprob update vs the reference on the generator variants (GPU).
+
+The default box room never reaches the structural drops (ceiling, floor, tall wall,
+apStructObject), the absence/gone/relink rules, or non-default parameters.  These runs feed
+byte-identical variant frames to both sides, compare every frame as the default parity test
+does, and check that the targeted counters and events really occurred (equal on both sides).
+"""
+import numpy as np
+import pytest
+
+import variants
+from conftest import has_gpu
+from parity_util import compare_frame
+
+pytestmark = pytest.mark.gpu
+
+
+def _need():
+    if not has_gpu():
+        pytest.skip("no GPU")
+    from oracle import ref
+    if not ref.available():
+        pytest.skip("reference oracle library not built")
+
+
+def _run_variant(v: dict, bf16: bool = False, deep_every: int = 10, D: int = 1152):
+    from oracle import ref
+    from scenemap_b200 import smg
+    g = variants.make_gen(v, D=D, bf16=bf16)
+    R = ref.RefMap(v["kv"])
+    B = smg.Batch(1, max_objects=256, emb_dim=D, max_det=32, params=smg.Params(v["kv"]))
+    dtype = smg.SMG_EMB_BF16 if bf16 else smg.SMG_EMB_F32
+    n = v["n_frames"]
+    for f in range(n):
+        fr = g.frame(f)
+        R.frame(fr)
+        B.push([fr], smg.SMG_MEM_HOST, dtype)
+        errs = compare_frame(R, B, 0, D, deep=(f % deep_every == 0 or f == n - 1))
+        assert not errs, f"frame {f}: " + "\n".join(errs[:20])
+    assert B.error_word() == 0
+    st = B.stats(0)
+    for k in v["stats"]:
+        assert st[k] > 0, f"{k} never fired ({st})"
+    seen = {e[2] for e in R.events()}
+    for k in v["events"]:
+        assert k in seen, f"no event of kind {k} (seen {sorted(seen)})"
+    B.close()
+
+
+def test_parity_structure_variant():
+    """Walls/floor/ceiling as detections: ceiling, floor and tall-wall drops, apStructObject."""
+    _need()
+    _run_variant(variants.structure())
+
+
+def test_parity_moving_boxes():
+    """Boxes that slide, jump, vanish and appear: absence, gone, relink, seen again."""
+    _need()
+    _run_variant(variants.moving(), deep_every=20)
+
+
+def test_parity_engine_params():
+    """The reference's engine parameter file (yolo26n-seg-obj-416 obj_params), bf16 embeddings."""
+    _need()
+    _run_variant(variants.engine_params(), bf16=True)
