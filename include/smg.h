@@ -92,6 +92,15 @@ typedef struct smg_params {
   int32_t reenc_max;
   double reenc_gain, reenc_min_vis;
   int32_t reenc_min_px;
+  /* ObjParams hands (objmap.hpp:66-76): grasp radius, closed-gripper threshold, hands used,
+   * grasp checks, gripper settling, and the gripper value -> finger gap table (ascending,
+   * linear in between, clamped outside; n_grip_gap <= 8 pairs) */
+  double grasp_r;
+  float grip_closed;
+  int32_t n_hands;
+  double grasp_max_w, grasp_min_gap, grasp_w_tol, grip_settle_s, grip_settle_eps;
+  int32_t n_grip_gap;
+  double grip_gap[8][2];
 } smg_params;
 
 /* One frame of one map.  depth/label/emb/dets live in device memory (SMG_MEM_DEVICE) or in
@@ -117,6 +126,8 @@ typedef struct smg_frame {
   const float* score;          /* n_det or NULL */
   const void* emb;             /* n_det x emb_dim, L2-normalised */
   int32_t emb_dtype;           /* SMG_EMB_F32 | SMG_EMB_BF16 */
+  float grip[2];               /* gripper values (ObjFrame::grip, rad; the reference's default is
+                                  1 = open: a zero-filled frame means a closed gripper) */
 } smg_frame;
 
 typedef struct smg_batch smg_batch;
@@ -175,6 +186,9 @@ typedef struct smg_object {
   int32_t n_views, n_ap_obs, need_whole;
   double P[3];
   int32_t n_cams, geo;
+  int32_t held_by;             /* hand holding the object, -1 = none (MapObject::held_by) */
+  uint32_t parent;             /* object it rests on / in and follows, 0 = none (MapObject::parent) */
+  double parent_rel[3];
 } smg_object;
 
 /* ObjectMap::objects() (scenemap objmap.hpp:242) of map m, in the reference's order. */
@@ -215,7 +229,7 @@ int smg_get_reencode(smg_batch* b, int m, smg_reenc_req* reqs, uint32_t* bits, i
 /* Per-kernel device time with CUDA events on the launch stream (instrumentation, off by
  * default).  smg_timing_read fills ms[k] (total milliseconds) and n[k] (launches) for the
  * SMG_NUM_KERNELS kernels of the keyframe chain and resets the counters; names[k] is static. */
-#define SMG_NUM_KERNELS 15
+#define SMG_NUM_KERNELS 16
 int smg_timing_enable(smg_batch* b, int on);
 int smg_timing_read(smg_batch* b, double* ms, int64_t* n, const char** names);
 /* First failed self-check of a -DSMG_CHECKS build: (site, index, bound); all zero when none

@@ -24,7 +24,7 @@ class RfFrame(C.Structure):
                 ("eef", C.c_double * 6), ("eef_base", C.c_float * 6), ("n_det", C.c_int),
                 ("det_label", C.POINTER(C.c_uint16)), ("box", C.POINTER(C.c_float)), ("cls", C.POINTER(C.c_int32)),
                 ("score", C.POINTER(C.c_float)), ("emb", C.POINTER(C.c_float)), ("emb_dim", C.c_int),
-                ("grid_only", C.c_int)]
+                ("grid_only", C.c_int), ("grip", C.c_float * 2)]
 
 
 class RfObj(C.Structure):
@@ -40,7 +40,8 @@ class RfObj(C.Structure):
                 ("ap_ver", C.c_uint32), ("k_frag", C.c_double), ("k_whole", C.c_double), ("n_views", C.c_int32),
                 ("n_ap_obs", C.c_int32), ("n_wall_obs", C.c_int32), ("n_struct_look", C.c_int32),
                 ("need_whole", C.c_int32), ("n_whole", C.c_int32), ("P", C.c_double * 3), ("n_cams", C.c_int32),
-                ("geo", C.c_int32), ("drop", C.c_int32), ("hide", C.c_int32)]
+                ("geo", C.c_int32), ("drop", C.c_int32), ("hide", C.c_int32), ("held_by", C.c_int32),
+                ("parent", C.c_uint32), ("parent_rel", C.c_double * 3)]
 
 
 STAT_FIELDS = ["n_through", "n_obs", "n_wall", "n_wall_name", "n_ceil", "n_floor", "n_assoc", "n_new", "n_merge",
@@ -151,6 +152,8 @@ def make_rf_frame(fr: dict, keep: list) -> RfFrame:
         f.emb = _p(em, C.c_float)
         f.emb_dim = int(fr["emb_dim"])
     f.grid_only = 0
+    grip = np.asarray(fr.get("grip", (1.0, 1.0)), np.float32).reshape(-1)
+    f.grip[0], f.grip[1] = float(grip[0]), float(grip[1])
     return f
 
 

@@ -47,6 +47,7 @@ typedef struct {
   const float* emb;
   int emb_dim;
   int grid_only;          // 1: keyframe only (no detections)
+  float grip[2];          // gripper values (ObjFrame::grip; 1 = open)
 } rf_frame;
 
 typedef struct {
@@ -73,6 +74,9 @@ typedef struct {
   double P[3];
   int32_t n_cams, geo;
   int32_t drop, hide;
+  int32_t held_by;
+  uint32_t parent;
+  double parent_rel[3];
 } rf_obj;
 
 typedef struct {
@@ -167,7 +171,8 @@ int ref_frame(void* h, const rf_frame* f) {
   memcpy(F.T_mc, f->T_mc, sizeof(F.T_mc));
   F.dets = n > 0 ? &d : nullptr;
   for (int s = 0; s < 2; ++s) for (int k = 0; k < 3; ++k) F.eef[s][k] = f->eef[s][k];
-  F.grip[0] = F.grip[1] = 1.f;
+  F.grip[0] = f->grip[0];
+  F.grip[1] = f->grip[1];
   F.base_yaw = f->base[2];
   F.base_xy[0] = f->base[0];
   F.base_xy[1] = f->base[1];
@@ -256,6 +261,9 @@ int ref_objects(void* h, rf_obj* out, int cap) {
     r.first_miss = o.first_miss;
     r.cloud_n = int(o.cloud.size());
     r.cloud_version = o.cloud.version;
+    r.held_by = o.held_by;
+    r.parent = o.parent;
+    for (int k = 0; k < 3; ++k) r.parent_rel[k] = o.parent_rel[k];
     if (o.ap) {
       const ApState& s = *o.ap;
       r.ap_ver = s.ver;

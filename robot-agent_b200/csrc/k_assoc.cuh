@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
         g2 += g * g;
       }
       pp[b] = -1.0;
-      if (g2 > gate2) continue;
+      if (g2 > gate2 || ob.held_by >= 0) continue;   // held objects take no observation (objmap.cpp:785)
       const int q = atomicAdd(&ngl, 1);
       if (q < ASSOC_GATED) gl[q] = b;
       else set_err(&B.maps[m], SMG_E_ARGS);

@@ -74,37 +74,134 @@ DEV uint32_t pack_rgb(const uint8_t* rgb, int i) {
   return rgb ? ((uint32_t)rgb[3 * i] | (uint32_t)rgb[3 * i + 1] << 8 | (uint32_t)rgb[3 * i + 2] << 16) : (128u | 128u << 8 | 128u << 16);
 }
 
-// cap trim (cloud.cpp:114-123): keep the max(1, cap*9/10) newest points by seq in their
-// original order; among points whose seq equals the cut value the highest indices are kept
-// (std::nth_element leaves which of the tied points survive, and their order, unspecified).
+// cap trim (cloud.cpp:114-123): std::nth_element(pts, pts + (n - keep), by seq), then the first
+// n - keep elements are erased and the rest keep the order the selection left them in.  Later
+// steps sample the cloud with a stride, so that order is an output: the selection reproduces
+// libstdc++'s (the reference's build): median-of-three pivot moved to the front, unguarded
+// Hoare partition, depth limit 2 floor(log2 n), insertion sort below four elements.  Each
+// partition is computed in parallel from its two stopping sequences: with L = positions whose
+// key is >= the pivot (ascending) and R = positions whose key is <= the pivot (descending), the
+// sequential loop swaps L[i] <-> R[i] while L[i] < R[i], and returns L[0] when it made no swap,
+// else min(L[k], R[k-1]) after k swaps.  (tests/trim_order_check.cpp checks the rule against
+// std::nth_element.)  Elements are (seq << 32 | index) words; only seq is compared.
+DEV bool trim_lt(uint64_t a, uint64_t b) { return (uint32_t)(a >> 32) < (uint32_t)(b >> 32); }
+
 DEV void cloud_trim(const Batch& B, size_t cs, const Work& W, int* hist, BlockScratch& bs) {
   CloudRec& C = B.clouds[cs];
   const int cap = B.p.cloud_cap;
   const int n = C.n;
   if (cap <= 0 || n <= cap) return;
-  const int keep = max(1, cap * 9 / 10), drop = n - keep;
+  const int keep = max(1, cap * 9 / 10), nth = n - keep;
   float4* pts = B.cpts + cs * B.cap;
   uint32_t* col = B.crgb + cs * B.cap;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) W.scr[i] = (double)__float_as_uint(pts[i].w);
-  __syncthreads();
-  const double cut = block_select(W.scr, n, drop, hist, bs);
-  int lt = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) lt += W.scr[i] < cut;
-  const int eq_drop = drop - block_sum_i(lt, bs);
-  int w = 0, eq_seen = 0;
+  uint64_t* E = W.keys;               // the elements being selected
+  int32_t* PL = W.dst;                // L positions, ascending
+  int32_t* PR = (int32_t*)W.tab;      // R positions, ascending (R[i] = PR[nR - 1 - i])
+  for (int i = threadIdx.x; i < n; i += blockDim.x) E[i] = ((uint64_t)__float_as_uint(pts[i].w) << 32) | (uint32_t)i;
+  __shared__ int s_first, s_last, s_depth, s_fail;
   __shared__ int trim_db[2][33];
   int trim_it = 0;
-  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
-    const int i = c0 + threadIdx.x;
-    const int is_eq = i < n && W.scr[i] == cut;
-    int toteq;
-    const int peq = block_scan_db(is_eq, &toteq, trim_db, trim_it++);
-    const int k = i < n && (W.scr[i] > cut || (is_eq && eq_seen + peq >= eq_drop));
-    int tot;
-    const int pos = block_scan_db(k, &tot, trim_db, trim_it++);
-    if (k && INB(w + pos, B.work_n, 404)) { W.t4[w + pos] = pts[i]; W.tc[w + pos] = col[i]; }
-    w += tot;
-    eq_seen += toteq;
+  if (threadIdx.x == 0) {
+    s_first = 0;
+    s_last = n;
+    int lg = 0;
+    for (int v = n; v > 1; v >>= 1) ++lg;
+    s_depth = 2 * lg;
+    s_fail = 0;
+  }
+  __syncthreads();
+  while (true) {
+    const int first = s_first, last = s_last;
+    if (last - first <= 3) break;
+    if (threadIdx.x == 0) {
+      if (s_depth == 0) {
+        s_fail = 1;
+      } else {
+        --s_depth;
+        const int x = first + 1, y = first + (last - first) / 2, z = last - 1;
+        int md;
+        if (trim_lt(E[x], E[y])) md = trim_lt(E[y], E[z]) ? y : (trim_lt(E[x], E[z]) ? z : x);
+        else md = trim_lt(E[x], E[z]) ? x : (trim_lt(E[y], E[z]) ? z : y);
+        const uint64_t t = E[first]; E[first] = E[md]; E[md] = t;
+      }
+    }
+    __syncthreads();
+    if (s_fail) break;
+    const uint64_t pv = E[first];
+    int nL = 0, nR = 0;
+    for (int c0 = first + 1; c0 < last; c0 += blockDim.x) {
+      const int j = c0 + threadIdx.x;
+      const bool in = j < last;
+      const uint64_t e = in ? E[j] : 0;
+      const int fl = in && !trim_lt(e, pv), fr = in && !trim_lt(pv, e);
+      int tl, tr;
+      const int ol = block_scan_db(fl, &tl, trim_db, trim_it++);
+      const int orr = block_scan_db(fr, &tr, trim_db, trim_it++);
+      if (fl && INB(nL + ol, B.work_n, 421)) PL[nL + ol] = j;
+      if (fr && INB(nR + orr, B.work_n, 422)) PR[nR + orr] = j;
+      nL += tl;
+      nR += tr;
+    }
+    __syncthreads();
+    // swaps made: the pairs i with L[i] < R[i] (a prefix of the pairs)
+    const int np = min(nL, nR);
+    int cnt = 0;
+    for (int i = threadIdx.x; i < np; i += blockDim.x) cnt += PL[i] < PR[nR - 1 - i];
+    const int k = block_sum_i(cnt, bs);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+      const int l = PL[i], r = PR[nR - 1 - i];
+      const uint64_t t = E[l]; E[l] = E[r]; E[r] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int cut = k == 0 ? PL[0] : min(k < nL ? PL[k] : last, PR[nR - k]);
+      if (cut <= nth) s_first = cut;
+      else s_last = cut;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    if (s_fail) {
+      // the depth limit ran out (the reference would switch to a heap selection): keep the
+      // newest points in storage order and report it
+      set_err(&B.maps[cs / B.O], SMG_E_TRIM);
+    } else {
+      for (int i = s_first + 1; i < s_last; ++i) {   // stable insertion sort of the last few
+        const uint64_t v = E[i];
+        int j = i;
+        while (j > s_first && trim_lt(v, E[j - 1])) { E[j] = E[j - 1]; --j; }
+        E[j] = v;
+      }
+    }
+  }
+  __syncthreads();
+  int w = 0;
+  if (!s_fail) {
+    for (int i = threadIdx.x; i < keep; i += blockDim.x) {
+      const int src = (int)(uint32_t)E[nth + i];
+      if (INB(src, n, 404)) { W.t4[i] = pts[src]; W.tc[i] = col[src]; }
+    }
+    w = keep;
+  } else {   // fallback: the keep newest in storage order
+    for (int i = threadIdx.x; i < n; i += blockDim.x) W.scr[i] = (double)__float_as_uint(pts[i].w);
+    __syncthreads();
+    const double cut = block_select(W.scr, n, nth, hist, bs);
+    int lt = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) lt += W.scr[i] < cut;
+    const int eq_drop = nth - block_sum_i(lt, bs);
+    int eq_seen = 0;
+    for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+      const int i = c0 + threadIdx.x;
+      const int is_eq = i < n && W.scr[i] == cut;
+      int toteq;
+      const int peq = block_scan_db(is_eq, &toteq, trim_db, trim_it++);
+      const int k = i < n && (W.scr[i] > cut || (is_eq && eq_seen + peq >= eq_drop));
+      int tot;
+      const int pos = block_scan_db(k, &tot, trim_db, trim_it++);
+      if (k && INB(w + pos, B.work_n, 404)) { W.t4[w + pos] = pts[i]; W.tc[w + pos] = col[i]; }
+      w += tot;
+      eq_seen += toteq;
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < w; i += blockDim.x) { pts[i] = W.t4[i]; col[i] = W.tc[i]; }

@@ -90,7 +90,8 @@ __global__ void __launch_bounds__(256) k_absent(Batch B) {
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), nwarps = gridDim.x * (blockDim.x >> 5);
   for (int b = gw; b < R->n_obj; b += nwarps) {
     ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
-    if (!o.confirmed || B.obj_hit[(size_t)m * B.O + b] || o.state == 1) continue;
+    if (!o.confirmed || o.held_by >= 0 || B.obj_hit[(size_t)m * B.O + b] || o.state == 1) continue;
+    if (o.parent) continue;   // an object put on / in another one stays where it was put
     if (dist3(o.pos, F.eef[0]) < (double)P.hand_r + 0.1 || dist3(o.pos, F.eef[1]) < (double)P.hand_r + 0.1) continue;
     const int ev = absent_evidence_warp(B, m, o, F);
     if (lane != 0 || !ev || B.touched[(size_t)m * B.O + b]) continue;
@@ -141,7 +142,8 @@ DEV int find_pos(const Batch& B, int m, uint32_t id) {
   return -1;
 }
 
-// remapId (objmap.cpp:314-318) on this frame's association and cloud lists
+// remapId (objmap.cpp:314-318) on this frame's association and cloud lists and on the objects'
+// parent links
 DEV void remap_id(const Batch& B, int m, uint32_t from, uint32_t to) {
   const MapRec& R = B.maps[m];
   const FrameDev& F = B.frames[m];
@@ -149,6 +151,10 @@ DEV void remap_id(const Batch& B, int m, uint32_t from, uint32_t to) {
     if (B.assoc[(size_t)m * B.max_det + k].obj_id == from) B.assoc[(size_t)m * B.max_det + k].obj_id = to;
   for (int e = 0; e < R.n_pts; ++e)
     if (B.ptsl[(size_t)m * B.max_det + e].obj_id == from) B.ptsl[(size_t)m * B.max_det + e].obj_id = to;
+  for (int i = 0; i < R.n_obj; ++i) {
+    ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, i))];
+    if (o.parent == from) o.parent = to;
+  }
 }
 
 #define RELINK_MAXC 256
@@ -210,7 +216,7 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
   for (int i = tid; i < nobj && staged; i += blockDim.x) {
     const ObjRec& o = obj_at(B, m, i);
     s_state[i] = o.state;
-    s_flags[i] = (o.appeared ? 1 : 0) | (o.confirmed ? 2 : 0) | (o.moved ? 4 : 0);
+    s_flags[i] = (o.appeared ? 1 : 0) | (o.confirmed ? 2 : 0) | (o.moved ? 4 : 0) | (o.held_by >= 0 ? 8 : 0);
     s_nobs[i] = (int)o.n_obs;
     s_cls[i] = o.cls;
     s_first[i] = o.first_seen;
@@ -226,17 +232,18 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
   // scalar tests of the relink candidates (a pair needs a gone object m), one thread per n;
   // the candidates are sorted by (distance, m id, n id) below, so their list order is free
   for (int i = tid; staged && i < nobj; i += blockDim.x) {
-    if (!(s_flags[i] & 1) || !(s_flags[i] & 2) || s_state[i] == 1 || s_nobs[i] < P.link_min_obs) continue;
+    if (!(s_flags[i] & 1) || !(s_flags[i] & 2) || (s_flags[i] & 8) || s_state[i] == 1 || s_nobs[i] < P.link_min_obs) continue;
     if (t - s_first[i] > P.link_window_s) continue;
     for (int j = 0; j < nobj; ++j) {
-      if (j == i || s_state[j] != 1 || !(s_flags[j] & 2) || (!(s_flags[j] & 4) && s_nobs[j] < P.spurious_obs)) continue;
+      if (j == i || s_state[j] != 1 || !(s_flags[j] & 2) || (s_flags[j] & 8) || (!(s_flags[j] & 4) && s_nobs[j] < P.spurious_obs))
+        continue;
       if (!(s_first[i] > s_last[j])) continue;
       const double d = dist3(&s_pos[3 * i], &s_pos[3 * j]);
       if (d > smin(P.link_max_d, P.link_d0 + P.link_v * (s_first[i] - s_last[j]))) continue;
       bool wait = false;
       if (t - s_first[i] < P.link_wait_s)
         for (int q = 0; q < nobj; ++q) {
-          if (q == i || q == j || !(s_flags[q] & 2) || s_state[q] == 1 || s_cls[q] != s_cls[i]) continue;
+          if (q == i || q == j || !(s_flags[q] & 2) || (s_flags[q] & 8) || s_state[q] == 1 || s_cls[q] != s_cls[i]) continue;
           if (s_last[q] < s_first[i] && dist3(&s_pos[3 * q], &s_pos[3 * i]) < d) { wait = true; break; }
         }
       if (wait) continue;
@@ -312,6 +319,7 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
     mo.moved = 1;
     mo.state = 2;
     mo.misses = 0;
+    mo.parent = 0;
     remap_id(B, m, pn_[p], pm_[p]);
     push_event(B, m, t, mo, 2, (4u << 24) | (uint32_t)p);
     erase_pos(B, m, ni, true);
@@ -347,7 +355,7 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
     if (b < R.n_obj) {
       const ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
       const CloudRec& C = B.clouds[(size_t)m * B.O + o.cloud_slot];
-      need = o.geo_ver != C.version && C.n >= 30;
+      need = o.held_by < 0 && o.geo_ver != C.version && C.n >= 30;
     }
     int tot;
     const int rank = before + block_scan_db(need, &tot, scan_db, it++);
@@ -424,8 +432,12 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
   for (int b = tid; b < n; b += blockDim.x) {
     const int slot = slot_at(B, m, b);
     ObjRec& o = B.objs[oglob(B, m, slot)];
-    o.hide = 0;
-    o.drop = o.geo == 1 || o.geo == 2;
+    if (o.held_by >= 0) {   // apStructObject returns false for a held object (objmap.cpp:1256)
+      o.drop = 0;
+    } else {
+      o.hide = 0;
+      o.drop = o.geo == 1 || o.geo == 2;
+    }
     bool rm;
     if (o.drop) { ++nstruct; rm = true; }
     else if (!o.confirmed) rm = F.stamp - o.last_seen > P.prune_s;

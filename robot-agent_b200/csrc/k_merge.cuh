@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(256) k_merge_gate(Batch B) {
   for (int b = tid; b < n; b += blockDim.x) {
     const ObjRec& o = obj_at(B, m, b);
     for (int k = 0; k < 3; ++k) { slo[3 * b + k] = o.lo[k]; shi[3 * b + k] = o.hi[k]; }
-    sst[b] = o.state;
+    sst[b] = o.held_by >= 0 ? 1 : o.state;   // held objects are left out like gone ones (objmap.cpp:1162-1165)
   }
   __syncthreads();
   // 2. box-gap and size gates of all pairs (objmap.cpp:1160-1173); this CTA takes every
@@ -231,6 +231,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
         a.misses = min(a.misses, b.misses);
         a.n_vis_miss += b.n_vis_miss;
         if (a.state != 0 && b.state == 0) a.state = 0;
+        if (!a.parent) { a.parent = b.parent; for (int k = 0; k < 3; ++k) a.parent_rel[k] = b.parent_rel[k]; }
       }
     }
     __syncthreads();
@@ -314,7 +315,12 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
       a.wall_like = a.wall_like && b.wall_like;
       a.confirmed = a.confirmed || b.confirmed;
       ++R->st.n_merge;
+      const uint32_t did = b.id;
       { const int pe = sh_pkb; if (INB(pe, R->n_obj, 604)) erase_pos(B, m, pe, false); }   // b's position (findPos)
+      for (int i = 0; i < R->n_obj; ++i) {   // remapId(did, kid) (objmap.cpp:1222) on the parent links
+        ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, i))];
+        if (o.parent == did) o.parent = a.id;
+      }
       push_event(B, m, t, a, 7, (1u << 24) | (uint32_t)R->n_evn++);
     }
     __syncthreads();

@@ -81,9 +81,9 @@ DEV float block_select_f(const float* a, int n, int k, int* hist, int* s_pick) {
   return f_unord(prefix);
 }
 
-// the cheap tests of objmap.cpp:1383 (every object here is an objprob object and none is held)
+// the cheap tests of objmap.cpp:1383 (every object here is an objprob object)
 DEV bool reenc_candidate(const Batch& B, int m, const ObjRec& o, double stamp) {
-  return o.confirmed && o.state != 1 && o.last_kf == stamp && B.clouds[(size_t)m * B.O + o.cloud_slot].n >= 30;
+  return o.confirmed && o.held_by < 0 && o.state != 1 && o.last_kf == stamp && B.clouds[(size_t)m * B.O + o.cloud_slot].n >= 30;
 }
 
 // viewKappa (bestview.cpp:77-81, objprob_math.h:78-87) with a visible fraction; the camera blur

@@ -333,6 +333,7 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
       const ObsRec& o = OB[OL[a]];
       if (act == 2) {   // new candidate (objmap.cpp:951-978)
         memset(&mo, 0, sizeof(ObjRec));
+        mo.held_by = -1;
         mo.id = s_newid[a];
         mo.cls = o.cls;
         for (int k = 0; k < 3; ++k) { mo.pos[k] = mo.first_pos[k] = o.pos[k]; mo.ext[k] = o.ext[k]; mo.lo[k] = o.lo[k]; mo.hi[k] = o.hi[k]; }
@@ -383,11 +384,12 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
           mo.wall_like = 2 * mo.n_wall_obs >= mo.n_ap_obs;
           if (!o.sec) {
             const double dt_seen = F.stamp - mo.last_seen;
+            if (mo.parent && dist3(mo.pos, o.pos) > 0.3) mo.parent = 0;
             if (mo.last_kf != F.stamp) ++mo.n_obs;
             mo.last_kf = F.stamp;
             const bool big = smax(smax(mo.hi[0] - mo.lo[0], mo.hi[1] - mo.lo[1]), smax(o.ext[0], o.ext[1])) > P.big;
             bool snap = false;
-            if (P.move_n > 0 && mo.trk_t > 0 && !o.trunc && F.cam_steady) {
+            if (P.move_n > 0 && mo.trk_t > 0 && mo.held_by < 0 && !o.trunc && F.cam_steady) {
               const double dt = F.stamp - mo.trk_t;
               const double sx = o.pos[0] - mo.trk_pos[0], sy = o.pos[1] - mo.trk_pos[1];
               const double sp = dt > 1e-6 && dt <= 0.6 ? sqrt(sx * sx + sy * sy) / dt : 0.0;
@@ -427,6 +429,7 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
               }
               if (dist3(mo.pos, mo.first_pos) > P.moved_d) mo.moved = 1;
               if (mo.moved && mo.state == 0) mo.state = 2;
+              mo.parent = 0;
             }
             const bool fresh = mo.first_seen == F.stamp;
             for (int k = 0; k < 3 && !snap; ++k) {

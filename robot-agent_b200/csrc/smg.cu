@@ -3,6 +3,8 @@
 //
 // Launch chain of one smg_push_frames call (all maps of the batch in every launch):
 //   k_begin         per-frame resets
+//   k_hands         grasp / hold / release, support links (objmap.cpp:435-506; only once a
+//                   gripper of the batch has closed)
 //   k_merge_pairs   apMergePass pair evaluation        (objmap.cpp:1154-1200)
 //   k_merge_apply   greedy merges (absorb + apMerge)   (objmap.cpp:1202-1224)
 //   k_obs           back-projection .. plane fit       (objmap.cpp:645-765)
@@ -32,6 +34,7 @@
 #include "k_text.cuh"
 #include "k_gather.cuh"
 #include "k_reenc.cuh"
+#include "k_hands.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -77,6 +80,11 @@ struct smg_batch {
   uint16_t* d_label = nullptr;
   unsigned char* d_emb = nullptr;
   std::vector<double> last_cam_t, last_cam_fwd;
+  // updateHands' per-hand gripper state of every map (ObjectMap::closed_, gref_, gref_t_, tried_;
+  // objmap.hpp:320-323), [2 * m + h]
+  std::vector<int> h_closed, h_tried;
+  std::vector<double> h_gref, h_gref_t;
+  bool hands_on = false;   // some map has tried a grasp: held objects and support links may exist
   long long launches = 0;
   long long h2d_host = 0;   // host-input bytes copied by the copy engines
   cudaStream_t last_stream = nullptr;
@@ -90,7 +98,7 @@ struct smg_batch {
 
 static const char* k_names[SMG_NUM_KERNELS] = {"k_begin", "k_merge_pairs", "k_merge_apply", "k_obs", "k_obs_finalize", "k_assoc",
                                                "k_update", "k_absent", "k_relink", "k_struct", "k_prune", "k_markview",
-                                               "k_cloud_add", "k_grid", "k_reenc"};
+                                               "k_cloud_add", "k_grid", "k_reenc", "k_hands"};
 
 static cudaEvent_t ev_get(smg_batch* b) {
   if (b->ev_pool.empty()) {
@@ -185,6 +193,12 @@ int smg_params_default(smg_params* p) {
   p->match_hi = 3.0f; p->vert_nz = 0.7f; p->match_cell = 0.025f; p->dense = 1;
   p->change_bins = 2; p->change_cells = 1; p->still_every = 50;
   p->reenc_max = 8; p->reenc_gain = 1.3; p->reenc_min_vis = 0.5; p->reenc_min_px = 24;   // objprob.hpp:90-93
+  // hands (objmap.hpp:66-76)
+  p->grasp_r = 0.12; p->grip_closed = 0.6f; p->n_hands = 1;
+  p->grasp_max_w = 0.06; p->grasp_min_gap = 0.005; p->grasp_w_tol = 0.025; p->grip_settle_s = 0.2; p->grip_settle_eps = 0.01;
+  const double gg[7][2] = {{0.0, 0.0}, {0.095, 0.01}, {0.231, 0.02}, {0.347, 0.03}, {0.408, 0.04}, {0.5236, 0.0551}, {0.7854, 0.0933}};
+  p->n_grip_gap = 7;
+  memcpy(p->grip_gap, gg, sizeof gg);
   return SMG_OK;
 }
 
@@ -314,7 +328,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
                int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out) {
   if (!p || !out || n_maps <= 0 || max_objects <= 0 || emb_dim <= 0 || emb_dim > 2048 || max_w <= 0 || max_h <= 0 || max_det <= 0 ||
       max_det > SMG_MAX_DET || grid_w <= 0 || grid_h <= 0 || p->topk <= 0 || p->topk > SMG_TOPK_MAX || p->bins <= 0 ||
-      p->bins > SMG_BINS_MAX || max_objects > PRUNE_MAX || p->cloud_cap <= 0 || p->voxel <= 0 || p->ransac_iters > RANSAC_MAX ||
+      p->bins > SMG_BINS_MAX || max_objects > PRUNE_MAX || p->n_grip_gap < 0 || p->n_grip_gap > 8 || p->cloud_cap <= 0 || p->voxel <= 0 || p->ransac_iters > RANSAC_MAX ||
       (size_t)max_h * ((max_w + 31) / 32) * 4 + RE_ZMAX * 4 > 227 * 1024)   // re-encode mask held in shared memory
     return fail(SMG_ERR_ARGS, "smg_create: bad arguments");
   *out = nullptr;
@@ -509,6 +523,10 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   }
   b->last_cam_t.assign(M, -1e300);
   b->last_cam_fwd.assign(3 * (size_t)M, 0.0);
+  b->h_closed.assign(2 * (size_t)M, 0);
+  b->h_tried.assign(2 * (size_t)M, 0);
+  b->h_gref.assign(2 * (size_t)M, 0.0);
+  b->h_gref_t.assign(2 * (size_t)M, -1e300);
   // kernels with large dynamic shared memory
   CK(cudaFuncSetAttribute(k_obs, cudaFuncAttributeMaxDynamicSharedMemorySize, OBS_SMEM));
   {
@@ -554,6 +572,13 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   k_begin<<<Mg, 128, 0, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({0, {e0, e1}}); } }
+  if (b->hands_on) {
+    cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+    k_hands<<<Mg, HANDS_THREADS, 0, st>>>(B);
+    ++b->launches;
+    if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after k_hands: ") + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } }
+    if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({15, {e0, e1}}); }
+  }
   // fork: the occupancy grid (Mapper2D::keyframe) is independent of the object chain
   CK(cudaEventRecord(efork, st));
   CK(cudaStreamWaitEvent(sgrid, efork, 0));
@@ -619,6 +644,19 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   CK(cudaStreamWaitEvent(st, ejoin, 0));   // join
   b->launches += 17;
   return SMG_OK;
+}
+
+// ObjectMap::gripGap (objmap.cpp:387-397): gripper value -> finger gap, piecewise linear
+static double grip_gap(const smg_params& P, double g) {
+  const int n = P.n_grip_gap;
+  if (n <= 0) return 0;
+  if (g <= P.grip_gap[0][0]) return P.grip_gap[0][1];
+  for (int i = 1; i < n; ++i)
+    if (g <= P.grip_gap[i][0]) {
+      const double a = (g - P.grip_gap[i - 1][0]) / std::max(1e-12, P.grip_gap[i][0] - P.grip_gap[i - 1][0]);
+      return P.grip_gap[i - 1][1] + a * (P.grip_gap[i][1] - P.grip_gap[i - 1][1]);
+    }
+  return P.grip_gap[n - 1][1];
 }
 
 int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, void* stream) {
@@ -724,7 +762,31 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     d.blur_fac = P.kap_blur_w > 0 ? std::exp(-std::max(0.0, (double)std::max(0.f, (float)cam_w)) / P.kap_blur_w) : 1.0;
     d.cos_th = std::cos(f.base[2]);
     d.sin_th = std::sin(f.base[2]);
+    // ObjectMap::updateHands' gripper state machine (objmap.cpp:448-472), host doubles like the
+    // reference; the device does the object side of what it decides
+    for (int h = 0; h < P.n_hands && h < 2; ++h) {
+      const size_t i = 2 * (size_t)m + h;
+      const float g = f.grip[h];
+      const bool closed = g < P.grip_closed;
+      if (b->h_gref_t[i] < -1e299 || std::fabs(g - b->h_gref[i]) > P.grip_settle_eps) { b->h_gref[i] = g; b->h_gref_t[i] = f.stamp; }
+      const bool settled = f.stamp - b->h_gref_t[i] >= P.grip_settle_s - 1e-9;
+      if (closed && !b->h_closed[i]) b->h_tried[i] = 0;
+      const double gap = grip_gap(P, g);
+      int act = 0;
+      if (closed && settled && !b->h_tried[i]) {
+        b->h_tried[i] = 1;
+        act |= 1;
+      } else if (closed && settled && gap < P.grasp_min_gap) {
+        act |= 2;
+      }
+      if (!closed && b->h_closed[i]) act |= 4;
+      b->h_closed[i] = closed;
+      d.hand_act[h] = act;
+      d.hand_gap[h] = gap;
+      if (act & 1) b->hands_on = true;
+    }
   }
+  for (int m = 0; m < n; ++m) b->h_frames[m].hands_on = b->hands_on;
   // Stream groups: maps [g*M/G, (g+1)*M/G) run their chain on stream g (the caller's stream
   // for g = 0), so the groups' kernels overlap; with host inputs, group g's chain starts as soon
   // as its own inputs have arrived on the copy stream.
@@ -927,6 +989,9 @@ int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap) {
     r.need_whole = o.need_whole;
     r.n_cams = o.n_cams;
     r.geo = o.geo;
+    r.held_by = o.held_by;
+    r.parent = o.parent;
+    for (int k = 0; k < 3; ++k) r.parent_rel[k] = o.parent_rel[k];
   }
   return R.n_obj;
 }

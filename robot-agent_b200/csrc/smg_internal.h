@@ -41,6 +41,7 @@
 #define SMG_E_CAP_EVENTS 16
 #define SMG_E_ARGS 32
 #define SMG_E_CAP_REENC 64   // more re-encode candidates in a keyframe than RE_CAND
+#define SMG_E_TRIM 128       // a cloud trim's selection ran past its depth limit (point order then differs)
 
 // Per (map, frame) input descriptor on the device (smg_frame + host-derived scalars).
 typedef struct {
@@ -71,6 +72,13 @@ typedef struct {
   double blur_fac;       // exp(-cam_w/blur_w) factor of viewKappa (1 when blur_w == 0)
   double cos_th, sin_th; // cos/sin of base yaw (grid.cpp:202)
   int32_t active;        // map takes part in this push
+  // ObjectMap::updateHands (objmap.cpp:435-506): the per-hand gripper state machine depends only
+  // on the gripper values and stamps, so the host runs it (host doubles, like the reference)
+  // and passes per hand: act bit 0 = try a grasp, bit 1 = release (closed to the end after a
+  // grasp), bit 2 = release (opened); gap = gripGap(grip) (objmap.cpp:387-397)
+  int32_t hand_act[2];
+  double hand_gap[2];
+  int32_t hands_on;      // run the hand step (some map of the batch has used a gripper)
 } FrameDev;
 
 // Observation (one detection after back-projection; scenemap objmap.cpp:52-74 `Obs`)
@@ -121,6 +129,10 @@ typedef struct __align__(16) {   // 16-byte aligned: staged in shared memory in 
   uint32_t geo_ver;
   int32_t geo, drop, hide;
   double nrm_frag;       // |r_frag|^2 (ApState::nrm_frag, refreshed whenever r_frag changes)
+  // hands (MapObject, objmap.hpp:175-178)
+  int32_t held_by;       // hand holding it, -1 = none
+  uint32_t parent;       // id of the object it rests on and follows, 0 = none
+  double parent_rel[3], held_rel[3], grasp_pos[3];
 } ObjRec;
 
 typedef struct {

@@ -27,7 +27,7 @@ class SmgFrame(C.Structure):
                 ("fx", C.c_float), ("fy", C.c_float), ("cx", C.c_float), ("cy", C.c_float), ("T_mc", C.c_double * 12),
                 ("T_bc", C.c_float * 12), ("base", C.c_double * 3), ("eef", C.c_double * 6), ("eef_base", C.c_float * 6),
                 ("n_det", C.c_int32), ("det_label", C.c_void_p), ("box", C.c_void_p), ("cls", C.c_void_p),
-                ("score", C.c_void_p), ("emb", C.c_void_p), ("emb_dtype", C.c_int32)]
+                ("score", C.c_void_p), ("emb", C.c_void_p), ("emb_dtype", C.c_int32), ("grip", C.c_float * 2)]
 
 
 class SmgReencReq(C.Structure):
@@ -43,7 +43,8 @@ class SmgObject(C.Structure):
                 ("max_det_z", C.c_double), ("last_kf", C.c_double), ("appeared", C.c_int32), ("cloud_n", C.c_int32),
                 ("cloud_version", C.c_uint32), ("cloud_org", C.c_double * 3), ("ap_ver", C.c_uint32),
                 ("k_frag", C.c_double), ("n_views", C.c_int32), ("n_ap_obs", C.c_int32), ("need_whole", C.c_int32),
-                ("P", C.c_double * 3), ("n_cams", C.c_int32), ("geo", C.c_int32)]
+                ("P", C.c_double * 3), ("n_cams", C.c_int32), ("geo", C.c_int32), ("held_by", C.c_int32),
+                ("parent", C.c_uint32), ("parent_rel", C.c_double * 3)]
 
 
 _lib = None
@@ -95,7 +96,7 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
            "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode"]
 
-NUM_KERNELS = 15
+NUM_KERNELS = 16
 
 
 def _ptr(a):
@@ -179,6 +180,8 @@ class Batch:
         keep += [dl, bx, cl, sc]
         f.det_label, f.box, f.cls, f.score = _ptr(dl), _ptr(bx), _ptr(cl), _ptr(sc)
         f.emb_dtype = emb_dtype
+        grip = np.asarray(fr.get("grip", (1.0, 1.0)), np.float32).reshape(-1)
+        f.grip[0], f.grip[1] = float(grip[0]), float(grip[1])
         if ptrs is not None:
             f.depth, f.label, f.emb = ptrs["depth"], ptrs["label"], ptrs["emb"]
         else:

@@ -4,9 +4,9 @@ from __future__ import annotations
 import numpy as np
 
 EXACT_FIELDS = ["id", "cls", "n_obs", "state", "confirmed", "moved", "misses", "n_vis_miss", "appeared", "cloud_n",
-                "cloud_version", "ap_ver", "n_views", "n_ap_obs", "need_whole", "n_cams", "geo"]
+                "cloud_version", "ap_ver", "n_views", "n_ap_obs", "need_whole", "n_cams", "geo", "held_by", "parent"]
 FLOAT_FIELDS = ["pos", "ext", "first_pos", "lo", "hi", "first_seen", "last_seen", "max_det_z", "last_kf", "k_frag",
-                "P", "cloud_org"]
+                "P", "cloud_org", "parent_rel"]
 
 
 def compare_objects(ref_objs: list, gpu_objs: list, rel: float = 1e-5) -> list:

@@ -63,3 +63,10 @@ def test_parity_engine_params():
     """The reference's engine parameter file (yolo26n-seg-obj-416 obj_params), bf16 embeddings."""
     _need()
     _run_variant(variants.engine_params(), bf16=True)
+
+
+def test_parity_hands():
+    """A gripper picks up a small box, carries it, puts it on a larger one that is then pushed:
+    grasp, hold, release, support link and the supported object following (updateHands)."""
+    _need()
+    _run_variant(variants.hands(), deep_every=5)

@@ -15,7 +15,7 @@ def _need():
         pytest.skip("reference oracle library not built")
 
 
-@pytest.mark.parametrize("name", ["structure", "moving"])
+@pytest.mark.parametrize("name", ["structure", "moving", "hands"])
 def test_variant_fires_its_rules_on_the_reference(name):
     _need()
     from oracle import ref

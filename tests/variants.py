@@ -42,3 +42,49 @@ def make_gen(v: dict, D: int = 1152, bf16: bool = False):
     kw = dict(v["gen"])
     seed = synth.map_seed(kw.pop("seed_base"), 0)
     return synth.BoxRoom(seed=seed, n_frames=v["n_frames"], D=D, bf16=bf16, **kw)
+
+
+def hands(n_frames: int = 110, seed_base: int = 41, support: int = 2) -> dict:
+    """A robot hand picks a small box off a larger one, carries it, puts it back on top (the
+    support link), and the larger box is then pushed: grasp, hold (the object follows the hand),
+    release, and an object that follows its support.  The small box is rendered where the hand
+    carries it; the hand's gripper closes at frame 40 and opens at frame 66."""
+    import numpy as np
+    from scenemap_b200 import synth
+    g0 = synth.BoxRoom(seed=synth.map_seed(seed_base, 0), n_frames=1)
+    S = g0.scene
+    b = S.box[support]
+    cx, cy, top = 0.5 * (b.lo[0] + b.hi[0]), 0.5 * (b.lo[1] + b.hi[1]), b.hi[2]
+    small = ((cx - 0.02, cy - 0.025, top), (cx + 0.02, cy + 0.025, top + 0.10))
+    k_small = S.n_boxes   # index of the added box
+    far = np.full((2, 3), 1000.0)
+    path = {}
+    p = np.array([cx, cy, top + 0.05])
+    for f in range(40, 66):
+        if 45 <= f < 50:
+            p = p + np.array([0.0, 0.0, 0.03])      # lift
+        elif 50 <= f < 58:
+            p = p + np.array([0.02, 0.0, 0.0])      # carry
+        elif 58 <= f < 63:
+            p = p + np.array([0.0, 0.0, -0.03])     # put down on the support, offset in x
+        path[f] = p.copy()
+    moves = []
+    prev = np.array([cx, cy, top + 0.05])
+    for f in range(40, 66):
+        d = path[f] - prev
+        if np.any(d != 0):
+            moves.append((f, k_small, tuple(float(x) for x in d)))
+        prev = path[f]
+    for f in range(80, 92):   # push the support, with the small box on it
+        moves.append((f, support, (0.03, 0.0, 0.0)))
+        moves.append((f, k_small, (0.03, 0.0, 0.0)))
+
+    def hand(f):
+        if f in path:
+            eef = far.copy()
+            eef[0] = path[f]
+            return eef, np.array([0.35 if f < 66 else 1.0, 1.0], np.float32)
+        return far, np.ones(2, np.float32)
+
+    return dict(gen=dict(seed_base=seed_base, box_extra=[small], box_moves=moves, hands=hand), kv="", n_frames=n_frames,
+                stats=(), events=(4, 5))
