@@ -103,11 +103,11 @@ typedef struct smg_params {
   double grip_gap[8][2];
 } smg_params;
 
-/* One frame of one map.  depth/label/emb/dets live in device memory (SMG_MEM_DEVICE) or in
- * host memory (SMG_MEM_HOST: copied in by the call, on the caller's stream).
- * The detector mask of detection k is the set of pixels whose label equals det_label[k]
- * (mask grid = depth image grid); the reference's bit-mask form (scenemap.h:20-34) maps to
- * it one to one when mask_sx = mask_sy = 1 and mask_ox = mask_oy = 0. */
+/* One frame of one map.  depth/label/emb/dets/masks live in device memory (SMG_MEM_DEVICE) or
+ * in host memory (SMG_MEM_HOST: copied in by the call, on the caller's stream).
+ * Detections come in one of two forms: a label image (the mask of detection k is the set of
+ * pixels whose label equals det_label[k]: a mask grid equal to the depth grid), or the
+ * reference's bit masks on their own grid (mask_bits below). */
 typedef struct smg_frame {
   double stamp;
   int32_t w, h;
@@ -128,6 +128,19 @@ typedef struct smg_frame {
   int32_t emb_dtype;           /* SMG_EMB_F32 | SMG_EMB_BF16 */
   float grip[2];               /* gripper values (ObjFrame::grip, rad; the reference's default is
                                   1 = open: a zero-filled frame means a closed gripper) */
+  /* The detector's masks in the reference's own form (sm_detections, scenemap
+   * include/scenemap.h:20-34), used instead of label/det_label when mask_bits is set:
+   * n_det x ceil(mask_w * mask_h / 32) words, cell (i, j) is bit j * mask_w + i, LSB first;
+   * cell (i, j) covers detector-image x in [i sx + ox, (i+1) sx + ox), y likewise.  img_w x img_h
+   * is the detector image (box is in its pixels); 0 means the depth image's size.  The mask grid
+   * may be at most max_w x max_h cells. */
+  const uint32_t* mask_bits;
+  int32_t mask_w, mask_h;
+  float mask_sx, mask_sy, mask_ox, mask_oy;
+  int32_t img_w, img_h;
+  /* ObjFrame::depth_mm: depth as uint16 millimetres (read as mm * 1e-3f, like the reference),
+   * used when depth is NULL */
+  const uint16_t* depth_mm;
 } smg_frame;
 
 typedef struct smg_batch smg_batch;

@@ -24,7 +24,10 @@ class RfFrame(C.Structure):
                 ("eef", C.c_double * 6), ("eef_base", C.c_float * 6), ("n_det", C.c_int),
                 ("det_label", C.POINTER(C.c_uint16)), ("box", C.POINTER(C.c_float)), ("cls", C.POINTER(C.c_int32)),
                 ("score", C.POINTER(C.c_float)), ("emb", C.POINTER(C.c_float)), ("emb_dim", C.c_int),
-                ("grid_only", C.c_int), ("grip", C.c_float * 2)]
+                ("grid_only", C.c_int), ("grip", C.c_float * 2), ("mask_bits", C.POINTER(C.c_uint32)),
+                ("mask_w", C.c_int), ("mask_h", C.c_int), ("mask_sx", C.c_float), ("mask_sy", C.c_float),
+                ("mask_ox", C.c_float), ("mask_oy", C.c_float), ("img_w", C.c_int), ("img_h", C.c_int),
+                ("depth_mm", C.POINTER(C.c_uint16))]
 
 
 class RfObj(C.Structure):
@@ -120,11 +123,25 @@ def make_rf_frame(fr: dict, keep: list) -> RfFrame:
     f = RfFrame()
     f.stamp = fr["stamp"]
     f.w, f.h = fr["w"], fr["h"]
-    depth = np.ascontiguousarray(fr["depth"], np.float32)
-    label = np.ascontiguousarray(fr["label"], np.uint16)
-    keep += [depth, label]
-    f.depth = _p(depth, C.c_float)
-    f.label = _p(label, C.c_uint16)
+    if fr.get("depth_mm") is not None:   # millimetre depth instead of metres
+        dmm = np.ascontiguousarray(fr["depth_mm"], np.uint16)
+        keep.append(dmm)
+        f.depth_mm = _p(dmm, C.c_uint16)
+    else:
+        depth = np.ascontiguousarray(fr["depth"], np.float32)
+        keep.append(depth)
+        f.depth = _p(depth, C.c_float)
+    if fr.get("label") is not None:
+        label = np.ascontiguousarray(fr["label"], np.uint16)
+        keep.append(label)
+        f.label = _p(label, C.c_uint16)
+    if fr.get("mask_bits") is not None:   # the detector's bit masks on their own grid
+        mb = np.ascontiguousarray(fr["mask_bits"], np.uint32)
+        keep.append(mb)
+        f.mask_bits = _p(mb, C.c_uint32)
+        f.mask_w, f.mask_h = fr["mask_w"], fr["mask_h"]
+        f.mask_sx, f.mask_sy, f.mask_ox, f.mask_oy = fr["mask_affine"]
+    f.img_w, f.img_h = fr.get("img_w", 0), fr.get("img_h", 0)
     f.fx, f.fy, f.cx, f.cy = fr["fx"], fr["fy"], fr["cx"], fr["cy"]
     for i in range(12):
         f.T_mc[i] = fr["T_mc"][i]

@@ -48,6 +48,12 @@ typedef struct {
   int emb_dim;
   int grid_only;          // 1: keyframe only (no detections)
   float grip[2];          // gripper values (ObjFrame::grip; 1 = open)
+  // detector bit masks on their own grid (sm_detections), used instead of the label image
+  const uint32_t* mask_bits;
+  int mask_w, mask_h;
+  float mask_sx, mask_sy, mask_ox, mask_oy;
+  int img_w, img_h;       // detector image (0 = the depth image's size)
+  const uint16_t* depth_mm;   // ObjFrame::depth_mm / DepthView::mm, when depth is null
 } rf_frame;
 
 typedef struct {
@@ -121,12 +127,13 @@ void ref_destroy(void* h) { delete static_cast<RefMap*>(h); }
 
 int ref_frame(void* h, const rf_frame* f) {
   RefMap* m = static_cast<RefMap*>(h);
-  if (!m || !f || f->w <= 0 || f->h <= 0 || !f->depth) return -1;
+  if (!m || !f || f->w <= 0 || f->h <= 0 || (!f->depth && !f->depth_mm)) return -1;
   if (m->mapper) {   // Mapper2D::keyframe as capi.cpp:809-820 sets it up (no FK capsules)
     DepthView dv;
     dv.w = f->w;
     dv.h = f->h;
     dv.m = f->depth;
+    dv.mm = f->depth ? nullptr : f->depth_mm;
     dv.step = std::max(1, int(std::lround(f->w / 160.0)));
     dv.fx = f->fx; dv.fy = f->fy; dv.cx = f->cx; dv.cy = f->cy;
     memcpy(dv.T_bc, f->T_bc, sizeof(dv.T_bc));
@@ -137,36 +144,49 @@ int ref_frame(void* h, const rf_frame* f) {
   }
   m->reenc.clear();
   if (f->grid_only) return 0;
-  // label image -> sm_detections (mask grid = image grid)
+  // detections: the caller's bit masks, or the label image turned into bit masks on the image
+  // grid (sm_detections, scenemap include/scenemap.h:20-34)
   const int n = f->n_det;
-  const size_t words = (size_t(f->w) * f->h + 31) / 32;
-  m->bits.assign(words * size_t(std::max(0, n)), 0u);
-  std::vector<size_t> slot(65536, SIZE_MAX);
-  for (int k = 0; k < n; ++k) slot[f->det_label[k]] = size_t(k);
-  if (f->label)
-    for (size_t c = 0; c < size_t(f->w) * f->h; ++c) {
-      const size_t k = slot[f->label[c]];
-      if (k != SIZE_MAX) m->bits[k * words + (c >> 5)] |= 1u << (c & 31);
-    }
+  const int img_w = f->img_w > 0 ? f->img_w : f->w, img_h = f->img_h > 0 ? f->img_h : f->h;
   sm_detections d;
   memset(&d, 0, sizeof(d));
   d.stamp = f->stamp;
-  d.img_w = f->w;
-  d.img_h = f->h;
+  d.img_w = img_w;
+  d.img_h = img_h;
   d.n = n;
   d.cls = f->cls;
   d.score = f->score;
   d.box = f->box;
-  d.mask_w = f->w;
-  d.mask_h = f->h;
-  d.mask_sx = d.mask_sy = 1.f;
-  d.mask_ox = d.mask_oy = 0.f;
-  d.mask_bits = m->bits.data();
+  if (f->mask_bits) {
+    d.mask_w = f->mask_w;
+    d.mask_h = f->mask_h;
+    d.mask_sx = f->mask_sx;
+    d.mask_sy = f->mask_sy;
+    d.mask_ox = f->mask_ox;
+    d.mask_oy = f->mask_oy;
+    d.mask_bits = f->mask_bits;
+  } else {
+    const size_t words = (size_t(f->w) * f->h + 31) / 32;
+    m->bits.assign(words * size_t(std::max(0, n)), 0u);
+    std::vector<size_t> slot(65536, SIZE_MAX);
+    for (int k = 0; k < n; ++k) slot[f->det_label[k]] = size_t(k);
+    if (f->label)
+      for (size_t c = 0; c < size_t(f->w) * f->h; ++c) {
+        const size_t k = slot[f->label[c]];
+        if (k != SIZE_MAX) m->bits[k * words + (c >> 5)] |= 1u << (c & 31);
+      }
+    d.mask_w = f->w;
+    d.mask_h = f->h;
+    d.mask_sx = d.mask_sy = 1.f;
+    d.mask_ox = d.mask_oy = 0.f;
+    d.mask_bits = m->bits.data();
+  }
   ObjFrame F;
   F.stamp = f->stamp;
   F.w = f->w;
   F.h = f->h;
   F.depth_m = f->depth;
+  F.depth_mm = f->depth ? nullptr : f->depth_mm;
   F.fx = f->fx; F.fy = f->fy; F.cx = f->cx; F.cy = f->cy;
   memcpy(F.T_mc, f->T_mc, sizeof(F.T_mc));
   F.dets = n > 0 ? &d : nullptr;
@@ -184,8 +204,9 @@ int ref_frame(void* h, const rf_frame* f) {
   for (const ObsPoints& q : m->pts) m->om.addPoints(q.obj_id, q.xyz.data(), nullptr, int(q.px.size() / 2), f->stamp);
   // whole-object re-encode requests on frames with detection embeddings (capi.cpp:1002-1005),
   // the mask grid being the image grid
-  if (n > 0 && f->emb) m->om.buildReencode(F, f->w, f->h, f->w, f->h, 1.f, 1.f, 0.f, 0.f, &m->reenc);
-  m->reenc_words = int((size_t(f->w) * f->h + 31) / 32);
+  if (n > 0 && f->emb)
+    m->om.buildReencode(F, d.img_w, d.img_h, d.mask_w, d.mask_h, d.mask_sx, d.mask_sy, d.mask_ox, d.mask_oy, &m->reenc);
+  m->reenc_words = int((size_t(d.mask_w) * d.mask_h + 31) / 32);
   return 0;
 }
 

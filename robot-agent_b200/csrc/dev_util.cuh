@@ -546,6 +546,38 @@ DEV double dist3(const double* a, const double* b) {
 }
 
 DEV void set_err(MapRec* m, int bit) { atomicOr(&m->err, bit); }
+
+// Scan box of detection k in depth pixels (objmap.cpp:648-652): the detector box scaled from
+// the detector image to the depth image (float scale, truncation to int), grown by one pixel
+// and clipped to the frame.
+DEV void det_scan_box(const FrameDev& F, int k, int* u0, int* u1, int* v0, int* v1) {
+  const float* b = F.box[k];
+  *u0 = max(0, (int)(b[0] * F.sxu_f) - 1);
+  *u1 = min(F.w - 1, (int)(b[2] * F.sxu_f) + 1);
+  *v0 = max(0, (int)(b[1] * F.syv_f) - 1);
+  *v1 = min(F.h - 1, (int)(b[3] * F.syv_f) + 1);
+}
+
+// Bit-mask form of detection k's mask (sm_detections): depth pixel (u, v) -> detector pixel
+// centre -> mask cell, 1-cell 4-neighbour erosion, rows at the grid's edge skipped
+// (objmap.cpp:655-678).  pu, pv: the detector pixel (PU, PV of the observation's points).
+DEV bool det_bits_at(const FrameDev& F, int k, int u, int v, int* pu, int* pv) {
+  const float yi = ((float)v + 0.5f) / F.syv_f;
+  const int j = (int)floorf((yi - F.mask_oy) / F.mask_sy);
+  const int MW = F.mask_w, MH = F.mask_h;
+  if (j < 1 || j >= MH - 1) return false;
+  const float xi = ((float)u + 0.5f) / F.sxu_f;
+  const int i = (int)floorf((xi - F.mask_ox) / F.mask_sx);
+  const uint32_t* bits = F.mask_bits + (size_t)k * F.mask_words;
+  auto bit = [&](int a, int c) -> bool {
+    if (a < 0 || c < 0 || a >= MW || c >= MH) return false;
+    const size_t q = (size_t)c * MW + a;
+    return (bits[q >> 5] >> (q & 31)) & 1u;
+  };
+  *pu = (int)xi;
+  *pv = (int)yi;
+  return bit(i, j) && bit(i - 1, j) && bit(i + 1, j) && bit(i, j - 1) && bit(i, j + 1);
+}
 DEV void wk_add(MapRec* m, int k, long long v) {
   if (v) atomicAdd((unsigned long long*)&m->wk[k], (unsigned long long)v);
 }

@@ -1,9 +1,9 @@
 // Host-input gather: with pinned (device-accessible) host frames, the chain's staging images
 // receive only the pixels the chain reads, fetched by the SMs straight from host memory, instead
 // of whole-frame copies.  Which pixels a kernel reads is fixed by the frame's descriptor alone:
-//  - k_obs: depth over each detection's scan box [u0, u1] x [v0, v1] and labels over that box
-//    grown by one pixel (the 4-neighbour erosion), with u0 = max(0, int(x0) - 1) etc.
-//    (objmap.cpp:648-652, the same expressions as k_obs);
+//  - k_obs: depth over each detection's scan box [u0, u1] x [v0, v1] and, for the label-image
+//    form, labels over that box grown by one pixel (the 4-neighbour erosion), with
+//    u0 = max(0, int(x0 * sx) - 1) etc. (objmap.cpp:648-652, det_scan_box as k_obs uses it);
 //  - k_grid: the depth rows v = j * step (makeScan's grid, scan.cpp:233-251);
 //  - k_markview: the depth rows v = stp/2 + j * stp (objmap.cpp:219-245).
 // Those whole rows travel by strided copies on the copy engines, beside this kernel; the kernel
@@ -23,7 +23,7 @@ __global__ void __launch_bounds__(GATHER_THREADS) k_gather(Batch B) {
   const int v = blockIdx.x, m = B.map0 + blockIdx.y, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active || !F.depth_host || v >= F.h) return;
-  const int W = F.w, H = F.h, nw = (W + 31) >> 5;
+  const int W = F.w, nw = (W + 31) >> 5;
   if (W > GATHER_WMAX) return;   // rejected on the host
   // whole rows (copied by the copy engines): makeScan's and markView's sample rows
   const int step = max(1, (int)llround(F.w / 160.0));
@@ -41,9 +41,8 @@ __global__ void __launch_bounds__(GATHER_THREADS) k_gather(Batch B) {
     }
   };
   for (int k = tid; k < F.n_det; k += blockDim.x) {
-    const float* b = F.box[k];
-    const int u0 = max(0, (int)(b[0]) - 1), u1 = min(W - 1, (int)(b[2]) + 1);
-    const int v0 = max(0, (int)(b[1]) - 1), v1 = min(H - 1, (int)(b[3]) + 1);
+    int u0, u1, v0, v1;
+    det_scan_box(F, k, &u0, &u1, &v0, &v1);
     if (u1 < u0 || v < v0 - 1 || v > v1 + 1) continue;
     set_bits(lmask, max(0, u0 - 1), min(W - 1, u1 + 1));
     if (!full && v >= v0 && v <= v1) set_bits(dmask, u0, u1);

@@ -488,7 +488,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   const smg_params& P = B.p;
   const int W = F.w, H = F.h;
 #ifdef SMG_CHECKS
-  if (F.depth == nullptr || F.label == nullptr || W <= 0 || H <= 0 || W > B.W || H > B.H || m >= B.M) {
+  if (F.depth == nullptr || (F.label == nullptr && F.mask_bits == nullptr) || W <= 0 || H <= 0 || W > B.W || H > B.H || m >= B.M) {
     if (tid == 0) smg_chk_fail(110, (long long)(size_t)F.depth, (long long)(size_t)F.label);
     return;
   }
@@ -507,11 +507,11 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   int32_t* CP = B.cpx + slot * 2 * B.pmax;
   double* SCR = B.sel + slot * 4 * B.pmax;
   const uint16_t L = F.det_label[k];
-  const float* b = F.box[k];
-  // box scan (objmap.cpp:648-652); label grid == depth grid, so the detection->depth scale is 1
+  const bool bits_form = F.mask_bits != nullptr;
+  // box scan (objmap.cpp:648-652): detector box -> depth pixels
   const int st = P.step > 1 ? P.step : 1;
-  const int u0 = max(0, (int)(b[0]) - 1), u1 = min(W - 1, (int)(b[2]) + 1);
-  const int v0 = max(0, (int)(b[1]) - 1), v1 = min(H - 1, (int)(b[3]) + 1);
+  int u0, u1, v0, v1;
+  det_scan_box(F, k, &u0, &u1, &v0, &v1);
   const double box_px = (double)max(0, u1 - u0 + 1) * (double)max(0, v1 - v0 + 1);
   const int sk = max(st, (int)ceil(sqrt(box_px / (double)max(1, P.max_pts))));
   const int ncols = u1 >= u0 ? (u1 - u0) / sk + 1 : 0, nrows = v1 >= v0 ? (v1 - v0) / sk + 1 : 0;
@@ -539,8 +539,15 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
       if (idx < npix) {
         const int r = idx / ncols, cc = idx - r * ncols;
         const int uu = u0 + cc * sk, vv = v0 + r * sk;
-        // mask cell (i, j) = pixel (u, v); 1-cell erosion; rows j < 1 or j >= MH-1 are skipped
-        if (vv >= 1 && vv < H - 1 && INB((size_t)vv * W + uu, (size_t)W * H, 111)) {
+        if (bits_form) {   // the detector's bit masks on their own grid
+          int pu, pv;
+          if (det_bits_at(F, k, uu, vv, &pu, &pv) && INB((size_t)vv * W + uu, (size_t)W * H, 111)) {
+            const float z = F.depth[(size_t)vv * W + uu];
+            if (z > P.zmin && z < P.zmax) { okm |= 1 << j; zv[j] = z; }
+          }
+        } else if (vv >= 1 && vv < H - 1 && INB((size_t)vv * W + uu, (size_t)W * H, 111)) {
+          // label image: mask cell (i, j) = pixel (u, v); 1-cell erosion; rows j < 1 or j >= MH-1
+          // are skipped
           const size_t at = (size_t)vv * W + uu;
           const uint16_t* lp = F.label + at;
           const bool lm = (lp[0] == L) & (uu > 0 && lp[-1] == L) & (uu + 1 < W && lp[1] == L) & (lp[-W] == L) & (lp[W] == L);
@@ -564,7 +571,12 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
         Y[o] = T[4] * xc + T[5] * yc + T[6] * zd + T[7];
         Z[o] = T[8] * xc + T[9] * yc + T[10] * zd + T[11];
         ZC[o] = zd;
-        PU[o] = uu; PV[o] = vv;
+        if (bits_form) {
+          PU[o] = (int)(((float)uu + 0.5f) / F.sxu_f);
+          PV[o] = (int)(((float)vv + 0.5f) / F.syv_f);
+        } else {
+          PU[o] = uu; PV[o] = vv;
+        }
       }
       ++o;
     }
@@ -667,7 +679,8 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     for (int a = 0; a < 3; ++a) { md[a] = sel9[3 * a]; lo[a] = sel9[3 * a + 1]; hi[a] = sel9[3 * a + 2]; }
     __syncthreads();
   }
-  const int trunc = (b[0] <= 2 || b[1] <= 2 || b[2] >= W - 3 || b[3] >= H - 3);
+  const float* b = F.box[k];   // detector-image pixels
+  const int trunc = (b[0] <= 2 || b[1] <= 2 || b[2] >= F.img_w - 3 || b[3] >= F.img_h - 3);
   if (tid == 0) {
     O->det = k;
     O->sk = sk;
@@ -680,7 +693,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     for (int a = 0; a < 3; ++a) { O->pos[a] = md[a]; O->lo[a] = lo[a]; O->hi[a] = hi[a]; O->ext[a] = hi[a] - lo[a]; }
     O->floor_drop = hi[2] < P.floor_h;   // no floor-level class table: floorLevel() is false
     // viewKappa of a detection fragment (objmap.cpp:757-762, bestview.cpp:77-81)
-    const float size_px = (float)sqrt((double)np * sk * sk / smax(1e-9, 1.0));
+    const float size_px = (float)sqrt((double)np * sk * sk / smax(1e-9, (double)F.sxu_f * (double)F.syv_f));
     const float depth_m = (float)zmed;
     O->kappa = view_kappa((double)fmaxf(0.f, size_px), trunc, (double)fmaxf(0.f, depth_m), P.kap_k0, P.kap_s0, P.kap_trunc,
                           P.kap_d0, P.kap_occ, P.kap_blur_w, F.blur_fac);

@@ -107,9 +107,8 @@ DEV float reenc_depth(const FrameDev& F, int u, int v, int step, int stp, int& h
   if (!F.depth_host) return F.depth[i];
   if (v % step == 0 || (v >= stp / 2 && (v - stp / 2) % stp == 0)) return F.depth[i];
   for (int k = 0; k < F.n_det; ++k) {
-    const float* b = F.box[k];
-    const int u0 = max(0, (int)(b[0]) - 1), u1 = min(F.w - 1, (int)(b[2]) + 1);
-    const int v0 = max(0, (int)(b[1]) - 1), v1 = min(F.h - 1, (int)(b[3]) + 1);
+    int u0, u1, v0, v1;
+    det_scan_box(F, k, &u0, &u1, &v0, &v1);
     if (u >= u0 && u <= u1 && v >= v0 && v <= v1) return F.depth[i];
   }
   ++host_reads;
@@ -132,9 +131,11 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
   }
   const smg_params& P = B.p;
   const double* T = F.T_mc;
-  // the mask grid is the image grid (smg_frame): mask_w = img_w = w, scale 1, offset 0
-  const int mw = F.w, mh = F.h, img_w = F.w, img_h = F.h;
-  const float msx = 1.f, msy = 1.f;
+  // the detector's mask grid and its affine to detector pixels; the label-image form has the
+  // depth grid as its mask grid (scale 1, offset 0)
+  const int mw = F.mask_w, mh = F.mask_h, img_w = F.img_w, img_h = F.img_h;
+  const double msx = F.mask_sx, msy = F.mask_sy, mox = F.mask_ox, moy = F.mask_oy;
+  const double sxu = F.sxu_d, syv = F.syv_d;
   const int wpr = (mw + 31) >> 5, nwords = mh * wpr;
   const int step = max(1, (int)llround(F.w / 160.0)), stp_mv = max(1, F.w / 32);
   uint32_t* g = (uint32_t*)re_smem;
@@ -199,14 +200,12 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
         const int zi = __shfl_sync(am, zb, lead) + __popc(am & ((1u << lane) - 1u));
         if (INB(zi, RE_ZMAX, 802)) zs[zi] = (float)cz;
       }
-      // detection pixel -> mask cells, painted over the voxel's footprint.  The reference divides
-      // by the detection/depth scale and the mask scale and subtracts the mask offset; with the
-      // mask grid equal to the image grid those are divisions by 1.0 and subtractions of 0.0,
-      // exact identities, so they are left out.
-      const double ui = ud, vi = vd;
-      const double rpx = 0.6 * P.voxel * (double)F.fx / cz;
-      const int i0 = (int)floor(ui - rpx), i1 = (int)floor(ui + rpx);
-      const int j0 = (int)floor(vi - rpx), j1 = (int)floor(vi + rpx);
+      // depth pixel -> detector pixel -> mask cells, painted over the voxel's footprint
+      // (objmap.cpp:1403-1410; for the label-image form the scales are 1 and the offsets 0)
+      const double ui = ud / sxu, vi = vd / syv;
+      const double rpx = 0.6 * P.voxel * (double)F.fx / cz / sxu;
+      const int i0 = (int)floor((ui - rpx - mox) / msx), i1 = (int)floor((ui + rpx - mox) / msx);
+      const int j0 = (int)floor((vi - rpx - moy) / msy), j1 = (int)floor((vi + rpx - moy) / msy);
       const int ia = max(0, i0), ib = min(mw - 1, i1), ja = max(0, j0), jb = min(mh - 1, j1);
       if (ia <= ib && ja <= jb) { pi0 = min(pi0, ia); pi1 = max(pi1, ib); pj0 = min(pj0, ja); pj1 = max(pj1, jb); }
       for (int jj = ja; jj <= jb; ++jj) {
@@ -259,7 +258,7 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
         area += __popc(g2);
       }
       area = block_sum_ll(area, bs);
-      size_px = sqrt((double)area * (double)msx * (double)msy);
+      size_px = sqrt((double)area * msx * msy);
       ok = !(size_px < (double)P.reenc_min_px);
     }
     float zmed = 0.f;

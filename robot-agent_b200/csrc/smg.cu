@@ -79,6 +79,9 @@ struct smg_batch {
   float* d_depth = nullptr;       // staging for SMG_MEM_HOST
   uint16_t* d_label = nullptr;
   unsigned char* d_emb = nullptr;
+  uint16_t* d_depth_mm = nullptr;  // staging of host millimetre depth
+  uint32_t* d_mask = nullptr;      // staging of host detector bit masks: M x max_det x mask_words_max
+  size_t mask_words_max = 0;       // ceil(max_w * max_h / 32)
   std::vector<double> last_cam_t, last_cam_fwd;
   // updateHands' per-hand gripper state of every map (ObjectMap::closed_, gref_, gref_t_, tried_;
   // objmap.hpp:320-323), [2 * m + h]
@@ -455,6 +458,9 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(b->d_depth, (size_t)M * max_w * max_h);
   DA(b->d_label, (size_t)M * max_w * max_h);
   DA(b->d_emb, (size_t)M * max_det * D * 4);
+  DA(b->d_depth_mm, (size_t)M * max_w * max_h);
+  b->mask_words_max = ((size_t)max_w * max_h + 31) / 32;
+  DA(b->d_mask, (size_t)M * max_det * b->mask_words_max);
   // host-side initial state
   {
     std::vector<MapRec> maps((size_t)M);
@@ -541,6 +547,18 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   CK(cudaDeviceSynchronize());
   *out = b;
   return SMG_OK;
+}
+
+// ObjFrame::depth_mm: every reference reader takes mm * 1e-3f (objmap.cpp:227, :269, :677,
+// :1400, scan.cpp:120); the chain reads the same floats from the staging image
+__global__ void k_depth_mm(Batch B) {
+  const int m = B.map0 + blockIdx.y;
+  const FrameDev& F = B.frames[m];
+  if (!F.active || !F.depth_mm) return;
+  const size_t n = (size_t)F.w * F.h;
+  float* out = const_cast<float*>(F.depth);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = (float)F.depth_mm[i] * 1e-3f;
 }
 
 __global__ void k_begin(Batch B) {
@@ -669,9 +687,13 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   const smg_params& P = B.p;
   for (int i = 0; i < n; ++i) {
     const smg_frame& f = frames[i];
-    if (f.w <= 0 || f.h <= 0 || f.w > b->max_w || f.h > b->max_h || !f.depth || f.n_det < 0 || f.n_det > B.max_det ||
-        (f.n_det > 0 && (!f.label || !f.det_label || !f.box || !f.cls)) || (f.emb && f.emb_dtype != SMG_EMB_F32 && f.emb_dtype != SMG_EMB_BF16))
+    if (f.w <= 0 || f.h <= 0 || f.w > b->max_w || f.h > b->max_h || (!f.depth && !f.depth_mm) || f.n_det < 0 || f.n_det > B.max_det ||
+        (f.n_det > 0 && (!f.box || !f.cls || (!f.mask_bits && (!f.label || !f.det_label)))) ||
+        (f.emb && f.emb_dtype != SMG_EMB_F32 && f.emb_dtype != SMG_EMB_BF16))
       return fail(SMG_ERR_ARGS, "smg_push_frames: bad frame");
+    if (f.mask_bits && (f.mask_w <= 0 || f.mask_h <= 0 || f.mask_w > b->max_w || f.mask_h > b->max_h || !(f.mask_sx > 0) ||
+                        !(f.mask_sy > 0) || f.img_w < 0 || f.img_h < 0))
+      return fail(SMG_ERR_ARGS, "smg_push_frames: bad detection mask grid (mask_w x mask_h <= max_w x max_h, scales > 0)");
   }
   // pinned descriptor ring: wait until the copy that last read this slot has run
   b->dbg_last = 0;
@@ -683,6 +705,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   // Host frames in pinned (device-accessible) memory are read in place: k_gather fetches only
   // the pixels the chain reads.  Any other host memory goes through whole-frame copies.
   bool gather = where == SMG_MEM_HOST && b->host_gather && b->max_w <= GATHER_WMAX;
+  for (int i = 0; i < n && gather; ++i) gather = frames[i].depth != nullptr;   // millimetre depth travels whole
   auto dev_ptr = [](const void* p, size_t bytes) -> const void* {
     cudaPointerAttributes a0, a1;
     if (cudaPointerGetAttributes(&a0, p) != cudaSuccess || cudaPointerGetAttributes(&a1, (const char*)p + bytes - 1) != cudaSuccess) {
@@ -732,12 +755,31 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
       d.score[k] = f.score ? f.score[k] : 1.f;
     }
     d.emb_dtype = f.emb_dtype;
+    // detector image and masks (sm_detections); the label-image form has the depth grid as its
+    // mask grid.  Scales as the reference computes them (objmap.cpp:635-636 float, :1377 double).
+    d.img_w = f.img_w > 0 ? f.img_w : f.w;
+    d.img_h = f.img_h > 0 ? f.img_h : f.h;
+    d.sxu_f = float(f.w) / d.img_w;
+    d.syv_f = float(f.h) / d.img_h;
+    d.sxu_d = double(f.w) / d.img_w;
+    d.syv_d = double(f.h) / d.img_h;
+    if (f.mask_bits && f.n_det > 0) {
+      d.mask_w = f.mask_w; d.mask_h = f.mask_h;
+      d.mask_sx = f.mask_sx; d.mask_sy = f.mask_sy; d.mask_ox = f.mask_ox; d.mask_oy = f.mask_oy;
+    } else {
+      d.mask_w = f.w; d.mask_h = f.h;
+      d.mask_sx = d.mask_sy = 1.f; d.mask_ox = d.mask_oy = 0.f;
+    }
+    d.mask_words = (int32_t)(((size_t)d.mask_w * d.mask_h + 31) / 32);
     if (where == SMG_MEM_DEVICE) {
-      d.depth = f.depth;
+      d.depth = f.depth ? f.depth : b->d_depth + (size_t)m * WH;   // millimetres: converted into staging
+      d.depth_mm = f.depth ? nullptr : f.depth_mm;
       d.label = f.label;
       d.emb = f.emb;
+      d.mask_bits = f.n_det > 0 ? f.mask_bits : nullptr;
     } else {
       d.depth = b->d_depth + (size_t)m * WH;
+      d.depth_mm = f.depth ? nullptr : b->d_depth_mm + (size_t)m * WH;
       d.label = b->d_label + (size_t)m * WH;
       if (gather) {
         d.depth_host = (const float*)dh[2 * m];
@@ -745,6 +787,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
       }
       d.emb = f.emb && f.n_det > 0 ? (const void*)(b->d_emb + emb_off) : nullptr;
       if (d.emb) emb_off += (size_t)f.n_det * B.D * (f.emb_dtype == SMG_EMB_BF16 ? 2 : 4);
+      d.mask_bits = f.mask_bits && f.n_det > 0 ? b->d_mask + (size_t)m * B.max_det * b->mask_words_max : nullptr;
     }
     // host-libm scalars (objmap.cpp:520-531, bestview.cpp:77-81, grid.cpp:202)
     const double* T = f.T_mc;
@@ -829,10 +872,36 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
                (const char*)frames[j].label == (const char*)frames[i].label + (j - i) * WH * 2 && frames[i].label)
           ++j;
         const size_t run = j - i > 1 ? (size_t)(j - i) * WH : pi;
-        CK(cudaMemcpyAsync(b->d_depth + i * WH, frames[i].depth, run * 4, cudaMemcpyHostToDevice, b->s_copy));
-        if (frames[i].label) CK(cudaMemcpyAsync(b->d_label + i * WH, frames[i].label, run * 2, cudaMemcpyHostToDevice, b->s_copy));
-        b->h2d_host += (long long)run * (frames[i].label ? 6 : 4);
+        if (frames[i].depth) {
+          CK(cudaMemcpyAsync(b->d_depth + i * WH, frames[i].depth, run * 4, cudaMemcpyHostToDevice, b->s_copy));
+          b->h2d_host += (long long)run * 4;
+        } else {   // millimetres: staged, converted below
+          CK(cudaMemcpyAsync(b->d_depth_mm + i * WH, frames[i].depth_mm, pi * 2, cudaMemcpyHostToDevice, b->s_copy));
+          b->h2d_host += (long long)pi * 2;
+          j = i + 1;
+        }
+        if (frames[i].label && !frames[i].mask_bits) {
+          CK(cudaMemcpyAsync(b->d_label + i * WH, frames[i].label, run * 2, cudaMemcpyHostToDevice, b->s_copy));
+          b->h2d_host += (long long)run * 2;
+        }
         i = j;
+      }
+      for (int i = m0; i < m1; ++i)   // detector bit masks: whole planes
+        if (frames[i].mask_bits && frames[i].n_det > 0) {
+          const size_t bytes = (size_t)frames[i].n_det * b->h_frames[i].mask_words * 4;
+          CK(cudaMemcpyAsync(b->d_mask + (size_t)i * B.max_det * b->mask_words_max, frames[i].mask_bits, bytes,
+                             cudaMemcpyHostToDevice, b->s_copy));
+          b->h2d_host += (long long)bytes;
+        }
+      {   // millimetre depth -> metres (mm * 1e-3f, as every reference reader computes it)
+        bool any = false;
+        for (int i = m0; i < m1; ++i) any = any || !frames[i].depth;
+        if (any) {
+          Batch Bg = B;
+          Bg.map0 = m0;
+          k_depth_mm<<<dim3(64, m1 - m0), 256, 0, b->s_copy>>>(Bg);
+          b->launches += 1;
+        }
       }
       // embeddings: packed on the device; one copy per run that is packed on the host too
       for (int i = m0; i < m1;) {
@@ -869,6 +938,15 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
         b->launches += 1;
       }
       CK(cudaEventRecord(b->ev_copied[g], b->s_copy));
+    }
+  }
+  if (where == SMG_MEM_DEVICE) {   // millimetre depth -> metres in the staging images
+    bool any = false;
+    for (int i = 0; i < n; ++i) any = any || !frames[i].depth;
+    if (any) {
+      k_depth_mm<<<dim3(64, n), 256, 0, st>>>(B);
+      b->launches += 1;
+      CK(cudaEventRecord(b->ev_up, st));
     }
   }
   for (int g = 0; g < G; ++g) {

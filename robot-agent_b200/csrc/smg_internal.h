@@ -79,6 +79,16 @@ typedef struct {
   int32_t hand_act[2];
   double hand_gap[2];
   int32_t hands_on;      // run the hand step (some map of the batch has used a gripper)
+  // detector masks (sm_detections): bit masks on their own grid (mask_bits != null) or the label
+  // image; the detector image size and its scale to the depth grid, as the reference computes
+  // them (float in ObjectMap::update, objmap.cpp:635-636; double in buildReencode, :1377)
+  const uint16_t* depth_mm;    // millimetre source converted into depth before the chain, or null
+  const uint32_t* mask_bits;   // n_det x mask_words
+  int32_t mask_w, mask_h, mask_words;
+  float mask_sx, mask_sy, mask_ox, mask_oy;
+  int32_t img_w, img_h;
+  float sxu_f, syv_f;
+  double sxu_d, syv_d;
 } FrameDev;
 
 // Observation (one detection after back-projection; scenemap objmap.cpp:52-74 `Obs`)

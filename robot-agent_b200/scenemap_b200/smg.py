@@ -27,7 +27,10 @@ class SmgFrame(C.Structure):
                 ("fx", C.c_float), ("fy", C.c_float), ("cx", C.c_float), ("cy", C.c_float), ("T_mc", C.c_double * 12),
                 ("T_bc", C.c_float * 12), ("base", C.c_double * 3), ("eef", C.c_double * 6), ("eef_base", C.c_float * 6),
                 ("n_det", C.c_int32), ("det_label", C.c_void_p), ("box", C.c_void_p), ("cls", C.c_void_p),
-                ("score", C.c_void_p), ("emb", C.c_void_p), ("emb_dtype", C.c_int32), ("grip", C.c_float * 2)]
+                ("score", C.c_void_p), ("emb", C.c_void_p), ("emb_dtype", C.c_int32), ("grip", C.c_float * 2),
+                ("mask_bits", C.c_void_p), ("mask_w", C.c_int32), ("mask_h", C.c_int32), ("mask_sx", C.c_float),
+                ("mask_sy", C.c_float), ("mask_ox", C.c_float), ("mask_oy", C.c_float), ("img_w", C.c_int32),
+                ("img_h", C.c_int32), ("depth_mm", C.c_void_p)]
 
 
 class SmgReencReq(C.Structure):
@@ -182,10 +185,23 @@ class Batch:
         f.emb_dtype = emb_dtype
         grip = np.asarray(fr.get("grip", (1.0, 1.0)), np.float32).reshape(-1)
         f.grip[0], f.grip[1] = float(grip[0]), float(grip[1])
+        f.img_w, f.img_h = fr.get("img_w", 0), fr.get("img_h", 0)
+        if fr.get("mask_w"):
+            f.mask_w, f.mask_h = fr["mask_w"], fr["mask_h"]
+            f.mask_sx, f.mask_sy, f.mask_ox, f.mask_oy = fr["mask_affine"]
         if ptrs is not None:
             f.depth, f.label, f.emb = ptrs["depth"], ptrs["label"], ptrs["emb"]
+            f.mask_bits = ptrs.get("mask_bits")
         else:
-            depth = np.ascontiguousarray(fr["depth"], np.float32)
+            if fr.get("mask_bits") is not None:
+                mb = np.ascontiguousarray(fr["mask_bits"], np.uint32)
+                keep.append(mb)
+                f.mask_bits = _ptr(mb)
+            if fr.get("depth_mm") is not None:
+                dmm = np.ascontiguousarray(fr["depth_mm"], np.uint16)
+                keep.append(dmm)
+                f.depth_mm = _ptr(dmm)
+            depth = np.ascontiguousarray(fr["depth"], np.float32) if fr.get("depth_mm") is None else None
             label = np.ascontiguousarray(fr["label"], np.uint16)
             if emb_dtype == SMG_EMB_BF16:
                 e32 = np.ascontiguousarray(fr["emb"], np.float32)

@@ -67,6 +67,22 @@ def _p(a, t):
     return a.ctypes.data_as(C.POINTER(t))
 
 
+def label_masks(label: np.ndarray, det_label, s: int) -> np.ndarray:
+    """Detector bit masks on an s-pixel grid (the sm_detections form): cell (i, j) covers pixels
+    [s i, s i + s) x [s j, s j + s) and is set when the label at its centre pixel (s i + s/2,
+    s j + s/2) is the detection's; (w // s) x (h // s) cells, LSB-first row-major words."""
+    h, w = label.shape
+    MW, MH = w // s, h // s
+    samp = label[s // 2::s, s // 2::s][:MH, :MW]
+    words = (MW * MH + 31) // 32
+    out = np.zeros((max(len(det_label), 1), words), np.uint32)
+    for k, l in enumerate(det_label):
+        flat = np.zeros(words * 32, bool)
+        flat[:MW * MH] = (samp == l).reshape(-1)
+        out[k] = np.packbits(flat, bitorder="little").view("<u4")
+    return out[:len(det_label)]
+
+
 def map_seed(base: int, index: int) -> int:
     """Per-map seed: splitmix64 of base xor map index."""
     z = (base ^ index) & 0xFFFFFFFFFFFFFFFF
@@ -86,7 +102,10 @@ class BoxRoom:
       box_extra     [(lo, hi), ...]: boxes added after the seeded ones (their placement is the
                     caller's, e.g. small graspable boxes or boxes that only enter through a move);
       hands         callable f -> (eef (2, 3) map frame, grip (2,)): the robot hand's point and
-                    gripper value per frame (default: far away, open).
+                    gripper value per frame (default: far away, open);
+      mask_grid     s > 0: detections also carry bit masks on an s-pixel grid (label_masks), the
+                    form the reference's detector produces; both sides then read those;
+      depth_mm      depth also as uint16 millimetres (rounded), which both sides then read.
     """
 
     def __init__(self, seed: int, n_boxes: int = 20, room=(6.0, 5.0, 2.6), noise_k: float = 0.005,
@@ -94,7 +113,8 @@ class BoxRoom:
                  fy: float = 525.0, cx: float = 319.5, cy: float = 239.5, dt: float = 0.1, speed: float = 0.3,
                  n_frames: int = 300, D: int = 1152, bf16: bool = False, emb_sigma: float = 0.05,
                  min_px: int = 64, max_det: int = 24, cam_height: float = 0.9, pitch_deg: float = 20.0,
-                 shell_labels: bool = False, box_moves=(), box_extra=(), hands=None):
+                 shell_labels: bool = False, box_moves=(), box_extra=(), hands=None, mask_grid: int = 0,
+                 depth_mm: bool = False):
         L = lib()
         self.seed = seed
         self.scene = SyScene()
@@ -108,6 +128,7 @@ class BoxRoom:
                 self.scene.box[b].hi[k] = hi[k]
             self.scene.n_boxes = b + 1
         self.scene.shell_labels = 1 if shell_labels else 0
+        self.mask_grid, self.depth_mm = mask_grid, depth_mm
         self.box_moves = sorted(box_moves, key=lambda e: e[0])
         self.hands = hands
         self.cam = SyCamera(w, h, fx, fy, cx, cy)
@@ -162,7 +183,15 @@ class BoxRoom:
             L.sy_embed(C.byref(S), key, n, _p(det_label, C.c_uint16), self.D, self.emb_sigma,
                        1 if self.bf16 else 0, _p(emb, C.c_float))
         eef, grip = (self.eef, np.ones(2, np.float32)) if self.hands is None else self.hands(f)
+        extra = {}
+        if self.mask_grid > 0:
+            s = self.mask_grid
+            extra.update(mask_bits=label_masks(label, det_label[:n], s), mask_w=self.w // s, mask_h=self.h // s,
+                         mask_affine=(float(s), float(s), 0.0, 0.0), img_w=self.w, img_h=self.h)
+        if self.depth_mm:
+            extra["depth_mm"] = np.clip(np.rint(depth * 1000.0), 0, 65535).astype(np.uint16)
         return dict(stamp=f * self.dt, w=self.w, h=self.h, depth=depth, label=label, fx=self.fx, fy=self.fy,
                     cx=self.cx, cy=self.cy, T_mc=T, T_bc=self.T_bc, base=self.poses[f].copy(),
-                    eef=np.asarray(eef, np.float64), grip=np.asarray(grip, np.float32), eef_base=self.eef_base, n_det=n, det_label=det_label[:n].copy(), box=box[:n].copy(),
-                    cls=cls[:n].copy(), score=score[:n].copy(), emb=emb[:n].copy(), emb_dim=self.D)
+                    eef=np.asarray(eef, np.float64), grip=np.asarray(grip, np.float32), eef_base=self.eef_base,
+                    n_det=n, det_label=det_label[:n].copy(), box=box[:n].copy(), cls=cls[:n].copy(),
+                    score=score[:n].copy(), emb=emb[:n].copy(), emb_dim=self.D, **extra)

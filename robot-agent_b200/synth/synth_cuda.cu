@@ -87,7 +87,39 @@ __global__ void sy_embed_kernel(const sy_scene* __restrict__ scenes, const int* 
   }
 }
 
+// Detector bit masks on an s-pixel grid (synth.py label_masks): cell (i, j) of detection k of
+// image img is set when the label at pixel (s i + s/2, s j + s/2) is that detection's label.
+// One thread per output word (32 cells, LSB first).
+__global__ void sy_masks_kernel(const uint16_t* __restrict__ label, int w, int h, int s, const uint16_t* __restrict__ det_label,
+                                const int* __restrict__ n_det, int max_det, uint32_t* __restrict__ out) {
+  const int img = blockIdx.z, k = blockIdx.y;
+  const int MW = w / s, MH = h / s, words = (MW * MH + 31) / 32;
+  const int wd = blockIdx.x * blockDim.x + threadIdx.x;
+  if (wd >= words || k >= max_det) return;
+  uint32_t v = 0;
+  if (k < n_det[img]) {
+    const uint16_t L = det_label[(size_t)img * max_det + k];
+    const uint16_t* lab = label + (size_t)img * w * h;
+    for (int b = 0; b < 32; ++b) {
+      const int q = wd * 32 + b;
+      if (q >= MW * MH) break;
+      const int i = q % MW, j = q / MW;
+      if (lab[(size_t)(s * j + s / 2) * w + (s * i + s / 2)] == L) v |= 1u << b;
+    }
+  }
+  out[((size_t)img * max_det + k) * words + wd] = v;
+}
+
 extern "C" {
+
+int sy_masks_device(const uint16_t* label_dev, int w, int h, int s, const uint16_t* det_label_dev, const int* n_det_dev, int max_det,
+                    int n_img, uint32_t* out_dev, void* stream) {
+  if (s <= 0 || w / s <= 0 || h / s <= 0 || max_det <= 0 || n_img <= 0) return -1;
+  const int words = ((w / s) * (h / s) + 31) / 32;
+  sy_masks_kernel<<<dim3((words + 255) / 256, max_det, n_img), 256, 0, (cudaStream_t)stream>>>(label_dev, w, h, s, det_label_dev, n_det_dev,
+                                                                                              max_det, out_dev);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
 
 int sy_render_batch_device(const sy_scene* scenes_dev, const sy_camera* C, const double* T_dev, const uint64_t* keys_dev, int M,
                            int n_img, float* depth_dev, uint16_t* label_dev, void* stream) {

@@ -48,6 +48,15 @@ def test_device_renderer_matches_host_generator():
                 for k in ("det_label", "box", "cls", "score"):
                     assert np.array_equal(np.asarray(d[k]), np.asarray(ref_fr[k])), (k, m, f0 + fi)
                 assert np.array_equal(d["emb"].view(np.uint32), ref_fr["emb"].view(np.uint32)), (m, f0 + fi)
+    # detector bit masks on a 4-pixel grid, built on the device from the rendered labels
+    wl4 = RoomBatch(M, 1000, 40, D=1152, bf16=True, max_det=24, mask_grid=4)
+    R = wl4.render(5, 2)
+    for fi in range(2):
+        hf = wl4.host_frames(R, fi)
+        for m in range(M):
+            ref_fr = wl4.rooms[m].frame(5 + fi)
+            want = synth.label_masks(ref_fr["label"], ref_fr["det_label"], 4)
+            assert np.array_equal(hf[m]["mask_bits"], want), (m, 5 + fi)
 
 
 def test_parity_bench_configuration():

@@ -26,6 +26,7 @@ def _need():
 def _run_variant(v: dict, bf16: bool = False, deep_every: int = 10, D: int = 1152):
     from oracle import ref
     from scenemap_b200 import smg
+    bf16 = bf16 or v.get("bf16", False)
     g = variants.make_gen(v, D=D, bf16=bf16)
     R = ref.RefMap(v["kv"])
     B = smg.Batch(1, max_objects=256, emb_dim=D, max_det=32, params=smg.Params(v["kv"]))
@@ -70,3 +71,40 @@ def test_parity_hands():
     grasp, hold, release, support link and the supported object following (updateHands)."""
     _need()
     _run_variant(variants.hands(), deep_every=5)
+
+
+def test_parity_coarse_detector_masks():
+    """Bit masks on a 4-pixel grid (sm_detections with mask_sx = mask_sy = 4)."""
+    _need()
+    _run_variant(variants.coarse_masks(), deep_every=8)
+
+
+def test_parity_depth_millimetres():
+    """uint16 millimetre depth (ObjFrame::depth_mm), read as mm * 1e-3f everywhere."""
+    _need()
+    _run_variant(variants.depth_millimetres(), deep_every=8)
+
+
+def test_bit_masks_on_the_image_grid_equal_the_label_image():
+    """The two input forms of the same detections (label image, or bit masks with scale 1)
+    give the same results, field for field."""
+    _need()
+    from scenemap_b200 import smg, synth
+    import numpy as np
+    D = 1152
+    g = synth.BoxRoom(seed=synth.map_seed(71, 0), n_frames=20, D=D, bf16=True)
+    A = smg.Batch(1, max_objects=128, emb_dim=D, max_det=32)
+    Bm = smg.Batch(1, max_objects=128, emb_dim=D, max_det=32)
+    for f in range(20):
+        fr = g.frame(f)
+        frb = dict(fr, mask_bits=synth.label_masks(fr["label"], fr["det_label"], 1), mask_w=fr["w"], mask_h=fr["h"],
+                   mask_affine=(1.0, 1.0, 0.0, 0.0))
+        A.push([fr], smg.SMG_MEM_HOST, smg.SMG_EMB_BF16)
+        Bm.push([frb], smg.SMG_MEM_HOST, smg.SMG_EMB_BF16)
+        assert A.objects(0) == Bm.objects(0), f"frame {f}"
+        ra, rb = A.reencode(0), Bm.reencode(0)
+        for k in ("id", "box", "kappa", "bits"):
+            assert np.array_equal(ra[k], rb[k]), (f, k)
+        assert np.array_equal(A.assoc(0)["obj_id"], Bm.assoc(0)["obj_id"])
+    A.close()
+    Bm.close()

@@ -30,3 +30,20 @@ def test_variant_fires_its_rules_on_the_reference(name):
     seen = {e[2] for e in R.events()}   # the reference keeps every event of the run
     for k in v["events"]:
         assert k in seen, f"{name}: no event of kind {k} on the reference (seen {sorted(seen)})"
+
+
+def test_bit_masks_on_the_image_grid_equal_the_label_image_on_the_reference():
+    """The reference gets the same result from the label image (turned into bit masks on the
+    image grid by the oracle driver) and from bit masks with scale 1 given directly."""
+    _need()
+    from oracle import ref
+    from scenemap_b200 import synth
+    g = synth.BoxRoom(seed=synth.map_seed(71, 0), n_frames=12, bf16=True)
+    A, Bm = ref.RefMap(), ref.RefMap()
+    for f in range(12):
+        fr = g.frame(f)
+        A.frame(fr)
+        Bm.frame(dict(fr, mask_bits=synth.label_masks(fr["label"], fr["det_label"], 1), mask_w=fr["w"], mask_h=fr["h"],
+                      mask_affine=(1.0, 1.0, 0.0, 0.0)))
+        assert A.objects() == Bm.objects()
+        assert A.stats() == Bm.stats()

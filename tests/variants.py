@@ -37,6 +37,18 @@ def engine_params(n_frames: int = 40) -> dict:
     return dict(gen=dict(seed_base=31), kv=YOLO26N_OBJ_PARAMS, n_frames=n_frames, stats=(), events=())
 
 
+def coarse_masks(n_frames: int = 40) -> dict:
+    """Detections as bit masks on a 4-pixel grid (the form the reference's detector emits, and
+    the grid of its own object-memory test), bf16 embeddings: the mask-cell arithmetic of the
+    back-projection and of the re-encode requests on a grid coarser than the image."""
+    return dict(gen=dict(seed_base=51, mask_grid=4), kv="", n_frames=n_frames, stats=(), events=(), bf16=True)
+
+
+def depth_millimetres(n_frames: int = 30) -> dict:
+    """Depth as uint16 millimetres (ObjFrame::depth_mm) instead of float metres."""
+    return dict(gen=dict(seed_base=61, depth_mm=True), kv="", n_frames=n_frames, stats=(), events=(), bf16=True)
+
+
 def make_gen(v: dict, D: int = 1152, bf16: bool = False):
     from scenemap_b200 import synth
     kw = dict(v["gen"])
