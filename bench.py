@@ -112,6 +112,16 @@ def parse():
                     help="objprob = config 1 (headline); occ = config 3 (grid insert + correlative scan matching); "
                          "assoc = config 2 (association GEMM)")
     ap.add_argument("--scans", type=int, default=5000, help="config 3: scans per map")
+    ap.add_argument("--mask-grid", type=int, default=0, metavar="S",
+                    help="detections as the detector's bit masks on an S-pixel grid (sm_detections form) instead of "
+                         "the label image; both arms read the same masks")
+    ap.add_argument("--no-reencode-pass", action="store_true",
+                    help="skip the extra timed pass (and CPU baseline) without the re-encode stage")
+    ap.add_argument("--max-clouds", type=int, default=None,
+                    help="cloud slots per map (smg_create_pooled; default = --max-objects)")
+    ap.add_argument("--width", type=int, default=640, help="depth image width (config 4: 848)")
+    ap.add_argument("--dets", type=int, default=24, help="detections per frame at most (config 4: 32)")
+    ap.add_argument("--boxes", type=int, default=20, help="boxes per room")
     ap.add_argument("--check-run", type=int, default=0, metavar="FRAMES",
                     help="checked run instead of the benchmark: push --maps maps (device-resident config-1 frames, "
                          "--max-objects slots) for FRAMES keyframes; after every 16 frames print the device error word "
@@ -163,7 +173,8 @@ class Clocks:
 
 
 # ------------------------------------------------------------------ CPU baseline (reference scenemap code)
-def cpu_reference(M_sample: int, lead: int, timed: int, threads: int, base_seed: int = 1000, obj_kv: str = ""):
+def cpu_reference(M_sample: int, lead: int, timed: int, threads: int, base_seed: int = 1000, obj_kv: str = "",
+                  mask_grid: int = 0, reencode: bool = True):
     """The reference scenemap (oracle/_ref, compiled from the reference sources) on the host cores:
     one map per thread.  Every map runs `lead` untimed keyframes, then `timed` timed ones: the
     same frames (same seeds, same frame indices) the device arm pre-rolls and times.  Inputs come
@@ -184,11 +195,13 @@ def cpu_reference(M_sample: int, lead: int, timed: int, threads: int, base_seed:
         pass
     if gen_dev:
         from scenemap_b200.workload import RoomBatch
-        wl = RoomBatch(M_sample, base_seed, frames, D=D_EMB, bf16=True, max_det=24)
+        wl = RoomBatch(M_sample, base_seed, frames, D=D_EMB, bf16=True, max_det=24, mask_grid=mask_grid)
     else:
-        gens = [synth.BoxRoom(seed=synth.map_seed(base_seed, m), n_frames=frames, bf16=True, max_det=24)
+        gens = [synth.BoxRoom(seed=synth.map_seed(base_seed, m), n_frames=frames, bf16=True, max_det=24, mask_grid=mask_grid)
                 for m in range(M_sample)]
     maps = [ref.RefMap(obj_kv) for _ in range(M_sample)]
+    for R in maps:
+        R.set_reencode(reencode)
     span = 0.0
     for f0 in range(0, frames, 10):
         nf = min(10, frames - f0)
@@ -215,7 +228,8 @@ def cpu_reference(M_sample: int, lead: int, timed: int, threads: int, base_seed:
     value = M_sample * timed / span
     return dict(value=value, unit=UNIT, cores=M_sample, kind="reference", frames_timed=f"{lead}..{frames - 1}",
                 sample=f"{M_sample} maps, keyframes {lead}..{frames - 1} timed after {lead} untimed, one map per host "
-                       f"thread, reference scenemap C++ (-O2) from oracle/_ref")
+                       f"thread, reference scenemap C++ (-O2) from oracle/_ref"
+                       + ("" if reencode else ", buildReencode not run"))
 
 
 # ------------------------------------------------------------------ B200 arm
@@ -228,10 +242,13 @@ def run_b200(args, rank, world, local_rank):
     M = args.maps
     n_total = args.preroll + args.warmup + args.steps + args.kt_steps + args.e2e_steps
     from scenemap_b200 import dist
-    wl = RoomBatch(M, 1000, n_total, D=1152, bf16=True, max_det=24, map_offset=dist.rank_maps(rank, world, M)[0],
-                   device=str(dev))
-    B = smg.Batch(M, max_objects=args.max_objects, emb_dim=1152, max_w=640, max_h=480, max_det=24,
-                  grid=(512, 512, -256 + 60, -256 + 50), dev=local_rank)
+    n_total += 0 if args.no_reencode_pass else args.steps
+    W, H = args.width, 480
+    wl = RoomBatch(M, 1000, n_total, D=1152, bf16=True, w=W, h=H, max_det=args.dets,
+                   map_offset=dist.rank_maps(rank, world, M)[0], device=str(dev), mask_grid=args.mask_grid,
+                   n_boxes=args.boxes)
+    B = smg.Batch(M, max_objects=args.max_objects, emb_dim=1152, max_w=W, max_h=H, max_det=args.dets,
+                  grid=(512, 512, -256 + 60, -256 + 50), dev=local_rank, **pool_kw(args))
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     f = 0
@@ -272,6 +289,26 @@ def run_b200(args, rank, world, local_rank):
     err = B.error_word()
     f += args.steps
     del R, structs
+    # the same chain without the re-encode stage, on the next K keyframes (its CPU baseline times
+    # the same keyframes): the reference's stage fills a whole mask grid per candidate object
+    t_nr, f_nr = None, f
+    if not args.no_reencode_pass:
+        R = wl.render(f, args.steps, sp)
+        keep = []
+        structs = [wl.structs(R, fi, keep) for fi in range(args.steps)]
+        B.set_reencode(False)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for fi in range(args.steps):
+            B.push(None, smg.SMG_MEM_DEVICE, structs=structs[fi], stream=sp)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t_nr = e0.elapsed_time(e1) / 1e3
+        B.set_reencode(True)
+        f += args.steps
+        del R, structs
     # per-kernel breakdown: a separate pass with event timing around every launch (the chain
     # then runs as one stream group, so each kernel's time is its own)
     R = wl.render(f, args.kt_steps, sp)
@@ -288,14 +325,19 @@ def run_b200(args, rank, world, local_rank):
     f += args.kt_steps
     del R, structs
     # e2e: host (pinned) inputs through the C ABI, association read back every step
-    E = args.e2e_steps
+    # (pinned host frames of at most ~8 GB: fewer e2e steps for very large batches)
+    E = max(2, min(args.e2e_steps, int(8e9 // (M * W * H * 6))))
     R = wl.render(f, E, sp)
-    depth_h = torch.empty((E, M, 480, 640), dtype=torch.float32, pin_memory=True)
-    label_h = torch.empty((E, M, 480, 640), dtype=torch.int16, pin_memory=True)
+    depth_h = torch.empty((E, M, H, W), dtype=torch.float32, pin_memory=True)
+    label_h = torch.empty((E, M, H, W), dtype=torch.int16, pin_memory=True)
     emb_h = torch.empty(R["emb"].shape, dtype=torch.int16, pin_memory=True)
     depth_h.copy_(R["depth"])
     label_h.copy_(R["label"].view(torch.int16))
     emb_h.copy_(R["emb"].view(torch.int16))
+    masks_h = None
+    if R["masks"] is not None:
+        masks_h = torch.empty(R["masks"].shape, dtype=torch.int32, pin_memory=True)
+        masks_h.copy_(R["masks"])
     torch.cuda.synchronize()
     e_structs, keep2 = [], []
     h2d = 0
@@ -306,11 +348,13 @@ def run_b200(args, rank, world, local_rank):
             d = R["dets"][fi * M + m]
             ptrs = dict(depth=depth_h[fi, m].data_ptr(), label=label_h[fi, m].data_ptr(),
                         emb=emb_h.data_ptr() + d["emb_off"] * 1152 * 2 if d["n"] else None)
+            if masks_h is not None:
+                ptrs["mask_bits"] = masks_h[fi * M + m].data_ptr()
             arr[m] = smg.Batch.frame_struct(fd, keep2, smg.SMG_EMB_BF16, ptrs=ptrs)
-            h2d += 640 * 480 * 6 + d["n"] * 1152 * 2
+            h2d += W * H * 6 + d["n"] * 1152 * 2
         e_structs.append(arr)
     h2d //= E
-    d2h = M * 24 * 16
+    d2h = M * args.dets * 16
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -335,11 +379,19 @@ def run_b200(args, rank, world, local_rank):
         stats[m] = list(s.values())
     from scenemap_b200 import dist
     all_stats = dist.gather_stats(stats, world, dev)          # NCCL all_gather when world > 1
-    t, t_e2e = dist.max_over_ranks([t, t_e2e], world, dev)   # device times: max over ranks
+    if t_nr is not None:
+        t, t_e2e, t_nr = dist.max_over_ranks([t, t_e2e, t_nr], world, dev)   # device times: max over ranks
+    else:
+        t, t_e2e = dist.max_over_ranks([t, t_e2e], world, dev)
     n_obj = [len(B.objects(m)) for m in range(min(M, 4))]
     B.close()
-    return dict(t=t, t_e2e=t_e2e, kt=kt, launches=launches, err=err, clocks=clocks, work=work,
+    return dict(t=t, t_e2e=t_e2e, E=E, t_nr=t_nr, f_nr=f_nr, kt=kt, launches=launches, err=err, clocks=clocks, work=work,
                 stats=all_stats, h2d=h2d, h2d_input=h2d_input, d2h=d2h, n_obj=n_obj)
+
+
+def pool_kw(args) -> dict:
+    """smg_create_pooled's cloud pool size when --max-clouds is given."""
+    return {"max_clouds": args.max_clouds} if args.max_clouds else {}
 
 
 def check_run(args, local_rank):
@@ -518,11 +570,17 @@ def main():
     if args.check_run:
         check_run(args, local_rank)
         return
-    cfg = {"workload": "config 1: 64 box-room maps per GPU, 640x480 fp32 depth + u16 labels, 8-24 dets, "
-                       f"1152-d bf16 embeddings, <={args.max_objects} object slots, 512x512 grid",
+    masks = ("u16 label image (mask grid = image grid)" if args.mask_grid <= 0 else
+             f"detector bit masks on a {args.mask_grid}-pixel grid (sm_detections form)")
+    big = args.maps > 64 or args.width != 640
+    cfg = {"workload": f"config {4 if big else 1}: {args.maps} box-room maps per GPU ({args.boxes} boxes), {args.width}x480 fp32 "
+                       f"depth + {masks}, <= {args.dets} dets, 1152-d bf16 embeddings, <={args.max_objects} object slots"
+                       + (f" ({args.max_clouds} cloud slots)" if args.max_clouds else "") + ", 512x512 grid",
+           "detections": masks,
            "keyframe": "Mapper2D::keyframe + ObjectMap::update + addPoints + buildReencode (capi.cpp:811-1010)",
            "maps_per_gpu": args.maps, "frames_timed": f"{args.preroll + args.warmup}..{args.preroll + args.warmup + args.steps - 1}",
-           "l2": "fresh frames every step (118 MB/step at 64 maps), no flush", "parallelism": f"dp{world} (maps)"}
+           "l2": f"fresh frames every step ({args.maps * args.width * 480 * 6 / 1e6:.0f} MB/step of depth + labels), no flush",
+           "parallelism": f"dp{world} (maps)"}
     if args.impl == "reference":
         if rank != 0:
             return
@@ -530,14 +588,19 @@ def main():
         # the same keyframes the device arm times: frames preroll+W .. preroll+W+K-1 of the same
         # maps, after the same untimed pre-roll and warm-up frames
         lead = args.preroll + args.warmup
-        cb = cpu_reference(min(cores, 64), lead, args.steps, min(cores, 64))
+        cb = cpu_reference(min(cores, 64), lead, args.steps, min(cores, 64), mask_grid=args.mask_grid)
         if cb is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libscenemap_ref.so not built"}))
             return
+        extra = {}
+        if not args.no_reencode_pass:   # the keyframes the device arm times without the stage
+            cb_nr = cpu_reference(min(cores, 64), lead + args.steps, args.steps, min(cores, 64), mask_grid=args.mask_grid,
+                                  reencode=False)
+            extra = {"value_without_reencode": cb_nr["value"], "frames_timed_without_reencode": cb_nr["frames_timed"]}
         print(json.dumps({"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
                           "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
                           "vs_baseline": None, "dtype": "f64/f32", "data": "synthetic", "config": cfg, "impl": "reference",
-                          "frames_timed": cb["frames_timed"],
+                          "frames_timed": cb["frames_timed"], **extra,
                           "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                           "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
@@ -600,13 +663,16 @@ def main():
         return
     K, M = args.steps, args.maps
     value = M * world * K / r["t"]
-    e2e = M * world * args.e2e_steps / r["t_e2e"]
+    e2e = M * world * r["E"] / r["t_e2e"]
     # roofline: algorithmic bytes from the device work counters (one launch per kernel per step)
     roof, roof_step, roof_all = rooflines(r["kt"], r["work"], r["t"] / K, D_EMB)
-    cb = None
+    cb = cb_nr = None
     if not args.no_cpu_baseline and world == 1:
         cores = os.cpu_count() or 1
-        cb = cpu_reference(min(cores, 64), args.preroll + args.warmup, args.cpu_timed, min(cores, 64))
+        cb = cpu_reference(min(cores, 64), args.preroll + args.warmup, args.cpu_timed, min(cores, 64), mask_grid=args.mask_grid)
+        if r["t_nr"] is not None:
+            cb_nr = cpu_reference(min(cores, 64), r["f_nr"], args.cpu_timed, min(cores, 64), mask_grid=args.mask_grid,
+                                  reencode=False)
     out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
            "ms_per_step": 1e3 * r["t"] / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "f64/f32 (bf16 embeddings)", "data": "synthetic", "config": cfg,
@@ -620,8 +686,16 @@ def main():
                                                      "n_assoc", "n_new", "n_merge", "n_obj_struct", "n_reenc_req",
                                                      "n_reenc_done", "n_blocked", "n_wall_tall", "n_so_big", "n_bridge"],
                                                     r["stats"].sum(0))}}
+    if r["t_nr"] is not None:
+        out["value_without_reencode"] = M * world * K / r["t_nr"]
+        out["frames_timed_without_reencode"] = f"{r['f_nr']}..{r['f_nr'] + K - 1}"
     if cb is not None:
         out["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        ratios = {"with_reencode": value / cb["value"]}
+        if cb_nr is not None:
+            out["cpu_baseline_without_reencode"] = {k: cb_nr[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            ratios["without_reencode"] = out["value_without_reencode"] / cb_nr["value"]
+        out["vs_cpu_baseline"] = ratios
     print(json.dumps(out))
 
 

@@ -169,6 +169,15 @@ int smg_params_set_cloud(smg_params* p, double voxel, int cap);
  * Replaces `new ObjectMap(p)` + `Mapper2D(p)` (scenemap objmap.hpp:235, mapper2d.hpp:39). */
 int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, int max_w, int max_h, int max_det, int grid_w,
                int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out);
+/* smg_create with the object clouds in a pool of max_clouds slots per map (<= max_objects).  An
+ * object slot holds the object's scalars and vectors (about 28 KB at D = 1152); a cloud slot
+ * reserves a full-capacity cloud with its voxel index and contact cells (about 1.2 MB at
+ * cloud_cap 8000), and every live object holds one.  A map whose live objects would exceed
+ * max_clouds sets the capacity bit of its error word (the observation that would have created
+ * the object is dropped), as running out of object slots does.  smg_create is this call with
+ * max_clouds = max_objects. */
+int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_clouds, int emb_dim, int max_w, int max_h,
+                      int max_det, int grid_w, int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out);
 int smg_destroy(smg_batch* b);
 
 /* One keyframe for each of the first n maps (frames[i] -> map i).  Replaces, per map,
@@ -178,6 +187,12 @@ int smg_destroy(smg_batch* b);
  * (NULL = the legacy default stream).  Returns before the device work finishes; results
  * are read with the getters below (which synchronise the stream). */
 int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, void* stream);
+
+/* Whether pushes build the whole-object re-encode requests (on by default).  The reference's
+ * push builds them on every frame that carries detection embeddings (capi.cpp:1002-1010); a
+ * caller that never encodes whole-object crops can switch the stage off.  With it off,
+ * smg_get_reencode returns no requests. */
+int smg_set_reencode(smg_batch* b, int on);
 
 /* ---- results (device -> host on request; each getter synchronises the batch stream) ---- */
 typedef struct smg_object {

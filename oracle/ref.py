@@ -72,6 +72,7 @@ def ref_lib():
         L.ref_create.restype = C.c_void_p
         L.ref_create.argtypes = [C.c_char_p, C.c_double, C.c_int, C.c_int, P(C.c_float), C.c_int]
         L.ref_destroy.argtypes = [C.c_void_p]
+        L.ref_set_reencode.argtypes = [C.c_void_p, C.c_int]
         L.ref_frame.argtypes = [C.c_void_p, P(RfFrame)]
         L.ref_n_objects.argtypes = [C.c_void_p]
         L.ref_objects.argtypes = [C.c_void_p, P(RfObj), C.c_int]
@@ -188,6 +189,9 @@ class RefMap:
         if getattr(self, "_h", None):
             ref_lib().ref_destroy(self._h)
             self._h = None
+
+    def set_reencode(self, on: bool) -> None:
+        ref_lib().ref_set_reencode(self._h, 1 if on else 0)
 
     def frame(self, fr: dict) -> None:
         keep = []

@@ -98,6 +98,7 @@ struct RefMap {
   std::vector<ObsPoints> pts;   // copy of lastPoints() as handed to addPoints
   std::vector<ReencReq> reenc;  // re-encode requests of the last keyframe
   int reenc_words = 0;
+  bool reenc_on = true;   // build the re-encode requests (the reference's push always does)
   explicit RefMap(const ObjParams& p) : om(p) {}
 };
 
@@ -124,6 +125,9 @@ void* ref_create(const char* obj_kv, double voxel, int cloud_cap, int grid_on, c
 }
 
 void ref_destroy(void* h) { delete static_cast<RefMap*>(h); }
+
+// Skip buildReencode (to time the keyframe without the re-encode stage, as the device can).
+void ref_set_reencode(void* h, int on) { static_cast<RefMap*>(h)->reenc_on = on != 0; }
 
 int ref_frame(void* h, const rf_frame* f) {
   RefMap* m = static_cast<RefMap*>(h);
@@ -204,7 +208,7 @@ int ref_frame(void* h, const rf_frame* f) {
   for (const ObsPoints& q : m->pts) m->om.addPoints(q.obj_id, q.xyz.data(), nullptr, int(q.px.size() / 2), f->stamp);
   // whole-object re-encode requests on frames with detection embeddings (capi.cpp:1002-1005),
   // the mask grid being the image grid
-  if (n > 0 && f->emb)
+  if (n > 0 && f->emb && m->reenc_on)
     m->om.buildReencode(F, d.img_w, d.img_h, d.mask_w, d.mask_h, d.mask_sx, d.mask_sy, d.mask_ox, d.mask_oy, &m->reenc);
   m->reenc_words = int((size_t(d.mask_w) * d.mask_h + 31) / 32);
   return 0;

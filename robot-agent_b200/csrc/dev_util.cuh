@@ -547,6 +547,10 @@ DEV double dist3(const double* a, const double* b) {
 
 DEV void set_err(MapRec* m, int bit) { atomicOr(&m->err, bit); }
 
+// global index of cloud slot `slot` of map m (clouds are a pool of B.C slots per map, separate
+// from the B.O object slots)
+__host__ __device__ inline size_t cglob(const Batch& B, int m, int slot) { return (size_t)m * B.C + slot; }
+
 // Scan box of detection k in depth pixels (objmap.cpp:648-652): the detector box scaled from
 // the detector image to the depth image (float scale, truncation to int), grown by one pixel
 // and clipped to the frame.

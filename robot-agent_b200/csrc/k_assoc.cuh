@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
     if (!INB(slot, B.O, 202)) continue;
     const double cs = has_z ? cos_max_warp(B, og, ob, zs) : -2.0;
     if (has_z && lane == 0) wk_add(&B.maps[m], SMG_WK_VEC16, (ob.nrm_frag > 0 ? 2 : 0) + ob.n_views);
-    const size_t cslot = oglob(B, m, ob.cloud_slot);
+    const size_t cslot = cglob(B, m, ob.cloud_slot);
     const int hits = contact_hits_warp(B, cslot, sp, nsp, P.contact_cell);
     if (lane == 0) {
       const double contact = (nsp > 0 && B.clouds[cslot].cn > 0) ? (double)hits / (double)nsp : 0.0;

@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(512) k_cloud_add(Batch B) {
     const int slot = B.tgt_slot[(size_t)m * B.O + j];
     if (!INB(slot, B.O, 406)) continue;
     const ObjRec& o = B.objs[oglob(B, m, slot)];
-    const size_t cs = (size_t)m * B.O + o.cloud_slot;
+    const size_t cs = cglob(B, m, o.cloud_slot);
     for (int e = 0; e < R.n_pts; ++e) {
       if (!INB(e, B.max_det, 407)) break;
       const PtsRec& pr = B.ptsl[(size_t)m * B.max_det + e];

@@ -18,7 +18,7 @@
 
 // ObjCloud::translate (cloud.cpp:79-84) along axis k only, as the reference calls it once per axis
 DEV void cloud_translate_axis(const Batch& B, int m, const ObjRec& o, int k, double dk, double t) {
-  CloudRec& C = B.clouds[(size_t)m * B.O + o.cloud_slot];
+  CloudRec& C = B.clouds[cglob(B, m, o.cloud_slot)];
   if (C.n <= 0 || dk == 0) return;
   C.org[k] += dk;
   ++C.version;
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(HANDS_THREADS) k_hands(Batch B) {
   // this frame read it, so it is rebuilt here.  Every index is current at the start of a frame
   // (k_cloud_add rebuilds the stale ones), so a stale one now is a cloud moved above.
   for (int i = 0; i < n; ++i) {
-    const size_t cs = (size_t)m * B.O + obj_at(B, m, i).cloud_slot;
+    const size_t cs = cglob(B, m, obj_at(B, m, i).cloud_slot);
     if (B.clouds[cs].cver != B.clouds[cs].version) contact_rebuild(B, cs, bs);
     __syncthreads();
   }

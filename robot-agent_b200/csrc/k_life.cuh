@@ -24,7 +24,7 @@ DEV int absent_evidence_warp(const Batch& B, int m, const ObjRec& o, const Frame
   to_cam(T, o.pos, cc);
   if (cc[2] < 0.3 || cc[2] > (double)P.zmax) return 0;
   if (o.max_det_z > 0 && cc[2] > P.absent_det_k * o.max_det_z + 0.2) return 0;
-  const size_t cs = (size_t)m * B.O + o.cloud_slot;
+  const size_t cs = cglob(B, m, o.cloud_slot);
   const CloudRec& C = B.clouds[cs];
   const int nc = C.n;
   const int K = max(8, P.absent_samples);
@@ -129,7 +129,7 @@ DEV void erase_pos(const Batch& B, int m, int pos, bool keep_cloud) {
   const int slot = ord[pos];
   const ObjRec& o = B.objs[oglob(B, m, slot)];
   if (!INB(pos, R->n_obj, 501)) return;
-  if (!keep_cloud) { if (INB(R->n_cfree, B.O, 502)) B.cfreel[(size_t)m * B.O + R->n_cfree++] = o.cloud_slot; }
+  if (!keep_cloud) { if (INB(R->n_cfree, B.C, 502)) B.cfreel[(size_t)m * B.C + R->n_cfree++] = o.cloud_slot; }
   if (INB(R->n_free, B.O, 503)) B.freel[(size_t)m * B.O + R->n_free++] = slot;
   for (int i = pos + 1; i < R->n_obj; ++i) ord[i - 1] = ord[i];
   --R->n_obj;
@@ -303,10 +303,10 @@ __global__ void __launch_bounds__(256) k_relink(Batch B) {
     const ObjRec& no = B.objs[oglob(B, m, slot_at(B, m, ni))];
     for (int k = 0; k < 3; ++k) { mo.pos[k] = no.pos[k]; mo.ext[k] = no.ext[k]; mo.lo[k] = no.lo[k]; mo.hi[k] = no.hi[k]; }
     // m takes n's cloud (m.cloud = n.cloud; version = n.version + 1); m's old cloud slot is freed
-    if (!INB(R->n_cfree, B.O, 505)) continue;
-    B.cfreel[(size_t)m * B.O + R->n_cfree++] = mo.cloud_slot;
+    if (!INB(R->n_cfree, B.C, 505)) continue;
+    B.cfreel[(size_t)m * B.C + R->n_cfree++] = mo.cloud_slot;
     mo.cloud_slot = no.cloud_slot;
-    ++B.clouds[(size_t)m * B.O + mo.cloud_slot].version;
+    ++B.clouds[cglob(B, m, mo.cloud_slot)].version;
     mo.n_obs += no.n_obs;
     mo.last_seen = no.last_seen;
     mo.last_kf = no.last_kf;
@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
     int need = 0;
     if (b < R.n_obj) {
       const ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
-      const CloudRec& C = B.clouds[(size_t)m * B.O + o.cloud_slot];
+      const CloudRec& C = B.clouds[cglob(B, m, o.cloud_slot)];
       need = o.held_by < 0 && o.geo_ver != C.version && C.n >= 30;
     }
     int tot;
@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
   for (int q = 0; q < nm; ++q) {
     const int b = mine[q];
     ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
-    const size_t cs = (size_t)m * B.O + o.cloud_slot;
+    const size_t cs = cglob(B, m, o.cloud_slot);
     const CloudRec& C = B.clouds[cs];
     // cloudSample(m, 800) (objmap.cpp:1107-1114)
     const size_t stp = (size_t)C.n / 800 > 1 ? (size_t)C.n / 800 : 1;
@@ -442,7 +442,7 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
     if (o.drop) { ++nstruct; rm = true; }
     else if (!o.confirmed) rm = F.stamp - o.last_seen > P.prune_s;
     else rm = o.state == 1 && !o.moved && (int)o.n_obs < P.spurious_obs;
-    const CloudRec& C = B.clouds[(size_t)m * B.O + o.cloud_slot];
+    const CloudRec& C = B.clouds[cglob(B, m, o.cloud_slot)];
     s_slot[b] = slot;
     s_id[b] = o.id;
     s_rm[b] = rm;
@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
     }
     if (rm) {
       const ObjRec& o = B.objs[oglob(B, m, s_slot[b])];
-      if (INB(ncfree0 + rmd + pr, B.O, 510)) B.cfreel[(size_t)m * B.O + ncfree0 + rmd + pr] = o.cloud_slot;
+      if (INB(ncfree0 + rmd + pr, B.C, 510)) B.cfreel[(size_t)m * B.C + ncfree0 + rmd + pr] = o.cloud_slot;
       if (INB(nfree0 + rmd + pr, B.O, 511)) B.freel[(size_t)m * B.O + nfree0 + rmd + pr] = s_slot[b];
     }
     kept += tk;
@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
   }
   if (tid == 0) {
     R->st.n_obj_struct += nstruct;
-    R->n_cfree = ncfree0 + rmd <= B.O ? ncfree0 + rmd : B.O;
+    R->n_cfree = ncfree0 + rmd <= B.C ? ncfree0 + rmd : B.C;
     R->n_free = nfree0 + rmd <= B.O ? nfree0 + rmd : B.O;
     R->n_obj = kept;
     R->n_targets = nt;

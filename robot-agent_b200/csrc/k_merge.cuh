@@ -92,16 +92,16 @@ __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
     const size_t ogi = oglob(B, m, si), ogj = oglob(B, m, sj);
     const ObjRec& a = B.objs[ogi];
     const ObjRec& b = B.objs[ogj];
-    const int scn_i = B.clouds[(size_t)m * B.O + a.cloud_slot].n, scn_j = B.clouds[(size_t)m * B.O + b.cloud_slot].n;
+    const int scn_i = B.clouds[cglob(B, m, a.cloud_slot)].n, scn_j = B.clouds[cglob(B, m, b.cloud_slot)].n;
     const bool a_small = scn_i <= scn_j;
     const ObjRec& sm = a_small ? a : b;
     const ObjRec& lg = a_small ? b : a;
-    const size_t css = (size_t)m * B.O + sm.cloud_slot, csl = (size_t)m * B.O + lg.cloud_slot;
+    const size_t css = cglob(B, m, sm.cloud_slot), csl = cglob(B, m, lg.cloud_slot);
     const int cn = a_small ? scn_i : scn_j;
     const int stp = max(1, cn / max(1, P.contact_samples));
     const int nsp = cn > 0 ? (cn + stp - 1) / stp : 0;
     // cached cosine and contact of an unchanged pair
-    const uint32_t ca = B.clouds[(size_t)m * B.O + a.cloud_slot].version, cb = B.clouds[(size_t)m * B.O + b.cloud_slot].version;
+    const uint32_t ca = B.clouds[cglob(B, m, a.cloud_slot)].version, cb = B.clouds[cglob(B, m, b.cloud_slot)].version;
     PairCacheRec& pc = B.pcache[(size_t)m * PCACHE_SLOTS + (hmix(((uint64_t)a.id << 32) | b.id) & (PCACHE_SLOTS - 1))];
     const bool hit = pc.ida == a.id && pc.idb == b.id && pc.va == a.ver && pc.vb == b.ver && pc.ca == ca && pc.cb == cb;
     double cs = -2, contact = 0.0;
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
     const size_t oga = oglob(B, m, sh_ka), ogb = oglob(B, m, sh_kb);
     ObjRec& a = B.objs[oga];
     const ObjRec& b = B.objs[ogb];
-    const size_t csa = (size_t)m * B.O + a.cloud_slot, csb = (size_t)m * B.O + b.cloud_slot;
+    const size_t csa = cglob(B, m, a.cloud_slot), csb = cglob(B, m, b.cloud_slot);
     // cloud: b's points (org + p) into a (merge.cpp:64-75)
     const CloudRec& Cb = B.clouds[csb];
     const int nb = Cb.n;

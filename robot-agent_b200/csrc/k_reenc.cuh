@@ -83,7 +83,7 @@ DEV float block_select_f(const float* a, int n, int k, int* hist, int* s_pick) {
 
 // the cheap tests of objmap.cpp:1383 (every object here is an objprob object)
 DEV bool reenc_candidate(const Batch& B, int m, const ObjRec& o, double stamp) {
-  return o.confirmed && o.held_by < 0 && o.state != 1 && o.last_kf == stamp && B.clouds[(size_t)m * B.O + o.cloud_slot].n >= 30;
+  return o.confirmed && o.held_by < 0 && o.state != 1 && o.last_kf == stamp && B.clouds[cglob(B, m, o.cloud_slot)].n >= 30;
 }
 
 // viewKappa (bestview.cpp:77-81, objprob_math.h:78-87) with a visible fraction; the camera blur
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
     const int j = blockIdx.x + q * gridDim.x;
     const int b = s_cand[q];
     const ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, b))];
-    const size_t cs = (size_t)m * B.O + o.cloud_slot;
+    const size_t cs = cglob(B, m, o.cloud_slot);
     const CloudRec& C = B.clouds[cs];
     const float4* pts = B.cpts + cs * B.cap;
     const int n = C.n;

@@ -33,7 +33,7 @@ DEV void rec_load(ObjRec* dst, const ObjRec* src) {
     if (j * 32 + lane < NW) d[j * 32 + lane] = t[j];
 }
 
-DEV size_t cslot_glob(const Batch& B, int m, const ObjRec& o) { return (size_t)m * B.O + o.cloud_slot; }
+DEV size_t cslot_glob(const Batch& B, int m, const ObjRec& o) { return cglob(B, m, o.cloud_slot); }
 
 // ObjectMap::firstView (objmap.cpp:247-252) over the view-first hash
 DEV int64_t view_cell_key(double x, double y, double cell) {
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
     obs_rec[tid] = valid ? first : -1;
     rec_slot[tid] = valid && first == tid ? slot_at(B, m, b) : -1;
     fl[tid] = tid < n_free0 && INB(n_free0 - 1 - tid, B.O, 303) ? B.freel[(size_t)m * B.O + n_free0 - 1 - tid] : -1;
-    cfl[tid] = tid < n_cfree0 && INB(n_cfree0 - 1 - tid, B.O, 303) ? B.cfreel[(size_t)m * B.O + n_cfree0 - 1 - tid] : -1;
+    cfl[tid] = tid < n_cfree0 && INB(n_cfree0 - 1 - tid, B.C, 303) ? B.cfreel[(size_t)m * B.C + n_cfree0 - 1 - tid] : -1;
   }
   __syncthreads();
   for (int r = tid >> 5; r < nobs; r += blockDim.x >> 5)
@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
         mo.geo_ver = 0xffffffffu;
         const double sd = P.ap_r0 + P.ap_r1 * o.zmed;
         for (int k = 0; k < 3; ++k) mo.P[k] = sd * sd + (o.trunc ? 0.25 * o.ext[k] * o.ext[k] : 0.0);
-        CloudRec& C = B.clouds[(size_t)m * B.O + s_cs[a]];
+        CloudRec& C = B.clouds[cglob(B, m, s_cs[a])];
         C.has_org = 0;
         C.n = 0;
         C.version = 0;

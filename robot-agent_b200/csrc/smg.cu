@@ -329,7 +329,13 @@ static int pow2_at_least(long long n) {
 
 int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, int max_w, int max_h, int max_det, int grid_w,
                int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out) {
-  if (!p || !out || n_maps <= 0 || max_objects <= 0 || emb_dim <= 0 || emb_dim > 2048 || max_w <= 0 || max_h <= 0 || max_det <= 0 ||
+  return smg_create_pooled(p, n_maps, max_objects, max_objects, emb_dim, max_w, max_h, max_det, grid_w, grid_h, grid_x0, grid_y0,
+                           dev, out);
+}
+
+int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_clouds, int emb_dim, int max_w, int max_h,
+                      int max_det, int grid_w, int grid_h, int grid_x0, int grid_y0, int dev, smg_batch** out) {
+  if (!p || !out || n_maps <= 0 || max_objects <= 0 || max_clouds <= 0 || max_clouds > max_objects || emb_dim <= 0 || emb_dim > 2048 || max_w <= 0 || max_h <= 0 || max_det <= 0 ||
       max_det > SMG_MAX_DET || grid_w <= 0 || grid_h <= 0 || p->topk <= 0 || p->topk > SMG_TOPK_MAX || p->bins <= 0 ||
       p->bins > SMG_BINS_MAX || max_objects > PRUNE_MAX || p->n_grip_gap < 0 || p->n_grip_gap > 8 || p->cloud_cap <= 0 || p->voxel <= 0 || p->ransac_iters > RANSAC_MAX ||
       (size_t)max_h * ((max_w + 31) / 32) * 4 + RE_ZMAX * 4 > 227 * 1024)   // re-encode mask held in shared memory
@@ -348,7 +354,9 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   Batch& B = b->B;
   memset(&B, 0, sizeof(B));
   const int M = n_maps, O = max_objects, D = emb_dim;
-  B.M = M; B.O = O; B.D = D; B.topk = p->topk; B.max_det = max_det; B.W = max_w; B.H = max_h; B.map0 = 0;
+  const int CP = max_clouds;
+  B.M = M; B.O = O; B.C = CP; B.D = D; B.topk = p->topk; B.max_det = max_det; B.W = max_w; B.H = max_h; B.map0 = 0;
+  B.reenc_on = 1;
   B.p = *p;
   B.cap = 2 * p->cloud_cap;
   B.HC = pow2_at_least(2LL * B.cap);
@@ -380,20 +388,21 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
   DA(B.objs, MO);
   DA(B.order, MO);
   DA(B.freel, MO);
-  DA(B.cfreel, MO);
+  const size_t MC = (size_t)M * CP;
+  DA(B.cfreel, MC);
   DA(B.assoc, (size_t)M * max_det);
   DA(B.rfrag, MO * D);
   DA(B.mu, MO * D);
   DA(B.views, MO * (B.topk + 1) * D);
-  DA(B.clouds, MO);
-  DA(B.cpts, MO * B.cap);
-  DA(B.crgb, MO * B.cap);
-  DA(B.chkey, MO * B.HC);
-  DA(B.chidx, MO * B.HC);
-  DA(B.chgen, MO * B.HC);
-  DA(B.cbits, MO * 2 * CB_WORDS);
-  DA(B.ckey, MO * B.HCC);
-  DA(B.cgen, MO * B.HCC);
+  DA(B.clouds, MC);
+  DA(B.cpts, MC * B.cap);
+  DA(B.crgb, MC * B.cap);
+  DA(B.chkey, MC * B.HC);
+  DA(B.chidx, MC * B.HC);
+  DA(B.chgen, MC * B.HC);
+  DA(B.cbits, MC * 2 * CB_WORDS);
+  DA(B.ckey, MC * B.HCC);
+  DA(B.cgen, MC * B.HCC);
   const size_t MD = (size_t)M * max_det;
   DA(B.px, MD * 4 * B.pmax);
   DA(B.ppix, MD * 2 * B.pmax);
@@ -468,7 +477,7 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
       memset(&r, 0, sizeof(r));
       r.next_id = 1;
       r.n_free = O;
-      r.n_cfree = O;
+      r.n_cfree = CP;
       r.kf_first = 1;
       r.kf_last_changed = 1 << 30;
     }
@@ -477,10 +486,13 @@ int smg_create(const smg_params* p, int n_maps, int max_objects, int emb_dim, in
     for (int m = 0; m < M; ++m)
       for (int i = 0; i < O; ++i) fl[(size_t)m * O + i] = O - 1 - i;   // pop order 0, 1, 2, ...
     CK(cudaMemcpy(B.freel, fl.data(), sizeof(int32_t) * MO, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(B.cfreel, fl.data(), sizeof(int32_t) * MO, cudaMemcpyHostToDevice));
-    std::vector<CloudRec> cl(MO);
+    std::vector<int32_t> cfl(MC);
+    for (int m = 0; m < M; ++m)
+      for (int i = 0; i < CP; ++i) cfl[(size_t)m * CP + i] = CP - 1 - i;   // pop order 0, 1, 2, ...
+    CK(cudaMemcpy(B.cfreel, cfl.data(), sizeof(int32_t) * MC, cudaMemcpyHostToDevice));
+    std::vector<CloudRec> cl(MC);
     for (auto& c : cl) { memset(&c, 0, sizeof(c)); c.vgen = 1; c.cgen = 1; c.cver = 0xffffffffu; }
-    CK(cudaMemcpy(B.clouds, cl.data(), sizeof(CloudRec) * MO, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(B.clouds, cl.data(), sizeof(CloudRec) * MC, cudaMemcpyHostToDevice));
     const std::vector<int32_t>& need = need_table();
     CK(cudaMemcpy(B.need_tab, need.data(), sizeof(int32_t) * need.size(), cudaMemcpyHostToDevice));
     // export8 / probability LUTs (grid.cpp:118-123)
@@ -576,6 +588,7 @@ __global__ void k_begin(Batch B) {
     R->n_obs = 0;
     R->n_pts = 0;
     R->n_targets = 0;
+    if (!B.reenc_on) R->re_n = 0;
     B.mcand_n[m] = 0;
     B.mgl_n[m] = 0;
     B.mgl_n[B.M + m] = 0;
@@ -655,12 +668,12 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   k_cloud_add<<<dim3(WORK_SLOTS, Mg), 512, 0, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({12, {e0, e1}}); } }
-  { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+  if (B.reenc_on) { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_reenc<<<dim3(RE_CTAS, Mg), RE_THREADS, RE_SMEM(B), st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({14, {e0, e1}}); } }
   CK(cudaStreamWaitEvent(st, ejoin, 0));   // join
-  b->launches += 17;
+  b->launches += B.reenc_on ? 17 : 16;
   return SMG_OK;
 }
 
@@ -1037,7 +1050,7 @@ int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap) {
     ObjRec o;
     CK(cudaMemcpy(&o, B.objs + (size_t)m * B.O + ord[i], sizeof(ObjRec), cudaMemcpyDeviceToHost));
     CloudRec c;
-    CK(cudaMemcpy(&c, B.clouds + (size_t)m * B.O + o.cloud_slot, sizeof(CloudRec), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(&c, B.clouds + cglob(B, m, o.cloud_slot), sizeof(CloudRec), cudaMemcpyDeviceToHost));
     smg_object& r = out[i];
     memset(&r, 0, sizeof(r));
     r.id = o.id;
@@ -1107,7 +1120,7 @@ int smg_get_object_cloud(smg_batch* b, int m, int i, float* xyz, uint32_t* seq, 
   CK(cudaMemcpy(&slot, B.order + (size_t)m * B.O + i, sizeof(int32_t), cudaMemcpyDeviceToHost));
   ObjRec o;
   CK(cudaMemcpy(&o, B.objs + (size_t)m * B.O + slot, sizeof(ObjRec), cudaMemcpyDeviceToHost));
-  const size_t cs = (size_t)m * B.O + o.cloud_slot;
+  const size_t cs = cglob(B, m, o.cloud_slot);
   CloudRec c;
   CK(cudaMemcpy(&c, B.clouds + cs, sizeof(CloudRec), cudaMemcpyDeviceToHost));
   const int n = std::min(cap, c.n);
@@ -1905,6 +1918,13 @@ int smg_plane_fit_noalloc(const float* xyz, const int32_t* off, int n_sets, int 
   k_plane_sets<<<n_sets, PF_THREADS, 0, (cudaStream_t)stream>>>(xyz, off, n_sets, n_points, tau, seeds, max_iters, d.need,
                                                                   d.scratch, out);
   CK(cudaGetLastError());
+  return SMG_OK;
+}
+
+int smg_set_reencode(smg_batch* b, int on) {
+  if (!b) return fail(SMG_ERR_ARGS, "smg_set_reencode: bad arguments");
+  if (int r = sync_b(b)) return r;
+  b->B.reenc_on = on != 0;
   return SMG_OK;
 }
 

@@ -8,7 +8,7 @@
 //                             through order[M*O] (slot indices), slots are recycled through a free list
 //   rfrag[M*O*D]  f32         ApState::r_frag
 //   views[M*O*(topk+1)*D] u16 ApState::views[].z (fp16 bits), one spare slot for insertion
-//   cloud pool, one per object slot (ObjCloud, cloud.hpp:165-189):
+//   cloud pool, C slots per map, one held by each object (ObjCloud, cloud.hpp:165-189):
 //     cpts[cap] float4 (x,y,z relative to org, seq bits), crgb[cap] u32,
 //     chkey/chidx[HC]   voxel-key -> point index hash (VoxelIndex, cloud.cpp:48-64),
 //     ckey/cgen[HC]     4 cm contact-cell set (ApContactIdx, objprob.cpp:470-487), generation-cleared
@@ -257,7 +257,9 @@ typedef struct {
 typedef struct {
   // sizes
   int32_t M, O, D, topk, cap, HC, HCC, pmax, max_det, W, H;
+  int32_t C;                            // cloud slots per map (a pool shared by the map's objects)
   int32_t map0;                         // first map of the launch (maps are split into stream groups)
+  int32_t reenc_on;                     // build whole-object re-encode requests (smg_set_reencode)
   int32_t work_n;                       // points per work area
   size_t work_stride;                   // bytes per work area
   int32_t gw_grid, gh_grid, gx0, gy0;   // occupancy window
@@ -277,20 +279,20 @@ typedef struct {
   ObjRec* objs;
   int32_t* order;        // [M*O]
   int32_t* freel;        // [M*O] free object-slot stack
-  int32_t* cfreel;       // [M*O] free cloud-slot stack
+  int32_t* cfreel;       // [M*C] free cloud-slot stack
   AssocRec* assoc;       // [M*max_det]
   float* rfrag;          // [M*O*D]
   float* mu;             // [M*O*D] float(r_frag / |r_frag|) (ApState mu_c), refreshed with r_frag
   uint16_t* views;       // [M*O*(topk+1)*D]
-  CloudRec* clouds;      // [M*O]
-  float4* cpts;          // [M*O*cap]
-  uint32_t* crgb;        // [M*O*cap]
-  uint64_t* chkey;       // [M*O*HC]
-  uint32_t* chidx;       // [M*O*HC]
-  uint32_t* chgen;       // [M*O*HC]
-  uint32_t* cbits;       // [M*O*2*CB_WORDS] occupancy + dilated bitsets
-  uint64_t* ckey;        // [M*O*HCC]
-  uint32_t* cgen;        // [M*O*HCC]
+  CloudRec* clouds;      // [M*C]
+  float4* cpts;          // [M*C*cap]
+  uint32_t* crgb;        // [M*C*cap]
+  uint64_t* chkey;       // [M*C*HC]
+  uint32_t* chidx;       // [M*C*HC]
+  uint32_t* chgen;       // [M*C*HC]
+  uint32_t* cbits;       // [M*C*2*CB_WORDS] occupancy + dilated bitsets
+  uint64_t* ckey;        // [M*C*HCC]
+  uint32_t* cgen;        // [M*C*HCC]
   // per-frame scratch
   double* px;            // [M*max_det*pmax] x4 (X, Y, Z, ZC)
   int32_t* ppix;         // [M*max_det*pmax] x2 (PU, PV)

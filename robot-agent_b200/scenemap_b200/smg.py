@@ -65,6 +65,7 @@ def lib():
         L.smg_params_apply.argtypes = [vp, C.c_char_p]
         L.smg_params_set_cloud.argtypes = [vp, C.c_double, C.c_int]
         L.smg_create.argtypes = [vp] + [C.c_int] * 11 + [P(vp)]
+        L.smg_create_pooled.argtypes = [vp] + [C.c_int] * 12 + [P(vp)]
         L.smg_destroy.argtypes = [vp]
         L.smg_push_frames.argtypes = [vp, P(SmgFrame), C.c_int, C.c_int, vp]
         L.smg_get_objects.argtypes = [vp, C.c_int, P(SmgObject), C.c_int]
@@ -85,17 +86,18 @@ def lib():
         L.smg_kernel_launches.restype = C.c_int64
         L.smg_kernel_launches.argtypes = [vp]
         L.smg_get_work.argtypes = [vp, C.POINTER(C.c_int64), C.c_int]
+        L.smg_set_reencode.argtypes = [vp, C.c_int]
         L.smg_plane_fit.argtypes = [vp, vp, C.c_int, C.c_int, C.c_double, vp, C.c_int, vp, vp]
         L.smg_plane_fit_noalloc.argtypes = [vp, vp, C.c_int, C.c_int, C.c_double, vp, C.c_int, vp, vp]
         _lib = L
     return _lib
 
 
-EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "smg_params_apply", "smg_create", "smg_destroy", "smg_push_frames",
+EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "smg_params_apply", "smg_create", "smg_create_pooled", "smg_destroy", "smg_push_frames",
             "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
             "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
             "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
-           "smg_get_work", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
+           "smg_get_work", "smg_set_reencode", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
            "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode"]
 
@@ -133,7 +135,7 @@ class Params:
 class Batch:
     def __init__(self, n_maps: int, max_objects: int = 256, emb_dim: int = 1152, max_w: int = 640, max_h: int = 480,
                  max_det: int = 32, grid=(512, 512, -256 + 60, -256 + 50), params: Params | None = None, dev: int = 0,
-                 cloud_cap: int | None = None):
+                 cloud_cap: int | None = None, max_clouds: int | None = None):
         L = lib()
         self.params = params or Params()
         if cloud_cap is not None:   # ObjectMap::setCloudParams (objmap.hpp:255-258)
@@ -142,8 +144,9 @@ class Batch:
         self.max_w, self.max_h = max_w, max_h
         self.grid = grid
         h = C.c_void_p()
-        _check(L.smg_create(self.params.buf, n_maps, max_objects, emb_dim, max_w, max_h, max_det, grid[0], grid[1],
-                            grid[2], grid[3], dev, C.byref(h)), "smg_create")
+        self.max_clouds = max_clouds or max_objects
+        _check(L.smg_create_pooled(self.params.buf, n_maps, max_objects, self.max_clouds, emb_dim, max_w, max_h, max_det,
+                                   grid[0], grid[1], grid[2], grid[3], dev, C.byref(h)), "smg_create_pooled")
         self.h = h
 
     def close(self):
@@ -309,6 +312,9 @@ class Batch:
         out = np.zeros(self.n_maps * self.max_det, np.uint32)
         _check(lib().smg_get_assoc_all(self.h, _ptr(out)), "smg_get_assoc_all")
         return out.reshape(self.n_maps, self.max_det)
+
+    def set_reencode(self, on: bool):
+        _check(lib().smg_set_reencode(self.h, 1 if on else 0), "smg_set_reencode")
 
     def timing(self, on: bool = True):
         _check(lib().smg_timing_enable(self.h, 1 if on else 0), "smg_timing_enable")
