@@ -214,6 +214,8 @@ typedef struct smg_object {
   int32_t n_views, n_ap_obs, need_whole;
   double P[3];
   int32_t n_cams, geo;
+  double k_whole;              /* ApState::k_whole (sum of whole-view kappas) */
+  int32_t n_whole;             /* whole views since the last merge (ApState::n_whole) */
   int32_t held_by;             /* hand holding the object, -1 = none (MapObject::held_by) */
   uint32_t parent;             /* object it rests on / in and follows, 0 = none (MapObject::parent) */
   double parent_rel[3];
@@ -254,6 +256,20 @@ typedef struct smg_reenc_req {
  * bits + r * ceil(max_w * max_h / 32): ceil(mask_w * mask_h / 32) words, bit q = pixel q of
  * the row-major mask grid, LSB first.  Returns the number of requests (up to cap copied). */
 int smg_get_reencode(smg_batch* b, int m, smg_reenc_req* reqs, uint32_t* bits, int cap);
+/* The whole-object embeddings the caller computed for the re-encode requests (sm_set_object_
+ * embeddings, scenemap include/scenemap.h:410, capi.cpp:1825-1835): entry i is an L2-normalised
+ * fp32 embedding (dim = the batch's emb_dim) of object ids[i] of map maps[i].  It is added as a
+ * whole view (ObjectMap::addWholeView, objmap.cpp:1361-1369: r_whole, whole-first view order,
+ * need_whole cleared) when that map's last keyframe requested the object and the object still
+ * exists, with the request's kappa and camera; otherwise it is ignored, as in the reference.
+ * Entries of one map apply in call order.  n <= n_maps * 64.  Runs on `stream` after the last
+ * push; with SMG_MEM_HOST arrays the call returns when they have been read. */
+int smg_set_object_embeddings(smg_batch* b, const int32_t* maps, const uint32_t* ids, const float* emb, int n, int dim, int where,
+                              void* stream);
+/* r_whole (emb_dim floats, zeros when the object has none) and k_whole of object i of map m;
+ * returns n_whole. */
+int smg_get_object_whole(smg_batch* b, int m, int i, float* r_whole, double* k_whole);
+
 /* Per-kernel device time with CUDA events on the launch stream (instrumentation, off by
  * default).  smg_timing_read fills ms[k] (total milliseconds) and n[k] (launches) for the
  * SMG_NUM_KERNELS kernels of the keyframe chain and resets the counters; names[k] is static. */

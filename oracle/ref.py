@@ -90,6 +90,7 @@ def ref_lib():
                                 C.c_int]
         L.ref_reenc_words.argtypes = [C.c_void_p]
         L.ref_add_whole_views.argtypes = [C.c_void_p, P(C.c_uint32), P(C.c_float), C.c_int, C.c_int, C.c_double]
+        L.ref_object_whole.argtypes = [C.c_void_p, C.c_int, P(C.c_float), C.c_int, P(C.c_double)]
         L.ref_grid_geom.argtypes = [C.c_void_p, P(C.c_int32)]
         L.ref_grid_cells.argtypes = [C.c_void_p, P(C.c_int16), P(C.c_uint8), P(C.c_int8)]
         L.ref_occ_create.restype = C.c_void_p
@@ -224,6 +225,13 @@ class RefMap:
         nv = L.ref_object_vectors(self._h, i, _p(r, C.c_float), D, _p(views, C.c_uint16), _p(vk, C.c_float),
                                   _p(vs, C.c_double), 5)
         return r, views[:nv], vk[:nv], vs[:nv]
+
+    def object_whole(self, i: int, D: int):
+        """r_whole (zeros when empty), k_whole and n_whole of object i."""
+        r = np.zeros(D, np.float32)
+        k = C.c_double(0)
+        n = ref_lib().ref_object_whole(self._h, i, _p(r, C.c_float), D, C.byref(k))
+        return r, k.value, n
 
     def object_cloud(self, i: int):
         L = ref_lib()

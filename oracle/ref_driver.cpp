@@ -248,6 +248,16 @@ int ref_add_whole_views(void* h, const uint32_t* ids, const float* emb, int n, i
   return added;
 }
 
+// r_whole of object i (zeros when it has none) and k_whole; returns n_whole (-1: no object)
+int ref_object_whole(void* h, int i, float* r_whole, int D, double* k_whole) {
+  const auto& objs = static_cast<RefMap*>(h)->om.objects();
+  if (i < 0 || size_t(i) >= objs.size() || !objs[size_t(i)].ap) return -1;
+  const ApState& s = *objs[size_t(i)].ap;
+  for (int k = 0; k < D; ++k) r_whole[k] = size_t(k) < s.r_whole.size() ? s.r_whole[size_t(k)] : 0.f;
+  *k_whole = s.k_whole;
+  return s.r_whole.empty() ? 0 : s.n_whole;
+}
+
 int ref_n_objects(void* h) { return int(static_cast<RefMap*>(h)->om.objects().size()); }
 
 int ref_objects(void* h, rf_obj* out, int cap) {

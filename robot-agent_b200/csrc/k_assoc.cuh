@@ -136,6 +136,7 @@ DEV double cos_max_warp(const Batch& B, size_t og, const ObjRec& o, const float*
   const int D = B.D;
   double best = -1;
   if (o.nrm_frag > 0) best = smax(best, dot_f32_warp(rfrag_of(B, og), z, D) / sqrt(o.nrm_frag));
+  if (o.has_whole && o.nrm_whole > 0) best = smax(best, dot_f32_warp(B.rwhole + og * B.D, z, D) / sqrt(o.nrm_whole));
   for (int v = 0; v < o.n_views; ++v) best = smax(best, dot_f16_warp(view_of(B, og, o.view_slot[v]), z, D));
   return best;
 }

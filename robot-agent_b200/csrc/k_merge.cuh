@@ -257,10 +257,20 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
     }
     __syncthreads();
     if (nb > 0) cloud_add(B, m, csa, xyz, rgb, nb, t, W, hist, bs);
-    // apMerge: vectors (objprob.cpp:359-377)
+    // apMerge: vectors (objprob.cpp:359-377): whole views were parts of the merged object, so
+    // r_frag += a.r_whole, += b.r_frag, += b.r_whole (each added only when it holds a vector)
     float* ra = B.rfrag + oga * B.D;
     const float* rb = B.rfrag + ogb * B.D;
-    for (int i = tid; i < B.D; i += blockDim.x) ra[i] += rb[i];
+    const float* raw = B.rwhole + oga * B.D;
+    const float* rbw = B.rwhole + ogb * B.D;
+    const bool aw = a.has_whole != 0, bw = b.has_whole != 0;
+    for (int i = tid; i < B.D; i += blockDim.x) {
+      float x = ra[i];
+      if (aw) x += raw[i];
+      x += rb[i];
+      if (bw) x += rbw[i];
+      ra[i] = x;
+    }
     __syncthreads();
     // views: a's and b's in one list, fragments, stable by kappa desc, top-k (objprob.cpp:382-385)
     __shared__ int vsrc[2 * SMG_TOPK_MAX + 2], vphys[2 * SMG_TOPK_MAX + 2], dstp[2 * SMG_TOPK_MAX + 2], nkeep;
@@ -299,10 +309,13 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
     }
     __syncthreads();
     if (tid == 0) {
-      for (int v = 0; v < nkeep; ++v) { a.view_slot[v] = dstp[v]; a.vkappa[v] = vk[v]; a.vstamp[v] = vs[v]; }
+      for (int v = 0; v < nkeep; ++v) { a.view_slot[v] = dstp[v]; a.vkappa[v] = vk[v]; a.vstamp[v] = vs[v]; a.vwhole[v] = 0; }
       a.n_views = nkeep;
       ++a.ver;
-      a.k_frag += (0.0 + b.k_frag) + 0.0;
+      a.k_frag += (a.k_whole + b.k_frag) + b.k_whole;
+      a.k_whole = 0;
+      a.has_whole = 0;
+      a.nrm_whole = 0;
       a.n_whole = 0;
       a.whole_kappa = 0;
       a.need_whole = 1;

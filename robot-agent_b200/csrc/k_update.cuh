@@ -60,38 +60,38 @@ DEV double first_view(const Batch& B, int m, double x, double y, double range) {
 
 // |r_frag|^2 and the mean direction mu = float(r / |r|) (ApState mu cache, objprob.cpp:228-240),
 // block-wide, after every change of r_frag
-DEV void refresh_nrm(const Batch& B, size_t og, BlockScratch& bs) {
-  const float* r = B.rfrag + og * B.D;
-  double s = 0;
-  for (int i = threadIdx.x; i < B.D; i += blockDim.x) s += (double)r[i] * (double)r[i];
-  s = block_sum_d(s, bs);
-  if (threadIdx.x == 0) B.objs[og].nrm_frag = s;
-  const double nn = sqrt(s);
-  float* mu = B.mu + og * B.D;
-  for (int i = threadIdx.x; i < B.D; i += blockDim.x) mu[i] = s > 0 ? (float)((double)r[i] / nn) : 0.f;
-  __syncthreads();
-}
-
-// refresh_nrm writing |r|^2 into the given (shared) record
+// apCache (objprob.cpp:228-240): |r_frag|^2, |r_whole|^2 and mu = the whole vector's direction
+// when the object has whole-view weight (k_whole > 0), else the fragment sum's.  Block-wide;
+// the norms go to record `o` (a staged copy or the object itself).
 DEV void refresh_nrm_into(const Batch& B, ObjRec& o, size_t og, BlockScratch& bs) {
-  const float* r = B.rfrag + og * B.D;
-  double s = 0;
-  for (int i = threadIdx.x; i < B.D; i += blockDim.x) s += (double)r[i] * (double)r[i];
+  const float* rf = B.rfrag + og * B.D;
+  const float* rw = B.rwhole + og * B.D;
+  const bool hw = o.has_whole != 0;
+  double s = 0, sw = 0;
+  for (int i = threadIdx.x; i < B.D; i += blockDim.x) {
+    s += (double)rf[i] * (double)rf[i];
+    if (hw) sw += (double)rw[i] * (double)rw[i];
+  }
   s = block_sum_d(s, bs);
-  if (threadIdx.x == 0) o.nrm_frag = s;
-  const double nn = sqrt(s);
+  sw = hw ? block_sum_d(sw, bs) : 0.0;
+  const bool use_w = o.k_whole > 0;
+  __syncthreads();
+  if (threadIdx.x == 0) { o.nrm_frag = s; o.nrm_whole = sw; }
+  const float* r = use_w ? rw : rf;
+  const double n2 = use_w ? sw : s, nn = sqrt(n2);
   float* mu = B.mu + og * B.D;
-  for (int i = threadIdx.x; i < B.D; i += blockDim.x) mu[i] = s > 0 ? (float)((double)r[i] / nn) : 0.f;
+  for (int i = threadIdx.x; i < B.D; i += blockDim.x) mu[i] = n2 > 0 ? (float)((double)r[i] / nn) : 0.f;
   __syncthreads();
 }
+DEV void refresh_nrm(const Batch& B, size_t og, BlockScratch& bs) { refresh_nrm_into(B, B.objs[og], og, bs); }
 
-// apAddView (scenemap objprob.cpp:312-356) for a detection fragment (whole = false), no text
-// model: the scalar part, run by one thread -- view tempering against the camera ring
+// apAddView (scenemap objprob.cpp:312-356), no text model: the scalar part, run by one thread -- view tempering against the camera ring
 // (similar view at another stamp: kappa * temper), the ring of the newest 32 cameras, ver and
 // k_frag, the physical view slot the fp16 copy goes to and the view list kept sorted by kappa
 // (stable, top-k).  The D-length part (r_frag += k z, the fp16 copy, |r|^2, mu) is recorded as
 // a job for k_update_vec.
-DEV void ap_add_view_plan(const Batch& B, ObjRec& o, double kappa, double stamp, const double cam[6], double* k_out, int* phys_out) {
+DEV void ap_add_view_plan(const Batch& B, ObjRec& o, double kappa, double stamp, const double cam[6], double* k_out, int* phys_out,
+                          bool whole = false) {
   double k = kappa;
   const double cmin = B.cos_temper;
   const double td = B.p.temper_d, td2 = td * td;
@@ -112,25 +112,35 @@ DEV void ap_add_view_plan(const Batch& B, ObjRec& o, double kappa, double stamp,
     cam_push(o, c7);
   }
   ++o.ver;
-  o.k_frag += k;
+  if (whole) {
+    o.k_whole += k;
+    ++o.n_whole;
+    o.whole_kappa = smax(o.whole_kappa, kappa);
+    o.need_whole = 0;
+  } else {
+    o.k_frag += k;
+  }
   // free physical view slot: the one of 0..topk not referenced by the current views
   int used = 0;
   for (int v = 0; v < o.n_views; ++v) if (INB(o.view_slot[v], B.topk + 1, 301)) used |= 1 << o.view_slot[v];
   int f = 0;
   while (used & (1 << f)) ++f;
-  // stable sort by (whole desc, kappa desc): every view is a fragment, so insert after the
-  // views whose kappa is >= the new one, then keep the top-k
+  // stable sort by (whole desc, kappa desc): the new view goes after every view that is whole
+  // while it is not, or of its own kind with a kappa >= its own; then keep the top-k
   const float kv = (float)kappa;
+  const int wv = whole ? 1 : 0;
   int pos = o.n_views;
-  while (pos > 0 && o.vkappa[pos - 1] < kv) --pos;
+  while (pos > 0 && (o.vwhole[pos - 1] < wv || (o.vwhole[pos - 1] == wv && o.vkappa[pos - 1] < kv))) --pos;
   for (int v = o.n_views; v > pos; --v) {
     o.view_slot[v] = o.view_slot[v - 1];
     o.vkappa[v] = o.vkappa[v - 1];
     o.vstamp[v] = o.vstamp[v - 1];
+    o.vwhole[v] = o.vwhole[v - 1];
   }
   o.view_slot[pos] = f;
   o.vkappa[pos] = kv;
   o.vstamp[pos] = stamp;
+  o.vwhole[pos] = wv;
   ++o.n_views;
   if (o.n_views > B.topk) o.n_views = B.topk;
   *k_out = k;

@@ -81,6 +81,13 @@ struct smg_batch {
   unsigned char* d_emb = nullptr;
   uint16_t* d_depth_mm = nullptr;  // staging of host millimetre depth
   uint32_t* d_mask = nullptr;      // staging of host detector bit masks: M x max_det x mask_words_max
+  // whole-view answers (smg_set_object_embeddings): staging of up to M * RE_CAND entries, and the
+  // stamp of every map's last keyframe (the stamp the reference gives the whole views)
+  int32_t* d_wv_map = nullptr;
+  uint32_t* d_wv_id = nullptr;
+  float* d_wv_emb = nullptr;
+  double* d_wv_stamp = nullptr;
+  std::vector<double> last_stamp;
   size_t mask_words_max = 0;       // ceil(max_w * max_h / 32)
   std::vector<double> last_cam_t, last_cam_fwd;
   // updateHands' per-hand gripper state of every map (ObjectMap::closed_, gref_, gref_t_, tried_;
@@ -468,6 +475,12 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
   DA(b->d_label, (size_t)M * max_w * max_h);
   DA(b->d_emb, (size_t)M * max_det * D * 4);
   DA(b->d_depth_mm, (size_t)M * max_w * max_h);
+  DA(b->d_wv_map, (size_t)M * RE_CAND);
+  DA(b->d_wv_id, (size_t)M * RE_CAND);
+  DA(b->d_wv_emb, (size_t)M * RE_CAND * D);
+  DA(b->d_wv_stamp, M);
+  DA(B.rwhole, MO * D);
+  b->last_stamp.assign(M, 0.0);
   b->mask_words_max = ((size_t)max_w * max_h + 31) / 32;
   DA(b->d_mask, (size_t)M * max_det * b->mask_words_max);
   // host-side initial state
@@ -752,6 +765,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     const smg_frame& f = frames[m];
     d.active = 1;
     d.stamp = f.stamp;
+    b->last_stamp[m] = f.stamp;
     d.w = f.w;
     d.h = f.h;
     d.fx = f.fx; d.fy = f.fy; d.cx = f.cx; d.cy = f.cy;
@@ -1080,6 +1094,8 @@ int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap) {
     r.need_whole = o.need_whole;
     r.n_cams = o.n_cams;
     r.geo = o.geo;
+    r.k_whole = o.k_whole;
+    r.n_whole = o.n_whole;
     r.held_by = o.held_by;
     r.parent = o.parent;
     for (int k = 0; k < 3; ++k) r.parent_rel[k] = o.parent_rel[k];
@@ -1107,6 +1123,25 @@ int smg_get_object_vectors(smg_batch* b, int m, int i, float* r_frag, uint16_t* 
     if (vstamp) vstamp[v] = o.vstamp[v];
   }
   return nv;
+}
+
+int smg_get_object_whole(smg_batch* b, int m, int i, float* r_whole, double* k_whole) {
+  if (!b || m < 0 || m >= b->B.M || i < 0) return fail(SMG_ERR_ARGS, "smg_get_object_whole: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  if (i >= R.n_obj) return fail(SMG_ERR_ARGS, "smg_get_object_whole: no such object");
+  int32_t slot;
+  CK(cudaMemcpy(&slot, B.order + (size_t)m * B.O + i, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  ObjRec o;
+  CK(cudaMemcpy(&o, B.objs + (size_t)m * B.O + slot, sizeof(ObjRec), cudaMemcpyDeviceToHost));
+  if (k_whole) *k_whole = o.k_whole;
+  if (r_whole) {
+    if (o.has_whole) CK(cudaMemcpy(r_whole, B.rwhole + ((size_t)m * B.O + slot) * B.D, sizeof(float) * B.D, cudaMemcpyDeviceToHost));
+    else memset(r_whole, 0, sizeof(float) * B.D);
+  }
+  return o.has_whole ? o.n_whole : 0;
 }
 
 int smg_get_object_cloud(smg_batch* b, int m, int i, float* xyz, uint32_t* seq, int cap) {
@@ -1918,6 +1953,93 @@ int smg_plane_fit_noalloc(const float* xyz, const int32_t* off, int n_sets, int 
   k_plane_sets<<<n_sets, PF_THREADS, 0, (cudaStream_t)stream>>>(xyz, off, n_sets, n_points, tau, seeds, max_iters, d.need,
                                                                   d.scratch, out);
   CK(cudaGetLastError());
+  return SMG_OK;
+}
+
+// ObjectMap::addWholeView (objmap.cpp:1361-1369) for the answers of sm_set_object_embeddings
+// (capi.cpp:1825-1835): entry i is applied when map maps[i]'s last keyframe requested object
+// ids[i] and the object still exists, with the request's kappa and camera and the keyframe's
+// stamp.  One CTA per map takes that map's entries in call order.
+__global__ void __launch_bounds__(256) k_whole_views(Batch B, const int32_t* maps, const uint32_t* ids, const float* emb, int n,
+                                                     const double* stamps) {
+  __shared__ BlockScratch bs;
+  __shared__ int s_pos, s_phys, s_zero;
+  __shared__ double s_k;
+  const int m = blockIdx.x, tid = threadIdx.x;
+  MapRec* R = &B.maps[m];
+  const ReencRec* recs = B.reenc + (size_t)m * RE_CAND;
+  for (int i = 0; i < n; ++i) {
+    if (maps[i] != m) continue;
+    if (tid == 0) {
+      s_pos = -1;
+      int req = -1;
+      for (int r = 0; r < R->re_n && r < RE_CAND && req < 0; ++r) {
+        const int j = R->re_rank[r];
+        if (j >= 0 && j < RE_CAND && recs[j].id == ids[i]) req = j;
+      }
+      if (req >= 0)
+        for (int q = 0; q < R->n_obj; ++q)
+          if (obj_at(B, m, q).id == ids[i]) { s_pos = q; break; }
+      if (s_pos >= 0) {
+        ObjRec& o = B.objs[oglob(B, m, slot_at(B, m, s_pos))];
+        double k;
+        int phys;
+        ap_add_view_plan(B, o, (double)recs[req].kappa, stamps[m], recs[req].cam, &k, &phys, true);
+        s_k = k;
+        s_phys = phys;
+        s_zero = !o.has_whole;   // r_whole starts from zeros (objprob.cpp:329)
+        o.has_whole = 1;
+        ++R->st.n_reenc_done;
+      }
+    }
+    __syncthreads();
+    if (s_pos >= 0) {
+      const size_t og = oglob(B, m, slot_at(B, m, s_pos));
+      float* rw = B.rwhole + og * B.D;
+      uint16_t* vz = B.views + (og * (B.topk + 1) + s_phys) * B.D;
+      const float* z = emb + (size_t)i * B.D;
+      for (int q = tid; q < B.D; q += blockDim.x) {
+        rw[q] = (s_zero ? 0.f : rw[q]) + (float)(s_k * (double)z[q]);
+        vz[q] = ref_f2h(z[q]);
+      }
+      __syncthreads();
+      refresh_nrm(B, og, bs);
+    }
+    __syncthreads();
+  }
+}
+
+int smg_set_object_embeddings(smg_batch* b, const int32_t* maps, const uint32_t* ids, const float* emb, int n, int dim, int where,
+                              void* stream) {
+  if (!b || n < 0 || (n > 0 && (!maps || !ids || !emb)) || dim != b->B.D || (size_t)n > (size_t)b->B.M * RE_CAND ||
+      (where != SMG_MEM_DEVICE && where != SMG_MEM_HOST))
+    return fail(SMG_ERR_ARGS, "smg_set_object_embeddings: bad arguments (dim must be the batch's, n <= maps * 64)");
+  if (n == 0) return SMG_OK;
+  CK(cudaSetDevice(b->dev));
+  cudaStream_t st = (cudaStream_t)stream;
+  const Batch& B = b->B;
+  const int32_t* dm = maps;
+  const uint32_t* di = ids;
+  const float* de = emb;
+  if (where == SMG_MEM_HOST) {
+    for (int i = 0; i < n; ++i)
+      if (maps[i] < 0 || maps[i] >= B.M) return fail(SMG_ERR_ARGS, "smg_set_object_embeddings: map index out of range");
+    CK(cudaMemcpyAsync(b->d_wv_map, maps, sizeof(int32_t) * n, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(b->d_wv_id, ids, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(b->d_wv_emb, emb, sizeof(float) * (size_t)n * B.D, cudaMemcpyHostToDevice, st));
+    dm = b->d_wv_map;
+    di = b->d_wv_id;
+    de = b->d_wv_emb;
+  }
+  CK(cudaMemcpyAsync(b->d_wv_stamp, b->last_stamp.data(), sizeof(double) * B.M, cudaMemcpyHostToDevice, st));
+  // after the keyframe that made the requests (all stream groups have joined on ev_done)
+  CK(cudaStreamWaitEvent(st, b->ev_done, 0));
+  k_whole_views<<<B.M, 256, 0, st>>>(B, dm, di, de, n, b->d_wv_stamp);
+  b->launches += 1;
+  CK(cudaGetLastError());
+  CK(cudaEventRecord(b->ev_done, st));   // later pushes (and the staging) wait for the answers
+  b->last_stream = st;
+  if (where == SMG_MEM_HOST) CK(cudaStreamSynchronize(st));   // the host arrays may go away after the call
   return SMG_OK;
 }
 

@@ -139,6 +139,11 @@ typedef struct __align__(16) {   // 16-byte aligned: staged in shared memory in 
   uint32_t geo_ver;
   int32_t geo, drop, hide;
   double nrm_frag;       // |r_frag|^2 (ApState::nrm_frag, refreshed whenever r_frag changes)
+  // whole-object views (ApState r_whole / k_whole / nrm_whole, objprob.hpp:158-169): has_whole = 1
+  // once r_whole holds a vector (until a merge folds it into r_frag); vwhole[v] marks whole views
+  double k_whole, nrm_whole;
+  int32_t has_whole;
+  int32_t vwhole[SMG_TOPK_MAX + 1];
   // hands (MapObject, objmap.hpp:175-178)
   int32_t held_by;       // hand holding it, -1 = none
   uint32_t parent;       // id of the object it rests on and follows, 0 = none
@@ -282,7 +287,8 @@ typedef struct {
   int32_t* cfreel;       // [M*C] free cloud-slot stack
   AssocRec* assoc;       // [M*max_det]
   float* rfrag;          // [M*O*D]
-  float* mu;             // [M*O*D] float(r_frag / |r_frag|) (ApState mu_c), refreshed with r_frag
+  float* mu;             // [M*O*D] ApState mu_c: float(r / |r|) of r_whole when k_whole > 0, else of r_frag
+  float* rwhole;         // [M*O*D] ApState::r_whole
   uint16_t* views;       // [M*O*(topk+1)*D]
   CloudRec* clouds;      // [M*C]
   float4* cpts;          // [M*C*cap]

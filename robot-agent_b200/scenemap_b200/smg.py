@@ -46,7 +46,8 @@ class SmgObject(C.Structure):
                 ("max_det_z", C.c_double), ("last_kf", C.c_double), ("appeared", C.c_int32), ("cloud_n", C.c_int32),
                 ("cloud_version", C.c_uint32), ("cloud_org", C.c_double * 3), ("ap_ver", C.c_uint32),
                 ("k_frag", C.c_double), ("n_views", C.c_int32), ("n_ap_obs", C.c_int32), ("need_whole", C.c_int32),
-                ("P", C.c_double * 3), ("n_cams", C.c_int32), ("geo", C.c_int32), ("held_by", C.c_int32),
+                ("P", C.c_double * 3), ("n_cams", C.c_int32), ("geo", C.c_int32), ("k_whole", C.c_double),
+                ("n_whole", C.c_int32), ("held_by", C.c_int32),
                 ("parent", C.c_uint32), ("parent_rel", C.c_double * 3)]
 
 
@@ -87,6 +88,8 @@ def lib():
         L.smg_kernel_launches.argtypes = [vp]
         L.smg_get_work.argtypes = [vp, C.POINTER(C.c_int64), C.c_int]
         L.smg_set_reencode.argtypes = [vp, C.c_int]
+        L.smg_set_object_embeddings.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, vp]
+        L.smg_get_object_whole.argtypes = [vp, C.c_int, C.c_int, vp, P(C.c_double)]
         L.smg_plane_fit.argtypes = [vp, vp, C.c_int, C.c_int, C.c_double, vp, C.c_int, vp, vp]
         L.smg_plane_fit_noalloc.argtypes = [vp, vp, C.c_int, C.c_int, C.c_double, vp, C.c_int, vp, vp]
         _lib = L
@@ -97,7 +100,7 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
             "smg_get_objects", "smg_get_object_vectors", "smg_get_object_cloud", "smg_get_assoc", "smg_get_stats",
             "smg_get_events", "smg_get_grid", "smg_get_keyframe", "smg_error_word", "smg_last_error",
             "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
-           "smg_get_work", "smg_set_reencode", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
+           "smg_get_work", "smg_set_reencode", "smg_set_object_embeddings", "smg_get_object_whole", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
            "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode"]
 
@@ -312,6 +315,20 @@ class Batch:
         out = np.zeros(self.n_maps * self.max_det, np.uint32)
         _check(lib().smg_get_assoc_all(self.h, _ptr(out)), "smg_get_assoc_all")
         return out.reshape(self.n_maps, self.max_det)
+
+    def set_object_embeddings(self, maps, ids, emb, stream: int = 0):
+        """Whole-object embeddings answering the last keyframe's re-encode requests (host arrays)."""
+        maps = np.ascontiguousarray(maps, np.int32)
+        ids = np.ascontiguousarray(ids, np.uint32)
+        emb = np.ascontiguousarray(emb, np.float32).reshape(len(ids), self.D)
+        _check(lib().smg_set_object_embeddings(self.h, _ptr(maps), _ptr(ids), _ptr(emb), len(ids), self.D, SMG_MEM_HOST,
+                                                C.c_void_p(stream)), "smg_set_object_embeddings")
+
+    def object_whole(self, m: int, i: int):
+        r = np.zeros(self.D, np.float32)
+        k = C.c_double(0)
+        n = _check(lib().smg_get_object_whole(self.h, m, i, _ptr(r), C.byref(k)), "smg_get_object_whole")
+        return r, k.value, n
 
     def set_reencode(self, on: bool):
         _check(lib().smg_set_reencode(self.h, 1 if on else 0), "smg_set_reencode")

@@ -4,9 +4,10 @@ from __future__ import annotations
 import numpy as np
 
 EXACT_FIELDS = ["id", "cls", "n_obs", "state", "confirmed", "moved", "misses", "n_vis_miss", "appeared", "cloud_n",
-                "cloud_version", "ap_ver", "n_views", "n_ap_obs", "need_whole", "n_cams", "geo", "held_by", "parent"]
+                "cloud_version", "ap_ver", "n_views", "n_ap_obs", "need_whole", "n_cams", "geo", "held_by", "parent",
+                "n_whole"]
 FLOAT_FIELDS = ["pos", "ext", "first_pos", "lo", "hi", "first_seen", "last_seen", "max_det_z", "last_kf", "k_frag",
-                "P", "cloud_org", "parent_rel"]
+                "P", "cloud_org", "parent_rel", "k_whole"]
 
 
 def compare_objects(ref_objs: list, gpu_objs: list, rel: float = 1e-5) -> list:
@@ -97,6 +98,10 @@ def compare_frame(ref, gpu, m: int, D: int, deep: bool = False) -> list:
                 errs.append(f"obj[{i}] r_frag max diff {np.abs(r1 - r2).max()}")
             if not (np.array_equal(v1, v2) and np.array_equal(k1, k2) and np.array_equal(s1, s2)):
                 errs.append(f"obj[{i}] views differ")
+            w1, kw1, nw1 = ref.object_whole(i, D)
+            w2, kw2, nw2 = gpu.object_whole(m, i)
+            if not (np.array_equal(w1, w2) and kw1 == kw2 and nw1 == nw2):
+                errs.append(f"obj[{i}] r_whole differs (n_whole {nw1} vs {nw2})")
             c1, q1 = ref.object_cloud(i)
             c2, q2 = gpu.object_cloud(m, i)
             if not (np.array_equal(c1, c2) and np.array_equal(q1, q2)):
