@@ -253,8 +253,9 @@ def run_b200(args, rank, world, local_rank):
     sp = stream.cuda_stream
     f = 0
     # untimed pre-roll + warm-up
+    chunk = max(1, min(16, int(4e9 // (M * W * H * 6))))   # rendered frames held at once: <= ~4 GB
     while f < args.preroll + args.warmup:
-        nf = min(16, args.preroll + args.warmup - f)
+        nf = min(chunk, args.preroll + args.warmup - f)
         R = wl.render(f, nf, sp)
         for fi in range(nf):
             keep = []
