@@ -279,6 +279,10 @@ int smg_timing_read(smg_batch* b, double* ms, int64_t* n, const char** names);
 /* First failed self-check of a -DSMG_CHECKS build: (site, index, bound); all zero when none
  * (always zero in the production build). */
 int smg_debug_check(smg_batch* b, uint64_t* out3);
+/* Instrumentation builds (-DSMG_PHASE_TIMING) only: per-phase clock cycles of the chain's
+ * largest kernels (thread 0 of every block), out[2k] cycles and out[2k+1] marks for k < 64,
+ * then reset.  The production build returns SMG_ERR_UNSUPPORTED. */
+int smg_phase_read(uint64_t* out);
 /* Device error word (0 = none) and a static description of the last host-side error. */
 int smg_error_word(smg_batch* b);
 const char* smg_last_error(void);

@@ -547,6 +547,26 @@ DEV double dist3(const double* a, const double* b) {
 
 DEV void set_err(MapRec* m, int bit) { atomicOr(&m->err, bit); }
 
+// Phase timing (instrumentation builds only, -DSMG_PHASE_TIMING): thread 0 of a block adds the
+// clock cycles since its previous mark to phase slot i (smg_phase_read).  No-ops otherwise.
+#ifdef SMG_PHASE_TIMING
+__device__ unsigned long long g_phase_cycles[64];
+__device__ unsigned long long g_phase_hits[64];
+#define PHASE_START() long long phase_t_ = clock64()
+#define PHASE_MARK(i)                                                              \
+  do {                                                                             \
+    if (threadIdx.x == 0) {                                                        \
+      const long long n_ = clock64();                                              \
+      atomicAdd(&g_phase_cycles[(i)], (unsigned long long)(n_ - phase_t_));        \
+      atomicAdd(&g_phase_hits[(i)], 1ull);                                         \
+      phase_t_ = n_;                                                               \
+    }                                                                              \
+  } while (0)
+#else
+#define PHASE_START() do { } while (0)
+#define PHASE_MARK(i) do { } while (0)
+#endif
+
 // global index of cloud slot `slot` of map m (clouds are a pool of B.C slots per map, separate
 // from the B.O object slots)
 __host__ __device__ inline size_t cglob(const Batch& B, int m, int slot) { return (size_t)m * B.C + slot; }

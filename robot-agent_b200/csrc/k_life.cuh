@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
     }
     __syncthreads();
     plane_fit(Pt, n, P.obj_tau, ap_seed((uint64_t)o.id, (uint64_t)C.version), P.ransac_iters, B.need_tab, scr, 4096, &ps, bs,
-              &pout);
+              &pout, 12);
     int up = 0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) up += (double)Pt[3 * i + 2] > R.ceil_est - P.ceil_band;
     up = block_sum_i(up, bs);

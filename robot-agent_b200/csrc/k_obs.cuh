@@ -132,7 +132,8 @@ DEV int pct_index(int n, double q) {   // min(n-1, size_t(q*(n-1) + 0.5)) (objma
 // draws, same adaptive stop; the stop count comes from a host-libm table).  Inlier sums are
 // block reductions (deterministic tree).  span1/span2 are not produced (no caller reads them).
 DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_iters, const int32_t* need_tab, double* scr, int cap,
-                   PlaneSmem* ps, BlockScratch& bs, PlaneOut* out) {
+                   PlaneSmem* ps, BlockScratch& bs, PlaneOut* out, int pbase = 8) {
+  PHASE_START();
   __shared__ double sh_best[4];
   __shared__ int sh_bestc;
   __shared__ double sh_m[3], sh_V[3][3], sh_ev[3];
@@ -268,6 +269,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     __syncthreads();
     return;
   }
+  PHASE_MARK(pbase + 0);   // RANSAC
   // two PCA refits (objprob.cpp:166-180); mp = plane whose inliers the last pass used.
   // Sums are block trees.  Where the outcome is ill-conditioned in the reference's own rounding
   // (a point within 1e-11 of the tau boundary, a near-double smallest eigenvalue, a nearly
@@ -411,6 +413,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     return;
   }
   const double m0 = sh_m[0], m1 = sh_m[1], hc = th_hc, hs = th_hs;
+  PHASE_MARK(pbase + 1);   // PCA refits
   // z and horizontal-span projections of the inliers -> exact percentiles (objprob.cpp:193-206)
   __shared__ int sh_cnt;
   if (tid == 0) sh_cnt = 0;
@@ -446,6 +449,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     out->zmed = zmd;
   }
   __syncthreads();
+  PHASE_MARK(pbase + 2);   // percentiles
 }
 
 // subsample (objmap.cpp:37-42) of v[0..n) into S (<= SMG_SUB values); returns its size.
@@ -521,6 +525,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     return;
   }
   if (tid == 0) { wk_add(&B.maps[m], SMG_WK_OBS_PX, npix); wk_add(&B.maps[m], SMG_WK_DET, 1); }
+  PHASE_START();
   const double* T = F.T_mc;
   __shared__ int scan_db[2][33];
   int scan_it = 0;
@@ -587,6 +592,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     return;
   }
   __syncthreads();
+  PHASE_MARK(0);   // back-projection
   // 2. MAD depth band (objmap.cpp:692-695)
   int nS = subsample_to(ZC, n, S);
   __syncthreads();
@@ -597,6 +603,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   const double mad = block_select(S, nS, kmed, hist, bs);
   const double band = smax(P.mad_k * 1.4826 * mad, P.mad_floor);
   __syncthreads();
+  PHASE_MARK(1);   // MAD band
   // 3. band filter, hand count, first point per voxel (objmap.cpp:696-719)
   for (int i = tid; i < OBS_HASH; i += blockDim.x) { hkey[i] = ~0ull; hidx[i] = 0xffffffffu; }
   __syncthreads();
@@ -661,6 +668,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     return;
   }
   __syncthreads();
+  PHASE_MARK(2);   // band filter + voxels
   // 4. 10/50/90 percentiles per axis (objmap.cpp:730-738): nine order statistics, one sweep
   double lo[3], md[3], hi[3];
   {
@@ -706,6 +714,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     if (tid == 0) { O->valid = 0; O->stage = 3; }
     return;
   }
+  PHASE_MARK(3);   // percentiles
   // 5. plane fit of the cloud candidates (apObsStructural, objmap.cpp:565-575)
   double c0s = 0, c1s = 0, c2s = 0;
   for (int i = tid; i < nc && INB(3 * i + 2, 3 * B.pmax, 115); i += blockDim.x) { c0s += CX[3 * i]; c1s += CX[3 * i + 1]; c2s += CX[3 * i + 2]; }
@@ -723,11 +732,13 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
       __syncthreads();
       PX = PXs;
     }
+    PHASE_MARK(4);   // plane-fit set-up
     plane_fit(PX, nc, tau, ap_seed(sb, (uint64_t)k), P.ransac_iters, B.need_tab, SCR, B.pmax, ps, bs, &pout);
   } else if (tid == 0) {
     pout.ok = 0;
   }
   __syncthreads();
+  PHASE_MARK(5);
   if (tid == 0) {
     O->pl_ok = pout.ok;
     for (int a = 0; a < 3; ++a) O->pl_n[a] = pout.n[a];

@@ -23,13 +23,25 @@
 // ranks the candidates: priority descending, list order on equal priority (the reference's
 // std::sort leaves the order of equal priorities unspecified).
 #pragma once
-#include "dev_util.cuh"
+#include "k_cloud.cuh"
 
 #define RE_THREADS 256
 #define RE_CTAS 16      // CTAs per map (a keyframe has about one candidate per detection)
 #define RE_ZMAX 6000    // sampled points per object: ceil(n / max(1, n / 3000)) < 6000 for every n
 // dynamic shared memory: the row-padded mask of the largest frame plus the visible depths
 #define RE_SMEM(B) ((size_t)(B).H * ((((B).W) + 31) >> 5) * 4 + (size_t)RE_ZMAX * 4)
+
+#define RE_PF 4        // points a thread projects at once (their loads in flight together)
+
+// x / s with exact shortcuts: s == 1 (mode 0: x), s a power of two (mode 1: x * (1 / s), which
+// rounds the same), otherwise a division (mode 2)
+DEV int re_scale_mode(double s, double* inv) {
+  int e;
+  const double f = frexp(s, &e);
+  *inv = 1.0 / s;
+  return s == 1.0 ? 0 : (f == 0.5 ? 1 : 2);
+}
+DEV double re_scale(double x, double s, double inv, int mode) { return mode == 0 ? x : (mode == 1 ? x * inv : x / s); }
 
 // order-preserving unsigned keys of floats
 DEV uint32_t f_ord(float x) {
@@ -119,11 +131,12 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
   extern __shared__ __align__(16) unsigned char re_smem[];
   __shared__ BlockScratch bs;
   __shared__ int s_cand[RE_CAND];
-  __shared__ int s_vis, s_last;
+  __shared__ int s_vis, s_last, s_nrec;
   __shared__ int s_hist[256], s_pick[2];
   const int m = B.map0 + blockIdx.y, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
+  PHASE_START();
   MapRec* R = &B.maps[m];
   if (!(F.emb != nullptr && F.n_det > 0)) {   // not an objprob keyframe: no requests
     if (blockIdx.x == 0 && tid == 0) R->re_n = 0;
@@ -136,6 +149,12 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
   const int mw = F.mask_w, mh = F.mask_h, img_w = F.img_w, img_h = F.img_h;
   const double msx = F.mask_sx, msy = F.mask_sy, mox = F.mask_ox, moy = F.mask_oy;
   const double sxu = F.sxu_d, syv = F.syv_d;
+  double sxu_inv, syv_inv, msx_inv, msy_inv;
+  const int sxu_mode = re_scale_mode(sxu, &sxu_inv), syv_mode = re_scale_mode(syv, &syv_inv);
+  const int msx_mode = re_scale_mode(msx, &msx_inv), msy_mode = re_scale_mode(msy, &msy_inv);
+  // footprint records of the candidate being projected: the CTA's cloud-add work area, free
+  // once the keyframe's cloud additions are done (RE_CTAS <= WORK_SLOTS)
+  uint2* recs_w = (uint2*)work_at(B, m, blockIdx.x).keys;
   const int wpr = (mw + 31) >> 5, nwords = mh * wpr;
   const int step = max(1, (int)llround(F.w / 160.0)), stp_mv = max(1, F.w / 32);
   uint32_t* g = (uint32_t*)re_smem;
@@ -161,6 +180,7 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
   int host_reads = 0;
   for (int i = tid; i < nwords; i += blockDim.x) g[i] = 0u;   // later candidates clear their window
   __syncthreads();
+  PHASE_MARK(16);   // candidates + mask clear
   for (int q = 0; (int)blockIdx.x + q * (int)gridDim.x < nc; ++q) {
     const int j = blockIdx.x + q * gridDim.x;
     const int b = s_cand[q];
@@ -171,56 +191,109 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
     const int n = C.n;
     const int stp = max(1, n / 3000);
     const int tot = (n + stp - 1) / stp;
-    if (tid == 0) s_vis = 0;
+    if (tid == 0) { s_vis = 0; s_nrec = 0; }
     __syncthreads();
     double u0 = 1e9, v0 = 1e9, u1 = -1e9, v1 = -1e9;
     int trunc = 0;
     int pi0 = INT_MAX, pi1 = -1, pj0 = INT_MAX, pj1 = -1;   // painted cells of this thread
-    // each thread takes a run of consecutive points: neighbouring cloud points paint the same
-    // words, which the thread then finds painted already, and the lanes of a warp work on
-    // distant parts of the cloud instead of contending for one word
-    const int per = (tot + (int)blockDim.x - 1) / (int)blockDim.x;
-    for (int s = tid * per, s_end = min(tot, s + per); s < s_end; ++s) {
-      if (!INB((size_t)s * stp, n, 801)) continue;
-      const float4 pt = pts[(size_t)s * stp];
-      const double p0 = C.org[0] + (double)pt.x - T[3], p1 = C.org[1] + (double)pt.y - T[7],
-                   p2 = C.org[2] + (double)pt.z - T[11];
-      const double cx = T[0] * p0 + T[4] * p1 + T[8] * p2, cy = T[1] * p0 + T[5] * p1 + T[9] * p2,
-                   cz = T[2] * p0 + T[6] * p1 + T[10] * p2;
-      if (cz < 0.15) continue;
-      const double ud = (double)F.fx * cx / cz + (double)F.cx, vd = (double)F.fy * cy / cz + (double)F.cy;
-      if (ud < 0 || vd < 0 || ud >= F.w || vd >= F.h) { trunc = 1; continue; }
-      const float d = reenc_depth(F, (int)ud, (int)vd, step, stp_mv, host_reads);
-      if (!(d > 0) || d < cz - 0.08) continue;
-      {   // append the depth: one shared-memory atomic per warp
-        const unsigned am = __activemask();
-        const int lane = tid & 31, lead = __ffs(am) - 1;
-        int zb = 0;
-        if (lane == lead) zb = atomicAdd(&s_vis, __popc(am));
-        const int zi = __shfl_sync(am, zb, lead) + __popc(am & ((1u << lane) - 1u));
-        if (INB(zi, RE_ZMAX, 802)) zs[zi] = (float)cz;
+    // 1. projection and visibility: thread t takes points t, t + blockDim.x, ... (independent
+    //    loads, RE_PF in flight per thread); a visible point appends its depth and, when its
+    //    footprint meets the mask grid, the footprint's cell rectangle to the CTA's record list
+    for (int base = 0; base < tot; base += RE_PF * (int)blockDim.x) {   // the same trip count for every thread
+      float4 pt[RE_PF];
+#pragma unroll
+      for (int u = 0; u < RE_PF; ++u) {
+        const int s = base + u * (int)blockDim.x + tid;
+        pt[u] = s < tot && INB((size_t)s * stp, n, 801) ? pts[(size_t)s * stp] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      // depth pixel -> detector pixel -> mask cells, painted over the voxel's footprint
-      // (objmap.cpp:1403-1410; for the label-image form the scales are 1 and the offsets 0)
-      const double ui = ud / sxu, vi = vd / syv;
-      const double rpx = 0.6 * P.voxel * (double)F.fx / cz / sxu;
-      const int i0 = (int)floor((ui - rpx - mox) / msx), i1 = (int)floor((ui + rpx - mox) / msx);
-      const int j0 = (int)floor((vi - rpx - moy) / msy), j1 = (int)floor((vi + rpx - moy) / msy);
-      const int ia = max(0, i0), ib = min(mw - 1, i1), ja = max(0, j0), jb = min(mh - 1, j1);
-      if (ia <= ib && ja <= jb) { pi0 = min(pi0, ia); pi1 = max(pi1, ib); pj0 = min(pj0, ja); pj1 = max(pj1, jb); }
-      for (int jj = ja; jj <= jb; ++jj) {
-        uint32_t* row = g + (size_t)jj * wpr;
-        for (int u = ia; u <= ib;) {
-          const int w = u >> 5, e = min(ib, (w << 5) + 31);
-          const uint32_t bits = (e - u == 31) ? 0xffffffffu : (((1u << (e - u + 1)) - 1u) << (u & 31));
-          if ((row[w] & bits) != bits) atomicOr(&row[w], bits);
-          u = e + 1;
+      double czv[RE_PF], udv[RE_PF], vdv[RE_PF];
+      float dv[RE_PF];
+      bool in[RE_PF];
+#pragma unroll
+      for (int u = 0; u < RE_PF; ++u) {
+        const int s = base + u * (int)blockDim.x + tid;
+        const double p0 = C.org[0] + (double)pt[u].x - T[3], p1 = C.org[1] + (double)pt[u].y - T[7],
+                     p2 = C.org[2] + (double)pt[u].z - T[11];
+        const double cx = T[0] * p0 + T[4] * p1 + T[8] * p2, cy = T[1] * p0 + T[5] * p1 + T[9] * p2,
+                     cz = T[2] * p0 + T[6] * p1 + T[10] * p2;
+        czv[u] = cz;
+        in[u] = s < tot && !(cz < 0.15);
+        udv[u] = vdv[u] = 0;
+        if (in[u]) {
+          udv[u] = (double)F.fx * cx / cz + (double)F.cx;
+          vdv[u] = (double)F.fy * cy / cz + (double)F.cy;
+          if (udv[u] < 0 || vdv[u] < 0 || udv[u] >= F.w || vdv[u] >= F.h) { trunc = 1; in[u] = false; }
         }
       }
-      u0 = fmin(u0, ui); u1 = fmax(u1, ui); v0 = fmin(v0, vi); v1 = fmax(v1, vi);
-      if (ui <= 2 || vi <= 2 || ui >= img_w - 3 || vi >= img_h - 3) trunc = 1;
+#pragma unroll
+      for (int u = 0; u < RE_PF; ++u) dv[u] = in[u] ? reenc_depth(F, (int)udv[u], (int)vdv[u], step, stp_mv, host_reads) : 0.f;
+#pragma unroll
+      for (int u = 0; u < RE_PF; ++u) {
+        const double cz = czv[u];
+        const bool vis = in[u] && !(!(dv[u] > 0) || dv[u] < cz - 0.08);
+        // depth pixel -> detector pixel -> mask cells over the voxel's footprint
+        // (objmap.cpp:1403-1410; divisions by the scales, exact shortcuts for 1 and powers of 2)
+        uint2 rec = make_uint2(0u, 0u);
+        bool paint = false;
+        if (vis) {
+          const double ui = re_scale(udv[u], sxu, sxu_inv, sxu_mode), vi = re_scale(vdv[u], syv, syv_inv, syv_mode);
+          const double rpx = re_scale(0.6 * P.voxel * (double)F.fx / cz, sxu, sxu_inv, sxu_mode);
+          const int i0 = (int)floor(re_scale(ui - rpx - mox, msx, msx_inv, msx_mode));
+          const int i1 = (int)floor(re_scale(ui + rpx - mox, msx, msx_inv, msx_mode));
+          const int j0 = (int)floor(re_scale(vi - rpx - moy, msy, msy_inv, msy_mode));
+          const int j1 = (int)floor(re_scale(vi + rpx - moy, msy, msy_inv, msy_mode));
+          const int ia = max(0, i0), ib = min(mw - 1, i1), ja = max(0, j0), jb = min(mh - 1, j1);
+          if (ia <= ib && ja <= jb) {
+            pi0 = min(pi0, ia); pi1 = max(pi1, ib); pj0 = min(pj0, ja); pj1 = max(pj1, jb);
+            rec = make_uint2((uint32_t)ia | (uint32_t)ib << 16, (uint32_t)ja | (uint32_t)jb << 16);
+            paint = true;
+          }
+          u0 = fmin(u0, ui); u1 = fmax(u1, ui); v0 = fmin(v0, vi); v1 = fmax(v1, vi);
+          if (ui <= 2 || vi <= 2 || ui >= img_w - 3 || vi >= img_h - 3) trunc = 1;
+        }
+        // append the depth and the footprint: one shared-memory atomic per warp each
+        const unsigned bv = __ballot_sync(0xffffffffu, vis), bp = __ballot_sync(0xffffffffu, paint);
+        const int lane = tid & 31;
+        int zb = 0, rb = 0;
+        if (lane == 0) {
+          if (bv) zb = atomicAdd(&s_vis, __popc(bv));
+          if (bp) rb = atomicAdd(&s_nrec, __popc(bp));
+        }
+        zb = __shfl_sync(0xffffffffu, zb, 0);
+        rb = __shfl_sync(0xffffffffu, rb, 0);
+        if (vis) {
+          const int zi = zb + __popc(bv & ((1u << lane) - 1u));
+          if (INB(zi, RE_ZMAX, 802)) zs[zi] = (float)cz;
+        }
+        if (paint) {
+          const int ri = rb + __popc(bp & ((1u << lane) - 1u));
+          if (INB(ri, RE_ZMAX, 804)) recs_w[ri] = rec;
+        }
+      }
+    }
+    __syncthreads();
+    // 2. paint the footprints: thread t takes a run of consecutive records (points that are
+    //    neighbours in the cloud paint the same words, which the thread then finds painted, and
+    //    the lanes of a warp work on distant parts instead of contending for one word)
+    {
+      const int nrec = min(s_nrec, RE_ZMAX);
+      const int per = (nrec + (int)blockDim.x - 1) / (int)blockDim.x;
+      for (int r = tid * per, r_end = min(nrec, r + per); r < r_end; ++r) {
+        const uint2 rec = recs_w[r];
+        const int ia = (int)(rec.x & 0xffffu), ib = (int)(rec.x >> 16), ja = (int)(rec.y & 0xffffu), jb = (int)(rec.y >> 16);
+        for (int jj = ja; jj <= jb; ++jj) {
+          uint32_t* row = g + (size_t)jj * wpr;
+          for (int u = ia; u <= ib;) {
+            const int w = u >> 5, e = min(ib, (w << 5) + 31);
+            const uint32_t bits = (e - u == 31) ? 0xffffffffu : (((1u << (e - u + 1)) - 1u) << (u & 31));
+            if ((row[w] & bits) != bits) atomicOr(&row[w], bits);
+            u = e + 1;
+          }
+        }
+      }
     }
     trunc = __syncthreads_or(trunc);
+    PHASE_MARK(17);   // projection + paint
     const int vis = s_vis;
     u0 = block_min_d(u0, bs); u1 = block_max_d(u1, bs);
     v0 = block_min_d(v0, bs); v1 = block_max_d(v1, bs);
@@ -261,8 +334,10 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
       size_px = sqrt((double)area * msx * msy);
       ok = !(size_px < (double)P.reenc_min_px);
     }
+    PHASE_MARK(18);   // windows + closing
     float zmed = 0.f;
     if (ok) zmed = block_select_f(zs, min(vis, RE_ZMAX), vis / 2, s_hist, s_pick);
+    PHASE_MARK(19);   // median
     if (tid == 0) {
       ReencRec rc;
       rc.id = o.id;
@@ -293,6 +368,7 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
     for (int t = tid; t < nwin; t += blockDim.x) g[(size_t)(r0 + t / nww) * wpr + w0 + t % nww] = 0u;   // painted cells lie inside
     __syncthreads();
   }
+  PHASE_MARK(20);   // records + window clears
   host_reads = __reduce_add_sync(0xffffffffu, host_reads);
   if ((tid & 31) == 0 && host_reads) wk_add(R, SMG_WK_H2D, 4LL * host_reads);
 
@@ -319,6 +395,7 @@ __global__ void __launch_bounds__(RE_THREADS) k_reenc(Batch B) {
     if (rank < P.reenc_max && INB(rank, RE_CAND, 803)) R->re_rank[rank] = j;
   }
   n_ok = block_sum_i(n_ok, bs);
+  PHASE_MARK(21);   // ranking (last CTA)
   if (tid == 0) {
     const int nreq = min(n_ok, max(0, P.reenc_max));
     R->re_n = nreq;

@@ -2043,6 +2043,27 @@ int smg_set_object_embeddings(smg_batch* b, const int32_t* maps, const uint32_t*
   return SMG_OK;
 }
 
+// Phase-timing counters of an instrumentation build (-DSMG_PHASE_TIMING): out[2k] = cycles
+// summed over the blocks' thread 0, out[2k+1] = marks, k < 64; the counters are reset.  Returns
+// SMG_ERR_UNSUPPORTED in the production build.
+int smg_phase_read(uint64_t* out) {
+#ifdef SMG_PHASE_TIMING
+  if (!out) return fail(SMG_ERR_ARGS, "smg_phase_read: bad arguments");
+  unsigned long long c[64], h[64];
+  CK(cudaDeviceSynchronize());
+  CK(cudaMemcpyFromSymbol(c, g_phase_cycles, sizeof c));
+  CK(cudaMemcpyFromSymbol(h, g_phase_hits, sizeof h));
+  for (int k = 0; k < 64; ++k) { out[2 * k] = c[k]; out[2 * k + 1] = h[k]; }
+  memset(c, 0, sizeof c);
+  CK(cudaMemcpyToSymbol(g_phase_cycles, c, sizeof c));
+  CK(cudaMemcpyToSymbol(g_phase_hits, c, sizeof c));
+  return SMG_OK;
+#else
+  (void)out;
+  return fail(SMG_ERR_UNSUPPORTED, "smg_phase_read: not an instrumentation build (-DSMG_PHASE_TIMING)");
+#endif
+}
+
 int smg_set_reencode(smg_batch* b, int on) {
   if (!b) return fail(SMG_ERR_ARGS, "smg_set_reencode: bad arguments");
   if (int r = sync_b(b)) return r;
