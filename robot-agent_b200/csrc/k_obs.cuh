@@ -213,55 +213,70 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     }
   }
   __syncthreads();
-  {
-    const int lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
-    for (int it = wid; it < iters; it += nw) {
-      if (!INB(h_id[it][0], n, 105) || !INB(h_id[it][1], n, 105) || !INB(h_id[it][2], n, 105)) { if (lane == 0) h_cnt[it] = -1; continue; }
-      const float* a = xyz + 3 * h_id[it][0];
-      const float* b = xyz + 3 * h_id[it][1];
-      const float* c = xyz + 3 * h_id[it][2];
-      const double u[3] = {(double)(b[0] - a[0]), (double)(b[1] - a[1]), (double)(b[2] - a[2])};
-      const double v[3] = {(double)(c[0] - a[0]), (double)(c[1] - a[1]), (double)(c[2] - a[2])};
-      double nn[3] = {u[1] * v[2] - u[2] * v[1], u[2] * v[0] - u[0] * v[2], u[0] * v[1] - u[1] * v[0]};
-      const double L = sqrt(nn[0] * nn[0] + nn[1] * nn[1] + nn[2] * nn[2]);
-      if (L < 1e-6) {   // nearly collinear: the reference skips the iteration
+  // Score the hypotheses a warp each, one batch of (warps) at a time; after each batch thread 0
+  // continues the reference's walk (best so far, adaptive stop) over the newly scored ones, and
+  // the scoring ends as soon as the walk has ended: later hypotheses would never be looked at.
+  __shared__ int sh_more;
+  if (tid == 0) sh_bestc = -1;
+  double best[4] = {0, 0, 1, 0};
+  int best_c = -1, need = max_iters > 1 ? max_iters : 1, walk = 0;   // thread 0's walk state
+  const int lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  for (int r0 = 0; r0 < iters; r0 += nw) {
+    const int it = r0 + wid;
+    if (it < iters) {
+      if (!INB(h_id[it][0], n, 105) || !INB(h_id[it][1], n, 105) || !INB(h_id[it][2], n, 105)) {
         if (lane == 0) h_cnt[it] = -1;
-        continue;
-      }
-      for (int k = 0; k < 3; ++k) nn[k] /= L;
-      const double d0 = -(nn[0] * (double)a[0] + nn[1] * (double)a[1] + nn[2] * (double)a[2]);
-      int cnt = 0;
-      for (int s = lane; s < nsamp; s += 32) {
-        const int i = s * sstep;
-        if (!INB(i, n, 119)) break;
-        cnt += fabs(nn[0] * (double)xyz[3 * i] + nn[1] * (double)xyz[3 * i + 1] + nn[2] * (double)xyz[3 * i + 2] + d0) <= tau;
-      }
-      cnt = warp_sum_i(cnt);
-      if (lane == 0) {
-        h_cnt[it] = cnt;
-        h_pl[it][0] = nn[0]; h_pl[it][1] = nn[1]; h_pl[it][2] = nn[2]; h_pl[it][3] = d0;
-      }
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    double best[4] = {0, 0, 1, 0};
-    int best_c = -1;
-    int need = max_iters > 1 ? max_iters : 1;
-    for (int it = 0; it < need && it < iters; ++it) {
-      const int cnt = h_cnt[it];
-      if (cnt < 0) continue;
-      if (cnt > best_c) {
-        best_c = cnt;
-        for (int k = 0; k < 4; ++k) best[k] = h_pl[it][k];
-        const double w = (double)cnt / (double)nsamp;
-        const double pw = w * w * w;
-        if (pw > 0.999999) break;
-        if (pw > 1e-9 && INB(nsamp * NEED_N + cnt, NEED_N * NEED_N, 120)) need = need_tab[nsamp * NEED_N + cnt];
+      } else {
+        const float* a = xyz + 3 * h_id[it][0];
+        const float* b = xyz + 3 * h_id[it][1];
+        const float* c = xyz + 3 * h_id[it][2];
+        const double u[3] = {(double)(b[0] - a[0]), (double)(b[1] - a[1]), (double)(b[2] - a[2])};
+        const double v[3] = {(double)(c[0] - a[0]), (double)(c[1] - a[1]), (double)(c[2] - a[2])};
+        double nn[3] = {u[1] * v[2] - u[2] * v[1], u[2] * v[0] - u[0] * v[2], u[0] * v[1] - u[1] * v[0]};
+        const double L = sqrt(nn[0] * nn[0] + nn[1] * nn[1] + nn[2] * nn[2]);
+        if (L < 1e-6) {   // nearly collinear: the reference skips the iteration
+          if (lane == 0) h_cnt[it] = -1;
+        } else {
+          for (int k = 0; k < 3; ++k) nn[k] /= L;
+          const double d0 = -(nn[0] * (double)a[0] + nn[1] * (double)a[1] + nn[2] * (double)a[2]);
+          int cnt = 0;
+          for (int s = lane; s < nsamp; s += 32) {
+            const int i = s * sstep;
+            if (!INB(i, n, 119)) break;
+            cnt += fabs(nn[0] * (double)xyz[3 * i] + nn[1] * (double)xyz[3 * i + 1] + nn[2] * (double)xyz[3 * i + 2] + d0) <= tau;
+          }
+          cnt = warp_sum_i(cnt);
+          if (lane == 0) {
+            h_cnt[it] = cnt;
+            h_pl[it][0] = nn[0]; h_pl[it][1] = nn[1]; h_pl[it][2] = nn[2]; h_pl[it][3] = d0;
+          }
+        }
       }
     }
-    sh_bestc = best_c;
-    for (int k = 0; k < 4; ++k) sh_best[k] = best[k];
+    __syncthreads();
+    if (tid == 0) {
+      const int end = r0 + nw < iters ? r0 + nw : iters;
+      bool stop = false;
+      for (; walk < need && walk < end; ++walk) {
+        const int cnt = h_cnt[walk];
+        if (cnt < 0) continue;
+        if (cnt > best_c) {
+          best_c = cnt;
+          for (int k = 0; k < 4; ++k) best[k] = h_pl[walk][k];
+          const double w = (double)cnt / (double)nsamp;
+          const double pw = w * w * w;
+          if (pw > 0.999999) { stop = true; break; }
+          if (pw > 1e-9 && INB(nsamp * NEED_N + cnt, NEED_N * NEED_N, 120)) need = need_tab[nsamp * NEED_N + cnt];
+        }
+      }
+      sh_more = !stop && walk < need && walk < iters;
+      if (!sh_more) {
+        sh_bestc = best_c;
+        for (int k = 0; k < 4; ++k) sh_best[k] = best[k];
+      }
+    }
+    __syncthreads();
+    if (!sh_more) break;
   }
   __syncthreads();
   if (sh_bestc < 3) {
@@ -346,6 +361,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     jacobi_cs(2 * sxy, sxx - syy, &th_hc, &th_hs);
   }
   __syncthreads();
+  PHASE_MARK(pbase + 1);   // PCA refits (parallel)
   if (sh_deg) {   // exact replay in the reference's order (pcaOf objprob.cpp:101-114, :166-192)
     if (tid == 0) {
       double q[4] = {sh_best[0], sh_best[1], sh_best[2], sh_best[3]}, qm[4] = {0, 0, 0, 0};
@@ -413,7 +429,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
     return;
   }
   const double m0 = sh_m[0], m1 = sh_m[1], hc = th_hc, hs = th_hs;
-  PHASE_MARK(pbase + 1);   // PCA refits
+  if (sh_deg) PHASE_MARK(pbase + 3);   // sequential replay (only when it ran)
   // z and horizontal-span projections of the inliers -> exact percentiles (objprob.cpp:193-206)
   __shared__ int sh_cnt;
   if (tid == 0) sh_cnt = 0;
