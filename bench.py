@@ -108,6 +108,10 @@ def parse():
     ap.add_argument("--cpu-timed", type=int, default=10,
                     help="CPU baseline: timed keyframes per map (the first of the device arm's timed frames)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="objprob: skip the short config-2 / config-3 runs recorded under extra_workloads")
+    ap.add_argument("--assoc-frames", type=int, default=8,
+                    help="config 2: frames per association call (their detections as one row block against the bank)")
     ap.add_argument("--workload", default="objprob", choices=["objprob", "occ", "assoc"],
                     help="objprob = config 1 (headline); occ = config 3 (grid insert + correlative scan matching); "
                          "assoc = config 2 (association GEMM)")
@@ -493,29 +497,31 @@ def run_occ(args, rank, world, local_rank):
 
 
 def run_assoc(args, rank, world, local_rank):
-    """Config 2: each step associates one frame of 256 detections with the 16384-vector bank
-    (tcgen05 GEMM + fused gate/top-1 + certification).  Frames are pre-generated and resident;
-    the bank (37.7 MB) stays resident across steps.  Per-kernel CUDA-event times give the GEMM's
-    TFLOP/s and the bytes it must move."""
+    """Config 2: each step associates F frames of 256 detections with the 16384-vector bank in
+    one call (the frames' detections as consecutive rows; tcgen05 GEMM + fused gate/top-1 +
+    certification).  Frames are pre-generated and resident; the bank (37.7 MB) stays resident
+    across steps.  Per-kernel CUDA-event times give the GEMM's TFLOP/s."""
     import torch
     from scenemap_b200.assoc import AssocGPU, AssocWorkload
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     W = AssocWorkload(seed=100 + rank)
-    n_frames = 64
-    frames = [W.frame(k) for k in range(n_frames)]
+    F = max(1, args.assoc_frames)
+    n_batches = 8
+    frames = [W.frame(k) for k in range(F * n_batches)]
     to_d = lambda a, dt=None: (torch.from_numpy(np.ascontiguousarray(a)).view(dt) if dt is not None
                                else torch.from_numpy(np.ascontiguousarray(a))).to(dev)
-    Z = [to_d(f[0], torch.int16) for f in frames]
-    Bx = [to_d(f[1]) for f in frames]
+    zb = [np.concatenate([frames[i * F + j][0] for j in range(F)]) for i in range(n_batches)]
+    bb = [np.concatenate([frames[i * F + j][1] for j in range(F)]) for i in range(n_batches)]
+    Z = [to_d(z, torch.int16) for z in zb]
+    Bx = [to_d(b) for b in bb]
     mem, mbox = to_d(W.mem, torch.int16), to_d(W.mem_box)
-    A = AssocGPU(W.n_det, W.n_mem, W.dim, dev=local_rank)
+    A = AssocGPU(W.n_det * F, W.n_mem, W.dim, dev=local_rank)
     st = torch.cuda.current_stream(dev)
     for k in range(args.warmup):
-        A.match(Z[k % n_frames], Bx[k % n_frames], mem, mbox, stream=st.cuda_stream)
+        A.match(Z[k % n_batches], Bx[k % n_batches], mem, mbox, stream=st.cuda_stream)
     torch.cuda.synchronize()
     K = args.steps
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -523,22 +529,22 @@ def run_assoc(args, rank, world, local_rank):
     e0.record(st)
     outs = []
     for k in range(K):
-        outs.append(A.match(Z[k % n_frames], Bx[k % n_frames], mem, mbox, stream=st.cuda_stream))
+        outs.append(A.match(Z[k % n_batches], Bx[k % n_batches], mem, mbox, stream=st.cuda_stream))
     e1.record(st)
     torch.cuda.synchronize()
     t = e0.elapsed_time(e1) / 1e3
     cert = float(np.mean([o[2].float().mean().item() for o in outs[:16]]))
     matched = float(np.mean([(o[0] >= 0).float().mean().item() for o in outs[:16]]))
-    # end to end: host frames (pinned) in, decisions out, every step
-    hz = [torch.from_numpy(f[0].view(np.int16)).pin_memory() for f in frames]
-    hb = [torch.from_numpy(f[1]).pin_memory() for f in frames]
+    # end to end: host batches (pinned) in, decisions out, every step
+    hz = [torch.from_numpy(z.view(np.int16)).pin_memory() for z in zb]
+    hb = [torch.from_numpy(b).pin_memory() for b in bb]
     zd, bd = torch.empty_like(Z[0]), torch.empty_like(Bx[0])
     KE = min(K, 200)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for k in range(KE):
-        zd.copy_(hz[k % n_frames], non_blocking=True)
-        bd.copy_(hb[k % n_frames], non_blocking=True)
+        zd.copy_(hz[k % n_batches], non_blocking=True)
+        bd.copy_(hb[k % n_batches], non_blocking=True)
         m, s, c = A.match(zd, bd, mem, mbox, stream=st.cuda_stream)
         m.cpu()
     t_e2e = time.perf_counter() - t0
@@ -557,8 +563,48 @@ def run_assoc(args, rank, world, local_rank):
             ao.decide(frames[k][0], frames[k][1], W.mem, W.mem_box)
         cb = {"value": ns / (time.perf_counter() - t0), "unit": "frames/s", "cores": 1, "kind": "port",
               "sample": f"{ns} frames: numpy restatement (float32 gate over all pairs, fp64 index-order dots of gated pairs)"}
-    return dict(t=t, K=K, t_e2e=t_e2e, KE=KE, cert=cert, matched=matched, err=err, cb=cb,
+    return dict(t=t, K=K, t_e2e=t_e2e, KE=KE, cert=cert, matched=matched, err=err, cb=cb, F=F,
                 flops=2.0 * W.n_det * W.n_mem * W.dim, bytes=2.0 * W.dim * (W.n_mem + W.n_det), n_det=W.n_det)
+
+
+def assoc_line(r: dict, args, world: int) -> dict:
+    """The config-2 JSON line of a run_assoc result."""
+    F = r["F"]
+    v = world * r["K"] * F / r["t"]
+    peaks_p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peaks = json.load(open(peaks_p)) if os.path.exists(peaks_p) else {}
+    tf = r["flops"] * r["K"] * F / r["t"] / 1e12
+    pk = peaks.get("bf16_tflops", 1590.0)
+    out = {"metric": "frames/s of association stress (config 2)", "value": v, "unit": "frames/s", "n_gpus": world,
+           "steps": r["K"], "warmup": args.warmup, "ms_per_step": 1e3 * r["t"] / r["K"], "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
+           "config": {"workload": "config 2: 256 detections x 16384 memories x 1152, IoU gate 0.1, cos 0.8, top-1",
+                      "frames_per_step": F,
+                      "l2": "bank (37.7 MB) resident in L2 across steps"},
+           "roofline": {"kernel": "k_assoc_gemm + k_assoc_decide", "bound": "tensor", "achieved": tf, "peak": pk,
+                        "unit": "TFLOP/s", "frac": tf / pk, "traffic": None,
+                        "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)" if peaks else "fallback"},
+           "certified_fraction": r["cert"], "matched_fraction": r["matched"], "device_error_word": r["err"],
+           "e2e": {"value": world * r["KE"] * F / r["t_e2e"], "unit": "frames/s",
+                   "h2d_bytes_per_step": int(F * r["n_det"] * (1152 * 2 + 24)),
+                   "d2h_bytes_per_step": int(F * r["n_det"] * 4)}}
+    return out
+
+
+def occ_line(r: dict, args, world: int) -> dict:
+    """The config-3 JSON line of a run_occ result."""
+    M = args.maps
+    v = M * world * r["K"] / r["t"]
+    out = {"metric": "scans/s of occupancy insert + correlative scan match (config 3)", "value": v, "unit": "scans/s",
+           "n_gpus": world, "steps": r["K"], "warmup": args.warmup, "ms_per_step": 1e3 * r["t"] / r["K"],
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i32 scores / f64 poses",
+           "data": "synthetic", "config": {"workload": f"config 3: {M} map(s) per GPU, 12-room floor plan, 720 beams, "
+                                                       "8 m, 1024^2 grid at 0.05 m, 13x13x41 search",
+                                           "maps_per_gpu": M},
+           "csm_lookups_per_s": v * r["n_hits"] * r["n_cand"],
+           "e2e": {"value": M * world * r["KE"] / r["t_e2e"], "unit": "scans/s",
+                   "h2d_bytes_per_step": int(M * (8 * 720 + 64)), "d2h_bytes_per_step": int(M * 56)}}
+    return out
 
 
 def main():
@@ -615,22 +661,7 @@ def main():
             import torch
             torch.distributed.destroy_process_group()
         if rank == 0:
-            v = world * r["K"] / r["t"]
-            peaks_p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-            peaks = json.load(open(peaks_p)) if os.path.exists(peaks_p) else {}
-            tf = r["flops"] * r["K"] / r["t"] / 1e12
-            pk = peaks.get("bf16_tflops", 1590.0)
-            out = {"metric": "frames/s of association stress (config 2)", "value": v, "unit": "frames/s", "n_gpus": world,
-                   "steps": r["K"], "warmup": args.warmup, "ms_per_step": 1e3 * r["t"] / r["K"], "higher_is_better": True,
-                   "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
-                   "config": {"workload": "config 2: 256 detections x 16384 memories x 1152, IoU gate 0.1, cos 0.8, top-1",
-                              "l2": "bank (37.7 MB) resident in L2 across steps"},
-                   "roofline": {"kernel": "k_assoc_gemm + k_assoc_decide", "bound": "tensor", "achieved": tf, "peak": pk,
-                                "unit": "TFLOP/s", "frac": tf / pk, "traffic": None,
-                                "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops)" if peaks else "fallback"},
-                   "certified_fraction": r["cert"], "matched_fraction": r["matched"], "device_error_word": r["err"],
-                   "e2e": {"value": world * r["KE"] / r["t_e2e"], "unit": "frames/s",
-                           "h2d_bytes_per_step": int(r["n_det"] * (1152 * 2 + 24)), "d2h_bytes_per_step": int(r["n_det"] * 4)}}
+            out = assoc_line(r, args, world)
             if r["cb"]:
                 out["cpu_baseline"] = r["cb"]
             print(json.dumps(out))
@@ -641,17 +672,7 @@ def main():
             import torch
             torch.distributed.destroy_process_group()
         if rank == 0:
-            M = args.maps
-            v = M * world * r["K"] / r["t"]
-            out = {"metric": "scans/s of occupancy insert + correlative scan match (config 3)", "value": v, "unit": "scans/s",
-                   "n_gpus": world, "steps": r["K"], "warmup": args.warmup, "ms_per_step": 1e3 * r["t"] / r["K"],
-                   "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "i32 scores / f64 poses",
-                   "data": "synthetic", "config": {"workload": f"config 3: {M} map(s) per GPU, 12-room floor plan, 720 beams, "
-                                                               "8 m, 1024^2 grid at 0.05 m, 13x13x41 search",
-                                                   "maps_per_gpu": M},
-                   "csm_lookups_per_s": v * r["n_hits"] * r["n_cand"],
-                   "e2e": {"value": M * world * r["KE"] / r["t_e2e"], "unit": "scans/s",
-                           "h2d_bytes_per_step": int(M * (8 * 720 + 64)), "d2h_bytes_per_step": int(M * 56)}}
+            out = occ_line(r, args, world)
             if r["cb"]:
                 out["cpu_baseline"] = r["cb"]
             print(json.dumps(out))
@@ -697,7 +718,30 @@ def main():
             out["cpu_baseline_without_reencode"] = {k: cb_nr[k] for k in ("value", "unit", "cores", "kind", "sample")}
             ratios["without_reencode"] = out["value_without_reencode"] / cb_nr["value"]
         out["vs_cpu_baseline"] = ratios
+    if world == 1 and not args.no_extra:
+        out["extra_workloads"] = extra_workloads(args, local_rank)
     print(json.dumps(out))
+
+
+def extra_workloads(args, local_rank: int) -> dict:
+    """Short device-timed runs of the other configurations, so the default run records them:
+    config 2 (association GEMM, 8 frames per call) and config 3 (occupancy insert + scan match,
+    one map).  Each is its own `--workload` run with fewer steps; no CPU baselines here."""
+    import copy
+    out = {}
+    a2 = copy.copy(args)
+    a2.steps, a2.warmup, a2.no_cpu_baseline, a2.assoc_frames = 30, 3, True, 8
+    try:
+        out["config2"] = assoc_line(run_assoc(a2, 0, 1, local_rank), a2, 1)
+    except Exception as e:   # recorded, not fatal to the headline line
+        out["config2"] = {"error": f"{type(e).__name__}: {e}"}
+    a3 = copy.copy(args)
+    a3.steps, a3.warmup, a3.no_cpu_baseline, a3.maps, a3.scans = 30, 3, True, 1, 200
+    try:
+        out["config3"] = occ_line(run_occ(a3, 0, 1, local_rank), a3, 1)
+    except Exception as e:
+        out["config3"] = {"error": f"{type(e).__name__}: {e}"}
+    return out
 
 
 if __name__ == "__main__":

@@ -141,6 +141,12 @@ typedef struct smg_frame {
   /* ObjFrame::depth_mm: depth as uint16 millimetres (read as mm * 1e-3f, like the reference),
    * used when depth is NULL */
   const uint16_t* depth_mm;
+  /* sm_image::rgba: w*h RGBA8 colour image registered with the depth image, or NULL.  With it
+   * (and a detector image the size of the depth image), the keyframe also colours the cloud
+   * points it adds (gatherRgbHost, bestview.cpp) and picks best views (capi.cpp:903-998):
+   * smg_get_views.  Without it, points are grey (128) and no view is picked, as in the
+   * reference with no RGB source. */
+  const uint8_t* rgba;
 } smg_frame;
 
 typedef struct smg_batch smg_batch;
@@ -195,6 +201,20 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
 int smg_set_reencode(smg_batch* b, int on);
 
 /* ---- results (device -> host on request; each getter synchronises the batch stream) ---- */
+/* A best view (scenemap include/scenemap/bestview.hpp BestView; chosen as capi.cpp:903-998
+ * does: quality q = valid mask area x score, a detection's crop replaces the object's view when
+ * q >= the view's q (ties: the newer), moved / put-down events reset the view's q to 0).  box:
+ * the crop (detection box + 10 % per side, clipped), det_box: the rounded detection box, both
+ * in image pixels [x0, y0, x1, y1); w x h: the crop's size (longer side <= 256). */
+typedef struct smg_view {
+  uint32_t id, version;
+  double q, stamp;
+  int32_t box[4], det_box[4];
+  float mask_area, depth_m, score;
+  double cam_T[12];
+  int32_t w, h;
+} smg_view;
+#define SMG_VIEW_MAX_SIDE 256
 typedef struct smg_object {
   uint32_t id;
   int32_t cls;
@@ -227,6 +247,16 @@ int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap);
 int smg_get_object_vectors(smg_batch* b, int m, int i, float* r_frag, uint16_t* views, float* vkappa, double* vstamp, int vcap);
 /* Cloud of object i of map m: points relative to cloud_org (float xyz) and seq; returns count. */
 int smg_get_object_cloud(smg_batch* b, int m, int i, float* xyz, uint32_t* seq, int cap);
+/* Cloud colours of object i of map m (ObjCloud point r, g, b; grey without an RGB source),
+ * 3 bytes per point in the order of smg_get_object_cloud; returns count. */
+int smg_get_object_cloud_rgb(smg_batch* b, int m, int i, uint8_t* rgb, int cap);
+/* The views of map m that its last keyframe replaced, in the order the reference installs
+ * them (its views map keeps, per object id, only the last).  Images (may be NULL) are written
+ * at a fixed stride per view, row-major and packed to w x h: rgb at rgb + v * 256*256*3 (area
+ * average of the crop box), depth at depth + v * 256*256 (uint16 mm, nearest, 0 = none;
+ * cropDepthMm) and mask at mask + v * 256*256 (255 inside the detection mask; cropMask).  They
+ * are valid until the next push.  Returns the number of views (up to cap copied). */
+int smg_get_views(smg_batch* b, int m, smg_view* out, uint8_t* rgb, uint16_t* depth, uint8_t* mask, int cap);
 /* ObjectMap::lastAssoc() (objmap.hpp:251) of map m: per detection obj_id, n_valid, area_px, depth_med. */
 int smg_get_assoc(smg_batch* b, int m, uint32_t* obj_id, int32_t* n_valid, float* area_px, float* depth_med, int cap);
 /* ApStats (objmap.hpp:132-139) of map m, 16 counters in declaration order. */
@@ -273,7 +303,7 @@ int smg_get_object_whole(smg_batch* b, int m, int i, float* r_whole, double* k_w
 /* Per-kernel device time with CUDA events on the launch stream (instrumentation, off by
  * default).  smg_timing_read fills ms[k] (total milliseconds) and n[k] (launches) for the
  * SMG_NUM_KERNELS kernels of the keyframe chain and resets the counters; names[k] is static. */
-#define SMG_NUM_KERNELS 16
+#define SMG_NUM_KERNELS 17
 int smg_timing_enable(smg_batch* b, int on);
 int smg_timing_read(smg_batch* b, double* ms, int64_t* n, const char** names);
 /* First failed self-check of a -DSMG_CHECKS build: (site, index, bound); all zero when none

@@ -27,7 +27,13 @@ class RfFrame(C.Structure):
                 ("grid_only", C.c_int), ("grip", C.c_float * 2), ("mask_bits", C.POINTER(C.c_uint32)),
                 ("mask_w", C.c_int), ("mask_h", C.c_int), ("mask_sx", C.c_float), ("mask_sy", C.c_float),
                 ("mask_ox", C.c_float), ("mask_oy", C.c_float), ("img_w", C.c_int), ("img_h", C.c_int),
-                ("depth_mm", C.POINTER(C.c_uint16))]
+                ("depth_mm", C.POINTER(C.c_uint16)), ("rgba", C.POINTER(C.c_uint8))]
+
+
+class RfView(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("version", C.c_uint32), ("q", C.c_double), ("stamp", C.c_double),
+                ("box", C.c_int32 * 4), ("det_box", C.c_int32 * 4), ("mask_area", C.c_float), ("depth_m", C.c_float),
+                ("score", C.c_float), ("cam_T", C.c_double * 12), ("w", C.c_int32), ("h", C.c_int32)]
 
 
 class RfObj(C.Structure):
@@ -79,6 +85,8 @@ def ref_lib():
         L.ref_object_vectors.argtypes = [C.c_void_p, C.c_int, P(C.c_float), C.c_int, P(C.c_uint16), P(C.c_float),
                                          P(C.c_double), C.c_int]
         L.ref_object_cloud.argtypes = [C.c_void_p, C.c_int, P(C.c_float), P(C.c_uint32), C.c_int]
+        L.ref_object_cloud_rgb.argtypes = [C.c_void_p, C.c_int, P(C.c_uint8), C.c_int]
+        L.ref_views.argtypes = [C.c_void_p, P(RfView), P(C.c_uint8), P(C.c_uint16), P(C.c_uint8), C.c_int]
         L.ref_assoc.argtypes = [C.c_void_p, P(C.c_uint32), P(C.c_int32), P(C.c_float), P(C.c_float), C.c_int]
         L.ref_n_points.argtypes = [C.c_void_p]
         L.ref_points.argtypes = [C.c_void_p, C.c_int, P(C.c_uint32), P(C.c_int32), P(C.c_float), P(C.c_int32), C.c_int]
@@ -144,6 +152,10 @@ def make_rf_frame(fr: dict, keep: list) -> RfFrame:
         f.mask_w, f.mask_h = fr["mask_w"], fr["mask_h"]
         f.mask_sx, f.mask_sy, f.mask_ox, f.mask_oy = fr["mask_affine"]
     f.img_w, f.img_h = fr.get("img_w", 0), fr.get("img_h", 0)
+    if fr.get("rgba") is not None:
+        rgba = np.ascontiguousarray(fr["rgba"], np.uint8)
+        keep.append(rgba)
+        f.rgba = _p(rgba, C.c_uint8)
     f.fx, f.fy, f.cx, f.cy = fr["fx"], fr["fy"], fr["cx"], fr["cy"]
     for i in range(12):
         f.T_mc[i] = fr["T_mc"][i]
@@ -240,6 +252,37 @@ class RefMap:
         seq = np.zeros(max(n, 1), np.uint32)
         L.ref_object_cloud(self._h, i, _p(xyz, C.c_float), _p(seq, C.c_uint32), n)
         return xyz[:n], seq[:n]
+
+    def object_cloud_rgb(self, i: int):
+        L = ref_lib()
+        n = L.ref_object_cloud_rgb(self._h, i, None, 0)
+        rgb = np.zeros((max(n, 1), 3), np.uint8)
+        L.ref_object_cloud_rgb(self._h, i, _p(rgb, C.c_uint8), n)
+        return rgb[:n]
+
+    def views(self) -> dict:
+        """The glue's views map after the last frame: id -> view dict with its images."""
+        L = ref_lib()
+        n = L.ref_views(self._h, None, None, None, None, 0)
+        arr = (RfView * max(n, 1))()
+        S = 256 * 256
+        rgb = np.zeros((max(n, 1), S * 3), np.uint8)
+        dep = np.zeros((max(n, 1), S), np.uint16)
+        msk = np.zeros((max(n, 1), S), np.uint8)
+        L.ref_views(self._h, arr, _p(rgb, C.c_uint8), _p(dep, C.c_uint16), _p(msk, C.c_uint8), n)
+        out = {}
+        for v in range(n):
+            o = arr[v]
+            d = {}
+            for name, _ in RfView._fields_:
+                x = getattr(o, name)
+                d[name] = list(x) if hasattr(x, "__len__") else x
+            w, h = o.w, o.h
+            d["rgb"] = rgb[v, :w * h * 3].reshape(h, w, 3).copy()
+            d["depth"] = dep[v, :w * h].reshape(h, w).copy()
+            d["mask"] = msk[v, :w * h].reshape(h, w).copy()
+            out[o.id] = d
+        return out
 
     def assoc(self):
         L = ref_lib()

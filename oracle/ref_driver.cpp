@@ -7,16 +7,21 @@
 //   ObjectMap::addPoints(scenemap src/objmap.cpp:508)    -> ObjCloud::add (cloud.cpp:86)
 //   ObjectMap::buildReencode (scenemap src/objmap.cpp:1371) -> whole-object re-encode requests
 // in the order the reference's keyframe glue runs them (scenemap src/capi.cpp:811-1010),
-// minus robot FK and best-view crops (outside the hot path).
+// minus robot FK.  With an RGBA image the glue's best-view selection and point colouring
+// (capi.cpp:903-998: restated here around the reference's own cropGeometry, cropMask,
+// cropRgbHost, cropDepthMm and gatherRgbHost from bestview.cpp) run as well.
 // The label image is turned into the sm_detections bit masks the reference consumes
 // (scenemap include/scenemap.h:20-34), with the mask grid equal to the image grid.
 #include <math.h>
 #include <stdint.h>
 #include <string.h>
 
+#include <map>
 #include <memory>
+#include <unordered_set>
 #include <vector>
 
+#include "scenemap/bestview.hpp"
 #include "scenemap/grid.hpp"
 #include "scenemap/mapper2d.hpp"
 #include "scenemap/objmap.hpp"
@@ -54,6 +59,7 @@ typedef struct {
   float mask_sx, mask_sy, mask_ox, mask_oy;
   int img_w, img_h;       // detector image (0 = the depth image's size)
   const uint16_t* depth_mm;   // ObjFrame::depth_mm / DepthView::mm, when depth is null
+  const uint8_t* rgba;        // sm_image::rgba (w x h x 4), or null
 } rf_frame;
 
 typedef struct {
@@ -99,6 +105,14 @@ struct RefMap {
   std::vector<ReencReq> reenc;  // re-encode requests of the last keyframe
   int reenc_words = 0;
   bool reenc_on = true;   // build the re-encode requests (the reference's push always does)
+  // best views (sm_ctx::views, view_ver, ev_seen: capi.cpp:113-116)
+  struct Slot {
+    std::shared_ptr<const BestView> v;
+    double q = 0;
+  };
+  std::map<uint32_t, Slot> views;
+  uint32_t view_ver = 0;
+  size_t ev_seen = 0;
   explicit RefMap(const ObjParams& p) : om(p) {}
 };
 
@@ -203,9 +217,88 @@ int ref_frame(void* h, const rf_frame* f) {
   F.emb = f->emb;
   F.emb_dim = f->emb_dim;
   m->om.update(F);
-  // cloud points, uncoloured (capi.cpp:986-992 with no RGB source)
+  // best views (capi.cpp:903-943): moved / put-down events reset the view quality, views of
+  // objects that are gone are dropped, detections attached to an object become candidates
+  const auto& ev = m->om.events();
+  for (; m->ev_seen < ev.size(); ++m->ev_seen)
+    if (ev[m->ev_seen].kind == 2 || ev[m->ev_seen].kind == 5) {
+      auto it = m->views.find(ev[m->ev_seen].id);
+      if (it != m->views.end()) it->second.q = 0;
+    }
+  if (!m->views.empty()) {
+    std::unordered_set<uint32_t> live;
+    for (const MapObject& o : m->om.objects()) live.insert(o.id);
+    for (auto it = m->views.begin(); it != m->views.end();) it = live.count(it->first) ? std::next(it) : m->views.erase(it);
+  }
+  const bool host_rgb = f->rgba && d.img_w == f->w && d.img_h == f->h;
+  struct Cand {
+    uint32_t id;
+    double q;
+    std::shared_ptr<BestView> v;
+  };
+  std::vector<Cand> cand;
+  const std::vector<DetAssoc>& as = m->om.lastAssoc();
+  for (size_t k = 0; k < as.size() && host_rgb; ++k) {
+    if (!as[k].obj_id) continue;
+    const float sc = d.score ? d.score[k] : 1.f;
+    const double q = double(as[k].area_px) * sc;
+    auto it = m->views.find(as[k].obj_id);
+    if (it != m->views.end() && q < it->second.q) continue;
+    auto v = std::make_shared<BestView>();
+    const float* b = d.box + 4 * k;
+    if (!cropGeometry(b, d.img_w, d.img_h, 0.10f, 256, v->box, &v->w, &v->h)) continue;   // kCropMargin, kCropMaxSide
+    v->id = as[k].obj_id;
+    v->q = q;
+    v->stamp = f->stamp;
+    for (int i = 0; i < 4; ++i) v->det_box[i] = int32_t(std::lround(b[i]));
+    v->mask_area = as[k].area_px;
+    v->depth_m = as[k].depth_med;
+    v->score = sc;
+    memcpy(v->cam_T, F.T_mc, sizeof(v->cam_T));
+    v->rgb.resize(size_t(v->w) * v->h * 3);
+    v->depth.resize(size_t(v->w) * v->h);
+    cropMask(&d, int(k), v->box, v->w, v->h, &v->mask);
+    cand.push_back(Cand{v->id, q, std::move(v)});
+  }
+  // cloud points, coloured from the image when there is one (capi.cpp:944-956, :986-992)
   m->pts = m->om.lastPoints();
-  for (const ObsPoints& q : m->pts) m->om.addPoints(q.obj_id, q.xyz.data(), nullptr, int(q.px.size() / 2), f->stamp);
+  size_t npt = 0;
+  for (const ObsPoints& q : m->pts) npt += q.px.size() / 2;
+  std::vector<int32_t> xy;
+  std::vector<uint8_t> rgb;
+  if (npt && host_rgb) {
+    xy.reserve(2 * npt);
+    for (const ObsPoints& q : m->pts) xy.insert(xy.end(), q.px.begin(), q.px.end());
+    rgb.assign(3 * npt, 128);
+    gatherRgbHost(f->rgba, int64_t(f->w) * 4, 4, f->w, f->h, xy.data(), int(npt), rgb.data());
+  }
+  // crops (capi.cpp:958-972); depth from the frame's metres (millimetre frames: mm * 1e-3f)
+  std::vector<float> dm;
+  const float* depth_m = f->depth;
+  if (!depth_m && !cand.empty()) {
+    dm.resize(size_t(f->w) * f->h);
+    for (size_t i = 0; i < dm.size(); ++i) dm[i] = float(f->depth_mm[i]) * 1e-3f;
+    depth_m = dm.data();
+  }
+  for (Cand& c : cand) {
+    const sm_crop_req r{c.v->box[0], c.v->box[1], c.v->box[2], c.v->box[3], c.v->w, c.v->h, c.v->rgb.data()};
+    cropRgbHost(f->rgba, int64_t(f->w) * 4, 4, r);
+    cropDepthMm(depth_m, f->w, f->h, d.img_w, d.img_h, c.v->box, c.v->w, c.v->h, c.v->depth.data());
+  }
+  size_t off = 0;
+  for (const ObsPoints& q : m->pts) {
+    const int np = int(q.px.size() / 2);
+    m->om.addPoints(q.obj_id, q.xyz.data(), host_rgb ? rgb.data() + 3 * off : nullptr, np, f->stamp);
+    off += size_t(np);
+  }
+  // installs (capi.cpp:994-998)
+  for (Cand& c : cand) {
+    RefMap::Slot& sl = m->views[c.id];
+    if (sl.v && c.q < sl.q) continue;
+    c.v->version = ++m->view_ver;
+    sl.v = std::move(c.v);
+    sl.q = c.q;
+  }
   // whole-object re-encode requests on frames with detection embeddings (capi.cpp:1002-1005),
   // the mask grid being the image grid
   if (n > 0 && f->emb && m->reenc_on)
@@ -355,6 +448,64 @@ int ref_object_cloud(void* h, int i, float* xyz, uint32_t* seq, int cap) {
     if (seq) seq[k] = pts[size_t(k)].seq;
   }
   return int(pts.size());
+}
+
+// Cloud colours of object i (3 bytes a point, the order of ref_object_cloud).
+int ref_object_cloud_rgb(void* h, int i, uint8_t* rgb, int cap) {
+  const auto& objs = static_cast<RefMap*>(h)->om.objects();
+  if (i < 0 || size_t(i) >= objs.size()) return -1;
+  const MapObject& o = objs[size_t(i)];
+  if (!o.cloud.data) return 0;
+  const auto& pts = o.cloud.data->pts;
+  const int n = std::min<int>(cap, int(pts.size()));
+  for (int k = 0; k < n && rgb; ++k) {
+    rgb[3 * k] = pts[size_t(k)].r;
+    rgb[3 * k + 1] = pts[size_t(k)].g;
+    rgb[3 * k + 2] = pts[size_t(k)].b;
+  }
+  return int(pts.size());
+}
+
+// The views map, by ascending id: id, version, q, stamp, box (4), det_box (4), mask_area,
+// depth_m, score, cam_T (12), w, h per view; images at a fixed stride of 256*256 pixels.
+typedef struct {
+  uint32_t id, version;
+  double q, stamp;
+  int32_t box[4], det_box[4];
+  float mask_area, depth_m, score;
+  double cam_T[12];
+  int32_t w, h;
+} rf_view;
+int ref_views(void* h, rf_view* out, uint8_t* rgb, uint16_t* depth, uint8_t* mask, int cap) {
+  RefMap* m = static_cast<RefMap*>(h);
+  int n = 0;
+  for (const auto& kv : m->views) {
+    if (!kv.second.v) continue;
+    if (n < cap) {
+      const BestView& v = *kv.second.v;
+      if (out) {
+        rf_view& o = out[n];
+        memset(&o, 0, sizeof(o));
+        o.id = v.id;
+        o.version = v.version;
+        o.q = v.q;
+        o.stamp = v.stamp;
+        for (int c = 0; c < 4; ++c) { o.box[c] = v.box[c]; o.det_box[c] = v.det_box[c]; }
+        o.mask_area = v.mask_area;
+        o.depth_m = v.depth_m;
+        o.score = v.score;
+        memcpy(o.cam_T, v.cam_T, sizeof(o.cam_T));
+        o.w = v.w;
+        o.h = v.h;
+      }
+      const size_t S = 256 * 256;
+      if (rgb && !v.rgb.empty()) memcpy(rgb + size_t(n) * S * 3, v.rgb.data(), v.rgb.size());
+      if (depth && !v.depth.empty()) memcpy(depth + size_t(n) * S, v.depth.data(), v.depth.size() * 2);
+      if (mask && !v.mask.empty()) memcpy(mask + size_t(n) * S, v.mask.data(), v.mask.size());
+    }
+    ++n;
+  }
+  return n;
 }
 
 // per detection: obj_id, n_valid, area_px, depth_med (ObjectMap::lastAssoc)

@@ -74,6 +74,16 @@ DEV uint32_t pack_rgb(const uint8_t* rgb, int i) {
   return rgb ? ((uint32_t)rgb[3 * i] | (uint32_t)rgb[3 * i + 1] << 8 | (uint32_t)rgb[3 * i + 2] << 16) : (128u | 128u << 8 | 128u << 16);
 }
 
+DEV int vclampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// gatherRgbHost (bestview.cpp:84-92) of one point: the colour at its pixel, clamped to the
+// image, packed r | g << 8 | b << 16 as the cloud stores it
+DEV uint32_t gather_rgba(const uint8_t* rgba, const int32_t* px, int i, int w, int h) {
+  const int x = vclampi(px[2 * i], 0, w - 1), y = vclampi(px[2 * i + 1], 0, h - 1);
+  const uchar4 c = ((const uchar4*)rgba)[(size_t)y * w + x];
+  return (uint32_t)c.x | (uint32_t)c.y << 8 | (uint32_t)c.z << 16;
+}
+
 // cap trim (cloud.cpp:114-123): std::nth_element(pts, pts + (n - keep), by seq), then the first
 // n - keep elements are erased and the rest keep the order the selection left them in.  Later
 // steps sample the cloud with a stride, so that order is an output: the selection reproduces
@@ -213,9 +223,11 @@ DEV void cloud_trim(const Batch& B, size_t cs, const Work& W, int* hist, BlockSc
   __syncthreads();
 }
 
-// ObjCloud::add of n map-frame points (float xyz, optional rgb).  Block-wide.
+// ObjCloud::add of n map-frame points (float xyz; colours from rgb, 3 bytes a point, or gathered
+// from an RGBA image at the points' pixels px, or grey).  Block-wide.
 DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uint8_t* rgb, int n, double stamp, const Work& W,
-                   int* hist, BlockScratch& bs) {
+                   int* hist, BlockScratch& bs, const int32_t* px = nullptr, const uint8_t* rgba = nullptr, int iw = 0,
+                   int ih = 0) {
   if (n <= 0) return;
   CloudRec& C = B.clouds[cs];
   const int tid = threadIdx.x;
@@ -289,7 +301,7 @@ DEV void cloud_add(const Batch& B, int m, size_t cs, const float* xyz, const uin
         const float x = (float)((double)xyz[3 * last] - sh_org[0]), y = (float)((double)xyz[3 * last + 1] - sh_org[1]),
                     z = (float)((double)xyz[3 * last + 2] - sh_org[2]);
         pts[d] = make_float4(x, y, z, __uint_as_float(sh_seq));
-        col[d] = pack_rgb(rgb, last);
+        col[d] = rgba && !rgb ? gather_rgba(rgba, px, last, iw, ih) : pack_rgb(rgb, last);
         atomicAdd(&sh_nw, 1);
         if (isnew) W.dst[i] = d;
       }
@@ -437,7 +449,8 @@ __global__ void __launch_bounds__(512) k_cloud_add(Batch B) {
       if (pr.obj_id != o.id) continue;
       if (!INB(pr.det, B.max_det, 408) || !INB(pr.n, B.pmax + 1, 409)) continue;
       const float* xyz = B.cxyz + ((size_t)m * B.max_det + pr.det) * 3 * B.pmax;
-      cloud_add(B, m, cs, xyz, nullptr, pr.n, F.stamp, W, hist, bs);
+      const int32_t* px = B.cpx + ((size_t)m * B.max_det + pr.det) * 2 * B.pmax;
+      cloud_add(B, m, cs, xyz, nullptr, pr.n, F.stamp, W, hist, bs, px, F.views_on ? F.rgba : nullptr, F.w, F.h);
     }
     if (B.clouds[cs].cver != B.clouds[cs].version) contact_rebuild(B, cs, bs);
   }

@@ -426,3 +426,204 @@ __global__ void __launch_bounds__(256) k_assoc_decide(AssocArgs g) {
     g.certified[d] = 0;
   }
 }
+
+// ---- persistent form: many frames against one bank, epilogue overlapped with the next MMAs ----
+//
+// The frames of a batch are rows of one detection matrix (frame f's detections are rows
+// f * n_det ..), so the batch is one GEMM of (frames x n_det) x n_mem x dim.  One CTA per SM walks
+// the 128 x 256 tiles in column-major tile order (consecutive tiles share a bank tile, which the
+// SMs running at the same time then read from L2 together).  Warp roles:
+//   warp 0     TMA producer: A and B K-blocks into a 4-stage ring (full / empty mbarriers);
+//   warp 1     MMA issuer: one elected thread, 72 tcgen05.mma per tile into one of two 256-column
+//              TMEM accumulators (tfull[a] committed when a tile's MMAs have completed; it waits
+//              on tempty[a] before reusing an accumulator);
+//   warp 2     allocates and frees the 512 TMEM columns;
+//   warps 4-11 epilogue: warp 4 + q + 4 h reads TMEM lanes 32q.. (detections) and columns
+//              128h.. of the tile (memories), applies the gate, keeps the per-row best and
+//              second-best, and writes them as tile-half 2 * (column tile) + h for k_assoc_decide;
+//              then it arrives on tempty[a], so the MMAs of tile i + 2 can start while it works on
+//              tile i + 1.
+// Every wait is bounded (AG_WAIT_NS); a timeout sets the error word, the roles run out, and the
+// CTA waits (bounded) for its issued loads and MMAs before freeing TMEM.
+#define AP_EPI_WARPS 8
+#define AP_THREADS ((4 + AP_EPI_WARPS) * 32)
+#define AP_TMEM_COLS 512
+#define AP_SMEM (AG_STAGES * (AG_A_BYTES + AG_B_BYTES) + 2 * AG_BN * 8 * 4 + 256 + 1024)
+
+DEV void ap_epi_bar() { asm volatile("bar.sync 1, %0;" ::"r"(AP_EPI_WARPS * 32) : "memory"); }
+
+__global__ void __launch_bounds__(AP_THREADS, 1)
+    k_assoc_gemm_p(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, AssocArgs g) {
+  extern __shared__ unsigned char ag_raw[];
+  unsigned char* base = (unsigned char*)(((uintptr_t)ag_raw + 1023) & ~(uintptr_t)1023);
+  unsigned char* sA = base;
+  unsigned char* sB = base + AG_STAGES * AG_A_BYTES;
+  float* mbox = (float*)(sB + AG_STAGES * AG_B_BYTES);   // [2][AG_BN][8]
+  uint64_t* full = (uint64_t*)(mbox + 2 * AG_BN * 8);
+  uint64_t* empty = full + AG_STAGES;
+  uint64_t* tfull = empty + AG_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
+  __shared__ int sh_fail;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nk = g.dim / AG_BK;
+  const int n_mt = (g.n_det + AG_BM - 1) / AG_BM, n_nt = (g.n_mem + AG_BN - 1) / AG_BN;
+  const int n_tiles = n_mt * n_nt;
+  if (tid == 0) {
+    for (int s = 0; s < AG_STAGES; ++s) {
+      ag_mbar_init(&full[s], 1);
+      ag_mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ag_mbar_init(&tfull[a], 1);
+      ag_mbar_init(&tempty[a], AP_EPI_WARPS);
+    }
+    ag_mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    sh_fail = 0;
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ag_smem(tmem_slot)),
+                 "r"(AP_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  ag_fence_before();
+  __syncthreads();
+  ag_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+  if (warp == 0) {
+    if (lane == 0) {   // TMA producer
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        const int mt = t % n_mt, nt = t / n_mt;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % AG_STAGES);
+          const uint32_t ph = (it / AG_STAGES) & 1u;
+          if (it >= AG_STAGES && !ag_wait(&empty[s], ph ^ 1u)) { ok = false; break; }
+          ag_expect_tx(&full[s], AG_A_BYTES + AG_B_BYTES);
+          ag_tma_2d(&tmA, &full[s], sA + s * AG_A_BYTES, kb * AG_BK, mt * AG_BM);
+          ag_tma_2d(&tmB, &full[s], sB + s * AG_B_BYTES, kb * AG_BK, nt * AG_BN);
+        }
+      }
+      // drain: the last loads issued must have landed before the CTA exits
+      const uint32_t first = it > AG_STAGES ? it - AG_STAGES : 0;
+      for (uint32_t j = first; j < it; ++j) ok = ag_wait(&full[j % AG_STAGES], (j / AG_STAGES) & 1u) && ok;
+      if (!ok) sh_fail = 1;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {   // MMA issuer
+      uint32_t it = 0, j = 0;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++j) {
+        const uint32_t acc = j & 1u;
+        if (j >= 2 && !ag_wait(&tempty[acc], ((j >> 1) & 1u) ^ 1u)) { ok = false; break; }
+        ag_fence_after();
+        const uint32_t dt = tmem + acc * AG_BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = (int)(it % AG_STAGES);
+          const uint32_t ph = (it / AG_STAGES) & 1u;
+          if (!ag_wait(&full[s], ph)) { ok = false; break; }
+          ag_fence_after();
+          const uint64_t da = ag_desc(sA + s * AG_A_BYTES), db = ag_desc(sB + s * AG_B_BYTES);
+#pragma unroll
+          for (int k = 0; k < AG_BK / 16; ++k) ag_mma(dt, da + 2 * k, db + 2 * k, (kb | k) != 0);
+          ag_commit(&empty[s]);
+        }
+        ag_commit(&tfull[acc]);   // also after a failed wait: arrives when the issued MMAs are done
+      }
+      ag_commit(done);
+      if (!ok) sh_fail = 1;
+    }
+  } else if (warp >= 4) {   // epilogue
+    const int ew = warp - 4, quarter = ew & 3, half = ew >> 2;
+    const int r = quarter * 32 + lane;
+    const float tmin = g.iou_min;
+    uint32_t j = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++j) {
+      const uint32_t acc = j & 1u;
+      const int mt = t % n_mt, nt = t / n_mt;
+      const int m0 = mt * AG_BM, n0 = nt * AG_BN;
+      // memory boxes of the tile into buffer acc (its previous user, tile j - 2, is done: every
+      // epilogue warp passed the barrier of tile j - 1 after it)
+      float* mb = mbox + acc * AG_BN * 8;
+      for (int c = ew * 32 + lane; c < AG_BN; c += AP_EPI_WARPS * 32) {
+        const int jm = n0 + c;
+        float b[6] = {0, 0, 0, 0, 0, 0};
+        if (jm < g.n_mem)
+          for (int k = 0; k < 6; ++k) b[k] = g.mem_box[(size_t)jm * 6 + k];
+        float* o = mb + 8 * c;
+        for (int k = 0; k < 6; ++k) o[k] = b[k];
+        o[6] = ((b[3] - b[0]) * (b[4] - b[1])) * (b[5] - b[2]);
+        o[7] = 0.f;
+      }
+      ap_epi_bar();
+      const int d = m0 + r;
+      float bx[6] = {0, 0, 0, 0, 0, 0};
+      if (d < g.n_det)
+        for (int k = 0; k < 6; ++k) bx[k] = g.det_box[(size_t)d * 6 + k];
+      const float avol = ((bx[3] - bx[0]) * (bx[4] - bx[1])) * (bx[5] - bx[2]);
+      // warp-uniform: tcgen05.ld below is a whole-warp instruction
+      const bool got = __all_sync(0xffffffffu, ag_wait(&tfull[acc], (j >> 1) & 1u) ? 1 : 0) != 0;
+      ag_fence_after();
+      float b1 = -INFINITY, b2 = -INFINITY;
+      int i1 = -1;
+      const int jlim = g.n_mem - n0;
+      const float4* mb4 = (const float4*)mb;
+      if (got) {
+        for (int c0 = half * (AG_BN / 2); c0 < (half + 1) * (AG_BN / 2); c0 += 16) {
+          uint32_t v[16];
+          ag_tmem_ld16(tmem + acc * AG_BN + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+          uint32_t mine = 0;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {   // x and y overlap (a superset of the gate)
+            const float4 p = mb4[2 * (c0 + c)], q = mb4[2 * (c0 + c) + 1];
+            const float e0 = fminf(bx[3], p.w) - fmaxf(bx[0], p.x);
+            const float e1 = fminf(bx[4], q.x) - fmaxf(bx[1], p.y);
+            mine |= (uint32_t)(e0 > 0.f && e1 > 0.f && c0 + c < jlim) << c;
+          }
+          const uint32_t any = __reduce_or_sync(0xffffffffu, mine);
+          if (!any) continue;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {   // the full gate and the top-2, columns in order
+            if (!((any >> c) & 1u)) continue;
+            const float4 p = mb4[2 * (c0 + c)], q = mb4[2 * (c0 + c) + 1];
+            const float e0 = fminf(bx[3], p.w) - fmaxf(bx[0], p.x);
+            const float e1 = fminf(bx[4], q.x) - fmaxf(bx[1], p.y);
+            const float e2 = fminf(bx[5], q.y) - fmaxf(bx[2], p.z);
+            const float inter = (e0 * e1) * e2;
+            const float uni = (avol + q.z) - inter;
+            const bool pass = ((mine >> c) & 1u) && e2 > 0.f && inter > tmin * uni;
+            const float sc = pass ? __uint_as_float(v[c]) : -INFINITY;
+            const bool gt = sc > b1;
+            b2 = gt ? b1 : fmaxf(b2, sc);
+            i1 = gt ? n0 + c0 + c : i1;
+            b1 = gt ? sc : b1;
+          }
+        }
+      } else if (lane == 0) {
+        sh_fail = 1;
+      }
+      ag_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(ag_smem(&tempty[acc])) : "memory");
+      if (d < g.n_det) {
+        const size_t q = (size_t)d * g.n_tiles + 2 * nt + half;
+        g.t_best[q] = i1 >= 0 ? b1 : -INFINITY;
+        g.t_second[q] = b2;
+        g.t_idx[q] = i1;
+      }
+    }
+  }
+  __syncwarp();
+  // every issued MMA has completed before TMEM is freed (the issuer's last commit)
+  if (!ag_wait(done, 0)) sh_fail = 1;
+  ag_fence_before();
+  __syncthreads();
+  if (tid == 0 && sh_fail) atomicOr(g.err, 1);
+  if (warp == 2) {
+    ag_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(AP_TMEM_COLS) : "memory");
+  }
+}

@@ -35,6 +35,7 @@
 #include "k_gather.cuh"
 #include "k_reenc.cuh"
 #include "k_hands.cuh"
+#include "k_views.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -81,6 +82,9 @@ struct smg_batch {
   unsigned char* d_emb = nullptr;
   uint16_t* d_depth_mm = nullptr;  // staging of host millimetre depth
   uint32_t* d_mask = nullptr;      // staging of host detector bit masks: M x max_det x mask_words_max
+  uint8_t* d_rgba = nullptr;       // staging of host RGBA images (allocated on first use)
+  bool views_alloc = false;        // best-view records and image slots allocated
+  bool views_push = false;         // some map of the current push picks views
   // whole-view answers (smg_set_object_embeddings): staging of up to M * RE_CAND entries, and the
   // stamp of every map's last keyframe (the stamp the reference gives the whole views)
   int32_t* d_wv_map = nullptr;
@@ -108,7 +112,7 @@ struct smg_batch {
 
 static const char* k_names[SMG_NUM_KERNELS] = {"k_begin", "k_merge_pairs", "k_merge_apply", "k_obs", "k_obs_finalize", "k_assoc",
                                                "k_update", "k_absent", "k_relink", "k_struct", "k_prune", "k_markview",
-                                               "k_cloud_add", "k_grid", "k_reenc", "k_hands"};
+                                               "k_cloud_add", "k_grid", "k_reenc", "k_hands", "k_views"};
 
 static cudaEvent_t ev_get(smg_batch* b) {
   if (b->ev_pool.empty()) {
@@ -600,6 +604,7 @@ __global__ void k_begin(Batch B) {
     R->n_evn = 0;
     R->n_obs = 0;
     R->n_pts = 0;
+    R->n_vnew = 0;
     R->n_targets = 0;
     if (!B.reenc_on) R->re_n = 0;
     B.mcand_n[m] = 0;
@@ -681,6 +686,14 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   k_cloud_add<<<dim3(WORK_SLOTS, Mg), 512, 0, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({12, {e0, e1}}); } }
+  if (b->views_alloc) {   // best views of the keyframe (capi.cpp:903-998); none exist before the first image
+    cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+    k_views_pick<<<Mg, VIEW_THREADS, 0, st>>>(B);
+    if (b->views_push) k_views_crop<<<dim3(B.max_det, Mg), VCROP_THREADS, 0, st>>>(B);
+    b->launches += b->views_push ? 2 : 1;
+    if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after k_views: ") + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } }
+    if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({16, {e0, e1}}); }
+  }
   if (B.reenc_on) { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_reenc<<<dim3(RE_CTAS, Mg), RE_THREADS, RE_SMEM(B), st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
@@ -703,6 +716,23 @@ static double grip_gap(const smg_params& P, double g) {
   return P.grip_gap[n - 1][1];
 }
 
+// Best-view records and image slots, and the RGBA staging of host frames: allocated by the first
+// push that carries an RGBA image (one allocation for the batch's life, not per frame).
+static int views_alloc(smg_batch* b, bool host) {
+  Batch& B = b->B;
+  const size_t MD = (size_t)B.M * B.max_det;
+  if (!b->views_alloc) {
+    if (int r = dalloc(b, &B.vrec, MD)) return r;
+    if (int r = dalloc(b, &B.vrgb, MD * VIEW_PIX * 3)) return r;
+    if (int r = dalloc(b, &B.vdepth, MD * VIEW_PIX)) return r;
+    if (int r = dalloc(b, &B.vmask, MD * VIEW_PIX)) return r;
+    b->views_alloc = true;
+  }
+  if (host && !b->d_rgba)
+    if (int r = dalloc(b, &b->d_rgba, (size_t)B.M * b->max_w * b->max_h * 4)) return r;
+  return SMG_OK;
+}
+
 int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, void* stream) {
   if (!b || !frames || n <= 0 || n > b->B.M || (where != SMG_MEM_DEVICE && where != SMG_MEM_HOST))
     return fail(SMG_ERR_ARGS, "smg_push_frames: bad arguments");
@@ -720,6 +750,12 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     if (f.mask_bits && (f.mask_w <= 0 || f.mask_h <= 0 || f.mask_w > b->max_w || f.mask_h > b->max_h || !(f.mask_sx > 0) ||
                         !(f.mask_sy > 0) || f.img_w < 0 || f.img_h < 0))
       return fail(SMG_ERR_ARGS, "smg_push_frames: bad detection mask grid (mask_w x mask_h <= max_w x max_h, scales > 0)");
+  }
+  {
+    bool any_rgba = false;
+    for (int i = 0; i < n; ++i) any_rgba = any_rgba || frames[i].rgba != nullptr;
+    if (any_rgba)
+      if (int r = views_alloc(b, where == SMG_MEM_HOST)) return r;
   }
   // pinned descriptor ring: wait until the copy that last read this slot has run
   b->dbg_last = 0;
@@ -798,6 +834,11 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
       d.mask_sx = d.mask_sy = 1.f; d.mask_ox = d.mask_oy = 0.f;
     }
     d.mask_words = (int32_t)(((size_t)d.mask_w * d.mask_h + 31) / 32);
+    // RGB source (capi.cpp:916): views and point colours need the detector image to be the image
+    if (f.rgba) {
+      d.rgba = where == SMG_MEM_DEVICE ? f.rgba : b->d_rgba + (size_t)m * WH * 4;
+      d.views_on = d.img_w == f.w && d.img_h == f.h;
+    }
     if (where == SMG_MEM_DEVICE) {
       d.depth = f.depth ? f.depth : b->d_depth + (size_t)m * WH;   // millimetres: converted into staging
       d.depth_mm = f.depth ? nullptr : f.depth_mm;
@@ -857,6 +898,8 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     }
   }
   for (int m = 0; m < n; ++m) b->h_frames[m].hands_on = b->hands_on;
+  b->views_push = false;
+  for (int m = 0; m < n; ++m) b->views_push = b->views_push || b->h_frames[m].views_on;
   // Stream groups: maps [g*M/G, (g+1)*M/G) run their chain on stream g (the caller's stream
   // for g = 0), so the groups' kernels overlap; with host inputs, group g's chain starts as soon
   // as its own inputs have arrived on the copy stream.
@@ -913,6 +956,12 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
         }
         i = j;
       }
+      for (int i = m0; i < m1; ++i)   // RGBA images: whole
+        if (frames[i].rgba) {
+          const size_t bytes = (size_t)frames[i].w * frames[i].h * 4;
+          CK(cudaMemcpyAsync(b->d_rgba + (size_t)i * WH * 4, frames[i].rgba, bytes, cudaMemcpyHostToDevice, b->s_copy));
+          b->h2d_host += (long long)bytes;
+        }
       for (int i = m0; i < m1; ++i)   // detector bit masks: whole planes
         if (frames[i].mask_bits && frames[i].n_det > 0) {
           const size_t bytes = (size_t)frames[i].n_det * b->h_frames[i].mask_words * 4;
@@ -1058,13 +1107,25 @@ int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap) {
   const Batch& B = b->B;
   MapRec R;
   if (int r = read_map(b, m, &R)) return r;
+  const int nr = out ? std::min(R.n_obj, cap) : 0;
+  if (nr <= 0) return R.n_obj;
+  // three copies whatever the object count: the list order, the object records up to the highest
+  // slot in use, and the map's cloud records
   std::vector<int32_t> ord(R.n_obj);
-  if (R.n_obj) CK(cudaMemcpy(ord.data(), B.order + (size_t)m * B.O, sizeof(int32_t) * R.n_obj, cudaMemcpyDeviceToHost));
-  for (int i = 0; i < R.n_obj && i < cap && out; ++i) {
-    ObjRec o;
-    CK(cudaMemcpy(&o, B.objs + (size_t)m * B.O + ord[i], sizeof(ObjRec), cudaMemcpyDeviceToHost));
-    CloudRec c;
-    CK(cudaMemcpy(&c, B.clouds + cglob(B, m, o.cloud_slot), sizeof(CloudRec), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(ord.data(), B.order + (size_t)m * B.O, sizeof(int32_t) * R.n_obj, cudaMemcpyDeviceToHost));
+  int top = 0;
+  for (int i = 0; i < nr; ++i) {
+    if (ord[i] < 0 || ord[i] >= B.O) return fail(SMG_ERR_DEVICE, "smg_get_objects: corrupt object order");
+    top = std::max(top, ord[i] + 1);
+  }
+  std::vector<ObjRec> objs((size_t)top);
+  CK(cudaMemcpy(objs.data(), B.objs + (size_t)m * B.O, sizeof(ObjRec) * top, cudaMemcpyDeviceToHost));
+  std::vector<CloudRec> clouds((size_t)B.C);
+  CK(cudaMemcpy(clouds.data(), B.clouds + cglob(B, m, 0), sizeof(CloudRec) * B.C, cudaMemcpyDeviceToHost));
+  for (int i = 0; i < nr; ++i) {
+    const ObjRec& o = objs[(size_t)ord[i]];
+    if (o.cloud_slot < 0 || o.cloud_slot >= B.C) return fail(SMG_ERR_DEVICE, "smg_get_objects: corrupt cloud slot");
+    const CloudRec& c = clouds[(size_t)o.cloud_slot];
     smg_object& r = out[i];
     memset(&r, 0, sizeof(r));
     r.id = o.id;
@@ -1168,6 +1229,68 @@ int smg_get_object_cloud(smg_batch* b, int m, int i, float* xyz, uint32_t* seq, 
     }
   }
   return c.n;
+}
+
+int smg_get_object_cloud_rgb(smg_batch* b, int m, int i, uint8_t* rgb, int cap) {
+  if (!b || m < 0 || m >= b->B.M) return fail(SMG_ERR_ARGS, "smg_get_object_cloud_rgb: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  if (i < 0 || i >= R.n_obj) return fail(SMG_ERR_ARGS, "smg_get_object_cloud_rgb: bad index");
+  int32_t slot;
+  CK(cudaMemcpy(&slot, B.order + (size_t)m * B.O + i, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  ObjRec o;
+  CK(cudaMemcpy(&o, B.objs + (size_t)m * B.O + slot, sizeof(ObjRec), cudaMemcpyDeviceToHost));
+  const size_t cs = cglob(B, m, o.cloud_slot);
+  CloudRec c;
+  CK(cudaMemcpy(&c, B.clouds + cs, sizeof(CloudRec), cudaMemcpyDeviceToHost));
+  const int n = std::min(cap, c.n);
+  if (n > 0 && rgb) {
+    std::vector<uint32_t> col(n);
+    CK(cudaMemcpy(col.data(), B.crgb + cs * B.cap, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost));
+    for (int k = 0; k < n; ++k)
+      for (int q = 0; q < 3; ++q) rgb[3 * k + q] = (uint8_t)((col[k] >> (8 * q)) & 255u);
+  }
+  return c.n;
+}
+
+int smg_get_views(smg_batch* b, int m, smg_view* out, uint8_t* rgb, uint16_t* depth, uint8_t* mask, int cap) {
+  if (!b || m < 0 || m >= b->B.M || cap < 0) return fail(SMG_ERR_ARGS, "smg_get_views: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  if (!b->views_alloc) return 0;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  const int nv = std::min(R.n_vnew, B.max_det);
+  for (int v = 0; v < nv && v < cap; ++v) {
+    const int k = R.vnew[v];
+    if (k < 0 || k >= B.max_det) return fail(SMG_ERR_DEVICE, "smg_get_views: corrupt view list");
+    const size_t vs = (size_t)m * B.max_det + k;
+    ViewRec V;
+    CK(cudaMemcpy(&V, B.vrec + vs, sizeof(ViewRec), cudaMemcpyDeviceToHost));
+    if (out) {
+      smg_view& o = out[v];
+      memset(&o, 0, sizeof(o));
+      o.id = V.id;
+      o.version = V.version;
+      o.q = V.q;
+      o.stamp = V.stamp;
+      for (int c = 0; c < 4; ++c) { o.box[c] = V.box[c]; o.det_box[c] = V.det_box[c]; }
+      o.mask_area = V.mask_area;
+      o.depth_m = V.depth_m;
+      o.score = V.score;
+      for (int c = 0; c < 12; ++c) o.cam_T[c] = V.cam_T[c];
+      o.w = V.w;
+      o.h = V.h;
+    }
+    const size_t np = (size_t)V.w * V.h;
+    if (np > VIEW_PIX) return fail(SMG_ERR_DEVICE, "smg_get_views: corrupt view size");
+    if (rgb) CK(cudaMemcpy(rgb + (size_t)v * VIEW_PIX * 3, B.vrgb + vs * VIEW_PIX * 3, np * 3, cudaMemcpyDeviceToHost));
+    if (depth) CK(cudaMemcpy(depth + (size_t)v * VIEW_PIX, B.vdepth + vs * VIEW_PIX, np * 2, cudaMemcpyDeviceToHost));
+    if (mask) CK(cudaMemcpy(mask + (size_t)v * VIEW_PIX, B.vmask + vs * VIEW_PIX, np, cudaMemcpyDeviceToHost));
+  }
+  return nv;
 }
 
 int smg_get_assoc(smg_batch* b, int m, uint32_t* obj_id, int32_t* n_valid, float* area_px, float* depth_med, int cap) {
@@ -1704,6 +1827,7 @@ struct smg_assoc {
   float* t_second = nullptr;
   int32_t* t_idx = nullptr;
   int32_t* err = nullptr;
+  int n_sm = 148;
 };
 
 static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
@@ -1753,7 +1877,7 @@ int smg_assoc_create(int max_det, int max_mem, int dim, int dev, smg_assoc** out
   CK(cudaSetDevice(dev));
   smg_assoc* a = new smg_assoc();
   a->dev = dev; a->max_det = max_det; a->max_mem = max_mem; a->dim = dim;
-  const size_t nt = (size_t)(max_mem + AG_BN - 1) / AG_BN;
+  const size_t nt = 2 * ((size_t)(max_mem + AG_BN - 1) / AG_BN);   // tile halves of the persistent kernel
   if (cudaMalloc(&a->t_best, sizeof(float) * max_det * nt) != cudaSuccess ||
       cudaMalloc(&a->t_second, sizeof(float) * max_det * nt) != cudaSuccess ||
       cudaMalloc(&a->t_idx, sizeof(int32_t) * max_det * nt) != cudaSuccess || cudaMalloc(&a->err, sizeof(int32_t)) != cudaSuccess) {
@@ -1762,6 +1886,8 @@ int smg_assoc_create(int max_det, int max_mem, int dim, int dev, smg_assoc** out
   }
   CK(cudaMemset(a->err, 0, sizeof(int32_t)));
   CK(cudaFuncSetAttribute(k_assoc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, AG_SMEM));
+  CK(cudaFuncSetAttribute(k_assoc_gemm_p, cudaFuncAttributeMaxDynamicSharedMemorySize, AP_SMEM));
+  CK(cudaDeviceGetAttribute(&a->n_sm, cudaDevAttrMultiProcessorCount, dev));
   *out = a;
   return SMG_OK;
 }
@@ -1780,15 +1906,22 @@ int smg_assoc_match(smg_assoc* a, const uint16_t* det, const float* det_box, int
   if (int r = encode_rows(&tB, mem, n_mem, a->dim, AG_BN)) return r;
   AssocArgs g;
   memset(&g, 0, sizeof(g));
-  g.n_det = n_det; g.n_mem = n_mem; g.dim = a->dim; g.n_tiles = (n_mem + AG_BN - 1) / AG_BN;
+  const int n_nt = (n_mem + AG_BN - 1) / AG_BN, n_mt = (n_det + AG_BM - 1) / AG_BM;
+  g.n_det = n_det; g.n_mem = n_mem; g.dim = a->dim;
+  g.n_tiles = a->stamping ? n_nt : 2 * n_nt;   // per-row partial results: tiles, or tile halves
   g.det_box = det_box; g.mem_box = mem_box; g.det = det; g.mem = mem;
   g.iou_min = iou_min; g.cos_min = cos_min;
   g.delta = (double)a->dim * std::ldexp(1.0, -22);   // > K * 2^-23 (fp32 accumulation, |z| <= 1.01)
   g.t_best = a->t_best; g.t_second = a->t_second; g.t_idx = a->t_idx;
   g.scores = scores; g.match = match; g.score = score; g.certified = certified; g.err = a->err;
   g.stamps = a->stamping ? a->stamps : nullptr;
-  const dim3 grid(g.n_tiles, (n_det + AG_BM - 1) / AG_BM);
-  k_assoc_gemm<<<grid, AG_THREADS, AG_SMEM, st>>>(tA, tB, g);
+  if (a->stamping || scores) {   // the one-tile kernel: instrumented, or writing the raw scores
+    const dim3 grid(n_nt, n_mt);
+    k_assoc_gemm<<<grid, AG_THREADS, AG_SMEM, st>>>(tA, tB, g);
+  } else {   // persistent: one CTA per SM over all tiles, epilogue overlapped with the next MMAs
+    const int grid = std::min(a->n_sm, n_nt * n_mt);
+    k_assoc_gemm_p<<<grid, AP_THREADS, AP_SMEM, st>>>(tA, tB, g);
+  }
   {   // programmatic dependent launch: the decide grid is scheduled while the GEMM drains
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((n_det + 7) / 8);

@@ -28,6 +28,7 @@
 #define SMG_VIEW_BANDS 5
 #define SMG_SUB 2048          // kPctMax (scenemap objmap.cpp:36)
 #define SMG_MAX_EVENTS 1024   // per map per frame
+#define VIEW_PIX (SMG_VIEW_MAX_SIDE * SMG_VIEW_MAX_SIDE)   // pixels of one best-view image slot
 #define SMG_BINS_MAX 1440
 #define SMG_MATCH_CELLS 12288 // kH * 3 / 4 (scenemap scan.cpp:319, :399)
 #define WORK_SLOTS 16         // per-map work areas (cloud add CTAs per map)
@@ -89,6 +90,10 @@ typedef struct {
   int32_t img_w, img_h;
   float sxu_f, syv_f;
   double sxu_d, syv_d;
+  // sm_image::rgba (w x h RGBA8), device copy, or null; views_on = an RGB source the reference
+  // uses: rgba present and the detector image the size of the depth image (capi.cpp:916)
+  const uint8_t* rgba;
+  int32_t views_on;
 } FrameDev;
 
 // Observation (one detection after back-projection; scenemap objmap.cpp:52-74 `Obs`)
@@ -148,6 +153,9 @@ typedef struct __align__(16) {   // 16-byte aligned: staged in shared memory in 
   int32_t held_by;       // hand holding it, -1 = none
   uint32_t parent;       // id of the object it rests on and follows, 0 = none
   double parent_rel[3], held_rel[3], grasp_pos[3];
+  // best view (capi.cpp ViewSlot: the view's quality; has_view = a view is installed)
+  double view_q;
+  int32_t has_view;
 } ObjRec;
 
 typedef struct {
@@ -231,6 +239,10 @@ typedef struct {
   // whole-object re-encode requests of the last keyframe (k_reenc): count, candidate of each rank
   int32_t re_n, re_done;
   int32_t re_rank[RE_CAND];
+  // best views (capi.cpp:903-998): version counter, views replaced by the last keyframe
+  uint32_t view_ver;
+  int32_t n_vnew;
+  int32_t vnew[SMG_MAX_DET];   // candidate (detection) of each replaced view, install order
 } MapRec;
 
 // Whole-object re-encode candidate of a keyframe (ReencReq, scenemap objmap.hpp:142-148, plus
@@ -244,6 +256,19 @@ typedef struct {
   int32_t mask_w, mask_h;
   int32_t win[4];        // rows r0..r1 and words w0..w1 written to the mask slot (zero elsewhere)
 } ReencRec;
+
+// Best-view candidate of a detection (BestView, bestview.hpp, plus the selection state): the
+// images live at Batch::vrgb / vdepth / vmask, one fixed-size slot per (map, detection).
+typedef struct {
+  uint32_t id, version;
+  int32_t cand;          // a candidate of this keyframe (quality test and crop geometry passed)
+  int32_t final_;        // the view its object keeps after this keyframe
+  double q, stamp;
+  int32_t box[4], det_box[4];
+  float mask_area, depth_m, score;
+  double cam_T[12];
+  int32_t w, h;
+} ViewRec;
 
 // ObjectMap::lastAssoc entry (DetAssoc, objmap.hpp:194-199)
 typedef struct {
@@ -328,6 +353,11 @@ typedef struct {
   struct PairCacheRec* pcache;   // [M * PCACHE_SLOTS] merge-pass pair features of unchanged pairs
   double* sscr;          // [M * STRUCT_CTAS * STRUCT_SCR] k_struct scratch
   struct UpdJob* upd_job;  // [M * max_det] vector jobs of k_update, observation order
+  // best views (allocated on the first push with an RGB image)
+  ViewRec* vrec;         // [M*max_det]
+  uint8_t* vrgb;         // [M*max_det*VIEW_PIX*3]
+  uint16_t* vdepth;      // [M*max_det*VIEW_PIX]
+  uint8_t* vmask;        // [M*max_det*VIEW_PIX]
   int64_t* upd_tg;         // [M * max_det] target objects (global slot) of those jobs
   int32_t* upd_n;          // [M * 2] jobs, targets
   // view-first hash (markView)

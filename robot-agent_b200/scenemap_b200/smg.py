@@ -30,7 +30,16 @@ class SmgFrame(C.Structure):
                 ("score", C.c_void_p), ("emb", C.c_void_p), ("emb_dtype", C.c_int32), ("grip", C.c_float * 2),
                 ("mask_bits", C.c_void_p), ("mask_w", C.c_int32), ("mask_h", C.c_int32), ("mask_sx", C.c_float),
                 ("mask_sy", C.c_float), ("mask_ox", C.c_float), ("mask_oy", C.c_float), ("img_w", C.c_int32),
-                ("img_h", C.c_int32), ("depth_mm", C.c_void_p)]
+                ("img_h", C.c_int32), ("depth_mm", C.c_void_p), ("rgba", C.c_void_p)]
+
+
+class SmgView(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("version", C.c_uint32), ("q", C.c_double), ("stamp", C.c_double),
+                ("box", C.c_int32 * 4), ("det_box", C.c_int32 * 4), ("mask_area", C.c_float), ("depth_m", C.c_float),
+                ("score", C.c_float), ("cam_T", C.c_double * 12), ("w", C.c_int32), ("h", C.c_int32)]
+
+
+VIEW_MAX_SIDE = 256
 
 
 class SmgReencReq(C.Structure):
@@ -73,6 +82,8 @@ def lib():
         L.smg_get_object_vectors.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp, vp, C.c_int]
         L.smg_get_object_cloud.argtypes = [vp, C.c_int, C.c_int, vp, vp, C.c_int]
         L.smg_get_assoc.argtypes = [vp, C.c_int, vp, vp, vp, vp, C.c_int]
+        L.smg_get_object_cloud_rgb.argtypes = [vp, C.c_int, C.c_int, vp, C.c_int]
+        L.smg_get_views.argtypes = [vp, C.c_int, vp, vp, vp, vp, C.c_int]
         L.smg_get_stats.argtypes = [vp, C.c_int, vp]
         L.smg_get_events.argtypes = [vp, C.c_int, vp, vp, vp, C.c_int]
         L.smg_get_grid.argtypes = [vp, C.c_int, vp, vp, vp]
@@ -102,9 +113,10 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
             "smg_kernel_launches", "smg_get_assoc_all", "smg_debug_check", "smg_timing_enable", "smg_timing_read",
            "smg_get_work", "smg_set_reencode", "smg_set_object_embeddings", "smg_get_object_whole", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
-           "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode"]
+           "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode",
+           "smg_get_object_cloud_rgb", "smg_get_views"]
 
-NUM_KERNELS = 16
+NUM_KERNELS = 17
 
 
 def _ptr(a):
@@ -198,7 +210,12 @@ class Batch:
         if ptrs is not None:
             f.depth, f.label, f.emb = ptrs["depth"], ptrs["label"], ptrs["emb"]
             f.mask_bits = ptrs.get("mask_bits")
+            f.rgba = ptrs.get("rgba")
         else:
+            if fr.get("rgba") is not None:
+                rgba = np.ascontiguousarray(fr["rgba"], np.uint8)
+                keep.append(rgba)
+                f.rgba = _ptr(rgba)
             if fr.get("mask_bits") is not None:
                 mb = np.ascontiguousarray(fr["mask_bits"], np.uint32)
                 keep.append(mb)
@@ -258,6 +275,36 @@ class Batch:
         seq = np.zeros(max(n, 1), np.uint32)
         lib().smg_get_object_cloud(self.h, m, i, _ptr(xyz), _ptr(seq), n)
         return xyz[:n], seq[:n]
+
+    def object_cloud_rgb(self, m: int, i: int):
+        n = _check(lib().smg_get_object_cloud_rgb(self.h, m, i, None, 0), "smg_get_object_cloud_rgb")
+        rgb = np.zeros((max(n, 1), 3), np.uint8)
+        lib().smg_get_object_cloud_rgb(self.h, m, i, _ptr(rgb), n)
+        return rgb[:n]
+
+    def views(self, m: int = 0) -> list:
+        """Best views the last keyframe of map m installed (smg_get_views), with their images."""
+        L = lib()
+        cap = self.max_det
+        arr = (SmgView * cap)()
+        S = VIEW_MAX_SIDE * VIEW_MAX_SIDE
+        rgb = np.zeros((cap, S * 3), np.uint8)
+        dep = np.zeros((cap, S), np.uint16)
+        msk = np.zeros((cap, S), np.uint8)
+        n = _check(L.smg_get_views(self.h, m, arr, _ptr(rgb), _ptr(dep), _ptr(msk), cap), "smg_get_views")
+        out = []
+        for v in range(n):
+            o = arr[v]
+            d = {}
+            for name, _ in SmgView._fields_:
+                x = getattr(o, name)
+                d[name] = list(x) if hasattr(x, "__len__") else x
+            w, h = o.w, o.h
+            d["rgb"] = rgb[v, :w * h * 3].reshape(h, w, 3).copy()
+            d["depth"] = dep[v, :w * h].reshape(h, w).copy()
+            d["mask"] = msk[v, :w * h].reshape(h, w).copy()
+            out.append(d)
+        return out
 
     def assoc(self, m: int = 0):
         cap = self.max_det

@@ -92,6 +92,20 @@ def map_seed(base: int, index: int) -> int:
     return z ^ (z >> 31)
 
 
+def rgba_image(label: np.ndarray, depth: np.ndarray) -> np.ndarray:
+    """A colour image for a rendered frame: a base colour per label plus a pixel texture and
+    depth shading, so crops average distinct values (deterministic; alpha 255)."""
+    h, w = label.shape
+    v, u = np.mgrid[0:h, 0:w].astype(np.uint32)
+    lab = label.astype(np.uint32)
+    dq = (np.clip(depth, 0.0, 10.0) * 20.0).astype(np.uint32)
+    r = (lab * 73 + 3 * u + v + dq) & 255
+    g = (lab * 151 + u + 5 * v) & 255
+    b = (lab * 29 + 7 * (u ^ v) + 2 * dq) & 255
+    a = np.full_like(r, 255)
+    return np.stack([r, g, b, a], axis=-1).astype(np.uint8)
+
+
 class BoxRoom:
     """Config 0/1/4 generator: 6x5x2.6 m room, 20 boxes, pinhole camera on a moving base.
 
@@ -105,7 +119,9 @@ class BoxRoom:
                     gripper value per frame (default: far away, open);
       mask_grid     s > 0: detections also carry bit masks on an s-pixel grid (label_masks), the
                     form the reference's detector produces; both sides then read those;
-      depth_mm      depth also as uint16 millimetres (rounded), which both sides then read.
+      depth_mm      depth also as uint16 millimetres (rounded), which both sides then read;
+      rgb           an RGBA colour image registered with the depth (rgba_image), which both sides
+                    use for best views and cloud-point colours.
     """
 
     def __init__(self, seed: int, n_boxes: int = 20, room=(6.0, 5.0, 2.6), noise_k: float = 0.005,
@@ -114,7 +130,7 @@ class BoxRoom:
                  n_frames: int = 300, D: int = 1152, bf16: bool = False, emb_sigma: float = 0.05,
                  min_px: int = 64, max_det: int = 24, cam_height: float = 0.9, pitch_deg: float = 20.0,
                  shell_labels: bool = False, box_moves=(), box_extra=(), hands=None, mask_grid: int = 0,
-                 depth_mm: bool = False):
+                 depth_mm: bool = False, rgb: bool = False):
         L = lib()
         self.seed = seed
         self.scene = SyScene()
@@ -128,7 +144,7 @@ class BoxRoom:
                 self.scene.box[b].hi[k] = hi[k]
             self.scene.n_boxes = b + 1
         self.scene.shell_labels = 1 if shell_labels else 0
-        self.mask_grid, self.depth_mm = mask_grid, depth_mm
+        self.mask_grid, self.depth_mm, self.rgb = mask_grid, depth_mm, rgb
         self.box_moves = sorted(box_moves, key=lambda e: e[0])
         self.hands = hands
         self.cam = SyCamera(w, h, fx, fy, cx, cy)
@@ -188,6 +204,8 @@ class BoxRoom:
             s = self.mask_grid
             extra.update(mask_bits=label_masks(label, det_label[:n], s), mask_w=self.w // s, mask_h=self.h // s,
                          mask_affine=(float(s), float(s), 0.0, 0.0), img_w=self.w, img_h=self.h)
+        if self.rgb:
+            extra["rgba"] = rgba_image(label, depth)
         if self.depth_mm:
             extra["depth_mm"] = np.clip(np.rint(depth * 1000.0), 0, 65535).astype(np.uint16)
         return dict(stamp=f * self.dt, w=self.w, h=self.h, depth=depth, label=label, fx=self.fx, fy=self.fy,

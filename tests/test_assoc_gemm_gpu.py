@@ -110,3 +110,29 @@ def test_near_threshold_and_ties_are_exact():
     assert m[-1] == 300 and c[-1] == 0       # the duplicate tie was resolved exactly
     assert (c[:-1] == 0).sum() > 10          # near-threshold cases took the exact path
     assert A.error() == 0
+
+
+@pytest.mark.parametrize("n_frames", [8, 3])
+def test_frame_batches_match_restatement(n_frames):
+    """Several frames against one bank in one call (their detections as consecutive rows): the
+    persistent kernel's tile walk and double-buffered accumulators give every frame the
+    decisions of the restatement."""
+    if not has_gpu():
+        pytest.skip("no GPU")
+    import torch
+    from oracle import assoc_oracle as ao
+    from scenemap_b200.assoc import AssocGPU, AssocWorkload
+    W = AssocWorkload(seed=5)
+    fr = [W.frame(k) for k in range(n_frames)]
+    z = np.concatenate([f[0] for f in fr])
+    box = np.concatenate([f[1] for f in fr])
+    A = AssocGPU(z.shape[0], W.n_mem, W.dim)
+    m, s, c = A.match(_dev(z, torch, torch.int16), _dev(box, torch), _dev(W.mem, torch, torch.int16), _dev(W.mem_box, torch))
+    torch.cuda.synchronize()
+    m, s = m.cpu().numpy(), s.cpu().numpy()
+    for k in range(n_frames):
+        want_m, want_s, _ = ao.decide(fr[k][0], fr[k][1], W.mem, W.mem_box)
+        sl = slice(k * W.n_det, (k + 1) * W.n_det)
+        assert np.array_equal(m[sl], want_m), f"frame {k}: {np.nonzero(m[sl] != want_m)[0][:10]}"
+        assert np.allclose(s[sl], want_s, rtol=0, atol=1e-12)
+    assert A.error() == 0
