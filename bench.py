@@ -110,7 +110,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="objprob: skip the short config-2 / config-3 runs recorded under extra_workloads")
-    ap.add_argument("--assoc-frames", type=int, default=8,
+    ap.add_argument("--assoc-frames", type=int, default=32,
                     help="config 2: frames per association call (their detections as one row block against the bank)")
     ap.add_argument("--workload", default="objprob", choices=["objprob", "occ", "assoc"],
                     help="objprob = config 1 (headline); occ = config 3 (grid insert + correlative scan matching); "
@@ -137,9 +137,42 @@ def parse():
 
 # ------------------------------------------------------------------ clocks
 class Clocks:
-    def __init__(self, gpu_index: int, path: str):
-        self.path = path
-        self.proc = None
+    """SM clock and clock-event (throttle) reasons sampled while the timed region runs: NVML
+    every 5 ms in a thread (a short timed region still gets samples), else `nvidia-smi -lms 200`
+    into a temporary CSV.  Reading only; nothing is set."""
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
+
+    def __init__(self, gpu_index: int, path: str, torch_dev=None):
+        self.path, self.proc, self.thread = path, None, None
+        self.sm, self.mx, self.bits = [], None, 0
+        self.stop_ev = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = None
+            try:   # the GPU torch runs on, by PCI address (indices differ under CUDA_VISIBLE_DEVICES)
+                import torch
+                pr = torch.cuda.get_device_properties(torch_dev if torch_dev is not None else gpu_index)
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0")
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+            self.mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def run():
+                while not self.stop_ev.is_set():
+                    try:
+                        self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                        self.bits |= int(reasons_fn(h))
+                    except Exception:
+                        pass
+                    self.stop_ev.wait(0.005)
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
@@ -151,6 +184,12 @@ class Clocks:
             self.proc = None
 
     def stop(self) -> dict:
+        if self.thread is not None:
+            self.stop_ev.set()
+            self.thread.join(timeout=5)
+            reasons = sorted(name for bit, name in self.REASONS.items() if self.bits & bit)
+            return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.mx, "reasons": reasons,
+                    "samples": len(self.sm), "source": "nvml, 5 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -172,8 +211,12 @@ class Clocks:
             for name, v in zip(["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"], p[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(name)
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 # ------------------------------------------------------------------ CPU baseline (reference scenemap code)
@@ -277,7 +320,8 @@ def run_b200(args, rank, world, local_rank):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     clk = Clocks(local_rank, os.path.join(tempfile.gettempdir(), f"smg_bench_clocks_{os.getpid()}_r{rank}.csv"))
-    time.sleep(0.3)
+    if clk.thread is None:
+        time.sleep(0.3)   # nvidia-smi's first sample
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for fi in range(args.steps):
@@ -359,15 +403,23 @@ def run_b200(args, rank, world, local_rank):
             h2d += W * H * 6 + d["n"] * 1152 * 2
         e_structs.append(arr)
     h2d //= E
-    d2h = M * args.dets * 16
+    d2h = M * args.dets * 4   # uint32 object id per detection slot
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     h2d_0 = B.work()["h2d"]
+    # pipelined like a streaming caller: push keyframe k + 1 (its host copies overlap keyframe
+    # k's chain) before waiting for keyframe k's association, which every step reads back
+    outs = [torch.empty((M, args.dets), dtype=torch.int32, pin_memory=True) for _ in range(2)]
     t0 = time.perf_counter()
+    prev = None
     for fi in range(E):
         B.push(None, smg.SMG_MEM_HOST, structs=e_structs[fi], stream=sp)
-        B.assoc_all()
+        tk = B.assoc_all_async(outs[fi % 2].data_ptr())
+        if prev is not None:
+            B.wait_read(prev)
+        prev = tk
+    B.wait_read(prev)
     torch.cuda.synchronize()
     t_e2e = time.perf_counter() - t0
     # bytes that crossed to the device: the library counts its copies and the pixels it read in
@@ -730,7 +782,7 @@ def extra_workloads(args, local_rank: int) -> dict:
     import copy
     out = {}
     a2 = copy.copy(args)
-    a2.steps, a2.warmup, a2.no_cpu_baseline, a2.assoc_frames = 30, 3, True, 8
+    a2.steps, a2.warmup, a2.no_cpu_baseline, a2.assoc_frames = 20, 3, True, 32
     try:
         out["config2"] = assoc_line(run_assoc(a2, 0, 1, local_rank), a2, 1)
     except Exception as e:   # recorded, not fatal to the headline line

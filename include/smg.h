@@ -270,6 +270,12 @@ int smg_get_grid(smg_batch* b, int m, int16_t* L, uint8_t* seen, int8_t* c8);
 int smg_get_keyframe(smg_batch* b, int m, int32_t* out3);
 /* Association of all maps in one read: obj_id[m * max_det + k] (0 = no object). */
 int smg_get_assoc_all(smg_batch* b, uint32_t* obj_id);
+/* The same read without waiting, for callers that keep pushes in flight: enqueued on the stream of
+ * the last push, after its keyframe; obj_id should be pinned host memory (the copy is then
+ * asynchronous) and stays the caller's until smg_wait_read(b, *ticket) returns.  At most four
+ * reads are in flight (a fifth waits for the oldest). */
+int smg_get_assoc_all_async(smg_batch* b, uint32_t* obj_id, int64_t* ticket);
+int smg_wait_read(smg_batch* b, int64_t ticket);
 /* Whole-object re-encode request (sm_reenc_req, scenemap include/scenemap.h:407, plus the
  * request's camera and mask grid; ReencReq, objmap.hpp:142-148): object id, crop box in image
  * pixels (x0 y0 x1 y1), the view kappa the whole view will carry, the camera position and

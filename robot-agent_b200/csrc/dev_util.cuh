@@ -11,6 +11,31 @@
 
 #define DEV __device__ __forceinline__
 
+// Phase timing (instrumentation builds only, -DSMG_PHASE_TIMING): thread 0 of a block adds the
+// clock cycles since its previous mark to phase slot i (smg_phase_read).  No-ops otherwise.
+#ifdef SMG_PHASE_TIMING
+__device__ unsigned long long g_phase_cycles[64];
+__device__ unsigned long long g_phase_hits[64];
+#define PHASE_START() long long phase_t_ = clock64()
+#define PHASE_MARK(i)                                                              \
+  do {                                                                             \
+    if (threadIdx.x == 0) {                                                        \
+      const long long n_ = clock64();                                              \
+      atomicAdd(&g_phase_cycles[(i)], (unsigned long long)(n_ - phase_t_));        \
+      atomicAdd(&g_phase_hits[(i)], 1ull);                                         \
+      phase_t_ = n_;                                                               \
+    }                                                                              \
+  } while (0)
+#define PHASE_COUNT(i)                                                             \
+  do {                                                                             \
+    if (threadIdx.x == 0) atomicAdd(&g_phase_hits[(i)], 1ull);                     \
+  } while (0)
+#else
+#define PHASE_START() do { } while (0)
+#define PHASE_MARK(i) do { } while (0)
+#define PHASE_COUNT(i) do { } while (0)
+#endif
+
 // Self-checks (built with -DSMG_CHECKS): an index outside [0, n) records (site, index, bound) of
 // the first failure in smg_chk and the access is skipped.  Without SMG_CHECKS they compile away.
 __device__ unsigned long long smg_chk[3];
@@ -365,6 +390,7 @@ DEV void block_select_multi(const double* const* a, const int* n, const int* kq,
       }
     }
     __syncthreads();
+    PHASE_COUNT(40 + round);   // selection rounds (instrumentation builds)
     if (sh_live == 0) break;
   }
   (void)s;
@@ -547,25 +573,6 @@ DEV double dist3(const double* a, const double* b) {
 
 DEV void set_err(MapRec* m, int bit) { atomicOr(&m->err, bit); }
 
-// Phase timing (instrumentation builds only, -DSMG_PHASE_TIMING): thread 0 of a block adds the
-// clock cycles since its previous mark to phase slot i (smg_phase_read).  No-ops otherwise.
-#ifdef SMG_PHASE_TIMING
-__device__ unsigned long long g_phase_cycles[64];
-__device__ unsigned long long g_phase_hits[64];
-#define PHASE_START() long long phase_t_ = clock64()
-#define PHASE_MARK(i)                                                              \
-  do {                                                                             \
-    if (threadIdx.x == 0) {                                                        \
-      const long long n_ = clock64();                                              \
-      atomicAdd(&g_phase_cycles[(i)], (unsigned long long)(n_ - phase_t_));        \
-      atomicAdd(&g_phase_hits[(i)], 1ull);                                         \
-      phase_t_ = n_;                                                               \
-    }                                                                              \
-  } while (0)
-#else
-#define PHASE_START() do { } while (0)
-#define PHASE_MARK(i) do { } while (0)
-#endif
 
 // global index of cloud slot `slot` of map m (clouds are a pool of B.C slots per map, separate
 // from the B.O object slots)

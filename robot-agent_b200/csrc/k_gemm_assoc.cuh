@@ -394,10 +394,21 @@ __global__ void __launch_bounds__(256) k_assoc_decide(AssocArgs g) {
   if (decided != -2) {
     double s = 0.0;
     if (decided >= 0) {   // fp64 score of the chosen pair (lane-parallel partial sums)
-      const uint16_t* a = g.det + (size_t)d * g.dim;
-      const uint16_t* b = g.mem + (size_t)decided * g.dim;
-      for (int k = lane; k < g.dim; k += 32)
-        s += (double)__uint_as_float((uint32_t)a[k] << 16) * (double)__uint_as_float((uint32_t)b[k] << 16);
+      // 16-byte loads (8 values), all of a lane's issued before its sums (rows are 16-byte
+      // aligned: dim is a multiple of 64)
+      const uint4* a = (const uint4*)(g.det + (size_t)d * g.dim);
+      const uint4* b = (const uint4*)(g.mem + (size_t)decided * g.dim);
+      const int n8 = g.dim >> 3;
+#pragma unroll 4
+      for (int q = lane; q < n8; q += 32) {
+        const uint4 x = a[q], y = b[q];
+        const uint32_t xa[4] = {x.x, x.y, x.z, x.w}, ya[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s += (double)__uint_as_float(xa[e] << 16) * (double)__uint_as_float(ya[e] << 16);
+          s += (double)__uint_as_float(xa[e] & 0xffff0000u) * (double)__uint_as_float(ya[e] & 0xffff0000u);
+        }
+      }
       s = warp_sum_d(s);
     }
     if (lane == 0) { g.match[d] = decided; g.score[d] = s; g.certified[d] = 1; }

@@ -58,6 +58,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   int16_t* SIG = B.sig + (size_t)m * nb;
   int64_t* MK = B.mkey + (size_t)m * B.scan_pmax;
   float4* MV = B.mval + (size_t)m * B.scan_pmax;
+  PHASE_START();
   // 1. base-frame points (scan.cpp:233-251)
   const float ifx = 1.f / F.fx;
   for (int c = tid; c < ng; c += blockDim.x) {
@@ -78,6 +79,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   }
   for (int k = tid; k < nb; k += blockDim.x) { HK[k] = ~0ull; FR[k] = 0.f; }
   __syncthreads();
+  PHASE_MARK(24);   // base-frame points
   // 2. classification (scan.cpp:254-416)
   const float bsc = (float)nb / (2.f * 3.14159274f);
   float ab[2][3], ab2[2];
@@ -136,6 +138,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     MV[c] = make_float4(px, py, ux, uy);
   }
   __syncthreads();
+  PHASE_MARK(25);   // classification
   // 3. match cells: first pixel per key, rank by first pixel, per-cell raster-order sums
   int64_t* HKY = B.mh_key + (size_t)m * MH_SLOTS;
   int32_t* HF = B.mh_first + (size_t)m * MH_SLOTS;
@@ -242,6 +245,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     OUT[4 * r + 3] = nn > 1e-6f ? sny / nn : 0.f;
   }
   __syncthreads();
+  PHASE_MARK(26);   // match cells
   // 4. laser line and free rays in bin order; signature (scan.cpp:427-440)
   const float isc = 1.f / P.grid_res;
   float* HOUT = OUT + 4 * SMG_MATCH_CELLS;
@@ -270,6 +274,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     nf += tf;
   }
   __syncthreads();
+  PHASE_MARK(27);   // laser line, free rays, signature
   // 5. insert policy (mapper2d.cpp:46-72)
   const int th_c = P.change_cells;
   int nd_l = 0;
@@ -296,6 +301,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     sh_n[0] = ncell; sh_n[1] = nh; sh_n[2] = nf;
   }
   __syncthreads();
+  PHASE_MARK(28);   // insert policy
   if (!sh_ins) return;
   // 6. OccGrid::insert (grid.cpp:95-159)
   const double c = F.cos_th, sn = F.sin_th;
@@ -436,4 +442,5 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   if (tid == 0) wk_add(R, SMG_WK_CELLS, applied_l);
   int16_t* ISw = B.ins_sig + (size_t)m * nb;
   for (int k = tid; k < nb; k += blockDim.x) ISw[k] = SIG[k];
+  PHASE_MARK(29);   // insert
 }

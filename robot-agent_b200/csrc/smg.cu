@@ -83,6 +83,17 @@ struct smg_batch {
   uint16_t* d_depth_mm = nullptr;  // staging of host millimetre depth
   uint32_t* d_mask = nullptr;      // staging of host detector bit masks: M x max_det x mask_words_max
   uint8_t* d_rgba = nullptr;       // staging of host RGBA images (allocated on first use)
+  // The staging above is double-buffered: push k fills set k % 2 while the chain of push k - 1
+  // still reads the other set, so a push's host-to-device copies overlap the previous chain.
+  // ev_set[s] marks the end of the last chain that read set s.
+  int stage_set = 0;
+  cudaEvent_t ev_set[2] = {nullptr, nullptr};
+  FrameDev* frames_base = nullptr;   // device descriptors: set s at frames_base + s * M
+  // asynchronous association reads (smg_get_assoc_all_async): a ring of device buffers + events
+  static const int kReads = 4;
+  uint32_t* d_aids = nullptr;        // kReads x M x max_det
+  cudaEvent_t ev_rd[4] = {nullptr, nullptr, nullptr, nullptr};
+  long long n_reads = 0;
   bool views_alloc = false;        // best-view records and image slots allocated
   bool views_push = false;         // some map of the current push picks views
   // whole-view answers (smg_set_object_embeddings): staging of up to M * RE_CAND entries, and the
@@ -310,7 +321,8 @@ int smg_destroy(smg_batch* b) {
     for (cudaEvent_t e : {b->ev_fork[g], b->ev_join[g], b->ev_copied[g], b->ev_gdone[g], b->ev_dma[g]}) if (e) cudaEventDestroy(e);
     for (cudaStream_t q : {b->s_grp[g], b->s_gridg[g]}) if (q) cudaStreamDestroy(q);
   }
-  for (cudaEvent_t e : {b->ev_up, b->ev_done}) if (e) cudaEventDestroy(e);
+  for (cudaEvent_t e : {b->ev_up, b->ev_done, b->ev_set[0], b->ev_set[1], b->ev_rd[0], b->ev_rd[1], b->ev_rd[2], b->ev_rd[3]})
+    if (e) cudaEventDestroy(e);
   if (b->s_copy) cudaStreamDestroy(b->s_copy);
   if (b->s_dma) cudaStreamDestroy(b->s_dma);
   delete b;
@@ -395,7 +407,8 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
   B.lut_off = -B.q_min;
   const size_t MO = (size_t)M * O;
   DA(B.maps, M);
-  DA(B.frames, M);
+  DA(B.frames, 2 * (size_t)M);   // two descriptor sets, alternating with the staging sets
+  b->frames_base = B.frames;
   DA(B.objs, MO);
   DA(B.order, MO);
   DA(B.freel, MO);
@@ -475,10 +488,10 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
   DA(B.mcell_pix, (size_t)M * B.scan_pmax);
   DA(B.sc_pts, (size_t)M * (2 * SMG_BINS_MAX + SMG_MATCH_CELLS) * 4);
   DA(B.work, (size_t)M * WORK_SLOTS * B.work_stride);
-  DA(b->d_depth, (size_t)M * max_w * max_h);
-  DA(b->d_label, (size_t)M * max_w * max_h);
-  DA(b->d_emb, (size_t)M * max_det * D * 4);
-  DA(b->d_depth_mm, (size_t)M * max_w * max_h);
+  DA(b->d_depth, 2 * (size_t)M * max_w * max_h);
+  DA(b->d_label, 2 * (size_t)M * max_w * max_h);
+  DA(b->d_emb, 2 * (size_t)M * max_det * D * 4);
+  DA(b->d_depth_mm, 2 * (size_t)M * max_w * max_h);
   DA(b->d_wv_map, (size_t)M * RE_CAND);
   DA(b->d_wv_id, (size_t)M * RE_CAND);
   DA(b->d_wv_emb, (size_t)M * RE_CAND * D);
@@ -486,7 +499,7 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
   DA(B.rwhole, MO * D);
   b->last_stamp.assign(M, 0.0);
   b->mask_words_max = ((size_t)max_w * max_h + 31) / 32;
-  DA(b->d_mask, (size_t)M * max_det * b->mask_words_max);
+  DA(b->d_mask, 2 * (size_t)M * max_det * b->mask_words_max);
   // host-side initial state
   {
     std::vector<MapRec> maps((size_t)M);
@@ -555,6 +568,10 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
     CK(cudaEventCreateWithFlags(&b->ev_up, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&b->ev_done, cudaEventDisableTiming));
     CK(cudaEventRecord(b->ev_done, 0));
+    for (int s2 = 0; s2 < 2; ++s2) {
+      CK(cudaEventCreateWithFlags(&b->ev_set[s2], cudaEventDisableTiming));
+      CK(cudaEventRecord(b->ev_set[s2], 0));
+    }
   }
   b->last_cam_t.assign(M, -1e300);
   b->last_cam_fwd.assign(3 * (size_t)M, 0.0);
@@ -729,7 +746,7 @@ static int views_alloc(smg_batch* b, bool host) {
     b->views_alloc = true;
   }
   if (host && !b->d_rgba)
-    if (int r = dalloc(b, &b->d_rgba, (size_t)B.M * b->max_w * b->max_h * 4)) return r;
+    if (int r = dalloc(b, &b->d_rgba, 2 * (size_t)B.M * b->max_w * b->max_h * 4)) return r;
   return SMG_OK;
 }
 
@@ -764,6 +781,15 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   b->h_frames = b->h_ring + (size_t)slot * B.M;
   const size_t WH = (size_t)b->max_w * b->max_h;
   size_t emb_off = 0;   // host embeddings are staged packed, frame after frame
+  // this push's staging set (the other one may still be read by the previous chain)
+  const int ss = b->stage_set;
+  b->stage_set ^= 1;
+  float* sd_depth = b->d_depth + (size_t)ss * B.M * WH;
+  uint16_t* sd_label = b->d_label + (size_t)ss * B.M * WH;
+  unsigned char* sd_emb = b->d_emb + (size_t)ss * B.M * B.max_det * B.D * 4;
+  uint16_t* sd_depth_mm = b->d_depth_mm + (size_t)ss * B.M * WH;
+  uint32_t* sd_mask = b->d_mask + (size_t)ss * B.M * B.max_det * b->mask_words_max;
+  uint8_t* sd_rgba = b->d_rgba ? b->d_rgba + (size_t)ss * B.M * WH * 4 : nullptr;
   // Host frames in pinned (device-accessible) memory are read in place: k_gather fetches only
   // the pixels the chain reads.  Any other host memory goes through whole-frame copies.
   bool gather = where == SMG_MEM_HOST && b->host_gather && b->max_w <= GATHER_WMAX;
@@ -836,26 +862,26 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     d.mask_words = (int32_t)(((size_t)d.mask_w * d.mask_h + 31) / 32);
     // RGB source (capi.cpp:916): views and point colours need the detector image to be the image
     if (f.rgba) {
-      d.rgba = where == SMG_MEM_DEVICE ? f.rgba : b->d_rgba + (size_t)m * WH * 4;
+      d.rgba = where == SMG_MEM_DEVICE ? f.rgba : sd_rgba + (size_t)m * WH * 4;
       d.views_on = d.img_w == f.w && d.img_h == f.h;
     }
     if (where == SMG_MEM_DEVICE) {
-      d.depth = f.depth ? f.depth : b->d_depth + (size_t)m * WH;   // millimetres: converted into staging
+      d.depth = f.depth ? f.depth : sd_depth + (size_t)m * WH;   // millimetres: converted into staging
       d.depth_mm = f.depth ? nullptr : f.depth_mm;
       d.label = f.label;
       d.emb = f.emb;
       d.mask_bits = f.n_det > 0 ? f.mask_bits : nullptr;
     } else {
-      d.depth = b->d_depth + (size_t)m * WH;
-      d.depth_mm = f.depth ? nullptr : b->d_depth_mm + (size_t)m * WH;
-      d.label = b->d_label + (size_t)m * WH;
+      d.depth = sd_depth + (size_t)m * WH;
+      d.depth_mm = f.depth ? nullptr : sd_depth_mm + (size_t)m * WH;
+      d.label = sd_label + (size_t)m * WH;
       if (gather) {
         d.depth_host = (const float*)dh[2 * m];
         d.label_host = (const uint16_t*)dh[2 * m + 1];
       }
-      d.emb = f.emb && f.n_det > 0 ? (const void*)(b->d_emb + emb_off) : nullptr;
+      d.emb = f.emb && f.n_det > 0 ? (const void*)(sd_emb + emb_off) : nullptr;
       if (d.emb) emb_off += (size_t)f.n_det * B.D * (f.emb_dtype == SMG_EMB_BF16 ? 2 : 4);
-      d.mask_bits = f.mask_bits && f.n_det > 0 ? b->d_mask + (size_t)m * B.max_det * b->mask_words_max : nullptr;
+      d.mask_bits = f.mask_bits && f.n_det > 0 ? sd_mask + (size_t)m * B.max_det * b->mask_words_max : nullptr;
     }
     // host-libm scalars (objmap.cpp:520-531, bestview.cpp:77-81, grid.cpp:202)
     const double* T = f.T_mc;
@@ -905,18 +931,22 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   // as its own inputs have arrived on the copy stream.
   const int G = (b->timing || b->dbg_sync) ? 1 : std::max(1, std::min(b->groups, B.M));
   auto gbeg = [&](int g) { return (int)((long long)B.M * g / G); };
-  CK(cudaMemcpyAsync(B.frames, b->h_frames, sizeof(FrameDev) * B.M, cudaMemcpyHostToDevice, st));
+  // this push's descriptors go to the set its staging uses, on the copy stream, once the last
+  // chain that read that set has finished (the previous chain may still be running)
+  B.frames = b->frames_base + (size_t)ss * B.M;
+  CK(cudaStreamWaitEvent(b->s_copy, b->ev_set[ss], 0));
+  CK(cudaMemcpyAsync(B.frames, b->h_frames, sizeof(FrameDev) * B.M, cudaMemcpyHostToDevice, b->s_copy));
   if (where == SMG_MEM_HOST) b->h2d_host += (long long)(sizeof(FrameDev) * B.M);
-  CK(cudaEventRecord(b->ring_ev[slot], st));
+  CK(cudaEventRecord(b->ring_ev[slot], b->s_copy));
   b->ring_used[slot] = true;
-  CK(cudaEventRecord(b->ev_up, st));
+  CK(cudaEventRecord(b->ev_up, b->s_copy));
   if (where == SMG_MEM_HOST) {
     // the staging buffers are free once the previous chain is done; the gather reads the
     // descriptors uploaded above
-    CK(cudaStreamWaitEvent(b->s_copy, b->ev_done, 0));
+    CK(cudaStreamWaitEvent(b->s_copy, b->ev_set[ss], 0));
     if (gather) {
       CK(cudaStreamWaitEvent(b->s_copy, b->ev_up, 0));
-      CK(cudaStreamWaitEvent(b->s_dma, b->ev_done, 0));
+      CK(cudaStreamWaitEvent(b->s_dma, b->ev_set[ss], 0));
     }
     // in gather mode the copy engines move the embeddings and the whole sample rows (makeScan's
     // rows v = j * step, markView's rows v = stp/2 + j * stp) on s_dma, beside the SMs' gather
@@ -926,7 +956,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
       const size_t spitch = (size_t)pitch * w * 4;
       const size_t nrow = j - i > 1 ? (size_t)(j - i) * h / pitch : (size_t)(h - first + pitch - 1) / pitch;
       if (nrow == 0) return 0;
-      CK(cudaMemcpy2DAsync(b->d_depth + i * WH + (size_t)first * w, spitch, frames[i].depth + (size_t)first * w, spitch,
+      CK(cudaMemcpy2DAsync(sd_depth + i * WH + (size_t)first * w, spitch, frames[i].depth + (size_t)first * w, spitch,
                            (size_t)w * 4, nrow, cudaMemcpyHostToDevice, sdma));
       b->h2d_host += (long long)(nrow * w * 4);
       return 0;
@@ -943,15 +973,15 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
           ++j;
         const size_t run = j - i > 1 ? (size_t)(j - i) * WH : pi;
         if (frames[i].depth) {
-          CK(cudaMemcpyAsync(b->d_depth + i * WH, frames[i].depth, run * 4, cudaMemcpyHostToDevice, b->s_copy));
+          CK(cudaMemcpyAsync(sd_depth + i * WH, frames[i].depth, run * 4, cudaMemcpyHostToDevice, b->s_copy));
           b->h2d_host += (long long)run * 4;
         } else {   // millimetres: staged, converted below
-          CK(cudaMemcpyAsync(b->d_depth_mm + i * WH, frames[i].depth_mm, pi * 2, cudaMemcpyHostToDevice, b->s_copy));
+          CK(cudaMemcpyAsync(sd_depth_mm + i * WH, frames[i].depth_mm, pi * 2, cudaMemcpyHostToDevice, b->s_copy));
           b->h2d_host += (long long)pi * 2;
           j = i + 1;
         }
         if (frames[i].label && !frames[i].mask_bits) {
-          CK(cudaMemcpyAsync(b->d_label + i * WH, frames[i].label, run * 2, cudaMemcpyHostToDevice, b->s_copy));
+          CK(cudaMemcpyAsync(sd_label + i * WH, frames[i].label, run * 2, cudaMemcpyHostToDevice, b->s_copy));
           b->h2d_host += (long long)run * 2;
         }
         i = j;
@@ -959,13 +989,13 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
       for (int i = m0; i < m1; ++i)   // RGBA images: whole
         if (frames[i].rgba) {
           const size_t bytes = (size_t)frames[i].w * frames[i].h * 4;
-          CK(cudaMemcpyAsync(b->d_rgba + (size_t)i * WH * 4, frames[i].rgba, bytes, cudaMemcpyHostToDevice, b->s_copy));
+          CK(cudaMemcpyAsync(sd_rgba + (size_t)i * WH * 4, frames[i].rgba, bytes, cudaMemcpyHostToDevice, b->s_copy));
           b->h2d_host += (long long)bytes;
         }
       for (int i = m0; i < m1; ++i)   // detector bit masks: whole planes
         if (frames[i].mask_bits && frames[i].n_det > 0) {
           const size_t bytes = (size_t)frames[i].n_det * b->h_frames[i].mask_words * 4;
-          CK(cudaMemcpyAsync(b->d_mask + (size_t)i * B.max_det * b->mask_words_max, frames[i].mask_bits, bytes,
+          CK(cudaMemcpyAsync(sd_mask + (size_t)i * B.max_det * b->mask_words_max, frames[i].mask_bits, bytes,
                              cudaMemcpyHostToDevice, b->s_copy));
           b->h2d_host += (long long)bytes;
         }
@@ -1020,6 +1050,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     bool any = false;
     for (int i = 0; i < n; ++i) any = any || !frames[i].depth;
     if (any) {
+      CK(cudaStreamWaitEvent(st, b->ev_up, 0));
       k_depth_mm<<<dim3(64, n), 256, 0, st>>>(B);
       b->launches += 1;
       CK(cudaEventRecord(b->ev_up, st));
@@ -1030,7 +1061,8 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     Bg.map0 = gbeg(g);
     const int Mg = gbeg(g + 1) - gbeg(g);
     cudaStream_t sg = g == 0 ? st : b->s_grp[g];
-    if (g > 0) CK(cudaStreamWaitEvent(sg, b->ev_up, 0));
+    CK(cudaStreamWaitEvent(sg, b->ev_up, 0));   // the descriptors (and staging conversions) are in place
+    CK(cudaStreamWaitEvent(sg, b->ev_done, 0));   // the previous chain (or whole-view answers) has run
     if (where == SMG_MEM_HOST) CK(cudaStreamWaitEvent(sg, b->ev_copied[g], 0));
     if (gather) CK(cudaStreamWaitEvent(sg, b->ev_dma[g], 0));
     if (Mg > 0)
@@ -1041,6 +1073,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     }
   }
   CK(cudaEventRecord(b->ev_done, st));
+  CK(cudaEventRecord(b->ev_set[ss], st));   // the staging set is free again after this chain
   CK(cudaGetLastError());
   return SMG_OK;
 }
@@ -1368,6 +1401,38 @@ int smg_debug_check(smg_batch* b, uint64_t* out3) {
   unsigned long long h[3];
   CK(cudaMemcpyFromSymbol(h, smg_chk, sizeof h));
   for (int k = 0; k < 3; ++k) out3[k] = h[k];
+  return SMG_OK;
+}
+
+__global__ void k_assoc_ids(const AssocRec* a, uint32_t* out, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = a[i].obj_id;
+}
+
+int smg_get_assoc_all_async(smg_batch* b, uint32_t* obj_id, int64_t* ticket) {
+  if (!b || !obj_id || !ticket) return fail(SMG_ERR_ARGS, "smg_get_assoc_all_async: bad arguments");
+  const Batch& B = b->B;
+  CK(cudaSetDevice(b->dev));
+  const size_t n = (size_t)B.M * B.max_det;
+  if (!b->d_aids) {
+    if (int r = dalloc(b, &b->d_aids, smg_batch::kReads * n)) return r;
+    for (int i = 0; i < smg_batch::kReads; ++i) CK(cudaEventCreateWithFlags(&b->ev_rd[i], cudaEventDisableTiming));
+  }
+  const int slot = (int)(b->n_reads % smg_batch::kReads);
+  if (b->n_reads >= smg_batch::kReads) CK(cudaEventSynchronize(b->ev_rd[slot]));   // the slot's last read is done
+  uint32_t* d = b->d_aids + (size_t)slot * n;
+  cudaStream_t st = b->last_stream;
+  k_assoc_ids<<<(int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, st>>>(B.assoc, d, (int)n);
+  CK(cudaMemcpyAsync(obj_id, d, n * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+  CK(cudaEventRecord(b->ev_rd[slot], st));
+  *ticket = b->n_reads++;
+  return SMG_OK;
+}
+
+int smg_wait_read(smg_batch* b, int64_t ticket) {
+  if (!b || ticket < 0 || ticket >= b->n_reads) return fail(SMG_ERR_ARGS, "smg_wait_read: bad ticket");
+  if (ticket < b->n_reads - smg_batch::kReads) return SMG_OK;   // long done: its slot was reused after it
+  CK(cudaSetDevice(b->dev));
+  CK(cudaEventSynchronize(b->ev_rd[ticket % smg_batch::kReads]));
   return SMG_OK;
 }
 
@@ -2170,7 +2235,7 @@ int smg_set_object_embeddings(smg_batch* b, const int32_t* maps, const uint32_t*
   k_whole_views<<<B.M, 256, 0, st>>>(B, dm, di, de, n, b->d_wv_stamp);
   b->launches += 1;
   CK(cudaGetLastError());
-  CK(cudaEventRecord(b->ev_done, st));   // later pushes (and the staging) wait for the answers
+  CK(cudaEventRecord(b->ev_done, st));   // the next push's chain waits for the answers
   b->last_stream = st;
   if (where == SMG_MEM_HOST) CK(cudaStreamSynchronize(st));   // the host arrays may go away after the call
   return SMG_OK;

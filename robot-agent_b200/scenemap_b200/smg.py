@@ -84,6 +84,8 @@ def lib():
         L.smg_get_assoc.argtypes = [vp, C.c_int, vp, vp, vp, vp, C.c_int]
         L.smg_get_object_cloud_rgb.argtypes = [vp, C.c_int, C.c_int, vp, C.c_int]
         L.smg_get_views.argtypes = [vp, C.c_int, vp, vp, vp, vp, C.c_int]
+        L.smg_get_assoc_all_async.argtypes = [vp, vp, C.POINTER(C.c_int64)]
+        L.smg_wait_read.argtypes = [vp, C.c_int64]
         L.smg_get_stats.argtypes = [vp, C.c_int, vp]
         L.smg_get_events.argtypes = [vp, C.c_int, vp, vp, vp, C.c_int]
         L.smg_get_grid.argtypes = [vp, C.c_int, vp, vp, vp]
@@ -114,7 +116,7 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
            "smg_get_work", "smg_set_reencode", "smg_set_object_embeddings", "smg_get_object_whole", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
            "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode",
-           "smg_get_object_cloud_rgb", "smg_get_views"]
+           "smg_get_object_cloud_rgb", "smg_get_views", "smg_get_assoc_all_async", "smg_wait_read"]
 
 NUM_KERNELS = 17
 
@@ -362,6 +364,16 @@ class Batch:
         out = np.zeros(self.n_maps * self.max_det, np.uint32)
         _check(lib().smg_get_assoc_all(self.h, _ptr(out)), "smg_get_assoc_all")
         return out.reshape(self.n_maps, self.max_det)
+
+    def assoc_all_async(self, out_ptr: int) -> int:
+        """Enqueue the read of every map's association into host memory at out_ptr (n_maps x
+        max_det uint32, pinned for an asynchronous copy); returns a ticket for wait_read."""
+        t = C.c_int64(0)
+        _check(lib().smg_get_assoc_all_async(self.h, C.c_void_p(out_ptr), C.byref(t)), "smg_get_assoc_all_async")
+        return t.value
+
+    def wait_read(self, ticket: int) -> None:
+        _check(lib().smg_wait_read(self.h, ticket), "smg_wait_read")
 
     def set_object_embeddings(self, maps, ids, emb, stream: int = 0):
         """Whole-object embeddings answering the last keyframe's re-encode requests (host arrays)."""
