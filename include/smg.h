@@ -101,6 +101,14 @@ typedef struct smg_params {
   double grasp_max_w, grasp_min_gap, grasp_w_tol, grip_settle_s, grip_settle_eps;
   int32_t n_grip_gap;
   double grip_gap[8][2];
+  /* ApParams text-model rules (objprob.hpp:84-136): naming (name_tau, name_wmax, size_w,
+   * whole_w, geo_w), the structure guards of association and merging (struct_look_block,
+   * flat_max_w), the small-wall-plane rules (wall_big, struct_p) and the structural-object
+   * size checks (so_*, wallhug_*, big_vinl).  They act only with a text model
+   * (smg_set_text_model). */
+  double name_tau, name_wmax, size_w, whole_w, geo_w, flat_max_w, wall_big, struct_p;
+  double so_dw_w, so_dw_thick, so_max_h, so_pillar, so_stairs, so_dw_min, so_hide_k, wallhug_frac, wallhug_w, big_vinl;
+  int32_t struct_look_block, so_min_obs;
 } smg_params;
 
 /* One frame of one map.  depth/label/emb/dets/masks live in device memory (SMG_MEM_DEVICE) or
@@ -199,6 +207,40 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
  * caller that never encodes whole-object crops can switch the stage off.  With it off,
  * smg_get_reencode returns no requests. */
 int smg_set_reencode(smg_batch* b, int on);
+
+/* ApText (scenemap objprob.hpp:40-54), device pointers (host pointers for smg_set_text_model): rows x dim L2-normalised text
+ * embeddings, the label of each row, SigLIP logit scale/bias, and the optional per-label
+ * log prior, log-size Gaussian (mu, sd; sd <= 0 = unused) and hypernym parent (-1 = none). */
+typedef struct smg_text {
+  int32_t dim, n_labels, rows;
+  const float* text;
+  const int32_t* row_label;
+  float scale, bias;
+  const float* log_prior;
+  const float* ls_mu;
+  const float* ls_sd;
+  const int32_t* parent;
+  int32_t object_label;
+} smg_text;
+/* The text model of every map of the batch (ObjectMap::setTextModel and setClassKinds; the
+ * reference sets them through sm_set_labels, sm_set_text_model and sm_set_label_stats,
+ * scenemap.h:396-401, capi.cpp:1769-1806).  With it, each observation's label likelihood
+ * (apLabelLogLik) gives its structure probabilities for the structural rules and the
+ * association guards (objmap.cpp:547-622, :785-800), every view adds to the object's label
+ * evidence (apAddView), and objects seen in a keyframe, merged objects and objects with a new
+ * whole view are renamed (apRename -> apName: posterior, name, class), which the merge pass,
+ * the structural-object test and isBig then read.  t: the text rows and label statistics
+ * (host arrays, copied; rows may be 0 for class kinds alone); per label, host arrays of
+ * t->n_labels bytes (NULL = all 0): kinds (0 object, 1 structure, 2 static, 3 structural
+ * object: door / window / stairs / pillar), so_shape (1 door or window, 2 stairs or railing,
+ * 3 pillar, 0 other: what capi.cpp:1778-1784 derives from the label names) and flat_ok
+ * (wall-mounted flat objects: picture, TV, clock ..., capi.cpp:1774-1777).  Call it before the
+ * first push; n_labels <= 1024 and dim = the batch's emb_dim when rows > 0. */
+int smg_set_text_model(smg_batch* b, const smg_text* t, const uint8_t* kinds, const uint8_t* so_shape, const uint8_t* flat_ok);
+/* The name state of object i of map m (ApState after apName): post (n_labels floats, zeros when
+ * the object has none yet), lab3 = {name_lab, top_lab, rolled}, val3 = {name_p, top_p, name_H};
+ * returns n_labels when the object has a posterior, else 0. */
+int smg_get_object_name(smg_batch* b, int m, int i, float* post, int32_t* lab3, float* val3);
 
 /* ---- results (device -> host on request; each getter synchronises the batch stream) ---- */
 /* A best view (scenemap include/scenemap/bestview.hpp BestView; chosen as capi.cpp:903-998
@@ -389,20 +431,6 @@ int smg_occ_track(smg_occ* o, const smg_scan2* scans, const double* pose0, const
 int smg_occ_get_cells(smg_occ* o, int m, int16_t* L, uint8_t* seen, int8_t* c8, uint16_t* q);
 
 /* ---- text model: label log-likelihoods and names ---- */
-/* ApText (scenemap objprob.hpp:40-54), device pointers: rows x dim L2-normalised text
- * embeddings, the label of each row, SigLIP logit scale/bias, and the optional per-label
- * log prior, log-size Gaussian (mu, sd; sd <= 0 = unused) and hypernym parent (-1 = none). */
-typedef struct smg_text {
-  int32_t dim, n_labels, rows;
-  const float* text;
-  const int32_t* row_label;
-  float scale, bias;
-  const float* log_prior;
-  const float* ls_mu;
-  const float* ls_sd;
-  const int32_t* parent;
-  int32_t object_label;
-} smg_text;
 /* apLabelLogLik (objprob.cpp:287-310) for n embeddings z (n x dim, device): out (n x n_labels,
  * device) = per-label log sigma(scale * max row cosine + bias), normalised over the labels;
  * labels without a text row get -1e30.  n_labels <= 1024.  Asynchronous on `stream`. */

@@ -86,6 +86,10 @@ def ref_lib():
                                          P(C.c_double), C.c_int]
         L.ref_object_cloud.argtypes = [C.c_void_p, C.c_int, P(C.c_float), P(C.c_uint32), C.c_int]
         L.ref_object_cloud_rgb.argtypes = [C.c_void_p, C.c_int, P(C.c_uint8), C.c_int]
+        L.ref_set_text_model.argtypes = [C.c_void_p, P(C.c_float), P(C.c_int32), C.c_int, C.c_int, C.c_float, C.c_float, C.c_int,
+                                         P(C.c_float), P(C.c_float), P(C.c_float), P(C.c_int32), C.c_int, P(C.c_uint8),
+                                         P(C.c_uint8), P(C.c_uint8)]
+        L.ref_object_name.argtypes = [C.c_void_p, C.c_int, P(C.c_float), C.c_int, P(C.c_int32), P(C.c_float)]
         L.ref_views.argtypes = [C.c_void_p, P(RfView), P(C.c_uint8), P(C.c_uint16), P(C.c_uint8), C.c_int]
         L.ref_assoc.argtypes = [C.c_void_p, P(C.c_uint32), P(C.c_int32), P(C.c_float), P(C.c_float), C.c_int]
         L.ref_n_points.argtypes = [C.c_void_p]
@@ -252,6 +256,29 @@ class RefMap:
         seq = np.zeros(max(n, 1), np.uint32)
         L.ref_object_cloud(self._h, i, _p(xyz, C.c_float), _p(seq, C.c_uint32), n)
         return xyz[:n], seq[:n]
+
+    def set_text_model(self, t: dict) -> None:
+        """ObjectMap::setTextModel + setClassKinds from a synth.text_model dict."""
+        self._text = {k: (np.ascontiguousarray(v) if isinstance(v, np.ndarray) else v) for k, v in t.items()}
+        x = self._text
+        rows = x["text"].shape[0]
+        dim = x["text"].shape[1] if rows else 0
+        opt = lambda k, ct: _p(x[k], ct) if x.get(k) is not None else None
+        rc = ref_lib().ref_set_text_model(self._h, _p(x["text"], C.c_float), _p(x["row_label"], C.c_int32), rows, dim, x["scale"],
+                                          x["bias"], x["n_labels"], opt("log_prior", C.c_float), opt("ls_mu", C.c_float),
+                                          opt("ls_sd", C.c_float), opt("parent", C.c_int32), x["object_label"],
+                                          opt("kinds", C.c_uint8), opt("so_shape", C.c_uint8), opt("flat_ok", C.c_uint8))
+        assert rc == 0
+        self._nlab = x["n_labels"]
+
+    def object_name(self, i: int) -> dict:
+        n = self._nlab
+        post = np.zeros(n, np.float32)
+        lab = np.zeros(3, np.int32)
+        val = np.zeros(3, np.float32)
+        k = ref_lib().ref_object_name(self._h, i, _p(post, C.c_float), n, _p(lab, C.c_int32), _p(val, C.c_float))
+        return dict(has_post=k > 0, post=post, name_lab=int(lab[0]), top_lab=int(lab[1]), rolled=int(lab[2]), name_p=float(val[0]),
+                    top_p=float(val[1]), name_H=float(val[2]))
 
     def object_cloud_rgb(self, i: int):
         L = ref_lib()

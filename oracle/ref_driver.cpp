@@ -450,6 +450,46 @@ int ref_object_cloud(void* h, int i, float* xyz, uint32_t* seq, int cap) {
   return int(pts.size());
 }
 
+// Text model and class kinds (ObjectMap::setTextModel, setClassKinds; what sm_set_labels,
+// sm_set_text_model and sm_set_label_stats install, capi.cpp:1769-1806).  Per-label arrays may be
+// null; so_shape and flat_ok are the tables the glue derives from label names.
+int ref_set_text_model(void* h, const float* text, const int32_t* row_label, int rows, int dim, float scale, float bias, int n_labels,
+                       const float* log_prior, const float* ls_mu, const float* ls_sd, const int32_t* parent, int object_label,
+                       const uint8_t* kinds, const uint8_t* so_shape, const uint8_t* flat_ok) {
+  RefMap* m = static_cast<RefMap*>(h);
+  if (!m || n_labels <= 0 || rows < 0) return -1;
+  ApText t;
+  t.dim = rows > 0 ? dim : 0;
+  if (rows > 0) {
+    t.text.assign(text, text + size_t(rows) * dim);
+    t.row_label.assign(row_label, row_label + rows);
+  }
+  t.scale = scale;
+  t.bias = bias;
+  t.n_labels = n_labels;
+  if (log_prior) t.log_prior.assign(log_prior, log_prior + n_labels);
+  if (ls_mu && ls_sd) { t.ls_mu.assign(ls_mu, ls_mu + n_labels); t.ls_sd.assign(ls_sd, ls_sd + n_labels); }
+  if (parent) t.parent.assign(parent, parent + n_labels);
+  t.object_label = object_label;
+  if (so_shape) t.so_shape.assign(so_shape, so_shape + n_labels);
+  if (flat_ok) t.flat_ok.assign(flat_ok, flat_ok + n_labels);
+  m->om.setTextModel(std::move(t));
+  if (kinds) m->om.setClassKinds(std::vector<uint8_t>(kinds, kinds + n_labels));
+  return 0;
+}
+
+// Name state of object i: post (n_labels floats; zeros when empty), lab3 = name_lab, top_lab,
+// rolled; val3 = name_p, top_p, name_H.  Returns the post size.
+int ref_object_name(void* h, int i, float* post, int n_labels, int32_t* lab3, float* val3) {
+  const auto& objs = static_cast<RefMap*>(h)->om.objects();
+  if (i < 0 || size_t(i) >= objs.size() || !objs[size_t(i)].ap) return -1;
+  const ApState& s = *objs[size_t(i)].ap;
+  for (int c = 0; c < n_labels && post; ++c) post[c] = size_t(c) < s.post.size() ? s.post[size_t(c)] : 0.f;
+  if (lab3) { lab3[0] = s.name_lab; lab3[1] = s.top_lab; lab3[2] = s.rolled; }
+  if (val3) { val3[0] = s.name_p; val3[1] = s.top_p; val3[2] = s.name_H; }
+  return int(s.post.size());
+}
+
 // Cloud colours of object i (3 bytes a point, the order of ref_object_cloud).
 int ref_object_cloud_rgb(void* h, int i, uint8_t* rgb, int cap) {
   const auto& objs = static_cast<RefMap*>(h)->om.objects();

@@ -640,3 +640,31 @@ DEV void push_event(const Batch& B, int map, double t, const ObjRec& o, int kind
   r.kind = kind;
   r.key = key;
 }
+
+// ---------------------------------------------------------------- class kinds and names
+DEV int kind_of(const Batch& B, int cls) {   // ObjectMap::kindOf (objmap.hpp:246)
+  return B.txt.kinds && cls >= 0 && cls < B.txt.n_labels ? (int)B.txt.kinds[cls] : KIND_OBJECT;
+}
+// ObjectMap::isBig (objmap.cpp:207-209)
+DEV bool is_big(const Batch& B, const ObjRec& o) {
+  const int k = kind_of(B, o.cls);
+  return k == KIND_STATIC || k == KIND_STRUCT_OBJ || smax(smax(o.hi[0] - o.lo[0], o.hi[1] - o.lo[1]), o.hi[2] - o.lo[2]) > B.p.big;
+}
+// flatNamed (objmap.hpp:306-308): the object's name is a wall-mounted flat object
+DEV bool flat_named(const Batch& B, const ObjRec& o) {
+  return B.txt.flat_ok && o.name_lab >= 0 && o.name_lab < B.txt.n_labels && B.txt.flat_ok[o.name_lab];
+}
+// ObjectMap::labelRelated (objmap.cpp:1243-1253): equal, or one an ancestor of the other
+DEV bool label_related(const Batch& B, int a, int b) {
+  if (a == b) return true;
+  const int* par = B.txt.parent;
+  const int C = B.txt.n_labels;
+  auto up = [&](int x, int y) {
+    for (int g = 0; x >= 0 && g < 8; ++g) {
+      x = par && x < C ? par[x] : -1;
+      if (x == y) return true;
+    }
+    return false;
+  };
+  return up(a, b) || up(b, a);
+}

@@ -143,10 +143,12 @@ DEV double cos_max_warp(const Batch& B, size_t og, const ObjRec& o, const float*
 
 // pairFeatures -> P (objmap.cpp:86-96): f0 = contact fraction, f1..f5 = pair_geo, logit, sigmoid
 DEV double pair_p(const double alo[3], const double ahi[3], const double apos[3], double contact, const double blo[3],
-                  const double bhi[3], const double bpos[3], double cs, const smg_params& P, bool merge, double* f0_out) {
+                  const double bhi[3], const double bpos[3], double cs, const smg_params& P, bool merge, double* f0_out,
+                  double f6 = 0.0) {
   double f[7] = {0, 0, 0, 0, 0, 0, 0};
   f[0] = contact;
   pair_geo(alo, ahi, apos, blo, bhi, bpos, cs, P.cos0, f);
+  f[6] = f6;   // the merge pair's name-distribution overlap (objmap.cpp:1129-1133), else 0
   if (f0_out) *f0_out = f[0];
   return sigmoid(same_logit(merge ? P.wm : P.w, f));
 }
@@ -196,10 +198,13 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
   const double gate2 = P.gate * P.gate;
   // box-gap gate of every object, one thread per object; the gated ones go to a list that the
   // warps then work through (the top-1 below reads pp in list order, so the list order is free)
-  __shared__ int gl[ASSOC_GATED];
-  __shared__ int ngl;
-  if (tid == 0) ngl = 0;
+  __shared__ int gl[ASSOC_GATED];   // list position, bit 30: blocked pair (features only)
+  __shared__ int ngl, sh_blocked;
+  if (tid == 0) { ngl = 0; sh_blocked = 0; }
   __syncthreads();
+  // text-model guards (objmap.cpp:792-799): this observation's structure probabilities
+  const double o_ps = O->ps, o_pso = O->pso, o_top_p = O->top_p;
+  const int o_top = O->top_lab, o_look = O->struct_look;
   {
     double olo[3], ohi[3];
     for (int k = 0; k < 3; ++k) { olo[k] = O->lo[k]; ohi[k] = O->hi[k]; }
@@ -213,15 +218,26 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
       }
       pp[b] = -1.0;
       if (g2 > gate2 || ob.held_by >= 0) continue;   // held objects take no observation (objmap.cpp:785)
+      // structure guard: a structure-named object does not take a fragment that is not
+      if (o_ps >= 0 && ob.has_post && ob.gp_so >= P.guard_obj && o_ps + o_pso <= P.guard_obs) continue;
+      // blocked pairs: a wall-looking fragment and a non-structure object; a flat wall-mounted
+      // name grown past its size
+      const bool blk = (P.struct_look_block && o_look && ob.has_post && ob.gp_so < 0.5) ||
+                       (flat_named(B, ob) && smax(smax(ohi[0], ob.hi[0]) - smin(olo[0], ob.lo[0]),
+                                                  smax(ohi[1], ob.hi[1]) - smin(olo[1], ob.lo[1])) > P.flat_max_w);
+      if (P.name_veto > 0 && o_top >= 0 && o_top_p >= P.name_veto && ob.top_lab >= 0 && (double)ob.top_p >= P.name_veto &&
+          !label_related(B, o_top, ob.top_lab))
+        continue;   // names in conflict
       const int q = atomicAdd(&ngl, 1);
-      if (q < ASSOC_GATED) gl[q] = b;
+      if (q < ASSOC_GATED) gl[q] = b | (blk ? 1 << 30 : 0);
       else set_err(&B.maps[m], SMG_E_ARGS);
     }
   }
   __syncthreads();
   const int ng = ngl < ASSOC_GATED ? ngl : ASSOC_GATED;
   for (int gi = wid; gi < ng; gi += nw) {
-    const int b = gl[gi];
+    const int b = gl[gi] & ~(1 << 30);
+    const bool blk = (gl[gi] >> 30) & 1;
     const int slot = slot_at(B, m, b);
     const size_t og = oglob(B, m, slot);
     const ObjRec& ob = B.objs[og];
@@ -235,7 +251,11 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
       double f0;
       const double p = pair_p(O->lo, O->hi, O->pos, contact, ob.lo, ob.hi, ob.pos, cs, P, false, &f0);
       if (f0 >= 0.3 || p >= 0.2) B.touched[(size_t)m * B.O + b] = 1;
-      pp[b] = p;
+      if (blk) {   // features (touched) only; a pair that would have matched blocks the fragment
+        if (p >= P.same_p) sh_blocked = 1;
+      } else {
+        pp[b] = p;
+      }
     }
   }
   __syncthreads();
@@ -267,6 +287,6 @@ __global__ void __launch_bounds__(ASSOC_THREADS) k_assoc(Batch B) {
     if (mi >= 0 && mp > best) to = mi;
     O->obs_to = to;
     O->n_same = nsame;
-    O->blocked = 0;
+    O->blocked = sh_blocked;
   }
 }

@@ -26,10 +26,11 @@ DEV void cloud_translate_axis(const Batch& B, int m, const ObjRec& o, int k, dou
 }
 
 // holdable (objmap.cpp:400-410): not big, middle side <= grasp_max_w, the gap fits the sides
-DEV bool holdable(const smg_params& P, const ObjRec& o, double gap) {
+DEV bool holdable(const Batch& B, const ObjRec& o, double gap) {
+  const smg_params& P = B.p;
+  if (is_big(B, o)) return false;
   double e[3];
   for (int k = 0; k < 3; ++k) e[k] = smax(0.0, o.hi[k] - o.lo[k]);
-  if (smax(smax(e[0], e[1]), e[2]) > P.big) return false;   // isBig without class kinds
   // sort the three sides
   if (e[0] > e[1]) { const double x = e[0]; e[0] = e[1]; e[1] = x; }
   if (e[1] > e[2]) { const double x = e[1]; e[1] = e[2]; e[2] = x; }
@@ -90,7 +91,7 @@ __global__ void __launch_bounds__(HANDS_THREADS) k_hands(Batch B) {
         const ObjRec& o = obj_at(B, m, i);
         if (!o.confirmed || o.held_by >= 0 || o.state == 1) continue;
         const double d = dist3(o.pos, F.eef[h]);
-        if (d < bd && holdable(P, o, F.hand_gap[h])) { bd = d; bi = i; }   // a thread's i ascend: first on ties
+        if (d < bd && holdable(B, o, F.hand_gap[h])) { bd = d; bi = i; }   // a thread's i ascend: first on ties
       }
       s_bd[tid] = bd;
       s_bi[tid] = bi;

@@ -74,9 +74,6 @@ DEV int absent_evidence_warp(const Batch& B, int m, const ObjRec& o, const Frame
   return thru * 10 >= vis * 3 ? 2 : 1;
 }
 
-DEV bool is_big(const smg_params& P, const ObjRec& o) {
-  return smax(smax(o.hi[0] - o.lo[0], o.hi[1] - o.lo[1]), o.hi[2] - o.lo[2]) > P.big;
-}
 
 // absence and misses (objmap.cpp:1021-1061), one warp per object in list order
 __global__ void __launch_bounds__(256) k_absent(Batch B) {
@@ -101,7 +98,7 @@ __global__ void __launch_bounds__(256) k_absent(Batch B) {
       if (dist3(cam_now, o.last_miss_cam) < P.gone_step_d && cosang > B.cos_gone_step) continue;
     }
     for (int k = 0; k < 3; ++k) { o.last_miss_cam[k] = cam_now[k]; o.last_miss_fwd[k] = fwd[k]; }
-    const bool big = is_big(P, o);
+    const bool big = is_big(B, o);
     ++o.n_vis_miss;
     if (o.misses++ == 0) {
       o.first_miss = F.stamp;
@@ -403,9 +400,87 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
       if (!geo && R.ceil_est > 0 && n > 0)
         if (up >= P.ceil_frac * n && smax(o.hi[0] - o.lo[0], o.hi[1] - o.lo[1]) >= P.ceil_wide) geo = 2;
       o.geo = geo;
+      o.vinl = pout.ok && nz < P.wall_vert ? (float)pout.inl : 0.f;
     }
     __syncthreads();
+    if (B.text_on && n > 0) {
+      // the shape the named-structure rules read (objmap.cpp:1281-1301): 5-95 % spans along the
+      // horizontal principal axes and in height (no wall segments here: the wall share fw is 0)
+      double sx = 0, sy = 0;
+      for (int i = threadIdx.x; i < n; i += blockDim.x) { sx += (double)Pt[3 * i]; sy += (double)Pt[3 * i + 1]; }
+      const double mx = block_sum_d(sx, bs) / n, my = block_sum_d(sy, bs) / n;
+      double a3[3] = {0, 0, 0};
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double dx = (double)Pt[3 * i] - mx, dy = (double)Pt[3 * i + 1] - my;
+        a3[0] += dx * dx; a3[1] += dx * dy; a3[2] += dy * dy;
+      }
+      __shared__ double red3[3 * 32];
+      block_sum_multi<3>(a3, red3);
+      const double th = 0.5 * atan2(2 * a3[1], a3[0] - a3[2]), c = cos(th), sn = sin(th);
+      double* U = scr;
+      double* V = scr + STRUCT_PTS;
+      double* Z = scr + 2 * STRUCT_PTS;
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double dx = (double)Pt[3 * i] - mx, dy = (double)Pt[3 * i + 1] - my;
+        U[i] = dx * c + dy * sn;
+        V[i] = -dx * sn + dy * c;
+        Z[i] = (double)Pt[3 * i + 2];
+      }
+      __syncthreads();
+      int* hist = (int*)Pt;   // the sample is dead: selection histograms
+      __shared__ double sel6[6];
+      const double* arr[6] = {U, U, V, V, Z, Z};
+      const int nn[6] = {n, n, n, n, n, n};
+      const int k5 = pct_index(n, 0.05), k95 = pct_index(n, 0.95);
+      const int kk[6] = {k95, k5, k95, k5, k95, k5};
+      block_select_multi(arr, nn, kk, sel6, 6, hist, bs);
+      if (threadIdx.x == 0) {
+        const double su = sel6[0] - sel6[1], sv = sel6[2] - sel6[3];
+        o.maj = (double)(float)smax(su, sv);
+        o.minr = (double)(float)smin(su, sv);
+        o.hgt = (double)(float)(sel6[4] - sel6[5]);
+      }
+      __syncthreads();
+    }
   }
+}
+
+// apStructObject's decision (objmap.cpp:1320-1349) on the object's geometry and name
+// posterior; sets hide.  No wall segments: the wall share fw is 0 and geo is never 3.
+DEV bool struct_object_drop(const Batch& B, size_t og, ObjRec& o) {
+  const smg_params& P = B.p;
+  o.hide = 0;
+  const int C = B.txt.n_labels;
+  const float* post = o.has_post ? B.post + og * C : nullptr;
+  double qso = 0;
+  if (post)
+    for (int l = 0; l < C; ++l)
+      if (kind_of(B, l) == KIND_STRUCT_OBJ) qso += (double)post[l];
+  const double fw = 0.0;
+  if (qso >= 0.5 && o.geo != 2) {
+    double qsh[4] = {0, 0, 0, 0};
+    for (int l = 0; l < C; ++l)
+      if (kind_of(B, l) == KIND_STRUCT_OBJ) qsh[B.txt.so_shape ? B.txt.so_shape[l] & 3 : 0] += (double)post[l];
+    int sh = 1;
+    for (int i = 2; i < 4; ++i)
+      if (qsh[i] > qsh[sh]) sh = i;
+    const bool fits = sh == 1   ? o.maj <= P.so_dw_w && o.minr <= P.so_dw_thick && o.hgt <= P.so_max_h
+                      : sh == 3 ? o.maj <= P.so_pillar
+                                : o.maj <= P.so_stairs;
+    if (sh == 1 && o.maj < P.so_dw_min && (int)o.n_obs >= P.so_min_obs) return true;
+    if (fits) return false;
+    const double lim = sh == 1 ? P.so_dw_w : sh == 3 ? P.so_pillar : P.so_stairs;
+    o.hide = o.geo != 0 || (fw >= P.wallhug_frac && o.maj >= P.wallhug_w) || (double)o.vinl >= P.big_vinl || o.maj > P.so_hide_k * lim;
+    return false;
+  }
+  if (flat_named(B, o) && o.maj > P.flat_max_w && (o.geo != 0 || fw >= 0.5 || (double)o.vinl >= P.big_vinl)) { o.hide = 1; return false; }
+  if (fw >= P.wallhug_frac && o.maj >= P.wallhug_w) { o.hide = 1; return false; }
+  if (o.geo == 1 || o.geo == 2) return true;
+  if (o.n_whole < P.struct_obj_min_views || !post) return false;
+  double q = 0;
+  for (int l = 0; l < C; ++l)
+    if (kind_of(B, l) == KIND_STRUCTURE) q += (double)post[l];
+  return q >= P.struct_obj_p;
 }
 
 // drop + prune (objmap.cpp:1064-1073), then the cloud-addition targets (objects named by this
@@ -434,6 +509,8 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
     ObjRec& o = B.objs[oglob(B, m, slot)];
     if (o.held_by >= 0) {   // apStructObject returns false for a held object (objmap.cpp:1256)
       o.drop = 0;
+    } else if (B.text_on || B.kinds_on) {
+      o.drop = struct_object_drop(B, oglob(B, m, slot), o);
     } else {
       o.hide = 0;
       o.drop = o.geo == 1 || o.geo == 2;

@@ -16,7 +16,7 @@
 
 #define MP_CTAS 8
 #define MGL_CAP 65536   // gated pairs per map and frame
-#define MP_SMEM(O) ((size_t)(O) * (6 * 8 + 4))   // k_merge_gate: boxes and states
+#define MP_SMEM(O) ((size_t)(O) * (7 * 8 + 8))   // k_merge_gate: boxes, guard mass, states, guard flags
 
 // p-th pair (i < j) of n objects in row-major order of the upper triangle
 DEV void pair_of(long long p, int n, int* pi, int* pj) {
@@ -41,12 +41,16 @@ __global__ void __launch_bounds__(256) k_merge_gate(Batch B) {
   if (n < 2) return;
   double* slo = (double*)smem_raw;
   double* shi = slo + 3 * (size_t)B.O;
-  int* sst = (int*)(shi + 3 * (size_t)B.O);
+  double* sgp = shi + 3 * (size_t)B.O;       // structure-group posterior mass
+  int* sst = (int*)(sgp + (size_t)B.O);
+  int* sfl = sst + B.O;                      // bit 0: post, bit 1: struct-looking, bit 2: flat name
   // 1. stage the gate inputs of every object (parallel loads)
   for (int b = tid; b < n; b += blockDim.x) {
     const ObjRec& o = obj_at(B, m, b);
     for (int k = 0; k < 3; ++k) { slo[3 * b + k] = o.lo[k]; shi[3 * b + k] = o.hi[k]; }
     sst[b] = o.held_by >= 0 ? 1 : o.state;   // held objects are left out like gone ones (objmap.cpp:1162-1165)
+    sgp[b] = o.gp_so;
+    sfl[b] = (o.has_post ? 1 : 0) | (2 * o.n_struct_look > o.n_ap_obs ? 2 : 0) | (flat_named(B, o) ? 4 : 0);
   }
   __syncthreads();
   // 2. box-gap and size gates of all pairs (objmap.cpp:1160-1173); this CTA takes every
@@ -65,6 +69,18 @@ __global__ void __launch_bounds__(256) k_merge_gate(Batch B) {
       too_big = too_big || smax(shi[3 * i + k], shi[3 * j + k]) - smin(slo[3 * i + k], slo[3 * j + k]) > P.max_ext;
     }
     if (g2 > gate2 || too_big) continue;
+    if ((sfl[i] & 1) && (sfl[j] & 1)) {   // structure guards (objmap.cpp:1174-1181)
+      const double sa = sgp[i], sb = sgp[j];
+      if ((sa >= P.guard_obj && sb <= P.guard_obs) || (sb >= P.guard_obj && sa <= P.guard_obs)) continue;
+      if (P.struct_look_block) {
+        const bool la = sfl[i] & 2, lb = sfl[j] & 2;
+        if ((la && !lb && sb < 0.5) || (lb && !la && sa < 0.5)) continue;
+      }
+    }
+    if (((sfl[i] | sfl[j]) & 4) &&   // a flat wall-mounted name past its size (objmap.cpp:1182-1184)
+        smax(smax(shi[3 * i], shi[3 * j]) - smin(slo[3 * i], slo[3 * j]), smax(shi[3 * i + 1], shi[3 * j + 1]) - smin(slo[3 * i + 1], slo[3 * j + 1])) >
+            P.flat_max_w)
+      continue;
     const int q = atomicAdd(&B.mgl_n[m], 1);
     if (q < MGL_CAP) B.mgl[(size_t)m * MGL_CAP + q] = i << 16 | j;
     else set_err(&B.maps[m], SMG_E_ARGS);
@@ -120,8 +136,19 @@ __global__ void __launch_bounds__(256) k_merge_pairs(Batch B) {
         pc.contact = contact;
       }
     }
+    // name-distribution overlap (objmap.cpp:1129-1133): Bhattacharyya coefficient - 0.5, label order
+    double f6 = 0;
+    const bool names = a.has_post && b.has_post;
+    if (names && lane == 0) {
+      const int C = B.txt.n_labels;
+      const float* pa = B.post + ogi * C;
+      const float* pb2 = B.post + ogj * C;
+      double bc = 0;
+      for (int l = 0; l < C; ++l) bc += sqrt((double)pa[l] * pb2[l]);
+      f6 = bc - 0.5;
+    }
     if (lane == 0) {
-      const double p = pair_p(sm.lo, sm.hi, sm.pos, contact, lg.lo, lg.hi, lg.pos, cs, P, true, nullptr);
+      const double p = pair_p(sm.lo, sm.hi, sm.pos, contact, lg.lo, lg.hi, lg.pos, cs, P, true, nullptr, f6);
       if (p >= P.merge_p) {
         const int c = atomicAdd(&B.mcand_n[m], 1);
         if (c < B.O * 8) {
@@ -203,7 +230,8 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
         // da::absorb scalar part (merge.cpp:33-62)
         ObjRec& a = B.objs[oglob(B, m, sh_ka)];
         const ObjRec& b = B.objs[oglob(B, m, sh_kb)];
-        const bool big = smax(smax(a.hi[0] - a.lo[0], a.hi[1] - a.lo[1]), smax(b.hi[0] - b.lo[0], b.hi[1] - b.lo[1])) > P.big;
+        const bool big = kind_of(B, a.cls) == KIND_STATIC ||   // bigPair (merge.cpp:25-29)
+                         smax(smax(a.hi[0] - a.lo[0], a.hi[1] - a.lo[1]), smax(b.hi[0] - b.lo[0], b.hi[1] - b.lo[1])) > P.big;
         const double wa = smax((double)a.n_obs, 1.0), wb = smax((double)b.n_obs, 1.0);
         for (int k = 0; k < 3; ++k) {
           if (big) {
@@ -271,7 +299,26 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
       if (bw) x += rbw[i];
       ra[i] = x;
     }
+    if (B.text_on) {   // the label vectors in the same order (a vector is added only when it is not empty)
+      const int C = B.txt.n_labels;
+      float* La = B.lfrag + oga * C;
+      const float* Law = B.lwhole + oga * C;
+      const float* Lb = B.lfrag + ogb * C;
+      const float* Lbw = B.lwhole + ogb * C;
+      const bool hf = a.has_lfrag, hw = a.has_lwhole, bf = b.has_lfrag, bhw = b.has_lwhole;
+      for (int l = tid; l < C; l += blockDim.x) {
+        float x = hf ? La[l] : 0.f;
+        if (hw) x += Law[l];
+        if (bf) x += Lb[l];
+        if (bhw) x += Lbw[l];
+        La[l] = x;
+      }
+    }
     __syncthreads();
+    if (tid == 0 && B.text_on) {
+      a.has_lfrag = a.has_lfrag || a.has_lwhole || b.has_lfrag || b.has_lwhole;
+      a.has_lwhole = 0;
+    }
     // views: a's and b's in one list, fragments, stable by kappa desc, top-k (objprob.cpp:382-385)
     __shared__ int vsrc[2 * SMG_TOPK_MAX + 2], vphys[2 * SMG_TOPK_MAX + 2], dstp[2 * SMG_TOPK_MAX + 2], nkeep;
     __shared__ float vk[2 * SMG_TOPK_MAX + 2];
@@ -327,6 +374,10 @@ __global__ void __launch_bounds__(512) k_merge_apply(Batch B) {
       a.n_struct_look += b.n_struct_look;
       a.wall_like = a.wall_like && b.wall_like;
       a.confirmed = a.confirmed || b.confirmed;
+      // label evidence (objprob.cpp:370-374): L_frag += a.L_whole, b.L_frag, b.L_whole
+      a.lw_frag += (a.lw_whole + b.lw_frag) + b.lw_whole;
+      a.lw_whole = 0;
+      a.rename = B.text_on;   // apRename after the absorb (objmap.cpp:1217)
       ++R->st.n_merge;
       const uint32_t did = b.id;
       { const int pe = sh_pkb; if (INB(pe, R->n_obj, 604)) erase_pos(B, m, pe, false); }   // b's position (findPos)

@@ -501,6 +501,9 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   const int m = B.map0 + blockIdx.y, k = blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   ObsRec* O = &B.obs[(size_t)m * B.max_det + k];
+  if (tid == 0) {   // no text model / embedding (k_obs_text overwrites these when there is one)
+    O->ps = -1.0; O->pso = 0.0; O->top_p = 0.0; O->top_lab = -1; O->so_sh = 1; O->wall_like = 0; O->struct_look = 0;
+  }
   if (!F.active || k >= F.n_det) {
     if (tid == 0) { O->valid = 0; O->stage = -1; O->floor_drop = 0; }
     return;
@@ -770,15 +773,16 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
 }
 
 // Structural decision and observation list, in detection order (objmap.cpp:741-765 and the
-// apObsStructural branches at :576-621 with no wall segments and no text model).
+// apObsStructural branches at :576-621 with no wall segments; ps, pso and the shape group come
+// from k_obs_text when a text model is set).
 __global__ void k_obs_finalize(Batch B) {
   const int m = B.map0 + blockIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
   // the fields the decision reads, staged by the warp; the walk then waits on no global load
   struct Fin {
-    int valid, stage, nc, pl_ok;
-    double inl, thick, nz, zmed, zhi, zlo, hspan;
+    int valid, stage, nc, pl_ok, so_sh;
+    double inl, thick, nz, zmed, zhi, zlo, hspan, ps, pso;
   };
   __shared__ Fin fs[SMG_MAX_DET];
   const int nd = min(F.n_det, B.max_det);
@@ -788,6 +792,7 @@ __global__ void k_obs_finalize(Batch B) {
     f.valid = O->valid; f.stage = O->stage; f.nc = O->nc; f.pl_ok = O->pl_ok;
     f.inl = O->pl_inl; f.thick = O->pl_thick; f.nz = fabs(O->pl_n[2]); f.zmed = O->pl_zmed;
     f.zhi = O->pl_zhi; f.zlo = O->pl_zlo; f.hspan = O->pl_hspan;
+    f.ps = O->ps; f.pso = O->pso; f.so_sh = O->so_sh;
     fs[k] = f;
   }
   __syncthreads();
@@ -830,10 +835,20 @@ __global__ void k_obs_finalize(Batch B) {
         if (O.zmed > cz) { ++st_ceil; drop = true; }
         else if (O.zhi < P.floor_z) { ++st_floor; drop = true; }
       } else if (!(nz > P.wall_vert)) {
+        // a thin upright plane that looks like structure: wall-like (objmap.cpp:594)
+        if (O.ps >= 0.5) {
+          B.obs[(size_t)m * B.max_det + k].wall_like = 1;
+          B.obs[(size_t)m * B.max_det + k].struct_look = 1;
+        }
+        // named door / window / pillar / stairs within that shape's size (objmap.cpp:595-597)
+        const int sh = O.so_sh;
+        const bool so_keep = O.pso >= 0.5 && (sh == 1   ? O.hspan <= P.so_dw_w && O.zhi - O.zlo <= P.so_max_h
+                                              : sh == 3 ? O.hspan <= P.so_pillar
+                                                        : O.hspan <= P.so_stairs);
         const double cz = ceil_est > 0 ? ceil_est : P.ceil_z + 0.4;
         const bool tall = O.zhi - O.zlo >= P.tall_h || (O.zlo <= P.tall_floor && O.zhi >= cz - P.tall_ceil);
-        const bool wide = O.hspan >= P.tall_w_any;   // structure probability -1 < tall_ps
-        if (tall && wide) { ++st_wall_tall; drop = true; }
+        const bool wide = O.hspan >= (O.ps >= P.tall_ps ? P.tall_w : P.tall_w_any);
+        if (tall && wide && !so_keep) { ++st_wall_tall; drop = true; }
       }
     }
     if (!drop) B.obs_list[(size_t)m * B.max_det + n++] = k;

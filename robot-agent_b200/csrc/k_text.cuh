@@ -15,25 +15,11 @@
 
 #define TXT_MAX_LABELS 1024
 
-struct TextDev {
-  int dim, n_labels, rows;
-  const float* text;         // rows x dim
-  const int32_t* row_label;  // rows
-  float scale, bias;
-  const float* log_prior;    // n_labels or null
-  const float* ls_mu;        // n_labels or null (with ls_sd)
-  const float* ls_sd;
-  const int32_t* parent;     // n_labels or null
-  int object_label;
-};
 
-__global__ void __launch_bounds__(256) k_label_loglik(TextDev T, const float* z, int n, float* out) {
-  extern __shared__ __align__(16) unsigned char tx_raw[];
-  float* zs = (float*)tx_raw;
-  float* best = zs + T.dim;   // per label: max cosine (float)
-  const int i = blockIdx.x, tid = threadIdx.x;
-  if (i >= n) return;
-  for (int k = tid; k < T.dim; k += blockDim.x) zs[k] = z[(size_t)i * T.dim + k];
+// apLabelLogLik of one embedding zs (shared memory, T.dim floats) into out[T.n_labels]; best:
+// T.n_labels floats of shared scratch.  All threads of the block call it; it ends with a barrier.
+DEV void label_loglik_block(const TextDev& T, const float* zs, float* best, float* out) {
+  const int tid = threadIdx.x;
   for (int l = tid; l < T.n_labels; l += blockDim.x) best[l] = -2.f;
   __syncthreads();
   for (int r = tid; r < T.rows; r += blockDim.x) {
@@ -52,23 +38,35 @@ __global__ void __launch_bounds__(256) k_label_loglik(TextDev T, const float* z,
     }
   }
   __syncthreads();
-  if (tid != 0) return;
-  float* o = out + (size_t)i * T.n_labels;
-  double mx = -1e300;
-  for (int l = 0; l < T.n_labels; ++l) {
-    o[l] = -1e30f;
-    if (best[l] < -1.5f) continue;
-    const double x = (double)best[l] * (double)T.scale + (double)T.bias;
-    const double ls = x >= 0 ? -log1p(exp(-x)) : x - log1p(exp(x));
-    o[l] = (float)ls;
-    mx = smax(mx, ls);
+  if (tid == 0) {
+    double mx = -1e300;
+    for (int l = 0; l < T.n_labels; ++l) {
+      out[l] = -1e30f;
+      if (best[l] < -1.5f) continue;
+      const double x = (double)best[l] * (double)T.scale + (double)T.bias;
+      const double ls = x >= 0 ? -log1p(exp(-x)) : x - log1p(exp(x));
+      out[l] = (float)ls;
+      mx = smax(mx, ls);
+    }
+    double se = 0;
+    for (int l = 0; l < T.n_labels; ++l)
+      if (out[l] > -1e29f) se += exp((double)out[l] - mx);
+    const double lz = mx + log(smax(se, 1e-300));
+    for (int l = 0; l < T.n_labels; ++l)
+      if (out[l] > -1e29f) out[l] = (float)((double)out[l] - lz);
   }
-  double se = 0;
-  for (int l = 0; l < T.n_labels; ++l)
-    if (o[l] > -1e29f) se += exp((double)o[l] - mx);
-  const double lz = mx + log(smax(se, 1e-300));
-  for (int l = 0; l < T.n_labels; ++l)
-    if (o[l] > -1e29f) o[l] = (float)((double)o[l] - lz);
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) k_label_loglik(TextDev T, const float* z, int n, float* out) {
+  extern __shared__ __align__(16) unsigned char tx_raw[];
+  float* zs = (float*)tx_raw;
+  float* best = zs + T.dim;   // per label: max cosine (float)
+  const int i = blockIdx.x, tid = threadIdx.x;
+  if (i >= n) return;
+  for (int k = tid; k < T.dim; k += blockDim.x) zs[k] = z[(size_t)i * T.dim + k];
+  __syncthreads();
+  label_loglik_block(T, zs, best, out + (size_t)i * T.n_labels);
 }
 
 struct NameArgs {

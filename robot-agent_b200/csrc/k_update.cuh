@@ -344,6 +344,9 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
       if (act == 2) {   // new candidate (objmap.cpp:951-978)
         memset(&mo, 0, sizeof(ObjRec));
         mo.held_by = -1;
+        mo.name_lab = -1;
+        mo.top_lab = -1;
+        mo.rename = B.text_on;   // seen this keyframe (objmap.cpp:1007-1008)
         mo.id = s_newid[a];
         mo.cls = o.cls;
         for (int k = 0; k < 3; ++k) { mo.pos[k] = mo.first_pos[k] = o.pos[k]; mo.ext[k] = o.ext[k]; mo.lo[k] = o.lo[k]; mo.hi[k] = o.hi[k]; }
@@ -375,29 +378,45 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update(Batch B) {
         ++C.vgen;
         C.cver = 0xffffffffu;
         mo.n_ap_obs = 1;
-        mo.n_wall_obs = 0;
-        mo.n_struct_look = 0;
-        mo.wall_like = 0;
+        mo.n_wall_obs = o.wall_like;
+        mo.n_struct_look = o.struct_look;
+        mo.wall_like = o.wall_like;
       }
       if (has_z) {   // a recycled slot starts from an empty r_frag (objprob.cpp:329 assigns zeros)
         double k;
         int phys;
         ap_add_view_plan(B, mo, o.kappa, F.stamp, cam6, &k, &phys);
+        // label evidence (objprob.cpp:333-340): weight w = k / kappa_ref; the job adds
+        // w max(log p, -60) to L_frag, from zeros when the object had none
+        const bool txt = B.text_on && B.txt.dim == B.D;
+        const double w = k / smax(1e-6, P.kappa_ref);
         if (s_job[a] >= 0) {
           UpdJob& j = B.upd_job[jbase + s_job[a]];
           j.k = k;
           j.phys = phys;
+          j.w = txt ? w : 0.0;
+          j.lzero = txt && !mo.has_lfrag;
+          j.ltext = txt;
+        }
+        if (txt) {
+          mo.lw_frag += w;
+          mo.has_lfrag = 1;
         }
       }
       if (act == 1) {
           ++mo.n_ap_obs;
+          if (o.wall_like) ++mo.n_wall_obs;
+          if (o.struct_look) ++mo.n_struct_look;
           mo.wall_like = 2 * mo.n_wall_obs >= mo.n_ap_obs;
           if (!o.sec) {
             const double dt_seen = F.stamp - mo.last_seen;
             if (mo.parent && dist3(mo.pos, o.pos) > 0.3) mo.parent = 0;
             if (mo.last_kf != F.stamp) ++mo.n_obs;
             mo.last_kf = F.stamp;
-            const bool big = smax(smax(mo.hi[0] - mo.lo[0], mo.hi[1] - mo.lo[1]), smax(o.ext[0], o.ext[1])) > P.big;
+            mo.rename = B.text_on;   // seen this keyframe (objmap.cpp:1007-1008)
+            const int kd = kind_of(B, mo.cls);
+            const bool big = kd == KIND_STATIC || kd == KIND_STRUCT_OBJ ||
+                             smax(smax(mo.hi[0] - mo.lo[0], mo.hi[1] - mo.lo[1]), smax(o.ext[0], o.ext[1])) > P.big;
             bool snap = false;
             if (P.move_n > 0 && mo.trk_t > 0 && mo.held_by < 0 && !o.trunc && F.cam_steady) {
               const double dt = F.stamp - mo.trk_t;
@@ -538,6 +557,12 @@ __global__ void __launch_bounds__(UPD_THREADS) k_update_vec(Batch B) {
       const float zi = emb_at(F.emb, F.emb_dtype, B.D, j.det, i);
       r[i] = (j.zero ? 0.f : r[i]) + (float)(j.k * (double)zi);
       vz[i] = ref_f2h(zi);
+    }
+    if (j.ltext) {   // L_frag += w max(log p, -60) (objprob.cpp:335-339: float per label)
+      const int C = B.txt.n_labels;
+      float* L = B.lfrag + og * C;
+      const float* ll = B.llz + ((size_t)m * B.max_det + j.det) * C;
+      for (int l = tid; l < C; l += blockDim.x) L[l] = (j.lzero ? 0.f : L[l]) + (float)(j.w * smax((double)ll[l], -60.0));
     }
   }
   if (tid == 0) wk_add(&B.maps[m], SMG_WK_UPD, nmine);

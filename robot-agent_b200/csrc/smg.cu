@@ -36,6 +36,7 @@
 #include "k_reenc.cuh"
 #include "k_hands.cuh"
 #include "k_views.cuh"
+#include "k_textmap.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -224,14 +225,19 @@ int smg_params_default(smg_params* p) {
   const double gg[7][2] = {{0.0, 0.0}, {0.095, 0.01}, {0.231, 0.02}, {0.347, 0.03}, {0.408, 0.04}, {0.5236, 0.0551}, {0.7854, 0.0933}};
   p->n_grip_gap = 7;
   memcpy(p->grip_gap, gg, sizeof gg);
+  // text-model rules (objprob.hpp:84-136)
+  p->name_tau = 0.5; p->name_wmax = 6.0; p->size_w = 1.0; p->whole_w = 1.0; p->geo_w = 3.0; p->flat_max_w = 2.2;
+  p->wall_big = 1.0; p->struct_p = 0.5;
+  p->so_dw_w = 2.2; p->so_dw_thick = 0.45; p->so_max_h = 2.8; p->so_pillar = 1.0; p->so_stairs = 6.0; p->so_dw_min = 0.3;
+  p->so_hide_k = 1.5; p->wallhug_frac = 0.75; p->wallhug_w = 2.0; p->big_vinl = 0.5;
+  p->struct_look_block = 1; p->so_min_obs = 12;
   return SMG_OK;
 }
 
 // ObjectMap::applyParams key table (scenemap src/objmap.cpp:135-180).  Keys whose feature the
-// device path does not run (the text model's naming and structural-name rules, wall segments,
-// the inspect pass, the export filter) only ever take the reference default here: any other
-// value is reported as unsupported, so a parameter file cannot change the reference's
-// behaviour and leave this one unchanged without an error.
+// device path does not run (wall segments, the inspect pass, the export filter) only ever take
+// the reference default here: any other value is reported as unsupported, so a parameter file
+// cannot change the reference's behaviour and leave this one unchanged without an error.
 int smg_params_apply(smg_params* p, const char* kv) {
   if (!p) return SMG_ERR_ARGS;
   if (!kv || !*kv) return 0;
@@ -249,21 +255,21 @@ int smg_params_apply(smg_params* p, const char* kv) {
       {"view_cell", &p->view_cell, 0, 0}, {"confirm", 0, &p->confirm, 0}, {"move_v", &p->move_v, 0, 0}, {"move_n", 0, &p->move_n, 0},
       {"move_min_d", &p->move_min_d, 0, 0}, {"move_max_cam_w", &p->move_max_cam_w, 0, 0}, {"self_pad", &p->self_pad, 0, 0},
       {"inspect", 0, 0, 0},
-      {"ap_same_p", &p->same_p, 0, 0}, {"ap_merge_p", &p->merge_p, 0, 0}, {"ap_gate", &p->gate, 0, 0}, {"ap_name_tau", 0, 0, 0.5},
-      {"ap_name_wmax", 0, 0, 6.0}, {"ap_size_w", 0, 0, 1.0}, {"ap_kappa_ref", &p->kappa_ref, 0, 0}, {"ap_temper", &p->temper, 0, 0},
-      {"ap_wall_big", 0, 0, 1.0}, {"ap_struct_p", 0, 0, 0.5}, {"ap_ceil_z", &p->ceil_z, 0, 0}, {"ap_struct_obj_p", &p->struct_obj_p, 0, 0},
+      {"ap_same_p", &p->same_p, 0, 0}, {"ap_merge_p", &p->merge_p, 0, 0}, {"ap_gate", &p->gate, 0, 0}, {"ap_name_tau", &p->name_tau, 0, 0},
+      {"ap_name_wmax", &p->name_wmax, 0, 0}, {"ap_size_w", &p->size_w, 0, 0}, {"ap_kappa_ref", &p->kappa_ref, 0, 0}, {"ap_temper", &p->temper, 0, 0},
+      {"ap_wall_big", &p->wall_big, 0, 0}, {"ap_struct_p", &p->struct_p, 0, 0}, {"ap_ceil_z", &p->ceil_z, 0, 0}, {"ap_struct_obj_p", &p->struct_obj_p, 0, 0},
       {"ap_obj_wall_span", &p->obj_wall_span, 0, 0}, {"ap_obj_wall_top", &p->obj_wall_top, 0, 0}, {"ap_reenc_max", 0, &p->reenc_max, 0},
-      {"ap_reenc_gain", &p->reenc_gain, 0, 0}, {"ap_link_cos", &p->link_cos, 0, 0}, {"ap_whole_w", 0, 0, 1.0},
+      {"ap_reenc_gain", &p->reenc_gain, 0, 0}, {"ap_link_cos", &p->link_cos, 0, 0}, {"ap_whole_w", &p->whole_w, 0, 0},
       {"ap_export_named", 0, 0, 1}, {"ap_guard_obj", &p->guard_obj, 0, 0}, {"ap_guard_obs", &p->guard_obs, 0, 0},
-      {"ap_geo_w", 0, 0, 3.0}, {"ap_name_veto", &p->name_veto, 0, 0}, {"ap_through_d", 0, 0, 0.20}, {"ap_bridge_max", 0, 0, 0.0},
+      {"ap_geo_w", &p->geo_w, 0, 0}, {"ap_name_veto", &p->name_veto, 0, 0}, {"ap_through_d", 0, 0, 0.20}, {"ap_bridge_max", 0, 0, 0.0},
       {"ap_frame_group", 0, &p->frame_group, 0}, {"ap_struct_obj_min_views", 0, &p->struct_obj_min_views, 0},
       {"ap_plane_inl", &p->plane_inl, 0, 0}, {"ap_obj_plane_inl", &p->obj_plane_inl, 0, 0}, {"ap_ransac_tau0", &p->ransac_tau0, 0, 0},
       {"ap_ransac_tau_k", &p->ransac_tau_k, 0, 0}, {"ap_obj_tau", &p->obj_tau, 0, 0}, {"ap_ransac_iters", 0, &p->ransac_iters, 0},
-      {"ap_so_dw_w", 0, 0, 2.2}, {"ap_so_dw_thick", 0, 0, 0.45}, {"ap_so_max_h", 0, 0, 2.8}, {"ap_so_pillar", 0, 0, 1.0},
-      {"ap_so_stairs", 0, 0, 6.0}, {"ap_wallhug_frac", 0, 0, 0.75}, {"ap_wallhug_w", 0, 0, 2.0},
-      {"ap_struct_look_block", 0, 0, 1}, {"ap_flat_max_w", 0, 0, 2.2}, {"ap_tall_h", &p->tall_h, 0, 0}, {"ap_tall_w", &p->tall_w, 0, 0},
-      {"ap_tall_ps", &p->tall_ps, 0, 0}, {"ap_tall_w_any", &p->tall_w_any, 0, 0}, {"ap_big_vinl", 0, 0, 0.5}, {"ap_so_dw_min", 0, 0, 0.3},
-      {"ap_so_hide_k", 0, 0, 1.5},
+      {"ap_so_dw_w", &p->so_dw_w, 0, 0}, {"ap_so_dw_thick", &p->so_dw_thick, 0, 0}, {"ap_so_max_h", &p->so_max_h, 0, 0}, {"ap_so_pillar", &p->so_pillar, 0, 0},
+      {"ap_so_stairs", &p->so_stairs, 0, 0}, {"ap_wallhug_frac", &p->wallhug_frac, 0, 0}, {"ap_wallhug_w", &p->wallhug_w, 0, 0},
+      {"ap_struct_look_block", 0, &p->struct_look_block, 0}, {"ap_flat_max_w", &p->flat_max_w, 0, 0}, {"ap_tall_h", &p->tall_h, 0, 0}, {"ap_tall_w", &p->tall_w, 0, 0},
+      {"ap_tall_ps", &p->tall_ps, 0, 0}, {"ap_tall_w_any", &p->tall_w_any, 0, 0}, {"ap_big_vinl", &p->big_vinl, 0, 0}, {"ap_so_dw_min", &p->so_dw_min, 0, 0},
+      {"ap_so_hide_k", &p->so_hide_k, 0, 0},
       {"ap_w0", &p->w[0], 0, 0}, {"ap_w1", &p->w[1], 0, 0}, {"ap_w2", &p->w[2], 0, 0}, {"ap_w3", &p->w[3], 0, 0}, {"ap_w4", &p->w[4], 0, 0},
       {"ap_w5", &p->w[5], 0, 0}, {"ap_w6", &p->w[6], 0, 0}, {"ap_w7", &p->w[7], 0, 0},
       {"ap_wm0", &p->wm[0], 0, 0}, {"ap_wm1", &p->wm[1], 0, 0}, {"ap_wm2", &p->wm[2], 0, 0}, {"ap_wm3", &p->wm[3], 0, 0},
@@ -563,8 +569,15 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
       for (cudaEvent_t* e : {&b->ev_fork[g], &b->ev_join[g], &b->ev_copied[g], &b->ev_gdone[g], &b->ev_dma[g]})
         CK(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
     }
-    CK(cudaStreamCreateWithFlags(&b->s_copy, cudaStreamNonBlocking));
-    CK(cudaStreamCreateWithFlags(&b->s_dma, cudaStreamNonBlocking));
+    {   // host-input streams; SMG_COPY_PRIORITY=1 gives them the highest priority (the SMs' reads of
+        // pinned host frames then get SMs ahead of the previous keyframe's chain)
+      int lo = 0, hi = 0;
+      CK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+      const char* pe = getenv("SMG_COPY_PRIORITY");
+      const int pr = pe && atoi(pe) != 0 ? hi : lo;
+      CK(cudaStreamCreateWithPriority(&b->s_copy, cudaStreamNonBlocking, pr));
+      CK(cudaStreamCreateWithPriority(&b->s_dma, cudaStreamNonBlocking, pr));
+    }
     CK(cudaEventCreateWithFlags(&b->ev_up, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&b->ev_done, cudaEventDisableTiming));
     CK(cudaEventRecord(b->ev_done, 0));
@@ -632,6 +645,12 @@ __global__ void k_begin(Batch B) {
 
 // The keyframe chain of one group of maps (B.map0 .. B.map0 + Mg - 1) on stream st, with the
 // occupancy kernel on the side stream sgrid (forked after k_begin, joined at the end).
+// dynamic shared memory of the text-model kernels
+#define RN_CTAS 8
+static size_t rn_smem(const Batch& B) { return (size_t)RN_WARPS * 2 * B.txt.n_labels * sizeof(double); }
+static size_t obt_smem(const Batch& B) { return ((size_t)B.D + B.txt.n_labels) * sizeof(float); }
+static size_t wv_smem(const Batch& B) { return B.text_on ? ((size_t)B.D + 2 * B.txt.n_labels) * sizeof(float) : 0; }
+
 static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, cudaStream_t sgrid, cudaEvent_t efork,
                         cudaEvent_t ejoin) {
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
@@ -660,10 +679,12 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({1, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_merge_apply<<<Mg, 512, 0, st>>>(B);
+  if (B.text_on) { k_rename<<<dim3(RN_CTAS, Mg), RN_WARPS * 32, rn_smem(B), st>>>(B); ++b->launches; }   // merged objects
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({2, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_obs<<<dim3(B.max_det, Mg), OBS_THREADS, OBS_SMEM, st>>>(B);
+  if (B.text_on) { k_obs_text<<<dim3(B.max_det, Mg), OBT_THREADS, obt_smem(B), st>>>(B); ++b->launches; }
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({3, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
@@ -677,6 +698,7 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_update<<<Mg, UPD_THREADS, UPD_SMEM(B), st>>>(B);
   k_update_vec<<<dim3(B.max_det, Mg), UPD_THREADS, 0, st>>>(B);   // timed together with k_update
+  if (B.text_on) { k_rename<<<dim3(RN_CTAS, Mg), RN_WARPS * 32, rn_smem(B), st>>>(B); ++b->launches; }   // objects seen
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({6, {e0, e1}}); } }
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
@@ -1040,7 +1062,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
       if (gather && gbeg(g + 1) > gbeg(g)) {   // group g's pixels, while group g-1 computes
         Batch Bg = B;
         Bg.map0 = gbeg(g);
-        k_gather<<<dim3(b->max_h, gbeg(g + 1) - gbeg(g)), GATHER_THREADS, 0, b->s_copy>>>(Bg);
+        k_gather<<<dim3(GATHER_CTAS, gbeg(g + 1) - gbeg(g)), GATHER_THREADS, 0, b->s_copy>>>(Bg);
         b->launches += 1;
       }
       CK(cudaEventRecord(b->ev_copied[g], b->s_copy));
@@ -2202,6 +2224,26 @@ __global__ void __launch_bounds__(256) k_whole_views(Batch B, const int32_t* map
       }
       __syncthreads();
       refresh_nrm(B, og, bs);
+      if (B.text_on && B.txt.dim == B.D) {   // label evidence of the whole view, then a rename
+        extern __shared__ __align__(16) unsigned char wv_raw[];
+        float* zs = (float*)wv_raw;
+        float* best = zs + B.D;
+        float* ll = best + B.txt.n_labels;
+        for (int q = tid; q < B.D; q += blockDim.x) zs[q] = z[q];
+        __syncthreads();
+        label_loglik_block(B.txt, zs, best, ll);
+        ObjRec& o = B.objs[og];
+        const double w = s_k / smax(1e-6, B.p.kappa_ref);
+        const bool lz = !o.has_lwhole;
+        float* L = B.lwhole + og * B.txt.n_labels;
+        for (int l = tid; l < B.txt.n_labels; l += blockDim.x) L[l] = (lz ? 0.f : L[l]) + (float)(w * smax((double)ll[l], -60.0));
+        __syncthreads();
+        if (tid == 0) {
+          o.lw_whole += w;
+          o.has_lwhole = 1;
+          o.rename = 1;   // apRename after addWholeView (objmap.cpp:1365)
+        }
+      }
     }
     __syncthreads();
   }
@@ -2232,7 +2274,11 @@ int smg_set_object_embeddings(smg_batch* b, const int32_t* maps, const uint32_t*
   CK(cudaMemcpyAsync(b->d_wv_stamp, b->last_stamp.data(), sizeof(double) * B.M, cudaMemcpyHostToDevice, st));
   // after the keyframe that made the requests (all stream groups have joined on ev_done)
   CK(cudaStreamWaitEvent(st, b->ev_done, 0));
-  k_whole_views<<<B.M, 256, 0, st>>>(B, dm, di, de, n, b->d_wv_stamp);
+  k_whole_views<<<B.M, 256, wv_smem(B), st>>>(B, dm, di, de, n, b->d_wv_stamp);
+  if (B.text_on) {   // the objects that took a whole view are renamed (objmap.cpp:1365)
+    k_rename<<<dim3(RN_CTAS, B.M), RN_WARPS * 32, rn_smem(B), st>>>(B);
+    b->launches += 1;
+  }
   b->launches += 1;
   CK(cudaGetLastError());
   CK(cudaEventRecord(b->ev_done, st));   // the next push's chain waits for the answers
@@ -2260,6 +2306,77 @@ int smg_phase_read(uint64_t* out) {
   (void)out;
   return fail(SMG_ERR_UNSUPPORTED, "smg_phase_read: not an instrumentation build (-DSMG_PHASE_TIMING)");
 #endif
+}
+
+
+int smg_set_text_model(smg_batch* b, const smg_text* t, const uint8_t* kinds, const uint8_t* so_shape, const uint8_t* flat_ok) {
+  if (!b || !t || t->n_labels <= 0 || t->n_labels > TXT_MAX_LABELS || t->rows < 0 ||
+      (t->rows > 0 && (t->dim != b->B.D || !t->text || !t->row_label)))
+    return fail(SMG_ERR_ARGS, "smg_set_text_model: bad arguments (0 < n_labels <= 1024; rows > 0 needs dim = emb_dim)");
+  if (b->n_push > 0) return fail(SMG_ERR_ARGS, "smg_set_text_model: set the text model before the first push");
+  if (b->B.txt.n_labels && b->B.txt.n_labels != t->n_labels)
+    return fail(SMG_ERR_ARGS, "smg_set_text_model: the label count cannot change");
+  CK(cudaSetDevice(b->dev));
+  Batch& B = b->B;
+  const int C = t->n_labels;
+  auto up = [&](auto** dst, const auto* src, size_t n) -> int {   // device copy of a host array (null stays null)
+    using T = std::remove_const_t<std::remove_pointer_t<std::remove_reference_t<decltype(src)>>>;
+    if (!src || n == 0) { *dst = nullptr; return SMG_OK; }
+    T* d = nullptr;
+    if (int r = dalloc(b, &d, n)) return r;
+    CK(cudaMemcpy(d, src, n * sizeof(T), cudaMemcpyHostToDevice));
+    *dst = d;
+    return SMG_OK;
+  };
+  TextDev T;
+  memset(&T, 0, sizeof(T));
+  T.dim = t->rows > 0 ? t->dim : B.D;
+  T.n_labels = C;
+  T.rows = t->rows;
+  T.scale = t->scale;
+  T.bias = t->bias;
+  T.object_label = t->object_label;
+  int r = 0;
+  if ((r = up(&T.text, t->text, (size_t)t->rows * t->dim)) || (r = up(&T.row_label, t->row_label, (size_t)t->rows)) ||
+      (r = up(&T.log_prior, t->log_prior, C)) || (r = up(&T.ls_mu, t->ls_sd ? t->ls_mu : nullptr, C)) ||
+      (r = up(&T.ls_sd, t->ls_mu ? t->ls_sd : nullptr, C)) || (r = up(&T.parent, t->parent, C)) || (r = up(&T.kinds, kinds, C)) ||
+      (r = up(&T.so_shape, so_shape, C)) || (r = up(&T.flat_ok, flat_ok, C)))
+    return r;
+  const size_t MOC = (size_t)B.M * B.O * C;
+  if (!B.lfrag) {
+    if ((r = dalloc(b, &B.lfrag, MOC)) || (r = dalloc(b, &B.lwhole, MOC)) || (r = dalloc(b, &B.post, MOC)) ||
+        (r = dalloc(b, &B.llz, (size_t)B.M * B.max_det * C)))
+      return r;
+  }
+  B.txt = T;
+  B.text_on = t->rows > 0;
+  B.kinds_on = kinds != nullptr;
+  CK(cudaFuncSetAttribute(k_rename, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rn_smem(B)));
+  CK(cudaFuncSetAttribute(k_obs_text, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)obt_smem(B)));
+  CK(cudaFuncSetAttribute(k_whole_views, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wv_smem(B)));
+  return SMG_OK;
+}
+
+int smg_get_object_name(smg_batch* b, int m, int i, float* post, int32_t* lab3, float* val3) {
+  if (!b || m < 0 || m >= b->B.M || i < 0) return fail(SMG_ERR_ARGS, "smg_get_object_name: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  if (i >= R.n_obj) return fail(SMG_ERR_ARGS, "smg_get_object_name: no such object");
+  int32_t slot;
+  CK(cudaMemcpy(&slot, B.order + (size_t)m * B.O + i, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  ObjRec o;
+  const size_t og = (size_t)m * B.O + slot;
+  CK(cudaMemcpy(&o, B.objs + og, sizeof(ObjRec), cudaMemcpyDeviceToHost));
+  const int C = B.txt.n_labels;
+  if (post && C) {
+    if (o.has_post) CK(cudaMemcpy(post, B.post + og * C, sizeof(float) * C, cudaMemcpyDeviceToHost));
+    else memset(post, 0, sizeof(float) * C);
+  }
+  if (lab3) { lab3[0] = o.name_lab; lab3[1] = o.top_lab; lab3[2] = o.rolled; }
+  if (val3) { val3[0] = o.name_p; val3[1] = o.top_p; val3[2] = o.name_H; }
+  return o.has_post ? C : 0;
 }
 
 int smg_set_reencode(smg_batch* b, int on) {

@@ -44,6 +44,27 @@
 #define SMG_E_CAP_REENC 64   // more re-encode candidates in a keyframe than RE_CAND
 #define SMG_E_TRIM 128       // a cloud trim's selection ran past its depth limit (point order then differs)
 
+// Text model on the device (ApText, scenemap objprob.hpp:40-54, plus the class-kind table of
+// ObjectMap::setClassKinds and the label tables the reference glue derives from label names).
+struct TextDev {
+  int dim, n_labels, rows;
+  const float* text;         // rows x dim
+  const int32_t* row_label;  // rows
+  float scale, bias;
+  const float* log_prior;    // n_labels or null
+  const float* ls_mu;        // n_labels or null (with ls_sd)
+  const float* ls_sd;
+  const int32_t* parent;     // n_labels or null
+  int object_label;
+  const uint8_t* kinds;      // n_labels: 0 object, 1 structure, 2 static, 3 structural object (or null)
+  const uint8_t* so_shape;   // n_labels: 1 door / window, 2 stairs / railing, 3 pillar (or null)
+  const uint8_t* flat_ok;    // n_labels: wall-mounted flat object (or null)
+};
+#define KIND_OBJECT 0
+#define KIND_STRUCTURE 1
+#define KIND_STATIC 2
+#define KIND_STRUCT_OBJ 3
+
 // Per (map, frame) input descriptor on the device (smg_frame + host-derived scalars).
 typedef struct {
   double stamp;
@@ -109,6 +130,11 @@ typedef struct {
   double pl_n[3], pl_thick, pl_inl, pl_zmed, pl_zlo, pl_zhi, pl_hspan;
   // association results
   int32_t obs_to, n_same, blocked, sec;
+  // text model (apObsStructural, objmap.cpp:547-564): structure and structural-object
+  // probabilities (ps = -1 without a text model or embedding), the single-fragment top label,
+  // the most likely structural-object shape group, and the wall-like flags of the structural rules
+  double ps, pso, top_p;
+  int32_t top_lab, so_sh, wall_like, struct_look;
 } ObsRec;
 
 typedef struct __align__(16) {   // 16-byte aligned: staged in shared memory in 16-byte words
@@ -156,6 +182,17 @@ typedef struct __align__(16) {   // 16-byte aligned: staged in shared memory in 
   // best view (capi.cpp ViewSlot: the view's quality; has_view = a view is installed)
   double view_q;
   int32_t has_view;
+  // label evidence and name (ApState lw_frag / lw_whole, post, name_*, top_*; the L_frag / L_whole
+  // / post vectors live in Batch::lfrag / lwhole / post); has_post = post is not empty;
+  // rename = apRename is due (seen this keyframe, merged, or a new whole view)
+  double lw_frag, lw_whole;
+  int32_t has_post, has_lfrag, has_lwhole, rename;
+  int32_t name_lab, top_lab, rolled;
+  float name_p, top_p, name_H;
+  uint32_t post_ver;     // changes whenever post does (merge pair features read post)
+  double gp_so;          // posterior mass of structure and structural-object labels (the guards' group)
+  double maj, minr, hgt; // apStructObject shape of the cloud sample (5-95 % spans), with geo
+  float vinl;            // inlier share of an upright dominant plane (ApState::vinl)
 } ObjRec;
 
 typedef struct {
@@ -209,6 +246,8 @@ typedef struct {
 struct UpdJob {
   int32_t tg, det, phys, zero;
   double k;
+  double w;              // label weight k / kappa_ref (text model)
+  int32_t lzero, ltext;  // L_frag starts from zeros; the job adds label evidence
 };
 struct PairCacheRec {
   uint32_t ida, idb, va, vb, ca, cb;
@@ -353,6 +392,14 @@ typedef struct {
   struct PairCacheRec* pcache;   // [M * PCACHE_SLOTS] merge-pass pair features of unchanged pairs
   double* sscr;          // [M * STRUCT_CTAS * STRUCT_SCR] k_struct scratch
   struct UpdJob* upd_job;  // [M * max_det] vector jobs of k_update, observation order
+  // text model (smg_set_text_model)
+  int32_t text_on;       // a text model with rows: label likelihoods and names run
+  int32_t kinds_on;      // a class-kind table is set (isBig reads it)
+  TextDev txt;
+  float* lfrag;          // [M*O*C] ApState::L_frag
+  float* lwhole;         // [M*O*C] ApState::L_whole
+  float* post;           // [M*O*C] ApState::post
+  float* llz;            // [M*max_det*C] apLabelLogLik of each detection's embedding
   // best views (allocated on the first push with an RGB image)
   ViewRec* vrec;         // [M*max_det]
   uint8_t* vrgb;         // [M*max_det*VIEW_PIX*3]

@@ -85,6 +85,8 @@ def lib():
         L.smg_get_object_cloud_rgb.argtypes = [vp, C.c_int, C.c_int, vp, C.c_int]
         L.smg_get_views.argtypes = [vp, C.c_int, vp, vp, vp, vp, C.c_int]
         L.smg_get_assoc_all_async.argtypes = [vp, vp, C.POINTER(C.c_int64)]
+        L.smg_set_text_model.argtypes = [vp, vp, vp, vp, vp]
+        L.smg_get_object_name.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp]
         L.smg_wait_read.argtypes = [vp, C.c_int64]
         L.smg_get_stats.argtypes = [vp, C.c_int, vp]
         L.smg_get_events.argtypes = [vp, C.c_int, vp, vp, vp, C.c_int]
@@ -116,7 +118,8 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
            "smg_get_work", "smg_set_reencode", "smg_set_object_embeddings", "smg_get_object_whole", "smg_plane_fit", "smg_plane_fit_noalloc", "smg_occ_create", "smg_occ_destroy",
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
            "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode",
-           "smg_get_object_cloud_rgb", "smg_get_views", "smg_get_assoc_all_async", "smg_wait_read"]
+           "smg_get_object_cloud_rgb", "smg_get_views", "smg_get_assoc_all_async", "smg_wait_read",
+           "smg_set_text_model", "smg_get_object_name"]
 
 NUM_KERNELS = 17
 
@@ -364,6 +367,35 @@ class Batch:
         out = np.zeros(self.n_maps * self.max_det, np.uint32)
         _check(lib().smg_get_assoc_all(self.h, _ptr(out)), "smg_get_assoc_all")
         return out.reshape(self.n_maps, self.max_det)
+
+    def set_text_model(self, t: dict) -> None:
+        """smg_set_text_model from a synth.text_model dict (host arrays, copied)."""
+        x = {k: (np.ascontiguousarray(v) if isinstance(v, np.ndarray) else v) for k, v in t.items()}
+        self._text_keep = x
+        rows = x["text"].shape[0]
+        from .text import SmgText
+        st = SmgText()
+        st.dim = x["text"].shape[1] if rows else self.D
+        st.n_labels = x["n_labels"]
+        st.rows = rows
+        st.text = _ptr(x["text"]) if rows else None
+        st.row_label = _ptr(x["row_label"]) if rows else None
+        st.scale, st.bias = x["scale"], x["bias"]
+        for k in ("log_prior", "ls_mu", "ls_sd", "parent"):
+            setattr(st, k, _ptr(x[k]) if x.get(k) is not None else None)
+        st.object_label = x["object_label"]
+        opt = lambda k: _ptr(x[k]) if x.get(k) is not None else None
+        _check(lib().smg_set_text_model(self.h, C.byref(st), opt("kinds"), opt("so_shape"), opt("flat_ok")), "smg_set_text_model")
+        self._nlab = x["n_labels"]
+
+    def object_name(self, m: int, i: int) -> dict:
+        n = self._nlab
+        post = np.zeros(n, np.float32)
+        lab = np.zeros(3, np.int32)
+        val = np.zeros(3, np.float32)
+        k = _check(lib().smg_get_object_name(self.h, m, i, _ptr(post), _ptr(lab), _ptr(val)), "smg_get_object_name")
+        return dict(has_post=k > 0, post=post, name_lab=int(lab[0]), top_lab=int(lab[1]), rolled=int(lab[2]), name_p=float(val[0]),
+                    top_p=float(val[1]), name_H=float(val[2]))
 
     def assoc_all_async(self, out_ptr: int) -> int:
         """Enqueue the read of every map's association into host memory at out_ptr (n_maps x

@@ -213,3 +213,55 @@ class BoxRoom:
                     eef=np.asarray(eef, np.float64), grip=np.asarray(grip, np.float32), eef_base=self.eef_base,
                     n_det=n, det_label=det_label[:n].copy(), box=box[:n].copy(), cls=cls[:n].copy(),
                     score=score[:n].copy(), emb=emb[:n].copy(), emb_dim=self.D, **extra)
+
+
+# ---- a synthetic text model for the box rooms (label table, text rows, statistics) ----
+# Labels 0..15 are the detector classes (a box's class is its index mod 16); 16-19 room structure
+# and stairs; 20 "furniture" (hypernym of chair / table / sofa / cabinet, no text row) and 21
+# "object" (the fallback name, no text row).  Kinds: 0 object, 1 structure, 2 static, 3
+# structural object (the reference's kKind* values).
+TEXT_LABELS = ["box", "chair", "table", "sofa", "cabinet", "door", "window", "pillar", "picture", "tv", "cup", "bottle", "book",
+               "bag", "lamp", "plant", "wall", "floor", "ceiling", "stairs", "furniture", "object"]
+TEXT_KINDS = [0, 0, 2, 2, 2, 3, 3, 3, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 3, 0, 0]
+TEXT_SO_SHAPE = [0, 0, 0, 0, 0, 1, 1, 3, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 2, 0, 0]
+TEXT_FLAT = [0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0]
+TEXT_PARENT = [-1, 20, 20, 20, 20, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1]
+TEXT_LOGSIZE = [(-0.9, 0.5), (-0.5, 0.4), (-0.2, 0.5), (0.0, 0.5), (-0.1, 0.5), (0.6, 0.4), (0.2, 0.5), (0.8, 0.6), (-0.9, 0.5),
+                (-0.7, 0.5), (-2.3, 0.4), (-1.9, 0.4), (-1.8, 0.4), (-1.0, 0.5), (-0.8, 0.5), (-0.9, 0.6), (1.2, 0.5), (1.4, 0.5),
+                (1.4, 0.5), (0.9, 0.5), (0.0, 0.0), (0.0, 0.0)]
+
+
+def text_model(room: "BoxRoom", scale: float = 20.0, bias: float = -6.0, seed: int = 7) -> dict:
+    """A text model whose rows sit near the rooms' own embeddings: the row of class c is the
+    normalised sum of the base directions (the noise-free embedding) of the boxes of class c,
+    walls / floor / ceiling rows come from the room faces' bases, and labels without boxes get a
+    seeded random row; "furniture" and "object" have none (a hypernym and the fallback name)."""
+    L = lib()
+    nl, D = len(TEXT_LABELS), room.D
+    rng = np.random.default_rng(seed)
+    base = np.zeros(D, np.float32)
+
+    def base_of(label_value: int) -> np.ndarray:
+        dl = np.array([label_value], np.uint16)
+        L.sy_embed(C.byref(room.scene), 1, 1, _p(dl, C.c_uint16), D, 0.0, 0, _p(base, C.c_float))
+        return base.astype(np.float64).copy()
+
+    acc = [np.zeros(D) for _ in range(nl)]
+    for b in range(room.scene.n_boxes):
+        acc[b % 16] += base_of(1 + 3 * b)
+    for face in range(6):
+        lab = 16 if face < 4 else (17 if face == 4 else 18)
+        acc[lab] += base_of(SY_SHELL_LABEL0 + face)
+    rows, row_label = [], []
+    for c in range(nl):
+        if c in (20, 21):
+            continue
+        v = acc[c] if np.any(acc[c]) else rng.normal(size=D)
+        rows.append((v / np.linalg.norm(v)).astype(np.float32))
+        row_label.append(c)
+    lp = np.log(np.full(nl, 1.0 / nl)) + rng.normal(scale=0.1, size=nl)
+    return dict(text=np.ascontiguousarray(np.stack(rows), np.float32), row_label=np.asarray(row_label, np.int32), scale=scale,
+                bias=bias, n_labels=nl, log_prior=lp.astype(np.float32),
+                ls_mu=np.asarray([m for m, _ in TEXT_LOGSIZE], np.float32), ls_sd=np.asarray([s for _, s in TEXT_LOGSIZE], np.float32),
+                parent=np.asarray(TEXT_PARENT, np.int32), object_label=21, kinds=np.asarray(TEXT_KINDS, np.uint8),
+                so_shape=np.asarray(TEXT_SO_SHAPE, np.uint8), flat_ok=np.asarray(TEXT_FLAT, np.uint8))
