@@ -470,6 +470,58 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
 
 // subsample (objmap.cpp:37-42) of v[0..n) into S (<= SMG_SUB values); returns its size.
 // Each thread issues its (up to 4) loads before storing any.  No barrier: the caller syncs.
+// A point of the back-projection is kept as its pixel (v << 16 | u) and float depth; its map
+// coordinates are recomputed where needed with the same operations (objmap.cpp:680-683), so
+// every use sees the same doubles the reference computes, and the per-point scratch traffic is
+// 8 bytes instead of 40.
+DEV void bp_map(const FrameDev& F, uint32_t pix, float z, double* X, double* Y, double* Zm) {
+  const int uu = (int)(pix & 0xffffu), vv = (int)(pix >> 16);
+  const double xc = (double)(((float)uu - F.cx) / F.fx * z), yc = (double)(((float)vv - F.cy) / F.fy * z);
+  const double zd = (double)z;
+  const double* T = F.T_mc;
+  *X = T[0] * xc + T[1] * yc + T[2] * zd + T[3];
+  *Y = T[4] * xc + T[5] * yc + T[6] * zd + T[7];
+  *Zm = T[8] * xc + T[9] * yc + T[10] * zd + T[11];
+}
+
+// the detector-image pixel a point's mask cell is read at (objmap.cpp:686-687)
+DEV void bp_cell(const FrameDev& F, uint32_t pix, bool bits_form, int32_t* pu, int32_t* pv) {
+  const int uu = (int)(pix & 0xffffu), vv = (int)(pix >> 16);
+  if (bits_form) {
+    *pu = (int)(((float)uu + 0.5f) / F.sxu_f);
+    *pv = (int)(((float)vv + 0.5f) / F.syv_f);
+  } else {
+    *pu = uu;
+    *pv = vv;
+  }
+}
+
+// subsample_to of the depths (double) of the float depth list
+DEV int subsample_z(const float* v, int n, double* S) {
+  const int nS = n <= SMG_SUB ? n : SMG_SUB;
+  for (int i = threadIdx.x; i < nS; i += blockDim.x) {
+    const size_t src = n <= SMG_SUB ? (size_t)i : (size_t)i * (size_t)n / SMG_SUB;
+    S[i] = INB(src, n, 118) ? (double)v[src] : 0.0;
+  }
+  return nS;
+}
+
+// the three coordinate subsamples of the kept points (indices KI into the point list)
+DEV int subsample_xyz(const FrameDev& F, const uint32_t* PIX, const float* ZF, const int32_t* KI, int np, int n, double* SX,
+                      double* SY, double* SZ) {
+  const int nS = np <= SMG_SUB ? np : SMG_SUB;
+  for (int i = threadIdx.x; i < nS; i += blockDim.x) {
+    const size_t src = np <= SMG_SUB ? (size_t)i : (size_t)i * (size_t)np / SMG_SUB;
+    double x = 0, y = 0, z = 0;
+    if (INB(src, np, 121)) {
+      const int p = KI[src];
+      if (INB(p, n, 122)) bp_map(F, PIX[p], ZF[p], &x, &y, &z);
+    }
+    SX[i] = x; SY[i] = y; SZ[i] = z;
+  }
+  return nS;
+}
+
 DEV int subsample_to(const double* v, int n, double* S) {
   const int nS = n <= SMG_SUB ? n : SMG_SUB;
   for (int c0 = 0; c0 < nS; c0 += 4 * blockDim.x) {
@@ -517,15 +569,9 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   }
 #endif
   const size_t slot = (size_t)m * B.max_det + k;
-  double* X = B.px + slot * 4 * B.pmax;
-  double* Y = X + B.pmax;
-  double* Z = Y + B.pmax;
-  double* ZC = Z + B.pmax;
-  int32_t* PU = B.ppix + slot * 2 * B.pmax;
-  int32_t* PV = PU + B.pmax;
-  double* XK = B.pk + slot * 3 * B.pmax;
-  double* YK = XK + B.pmax;
-  double* ZK = YK + B.pmax;
+  uint32_t* PIX = (uint32_t*)(B.px + slot * 4 * B.pmax);   // per point: pixel (v << 16 | u)
+  float* ZF = (float*)(PIX + B.pmax);                       // per point: depth
+  int32_t* KI = (int32_t*)(ZF + B.pmax);                    // kept points (band filter), in order
   float* CX = B.cxyz + slot * 3 * B.pmax;
   int32_t* CP = B.cpx + slot * 2 * B.pmax;
   double* SCR = B.sel + slot * 4 * B.pmax;
@@ -587,20 +633,9 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
       if (!((okm >> j) & 1)) continue;
       const int idx = i0 + j, r = idx / ncols, cc = idx - r * ncols;
       const int uu = u0 + cc * sk, vv = v0 + r * sk;
-      const float z = zv[j];
-      const double xc = (double)(((float)uu - F.cx) / F.fx * z), yc = (double)(((float)vv - F.cy) / F.fy * z);
-      const double zd = (double)z;
       if (INB(o, B.pmax, 101)) {
-        X[o] = T[0] * xc + T[1] * yc + T[2] * zd + T[3];
-        Y[o] = T[4] * xc + T[5] * yc + T[6] * zd + T[7];
-        Z[o] = T[8] * xc + T[9] * yc + T[10] * zd + T[11];
-        ZC[o] = zd;
-        if (bits_form) {
-          PU[o] = (int)(((float)uu + 0.5f) / F.sxu_f);
-          PV[o] = (int)(((float)vv + 0.5f) / F.syv_f);
-        } else {
-          PU[o] = uu; PV[o] = vv;
-        }
+        PIX[o] = (uint32_t)vv << 16 | (uint32_t)uu;
+        ZF[o] = zv[j];
       }
       ++o;
     }
@@ -613,7 +648,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   __syncthreads();
   PHASE_MARK(0);   // back-projection
   // 2. MAD depth band (objmap.cpp:692-695)
-  int nS = subsample_to(ZC, n, S);
+  int nS = subsample_z(ZF, n, S);
   __syncthreads();
   const int kmed = pct_index(nS, 0.5);
   const double zmed = block_select(S, nS, kmed, hist, bs);
@@ -635,9 +670,10 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     const int i = c0 + tid;
     int keep = 0, hs = -1;
     if (i < n) {
-      keep = INB(i, B.pmax, 112) && !(fabs(ZC[i] - zmed) > band);
+      keep = INB(i, B.pmax, 112) && !(fabs((double)ZF[i] - zmed) > band);
       if (keep) {
-        const double x = X[i], y = Y[i], z = Z[i];
+        double x, y, z;
+        bp_map(F, PIX[i], ZF[i], &x, &y, &z);
         const double d0 = (x - E0[0]) * (x - E0[0]) + (y - E0[1]) * (y - E0[1]) + (z - E0[2]) * (z - E0[2]);
         const double d1 = (x - E1[0]) * (x - E1[0]) + (y - E1[1]) * (y - E1[1]) + (z - E1[2]) * (z - E1[2]);
         const double dh2 = smin(d0, d1);
@@ -657,7 +693,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     }
     int tot;
     const int pos = block_scan_db(keep, &tot, scan_db, scan_it++);
-    if (keep && INB(w + pos, B.pmax, 102)) { XK[w + pos] = X[i]; YK[w + pos] = Y[i]; ZK[w + pos] = Z[i]; }
+    if (keep && INB(w + pos, B.pmax, 102)) KI[w + pos] = i;
     w += tot;
   }
   const int near_hand = block_sum_i(near_local, bs);
@@ -674,11 +710,12 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     int tot;
     const int pos = block_scan_db(emit, &tot, scan_db, scan_it++);
     if (emit && INB(nc + pos, B.pmax, 103)) {
-      CX[3 * (nc + pos)] = (float)X[i];
-      CX[3 * (nc + pos) + 1] = (float)Y[i];
-      CX[3 * (nc + pos) + 2] = (float)Z[i];
-      CP[2 * (nc + pos)] = PU[i];
-      CP[2 * (nc + pos) + 1] = PV[i];
+      double x, y, z;
+      bp_map(F, PIX[i], ZF[i], &x, &y, &z);
+      CX[3 * (nc + pos)] = (float)x;
+      CX[3 * (nc + pos) + 1] = (float)y;
+      CX[3 * (nc + pos) + 2] = (float)z;
+      bp_cell(F, PIX[i], bits_form, &CP[2 * (nc + pos)], &CP[2 * (nc + pos) + 1]);
     }
     nc += tot;
   }
@@ -691,11 +728,9 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   // 4. 10/50/90 percentiles per axis (objmap.cpp:730-738): nine order statistics, one sweep
   double lo[3], md[3], hi[3];
   {
-    const double* AX[3] = {XK, YK, ZK};
     double* SB[3] = {S, S + SMG_SUB, S + 2 * SMG_SUB};
     int* mh = (int*)(S + 3 * SMG_SUB);
-    int nS3 = 0;
-    for (int a = 0; a < 3; ++a) nS3 = subsample_to(AX[a], np, SB[a]);
+    const int nS3 = subsample_xyz(F, PIX, ZF, KI, np, n, SB[0], SB[1], SB[2]);
     __syncthreads();
     const double* arr[9] = {SB[0], SB[0], SB[0], SB[1], SB[1], SB[1], SB[2], SB[2], SB[2]};
     const int nn[9] = {nS3, nS3, nS3, nS3, nS3, nS3, nS3, nS3, nS3};
