@@ -47,3 +47,25 @@ def test_bit_masks_on_the_image_grid_equal_the_label_image_on_the_reference():
                       mask_affine=(1.0, 1.0, 0.0, 0.0)))
         assert A.objects() == Bm.objects()
         assert A.stats() == Bm.stats()
+
+
+def test_text_model_reaches_its_rules():
+    """With the synthetic text model the reference names objects (some through the hypernym /
+    fallback roll-up), blocks wall-looking fragments from non-structure objects, and drops
+    structure: the rules the device text model is compared on are reached."""
+    from oracle import ref
+    from scenemap_b200 import synth
+    if not ref.available():
+        pytest.skip("reference oracle library not built")
+    v = variants.structure(60)
+    kw = dict(v["gen"])
+    g = synth.BoxRoom(seed=synth.map_seed(kw.pop("seed_base"), 0), n_frames=v["n_frames"], D=1152, **kw)
+    R = ref.RefMap(v["kv"])
+    R.set_text_model(synth.text_model(g))
+    for f in range(v["n_frames"]):
+        R.frame(g.frame(f))
+    names = [R.object_name(i) for i in range(len(R.objects()))]
+    assert sum(n["has_post"] for n in names) >= 10
+    assert sum(n["rolled"] for n in names) >= 1
+    st = R.stats()
+    assert st["n_blocked"] > 0 and st["n_obj_struct"] > 0
