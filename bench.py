@@ -138,7 +138,7 @@ def parse():
 # ------------------------------------------------------------------ clocks
 class Clocks:
     """SM clock and clock-event (throttle) reasons sampled while the timed region runs: NVML
-    every 5 ms in a thread (a short timed region still gets samples), else `nvidia-smi -lms 200`
+    every 2 ms in a thread (a short timed region still gets samples), else `nvidia-smi -lms 200`
     into a temporary CSV.  Reading only; nothing is set."""
     REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
@@ -167,7 +167,7 @@ class Clocks:
                         self.bits |= int(reasons_fn(h))
                     except Exception:
                         pass
-                    self.stop_ev.wait(0.005)
+                    self.stop_ev.wait(0.002)
             self.thread = threading.Thread(target=run, daemon=True)
             self.thread.start()
             return
@@ -189,7 +189,7 @@ class Clocks:
             self.thread.join(timeout=5)
             reasons = sorted(name for bit, name in self.REASONS.items() if self.bits & bit)
             return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.mx, "reasons": reasons,
-                    "samples": len(self.sm), "source": "nvml, 5 ms"}
+                    "samples": len(self.sm), "source": "nvml, 2 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()

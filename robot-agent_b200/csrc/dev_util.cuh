@@ -235,12 +235,13 @@ DEV double d_unord(uint64_t k) {
 // Exact k-th smallest (0-based) of a[0..n) by MSB-first radix selection on the ordered bit
 // pattern: returns exactly the value std::nth_element leaves at position k.
 // hist: SEL_HIST(1) shared ints.  All threads of the block must call it.
-DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s);
-DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& s) {
+DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s,
+                            unsigned long long* list = nullptr);
+DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& s, unsigned long long* list = nullptr) {
   __shared__ double sel1;
   const double* arr[1] = {a};
   const int nn[1] = {n}, kk[1] = {k};
-  block_select_multi(arr, nn, kk, &sel1, 1, hist, s);
+  block_select_multi(arr, nn, kk, &sel1, 1, hist, s, list);
   return sel1;
 }
 
@@ -250,15 +251,20 @@ DEV double block_select(const double* a, int n, int k, int* hist, BlockScratch& 
 // 8 per round, with one histogram of the keys under its decided prefix per round.  Queries on
 // the same array share the first histogram (their prefixes only part after it).  Once the
 // chosen digit holds at most SEL_GATHER keys, those are gathered and ranked by one warp instead
-// of running the remaining rounds.  Two barriers per round.
+// of running the remaining rounds.  With list (nq x SEL_LIST shared words), a query whose chosen
+// digit holds at most SEL_LIST keys copies them to its list in the next round, and the rounds
+// after that read only the list.  Two barriers per round.
 // hist: SEL_HIST(nq) shared ints.  Needs nq <= warps of the block.  All threads must call it.
 #define SEL_MAXQ 9
 #define SEL_GATHER 32
+#define SEL_LIST 256
 #define SEL_HIST(nq) (2 * (nq) * 256)
-DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s) {
+DEV void block_select_multi(const double* const* a, const int* n, const int* kq, double* out, int nq, int* hist, BlockScratch& s,
+                            unsigned long long* list) {
   __shared__ unsigned long long sh_prefix[SEL_MAXQ], sh_mn[SEL_MAXQ], sh_mx[SEL_MAXQ];
   __shared__ unsigned long long sh_g[SEL_MAXQ][SEL_GATHER];
   __shared__ int sh_k[SEL_MAXQ], sh_dec[SEL_MAXQ], sh_mode[SEL_MAXQ], sh_gn[SEL_MAXQ], sh_first[SEL_MAXQ], sh_ld[SEL_MAXQ], sh_live;
+  __shared__ int sh_lst[SEL_MAXQ], sh_ln[SEL_MAXQ];   // list state (0 none, 1 filling this round, 2 filled), length
   const int tid = threadIdx.x, lane = tid & 31, wq = tid >> 5;
   int* hist0 = hist + nq * 256;   // first histogram of each group leader (queries on one array share it)
 #ifdef SMG_CHECKS
@@ -272,6 +278,7 @@ DEV void block_select_multi(const double* const* a, const int* n, const int* kq,
       if (a[q] == a[tid] && n[q] == n[tid]) { ld = q; break; }
     sh_ld[tid] = ld;
     sh_k[tid] = kq[tid]; sh_mode[tid] = 0; sh_gn[tid] = 0; sh_first[tid] = 1; sh_mn[tid] = ~0ull; sh_mx[tid] = 0ull;
+    sh_lst[tid] = 0; sh_ln[tid] = 0;
   }
   if (tid == 0) sh_live = nq;
   __syncthreads();
@@ -317,11 +324,17 @@ DEV void block_select_multi(const double* const* a, const int* n, const int* kq,
       const uint64_t pre = sh_prefix[q], msk = dec == 0 ? 0ull : ~0ull << (64 - dec);
       const int wdt = 64 - dec < 8 ? 64 - dec : 8, shift = 64 - dec - wdt;   // next digit: bits [shift, shift + wdt)
       int* hq = (first ? hist0 : hist) + q * 256;
+      const int lst = sh_lst[q];
+      unsigned long long* lq = list ? list + (size_t)q * SEL_LIST : nullptr;
       const double* aq = a[q];
-      const int nqq = n[q];
+      const int nqq = lst == 2 ? sh_ln[q] : n[q];
       for (int i = tid; i < nqq; i += blockDim.x) {
-        const uint64_t key = d_ord(aq[i]);
+        const uint64_t key = lst == 2 ? lq[i] : d_ord(aq[i]);
         if ((key & msk) != pre) continue;
+        if (lst == 1) {   // the keys under the new prefix go to the query's list
+          const int slot = atomicAdd(&sh_ln[q], 1);
+          if (INB(slot, SEL_LIST, 134)) lq[slot] = key;
+        }
         if (mode == 0) {
           atomicAdd(&hq[(unsigned)(key >> shift) & ((1u << wdt) - 1u)], 1);
         } else {
@@ -332,6 +345,11 @@ DEV void block_select_multi(const double* const* a, const int* n, const int* kq,
     }
     __syncthreads();
     // B: warp q picks the digit holding rank k (clearing its own counters), or ranks the gathered keys
+    if (wq < nq && sh_lst[wq] == 1) {   // the list was filled in this round's pass
+      __syncwarp();
+      if (lane == 0) sh_lst[wq] = 2;
+      __syncwarp();
+    }
     if (wq < nq && sh_mode[wq] != 2) {
       const int k = sh_k[wq];
       if (sh_mode[wq] == 0) {
@@ -365,6 +383,9 @@ DEV void block_select_multi(const double* const* a, const int* n, const int* kq,
             atomicSub(&sh_live, 1);
           } else if (c[b] <= SEL_GATHER) {
             sh_mode[wq] = 1;
+          } else if (list && sh_lst[wq] == 0 && c[b] <= SEL_LIST) {
+            sh_lst[wq] = 1;   // the next round copies the chosen digit's keys to the list
+            sh_ln[wq] = 0;
           }
         } else if (lane == 0 && !(k >= 0 && k < all)) {   // rank outside the keys: no selection
           out[wq] = d_unord(sh_prefix[wq]);

@@ -16,6 +16,8 @@
 #define OBS_THREADS 512
 #define OBS_HASH 8192
 #define OBS_SMEM (OBS_HASH * 12)   // k_obs dynamic shared memory: the voxel hash, reused by later phases
+static_assert(3 * SMG_SUB * 8 + SEL_HIST(9) * 4 + 9 * SEL_LIST * 8 <= OBS_SMEM,
+              "k_obs: the percentile subsamples, histograms and candidate lists must fit the hash's shared memory");
 #define OBS_PPT 4      // raster pixels per thread in the back-projection
 #define RANSAC_MAX 256
 #define RANSAC_DRAWS (3 * RANSAC_MAX + 64)
@@ -298,6 +300,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   if (tid == 0) sh_deg = 0;
   double pl[4] = {sh_best[0], sh_best[1], sh_best[2], sh_best[3]};
   double mp[4];
+  double ch[3] = {0, 0, 0};   // the last pass's horizontal second moments (c00, c01, c11)
   int ni = 0;
   for (int pass = 0; pass < 2; ++pass) {
     for (int k = 0; k < 4; ++k) mp[k] = pl[k];
@@ -325,6 +328,7 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
       }
     }
     block_sum_multi<6>(c, red);
+    ch[0] = c[0]; ch[1] = c[1]; ch[2] = c[3];
     double C[3][3];
     C[0][0] = c[0] * inv; C[0][1] = c[1] * inv; C[0][2] = c[2] * inv;
     C[1][1] = c[3] * inv; C[1][2] = c[4] * inv; C[2][2] = c[5] * inv;
@@ -345,18 +349,10 @@ DEV void plane_fit(const float* xyz, int n, double tau, uint64_t seed, int max_i
   }
   double th_hc = 0, th_hs = 0;
   if (ni >= 3) {
-    const double m0 = sh_m[0], m1 = sh_m[1];
-    // horizontal principal direction of the inliers (objprob.cpp:187-192)
-    double a3[3] = {0, 0, 0};
-    for (int i = tid; i < n; i += blockDim.x) {
-      const double x = xyz[3 * i], y = xyz[3 * i + 1], z = xyz[3 * i + 2];
-      if (fabs(mp[0] * x + mp[1] * y + mp[2] * z + mp[3]) <= tau) {
-        const double dx = x - m0, dy = y - m1;
-        a3[0] += dx * dx; a3[1] += dx * dy; a3[2] += dy * dy;
-      }
-    }
-    block_sum_multi<3>(a3, red);
-    const double sxx = a3[0], sxy = a3[1], syy = a3[2];
+    // horizontal principal direction of the inliers (objprob.cpp:187-192): its sums over the
+    // last pass's inliers about the last pass's mean are that pass's covariance sums c00, c01,
+    // c11 (the same points, the same operations, the same reduction tree)
+    const double sxx = ch[0], sxy = ch[1], syy = ch[2];
     if (tid == 0 && 2 * fabs(sxy) + fabs(sxx - syy) <= 1e-3 * (sxx + syy)) sh_deg = 1;
     jacobi_cs(2 * sxy, sxx - syy, &th_hc, &th_hs);
   }
@@ -651,10 +647,11 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   int nS = subsample_z(ZF, n, S);
   __syncthreads();
   const int kmed = pct_index(nS, 0.5);
-  const double zmed = block_select(S, nS, kmed, hist, bs);
+  unsigned long long* slist = (unsigned long long*)(hist + SEL_HIST(1));   // candidate list of the selection
+  const double zmed = block_select(S, nS, kmed, hist, bs, slist);
   for (int i = tid; i < nS; i += blockDim.x) S[i] = fabs(S[i] - zmed);
   __syncthreads();
-  const double mad = block_select(S, nS, kmed, hist, bs);
+  const double mad = block_select(S, nS, kmed, hist, bs, slist);
   const double band = smax(P.mad_k * 1.4826 * mad, P.mad_floor);
   __syncthreads();
   PHASE_MARK(1);   // MAD band
@@ -737,7 +734,7 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
     const int kk[9] = {pct_index(nS3, 0.5), pct_index(nS3, 0.1), pct_index(nS3, 0.9), pct_index(nS3, 0.5), pct_index(nS3, 0.1),
                        pct_index(nS3, 0.9), pct_index(nS3, 0.5), pct_index(nS3, 0.1), pct_index(nS3, 0.9)};
     __shared__ double sel9[9];
-    block_select_multi(arr, nn, kk, sel9, 9, mh, bs);
+    block_select_multi(arr, nn, kk, sel9, 9, mh, bs, (unsigned long long*)(mh + SEL_HIST(9)));
     for (int a = 0; a < 3; ++a) { md[a] = sel9[3 * a]; lo[a] = sel9[3 * a + 1]; hi[a] = sel9[3 * a + 2]; }
     __syncthreads();
   }
