@@ -32,6 +32,8 @@ enum {
 };
 
 enum { SMG_MEM_DEVICE = 0, SMG_MEM_HOST = 1 };
+/* wall segments a keyframe may carry (smg_frame::wall_segs) */
+#define SMG_WALL_SEGS_MAX 1024
 enum { SMG_EMB_F32 = 0, SMG_EMB_BF16 = 1 };
 
 /* Parameters.  Field names and defaults mirror the reference structs:
@@ -109,6 +111,14 @@ typedef struct smg_params {
   double name_tau, name_wmax, size_w, whole_w, geo_w, flat_max_w, wall_big, struct_p;
   double so_dw_w, so_dw_thick, so_max_h, so_pillar, so_stairs, so_dw_min, so_hide_k, wallhug_frac, wallhug_w, big_vinl;
   int32_t struct_look_block, so_min_obs;
+  /* ApParams wall-line rules (objprob.hpp:101-117): a point within wall_d of a wall segment is
+   * on a wall line, wall_frac of a thin upright fragment's points on one makes it a wall plane;
+   * a fragment whose centre lies beyond a wall segment, seen from the camera, by more than
+   * through_d is dropped; an object whose dominant plane is thinner than obj_flat_thick with
+   * obj_flat_frac of its points within obj_flat_d of a wall line is a flat plane on the wall
+   * (geo 3).  bridge_max: the longest gap between two collinear segments that the extracted set
+   * closes (capi.cpp:873-887; 0 = none).  They act when a keyframe carries wall segments. */
+  double wall_d, wall_frac, through_d, bridge_max, obj_flat_thick, obj_flat_d, obj_flat_frac;
 } smg_params;
 
 /* One frame of one map.  depth/label/emb/dets/masks live in device memory (SMG_MEM_DEVICE) or
@@ -155,6 +165,13 @@ typedef struct smg_frame {
    * smg_get_views.  Without it, points are grey (128) and no view is picked, as in the
    * reference with no RGB source. */
   const uint8_t* rgba;
+  /* ObjFrame::wall_segs / n_wall_segs (objmap.hpp:219-220): n_wall_segs x (ax, ay, bx, by),
+   * map metres, at most SMG_WALL_SEGS_MAX, or NULL.  A non-NULL set replaces the map's stored
+   * one (ObjectMap::wsegs_, read by apStructObject) and this keyframe's fragments get the
+   * wall-line tests (apObsStructural, the see-through drop); NULL keeps the stored set and
+   * skips the keyframe's tests, as in the reference (objmap.cpp:534, 605, 742). */
+  const double* wall_segs;
+  int32_t n_wall_segs;
 } smg_frame;
 
 typedef struct smg_batch smg_batch;
@@ -166,12 +183,9 @@ int smg_params_size(void);
 int smg_params_default(smg_params* p);
 /* ObjectMap::applyParams (scenemap src/objmap.cpp:132-205): "key=val,...".  Returns the number
  * of unknown keys (0 = all known), or SMG_ERR_ARGS.  Keys of reference features this build does
- * not run (text-model naming and structural-name rules, wall segments, inspect, the export
- * filter: ap_name_tau, ap_name_wmax, ap_size_w, ap_wall_big, ap_struct_p, ap_whole_w,
- * ap_export_named, ap_geo_w, ap_through_d, ap_bridge_max, ap_so_*, ap_wallhug_*,
- * ap_struct_look_block, ap_flat_max_w, ap_big_vinl, inspect) are accepted at their reference
- * default only; any other value makes the call return SMG_ERR_UNSUPPORTED (all other keys are
- * still applied) and smg_last_error names them. */
+ * not run (the inspect pass and the export filter: inspect, ap_export_named) are accepted at
+ * their reference default only; any other value makes the call return SMG_ERR_UNSUPPORTED (all
+ * other keys are still applied) and smg_last_error names them. */
 int smg_params_apply(smg_params* p, const char* kv);
 
 /* ObjectMap::setCloudParams (scenemap objmap.hpp:255-258): voxel > 0 and cap > 0 override. */
@@ -281,6 +295,11 @@ typedef struct smg_object {
   int32_t held_by;             /* hand holding the object, -1 = none (MapObject::held_by) */
   uint32_t parent;             /* object it rests on / in and follows, 0 = none (MapObject::parent) */
   double parent_rel[3];
+  /* ApState wall-line state: wall_like (a thin upright plane on a wall line or structure-looking),
+   * hide (apStructObject: kept but not exported as a node), n_wall_obs (wall-like fragments
+   * seen), fw (share of the cloud sample within wall_d of a wall segment) */
+  int32_t wall_like, hide, n_wall_obs;
+  float fw;
 } smg_object;
 
 /* ObjectMap::objects() (scenemap objmap.hpp:242) of map m, in the reference's order. */

@@ -27,7 +27,8 @@ class RfFrame(C.Structure):
                 ("grid_only", C.c_int), ("grip", C.c_float * 2), ("mask_bits", C.POINTER(C.c_uint32)),
                 ("mask_w", C.c_int), ("mask_h", C.c_int), ("mask_sx", C.c_float), ("mask_sy", C.c_float),
                 ("mask_ox", C.c_float), ("mask_oy", C.c_float), ("img_w", C.c_int), ("img_h", C.c_int),
-                ("depth_mm", C.POINTER(C.c_uint16)), ("rgba", C.POINTER(C.c_uint8))]
+                ("depth_mm", C.POINTER(C.c_uint16)), ("rgba", C.POINTER(C.c_uint8)),
+                ("wall_segs", C.POINTER(C.c_double)), ("n_wall_segs", C.c_int)]
 
 
 class RfView(C.Structure):
@@ -50,7 +51,7 @@ class RfObj(C.Structure):
                 ("n_ap_obs", C.c_int32), ("n_wall_obs", C.c_int32), ("n_struct_look", C.c_int32),
                 ("need_whole", C.c_int32), ("n_whole", C.c_int32), ("P", C.c_double * 3), ("n_cams", C.c_int32),
                 ("geo", C.c_int32), ("drop", C.c_int32), ("hide", C.c_int32), ("held_by", C.c_int32),
-                ("parent", C.c_uint32), ("parent_rel", C.c_double * 3)]
+                ("parent", C.c_uint32), ("parent_rel", C.c_double * 3), ("wall_like", C.c_int32), ("fw", C.c_float)]
 
 
 STAT_FIELDS = ["n_through", "n_obs", "n_wall", "n_wall_name", "n_ceil", "n_floor", "n_assoc", "n_new", "n_merge",
@@ -160,6 +161,11 @@ def make_rf_frame(fr: dict, keep: list) -> RfFrame:
         rgba = np.ascontiguousarray(fr["rgba"], np.uint8)
         keep.append(rgba)
         f.rgba = _p(rgba, C.c_uint8)
+    if fr.get("wall_segs") is not None:   # ObjFrame::wall_segs; an empty set is still a set
+        ws = np.ascontiguousarray(fr["wall_segs"], np.float64).reshape(-1, 4)
+        buf = ws if len(ws) else np.zeros(4)
+        keep.append(buf)
+        f.wall_segs, f.n_wall_segs = _p(buf, C.c_double), len(ws)
     f.fx, f.fy, f.cx, f.cy = fr["fx"], fr["fy"], fr["cx"], fr["cy"]
     for i in range(12):
         f.T_mc[i] = fr["T_mc"][i]

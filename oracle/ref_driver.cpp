@@ -60,6 +60,8 @@ typedef struct {
   int img_w, img_h;       // detector image (0 = the depth image's size)
   const uint16_t* depth_mm;   // ObjFrame::depth_mm / DepthView::mm, when depth is null
   const uint8_t* rgba;        // sm_image::rgba (w x h x 4), or null
+  const double* wall_segs;    // ObjFrame::wall_segs (n_wall_segs x 4), or null
+  int n_wall_segs;
 } rf_frame;
 
 typedef struct {
@@ -89,6 +91,8 @@ typedef struct {
   int32_t held_by;
   uint32_t parent;
   double parent_rel[3];
+  int32_t wall_like;
+  float fw;
 } rf_obj;
 
 typedef struct {
@@ -216,6 +220,8 @@ int ref_frame(void* h, const rf_frame* f) {
   F.base_xy[1] = f->base[1];
   F.emb = f->emb;
   F.emb_dim = f->emb_dim;
+  F.wall_segs = f->wall_segs;
+  F.n_wall_segs = f->n_wall_segs;
   m->om.update(F);
   // best views (capi.cpp:903-943): moved / put-down events reset the view quality, views of
   // objects that are gone are dropped, detections attached to an object become candidates
@@ -408,6 +414,8 @@ int ref_objects(void* h, rf_obj* out, int cap) {
       r.geo = s.geo;
       r.drop = s.drop;
       r.hide = s.hide;
+      r.wall_like = s.wall_like;
+      r.fw = s.fw;
     }
   }
   return n;

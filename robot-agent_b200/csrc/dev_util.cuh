@@ -588,6 +588,22 @@ DEV double hypot3(double x, double y, double z) {
   x /= a; y /= a; z /= a;
   return a * sqrt(x * x + y * y + z * z);
 }
+// segDist (scenemap objmap.cpp:77-84): horizontal distance from (px, py) to segment s = (ax, ay,
+// bx, by), the parameter clamped to [0, 1]
+DEV double seg_dist(double px, double py, const double* s) {
+  const double ax = s[0], ay = s[1], bx = s[2], by = s[3];
+  const double dx = bx - ax, dy = by - ay, l2 = dx * dx + dy * dy;
+  double u = l2 > 1e-12 ? ((px - ax) * dx + (py - ay) * dy) / l2 : 0.0;
+  u = u < 0.0 ? 0.0 : (1.0 < u ? 1.0 : u);
+  return hypot(px - ax - u * dx, py - ay - u * dy);
+}
+// min over the first segments of the set until one lies within `stop` (the reference's early-out
+// loops): the result is <= stop exactly when some segment does
+DEV double wall_dist(double px, double py, const double* S, int n, double stop) {
+  double dm = 1e9;
+  for (int k = 0; k < n && dm > stop; ++k) dm = smin(dm, seg_dist(px, py, S + 4 * k));
+  return dm;
+}
 DEV double dist3(const double* a, const double* b) {
   return sqrt((a[0] - b[0]) * (a[0] - b[0]) + (a[1] - b[1]) * (a[1] - b[1]) + (a[2] - b[2]) * (a[2] - b[2]));
 }

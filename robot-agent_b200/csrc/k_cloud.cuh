@@ -437,6 +437,7 @@ __global__ void __launch_bounds__(512) k_cloud_add(Batch B) {
   if (!F.active) return;
   const MapRec& R = B.maps[m];
   const Work W = work_at(B, m, blockIdx.x);
+  PHASE_START();
   for (int j = blockIdx.x; j < R.n_targets; j += gridDim.x) {
     if (!INB(j, B.O, 405)) break;
     const int slot = B.tgt_slot[(size_t)m * B.O + j];
@@ -452,6 +453,8 @@ __global__ void __launch_bounds__(512) k_cloud_add(Batch B) {
       const int32_t* px = B.cpx + ((size_t)m * B.max_det + pr.det) * 2 * B.pmax;
       cloud_add(B, m, cs, xyz, nullptr, pr.n, F.stamp, W, hist, bs, px, F.views_on ? F.rgba : nullptr, F.w, F.h);
     }
+    PHASE_MARK(37);   // cloud additions of a target
     if (B.clouds[cs].cver != B.clouds[cs].version) contact_rebuild(B, cs, bs);
+    PHASE_MARK(38);   // its contact index
   }
 }

@@ -150,6 +150,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   for (int i = tid; i < MH_SLOTS; i += blockDim.x) { HKY[i] = INT64_MIN; HF[i] = 0x7fffffff; }
   for (int c = tid; c < ng; c += blockDim.x) CF[c] = 0;
   __syncthreads();
+  PHASE_MARK(30);
   for (int c = tid; c < ng; c += blockDim.x) {
     const int64_t key = MK[c];
     if (key == INT64_MIN) continue;
@@ -161,9 +162,11 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     }
   }
   __syncthreads();
+  PHASE_MARK(31);
   for (int i = tid; i < MH_SLOTS; i += blockDim.x)
     if (HKY[i] != INT64_MIN && INB(HF[i], ng, 702)) CF[HF[i]] = 1;
   __syncthreads();
+  PHASE_MARK(32);
   // rank of each cell = number of cells whose first pixel comes earlier (ordered scan)
   int nrank = 0;
   for (int c0 = 0; c0 < ng; c0 += blockDim.x) {
@@ -175,6 +178,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     nrank += tot;
   }
   __syncthreads();
+  PHASE_MARK(33);
   const int ncell = nrank < SMG_MATCH_CELLS ? nrank : SMG_MATCH_CELLS;   // later cells are dropped
   for (int i = tid; i < MH_SLOTS; i += blockDim.x)
     if (HKY[i] != INT64_MIN) HC[i] = CF[HF[i]] - 1;
@@ -192,6 +196,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     if (r < ncell) atomicAdd(&CC[r], 1);
   }
   __syncthreads();
+  PHASE_MARK(34);
   int off = 0;
   for (int r0 = 0; r0 < ncell; r0 += blockDim.x) {
     const int r = r0 + tid;
@@ -209,6 +214,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     if (INB(slot, ng, 701)) CPX[slot] = c;
   }
   __syncthreads();
+  PHASE_MARK(35);
   // raster order within each cell: a bucketed pixel's place is the number of pixels of its
   // cell with a smaller index (every slot counts over its own bucket, in parallel)
   int32_t* SPX = CF;   // the per-pixel first flags are dead here: sorted buckets
@@ -222,6 +228,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
     if (INB(s0 + pos, ng, 706)) SPX[s0 + pos] = v;
   }
   __syncthreads();
+  PHASE_MARK(36);
   float* OUT = B.sc_pts + (size_t)m * (2 * SMG_BINS_MAX + SMG_MATCH_CELLS) * 4;
   for (int r = tid; r < ncell; r += blockDim.x) {
     const int n = CC[r], e = CO[r], s0 = e - n;

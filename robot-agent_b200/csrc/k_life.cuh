@@ -388,6 +388,21 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
     int up = 0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) up += (double)Pt[3 * i + 2] > R.ceil_est - P.ceil_band;
     up = block_sum_i(up, bs);
+    // wall lines (ObjectMap::wsegs_): points within wall_d (the share fw, objmap.cpp:1298-1302)
+    // and within obj_flat_d (the flat-plane test, :1310-1317) of some stored segment
+    const bool walls = R.n_wseg > 0;
+    int nw = 0, nflat = 0;
+    if (walls && n > 0) {
+      const double* S = B.wsegs + (size_t)m * SMG_WALL_SEGS_MAX * 4;
+      const double stop = smin(P.wall_d, P.obj_flat_d);
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double dm = wall_dist((double)Pt[3 * i], (double)Pt[3 * i + 1], S, R.n_wseg, stop);
+        nw += dm <= P.wall_d;
+        nflat += dm <= P.obj_flat_d;
+      }
+      nw = block_sum_i(nw, bs);
+      nflat = block_sum_i(nflat, bs);
+    }
     if (threadIdx.x == 0) {
       o.geo_ver = C.version;
       int geo = 0;
@@ -399,13 +414,18 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
       }
       if (!geo && R.ceil_est > 0 && n > 0)
         if (up >= P.ceil_frac * n && smax(o.hi[0] - o.lo[0], o.hi[1] - o.lo[1]) >= P.ceil_wide) geo = 2;
+      o.fw = n > 0 ? (float)((double)nw / n) : 0.f;
+      // a very thin upright plane on a wall line: door leaf, window pane (objmap.cpp:1310-1317)
+      if (!geo && plane && pout.thick < P.obj_flat_thick && nz < P.wall_vert && walls && n > 0 && !(nflat < P.obj_flat_frac * n))
+        geo = 3;
       o.geo = geo;
       o.vinl = pout.ok && nz < P.wall_vert ? (float)pout.inl : 0.f;
     }
     __syncthreads();
-    if (B.text_on && n > 0) {
-      // the shape the named-structure rules read (objmap.cpp:1281-1301): 5-95 % spans along the
-      // horizontal principal axes and in height (no wall segments here: the wall share fw is 0)
+    if ((B.text_on || walls) && n > 0) {
+      // the shape the named-structure and wall-hugging rules read (objmap.cpp:1281-1301): 5-95 %
+      // spans along the horizontal principal axes and in height.  Without a text model and
+      // without wall segments no rule reads it (fw is then 0).
       double sx = 0, sy = 0;
       for (int i = threadIdx.x; i < n; i += blockDim.x) { sx += (double)Pt[3 * i]; sy += (double)Pt[3 * i + 1]; }
       const double mx = block_sum_d(sx, bs) / n, my = block_sum_d(sy, bs) / n;
@@ -445,8 +465,8 @@ __global__ void __launch_bounds__(256, 4) k_struct(Batch B) {
   }
 }
 
-// apStructObject's decision (objmap.cpp:1320-1349) on the object's geometry and name
-// posterior; sets hide.  No wall segments: the wall share fw is 0 and geo is never 3.
+// apStructObject's decision (objmap.cpp:1320-1349) on the object's geometry, wall share and
+// name posterior; sets hide.
 DEV bool struct_object_drop(const Batch& B, size_t og, ObjRec& o) {
   const smg_params& P = B.p;
   o.hide = 0;
@@ -456,7 +476,7 @@ DEV bool struct_object_drop(const Batch& B, size_t og, ObjRec& o) {
   if (post)
     for (int l = 0; l < C; ++l)
       if (kind_of(B, l) == KIND_STRUCT_OBJ) qso += (double)post[l];
-  const double fw = 0.0;
+  const double fw = (double)o.fw;
   if (qso >= 0.5 && o.geo != 2) {
     double qsh[4] = {0, 0, 0, 0};
     for (int l = 0; l < C; ++l)
@@ -509,11 +529,8 @@ __global__ void __launch_bounds__(256) k_prune(Batch B) {
     ObjRec& o = B.objs[oglob(B, m, slot)];
     if (o.held_by >= 0) {   // apStructObject returns false for a held object (objmap.cpp:1256)
       o.drop = 0;
-    } else if (B.text_on || B.kinds_on) {
-      o.drop = struct_object_drop(B, oglob(B, m, slot), o);
     } else {
-      o.hide = 0;
-      o.drop = o.geo == 1 || o.geo == 2;
+      o.drop = struct_object_drop(B, oglob(B, m, slot), o);
     }
     bool rm;
     if (o.drop) { ++nstruct; rm = true; }

@@ -790,7 +790,23 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   }
   __syncthreads();
   PHASE_MARK(5);
+  // wall-line share of apObsStructural (objmap.cpp:606-611): every stp-th candidate, within
+  // wall_d of some segment of this keyframe's set
+  int w_near = 0, w_tot = 0;
+  if (F.wall_set && F.n_wseg > 0 && nc >= 8) {
+    const double* S = B.wsegs + (size_t)m * SMG_WALL_SEGS_MAX * 4;
+    const int stp = nc / 64 > 1 ? nc / 64 : 1;
+    w_tot = (nc + stp - 1) / stp;
+    int near = 0;
+    for (int j = tid; j < w_tot; j += blockDim.x) {
+      const int i = j * stp;
+      near += wall_dist((double)CX[3 * i], (double)CX[3 * i + 1], S, F.n_wseg, P.wall_d) <= P.wall_d;
+    }
+    w_near = block_sum_i(near, bs);
+  }
   if (tid == 0) {
+    O->w_near = w_near;
+    O->w_tot = w_tot;
     O->pl_ok = pout.ok;
     for (int a = 0; a < 3; ++a) O->pl_n[a] = pout.n[a];
     O->pl_thick = pout.thick;
@@ -804,16 +820,18 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   }
 }
 
-// Structural decision and observation list, in detection order (objmap.cpp:741-765 and the
-// apObsStructural branches at :576-621 with no wall segments; ps, pso and the shape group come
-// from k_obs_text when a text model is set).
+// Structural decision and observation list, in detection order (objmap.cpp:741-765, the
+// see-through drop at :742-753 and the apObsStructural branches at :576-621; ps, pso and the
+// shape group come from k_obs_text when a text model is set, the wall-line share from k_obs).
 __global__ void k_obs_finalize(Batch B) {
   const int m = B.map0 + blockIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
+  const bool walls = F.wall_set && F.n_wseg > 0;   // this keyframe carries wall segments
+  const double* S = B.wsegs + (size_t)m * SMG_WALL_SEGS_MAX * 4;
   // the fields the decision reads, staged by the warp; the walk then waits on no global load
   struct Fin {
-    int valid, stage, nc, pl_ok, so_sh;
+    int valid, stage, nc, pl_ok, so_sh, w_near, w_tot, through;
     double inl, thick, nz, zmed, zhi, zlo, hspan, ps, pso;
   };
   __shared__ Fin fs[SMG_MAX_DET];
@@ -825,13 +843,27 @@ __global__ void k_obs_finalize(Batch B) {
     f.inl = O->pl_inl; f.thick = O->pl_thick; f.nz = fabs(O->pl_n[2]); f.zmed = O->pl_zmed;
     f.zhi = O->pl_zhi; f.zlo = O->pl_zlo; f.hspan = O->pl_hspan;
     f.ps = O->ps; f.pso = O->pso; f.so_sh = O->so_sh;
+    f.w_near = O->w_near; f.w_tot = O->w_tot;
+    // seen through a window (objmap.cpp:742-753): the camera -> centre line crosses a wall
+    // segment of this keyframe and the centre lies more than through_d beyond it
+    f.through = 0;
+    if (O->valid && walls) {
+      const double cx0 = F.T_mc[3], cy0 = F.T_mc[7], dx = O->pos[0] - cx0, dy = O->pos[1] - cy0, L = hypot(dx, dy);
+      for (int s2 = 0; s2 < F.n_wseg && !f.through && L > 1e-6; ++s2) {
+        const double* w = S + 4 * s2;
+        const double ex = w[2] - w[0], ey = w[3] - w[1], den = dx * ey - dy * ex;
+        if (fabs(den) < 1e-9) continue;
+        const double t = ((w[0] - cx0) * ey - (w[1] - cy0) * ex) / den, u = ((w[0] - cx0) * dy - (w[1] - cy0) * dx) / den;
+        f.through = u >= 0 && u <= 1 && t > 0 && (1 - t) * L > B.p.through_d;
+      }
+    }
     fs[k] = f;
   }
   __syncthreads();
   if (threadIdx.x != 0) return;
   MapRec* R = &B.maps[m];
   const smg_params& P = B.p;
-  long long st_obs = 0, st_floor = 0, st_ceil = 0, st_wall_tall = 0;
+  long long st_obs = 0, st_floor = 0, st_ceil = 0, st_wall_tall = 0, st_through = 0, st_so_big = 0, st_wall = 0, st_wall_name = 0;
   int n_ceil = R->n_ceil;
   double ceil_est = R->ceil_est;
   int n = 0;
@@ -841,6 +873,7 @@ __global__ void k_obs_finalize(Batch B) {
       if (O.stage == 3) ++st_floor;
       continue;
     }
+    if (O.through) { ++st_through; continue; }
     ++st_obs;
     bool drop = false;
     if (O.nc >= 8 && O.pl_ok && !(O.inl < P.plane_inl) && !(O.thick > P.plane_thick)) {
@@ -881,6 +914,14 @@ __global__ void k_obs_finalize(Batch B) {
         const bool tall = O.zhi - O.zlo >= P.tall_h || (O.zlo <= P.tall_floor && O.zhi >= cz - P.tall_ceil);
         const bool wide = O.hspan >= (O.ps >= P.tall_ps ? P.tall_w : P.tall_w_any);
         if (tall && wide && !so_keep) { ++st_wall_tall; drop = true; }
+        else if (walls && !(O.w_near < P.wall_frac * O.w_tot) && !so_keep) {
+          // a plane on a wall line (objmap.cpp:605-621): big -> wall, structure-named -> wall,
+          // else kept as a wall-like fragment; a structural-object name keeps it within its size
+          if (O.pso >= 0.5) ++st_so_big;
+          if (smax(O.hspan, O.zhi - O.zlo) >= P.wall_big) { ++st_wall; drop = true; }
+          else if (O.ps >= P.struct_p) { ++st_wall_name; drop = true; }
+          else B.obs[(size_t)m * B.max_det + k].wall_like = 1;
+        }
       }
     }
     if (!drop) B.obs_list[(size_t)m * B.max_det + n++] = k;
@@ -889,6 +930,10 @@ __global__ void k_obs_finalize(Batch B) {
   R->st.n_floor += st_floor;
   R->st.n_ceil += st_ceil;
   R->st.n_wall_tall += st_wall_tall;
+  R->st.n_through += st_through;
+  R->st.n_so_big += st_so_big;
+  R->st.n_wall += st_wall;
+  R->st.n_wall_name += st_wall_name;
   R->n_ceil = n_ceil;
   R->ceil_est = ceil_est;
   R->n_obs = n;

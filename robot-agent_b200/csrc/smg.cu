@@ -84,6 +84,11 @@ struct smg_batch {
   uint16_t* d_depth_mm = nullptr;  // staging of host millimetre depth
   uint32_t* d_mask = nullptr;      // staging of host detector bit masks: M x max_det x mask_words_max
   uint8_t* d_rgba = nullptr;       // staging of host RGBA images (allocated on first use)
+  // wall segments of host frames (allocated by the first push that carries some): a pinned
+  // ring (kRing x M x SMG_WALL_SEGS_MAX x 4, slot = the descriptor ring's) and two device
+  // staging sets, packed frame after frame
+  double* h_wall = nullptr;
+  double* d_wall = nullptr;
   // The staging above is double-buffered: push k fills set k % 2 while the chain of push k - 1
   // still reads the other set, so a push's host-to-device copies overlap the previous chain.
   // ev_set[s] marks the end of the last chain that read set s.
@@ -228,6 +233,8 @@ int smg_params_default(smg_params* p) {
   // text-model rules (objprob.hpp:84-136)
   p->name_tau = 0.5; p->name_wmax = 6.0; p->size_w = 1.0; p->whole_w = 1.0; p->geo_w = 3.0; p->flat_max_w = 2.2;
   p->wall_big = 1.0; p->struct_p = 0.5;
+  p->wall_d = 0.12; p->wall_frac = 0.6; p->through_d = 0.20; p->bridge_max = 0.0;
+  p->obj_flat_thick = 0.012; p->obj_flat_d = 0.10; p->obj_flat_frac = 0.7;
   p->so_dw_w = 2.2; p->so_dw_thick = 0.45; p->so_max_h = 2.8; p->so_pillar = 1.0; p->so_stairs = 6.0; p->so_dw_min = 0.3;
   p->so_hide_k = 1.5; p->wallhug_frac = 0.75; p->wallhug_w = 2.0; p->big_vinl = 0.5;
   p->struct_look_block = 1; p->so_min_obs = 12;
@@ -235,7 +242,7 @@ int smg_params_default(smg_params* p) {
 }
 
 // ObjectMap::applyParams key table (scenemap src/objmap.cpp:135-180).  Keys whose feature the
-// device path does not run (wall segments, the inspect pass, the export filter) only ever take
+// device path does not run (the inspect pass, the export filter) only ever take
 // the reference default here: any other value is reported as unsupported, so a parameter file
 // cannot change the reference's behaviour and leave this one unchanged without an error.
 int smg_params_apply(smg_params* p, const char* kv) {
@@ -261,7 +268,7 @@ int smg_params_apply(smg_params* p, const char* kv) {
       {"ap_obj_wall_span", &p->obj_wall_span, 0, 0}, {"ap_obj_wall_top", &p->obj_wall_top, 0, 0}, {"ap_reenc_max", 0, &p->reenc_max, 0},
       {"ap_reenc_gain", &p->reenc_gain, 0, 0}, {"ap_link_cos", &p->link_cos, 0, 0}, {"ap_whole_w", &p->whole_w, 0, 0},
       {"ap_export_named", 0, 0, 1}, {"ap_guard_obj", &p->guard_obj, 0, 0}, {"ap_guard_obs", &p->guard_obs, 0, 0},
-      {"ap_geo_w", &p->geo_w, 0, 0}, {"ap_name_veto", &p->name_veto, 0, 0}, {"ap_through_d", 0, 0, 0.20}, {"ap_bridge_max", 0, 0, 0.0},
+      {"ap_geo_w", &p->geo_w, 0, 0}, {"ap_name_veto", &p->name_veto, 0, 0}, {"ap_through_d", &p->through_d, 0, 0}, {"ap_bridge_max", &p->bridge_max, 0, 0},
       {"ap_frame_group", 0, &p->frame_group, 0}, {"ap_struct_obj_min_views", 0, &p->struct_obj_min_views, 0},
       {"ap_plane_inl", &p->plane_inl, 0, 0}, {"ap_obj_plane_inl", &p->obj_plane_inl, 0, 0}, {"ap_ransac_tau0", &p->ransac_tau0, 0, 0},
       {"ap_ransac_tau_k", &p->ransac_tau_k, 0, 0}, {"ap_obj_tau", &p->obj_tau, 0, 0}, {"ap_ransac_iters", 0, &p->ransac_iters, 0},
@@ -322,6 +329,7 @@ int smg_destroy(smg_batch* b) {
   for (auto e : b->ev_pool) cudaEventDestroy(e);
   for (void* p : b->allocs) cudaFree(p);
   if (b->h_ring) cudaFreeHost(b->h_ring);
+  if (b->h_wall) cudaFreeHost(b->h_wall);
   for (auto e : b->ring_ev) if (e) cudaEventDestroy(e);
   for (int g = 0; g < smg_batch::kGroupsMax; ++g) {
     for (cudaEvent_t e : {b->ev_fork[g], b->ev_join[g], b->ev_copied[g], b->ev_gdone[g], b->ev_dma[g]}) if (e) cudaEventDestroy(e);
@@ -465,6 +473,7 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
   DA(B.vkey, (size_t)M * B.view_slots);
   DA(B.vfirst, (size_t)M * B.view_slots * SMG_VIEW_BANDS);
   DA(B.need_tab, NEED_N * NEED_N);
+  DA(B.wsegs, (size_t)M * SMG_WALL_SEGS_MAX * 4);
   const size_t G = (size_t)M * grid_w * grid_h;
   DA(B.gL, G);
   DA(B.gc8, G);
@@ -628,8 +637,14 @@ __global__ void k_begin(Batch B) {
     AssocRec& a = B.assoc[(size_t)m * B.max_det + k];
     a.obj_id = 0; a.n_valid = 0; a.area_px = 0; a.depth_med = 0;
   }
+  if (F.wall_set) {   // ObjectMap::wsegs_ = this keyframe's wall segments (objmap.cpp:534)
+    const int nw = min(F.n_wseg, SMG_WALL_SEGS_MAX);
+    double* dst = B.wsegs + (size_t)m * SMG_WALL_SEGS_MAX * 4;
+    for (int i = threadIdx.x; i < 4 * nw; i += blockDim.x) dst[i] = F.wsegs[i];
+  }
   if (threadIdx.x == 0) {
     MapRec* R = &B.maps[m];
+    if (F.wall_set) R->n_wseg = min(F.n_wseg, SMG_WALL_SEGS_MAX);
     R->n_events = 0;
     R->n_evn = 0;
     R->n_obs = 0;
@@ -789,12 +804,22 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     if (f.mask_bits && (f.mask_w <= 0 || f.mask_h <= 0 || f.mask_w > b->max_w || f.mask_h > b->max_h || !(f.mask_sx > 0) ||
                         !(f.mask_sy > 0) || f.img_w < 0 || f.img_h < 0))
       return fail(SMG_ERR_ARGS, "smg_push_frames: bad detection mask grid (mask_w x mask_h <= max_w x max_h, scales > 0)");
+    if (f.wall_segs && (f.n_wall_segs < 0 || f.n_wall_segs > SMG_WALL_SEGS_MAX))
+      return fail(SMG_ERR_ARGS, "smg_push_frames: n_wall_segs must be in [0, SMG_WALL_SEGS_MAX]");
   }
   {
-    bool any_rgba = false;
-    for (int i = 0; i < n; ++i) any_rgba = any_rgba || frames[i].rgba != nullptr;
+    bool any_rgba = false, any_wall = false;
+    for (int i = 0; i < n; ++i) {
+      any_rgba = any_rgba || frames[i].rgba != nullptr;
+      any_wall = any_wall || (frames[i].wall_segs != nullptr && frames[i].n_wall_segs > 0);
+    }
     if (any_rgba)
       if (int r = views_alloc(b, where == SMG_MEM_HOST)) return r;
+    if (any_wall && where == SMG_MEM_HOST && !b->h_wall) {
+      const size_t per = (size_t)B.M * SMG_WALL_SEGS_MAX * 4;
+      if (int r = dalloc(b, &b->d_wall, 2 * per)) return r;
+      CK(cudaMallocHost(&b->h_wall, sizeof(double) * per * smg_batch::kRing));
+    }
   }
   // pinned descriptor ring: wait until the copy that last read this slot has run
   b->dbg_last = 0;
@@ -812,6 +837,10 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   uint16_t* sd_depth_mm = b->d_depth_mm + (size_t)ss * B.M * WH;
   uint32_t* sd_mask = b->d_mask + (size_t)ss * B.M * B.max_det * b->mask_words_max;
   uint8_t* sd_rgba = b->d_rgba ? b->d_rgba + (size_t)ss * B.M * WH * 4 : nullptr;
+  const size_t wall_per = (size_t)B.M * SMG_WALL_SEGS_MAX * 4;
+  double* sd_wall = b->d_wall ? b->d_wall + (size_t)ss * wall_per : nullptr;
+  double* hs_wall = b->h_wall ? b->h_wall + (size_t)slot * wall_per : nullptr;
+  size_t wall_off = 0;   // host wall segments are staged packed, frame after frame
   // Host frames in pinned (device-accessible) memory are read in place: k_gather fetches only
   // the pixels the chain reads.  Any other host memory goes through whole-frame copies.
   bool gather = where == SMG_MEM_HOST && b->host_gather && b->max_w <= GATHER_WMAX;
@@ -887,6 +916,20 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
       d.rgba = where == SMG_MEM_DEVICE ? f.rgba : sd_rgba + (size_t)m * WH * 4;
       d.views_on = d.img_w == f.w && d.img_h == f.h;
     }
+    // ObjFrame::wall_segs: a set (even an empty one) replaces the stored one; none keeps it
+    if (f.wall_segs) {
+      d.wall_set = 1;
+      d.n_wseg = f.n_wall_segs;
+      if (f.n_wall_segs > 0) {
+        if (where == SMG_MEM_DEVICE) {
+          d.wsegs = f.wall_segs;
+        } else {
+          memcpy(hs_wall + wall_off, f.wall_segs, sizeof(double) * 4 * f.n_wall_segs);
+          d.wsegs = sd_wall + wall_off;
+          wall_off += 4 * (size_t)f.n_wall_segs;
+        }
+      }
+    }
     if (where == SMG_MEM_DEVICE) {
       d.depth = f.depth ? f.depth : sd_depth + (size_t)m * WH;   // millimetres: converted into staging
       d.depth_mm = f.depth ? nullptr : f.depth_mm;
@@ -957,6 +1000,10 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
   // chain that read that set has finished (the previous chain may still be running)
   B.frames = b->frames_base + (size_t)ss * B.M;
   CK(cudaStreamWaitEvent(b->s_copy, b->ev_set[ss], 0));
+  if (wall_off) {   // packed wall segments of host frames (the ring slot's event covers the source)
+    CK(cudaMemcpyAsync(sd_wall, hs_wall, sizeof(double) * wall_off, cudaMemcpyHostToDevice, b->s_copy));
+    b->h2d_host += (long long)(sizeof(double) * wall_off);
+  }
   CK(cudaMemcpyAsync(B.frames, b->h_frames, sizeof(FrameDev) * B.M, cudaMemcpyHostToDevice, b->s_copy));
   if (where == SMG_MEM_HOST) b->h2d_host += (long long)(sizeof(FrameDev) * B.M);
   CK(cudaEventRecord(b->ring_ev[slot], b->s_copy));
@@ -1215,6 +1262,10 @@ int smg_get_objects(smg_batch* b, int m, smg_object* out, int cap) {
     r.held_by = o.held_by;
     r.parent = o.parent;
     for (int k = 0; k < 3; ++k) r.parent_rel[k] = o.parent_rel[k];
+    r.wall_like = o.wall_like;
+    r.hide = o.hide;
+    r.n_wall_obs = o.n_wall_obs;
+    r.fw = o.fw;
   }
   return R.n_obj;
 }

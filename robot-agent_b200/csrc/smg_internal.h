@@ -115,6 +115,11 @@ typedef struct {
   // uses: rgba present and the detector image the size of the depth image (capi.cpp:916)
   const uint8_t* rgba;
   int32_t views_on;
+  // ObjFrame::wall_segs: wall_set = the keyframe carries a set (non-null pointer), which replaces
+  // the map's stored one (Batch::wsegs, MapRec::n_wseg) before the chain; n_wseg segments at
+  // wsegs (staging or the caller's device memory)
+  const double* wsegs;
+  int32_t n_wseg, wall_set;
 } FrameDev;
 
 // Observation (one detection after back-projection; scenemap objmap.cpp:52-74 `Obs`)
@@ -135,6 +140,9 @@ typedef struct {
   // the most likely structural-object shape group, and the wall-like flags of the structural rules
   double ps, pso, top_p;
   int32_t top_lab, so_sh, wall_like, struct_look;
+  // wall-line test of apObsStructural (objmap.cpp:606-611): of w_tot sampled candidates, w_near
+  // lie within wall_d of a wall segment; through = the centre lies beyond a wall (:742-753)
+  int32_t w_near, w_tot, through;
 } ObsRec;
 
 typedef struct __align__(16) {   // 16-byte aligned: staged in shared memory in 16-byte words
@@ -193,6 +201,7 @@ typedef struct __align__(16) {   // 16-byte aligned: staged in shared memory in 
   double gp_so;          // posterior mass of structure and structural-object labels (the guards' group)
   double maj, minr, hgt; // apStructObject shape of the cloud sample (5-95 % spans), with geo
   float vinl;            // inlier share of an upright dominant plane (ApState::vinl)
+  float fw;              // share of the cloud sample within wall_d of a wall segment (ApState::fw)
 } ObjRec;
 
 typedef struct {
@@ -282,6 +291,7 @@ typedef struct {
   uint32_t view_ver;
   int32_t n_vnew;
   int32_t vnew[SMG_MAX_DET];   // candidate (detection) of each replaced view, install order
+  int32_t n_wseg;        // the stored wall segments (ObjectMap::wsegs_), at Batch::wsegs
 } MapRec;
 
 // Whole-object re-encode candidate of a keyframe (ReencReq, scenemap objmap.hpp:142-148, plus
@@ -400,6 +410,7 @@ typedef struct {
   float* lwhole;         // [M*O*C] ApState::L_whole
   float* post;           // [M*O*C] ApState::post
   float* llz;            // [M*max_det*C] apLabelLogLik of each detection's embedding
+  double* wsegs;         // [M*SMG_WALL_SEGS_MAX*4] the stored wall segments of each map
   // best views (allocated on the first push with an RGB image)
   ViewRec* vrec;         // [M*max_det]
   uint8_t* vrgb;         // [M*max_det*VIEW_PIX*3]

@@ -30,7 +30,8 @@ class SmgFrame(C.Structure):
                 ("score", C.c_void_p), ("emb", C.c_void_p), ("emb_dtype", C.c_int32), ("grip", C.c_float * 2),
                 ("mask_bits", C.c_void_p), ("mask_w", C.c_int32), ("mask_h", C.c_int32), ("mask_sx", C.c_float),
                 ("mask_sy", C.c_float), ("mask_ox", C.c_float), ("mask_oy", C.c_float), ("img_w", C.c_int32),
-                ("img_h", C.c_int32), ("depth_mm", C.c_void_p), ("rgba", C.c_void_p)]
+                ("img_h", C.c_int32), ("depth_mm", C.c_void_p), ("rgba", C.c_void_p), ("wall_segs", C.c_void_p),
+                ("n_wall_segs", C.c_int32)]
 
 
 class SmgView(C.Structure):
@@ -57,7 +58,8 @@ class SmgObject(C.Structure):
                 ("k_frag", C.c_double), ("n_views", C.c_int32), ("n_ap_obs", C.c_int32), ("need_whole", C.c_int32),
                 ("P", C.c_double * 3), ("n_cams", C.c_int32), ("geo", C.c_int32), ("k_whole", C.c_double),
                 ("n_whole", C.c_int32), ("held_by", C.c_int32),
-                ("parent", C.c_uint32), ("parent_rel", C.c_double * 3)]
+                ("parent", C.c_uint32), ("parent_rel", C.c_double * 3), ("wall_like", C.c_int32), ("hide", C.c_int32),
+                ("n_wall_obs", C.c_int32), ("fw", C.c_float)]
 
 
 _lib = None
@@ -212,6 +214,11 @@ class Batch:
         if fr.get("mask_w"):
             f.mask_w, f.mask_h = fr["mask_w"], fr["mask_h"]
             f.mask_sx, f.mask_sy, f.mask_ox, f.mask_oy = fr["mask_affine"]
+        if fr.get("wall_segs") is not None:   # n x (ax, ay, bx, by) map metres, host memory
+            ws = np.ascontiguousarray(fr["wall_segs"], np.float64).reshape(-1, 4)
+            buf = ws if len(ws) else np.zeros(4)   # an empty set is still a set: a non-null pointer
+            keep.append(buf)
+            f.wall_segs, f.n_wall_segs = buf.ctypes.data, len(ws)
         if ptrs is not None:
             f.depth, f.label, f.emb = ptrs["depth"], ptrs["label"], ptrs["emb"]
             f.mask_bits = ptrs.get("mask_bits")

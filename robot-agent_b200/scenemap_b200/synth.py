@@ -121,7 +121,9 @@ class BoxRoom:
                     form the reference's detector produces; both sides then read those;
       depth_mm      depth also as uint16 millimetres (rounded), which both sides then read;
       rgb           an RGBA colour image registered with the depth (rgba_image), which both sides
-                    use for best views and cloud-point colours.
+                    use for best views and cloud-point colours;
+      walls         callable f -> (n, 4) wall segments (ax, ay, bx, by, map metres) the keyframe
+                    carries, or None for none (ObjFrame::wall_segs).
     """
 
     def __init__(self, seed: int, n_boxes: int = 20, room=(6.0, 5.0, 2.6), noise_k: float = 0.005,
@@ -130,7 +132,7 @@ class BoxRoom:
                  n_frames: int = 300, D: int = 1152, bf16: bool = False, emb_sigma: float = 0.05,
                  min_px: int = 64, max_det: int = 24, cam_height: float = 0.9, pitch_deg: float = 20.0,
                  shell_labels: bool = False, box_moves=(), box_extra=(), hands=None, mask_grid: int = 0,
-                 depth_mm: bool = False, rgb: bool = False):
+                 depth_mm: bool = False, rgb: bool = False, walls=None):
         L = lib()
         self.seed = seed
         self.scene = SyScene()
@@ -144,7 +146,7 @@ class BoxRoom:
                 self.scene.box[b].hi[k] = hi[k]
             self.scene.n_boxes = b + 1
         self.scene.shell_labels = 1 if shell_labels else 0
-        self.mask_grid, self.depth_mm, self.rgb = mask_grid, depth_mm, rgb
+        self.mask_grid, self.depth_mm, self.rgb, self.walls = mask_grid, depth_mm, rgb, walls
         self.box_moves = sorted(box_moves, key=lambda e: e[0])
         self.hands = hands
         self.cam = SyCamera(w, h, fx, fy, cx, cy)
@@ -208,6 +210,10 @@ class BoxRoom:
             extra["rgba"] = rgba_image(label, depth)
         if self.depth_mm:
             extra["depth_mm"] = np.clip(np.rint(depth * 1000.0), 0, 65535).astype(np.uint16)
+        if self.walls is not None:
+            ws = self.walls(f)
+            if ws is not None:
+                extra["wall_segs"] = np.asarray(ws, np.float64).reshape(-1, 4)
         return dict(stamp=f * self.dt, w=self.w, h=self.h, depth=depth, label=label, fx=self.fx, fy=self.fy,
                     cx=self.cx, cy=self.cy, T_mc=T, T_bc=self.T_bc, base=self.poses[f].copy(),
                     eef=np.asarray(eef, np.float64), grip=np.asarray(grip, np.float32), eef_base=self.eef_base,

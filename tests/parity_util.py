@@ -5,7 +5,7 @@ import numpy as np
 
 EXACT_FIELDS = ["id", "cls", "n_obs", "state", "confirmed", "moved", "misses", "n_vis_miss", "appeared", "cloud_n",
                 "cloud_version", "ap_ver", "n_views", "n_ap_obs", "need_whole", "n_cams", "geo", "held_by", "parent",
-                "n_whole"]
+                "n_whole", "wall_like", "hide", "n_wall_obs", "fw"]
 FLOAT_FIELDS = ["pos", "ext", "first_pos", "lo", "hi", "first_seen", "last_seen", "max_det_z", "last_kf", "k_frag",
                 "P", "cloud_org", "parent_rel", "k_whole"]
 

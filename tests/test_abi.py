@@ -57,8 +57,8 @@ YOLO26N_OBJ_PARAMS = ("ap_w0=-4.235,ap_w1=5.063,ap_w2=-5.289,ap_w3=-0.3241,ap_w4
 
 
 def test_params_unsupported_keys_are_not_silent():
-    """Keys of features the device does not run (wall segments, the inspect pass, the export
-    filter) are accepted at the reference default only; the text-model keys are real fields."""
+    """Keys of features the device does not run (the inspect pass, the export filter) are
+    accepted at the reference default only; the text-model and wall-line keys are real fields."""
     from scenemap_b200 import smg
     L = smg.lib()
     p = smg.Params()
@@ -66,10 +66,11 @@ def test_params_unsupported_keys_are_not_silent():
     # the reference defaults of inert keys are accepted (a full parameter dump stays loadable)
     assert L.smg_params_apply(p.buf, b"ap_through_d=0.2,ap_wall_big=1,ap_export_named=1,inspect=0,ap_so_dw_w=2.2") == 0
     before = p.buf.raw
-    rc = L.smg_params_apply(p.buf, b"ap_same_p=0.55,ap_through_d=0.5,ap_bridge_max=3,ap_wallhug_w=3")
+    rc = L.smg_params_apply(p.buf, b"ap_same_p=0.55,ap_through_d=0.5,ap_export_named=0,ap_bridge_max=3,inspect=1")
     assert rc == smg.SMG_ERR_UNSUPPORTED
     msg = L.smg_last_error().decode()
-    assert "ap_through_d" in msg and "ap_bridge_max" in msg and "ap_same_p" not in msg and "ap_wallhug_w" not in msg
+    assert "ap_export_named" in msg and "inspect" in msg
+    assert "ap_same_p" not in msg and "ap_through_d" not in msg and "ap_bridge_max" not in msg
     assert p.buf.raw != before                      # the supported key was still applied
     with pytest.raises(smg.SmgError):
         smg.Params("inspect=1")

@@ -54,6 +54,13 @@ def test_parity_structure_variant():
     _run_variant(variants.structure())
 
 
+def test_parity_wall_segments():
+    """Keyframes with wall segments: wall-line drops and wall-like fragments, the see-through
+    drop, the wall share and flat-plane test of apStructObject, stored vs per-keyframe sets."""
+    _need()
+    _run_variant(variants.walls(), deep_every=8)
+
+
 def test_parity_moving_boxes():
     """Boxes that slide, jump, vanish and appear: absence, gone, relink, seen again."""
     _need()

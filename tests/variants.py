@@ -49,6 +49,29 @@ def depth_millimetres(n_frames: int = 30) -> dict:
     return dict(gen=dict(seed_base=61, depth_mm=True), kv="", n_frames=n_frames, stats=(), events=(), bf16=True)
 
 
+def walls(n_frames: int = 80) -> dict:
+    """The structure variant with wall segments on the keyframes (ObjFrame::wall_segs): the room's
+    four walls, a collinear gap (a window) in one, and an interior segment the camera sees boxes
+    behind.  Reaches the wall-line rules of apObsStructural (wall planes dropped, wall-like
+    fragments kept), the see-through drop, and apStructObject's wall share and flat-plane test.
+    Every fourth keyframe carries no set (the stored one stays), one carries an empty set."""
+    rx, ry = 5.0, 4.5
+    segs = [(0.0, 0.0, rx, 0.0), (rx, 0.0, rx, 1.6), (rx, 2.4, rx, ry), (rx, ry, 0.0, ry), (0.0, ry, 0.0, 0.0),
+            (2.5, 0.4, 2.5, 2.2)]
+
+    def ws(f: int):
+        if f % 4 == 3:
+            return None
+        if f == 10:
+            return []
+        return segs
+
+    v = structure(n_frames)
+    v["gen"] = dict(v["gen"], seed_base=14, walls=ws)
+    v["stats"] = ("n_wall", "n_through")
+    return v
+
+
 def make_gen(v: dict, D: int = 1152, bf16: bool = False):
     from scenemap_b200 import synth
     kw = dict(v["gen"])
