@@ -32,8 +32,10 @@ enum {
 };
 
 enum { SMG_MEM_DEVICE = 0, SMG_MEM_HOST = 1 };
-/* wall segments a keyframe may carry (smg_frame::wall_segs) */
+/* wall segments a keyframe may carry (smg_frame::wall_segs) or an extraction may find */
 #define SMG_WALL_SEGS_MAX 1024
+/* the wall state vector (sm_snap_wall_state, scenemap include/scenemap.h:96-99) */
+#define SMG_WALL_STATE_LEN 56
 enum { SMG_EMB_F32 = 0, SMG_EMB_BF16 = 1 };
 
 /* Parameters.  Field names and defaults mirror the reference structs:
@@ -367,10 +369,30 @@ int smg_set_object_embeddings(smg_batch* b, const int32_t* maps, const uint32_t*
  * returns n_whole. */
 int smg_get_object_whole(smg_batch* b, int m, int i, float* r_whole, double* k_whole);
 
+/* Wall extraction from each map's own occupancy grid before every object update, as the
+ * reference's image push does (sm_push_image: refreshWalls, scenemap src/capi.cpp:646-698, and the
+ * bridged list of :866-890 handed to ObjectMap::update as ObjFrame::wall_segs; walls.cpp).  The
+ * floor footprints of confirmed, named objects are ignored; the dominant wall direction is
+ * re-measured at most every 2 s of frame stamps; tilted maps are extracted along it (at most
+ * every 0.5 s); the keyframe then carries the segments plus the bridges of gaps up to
+ * ap_bridge_max between collinear ones.  on = 1 enables (and resets the extraction state), 0
+ * disables; with it on, frames must not carry their own wall_segs.  The extraction runs on the
+ * batch's grid window (the reference runs it on its grown grid). */
+int smg_set_walls(smg_batch* b, int on);
+/* sm_snap_wall_segments (scenemap include/scenemap.h:100, capi.cpp:1247-1257): the segments of
+ * map m's last extraction (n x ax ay bx by, map metres, no bridges); returns their count (may
+ * exceed cap), or -1 when walls are off or not yet extracted. */
+int smg_get_wall_segments(smg_batch* b, int m, double* out, int cap);
+/* sm_snap_wall_state (scenemap include/scenemap.h:96-99, capi.cpp:1239-1245; walls.hpp: the first
+ * occupied cell along 16 rays from the pose, then the 8 nearest segments in the robot frame) of
+ * map m at pose (x, y, yaw): SMG_WALL_STATE_LEN floats.  Returns -1 when walls are off or not yet
+ * extracted. */
+int smg_wall_state(smg_batch* b, int m, const double pose[3], float* out);
+
 /* Per-kernel device time with CUDA events on the launch stream (instrumentation, off by
  * default).  smg_timing_read fills ms[k] (total milliseconds) and n[k] (launches) for the
  * SMG_NUM_KERNELS kernels of the keyframe chain and resets the counters; names[k] is static. */
-#define SMG_NUM_KERNELS 17
+#define SMG_NUM_KERNELS 18
 int smg_timing_enable(smg_batch* b, int on);
 int smg_timing_read(smg_batch* b, double* ms, int64_t* n, const char** names);
 /* First failed self-check of a -DSMG_CHECKS build: (site, index, bound); all zero when none

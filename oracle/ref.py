@@ -125,6 +125,11 @@ def ref_lib():
         L.ref_voxel_key.argtypes = [C.c_float, C.c_float, C.c_float, C.c_float]
         L.ref_contact.restype = C.c_double
         L.ref_contact.argtypes = [P(C.c_float), C.c_int, P(C.c_float), C.c_int, C.c_double]
+        L.ref_set_walls.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.ref_wall_segments.argtypes = [C.c_void_p, P(C.c_double), C.c_int]
+        L.ref_wall_state.argtypes = [C.c_void_p, P(C.c_double), P(C.c_float)]
+        L.ref_wall_segments_grid.argtypes = [P(C.c_int8), C.c_int, C.c_int, C.c_double, C.c_double, C.c_double, P(C.c_double),
+                                             C.c_int, C.c_int, C.c_double, P(C.c_double), P(C.c_double), C.c_int]
         _ref = L
     return _ref
 
@@ -262,6 +267,30 @@ class RefMap:
         seq = np.zeros(max(n, 1), np.uint32)
         L.ref_object_cloud(self._h, i, _p(xyz, C.c_float), _p(seq, C.c_uint32), n)
         return xyz[:n], seq[:n]
+
+    def set_walls(self, grid) -> None:
+        """Wall extraction before every object update (sm_push_image's refreshWalls and bridges),
+        on the reference grid laid over the window grid = (w, h, x0, y0) cells."""
+        w, h, x0, y0 = grid
+        assert ref_lib().ref_set_walls(self._h, 1, int(x0), int(y0), int(w), int(h)) == 0
+
+    def wall_segments(self):
+        """sm_snap_wall_segments: (n, 4) extracted segments, or None before the first extraction."""
+        L = ref_lib()
+        n = L.ref_wall_segments(self._h, None, 0)
+        if n < 0:
+            return None
+        out = np.zeros((max(n, 1), 4), np.float64)
+        L.ref_wall_segments(self._h, _p(out, C.c_double), n)
+        return out[:n]
+
+    def wall_state(self, pose) -> np.ndarray | None:
+        """sm_snap_wall_state at pose (x, y, yaw): the wall state vector (56 floats)."""
+        p = np.ascontiguousarray(pose, np.float64)
+        out = np.zeros(56, np.float32)
+        if ref_lib().ref_wall_state(self._h, _p(p, C.c_double), _p(out, C.c_float)) != 0:
+            return None
+        return out
 
     def set_text_model(self, t: dict) -> None:
         """ObjectMap::setTextModel + setClassKinds from a synth.text_model dict."""
@@ -575,3 +604,20 @@ def name(text, row_label, n_labels, scale, bias, log_prior, ls_mu, ls_sd, parent
                        _p(f6, C.c_double))
     del keep
     return post, int(f6[0]), float(f6[1]), int(f6[2]), float(f6[3]), float(f6[4]), int(f6[5]), bool(named)
+
+
+def wall_segments_grid(cells: np.ndarray, res: float, ox: float, oy: float, rects=(), mode: int = 0, th: float = 0.0):
+    """walls.hpp on a caller's export8 grid (h, w): mode 0 wallSegments -> (n, 4); 1 wallAngle ->
+    float; 2 wallSegmentsAtAngle(th) -> (n, 4).  rects: ignore areas (x0, y0, x1, y1)."""
+    L = ref_lib()
+    c = np.ascontiguousarray(cells, np.int8)
+    h, w = c.shape
+    rv = np.ascontiguousarray(np.asarray(rects, np.float64).reshape(-1, 4))
+    rp = _p(rv, C.c_double) if len(rv) else None
+    ang = C.c_double(0.0)
+    n = L.ref_wall_segments_grid(_p(c, C.c_int8), w, h, res, ox, oy, rp, len(rv), mode, th, C.byref(ang), None, 0)
+    if mode == 1:
+        return ang.value
+    out = np.zeros((max(n, 1), 4), np.float64)
+    L.ref_wall_segments_grid(_p(c, C.c_int8), w, h, res, ox, oy, rp, len(rv), mode, th, None, _p(out, C.c_double), n)
+    return out[:n]

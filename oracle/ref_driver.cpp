@@ -28,6 +28,7 @@
 #include "scenemap/objprob.hpp"
 #include "scenemap/scan.hpp"
 #include "scenemap/cloud.hpp"
+#include "scenemap/walls.hpp"
 
 using namespace scenemap;
 
@@ -117,8 +118,108 @@ struct RefMap {
   std::map<uint32_t, Slot> views;
   uint32_t view_ver = 0;
   size_t ev_seen = 0;
+  // wall extraction as sm_push_image runs it before the object update (refreshWalls and the
+  // window bridges, capi.cpp:646-698, 866-890: sm_ctx::wallsp, walls_rects, walls_grid_ver,
+  // wall_th, wall_th_t, walls_full_t), on the occupancy grid laid over a fixed window of cells
+  // [wx0, wx0 + ww) x [wy0, wy0 + wh) (the device library's grid window)
+  bool walls_on = false;
+  int wx0 = 0, wy0 = 0, ww = 0, wh = 0;
+  std::vector<int8_t> wgrid;
+  std::shared_ptr<const std::vector<WallSeg>> wallsp;
+  std::vector<WallRect> walls_rects;
+  uint64_t walls_grid_ver = ~0ull;
+  double wall_th = 0, wall_th_t = -1e300, walls_full_t = -1e300;
+  std::vector<double> wsegs;
   explicit RefMap(const ObjParams& p) : om(p) {}
 };
+
+// export8 of the reference grid laid over the window (cells outside the grid: -1 unknown);
+// false when a seen cell of the grid lies outside the window
+static bool window_grid(RefMap* m) {
+  const OccGrid& G = m->mapper->grid();
+  m->wgrid.assign(size_t(m->ww) * m->wh, int8_t(-1));
+  if (G.width() <= 0 || G.height() <= 0) return true;
+  const std::vector<int8_t> c8 = G.export8();
+  bool ok = true;
+  for (int y = 0; y < G.height(); ++y)
+    for (int x = 0; x < G.width(); ++x) {
+      const int8_t v = c8[size_t(y) * G.width() + x];
+      const int gx = G.x0() + x - m->wx0, gy = G.y0() + y - m->wy0;
+      if (gx < 0 || gy < 0 || gx >= m->ww || gy >= m->wh) { ok = ok && v < 0; continue; }
+      m->wgrid[size_t(gy) * m->ww + gx] = v;
+    }
+  return ok;
+}
+
+static WallGrid window_view(const RefMap* m) {
+  const double res = double(m->mapper->grid().res());
+  return WallGrid{m->wgrid.data(), m->ww, m->wh, res, m->wx0 * res, m->wy0 * res};
+}
+
+// refreshWalls (capi.cpp:646-698) and the bridged segment list of the keyframe (:866-890)
+static int refresh_walls(RefMap* m, double now) {
+  if (!window_grid(m)) return -2;
+  const OccGrid& gr = m->mapper->grid();
+  const bool grid_changed = m->walls_grid_ver != gr.cellsVersion();
+  std::vector<WallRect> rects;
+  for (const MapObject& o : m->om.objects()) {
+    if (!m->om.exportable(o) || o.held_by >= 0 || o.state == SM_GONE) continue;
+    if (o.lo[2] > 0.4) continue;
+    if (o.ap && o.ap->wall_like) continue;
+    if (m->om.kindOf(o.cls) == kKindStructObj) continue;
+    const double dx = o.hi[0] - o.lo[0], dy = o.hi[1] - o.lo[1];
+    if (dx > 5.0 || dy > 5.0) continue;
+    rects.push_back({o.lo[0] - 0.1, o.lo[1] - 0.1, o.hi[0] + 0.1, o.hi[1] + 0.1});
+  }
+  const bool rects_changed = !(rects == m->walls_rects);
+  const WallGrid wg = window_view(m);
+  bool th_changed = false;
+  if ((grid_changed || rects_changed) && now - m->wall_th_t >= 2.0) {
+    const double th = wallAngle(wg, &rects);
+    m->wall_th_t = now;
+    if (std::abs(th - m->wall_th) > M_PI / 180.0) {
+      const bool was_axis = std::abs(m->wall_th) <= kAlignTol, is_axis = std::abs(th) <= kAlignTol;
+      if (was_axis != is_axis) m->wallsp.reset();
+      m->wall_th = th;
+      th_changed = true;
+    }
+  }
+  bool redo;
+  if (std::abs(m->wall_th) > kAlignTol)
+    redo = !(m->wallsp && !th_changed && !rects_changed && (!grid_changed || now - m->walls_full_t < 0.5));
+  else
+    redo = !(m->wallsp && !grid_changed && !rects_changed);
+  if (redo) {
+    // the incremental extractor of the axis-aligned case returns what wallSegments does
+    m->wallsp = std::make_shared<const std::vector<WallSeg>>(
+        std::abs(m->wall_th) > kAlignTol ? wallSegmentsAtAngle(wg, m->wall_th, kMinLen, kMaxThick, 0.6, &rects)
+                                         : wallSegments(wg, kMinLen, kMaxThick, 0.6, &rects));
+    m->walls_rects = std::move(rects);
+    m->walls_grid_ver = gr.cellsVersion();
+    if (std::abs(m->wall_th) > kAlignTol) m->walls_full_t = now;
+  }
+  m->wsegs.clear();
+  if (m->wallsp) {
+    const auto& W = *m->wallsp;
+    for (const WallSeg& w : W) m->wsegs.insert(m->wsegs.end(), {w.ax, w.ay, w.bx, w.by});
+    const double bmax = m->om.params().ap.bridge_max;
+    for (size_t i = 0; i < W.size(); ++i)
+      for (size_t j = i + 1; j < W.size(); ++j) {
+        const double ux = W[i].bx - W[i].ax, uy = W[i].by - W[i].ay, li = std::hypot(ux, uy);
+        const double vx = W[j].bx - W[j].ax, vy = W[j].by - W[j].ay, lj = std::hypot(vx, vy);
+        if (li < 1e-6 || lj < 1e-6 || std::fabs(ux * vy - uy * vx) / (li * lj) > 0.03) continue;
+        const double nx = -uy / li, ny = ux / li;
+        if (std::fabs((W[j].ax - W[i].ax) * nx + (W[j].ay - W[i].ay) * ny) > 0.1) continue;
+        auto at = [&](double x, double y) { return ((x - W[i].ax) * ux + (y - W[i].ay) * uy) / li; };
+        double a0 = 0, a1 = li, b0 = at(W[j].ax, W[j].ay), b1 = at(W[j].bx, W[j].by);
+        if (b0 > b1) std::swap(b0, b1);
+        const double lo = a1 <= b0 ? a1 : b1, hi = a1 <= b0 ? b0 : a0;
+        if (hi - lo <= 0 || hi - lo > bmax) continue;
+        m->wsegs.insert(m->wsegs.end(), {W[i].ax + ux / li * lo, W[i].ay + uy / li * lo, W[i].ax + ux / li * hi, W[i].ay + uy / li * hi});
+      }
+  }
+  return 0;
+}
 
 void* ref_create(const char* obj_kv, double voxel, int cloud_cap, int grid_on, const float* grid /* res, l_hit, l_miss, l_min, l_max */,
                  int attach_on) {
@@ -144,6 +245,52 @@ void* ref_create(const char* obj_kv, double voxel, int cloud_cap, int grid_on, c
 
 void ref_destroy(void* h) { delete static_cast<RefMap*>(h); }
 
+// Wall extraction before every object update (sm_push_image's refreshWalls), on the grid window
+// x0, y0 (cells), w x h.
+int ref_set_walls(void* h, int on, int x0, int y0, int w, int hh) {
+  RefMap* m = static_cast<RefMap*>(h);
+  if (!m || !m->mapper || w <= 0 || hh <= 0) return -1;
+  m->walls_on = on != 0;
+  m->wx0 = x0; m->wy0 = y0; m->ww = w; m->wh = hh;
+  return 0;
+}
+
+// sm_snap_wall_segments (capi.cpp:1247-1257): the extracted segments (no bridges), count or -1
+int ref_wall_segments(void* h, double* out, int cap) {
+  RefMap* m = static_cast<RefMap*>(h);
+  if (!m || !m->wallsp) return -1;
+  const auto& W = *m->wallsp;
+  for (int i = 0; out && i < cap && i < int(W.size()); ++i) {
+    out[4 * i] = W[i].ax; out[4 * i + 1] = W[i].ay; out[4 * i + 2] = W[i].bx; out[4 * i + 3] = W[i].by;
+  }
+  return int(W.size());
+}
+
+// sm_snap_wall_state (capi.cpp:1239-1245) on the window grid: kStateLen floats
+int ref_wall_state(void* h, const double pose[3], float* out) {
+  RefMap* m = static_cast<RefMap*>(h);
+  if (!m || !m->wallsp || !window_grid(m)) return -1;
+  wallStateVector(window_view(m), *m->wallsp, pose, out);
+  return 0;
+}
+
+// the wall-extraction functions on a caller's grid (walls.hpp): wallSegments / wallAngle /
+// wallSegmentsAtAngle, for tests of the extraction alone
+int ref_wall_segments_grid(const int8_t* cells, int w, int hh, double res, double ox, double oy, const double* rects, int n_rects,
+                           int mode, double th, double* angle_out, double* out, int cap) {
+  const WallGrid g{cells, w, hh, res, ox, oy};
+  std::vector<WallRect> rv;
+  for (int i = 0; i < n_rects; ++i) rv.push_back({rects[4 * i], rects[4 * i + 1], rects[4 * i + 2], rects[4 * i + 3]});
+  std::vector<WallSeg> W;
+  if (mode == 0) W = wallSegments(g, kMinLen, kMaxThick, 0.6, &rv);
+  else if (mode == 1) { const double a = wallAngle(g, &rv); if (angle_out) *angle_out = a; return 0; }
+  else W = wallSegmentsAtAngle(g, th, kMinLen, kMaxThick, 0.6, &rv);
+  for (int i = 0; out && i < cap && i < int(W.size()); ++i) {
+    out[4 * i] = W[i].ax; out[4 * i + 1] = W[i].ay; out[4 * i + 2] = W[i].bx; out[4 * i + 3] = W[i].by;
+  }
+  return int(W.size());
+}
+
 // Skip buildReencode (to time the keyframe without the re-encode stage, as the device can).
 void ref_set_reencode(void* h, int on) { static_cast<RefMap*>(h)->reenc_on = on != 0; }
 
@@ -166,6 +313,10 @@ int ref_frame(void* h, const rf_frame* f) {
   }
   m->reenc.clear();
   if (f->grid_only) return 0;
+  if (m->walls_on) {
+    if (f->wall_segs || !m->mapper) return -1;
+    if (int r = refresh_walls(m, f->stamp)) return r;
+  }
   // detections: the caller's bit masks, or the label image turned into bit masks on the image
   // grid (sm_detections, scenemap include/scenemap.h:20-34)
   const int n = f->n_det;
@@ -222,6 +373,10 @@ int ref_frame(void* h, const rf_frame* f) {
   F.emb_dim = f->emb_dim;
   F.wall_segs = f->wall_segs;
   F.n_wall_segs = f->n_wall_segs;
+  if (m->walls_on) {   // an empty list is a null pointer there (a fresh vector)
+    F.wall_segs = m->wsegs.empty() ? nullptr : m->wsegs.data();
+    F.n_wall_segs = int(m->wsegs.size() / 4);
+  }
   m->om.update(F);
   // best views (capi.cpp:903-943): moved / put-down events reset the view quality, views of
   // objects that are gone are dropped, detections attached to an object become candidates

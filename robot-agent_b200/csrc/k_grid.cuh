@@ -39,6 +39,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   __shared__ BlockScratch bs;
   __shared__ int sh_n[4];
   __shared__ int sh_ins;
+  __shared__ int sh_c8;   // a visible (export8) value changed in this insert (cells_changed_)
   const int m = B.map0 + blockIdx.x, tid = threadIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
@@ -347,6 +348,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
   // rays: laser hits (end excluded), free rays (end included) — Bresenham (grid.cpp:236-256)
   const int nray = nhh + nff;
   int applied_l = 0;
+  if (tid == 0) sh_c8 = 0;
   for (int pass = 0; pass < 2; ++pass) {
     int changed_l = 0;
     for (int r = tid; r < nray; r += blockDim.x) {
@@ -378,7 +380,9 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
           if (!(nL == L && was_seen)) {
             ++changed_l;
             *Lp = (int16_t)nL;
-            B.gc8[gbase + ci] = B.lut8[nL + B.lut_off];
+            const int8_t c8 = B.lut8[nL + B.lut_off];
+            if (B.gc8[gbase + ci] != c8) sh_c8 = 1;
+            B.gc8[gbase + ci] = c8;
             if (nL <= 0 && (*fl & 2)) {
               *fl &= (uint8_t)~2u;
               B.gcold[gbase + ci] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -418,7 +422,9 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
         *fl |= 3;
         changed_l += (nL != L) | !was_seen;
         *Lp = (int16_t)nL;
-        B.gc8[gbase + ci] = B.lut8[nL + B.lut_off];
+        const int8_t c8 = B.lut8[nL + B.lut_off];
+        if (B.gc8[gbase + ci] != c8) sh_c8 = 1;
+        B.gc8[gbase + ci] = c8;
         float4 cold = B.gcold[gbase + ci];
         uint32_t cnt = B.gcnt[gbase + ci];
         uint32_t c1 = cnt & 0xffffu, c2 = cnt >> 16;
@@ -435,6 +441,7 @@ __global__ void __launch_bounds__(GRID_THREADS) k_grid(Batch B) {
       else {
         R->kf_changed = sh_n[3] + ch;
         R->kf_last_changed = R->kf_changed;
+        if (sh_c8) R->w_dirty = 1;   // the wall extraction's grid_changed (cellsVersion)
         R->kf_last_ins[0] = pose[0];
         R->kf_last_ins[1] = pose[1];
         R->kf_last_ins[2] = pose[2];

@@ -793,14 +793,15 @@ __global__ void __launch_bounds__(OBS_THREADS, 2) k_obs(Batch B) {   // 2 CTAs p
   // wall-line share of apObsStructural (objmap.cpp:606-611): every stp-th candidate, within
   // wall_d of some segment of this keyframe's set
   int w_near = 0, w_tot = 0;
-  if (F.wall_set && F.n_wseg > 0 && nc >= 8) {
+  const int n_wf = B.maps[m].wfr;   // wall segments this keyframe carries
+  if (n_wf > 0 && nc >= 8) {
     const double* S = B.wsegs + (size_t)m * SMG_WALL_SEGS_MAX * 4;
     const int stp = nc / 64 > 1 ? nc / 64 : 1;
     w_tot = (nc + stp - 1) / stp;
     int near = 0;
     for (int j = tid; j < w_tot; j += blockDim.x) {
       const int i = j * stp;
-      near += wall_dist((double)CX[3 * i], (double)CX[3 * i + 1], S, F.n_wseg, P.wall_d) <= P.wall_d;
+      near += wall_dist((double)CX[3 * i], (double)CX[3 * i + 1], S, n_wf, P.wall_d) <= P.wall_d;
     }
     w_near = block_sum_i(near, bs);
   }
@@ -827,7 +828,8 @@ __global__ void k_obs_finalize(Batch B) {
   const int m = B.map0 + blockIdx.x;
   const FrameDev& F = B.frames[m];
   if (!F.active) return;
-  const bool walls = F.wall_set && F.n_wseg > 0;   // this keyframe carries wall segments
+  const int n_wf = B.maps[m].wfr;   // wall segments this keyframe carries
+  const bool walls = n_wf > 0;
   const double* S = B.wsegs + (size_t)m * SMG_WALL_SEGS_MAX * 4;
   // the fields the decision reads, staged by the warp; the walk then waits on no global load
   struct Fin {
@@ -849,7 +851,7 @@ __global__ void k_obs_finalize(Batch B) {
     f.through = 0;
     if (O->valid && walls) {
       const double cx0 = F.T_mc[3], cy0 = F.T_mc[7], dx = O->pos[0] - cx0, dy = O->pos[1] - cy0, L = hypot(dx, dy);
-      for (int s2 = 0; s2 < F.n_wseg && !f.through && L > 1e-6; ++s2) {
+      for (int s2 = 0; s2 < n_wf && !f.through && L > 1e-6; ++s2) {
         const double* w = S + 4 * s2;
         const double ex = w[2] - w[0], ey = w[3] - w[1], den = dx * ey - dy * ex;
         if (fabs(den) < 1e-9) continue;

@@ -37,6 +37,7 @@
 #include "k_hands.cuh"
 #include "k_views.cuh"
 #include "k_textmap.cuh"
+#include "k_walls.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -73,6 +74,7 @@ struct smg_batch {
   int groups = 1;
   bool host_gather = getenv("SMG_HOST_GATHER") == nullptr || atoi(getenv("SMG_HOST_GATHER")) != 0;
   cudaStream_t s_grp[kGroupsMax] = {}, s_gridg[kGroupsMax] = {}, s_copy = nullptr, s_dma = nullptr;
+  cudaEvent_t ev_wall[kGroupsMax] = {};   // a group's wall extraction (grid stream) is done
   cudaEvent_t ev_fork[kGroupsMax] = {}, ev_join[kGroupsMax] = {}, ev_copied[kGroupsMax] = {}, ev_gdone[kGroupsMax] = {},
               ev_dma[kGroupsMax] = {};
   cudaEvent_t ev_up = nullptr, ev_done = nullptr;
@@ -89,6 +91,7 @@ struct smg_batch {
   // staging sets, packed frame after frame
   double* h_wall = nullptr;
   double* d_wall = nullptr;
+  float* d_wstate = nullptr;   // smg_wall_state's result
   // The staging above is double-buffered: push k fills set k % 2 while the chain of push k - 1
   // still reads the other set, so a push's host-to-device copies overlap the previous chain.
   // ev_set[s] marks the end of the last chain that read set s.
@@ -129,7 +132,7 @@ struct smg_batch {
 
 static const char* k_names[SMG_NUM_KERNELS] = {"k_begin", "k_merge_pairs", "k_merge_apply", "k_obs", "k_obs_finalize", "k_assoc",
                                                "k_update", "k_absent", "k_relink", "k_struct", "k_prune", "k_markview",
-                                               "k_cloud_add", "k_grid", "k_reenc", "k_hands", "k_views"};
+                                               "k_cloud_add", "k_grid", "k_reenc", "k_hands", "k_views", "k_walls"};
 
 static cudaEvent_t ev_get(smg_batch* b) {
   if (b->ev_pool.empty()) {
@@ -332,7 +335,7 @@ int smg_destroy(smg_batch* b) {
   if (b->h_wall) cudaFreeHost(b->h_wall);
   for (auto e : b->ring_ev) if (e) cudaEventDestroy(e);
   for (int g = 0; g < smg_batch::kGroupsMax; ++g) {
-    for (cudaEvent_t e : {b->ev_fork[g], b->ev_join[g], b->ev_copied[g], b->ev_gdone[g], b->ev_dma[g]}) if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : {b->ev_fork[g], b->ev_join[g], b->ev_copied[g], b->ev_gdone[g], b->ev_dma[g], b->ev_wall[g]}) if (e) cudaEventDestroy(e);
     for (cudaStream_t q : {b->s_grp[g], b->s_gridg[g]}) if (q) cudaStreamDestroy(q);
   }
   for (cudaEvent_t e : {b->ev_up, b->ev_done, b->ev_set[0], b->ev_set[1], b->ev_rd[0], b->ev_rd[1], b->ev_rd[2], b->ev_rd[3]})
@@ -525,6 +528,8 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
       r.n_cfree = CP;
       r.kf_first = 1;
       r.kf_last_changed = 1 << 30;
+      r.w_th_t = r.w_full_t = -1e300;
+      r.w_dirty = 1;
     }
     CK(cudaMemcpy(B.maps, maps.data(), sizeof(MapRec) * M, cudaMemcpyHostToDevice));
     std::vector<int32_t> fl(MO);
@@ -575,7 +580,7 @@ int smg_create_pooled(const smg_params* p, int n_maps, int max_objects, int max_
     for (int g = 0; g < smg_batch::kGroupsMax; ++g) {
       if (g > 0) CK(cudaStreamCreateWithFlags(&b->s_grp[g], cudaStreamNonBlocking));
       CK(cudaStreamCreateWithFlags(&b->s_gridg[g], cudaStreamNonBlocking));
-      for (cudaEvent_t* e : {&b->ev_fork[g], &b->ev_join[g], &b->ev_copied[g], &b->ev_gdone[g], &b->ev_dma[g]})
+      for (cudaEvent_t* e : {&b->ev_fork[g], &b->ev_join[g], &b->ev_copied[g], &b->ev_gdone[g], &b->ev_dma[g], &b->ev_wall[g]})
         CK(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
     }
     {   // host-input streams; SMG_COPY_PRIORITY=1 gives them the highest priority (the SMs' reads of
@@ -637,14 +642,15 @@ __global__ void k_begin(Batch B) {
     AssocRec& a = B.assoc[(size_t)m * B.max_det + k];
     a.obj_id = 0; a.n_valid = 0; a.area_px = 0; a.depth_med = 0;
   }
-  if (F.wall_set) {   // ObjectMap::wsegs_ = this keyframe's wall segments (objmap.cpp:534)
+  if (F.wall_set && !B.walls_on) {   // ObjectMap::wsegs_ = this keyframe's wall segments (objmap.cpp:534)
     const int nw = min(F.n_wseg, SMG_WALL_SEGS_MAX);
     double* dst = B.wsegs + (size_t)m * SMG_WALL_SEGS_MAX * 4;
     for (int i = threadIdx.x; i < 4 * nw; i += blockDim.x) dst[i] = F.wsegs[i];
   }
   if (threadIdx.x == 0) {
     MapRec* R = &B.maps[m];
-    if (F.wall_set) R->n_wseg = min(F.n_wseg, SMG_WALL_SEGS_MAX);
+    if (F.wall_set && !B.walls_on) R->n_wseg = min(F.n_wseg, SMG_WALL_SEGS_MAX);
+    R->wfr = F.wall_set && !B.walls_on ? min(F.n_wseg, SMG_WALL_SEGS_MAX) : 0;   // extracted ones: k_walls
     R->n_events = 0;
     R->n_evn = 0;
     R->n_obs = 0;
@@ -667,11 +673,18 @@ static size_t obt_smem(const Batch& B) { return ((size_t)B.D + B.txt.n_labels) *
 static size_t wv_smem(const Batch& B) { return B.text_on ? ((size_t)B.D + 2 * B.txt.n_labels) * sizeof(float) : 0; }
 
 static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, cudaStream_t sgrid, cudaEvent_t efork,
-                        cudaEvent_t ejoin) {
+                        cudaEvent_t ejoin, cudaEvent_t ewall) {
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_begin<<<Mg, 128, 0, st>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({0, {e0, e1}}); } }
+  if (B.walls_on) {   // the ignore footprints, from the objects as they were before this keyframe
+    cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
+    k_wall_rects<<<Mg, 256, 0, st>>>(B);
+    ++b->launches;
+    if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after k_wall_rects: ") + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } }
+    if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({17, {e0, e1}}); }
+  }
   if (b->hands_on) {
     cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
     k_hands<<<Mg, HANDS_THREADS, 0, st>>>(B);
@@ -686,6 +699,14 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   k_grid<<<Mg, GRID_THREADS, 0, sgrid>>>(B);
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(sgrid); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after k_grid: ") + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } }
   if (b->timing) { cudaEventRecord(e1, sgrid); b->ev_used.push_back({13, {e0, e1}}); } }
+  if (B.walls_on) {   // wall segments of the updated grid, before the observations read them
+    cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, sgrid); }
+    k_walls<<<Mg, WALL_THREADS, WALL_SMEM, sgrid>>>(B);
+    ++b->launches;
+    if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(sgrid); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after k_walls: ") + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } }
+    if (b->timing) { cudaEventRecord(e1, sgrid); b->ev_used.push_back({17, {e0, e1}}); }
+    CK(cudaEventRecord(ewall, sgrid));
+  }
   CK(cudaEventRecord(ejoin, sgrid));
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_merge_gate<<<dim3(MP_CTAS, Mg), 256, MP_SMEM(B.O), st>>>(B);
@@ -697,6 +718,7 @@ static int launch_group(smg_batch* b, const Batch& B, int Mg, cudaStream_t st, c
   if (B.text_on) { k_rename<<<dim3(RN_CTAS, Mg), RN_WARPS * 32, rn_smem(B), st>>>(B); ++b->launches; }   // merged objects
   if (b->dbg_sync) { cudaError_t e_ = cudaStreamSynchronize(st); if (e_ == cudaSuccess) e_ = cudaGetLastError(); if (e_ != cudaSuccess) { g_err = std::string("after launch ") + std::to_string(b->dbg_last) + ": " + cudaGetErrorString(e_); return SMG_ERR_DEVICE; } ++b->dbg_last; }
   if (b->timing) { cudaEventRecord(e1, st); b->ev_used.push_back({2, {e0, e1}}); } }
+  if (B.walls_on) CK(cudaStreamWaitEvent(st, ewall, 0));
   { cudaEvent_t e0 = nullptr, e1 = nullptr; if (b->timing) { e0 = ev_get(b); e1 = ev_get(b); cudaEventRecord(e0, st); }
   k_obs<<<dim3(B.max_det, Mg), OBS_THREADS, OBS_SMEM, st>>>(B);
   if (B.text_on) { k_obs_text<<<dim3(B.max_det, Mg), OBT_THREADS, obt_smem(B), st>>>(B); ++b->launches; }
@@ -806,6 +828,8 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
       return fail(SMG_ERR_ARGS, "smg_push_frames: bad detection mask grid (mask_w x mask_h <= max_w x max_h, scales > 0)");
     if (f.wall_segs && (f.n_wall_segs < 0 || f.n_wall_segs > SMG_WALL_SEGS_MAX))
       return fail(SMG_ERR_ARGS, "smg_push_frames: n_wall_segs must be in [0, SMG_WALL_SEGS_MAX]");
+    if (f.wall_segs && B.walls_on)
+      return fail(SMG_ERR_ARGS, "smg_push_frames: wall_segs given while the library extracts walls (smg_set_walls)");
   }
   {
     bool any_rgba = false, any_wall = false;
@@ -1135,7 +1159,7 @@ int smg_push_frames(smg_batch* b, const smg_frame* frames, int n, int where, voi
     if (where == SMG_MEM_HOST) CK(cudaStreamWaitEvent(sg, b->ev_copied[g], 0));
     if (gather) CK(cudaStreamWaitEvent(sg, b->ev_dma[g], 0));
     if (Mg > 0)
-      if (int r = launch_group(b, Bg, Mg, sg, b->s_gridg[g], b->ev_fork[g], b->ev_join[g])) return r;
+      if (int r = launch_group(b, Bg, Mg, sg, b->s_gridg[g], b->ev_fork[g], b->ev_join[g], b->ev_wall[g])) return r;
     if (g > 0) {
       CK(cudaEventRecord(b->ev_gdone[g], sg));
       CK(cudaStreamWaitEvent(st, b->ev_gdone[g], 0));
@@ -2428,6 +2452,77 @@ int smg_get_object_name(smg_batch* b, int m, int i, float* post, int32_t* lab3, 
   if (lab3) { lab3[0] = o.name_lab; lab3[1] = o.top_lab; lab3[2] = o.rolled; }
   if (val3) { val3[0] = o.name_p; val3[1] = o.top_p; val3[2] = o.name_H; }
   return o.has_post ? C : 0;
+}
+
+// sm_push_image's wall extraction (capi.cpp:646-698, 866-890) before every object update.
+int smg_set_walls(smg_batch* b, int on) {
+  if (!b || (on != 0 && on != 1)) return fail(SMG_ERR_ARGS, "smg_set_walls: bad arguments");
+  if (int r = sync_b(b)) return r;
+  Batch& B = b->B;
+  if (on) {
+    const int w = B.gw_grid, h = B.gh_grid;
+    const int D = (int)std::ceil(std::hypot((double)w, (double)h)) + 2;
+    if ((size_t)2 * (2 * D + 1) * sizeof(int) > WALL_SMEM || w > 65535 || h > 65535)
+      return fail(SMG_ERR_ARGS, "smg_set_walls: grid window too large for wall extraction");
+    if (!B.wbits) {
+      const int side = D;   // a rotated window fits: ceil(hypot(w, h)) + 1 cells a side
+      const size_t O = (size_t)B.O, M = (size_t)B.M;
+      const size_t nw = (w + 63) / 64, snw = (side + 63) / 64;
+      const size_t rp = std::min(side / 2 + 1, WALL_ACT_MAX + 1);
+      B.wscr_side = side;
+      B.wbits_half = (size_t)h * nw;
+      B.wbits_stride = B.wbits_half + (size_t)side * snw;
+      B.wruns_stride = 2 * (size_t)side * rp;
+      B.wscr_i_stride = 8 * O + 2 * (size_t)side + 16;
+      if (int r = dalloc(b, &B.wbits, M * B.wbits_stride)) return r;
+      if (int r = dalloc(b, &B.wruns, M * B.wruns_stride)) return r;
+      if (int r = dalloc(b, &B.wscr_i, M * B.wscr_i_stride)) return r;
+      if (int r = dalloc(b, &B.wrect, M * O * 4)) return r;
+      if (int r = dalloc(b, &B.wrect_prev, M * O * 4)) return r;
+      if (int r = dalloc(b, &B.wall_w, M * SMG_WALL_SEGS_MAX * 4)) return r;
+      if (int r = dalloc(b, &B.wall_raw, M * SMG_WALL_SEGS_MAX * 4)) return r;
+      if (int r = dalloc(b, &b->d_wstate, (size_t)WALL_STATE_LEN)) return r;
+      CK(cudaFuncSetAttribute(k_walls, cudaFuncAttributeMaxDynamicSharedMemorySize, WALL_SMEM));
+    }
+    // a fresh extraction state (sm_reset, capi.cpp:554-558)
+    std::vector<MapRec> maps((size_t)B.M);
+    CK(cudaMemcpy(maps.data(), B.maps, sizeof(MapRec) * maps.size(), cudaMemcpyDeviceToHost));
+    for (MapRec& r : maps) {
+      r.w_th = 0;
+      r.w_th_t = r.w_full_t = -1e300;
+      r.w_has = 0;
+      r.w_dirty = 1;
+      r.n_w = r.n_rect = r.n_rect_prev = r.w_rchg = 0;
+    }
+    CK(cudaMemcpy(B.maps, maps.data(), sizeof(MapRec) * maps.size(), cudaMemcpyHostToDevice));
+  }
+  B.walls_on = on;
+  return SMG_OK;
+}
+
+int smg_get_wall_segments(smg_batch* b, int m, double* out, int cap) {
+  if (!b || m < 0 || m >= b->B.M || cap < 0 || (cap > 0 && !out)) return fail(SMG_ERR_ARGS, "smg_get_wall_segments: bad arguments");
+  if (int r = sync_b(b)) return r;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  if (!b->B.walls_on || !R.w_has) return -1;
+  const int n = std::min(R.n_w, SMG_WALL_SEGS_MAX);
+  if (cap > 0 && n > 0)
+    CK(cudaMemcpy(out, b->B.wall_w + (size_t)m * SMG_WALL_SEGS_MAX * 4, sizeof(double) * 4 * std::min(n, cap), cudaMemcpyDeviceToHost));
+  return n;
+}
+
+int smg_wall_state(smg_batch* b, int m, const double pose[3], float* out) {
+  if (!b || m < 0 || m >= b->B.M || !pose || !out) return fail(SMG_ERR_ARGS, "smg_wall_state: bad arguments");
+  if (int r = sync_b(b)) return r;
+  MapRec R;
+  if (int r = read_map(b, m, &R)) return r;
+  if (!b->B.walls_on || !R.w_has) return -1;
+  k_wall_state<<<1, 256, 0, b->last_stream>>>(b->B, m, pose[0], pose[1], pose[2], b->d_wstate);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(out, b->d_wstate, sizeof(float) * WALL_STATE_LEN, cudaMemcpyDeviceToHost, b->last_stream));
+  CK(cudaStreamSynchronize(b->last_stream));
+  return SMG_OK;
 }
 
 int smg_set_reencode(smg_batch* b, int on) {

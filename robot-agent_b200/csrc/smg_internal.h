@@ -43,6 +43,7 @@
 #define SMG_E_ARGS 32
 #define SMG_E_CAP_REENC 64   // more re-encode candidates in a keyframe than RE_CAND
 #define SMG_E_TRIM 128       // a cloud trim's selection ran past its depth limit (point order then differs)
+#define SMG_E_CAP_WALLS 256  // wall extraction ran past a capacity (segments, runs of a row, lines, samples)
 
 // Text model on the device (ApText, scenemap objprob.hpp:40-54, plus the class-kind table of
 // ObjectMap::setClassKinds and the label tables the reference glue derives from label names).
@@ -292,6 +293,13 @@ typedef struct {
   int32_t n_vnew;
   int32_t vnew[SMG_MAX_DET];   // candidate (detection) of each replaced view, install order
   int32_t n_wseg;        // the stored wall segments (ObjectMap::wsegs_), at Batch::wsegs
+  int32_t wfr;           // segments this keyframe carries (ObjFrame::n_wall_segs; 0 = none)
+  // wall extraction from the map's grid (sm_ctx wall state, capi.cpp:142-160): direction and the
+  // stamps of its last measurement and of the last tilted extraction; has = segments extracted;
+  // dirty = a visible grid value changed since; n_w segments at Batch::wall_w; the ignore
+  // footprints of this keyframe (n_rect, changed = differ from the last extraction's)
+  double w_th, w_th_t, w_full_t;
+  int32_t w_has, w_dirty, n_w, n_rect, n_rect_prev, w_rchg;
 } MapRec;
 
 // Whole-object re-encode candidate of a keyframe (ReencReq, scenemap objmap.hpp:142-148, plus
@@ -411,6 +419,19 @@ typedef struct {
   float* post;           // [M*O*C] ApState::post
   float* llz;            // [M*max_det*C] apLabelLogLik of each detection's embedding
   double* wsegs;         // [M*SMG_WALL_SEGS_MAX*4] the stored wall segments of each map
+  // wall extraction (smg_set_walls; allocated when first enabled)
+  int32_t walls_on;
+  int32_t wscr_side;     // side of the largest grid an extraction handles (the window rotated)
+  uint64_t* wbits;       // [M*wbits_stride] occupancy bits: the window, then a rotated window
+  size_t wbits_stride, wbits_half;
+  uint32_t* wruns;       // [M*wruns_stride] runs of rows, then of columns
+  size_t wruns_stride;
+  int32_t* wscr_i;       // [M*wscr_i_stride] ignore cell ranges (2*O int4), run counts
+  size_t wscr_i_stride;
+  double* wrect;         // [M*O*4] ignore footprints of the keyframe
+  double* wrect_prev;    // [M*O*4] those of the last extraction
+  double* wall_w;        // [M*SMG_WALL_SEGS_MAX*4] extracted segments (no bridges)
+  double* wall_raw;      // [M*SMG_WALL_SEGS_MAX*4] raw segments of a rotated extraction
   // best views (allocated on the first push with an RGB image)
   ViewRec* vrec;         // [M*max_det]
   uint8_t* vrgb;         // [M*max_det*VIEW_PIX*3]

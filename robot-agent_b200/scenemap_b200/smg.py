@@ -90,6 +90,9 @@ def lib():
         L.smg_set_text_model.argtypes = [vp, vp, vp, vp, vp]
         L.smg_get_object_name.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp]
         L.smg_wait_read.argtypes = [vp, C.c_int64]
+        L.smg_set_walls.argtypes = [vp, C.c_int]
+        L.smg_get_wall_segments.argtypes = [vp, C.c_int, vp, C.c_int]
+        L.smg_wall_state.argtypes = [vp, C.c_int, vp, vp]
         L.smg_get_stats.argtypes = [vp, C.c_int, vp]
         L.smg_get_events.argtypes = [vp, C.c_int, vp, vp, vp, C.c_int]
         L.smg_get_grid.argtypes = [vp, C.c_int, vp, vp, vp]
@@ -121,9 +124,9 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
            "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode",
            "smg_get_object_cloud_rgb", "smg_get_views", "smg_get_assoc_all_async", "smg_wait_read",
-           "smg_set_text_model", "smg_get_object_name"]
+           "smg_set_text_model", "smg_get_object_name", "smg_set_walls", "smg_get_wall_segments", "smg_wall_state"]
 
-NUM_KERNELS = 17
+NUM_KERNELS = 18
 
 
 def _ptr(a):
@@ -403,6 +406,31 @@ class Batch:
         k = _check(lib().smg_get_object_name(self.h, m, i, _ptr(post), _ptr(lab), _ptr(val)), "smg_get_object_name")
         return dict(has_post=k > 0, post=post, name_lab=int(lab[0]), top_lab=int(lab[1]), rolled=int(lab[2]), name_p=float(val[0]),
                     top_p=float(val[1]), name_H=float(val[2]))
+
+    def set_walls(self, on: bool = True) -> None:
+        """Extract wall segments from every map's grid before each object update (sm_push_image)."""
+        _check(lib().smg_set_walls(self.h, 1 if on else 0), "smg_set_walls")
+
+    def wall_segments(self, m: int):
+        """(n, 4) segments of map m's last extraction, or None before the first one."""
+        L = lib()
+        n = L.smg_get_wall_segments(self.h, m, None, 0)
+        if n == -1:
+            return None
+        _check(n, "smg_get_wall_segments")
+        out = np.zeros((max(n, 1), 4), np.float64)
+        L.smg_get_wall_segments(self.h, m, _ptr(out), n)
+        return out[:n]
+
+    def wall_state(self, m: int, pose) -> np.ndarray | None:
+        """The wall state vector (56 floats) of map m at pose (x, y, yaw), or None."""
+        p = np.ascontiguousarray(pose, np.float64)
+        out = np.zeros(56, np.float32)
+        rc = lib().smg_wall_state(self.h, m, _ptr(p), _ptr(out))
+        if rc == -1:
+            return None
+        _check(rc, "smg_wall_state")
+        return out
 
     def assoc_all_async(self, out_ptr: int) -> int:
         """Enqueue the read of every map's association into host memory at out_ptr (n_maps x
