@@ -118,9 +118,10 @@ typedef struct smg_params {
    * a fragment whose centre lies beyond a wall segment, seen from the camera, by more than
    * through_d is dropped; an object whose dominant plane is thinner than obj_flat_thick with
    * obj_flat_frac of its points within obj_flat_d of a wall line is a flat plane on the wall
-   * (geo 3).  bridge_max: the longest gap between two collinear segments that the extracted set
-   * closes (capi.cpp:873-887; 0 = none).  They act when a keyframe carries wall segments. */
-  double wall_d, wall_frac, through_d, bridge_max, obj_flat_thick, obj_flat_d, obj_flat_frac;
+   * (geo 3), dropped unless its flat-object and structural-object names hold flat_keep_p.
+   * bridge_max: the longest gap between two collinear segments that the extracted set closes
+   * (capi.cpp:873-887; 0 = none).  They act when a keyframe carries wall segments. */
+  double wall_d, wall_frac, through_d, bridge_max, obj_flat_thick, obj_flat_d, obj_flat_frac, flat_keep_p;
 } smg_params;
 
 /* One frame of one map.  depth/label/emb/dets/masks live in device memory (SMG_MEM_DEVICE) or
@@ -386,7 +387,8 @@ int smg_get_wall_segments(smg_batch* b, int m, double* out, int cap);
 /* sm_snap_wall_state (scenemap include/scenemap.h:96-99, capi.cpp:1239-1245; walls.hpp: the first
  * occupied cell along 16 rays from the pose, then the 8 nearest segments in the robot frame) of
  * map m at pose (x, y, yaw): SMG_WALL_STATE_LEN floats.  Returns -1 when walls are off or not yet
- * extracted. */
+ * extracted.  Segments at equal distance come in segment order (the reference's partial_sort
+ * leaves their order unspecified). */
 int smg_wall_state(smg_batch* b, int m, const double pose[3], float* out);
 
 /* Per-kernel device time with CUDA events on the launch stream (instrumentation, off by

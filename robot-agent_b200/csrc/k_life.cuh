@@ -495,6 +495,13 @@ DEV bool struct_object_drop(const Batch& B, size_t og, ObjRec& o) {
   }
   if (flat_named(B, o) && o.maj > P.flat_max_w && (o.geo != 0 || fw >= 0.5 || (double)o.vinl >= P.big_vinl)) { o.hide = 1; return false; }
   if (fw >= P.wallhug_frac && o.maj >= P.wallhug_w) { o.hide = 1; return false; }
+  if (o.geo == 3) {   // a flat plane on a wall line stays only under a flat-object or structural-object name
+    double q = qso;
+    if (post && B.txt.flat_ok)
+      for (int l = 0; l < C; ++l)
+        if (B.txt.flat_ok[l]) q += (double)post[l];
+    if (q < P.flat_keep_p) return true;
+  }
   if (o.geo == 1 || o.geo == 2) return true;
   if (o.n_whole < P.struct_obj_min_views || !post) return false;
   double q = 0;

@@ -287,8 +287,8 @@ DEV void wall_extract(const uint64_t* bits, int w, int h, int nw, double res, do
 // arithmetic as the reference's).  A groups of threads each fill their own histograms.
 DEV void wall_scores(const uint64_t* bits, int h, int nw, int D, const double* th, int na, unsigned long long* score, int* hist) {
   const int nb = 2 * D + 1;
-  int A = WALL_SMEM / (int)(2 * nb * sizeof(int));
-  A = max(1, min(A, 8));
+  const int fit = WALL_SMEM / (int)(2 * nb * sizeof(int));
+  const int A = fit >= 8 ? 8 : fit >= 4 ? 4 : fit >= 2 ? 2 : 1;   // whole warps per group
   const int G = blockDim.x / A, grp = threadIdx.x / G, gt = threadIdx.x - grp * G;
   for (int i = threadIdx.x; i < na; i += blockDim.x) score[i] = 0;
   for (int a0 = 0; a0 < na; a0 += A) {
@@ -317,12 +317,11 @@ DEV void wall_scores(const uint64_t* bits, int h, int nw, int D, const double* t
       }
     }
     __syncthreads();
-    if (live) {
-      unsigned long long acc = 0;
+    unsigned long long acc = 0;
+    if (live)
       for (int i = gt; i < nb; i += G) acc += (unsigned long long)hx[i] * hx[i] + (unsigned long long)hy[i] * hy[i];
-      for (int o = 16; o; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
-      if ((threadIdx.x & 31) == 0) atomicAdd(&score[ai], acc);
-    }
+    for (int o = 16; o; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+    if (live && (threadIdx.x & 31) == 0) atomicAdd(&score[ai], acc);
     __syncthreads();
   }
 }
@@ -578,9 +577,14 @@ DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, in
     const WallLine l = hz ? WallLine{1, q[1], smin(q[0], q[2]), smax(q[0], q[2])} : WallLine{0, q[0], smin(q[1], q[3]), smax(q[1], q[3])};
     nl += wall_refine(G, l, f, on, pcs, lines + nl, WALL_LINES - nl, s_ovf);
   }
-  // merge collinear neighbours until none is left (the first pair in (i, j) order each time)
-  for (bool changed = true; changed;) {
-    changed = false;
+  // merge collinear neighbours until none is left (the first pair in (i, j) order each time);
+  // every merge leaves fewer lines or pieces more than 4 cells apart, the guard only bounds a
+  // damaged list
+  for (int guard = 0;; ++guard) {
+    if (guard >= 4 * WALL_LINES) {
+      if (lane == 0) *s_ovf = 1;
+      break;
+    }
     int pi = -1, pj = -1;
     if (lane == 0)
       for (int i = 0; i < nl && pi < 0; ++i)
@@ -612,7 +616,6 @@ DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, in
     }
     nl = __shfl_sync(0xffffffffu, nl, 0);
     __syncwarp();
-    changed = true;
   }
   // to segments, drop shadowed short parallels, rotate back into the map frame
   double* Wl = B.wall_w + (size_t)m * SMG_WALL_SEGS_MAX * 4;

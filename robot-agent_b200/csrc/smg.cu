@@ -237,7 +237,7 @@ int smg_params_default(smg_params* p) {
   p->name_tau = 0.5; p->name_wmax = 6.0; p->size_w = 1.0; p->whole_w = 1.0; p->geo_w = 3.0; p->flat_max_w = 2.2;
   p->wall_big = 1.0; p->struct_p = 0.5;
   p->wall_d = 0.12; p->wall_frac = 0.6; p->through_d = 0.20; p->bridge_max = 0.0;
-  p->obj_flat_thick = 0.012; p->obj_flat_d = 0.10; p->obj_flat_frac = 0.7;
+  p->obj_flat_thick = 0.012; p->obj_flat_d = 0.10; p->obj_flat_frac = 0.7; p->flat_keep_p = 0.5;
   p->so_dw_w = 2.2; p->so_dw_thick = 0.45; p->so_max_h = 2.8; p->so_pillar = 1.0; p->so_stairs = 6.0; p->so_dw_min = 0.3;
   p->so_hide_k = 1.5; p->wallhug_frac = 0.75; p->wallhug_w = 2.0; p->big_vinl = 0.5;
   p->struct_look_block = 1; p->so_min_obs = 12;
@@ -2473,7 +2473,7 @@ int smg_set_walls(smg_batch* b, int on) {
       B.wbits_half = (size_t)h * nw;
       B.wbits_stride = B.wbits_half + (size_t)side * snw;
       B.wruns_stride = 2 * (size_t)side * rp;
-      B.wscr_i_stride = 8 * O + 2 * (size_t)side + 16;
+      B.wscr_i_stride = (8 * O + 2 * (size_t)side + 16 + 3) & ~(size_t)3;   // int4-aligned per map
       if (int r = dalloc(b, &B.wbits, M * B.wbits_stride)) return r;
       if (int r = dalloc(b, &B.wruns, M * B.wruns_stride)) return r;
       if (int r = dalloc(b, &B.wscr_i, M * B.wscr_i_stride)) return r;

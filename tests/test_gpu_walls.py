@@ -6,7 +6,7 @@ Runs the structure room (walls, floor and ceiling come back as detections) with 
 so confirmed named objects give ignore footprints, and compares every keyframe as the default
 parity test does (the wall-line rules and the see-through drop then act on the extracted
 segments), plus the extracted segments themselves (bit for bit) and the wall state vector at the
-camera's pose.  The tilted case turns the whole map frame by 20 degrees: the dominant-direction
+base pose.  The tilted case turns the whole map frame by 20 degrees: the dominant-direction
 measurement, the rotated extraction and its refit to the original grid.
 """
 import math
@@ -79,7 +79,13 @@ def _run(th_deg: float, n_frames: int, seed_base: int, bridge: float = 0.0):
             n_seen = max(n_seen, len(wr))
             pose = fr["base"]
             sr, sg = R.wall_state(pose), B.wall_state(0, pose)
-            assert np.array_equal(sr, sg), f"frame {f}: wall state differs: {np.abs(sr - sg).max()}"
+            # rays exactly; the nearest segments as a set: std::partial_sort leaves the order of
+            # segments at equal distance (two walls meeting at the nearest corner) unspecified,
+            # the device takes them in segment order
+            assert np.array_equal(sr[:16], sg[:16]), f"frame {f}: wall rays differ: {np.abs(sr[:16] - sg[:16]).max()}"
+            a, b = sr[16:].reshape(8, 5), sg[16:].reshape(8, 5)
+            assert np.array_equal(np.array(sorted(map(tuple, a))), np.array(sorted(map(tuple, b)))), \
+                f"frame {f}: nearest wall segments differ"
     assert B.error_word() == 0
     st = R.stats()
     B.close()
