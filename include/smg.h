@@ -265,6 +265,22 @@ int smg_get_object_name(smg_batch* b, int m, int i, float* post, int32_t* lab3, 
  * q >= the view's q (ties: the newer), moved / put-down events reset the view's q to 0).  box:
  * the crop (detection box + 10 % per side, clipped), det_box: the rounded detection box, both
  * in image pixels [x0, y0, x1, y1); w x h: the crop's size (longer side <= 256). */
+/* sm_object (scenemap include/scenemap.h:55-66) of an exportable object as sm_snapshot lists it
+ * (capi.cpp:1051-1067), plus what scene.json and sm_snap_movable / sm_snap_points read of it. */
+typedef struct smg_snap_object {
+  uint32_t id;
+  int32_t name_lab;            /* class label (sm_object::name is that label's name); -1 = "?" */
+  float score;
+  double pos[3], extent[3], first_pos[3];   /* map */
+  uint32_t n_obs;
+  double last_seen;
+  int32_t state;               /* SM_SEEN 0, SM_GONE 1, SM_MOVED 2, SM_HELD 3 (held by a hand) */
+  int32_t structural;          /* static or structural-object kind, or a side longer than big */
+  int32_t movable;             /* neither static nor structural-object kind (sm_snap_movable) */
+  int32_t n_points;            /* cloud points (sm_snap_points) */
+  double cloud_stamp;          /* stamp of the cloud's last addition */
+} smg_snap_object;
+
 typedef struct smg_view {
   uint32_t id, version;
   double q, stamp;
@@ -390,6 +406,20 @@ int smg_get_wall_segments(smg_batch* b, int m, double* out, int cap);
  * extracted.  Segments at equal distance come in segment order (the reference's partial_sort
  * leaves their order unspecified). */
 int smg_wall_state(smg_batch* b, int m, const double pose[3], float* out);
+
+/* The object-memory snapshot of every map in one call: sm_snapshot's object list (scenemap
+ * capi.cpp:1051-1067: ObjectMap::exportable objects in object order, the hand's objects as
+ * SM_HELD) and dsg_save's object point files (dsg_save.cpp:70-89 plyBytes: per point float x, y,
+ * z in map metres and uchar r, g, b, 15 bytes, little-endian), packed on the device.
+ * map_off (n_maps + 1 entries): map m's objects are [map_off[m], map_off[m+1]).  Returns the
+ * number of objects n.  objs (and point_off, n + 1 entries: object i's points are records
+ * [point_off[i], point_off[i+1])) are filled when cap_objs >= n; points when cap_points >= the
+ * total records, which *n_points receives.  Call once with NULL buffers to size them. */
+int smg_snapshot(smg_batch* b, int32_t* map_off, smg_snap_object* objs, int cap_objs, int64_t* point_off, uint8_t* points,
+                 int64_t cap_points, int64_t* n_points);
+/* The PLY header plyBytes writes before n vertex records (ASCII, binary_little_endian 1.0, x y z
+ * float, red green blue uchar); returns its length, or the needed size when cap is too small. */
+int smg_ply_header(int64_t n, char* out, int cap);
 
 /* Per-kernel device time with CUDA events on the launch stream (instrumentation, off by
  * default).  smg_timing_read fills ms[k] (total milliseconds) and n[k] (launches) for the

@@ -17,6 +17,13 @@ REF_SO = os.path.join(HERE, "_ref", "libscenemap_ref.so")
 PORT_SO = os.path.join(HERE, "_ref", "libport.so")
 
 
+class RfSnap(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("name_lab", C.c_int32), ("score", C.c_float), ("pos", C.c_double * 3),
+                ("extent", C.c_double * 3), ("first_pos", C.c_double * 3), ("n_obs", C.c_uint32), ("last_seen", C.c_double),
+                ("state", C.c_int32), ("structural", C.c_int32), ("movable", C.c_int32), ("n_points", C.c_int32),
+                ("cloud_stamp", C.c_double)]
+
+
 class RfFrame(C.Structure):
     _fields_ = [("stamp", C.c_double), ("w", C.c_int), ("h", C.c_int), ("depth", C.POINTER(C.c_float)),
                 ("label", C.POINTER(C.c_uint16)), ("fx", C.c_float), ("fy", C.c_float), ("cx", C.c_float),
@@ -126,6 +133,9 @@ def ref_lib():
         L.ref_contact.restype = C.c_double
         L.ref_contact.argtypes = [P(C.c_float), C.c_int, P(C.c_float), C.c_int, C.c_double]
         L.ref_set_walls.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.ref_snapshot.argtypes = [C.c_void_p, P(RfSnap), C.c_int]
+        L.ref_snapshot_ply.restype = C.c_long
+        L.ref_snapshot_ply.argtypes = [C.c_void_p, C.c_int, P(C.c_uint8), C.c_long]
         L.ref_wall_segments.argtypes = [C.c_void_p, P(C.c_double), C.c_int]
         L.ref_wall_state.argtypes = [C.c_void_p, P(C.c_double), P(C.c_float)]
         L.ref_wall_segments_grid.argtypes = [P(C.c_int8), C.c_int, C.c_int, C.c_double, C.c_double, C.c_double, P(C.c_double),
@@ -267,6 +277,27 @@ class RefMap:
         seq = np.zeros(max(n, 1), np.uint32)
         L.ref_object_cloud(self._h, i, _p(xyz, C.c_float), _p(seq, C.c_uint32), n)
         return xyz[:n], seq[:n]
+
+    def snapshot(self) -> list:
+        """sm_snapshot's object list (exportable objects, object order) as dicts."""
+        L = ref_lib()
+        n = L.ref_snapshot(self._h, None, 0)
+        recs = (RfSnap * max(n, 1))()
+        L.ref_snapshot(self._h, recs, n)
+        out = []
+        for k in range(n):
+            r = recs[k]
+            out.append({name: (list(getattr(r, name)) if isinstance(getattr(r, name), C.Array) else getattr(r, name))
+                        for name, _ in RfSnap._fields_})
+        return out
+
+    def snapshot_ply(self, n: int) -> bytes:
+        """dsg_save's point file (plyBytes) of the n-th exportable object."""
+        L = ref_lib()
+        k = L.ref_snapshot_ply(self._h, n, None, 0)
+        buf = np.zeros(max(k, 1), np.uint8)
+        L.ref_snapshot_ply(self._h, n, _p(buf, C.c_uint8), k)
+        return buf[:k].tobytes()
 
     def set_walls(self, grid) -> None:
         """Wall extraction before every object update (sm_push_image's refreshWalls and bridges),

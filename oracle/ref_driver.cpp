@@ -16,9 +16,11 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <memory>
 #include <unordered_set>
+#include <string>
 #include <vector>
 
 #include "scenemap/bestview.hpp"
@@ -244,6 +246,75 @@ void* ref_create(const char* obj_kv, double voxel, int cloud_cap, int grid_on, c
 }
 
 void ref_destroy(void* h) { delete static_cast<RefMap*>(h); }
+
+// sm_snapshot's object list (capi.cpp:1051-1067; big = ObjParams::big): the exportable objects
+// in object order.  Record layout of smg_snap_object.
+typedef struct {
+  uint32_t id;
+  int32_t name_lab;
+  float score;
+  double pos[3], extent[3], first_pos[3];
+  uint32_t n_obs;
+  double last_seen;
+  int32_t state, structural, movable, n_points;
+  double cloud_stamp;
+} rf_snap;
+
+int ref_snapshot(void* h, rf_snap* out, int cap) {
+  RefMap* m = static_cast<RefMap*>(h);
+  const double big = m->om.params().big;
+  int n = 0;
+  for (const MapObject& o : m->om.objects()) {
+    if (!m->om.exportable(o)) continue;
+    if (out && n < cap) {
+      rf_snap& e = out[n];
+      memset(&e, 0, sizeof(e));
+      e.id = o.id;
+      e.name_lab = o.cls;   // the label index (the runtime names it from its label table)
+      e.score = o.score;
+      for (int k = 0; k < 3; ++k) { e.pos[k] = o.pos[k]; e.extent[k] = o.ext[k]; e.first_pos[k] = o.first_pos[k]; }
+      e.n_obs = o.n_obs;
+      e.last_seen = o.last_seen;
+      e.state = o.held_by >= 0 ? SM_HELD : o.state;
+      const int kind = m->om.kindOf(o.cls);
+      e.structural = kind == kKindStatic || kind == kKindStructObj || std::max({o.ext[0], o.ext[1], o.ext[2]}) > big;
+      e.movable = kind != kKindStatic && kind != kKindStructObj;
+      e.n_points = int(o.cloud.size());
+      e.cloud_stamp = o.cloud.stamp;
+    }
+    ++n;
+  }
+  return n;
+}
+
+// dsg_save.cpp:70-89 plyBytes of the n-th exportable object: the whole file (header and 15-byte
+// vertex records); returns its size
+long ref_snapshot_ply(void* h, int n, uint8_t* out, long cap) {
+  RefMap* m = static_cast<RefMap*>(h);
+  int k = -1;
+  for (const MapObject& o : m->om.objects()) {
+    if (!m->om.exportable(o) || ++k != n) continue;
+    const ObjCloud& c = o.cloud;
+    const size_t np = c.size();
+    std::string hdr = "ply\nformat binary_little_endian 1.0\nelement vertex " + std::to_string(np) +
+                      "\nproperty float x\nproperty float y\nproperty float z\nproperty uchar red\nproperty uchar green\n"
+                      "property uchar blue\nend_header\n";
+    const long total = long(hdr.size() + np * 15);
+    if (!out || cap < total) return total;
+    memcpy(out, hdr.data(), hdr.size());
+    uint8_t* p = out + hdr.size();
+    for (size_t i = 0; i < np; ++i, p += 15) {
+      const CloudPt& q = c.data->pts[i];
+      const float xyz[3] = {float(c.org[0] + q.x), float(c.org[1] + q.y), float(c.org[2] + q.z)};
+      memcpy(p, xyz, 12);
+      p[12] = q.r;
+      p[13] = q.g;
+      p[14] = q.b;
+    }
+    return total;
+  }
+  return -1;
+}
 
 // Wall extraction before every object update (sm_push_image's refreshWalls), on the grid window
 // x0, y0 (cells), w x h.

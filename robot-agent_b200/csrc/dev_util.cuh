@@ -682,6 +682,13 @@ DEV void push_event(const Batch& B, int map, double t, const ObjRec& o, int kind
 DEV int kind_of(const Batch& B, int cls) {   // ObjectMap::kindOf (objmap.hpp:246)
   return B.txt.kinds && cls >= 0 && cls < B.txt.n_labels ? (int)B.txt.kinds[cls] : KIND_OBJECT;
 }
+// ObjectMap::exportable (objmap.hpp:273-279) with export_named on (the only setting accepted
+// here): confirmed, named (a posterior), not hidden, not the fallback name, not a structure label
+DEV bool exportable(const Batch& B, const ObjRec& o) {
+  if (!o.confirmed || !o.has_post || o.hide) return false;
+  if (B.txt.object_label >= 0 && o.cls == B.txt.object_label) return false;
+  return kind_of(B, o.cls) != KIND_STRUCTURE;
+}
 // ObjectMap::isBig (objmap.cpp:207-209)
 DEV bool is_big(const Batch& B, const ObjRec& o) {
   const int k = kind_of(B, o.cls);

@@ -48,10 +48,7 @@
 // (confirmed, named, not hidden, not the fallback name, not a structure label), not held, not
 // gone, reaching down to 0.4 m, not wall-like, not a structural object, at most 5 m wide.
 DEV bool wall_ignores(const Batch& B, const ObjRec& o) {
-  if (!o.confirmed || !o.has_post || o.hide) return false;
-  if (B.txt.object_label >= 0 && o.cls == B.txt.object_label) return false;
-  const int kd = kind_of(B, o.cls);
-  if (kd == KIND_STRUCTURE || kd == KIND_STRUCT_OBJ) return false;
+  if (!exportable(B, o) || kind_of(B, o.cls) == KIND_STRUCT_OBJ) return false;
   if (o.held_by >= 0 || o.state == 1 || o.lo[2] > 0.4 || o.wall_like) return false;
   const double dx = o.hi[0] - o.lo[0], dy = o.hi[1] - o.lo[1];
   return !(dx > 5.0 || dy > 5.0);

@@ -38,6 +38,7 @@
 #include "k_views.cuh"
 #include "k_textmap.cuh"
 #include "k_walls.cuh"
+#include "k_snap.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -92,6 +93,16 @@ struct smg_batch {
   double* h_wall = nullptr;
   double* d_wall = nullptr;
   float* d_wstate = nullptr;   // smg_wall_state's result
+  // smg_snapshot scratch (allocated on the first call; the point records grow as needed)
+  smg_snap_object* d_snap_rec = nullptr;
+  smg_snap_object* d_snap_out = nullptr;
+  int32_t* d_snap_cnt = nullptr;
+  int32_t* d_snap_src = nullptr;
+  int32_t* d_snap_moff = nullptr;
+  int64_t* d_snap_npts = nullptr;
+  int64_t* d_snap_poff = nullptr;
+  uint8_t* d_snap_pts = nullptr;
+  size_t snap_pts_cap = 0;
   // The staging above is double-buffered: push k fills set k % 2 while the chain of push k - 1
   // still reads the other set, so a push's host-to-device copies overlap the previous chain.
   // ev_set[s] marks the end of the last chain that read set s.
@@ -333,6 +344,7 @@ int smg_destroy(smg_batch* b) {
   for (void* p : b->allocs) cudaFree(p);
   if (b->h_ring) cudaFreeHost(b->h_ring);
   if (b->h_wall) cudaFreeHost(b->h_wall);
+  if (b->d_snap_pts) cudaFree(b->d_snap_pts);
   for (auto e : b->ring_ev) if (e) cudaEventDestroy(e);
   for (int g = 0; g < smg_batch::kGroupsMax; ++g) {
     for (cudaEvent_t e : {b->ev_fork[g], b->ev_join[g], b->ev_copied[g], b->ev_gdone[g], b->ev_dma[g], b->ev_wall[g]}) if (e) cudaEventDestroy(e);
@@ -2523,6 +2535,65 @@ int smg_wall_state(smg_batch* b, int m, const double pose[3], float* out) {
   CK(cudaMemcpyAsync(out, b->d_wstate, sizeof(float) * WALL_STATE_LEN, cudaMemcpyDeviceToHost, b->last_stream));
   CK(cudaStreamSynchronize(b->last_stream));
   return SMG_OK;
+}
+
+int smg_snapshot(smg_batch* b, int32_t* map_off, smg_snap_object* objs, int cap_objs, int64_t* point_off, uint8_t* points,
+                 int64_t cap_points, int64_t* n_points) {
+  if (!b || !map_off || cap_objs < 0 || cap_points < 0) return fail(SMG_ERR_ARGS, "smg_snapshot: bad arguments");
+  if (int r = sync_b(b)) return r;
+  const Batch& B = b->B;
+  const size_t MO = (size_t)B.M * B.O;
+  if (!b->d_snap_rec) {
+    if (int r = dalloc(b, &b->d_snap_rec, MO)) return r;
+    if (int r = dalloc(b, &b->d_snap_out, MO)) return r;
+    if (int r = dalloc(b, &b->d_snap_cnt, (size_t)B.M)) return r;
+    if (int r = dalloc(b, &b->d_snap_src, MO)) return r;
+    if (int r = dalloc(b, &b->d_snap_moff, (size_t)B.M + 1)) return r;
+    if (int r = dalloc(b, &b->d_snap_npts, MO)) return r;
+    if (int r = dalloc(b, &b->d_snap_poff, MO + 1)) return r;
+  }
+  cudaStream_t st = b->last_stream;
+  k_snap_list<<<B.M, 256, 0, st>>>(B, b->d_snap_rec, b->d_snap_cnt, b->d_snap_npts, b->d_snap_src);
+  k_snap_scan<<<1, SNAP_SCAN_THREADS, 0, st>>>(B, b->d_snap_cnt, b->d_snap_npts, b->d_snap_moff, b->d_snap_poff);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(map_off, b->d_snap_moff, sizeof(int32_t) * (B.M + 1), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  const int n = map_off[B.M];
+  int64_t total = 0;
+  CK(cudaMemcpy(&total, b->d_snap_poff + n, sizeof(int64_t), cudaMemcpyDeviceToHost));
+  if (n_points) *n_points = total;
+  const bool want_objs = objs && cap_objs >= n;
+  const bool want_pts = points && cap_points >= total && total > 0;
+  if (want_pts && (size_t)total * 15 > b->snap_pts_cap) {
+    if (b->d_snap_pts) CK(cudaFree(b->d_snap_pts));
+    b->d_snap_pts = nullptr;
+    b->snap_pts_cap = 0;
+    CK(cudaMalloc(&b->d_snap_pts, (size_t)total * 15));
+    b->snap_pts_cap = (size_t)total * 15;
+  }
+  if ((want_objs || want_pts) && n > 0) {
+    k_snap_pack<<<dim3(64, B.M), 256, 0, st>>>(B, b->d_snap_rec, b->d_snap_cnt, b->d_snap_src, b->d_snap_moff, b->d_snap_poff,
+                                               want_objs ? b->d_snap_out : nullptr, want_pts ? b->d_snap_pts : nullptr);
+    CK(cudaGetLastError());
+    if (want_objs) {
+      CK(cudaMemcpyAsync(objs, b->d_snap_out, sizeof(smg_snap_object) * n, cudaMemcpyDeviceToHost, st));
+      if (point_off) CK(cudaMemcpyAsync(point_off, b->d_snap_poff, sizeof(int64_t) * (n + 1), cudaMemcpyDeviceToHost, st));
+    }
+    if (want_pts) CK(cudaMemcpyAsync(points, b->d_snap_pts, (size_t)total * 15, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+  } else if (want_objs && point_off) {
+    point_off[0] = 0;
+  }
+  return n;
+}
+
+int smg_ply_header(int64_t n, char* out, int cap) {
+  if (n < 0 || cap < 0) return fail(SMG_ERR_ARGS, "smg_ply_header: bad arguments");
+  const std::string h = "ply\nformat binary_little_endian 1.0\nelement vertex " + std::to_string(n) +
+                        "\nproperty float x\nproperty float y\nproperty float z\nproperty uchar red\nproperty uchar green\n"
+                        "property uchar blue\nend_header\n";
+  if (out && cap >= (int)h.size()) memcpy(out, h.data(), h.size());
+  return (int)h.size();
 }
 
 int smg_set_reencode(smg_batch* b, int on) {

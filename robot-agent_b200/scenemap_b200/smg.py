@@ -34,6 +34,13 @@ class SmgFrame(C.Structure):
                 ("n_wall_segs", C.c_int32)]
 
 
+class SmgSnapObject(C.Structure):
+    _fields_ = [("id", C.c_uint32), ("name_lab", C.c_int32), ("score", C.c_float), ("pos", C.c_double * 3),
+                ("extent", C.c_double * 3), ("first_pos", C.c_double * 3), ("n_obs", C.c_uint32), ("last_seen", C.c_double),
+                ("state", C.c_int32), ("structural", C.c_int32), ("movable", C.c_int32), ("n_points", C.c_int32),
+                ("cloud_stamp", C.c_double)]
+
+
 class SmgView(C.Structure):
     _fields_ = [("id", C.c_uint32), ("version", C.c_uint32), ("q", C.c_double), ("stamp", C.c_double),
                 ("box", C.c_int32 * 4), ("det_box", C.c_int32 * 4), ("mask_area", C.c_float), ("depth_m", C.c_float),
@@ -91,6 +98,8 @@ def lib():
         L.smg_get_object_name.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp]
         L.smg_wait_read.argtypes = [vp, C.c_int64]
         L.smg_set_walls.argtypes = [vp, C.c_int]
+        L.smg_snapshot.argtypes = [vp, vp, vp, C.c_int, vp, vp, C.c_int64, C.POINTER(C.c_int64)]
+        L.smg_ply_header.argtypes = [C.c_int64, vp, C.c_int]
         L.smg_get_wall_segments.argtypes = [vp, C.c_int, vp, C.c_int]
         L.smg_wall_state.argtypes = [vp, C.c_int, vp, vp]
         L.smg_get_stats.argtypes = [vp, C.c_int, vp]
@@ -124,7 +133,8 @@ EXPORTED = ["smg_params_set_cloud", "smg_params_size", "smg_params_default", "sm
            "smg_occ_insert", "smg_occ_match", "smg_occ_track", "smg_occ_get_cells", "smg_assoc_create", "smg_assoc_destroy",
            "smg_assoc_match", "smg_assoc_error", "smg_assoc_stamps", "smg_label_loglik", "smg_name", "smg_get_reencode",
            "smg_get_object_cloud_rgb", "smg_get_views", "smg_get_assoc_all_async", "smg_wait_read",
-           "smg_set_text_model", "smg_get_object_name", "smg_set_walls", "smg_get_wall_segments", "smg_wall_state"]
+           "smg_set_text_model", "smg_get_object_name", "smg_set_walls", "smg_get_wall_segments", "smg_wall_state",
+           "smg_snapshot", "smg_ply_header"]
 
 NUM_KERNELS = 18
 
@@ -431,6 +441,33 @@ class Batch:
             return None
         _check(rc, "smg_wall_state")
         return out
+
+    def snapshot(self, points: bool = True) -> dict:
+        """The object-memory snapshot of every map: map_off (n_maps + 1), objects (list of dicts,
+        map after map), point_off and the packed 15-byte PLY vertex records (bytes)."""
+        L = lib()
+        moff = np.zeros(self.n_maps + 1, np.int32)
+        tot = C.c_int64(0)
+        n = _check(L.smg_snapshot(self.h, _ptr(moff), None, 0, None, None, 0, C.byref(tot)), "smg_snapshot")
+        recs = (SmgSnapObject * max(n, 1))()
+        poff = np.zeros(n + 1, np.int64)
+        pts = np.zeros(max(int(tot.value), 1) * 15, np.uint8)
+        _check(L.smg_snapshot(self.h, _ptr(moff), recs, n, _ptr(poff), _ptr(pts) if points else None, int(tot.value) if points else 0,
+                              C.byref(tot)), "smg_snapshot")
+        objs = []
+        for k in range(n):
+            r = recs[k]
+            objs.append({name: (list(getattr(r, name)) if isinstance(getattr(r, name), C.Array) else getattr(r, name))
+                         for name, _ in SmgSnapObject._fields_})
+        return dict(map_off=moff, objects=objs, point_off=poff, points=pts[:int(tot.value) * 15].tobytes() if points else None)
+
+    @staticmethod
+    def ply_header(n: int) -> bytes:
+        L = lib()
+        k = L.smg_ply_header(n, None, 0)
+        buf = C.create_string_buffer(k)
+        L.smg_ply_header(n, buf, k)
+        return buf.raw[:k]
 
     def assoc_all_async(self, out_ptr: int) -> int:
         """Enqueue the read of every map's association into host memory at out_ptr (n_maps x
