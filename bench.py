@@ -775,6 +775,64 @@ def main():
     print(json.dumps(out))
 
 
+def run_walls(args, local_rank: int, n_frames: int = 40) -> dict:
+    """Wall extraction (smg_set_walls) on the config-1 maps: every keyframe's grid insert changes
+    visible cells, so k_walls re-extracts all 64 maps each keyframe (the direction every 2 s of
+    stamps).  Device time of k_walls per launch by CUDA events (timing mode), and the reference's
+    walls.cpp (wallAngle + wallSegments) on the same final grids on one host core."""
+    import torch
+    from scenemap_b200 import smg
+    from scenemap_b200.workload import RoomBatch
+    torch.cuda.set_device(local_rank)
+    M = args.maps
+    grid = (512, 512, -256 + 60, -256 + 50)
+    wl = RoomBatch(M, 1000, n_frames, D=1152, bf16=True, max_det=24, device=f"cuda:{local_rank}")
+    B = smg.Batch(M, max_objects=args.max_objects, emb_dim=1152, max_w=640, max_h=480, max_det=24, grid=grid, dev=local_rank,
+                  **pool_kw(args))
+    B.set_walls(True)
+    B.timing(True)
+    for f0 in range(0, n_frames, 8):
+        nf = min(8, n_frames - f0)
+        R = wl.render(f0, nf, 0)
+        for fi in range(nf):
+            keep = []
+            if f0 + fi == n_frames // 2:
+                B.timing_read()   # the first half fills the grids
+            B.push(None, smg.SMG_MEM_DEVICE, structs=wl.structs(R, fi, keep), stream=0)
+        torch.cuda.synchronize()
+    kt = B.timing_read()
+    ms, n = kt.get("k_walls", (0.0, 0))
+    per = ms / max(1, n // 2)   # k_wall_rects + k_walls: two launches per keyframe
+    nseg = []
+    for m in range(M):
+        w = B.wall_segments(m)
+        nseg.append(0 if w is None else len(w))
+    err = B.error_word()
+    cells = [B.grid_cells(m)["c8"] for m in range(M)]
+    B.close()
+    res = 0.05
+    ox, oy = grid[2] * float(np.float32(res)), grid[3] * float(np.float32(res))
+    line = {"metric": "wall extractions/s (every map's grid, one launch)", "value": M / (per * 1e-3) if per > 0 else None,
+            "unit": "map-extractions/s", "ms_per_launch": per, "maps": M, "segments_per_map": float(np.mean(nseg)),
+            "error_word": err,
+            "roofline": {"bound": "latency (one CTA per map; the chaining warp walks every row and column)",
+                         "alg_bytes_per_map": 512 * 512, "achieved_gbs": M * 512 * 512 / (per * 1e-3) / 1e9 if per > 0 else None}}
+    try:
+        import time
+        from oracle import ref
+        if ref.available():
+            t0 = time.perf_counter()
+            for c in cells:
+                ref.wall_segments_grid(c, float(np.float32(res)), ox, oy, mode=1)
+                ref.wall_segments_grid(c, float(np.float32(res)), ox, oy, mode=0)
+            dt = time.perf_counter() - t0
+            line["cpu_baseline"] = {"value": M / dt, "unit": "map-extractions/s", "cores": 1, "kind": "reference",
+                                    "sample": f"walls.cpp wallAngle + wallSegments on the {M} final grids"}
+    except Exception as e:
+        line["cpu_baseline"] = {"error": f"{type(e).__name__}: {e}"}
+    return line
+
+
 def extra_workloads(args, local_rank: int) -> dict:
     """Short device-timed runs of the other configurations, so the default run records them:
     config 2 (association GEMM, 8 frames per call) and config 3 (occupancy insert + scan match,
@@ -793,6 +851,10 @@ def extra_workloads(args, local_rank: int) -> dict:
         out["config3"] = occ_line(run_occ(a3, 0, 1, local_rank), a3, 1)
     except Exception as e:
         out["config3"] = {"error": f"{type(e).__name__}: {e}"}
+    try:
+        out["walls"] = run_walls(args, local_rank)
+    except Exception as e:
+        out["walls"] = {"error": f"{type(e).__name__}: {e}"}
     return out
 
 
