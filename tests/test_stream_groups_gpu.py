@@ -26,7 +26,7 @@ def _pinned(fr: dict) -> dict:
     return out
 
 
-def _run(groups: int, M: int, N: int, D: int, pinned: bool = False):
+def _run(groups: int, M: int, N: int, D: int, pinned: bool = False, walls: bool = False):
     from scenemap_b200 import smg, synth
     os.environ["SMG_STREAM_GROUPS"] = str(groups)
     try:
@@ -34,6 +34,9 @@ def _run(groups: int, M: int, N: int, D: int, pinned: bool = False):
     finally:
         del os.environ["SMG_STREAM_GROUPS"]
     gens = [synth.BoxRoom(seed=synth.map_seed(9090, i), n_frames=N, D=D, bf16=True) for i in range(M)]
+    if walls:   # wall extraction on each group's grid stream, the object streams waiting for it
+        B.set_text_model(synth.text_model(gens[0]))
+        B.set_walls(True)
     trace = []
     for f in range(N):
         frs = [g.frame(f) for g in gens]
@@ -49,6 +52,8 @@ def _run(groups: int, M: int, N: int, D: int, pinned: bool = False):
         out[f"events{m}"] = B.events(m)
         out[f"grid{m}"] = B.grid_cells(m)
         out[f"kf{m}"] = B.keyframe(m)
+        if walls:
+            out[f"walls{m}"] = B.wall_segments(m)
     B.close()
     return out
 
@@ -91,3 +96,15 @@ def test_pinned_host_frames_gathered():
     pinned = _run(4, M, N, D, pinned=True)
     assert paged["err"] == 0 and pinned["err"] == 0
     _same(paged, pinned)
+
+
+def test_stream_groups_with_walls():
+    """Wall extraction on every group's grid stream gives what one chain gives."""
+    if not has_gpu():
+        pytest.skip("no GPU")
+    M, N, D = 8, 24, 1152
+    one = _run(1, M, N, D, walls=True)
+    four = _run(4, M, N, D, walls=True)
+    assert one["err"] == 0 and four["err"] == 0
+    assert any(one[f"walls{m}"] is not None and len(one[f"walls{m}"]) for m in range(M))
+    _same(one, four)
