@@ -112,9 +112,9 @@ def parse():
                     help="objprob: skip the short config-2 / config-3 runs recorded under extra_workloads")
     ap.add_argument("--assoc-frames", type=int, default=32,
                     help="config 2: frames per association call (their detections as one row block against the bank)")
-    ap.add_argument("--workload", default="objprob", choices=["objprob", "occ", "assoc"],
+    ap.add_argument("--workload", default="objprob", choices=["objprob", "occ", "assoc", "walls"],
                     help="objprob = config 1 (headline); occ = config 3 (grid insert + correlative scan matching); "
-                         "assoc = config 2 (association GEMM)")
+                         "assoc = config 2 (association GEMM); walls = wall extraction from the config-1 grids")
     ap.add_argument("--scans", type=int, default=5000, help="config 3: scans per map")
     ap.add_argument("--mask-grid", type=int, default=0, metavar="S",
                     help="detections as the detector's bit masks on an S-pixel grid (sm_detections form) instead of "
@@ -662,12 +662,16 @@ def occ_line(r: dict, args, world: int) -> dict:
 def main():
     args = parse()
     if args.maps is None:
-        args.maps = 64 if args.workload == "objprob" else 1
+        args.maps = 64 if args.workload in ("objprob", "walls") else 1
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.check_run:
         check_run(args, local_rank)
+        return
+    if args.workload == "walls":   # the wall-extraction line alone (one GPU)
+        if rank == 0:
+            print(json.dumps(run_walls(args, local_rank)))
         return
     masks = ("u16 label image (mask grid = image grid)" if args.mask_grid <= 0 else
              f"detector bit masks on a {args.mask_grid}-pixel grid (sm_detections form)")

@@ -12,8 +12,9 @@
 //    keyframe's list: the extracted segments plus the window bridges between collinear ones.
 //    One CTA per map.  The occupancy of the window becomes row bits (top row first); runs of
 //    occupied cells along rows and along columns are found in parallel (a thread per row /
-//    column), and one warp chains runs of consecutive rows into groups in the reference's order
-//    (a ballot picks the first open group a run overlaps), emitting each group's centre line.
+//    column), and one warp per direction chains runs of consecutive rows (columns) into groups
+//    in the reference's order (a ballot picks the first open group a run overlaps), emitting
+//    each group's centre line.
 //    The dominant direction scores all candidate angles of a stage at once: each group of
 //    threads fills its own shared-memory projection histograms.
 //  - k_wall_state: sm_snap_wall_state (capi.cpp:1239-1245, walls.cpp rayDistances /
@@ -257,7 +258,8 @@ DEV void wall_group_warp(const uint32_t* runs, const int32_t* cnt, int nrows, in
 // wallSegments on the bits already built (walls.cpp update: rows first, then columns).  The
 // caller's scratch: runs (h * rp_h + w * rp_v), counts (h + w), group lists in shared memory.
 DEV void wall_extract(const uint64_t* bits, int w, int h, int nw, double res, double ox, double oy, uint32_t* runs, int32_t* cnt,
-                      unsigned char* smem, WallOut& o, int* s_ovf) {
+                      unsigned char* smem, WallOut& o, double* vtmp, int* s_ovf) {
+  __shared__ int s_hn, s_vn, s_vovf;
   const int min_run = max(1, (int)llround(WALL_MIN_LEN / res));
   const int rp_h = min(w / 2 + 1, WALL_ACT_MAX + 1), rp_v = min(h / 2 + 1, WALL_ACT_MAX + 1);
   uint32_t* hr = runs;
@@ -267,12 +269,29 @@ DEV void wall_extract(const uint64_t* bits, int w, int h, int nw, double res, do
   wall_row_runs(bits, h, nw, min_run, hr, rp_h, hc, s_ovf);
   wall_col_runs(bits, w, h, nw, min_run, vr, rp_v, vc, s_ovf);
   __syncthreads();
-  if (threadIdx.x < 32) {
-    int4* act = (int4*)smem;
+  // rows (warp 0, into o) and columns (warp 1, into vtmp) are chained at the same time; the
+  // column segments then follow the row segments, the reference's order
+  const int wq = threadIdx.x >> 5;
+  if (wq < 2) {
+    int4* act = (int4*)smem + (size_t)wq * 2 * WALL_ACT_MAX;
     int4* nxt = act + WALL_ACT_MAX;
-    uint8_t* used = (uint8_t*)(nxt + WALL_ACT_MAX);
-    wall_group_warp(hr, hc, h, rp_h, false, h, res, ox, oy, act, nxt, used, o);
-    wall_group_warp(vr, vc, w, rp_v, true, h, res, ox, oy, act, nxt, used, o);
+    uint8_t* used = (uint8_t*)((int4*)smem + 4 * WALL_ACT_MAX) + (size_t)wq * WALL_ACT_MAX;
+    if (wq == 0) {
+      wall_group_warp(hr, hc, h, rp_h, false, h, res, ox, oy, act, nxt, used, o);
+      if ((threadIdx.x & 31) == 0) s_hn = o.n;
+    } else {
+      WallOut ov{vtmp, o.cap, 0, 0};
+      wall_group_warp(vr, vc, w, rp_v, true, h, res, ox, oy, act, nxt, used, ov);
+      if ((threadIdx.x & 31) == 0) { s_vn = ov.n; s_vovf = ov.ovf; }
+    }
+  }
+  __syncthreads();
+  const int hn = s_hn, vn = s_vn;
+  for (int i = threadIdx.x; i < 4 * vn; i += blockDim.x)
+    if (4 * (size_t)hn + i < 4 * (size_t)o.cap) o.seg[4 * (size_t)hn + i] = vtmp[i];
+  if (threadIdx.x == 0) {
+    o.n = min(hn + vn, o.cap);
+    if (hn + vn > o.cap || s_vovf) o.ovf = 1;
   }
   __syncthreads();
 }
@@ -303,14 +322,22 @@ DEV void wall_scores(const uint64_t* bits, int h, int nw, int D, const double* t
         if (!v) continue;
         const int iy = wi / nw, k = wi - iy * nw;
         const float py = (float)(h - 1 - iy);
+        int pb = -1, pc = 0;   // the y-axis bin changes slowly along a row: counted in a register
         while (v) {
           const float px = (float)(k * 64 + __ffsll((long long)v) - 1);
           v &= v - 1;
           const int i1 = (int)__fadd_rn(__fadd_rn(__fmul_rn(c, px), __fmul_rn(s, py)), d);
           const int i2 = (int)__fadd_rn(__fadd_rn(__fmul_rn(-s, px), __fmul_rn(c, py)), d);
           if ((unsigned)i1 < (unsigned)nb) atomicAdd(&hx[i1], 1);
-          if ((unsigned)i2 < (unsigned)nb) atomicAdd(&hy[i2], 1);
+          if (i2 == pb) {
+            ++pc;
+          } else {
+            if (pc && (unsigned)pb < (unsigned)nb) atomicAdd(&hy[pb], pc);
+            pb = i2;
+            pc = 1;
+          }
         }
+        if (pc && (unsigned)pb < (unsigned)nb) atomicAdd(&hy[pb], pc);
       }
     }
     __syncthreads();
@@ -548,7 +575,7 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
   WallOut o{raw, SMG_WALL_SEGS_MAX, 0, 0};
   uint32_t* runs = B.wruns + (size_t)m * B.wruns_stride;
   int32_t* cnt = (int32_t*)(rc1 + B.O);
-  wall_extract(rbits, RW, RH, rnw, res, u0, v0, runs, cnt, smem, o, s_ovf);
+  wall_extract(rbits, RW, RH, rnw, res, u0, v0, runs, cnt, smem, o, B.wall_tmp + (size_t)m * SMG_WALL_SEGS_MAX * 4, s_ovf);
   if (threadIdx.x < 32) wall_refit_warp(B, m, obits, w, h, nw, res, ox, oy, c, s, raw, o, smem, s_ovf);
   __syncthreads();
 }
@@ -749,7 +776,7 @@ __global__ void __launch_bounds__(WALL_THREADS) k_walls(Batch B) {
     WallOut o{Wl, SMG_WALL_SEGS_MAX, 0, 0};
     uint32_t* runs = B.wruns + (size_t)m * B.wruns_stride;
     int32_t* cnt = (int32_t*)(rc1 + O);
-    wall_extract(bits, w, h, nw, res, ox, oy, runs, cnt, wl_smem, o, &s_ovf);
+    wall_extract(bits, w, h, nw, res, ox, oy, runs, cnt, wl_smem, o, B.wall_tmp + (size_t)m * SMG_WALL_SEGS_MAX * 4, &s_ovf);
     if (threadIdx.x == 0) {
       R->n_w = o.n;
       if (o.ovf) s_ovf = 1;

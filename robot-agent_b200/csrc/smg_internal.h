@@ -432,6 +432,7 @@ typedef struct {
   double* wrect_prev;    // [M*O*4] those of the last extraction
   double* wall_w;        // [M*SMG_WALL_SEGS_MAX*4] extracted segments (no bridges)
   double* wall_raw;      // [M*SMG_WALL_SEGS_MAX*4] raw segments of a rotated extraction
+  double* wall_tmp;      // [M*SMG_WALL_SEGS_MAX*4] column segments while the rows' are chained
   // best views (allocated on the first push with an RGB image)
   ViewRec* vrec;         // [M*max_det]
   uint8_t* vrgb;         // [M*max_det*VIEW_PIX*3]
