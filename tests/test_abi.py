@@ -82,3 +82,13 @@ def test_bad_arguments_fail_cleanly_without_gpu():
     assert L.smg_destroy(None) == -1
     assert L.smg_plane_fit(None, None, 0, 0, 0.02, None, 64, None, None) == -1
     assert b"bad arguments" in L.smg_last_error()
+
+
+def test_ply_header_is_the_reference_format():
+    """smg_ply_header writes plyBytes' header (dsg_save.cpp:70-76): binary little-endian, float
+    x y z, uchar red green blue; a buffer too small gets the needed size and no bytes."""
+    from scenemap_b200 import smg
+    want = (b"ply\nformat binary_little_endian 1.0\nelement vertex 1234\nproperty float x\nproperty float y\n"
+            b"property float z\nproperty uchar red\nproperty uchar green\nproperty uchar blue\nend_header\n")
+    assert smg.Batch.ply_header(1234) == want
+    assert smg.lib().smg_ply_header(1234, None, 0) == len(want)
