@@ -301,7 +301,20 @@ DEV void wall_extract(const uint64_t* bits, int w, int h, int nw, double res, do
 // Projection-histogram scores of angles th[0..na): for each, the sum over bins of squared counts
 // of the occupied cells projected on the rotated x and y axes (bins of one cell, float
 // arithmetic as the reference's).  A groups of threads each fill their own histograms.
-DEV void wall_scores(const uint64_t* bits, int h, int nw, int D, const double* th, int na, unsigned long long* score, int* hist) {
+// The occupancy again, column by column (word (x, b) holds rows 64 b .. 64 b + 63 of column x,
+// top row first), for the rotated x-axis histogram: its bin changes slowly down a column.
+DEV void wall_cbits(const uint64_t* bits, int w, int h, int nw, uint64_t* cbits) {
+  const int nwc = (h + 63) / 64;
+  for (int i = threadIdx.x; i < w * nwc; i += blockDim.x) {
+    const int x = i / nwc, kb = i - x * nwc, k = x >> 6, sh = x & 63;
+    uint64_t v = 0;
+    for (int b = 0; b < 64 && kb * 64 + b < h; ++b) v |= ((bits[(size_t)(kb * 64 + b) * nw + k] >> sh) & 1ull) << b;
+    cbits[i] = v;
+  }
+}
+
+DEV void wall_scores(const uint64_t* bits, const uint64_t* cbits, int w, int h, int nw, int D, const double* th, int na,
+                     unsigned long long* score, int* hist) {
   const int nb = 2 * D + 1;
   const int fit = WALL_SMEM / (int)(2 * nb * sizeof(int));
   const int A = fit >= 8 ? 8 : fit >= 4 ? 4 : fit >= 2 ? 2 : 1;   // whole warps per group
@@ -316,19 +329,19 @@ DEV void wall_scores(const uint64_t* bits, int h, int nw, int D, const double* t
       for (int i = gt; i < 2 * nb; i += G) hx[i] = 0;
     __syncthreads();
     if (live) {
+      // each bin is counted along the direction it changes slowly in, runs of equal bins in a
+      // register: y-axis bins along rows, x-axis bins down columns
       const float c = (float)cos(th[ai]), s = (float)sin(th[ai]), d = __fadd_rn((float)D, 0.5f);
       for (int wi = gt; wi < h * nw; wi += G) {
         uint64_t v = bits[wi];
         if (!v) continue;
         const int iy = wi / nw, k = wi - iy * nw;
         const float py = (float)(h - 1 - iy);
-        int pb = -1, pc = 0;   // the y-axis bin changes slowly along a row: counted in a register
+        int pb = -1, pc = 0;
         while (v) {
           const float px = (float)(k * 64 + __ffsll((long long)v) - 1);
           v &= v - 1;
-          const int i1 = (int)__fadd_rn(__fadd_rn(__fmul_rn(c, px), __fmul_rn(s, py)), d);
           const int i2 = (int)__fadd_rn(__fadd_rn(__fmul_rn(-s, px), __fmul_rn(c, py)), d);
-          if ((unsigned)i1 < (unsigned)nb) atomicAdd(&hx[i1], 1);
           if (i2 == pb) {
             ++pc;
           } else {
@@ -338,6 +351,27 @@ DEV void wall_scores(const uint64_t* bits, int h, int nw, int D, const double* t
           }
         }
         if (pc && (unsigned)pb < (unsigned)nb) atomicAdd(&hy[pb], pc);
+      }
+      const int nwc = (h + 63) / 64;
+      for (int wi = gt; wi < w * nwc; wi += G) {
+        uint64_t v = cbits[wi];
+        if (!v) continue;
+        const int x = wi / nwc, kb = wi - x * nwc;
+        const float px = (float)x;
+        int pb = -1, pc = 0;
+        while (v) {
+          const float py = (float)(h - 1 - (kb * 64 + __ffsll((long long)v) - 1));
+          v &= v - 1;
+          const int i1 = (int)__fadd_rn(__fadd_rn(__fmul_rn(c, px), __fmul_rn(s, py)), d);
+          if (i1 == pb) {
+            ++pc;
+          } else {
+            if (pc && (unsigned)pb < (unsigned)nb) atomicAdd(&hx[pb], pc);
+            pb = i1;
+            pc = 1;
+          }
+        }
+        if (pc && (unsigned)pb < (unsigned)nb) atomicAdd(&hx[pb], pc);
       }
     }
     __syncthreads();
@@ -353,7 +387,7 @@ DEV void wall_scores(const uint64_t* bits, int h, int nw, int D, const double* t
 // wallAngle (walls.cpp:224-257) on the bits: 1-degree scan of [-45, 45), then 0.25 and 0.05
 // degree refinements around the best, folded to [-45, 45) degrees; 0 when fewer than 20 cells are
 // occupied or the best beats 0 degrees by less than kAlignGain.
-DEV double wall_angle(const uint64_t* bits, int w, int h, int nw, unsigned char* smem, BlockScratch& bs) {
+DEV double wall_angle(const uint64_t* bits, uint64_t* cbits, int w, int h, int nw, unsigned char* smem, BlockScratch& bs) {
   __shared__ double s_th[96];
   __shared__ unsigned long long s_sc[96];
   __shared__ double s_best;
@@ -369,7 +403,9 @@ DEV double wall_angle(const uint64_t* bits, int w, int h, int nw, unsigned char*
     for (int k = -45; k < 45; ++k) s_th[1 + k + 45] = k * deg;
   }
   __syncthreads();
-  wall_scores(bits, h, nw, D, s_th, 91, s_sc, (int*)smem);
+  wall_cbits(bits, w, h, nw, cbits);
+  __syncthreads();
+  wall_scores(bits, cbits, w, h, nw, D, s_th, 91, s_sc, (int*)smem);
   if (threadIdx.x == 0) {
     s_v0 = s_sc[0];
     double best = 0.0;
@@ -387,7 +423,7 @@ DEV double wall_angle(const uint64_t* bits, int w, int h, int nw, unsigned char*
       for (int k = -4; k <= 4; ++k) s_th[k + 4] = c0 + k * step;
     }
     __syncthreads();
-    wall_scores(bits, h, nw, D, s_th, 9, s_sc, (int*)smem);
+    wall_scores(bits, cbits, w, h, nw, D, s_th, 9, s_sc, (int*)smem);
     if (threadIdx.x == 0)
       for (int k = 0; k < 9; ++k)
         if (s_sc[k] > s_bv) { s_bv = s_sc[k]; s_best = s_th[k]; }
@@ -745,7 +781,7 @@ __global__ void __launch_bounds__(WALL_THREADS) k_walls(Batch B) {
     wall_bits(cells, w, h, nw, bits, rc0, rc1, nrc);
     __syncthreads();
     built = true;
-    const double th = wall_angle(bits, w, h, nw, wl_smem, bs);
+    const double th = wall_angle(bits, bits + B.wbits_half, w, h, nw, wl_smem, bs);   // the rotated half is free here
     if (threadIdx.x == 0) s_thn = th;
   }
   if (threadIdx.x == 0) {
