@@ -10,9 +10,9 @@
 //    2 s of stamps when the grid or the footprints changed, 1-degree hysteresis; axis-aligned maps
 //    re-extract on every change, tilted ones at most every 0.5 s), the extraction itself, and the
 //    keyframe's list: the extracted segments plus the window bridges between collinear ones.
-//    One CTA per map.  The occupancy of the window becomes row bits (top row first); runs of
-//    occupied cells along rows and along columns are found in parallel (a thread per row /
-//    column), and one warp per direction chains runs of consecutive rows (columns) into groups
+//    One CTA per map.  The occupancy of the window becomes row bits (top row first) and, by
+//    warp ballots, column bits; runs of occupied cells along rows and along columns are found
+//    word-wise in parallel (a thread per row / column), and one warp per direction chains runs of consecutive rows (columns) into groups
 //    in the reference's order (a ballot picks the first open group a run overlaps), emitting
 //    each group's centre line.
 //    The dominant direction scores all candidate angles of a stage at once: each group of
@@ -107,7 +107,19 @@ DEV void wall_bits(const int8_t* cells, int w, int h, int nw, uint64_t* bits, co
     const int8_t* row = cells + (size_t)y * w;
     const int x0 = k * 64, x1 = min(w, x0 + 64);
     uint64_t v = 0;
-    for (int x = x0; x < x1; ++x) v |= (uint64_t)(row[x] >= WALL_OCC) << (x - x0);
+    if (x1 - x0 == 64 && (((size_t)(row + x0)) & 15) == 0) {   // four 16-byte loads in flight
+      uint4 q[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q[j] = ((const uint4*)(row + x0))[j];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t wd[4] = {q[j].x, q[j].y, q[j].z, q[j].w};
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v |= (uint64_t)((int8_t)(wd[e >> 2] >> (8 * (e & 3))) >= WALL_OCC) << (16 * j + e);
+      }
+    } else {
+      for (int x = x0; x < x1; ++x) v |= (uint64_t)(row[x] >= WALL_OCC) << (x - x0);
+    }
     for (int r = 0; r < n_rc && v; ++r) {
       const int4 a = rc0[r], b = rc1[r];   // a = (x0, y0), b = (x1, y1)
       if (y < a.y || y > b.y || b.x < x0 || a.x >= x1) continue;
@@ -152,28 +164,6 @@ DEV void wall_row_runs(const uint64_t* bits, int h, int nw, int min_run, uint32_
   }
 }
 
-// Runs of every column, top to bottom (a thread per column): run = first row | last row << 16.
-DEV void wall_col_runs(const uint64_t* bits, int w, int h, int nw, int min_run, uint32_t* runs, int rp, int32_t* cnt, int* ovf) {
-  for (int x = threadIdx.x; x < w; x += blockDim.x) {
-    const int k = x >> 6, sh = x & 63;
-    int n = 0, start = -1;
-    for (int iy = 0; iy <= h; ++iy) {
-      const bool b = iy < h && ((bits[(size_t)iy * nw + k] >> sh) & 1ull);
-      if (b && start < 0) {
-        start = iy;
-      } else if (!b && start >= 0) {
-        if (iy - start >= min_run) {
-          if (n < rp) runs[(size_t)x * rp + n] = (uint32_t)start | (uint32_t)(iy - 1) << 16;
-          ++n;
-        }
-        start = -1;
-      }
-    }
-    if (n > rp) atomicOr(ovf, 1);
-    cnt[x] = min(n, rp);
-  }
-}
-
 struct WallOut {
   double* seg;   // n x 4
   int cap, n, ovf;
@@ -202,14 +192,18 @@ DEV void wall_group_warp(const uint32_t* runs, const int32_t* cnt, int nrows, in
                          double oy, int4* act, int4* nxt, uint8_t* used, WallOut& o) {
   const int lane = threadIdx.x & 31;
   int nact = 0;
+  int cl = 0;            // lane l holds the run count of row (r & ~31) + l
+  uint32_t myrun = 0u;   // lane q holds run q of the current row
   for (int r = 0; r < nrows; ++r) {
-    const int nr = cnt[r];
+    if ((r & 31) == 0) cl = r + lane < nrows ? cnt[r + lane] : 0;   // 32 rows' counts, one load each
+    const int nr = __shfl_sync(0xffffffffu, cl, r & 31);
     if (nr == 0 && nact == 0) continue;
+    myrun = lane < nr ? runs[(size_t)r * rp + lane] : 0u;   // the row's runs in one load per lane
     for (int i = lane; i < nact; i += 32) used[i] = 0;
     __syncwarp();
     int nn = 0;
     for (int q = 0; q < nr && nn < WALL_ACT_MAX; ++q) {
-      const uint32_t rv = runs[(size_t)r * rp + q];
+      const uint32_t rv = q < 32 ? __shfl_sync(0xffffffffu, myrun, q) : runs[(size_t)r * rp + q];
       const int a = (int)(rv & 0xffffu), b = (int)(rv >> 16);
       int hit = -1;
       for (int base = 0; base < nact && hit < 0; base += 32) {
@@ -257,8 +251,9 @@ DEV void wall_group_warp(const uint32_t* runs, const int32_t* cnt, int nrows, in
 
 // wallSegments on the bits already built (walls.cpp update: rows first, then columns).  The
 // caller's scratch: runs (h * rp_h + w * rp_v), counts (h + w), group lists in shared memory.
-DEV void wall_extract(const uint64_t* bits, int w, int h, int nw, double res, double ox, double oy, uint32_t* runs, int32_t* cnt,
-                      unsigned char* smem, WallOut& o, double* vtmp, int* s_ovf) {
+DEV void wall_cbits(const uint64_t* bits, int w, int h, int nw, uint64_t* cbits);
+DEV void wall_extract(const uint64_t* bits, uint64_t* cbits, int w, int h, int nw, double res, double ox, double oy, uint32_t* runs,
+                      int32_t* cnt, unsigned char* smem, WallOut& o, double* vtmp, int* s_ovf) {
   __shared__ int s_hn, s_vn, s_vovf;
   const int min_run = max(1, (int)llround(WALL_MIN_LEN / res));
   const int rp_h = min(w / 2 + 1, WALL_ACT_MAX + 1), rp_v = min(h / 2 + 1, WALL_ACT_MAX + 1);
@@ -266,8 +261,10 @@ DEV void wall_extract(const uint64_t* bits, int w, int h, int nw, double res, do
   uint32_t* vr = runs + (size_t)h * rp_h;
   int32_t* hc = cnt;
   int32_t* vc = cnt + h;
+  wall_cbits(bits, w, h, nw, cbits);   // columns as rows of bits: their runs are found word-wise too
   wall_row_runs(bits, h, nw, min_run, hr, rp_h, hc, s_ovf);
-  wall_col_runs(bits, w, h, nw, min_run, vr, rp_v, vc, s_ovf);
+  __syncthreads();
+  wall_row_runs(cbits, w, (h + 63) / 64, min_run, vr, rp_v, vc, s_ovf);
   __syncthreads();
   // rows (warp 0, into o) and columns (warp 1, into vtmp) are chained at the same time; the
   // column segments then follow the row segments, the reference's order
@@ -303,13 +300,24 @@ DEV void wall_extract(const uint64_t* bits, int w, int h, int nw, double res, do
 // arithmetic as the reference's).  A groups of threads each fill their own histograms.
 // The occupancy again, column by column (word (x, b) holds rows 64 b .. 64 b + 63 of column x,
 // top row first), for the rotated x-axis histogram: its bin changes slowly down a column.
+// A warp transposes 32 rows x 64 columns: each lane loads one row's word, 64 ballots give the 64
+// columns' 32-bit halves (half g of column x is 32-bit word x * 2 * nwc + g).
 DEV void wall_cbits(const uint64_t* bits, int w, int h, int nw, uint64_t* cbits) {
-  const int nwc = (h + 63) / 64;
-  for (int i = threadIdx.x; i < w * nwc; i += blockDim.x) {
-    const int x = i / nwc, kb = i - x * nwc, k = x >> 6, sh = x & 63;
-    uint64_t v = 0;
-    for (int b = 0; b < 64 && kb * 64 + b < h; ++b) v |= ((bits[(size_t)(kb * 64 + b) * nw + k] >> sh) & 1ull) << b;
-    cbits[i] = v;
+  const int nwc = (h + 63) / 64, lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  uint32_t* c32 = (uint32_t*)cbits;
+  for (int t = wid; t < 2 * nwc * nw; t += nwarps) {
+    const int g = t / nw, k = t - g * nw, iy = g * 32 + lane;
+    const uint64_t v = iy < h ? bits[(size_t)iy * nw + k] : 0ull;
+    uint32_t lo = 0u, hi = 0u;
+#pragma unroll
+    for (int b = 0; b < 64; ++b) {
+      const uint32_t col = __ballot_sync(0xffffffffu, (unsigned)((v >> b) & 1ull));
+      if (b == lane) lo = col;
+      if (b == lane + 32) hi = col;
+    }
+    const int x0 = k * 64 + lane, x1 = x0 + 32;
+    if (x0 < w) c32[(size_t)x0 * 2 * nwc + g] = lo;
+    if (x1 < w) c32[(size_t)x1 * 2 * nwc + g] = hi;
   }
 }
 
@@ -585,8 +593,16 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
     return;
   }
   __syncthreads();
-  // rotated occupancy bits, top row first
+  // rotated occupancy bits, top row first; the original bits are read from shared memory when
+  // they fit (a 512 x 512 window: 32 KB)
   uint64_t* rbits = obits + (size_t)B.wbits_half;
+  const uint64_t* src = obits;
+  if ((size_t)h * nw * 8 <= (size_t)WALL_SMEM) {
+    uint64_t* sob = (uint64_t*)smem;
+    for (int i = threadIdx.x; i < h * nw; i += blockDim.x) sob[i] = obits[i];
+    __syncthreads();
+    src = sob;
+  }
   for (int i = threadIdx.x; i < RH * rnw; i += blockDim.x) {
     const int iy = i / rnw, k = i - iy * rnw, j = RH - 1 - iy;
     const double v = v0 + (j + 0.5) * res;
@@ -599,7 +615,7 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
       for (int q = 0; q < 4 && !occ; ++q) {
         const int x = x0 + (q & 1), y = y0 + (q >> 1);
         if (x < 0 || y < 0 || x >= w || y >= h) continue;
-        occ = (obits[(size_t)(h - 1 - y) * nw + (x >> 6)] >> (x & 63)) & 1ull;
+        occ = (src[(size_t)(h - 1 - y) * nw + (x >> 6)] >> (x & 63)) & 1ull;
       }
       word |= (uint64_t)occ << b;
     }
@@ -611,7 +627,8 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
   WallOut o{raw, SMG_WALL_SEGS_MAX, 0, 0};
   uint32_t* runs = B.wruns + (size_t)m * B.wruns_stride;
   int32_t* cnt = (int32_t*)(rc1 + B.O);
-  wall_extract(rbits, RW, RH, rnw, res, u0, v0, runs, cnt, smem, o, B.wall_tmp + (size_t)m * SMG_WALL_SEGS_MAX * 4, s_ovf);
+  wall_extract(rbits, obits + B.wbits_cb, RW, RH, rnw, res, u0, v0, runs, cnt, smem, o, B.wall_tmp + (size_t)m * SMG_WALL_SEGS_MAX * 4,
+               s_ovf);
   if (threadIdx.x < 32) wall_refit_warp(B, m, obits, w, h, nw, res, ox, oy, c, s, raw, o, smem, s_ovf);
   __syncthreads();
 }
@@ -629,7 +646,16 @@ DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, in
   WallLine* tmp = pcs + WALL_PIECES;
   double* f = (double*)(tmp + WALL_PIECES);
   uint8_t* on = (uint8_t*)(f + 32);
-  const WallRot G{obits, w, h, nw, res, ox, oy, c, s};
+  // the original occupancy in shared memory when it fits beside the lists (a 512 x 512 window
+  // takes 32 KB), the samples' reads then wait for no global load
+  const uint64_t* ob = obits;
+  if ((size_t)32768 + (size_t)h * nw * 8 <= (size_t)WALL_SMEM) {
+    uint64_t* sob = (uint64_t*)(smem + 32768);
+    for (int i = lane; i < h * nw; i += 32) sob[i] = obits[i];
+    __syncwarp();
+    ob = sob;
+  }
+  const WallRot G{ob, w, h, nw, res, ox, oy, c, s};
   int nl = 0;
   for (int r = 0; r < nraw; ++r) {
     const double* q = raw + 4 * r;
@@ -781,7 +807,7 @@ __global__ void __launch_bounds__(WALL_THREADS) k_walls(Batch B) {
     wall_bits(cells, w, h, nw, bits, rc0, rc1, nrc);
     __syncthreads();
     built = true;
-    const double th = wall_angle(bits, bits + B.wbits_half, w, h, nw, wl_smem, bs);   // the rotated half is free here
+    const double th = wall_angle(bits, bits + B.wbits_cb, w, h, nw, wl_smem, bs);
     if (threadIdx.x == 0) s_thn = th;
   }
   if (threadIdx.x == 0) {
@@ -812,7 +838,8 @@ __global__ void __launch_bounds__(WALL_THREADS) k_walls(Batch B) {
     WallOut o{Wl, SMG_WALL_SEGS_MAX, 0, 0};
     uint32_t* runs = B.wruns + (size_t)m * B.wruns_stride;
     int32_t* cnt = (int32_t*)(rc1 + O);
-    wall_extract(bits, w, h, nw, res, ox, oy, runs, cnt, wl_smem, o, B.wall_tmp + (size_t)m * SMG_WALL_SEGS_MAX * 4, &s_ovf);
+    wall_extract(bits, bits + B.wbits_cb, w, h, nw, res, ox, oy, runs, cnt, wl_smem, o, B.wall_tmp + (size_t)m * SMG_WALL_SEGS_MAX * 4,
+                 &s_ovf);
     if (threadIdx.x == 0) {
       R->n_w = o.n;
       if (o.ovf) s_ovf = 1;

@@ -2483,7 +2483,8 @@ int smg_set_walls(smg_batch* b, int on) {
       const size_t rp = std::min(side / 2 + 1, WALL_ACT_MAX + 1);
       B.wscr_side = side;
       B.wbits_half = (size_t)h * nw;
-      B.wbits_stride = B.wbits_half + (size_t)side * snw;
+      B.wbits_cb = B.wbits_half + (size_t)side * snw;
+      B.wbits_stride = B.wbits_cb + (size_t)side * snw;
       B.wruns_stride = 2 * (size_t)side * rp;
       B.wscr_i_stride = (8 * O + 2 * (size_t)side + 16 + 3) & ~(size_t)3;   // int4-aligned per map
       if (int r = dalloc(b, &B.wbits, M * B.wbits_stride)) return r;

@@ -423,7 +423,7 @@ typedef struct {
   int32_t walls_on;
   int32_t wscr_side;     // side of the largest grid an extraction handles (the window rotated)
   uint64_t* wbits;       // [M*wbits_stride] occupancy bits: the window, then a rotated window
-  size_t wbits_stride, wbits_half;
+  size_t wbits_stride, wbits_half, wbits_cb;   // the rotated window at wbits_half, column bits at wbits_cb
   uint32_t* wruns;       // [M*wruns_stride] runs of rows, then of columns
   size_t wruns_stride;
   int32_t* wscr_i;       // [M*wscr_i_stride] ignore cell ranges (2*O int4), run counts
