@@ -446,23 +446,36 @@ DEV double wall_angle(const uint64_t* bits, uint64_t* cbits, int w, int h, int n
 
 // ---- tilted maps (wallSegmentsAtAngle, walls.cpp rotatedSegments) ----------------------------
 
+// floor(a / b - off) with a / b the correctly rounded quotient, as the reference computes it:
+// from a * (1 / b), whose error is a few ulps, falling back to the division only where that
+// product lies within 1e-6 of an integer (there the two floors could differ)
+DEV int wall_floor_div(double a, double b, double inv_b, double off) {
+  double t = a * inv_b - off;
+  if (fabs(t - rint(t)) < 1e-6) t = a / b - off;
+  return (int)floor(t);
+}
+
 #define WALL_LINES 512     // refined lines of one extraction
 #define WALL_PIECES 64     // pieces of one clip
 #define WALL_SAMPLES 4096  // samples along one line (half-cell steps)
+#define WALL_RPIECES 16    // refined lines one raw segment may leave
+#define WALL_RWARPS 16     // warps refining raw segments at once
+#define WALL_WSCR 1280     // their shared scratch each: snap profile, sample bits, clip pieces
 
 struct WallLine { int hz; double q, a0, a1; };
+static_assert(sizeof(WallLine) == 32, "refined lines are kept in 32-byte slots");
 
 struct WallRot {
   const uint64_t* obits;   // the original window's occupancy (ignore areas cleared), top row first
   int w, h, nw;
-  double res, ox, oy, c, s;
+  double res, ox, oy, c, s, inv_res;
 };
 
 // the original grid's occupancy at the rotated point (u, v) (the cell whose corner is at
 // origin + (x, y) * res holds it)
 DEV bool wall_occ_uv(const WallRot& G, double u, double v) {
   const double x = G.c * u - G.s * v, y = G.s * u + G.c * v;
-  const int ix = (int)floor((x - G.ox) / G.res), iy = (int)floor((y - G.oy) / G.res);
+  const int ix = wall_floor_div(x - G.ox, G.res, G.inv_res, 0.0), iy = wall_floor_div(y - G.oy, G.res, G.inv_res, 0.0);
   if (ix < 0 || iy < 0 || ix >= G.w || iy >= G.h) return false;
   return (G.obits[(size_t)(G.h - 1 - iy) * G.nw + (ix >> 6)] >> (ix & 63)) & 1ull;
 }
@@ -506,13 +519,19 @@ DEV bool wall_snap(const WallRot& G, WallLine& l, double* f) {
 // clip (warp): split the line where occupancy (within half a cell across it) breaks for more
 // than 4 cells and trim its ends to occupied samples; keep pieces of min_len (less a cell) at
 // least 70 % occupied.  Returns the number of pieces (lane 0's list).
-DEV int wall_clip(const WallRot& G, const WallLine& l, uint8_t* on, WallLine* out, int* ovf) {
+DEV int wall_clip(const WallRot& G, const WallLine& l, uint32_t* onw, WallLine* out, int pcap, int* ovf) {
   const int lane = threadIdx.x & 31, n = wall_nsamp(G, l);
   if (n + 1 > WALL_SAMPLES) { if (lane == 0) *ovf = 1; return 0; }
   const double hr = G.res / 2;
-  for (int i = lane; i <= n; i += 32) {
-    const double t = l.a0 + (l.a1 - l.a0) * i / n;
-    on[i] = wall_occ_line(G, l, t, 0) || wall_occ_line(G, l, t, -hr) || wall_occ_line(G, l, t, hr);
+  for (int i0 = 0; i0 <= n; i0 += 32) {   // occupancy of the samples as bits, 32 by a ballot
+    const int i = i0 + lane;
+    bool v = false;
+    if (i <= n) {
+      const double t = l.a0 + (l.a1 - l.a0) * i / n;
+      v = wall_occ_line(G, l, t, 0) || wall_occ_line(G, l, t, -hr) || wall_occ_line(G, l, t, hr);
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, v);
+    if (lane == 0) onw[i0 >> 5] = bal;
   }
   __syncwarp();
   int np = 0;
@@ -522,7 +541,7 @@ DEV int wall_clip(const WallRot& G, const WallLine& l, uint8_t* on, WallLine* ou
       if (first >= 0) {
         const double t0 = l.a0 + (l.a1 - l.a0) * first / n, t1 = l.a0 + (l.a1 - l.a0) * last / n;
         if (t1 - t0 >= WALL_MIN_LEN - G.res - 1e-9 && (double)cnt >= 0.7 * (last - first + 1)) {
-          if (np < WALL_PIECES) out[np++] = WallLine{l.hz, l.q, t0, t1};
+          if (np < pcap) out[np++] = WallLine{l.hz, l.q, t0, t1};
           else *ovf = 1;
         }
       }
@@ -531,7 +550,7 @@ DEV int wall_clip(const WallRot& G, const WallLine& l, uint8_t* on, WallLine* ou
       gap = 0;
     };
     for (int i = 0; i <= n; ++i) {
-      if (on[i]) {
+      if ((onw[i >> 5] >> (i & 31)) & 1u) {
         if (first < 0) first = i;
         last = i;
         ++cnt;
@@ -548,9 +567,9 @@ DEV int wall_clip(const WallRot& G, const WallLine& l, uint8_t* on, WallLine* ou
 }
 
 // refine (warp): snap, clip, snap every piece; appends to out (lane 0), returns the count added
-DEV int wall_refine(const WallRot& G, WallLine l, double* f, uint8_t* on, WallLine* pcs, WallLine* out, int cap, int* ovf) {
+DEV int wall_refine(const WallRot& G, WallLine l, double* f, uint32_t* onw, WallLine* pcs, int pcap, WallLine* out, int cap, int* ovf) {
   if (!wall_snap(G, l, f)) return 0;
-  const int np = wall_clip(G, l, on, pcs, ovf);
+  const int np = wall_clip(G, l, onw, pcs, pcap, ovf);
   int added = 0;
   for (int p = 0; p < np; ++p) {
     WallLine q = pcs[p];
@@ -567,8 +586,7 @@ DEV int wall_refine(const WallRot& G, WallLine l, double* f, uint8_t* on, WallLi
   return min(added, cap);
 }
 
-DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, int h, int nw, double res, double ox, double oy, double c,
-                         double s, const double* raw, const WallOut& o, unsigned char* smem, int* s_ovf);
+DEV void wall_refit_warp(const Batch& B, int m, const WallRot& G, const double* raw, int nraw, unsigned char* smem, int* s_ovf);
 
 // wallSegmentsAtAngle for |th| > kAlignTol: the window rotated by -th (a rotated cell is occupied
 // when any of the four original cells around its centre is), axis-aligned extraction there, each
@@ -577,6 +595,7 @@ DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, in
 DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits, const int4* rc0, const int4* rc1, int nrc, double th,
                      unsigned char* smem, BlockScratch& bs, int* s_ovf) {
   (void)cells; (void)bs;
+  PHASE_START();
   const int w = B.gw_grid, h = B.gh_grid, nw = (w + 63) / 64;
   const double res = (double)B.p.grid_res, ox = B.gx0 * res, oy = B.gy0 * res;
   wall_bits(cells, w, h, nw, obits, rc0, rc1, nrc);   // the masked source (maskIgnore)
@@ -593,6 +612,8 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
     return;
   }
   __syncthreads();
+  PHASE_MARK(50);   // tilted: masked source bits
+  const double inv_res = 1.0 / res;
   // rotated occupancy bits, top row first; the original bits are read from shared memory when
   // they fit (a 512 x 512 window: 32 KB)
   uint64_t* rbits = obits + (size_t)B.wbits_half;
@@ -603,14 +624,31 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
     __syncthreads();
     src = sob;
   }
+  // The cell centre in original cells is affine in the rotated cell (i, j): fx = c (i + 1/2) -
+  // s (j + 1/2) + Kx, fy = s (i + 1/2) + c (j + 1/2) + Ky.  Its floor comes from that form in
+  // float (error below 1e-6 of the terms' magnitude); the reference's double expression is
+  // evaluated only where the float value lies closer than that to an integer.
+  const float cf = (float)c, sf = (float)s;
+  const float Kx = (float)((c * u0 - s * v0 - ox) * inv_res - 0.5), Ky = (float)((s * u0 + c * v0 - oy) * inv_res - 0.5);
   for (int i = threadIdx.x; i < RH * rnw; i += blockDim.x) {
     const int iy = i / rnw, k = i - iy * rnw, j = RH - 1 - iy;
     const double v = v0 + (j + 0.5) * res;
+    const float jf = (float)j + 0.5f;
     uint64_t word = 0;
     for (int b = 0; b < 64 && k * 64 + b < RW; ++b) {
-      const double u = u0 + (k * 64 + b + 0.5) * res;
-      const double fx = (c * u - s * v - ox) / res - 0.5, fy = (s * u + c * v - oy) / res - 0.5;
-      const int x0 = (int)floor(fx), y0 = (int)floor(fy);
+      const float if_ = (float)(k * 64 + b) + 0.5f;
+      const float ax = cf * if_, bx = sf * jf, ay = sf * if_, by = cf * jf;
+      const float fxf = ax - bx + Kx, fyf = ay + by + Ky;
+      const float ex = 1e-6f * (fabsf(ax) + fabsf(bx) + fabsf(Kx) + 1.f), ey = 1e-6f * (fabsf(ay) + fabsf(by) + fabsf(Ky) + 1.f);
+      int x0, y0;
+      if (fabsf(fxf - rintf(fxf)) > ex && fabsf(fyf - rintf(fyf)) > ey) {
+        x0 = (int)floorf(fxf);
+        y0 = (int)floorf(fyf);
+      } else {
+        const double u = u0 + (k * 64 + b + 0.5) * res;
+        x0 = wall_floor_div(c * u - s * v - ox, res, inv_res, 0.5);
+        y0 = wall_floor_div(s * u + c * v - oy, res, inv_res, 0.5);
+      }
       bool occ = false;
       for (int q = 0; q < 4 && !occ; ++q) {
         const int x = x0 + (q & 1), y = y0 + (q >> 1);
@@ -622,6 +660,7 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
     rbits[i] = word;
   }
   __syncthreads();
+  PHASE_MARK(51);   // tilted: rotated bits
   // raw segments on the rotated grid (coordinates u, v)
   double* raw = B.wall_raw + (size_t)m * SMG_WALL_SEGS_MAX * 4;
   WallOut o{raw, SMG_WALL_SEGS_MAX, 0, 0};
@@ -629,40 +668,69 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
   int32_t* cnt = (int32_t*)(rc1 + B.O);
   wall_extract(rbits, obits + B.wbits_cb, RW, RH, rnw, res, u0, v0, runs, cnt, smem, o, B.wall_tmp + (size_t)m * SMG_WALL_SEGS_MAX * 4,
                s_ovf);
-  if (threadIdx.x < 32) wall_refit_warp(B, m, obits, w, h, nw, res, ox, oy, c, s, raw, o, smem, s_ovf);
+  PHASE_MARK(52);   // tilted: extraction on the rotated grid
+  __shared__ int s_nraw;
+  if (threadIdx.x == 0) {
+    s_nraw = o.n;
+    if (o.ovf) *s_ovf = 1;
+  }
+  // the original occupancy in shared memory when it fits beside the lists (a 512 x 512 window
+  // takes 32 KB): the samples' reads then wait for no global load
+  const uint64_t* ob = obits;
+  if ((size_t)32768 + (size_t)h * nw * 8 <= (size_t)65536) {
+    uint64_t* sob = (uint64_t*)(smem + 32768);
+    for (int i = threadIdx.x; i < h * nw; i += blockDim.x) sob[i] = obits[i];
+    ob = sob;
+  }
+  __syncthreads();
+  const WallRot G{ob, w, h, nw, res, ox, oy, c, s, inv_res};
+  // refine the raw segments (independent of one another), WALL_RWARPS warps at once; each
+  // leaves its lines in the segment's slot
+  const int nraw = s_nraw, wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (wid < WALL_RWARPS) {
+    unsigned char* ws = smem + 65536 + (size_t)wid * WALL_WSCR;
+    double* f = (double*)ws;
+    uint32_t* onw = (uint32_t*)(ws + 256);
+    WallLine* pcs = (WallLine*)(ws + 768);
+    for (int r = wid; r < nraw; r += WALL_RWARPS) {
+      const double* q = raw + 4 * r;
+      const bool hz = q[1] == q[3];
+      const WallLine l = hz ? WallLine{1, q[1], smin(q[0], q[2]), smax(q[0], q[2])} : WallLine{0, q[0], smin(q[1], q[3]), smax(q[1], q[3])};
+      WallLine* outl = (WallLine*)B.wall_lines + ((size_t)m * SMG_WALL_SEGS_MAX + r) * WALL_RPIECES;
+      const int k = wall_refine(G, l, f, onw, pcs, (WALL_WSCR - 768) / (int)sizeof(WallLine), outl, WALL_RPIECES, s_ovf);
+      if (lane == 0) B.wall_lcnt[(size_t)m * SMG_WALL_SEGS_MAX + r] = k;
+    }
+  }
+  __syncthreads();
+  PHASE_MARK(53);   // refit: the raw segments refined
+  if (threadIdx.x < 32) wall_refit_warp(B, m, G, raw, nraw, smem, s_ovf);
   __syncthreads();
 }
 
-// The refit of the raw rotated segments by one warp (rotatedSegments after its wallSegments):
-// shared memory holds the lines, clip pieces, samples and the snap profile.
-DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, int h, int nw, double res, double ox, double oy, double c,
-                         double s, const double* raw, const WallOut& o, unsigned char* smem, int* s_ovf) {
+// The rest of rotatedSegments by one warp: the refined lines in raw order, merges, shadows and
+// the rotation back.  Shared memory (below the staged occupancy) holds the lines, clip pieces,
+// the sample bits and the snap profile.
+DEV void wall_refit_warp(const Batch& B, int m, const WallRot& G, const double* raw, int nraw, unsigned char* smem, int* s_ovf) {
   MapRec* R = &B.maps[m];
   const int lane = threadIdx.x;
-  const int nraw = __shfl_sync(0xffffffffu, o.n, 0);
-  if (lane == 0 && o.ovf) *s_ovf = 1;
+  const double res = G.res, c = G.c, s = G.s;
+  PHASE_START();
+  (void)raw;
   WallLine* lines = (WallLine*)smem;
   WallLine* pcs = lines + WALL_LINES;
   WallLine* tmp = pcs + WALL_PIECES;
   double* f = (double*)(tmp + WALL_PIECES);
-  uint8_t* on = (uint8_t*)(f + 32);
-  // the original occupancy in shared memory when it fits beside the lists (a 512 x 512 window
-  // takes 32 KB), the samples' reads then wait for no global load
-  const uint64_t* ob = obits;
-  if ((size_t)32768 + (size_t)h * nw * 8 <= (size_t)WALL_SMEM) {
-    uint64_t* sob = (uint64_t*)(smem + 32768);
-    for (int i = lane; i < h * nw; i += 32) sob[i] = obits[i];
-    __syncwarp();
-    ob = sob;
-  }
-  const WallRot G{ob, w, h, nw, res, ox, oy, c, s};
+  uint32_t* on = (uint32_t*)(f + 32);
   int nl = 0;
-  for (int r = 0; r < nraw; ++r) {
-    const double* q = raw + 4 * r;
-    const bool hz = q[1] == q[3];
-    const WallLine l = hz ? WallLine{1, q[1], smin(q[0], q[2]), smax(q[0], q[2])} : WallLine{0, q[0], smin(q[1], q[3]), smax(q[1], q[3])};
-    nl += wall_refine(G, l, f, on, pcs, lines + nl, WALL_LINES - nl, s_ovf);
+  for (int r = 0; r < nraw; ++r) {   // the segments' lines, in the raw segments' order
+    const int k = B.wall_lcnt[(size_t)m * SMG_WALL_SEGS_MAX + r];
+    const WallLine* src = (const WallLine*)B.wall_lines + ((size_t)m * SMG_WALL_SEGS_MAX + r) * WALL_RPIECES;
+    for (int i = lane; i < k; i += 32)
+      if (nl + i < WALL_LINES) lines[nl + i] = src[i];
+    if (nl + k > WALL_LINES && lane == 0) *s_ovf = 1;
+    nl = min(nl + k, WALL_LINES);
   }
+  __syncwarp();
   // merge collinear neighbours until none is left (the first pair in (i, j) order each time);
   // every merge leaves fewer lines or pieces more than 4 cells apart, the guard only bounds a
   // damaged list
@@ -671,23 +739,30 @@ DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, in
       if (lane == 0) *s_ovf = 1;
       break;
     }
+    // the first mergeable pair in (i, j) order: for each i, the lanes test 32 j at a time
     int pi = -1, pj = -1;
-    if (lane == 0)
-      for (int i = 0; i < nl && pi < 0; ++i)
-        for (int j = i + 1; j < nl; ++j) {
-          const WallLine &a = lines[i], &b = lines[j];
-          if (a.hz != b.hz || fabs(a.q - b.q) > 2 * res + 1e-9 || smin(a.a1, b.a1) - smax(a.a0, b.a0) < -res - 1e-9) continue;
+    for (int i = 0; i < nl && pi < 0; ++i) {
+      const WallLine a = lines[i];
+      for (int j0 = i + 1; j0 < nl; j0 += 32) {
+        const int j = j0 + lane;
+        bool ok = false;
+        if (j < nl) {
+          const WallLine& b = lines[j];
+          ok = !(a.hz != b.hz || fabs(a.q - b.q) > 2 * res + 1e-9 || smin(a.a1, b.a1) - smax(a.a0, b.a0) < -res - 1e-9);
+        }
+        const unsigned msk = __ballot_sync(0xffffffffu, ok);
+        if (msk) {
           pi = i;
-          pj = j;
+          pj = j0 + __ffs(msk) - 1;
           break;
         }
-    pi = __shfl_sync(0xffffffffu, pi, 0);
-    pj = __shfl_sync(0xffffffffu, pj, 0);
+      }
+    }
     if (pi < 0) break;
     const WallLine a = lines[pi], b = lines[pj];
     const double la = a.a1 - a.a0 + res, lb = b.a1 - b.a0 + res;
     const WallLine mg{a.hz, (a.q * la + b.q * lb) / (la + lb), smin(a.a0, b.a0), smax(a.a1, b.a1)};
-    const int np = wall_refine(G, mg, f, on, pcs, tmp, WALL_PIECES, s_ovf);
+    const int np = wall_refine(G, mg, f, on, pcs, WALL_PIECES, tmp, WALL_PIECES, s_ovf);
     if (lane == 0) {
       // erase j, erase i, insert the pieces at i
       for (int k = pj; k + 1 < nl; ++k) lines[k] = lines[k + 1];
@@ -703,6 +778,7 @@ DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, in
     nl = __shfl_sync(0xffffffffu, nl, 0);
     __syncwarp();
   }
+  PHASE_MARK(54);   // refit: merges
   // to segments, drop shadowed short parallels, rotate back into the map frame
   double* Wl = B.wall_w + (size_t)m * SMG_WALL_SEGS_MAX * 4;
   if (lane == 0) {
@@ -741,6 +817,7 @@ DEV void wall_refit_warp(const Batch& B, int m, const uint64_t* obits, int w, in
     R->n_w = n;
   }
   __syncwarp();
+  PHASE_MARK(55);   // refit: shadows, rotation back
 }
 
 // ---- the keyframe's wall list ---------------------------------------------------------------

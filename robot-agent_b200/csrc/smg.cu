@@ -2495,6 +2495,8 @@ int smg_set_walls(smg_batch* b, int on) {
       if (int r = dalloc(b, &B.wall_w, M * SMG_WALL_SEGS_MAX * 4)) return r;
       if (int r = dalloc(b, &B.wall_raw, M * SMG_WALL_SEGS_MAX * 4)) return r;
       if (int r = dalloc(b, &B.wall_tmp, M * SMG_WALL_SEGS_MAX * 4)) return r;
+      if (int r = dalloc(b, &B.wall_lines, M * SMG_WALL_SEGS_MAX * WALL_RPIECES * 32)) return r;
+      if (int r = dalloc(b, &B.wall_lcnt, M * SMG_WALL_SEGS_MAX)) return r;
       if (int r = dalloc(b, &b->d_wstate, (size_t)WALL_STATE_LEN)) return r;
       CK(cudaFuncSetAttribute(k_walls, cudaFuncAttributeMaxDynamicSharedMemorySize, WALL_SMEM));
     }

@@ -433,6 +433,8 @@ typedef struct {
   double* wall_w;        // [M*SMG_WALL_SEGS_MAX*4] extracted segments (no bridges)
   double* wall_raw;      // [M*SMG_WALL_SEGS_MAX*4] raw segments of a rotated extraction
   double* wall_tmp;      // [M*SMG_WALL_SEGS_MAX*4] column segments while the rows' are chained
+  unsigned char* wall_lines;   // [M*SMG_WALL_SEGS_MAX*16] refined lines of each raw rotated segment (32 bytes each)
+  int32_t* wall_lcnt;    // [M*SMG_WALL_SEGS_MAX] their counts
   // best views (allocated on the first push with an RGB image)
   ViewRec* vrec;         // [M*max_det]
   uint8_t* vrgb;         // [M*max_det*VIEW_PIX*3]
