@@ -850,7 +850,8 @@ def extra_workloads(args, local_rank: int) -> dict:
     import copy
     out = {}
     a2 = copy.copy(args)
-    a2.steps, a2.warmup, a2.no_cpu_baseline, a2.assoc_frames = 20, 3, True, 32
+    # 200 calls (about 60 ms): a 20-call window (6 ms) was seen to catch the clocks ramping
+    a2.steps, a2.warmup, a2.no_cpu_baseline, a2.assoc_frames = 200, 20, True, 32
     try:
         out["config2"] = assoc_line(run_assoc(a2, 0, 1, local_rank), a2, 1)
     except Exception as e:   # recorded, not fatal to the headline line
