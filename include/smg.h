@@ -169,7 +169,8 @@ typedef struct smg_frame {
    * reference with no RGB source. */
   const uint8_t* rgba;
   /* ObjFrame::wall_segs / n_wall_segs (objmap.hpp:219-220): n_wall_segs x (ax, ay, bx, by),
-   * map metres, at most SMG_WALL_SEGS_MAX, or NULL.  A non-NULL set replaces the map's stored
+   * map metres, at most SMG_WALL_SEGS_MAX, or NULL; in the memory the push's `where` names (like
+   * depth).  A non-NULL set replaces the map's stored
    * one (ObjectMap::wsegs_, read by apStructObject) and this keyframe's fragments get the
    * wall-line tests (apObsStructural, the see-through drop); NULL keeps the stored set and
    * skips the keyframe's tests, as in the reference (objmap.cpp:534, 605, 742). */
