@@ -614,16 +614,27 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
   __syncthreads();
   PHASE_MARK(50);   // tilted: masked source bits
   const double inv_res = 1.0 / res;
-  // rotated occupancy bits, top row first; the original bits are read from shared memory when
-  // they fit (a 512 x 512 window: 32 KB)
+  // rotated occupancy bits, top row first.  A rotated cell is occupied when any of the four
+  // original cells (x0 .. x0 + 1, y0 .. y0 + 1) around its centre is: the 2 x 2 dilation D of the
+  // occupancy answers that with one lookup, D(x0, y0) at bit x0 + 1 of row y0 + 1 (x0, y0 from -1,
+  // cells outside the window unoccupied), kept in shared memory when it fits (37 KB for 512 x 512)
   uint64_t* rbits = obits + (size_t)B.wbits_half;
-  const uint64_t* src = obits;
-  if ((size_t)h * nw * 8 <= (size_t)WALL_SMEM) {
-    uint64_t* sob = (uint64_t*)smem;
-    for (int i = threadIdx.x; i < h * nw; i += blockDim.x) sob[i] = obits[i];
-    __syncthreads();
-    src = sob;
+  const int dnw = (w + 1 + 63) / 64, drows = h + 1;
+  // (else in the column-bit area, free until the extraction on the rotated grid)
+  uint64_t* D = (size_t)drows * dnw * 8 <= (size_t)WALL_SMEM ? (uint64_t*)smem : obits + B.wbits_cb;
+  for (int t = threadIdx.x; t < drows * dnw; t += blockDim.x) {
+    const int r = t / dnw, k = t - r * dnw, y0 = r - 1;
+    // E_y(b) = A_y(b - 1) | A_y(b): A_y = the occupancy of grid row y (bit x), shifted by one
+    auto row_e = [&](int y) -> uint64_t {
+      if (y < 0 || y >= h) return 0ull;
+      const uint64_t* A = obits + (size_t)(h - 1 - y) * nw;
+      const uint64_t a = k < nw ? A[k] : 0ull, ap = k > 0 && k - 1 < nw ? A[k - 1] : 0ull;
+      const uint64_t sh = (a << 1) | (ap >> 63);   // bit b = A(b - 1)
+      return sh | a;
+    };
+    D[t] = row_e(y0) | row_e(y0 + 1);
   }
+  __syncthreads();
   // The cell centre in original cells is affine in the rotated cell (i, j): fx = c (i + 1/2) -
   // s (j + 1/2) + Kx, fy = s (i + 1/2) + c (j + 1/2) + Ky.  Its floor comes from that form in
   // float (error below 1e-6 of the terms' magnitude); the reference's double expression is
@@ -650,10 +661,9 @@ DEV void wall_tilted(const Batch& B, int m, const int8_t* cells, uint64_t* obits
         y0 = wall_floor_div(s * u + c * v - oy, res, inv_res, 0.5);
       }
       bool occ = false;
-      for (int q = 0; q < 4 && !occ; ++q) {
-        const int x = x0 + (q & 1), y = y0 + (q >> 1);
-        if (x < 0 || y < 0 || x >= w || y >= h) continue;
-        occ = (src[(size_t)(h - 1 - y) * nw + (x >> 6)] >> (x & 63)) & 1ull;
+      if (x0 >= -1 && x0 < w && y0 >= -1 && y0 < h) {
+        const int bx1 = x0 + 1;
+        occ = (D[(size_t)(y0 + 1) * dnw + (bx1 >> 6)] >> (bx1 & 63)) & 1ull;
       }
       word |= (uint64_t)occ << b;
     }
