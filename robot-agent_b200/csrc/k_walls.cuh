@@ -193,9 +193,21 @@ DEV void wall_group_warp(const uint32_t* runs, const int32_t* cnt, int nrows, in
   const int lane = threadIdx.x & 31;
   int nact = 0;
   int cl = 0;            // lane l holds the run count of row (r & ~31) + l
+  unsigned nzm = 0u;     // the rows of that block with runs
   uint32_t myrun = 0u;   // lane q holds run q of the current row
   for (int r = 0; r < nrows; ++r) {
-    if ((r & 31) == 0) cl = r + lane < nrows ? cnt[r + lane] : 0;   // 32 rows' counts, one load each
+    if ((r & 31) == 0) {   // 32 rows' counts, one load each
+      cl = r + lane < nrows ? cnt[r + lane] : 0;
+      nzm = __ballot_sync(0xffffffffu, cl != 0);
+    }
+    if (nact == 0) {   // no group open: on to the next row with runs
+      const unsigned rest = nzm & (0xffffffffu << (r & 31));
+      if (!rest) {
+        r |= 31;
+        continue;
+      }
+      r = (r & ~31) + __ffs(rest) - 1;
+    }
     const int nr = __shfl_sync(0xffffffffu, cl, r & 31);
     if (nr == 0 && nact == 0) continue;
     myrun = lane < nr ? runs[(size_t)r * rp + lane] : 0u;   // the row's runs in one load per lane
@@ -261,11 +273,14 @@ DEV void wall_extract(const uint64_t* bits, uint64_t* cbits, int w, int h, int n
   uint32_t* vr = runs + (size_t)h * rp_h;
   int32_t* hc = cnt;
   int32_t* vc = cnt + h;
+  PHASE_START();
   wall_cbits(bits, w, h, nw, cbits);   // columns as rows of bits: their runs are found word-wise too
   wall_row_runs(bits, h, nw, min_run, hr, rp_h, hc, s_ovf);
   __syncthreads();
+  PHASE_MARK(56);   // extraction: column bits, row runs
   wall_row_runs(cbits, w, (h + 63) / 64, min_run, vr, rp_v, vc, s_ovf);
   __syncthreads();
+  PHASE_MARK(57);   // extraction: column runs
   // rows (warp 0, into o) and columns (warp 1, into vtmp) are chained at the same time; the
   // column segments then follow the row segments, the reference's order
   const int wq = threadIdx.x >> 5;
@@ -283,6 +298,7 @@ DEV void wall_extract(const uint64_t* bits, uint64_t* cbits, int w, int h, int n
     }
   }
   __syncthreads();
+  PHASE_MARK(58);   // extraction: chaining
   const int hn = s_hn, vn = s_vn;
   for (int i = threadIdx.x; i < 4 * vn; i += blockDim.x)
     if (4 * (size_t)hn + i < 4 * (size_t)o.cap) o.seg[4 * (size_t)hn + i] = vtmp[i];
