@@ -843,23 +843,39 @@ def run_walls(args, local_rank: int, n_frames: int = 40) -> dict:
     return line
 
 
+def _workload_child(argv: list, local_rank: int) -> dict:
+    """One `bench.py --workload …` run in a process of its own, on the same GPU; its JSON line.
+    In the config-1 process, after the 64-map chain and the 16-thread CPU baseline, the config-2
+    association ran at a quarter of its own process's rate (25.9 k vs 109.6 k frames/s at 32
+    frames per call), so each configuration is timed the way its own `--workload` run times it."""
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK",
+                                                            "ROLE_RANK", "MASTER_ADDR", "MASTER_PORT")}
+    env["LOCAL_RANK"] = str(local_rank)
+    p = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py")] + argv, env=env, cwd=ROOT,
+                       capture_output=True, text=True, timeout=600)
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+    if p.returncode != 0 or not lines:
+        raise RuntimeError(f"rc {p.returncode}: {(p.stderr or p.stdout)[-300:]}")
+    line = json.loads(lines[-1])
+    line["process"] = "own: bench.py " + " ".join(argv)
+    return line
+
+
 def extra_workloads(args, local_rank: int) -> dict:
     """Short device-timed runs of the other configurations, so the default run records them:
-    config 2 (association GEMM, 8 frames per call) and config 3 (occupancy insert + scan match,
-    one map).  Each is its own `--workload` run with fewer steps; no CPU baselines here."""
-    import copy
+    config 2 (association GEMM, 32 frames per call) and config 3 (occupancy insert + scan match,
+    one map), each as its own `--workload` process with fewer steps and no CPU baseline; then
+    the wall extraction on this process's config-1 maps."""
     out = {}
-    a2 = copy.copy(args)
     # 200 calls (about 60 ms): a 20-call window (6 ms) was seen to catch the clocks ramping
-    a2.steps, a2.warmup, a2.no_cpu_baseline, a2.assoc_frames = 200, 20, True, 32
     try:
-        out["config2"] = assoc_line(run_assoc(a2, 0, 1, local_rank), a2, 1)
+        out["config2"] = _workload_child(["--workload", "assoc", "--steps", "200", "--warmup", "20",
+                                          "--assoc-frames", "32", "--no-cpu-baseline"], local_rank)
     except Exception as e:   # recorded, not fatal to the headline line
         out["config2"] = {"error": f"{type(e).__name__}: {e}"}
-    a3 = copy.copy(args)
-    a3.steps, a3.warmup, a3.no_cpu_baseline, a3.maps, a3.scans = 30, 3, True, 1, 200
     try:
-        out["config3"] = occ_line(run_occ(a3, 0, 1, local_rank), a3, 1)
+        out["config3"] = _workload_child(["--workload", "occ", "--steps", "30", "--warmup", "3", "--maps", "1",
+                                          "--scans", "200", "--no-cpu-baseline"], local_rank)
     except Exception as e:
         out["config3"] = {"error": f"{type(e).__name__}: {e}"}
     try:
